@@ -1,0 +1,311 @@
+"""ZeRO stages 0, 1 and 2 over one flat parameter space.
+
+Behaviour per stage matches the reference:
+
+* stage 0 (``zero/stage0_ddp.py:27-169``): fp32 master + Adam moments for every
+  parameter; gradient all-reduce, average, optional global-norm clipping, AdamW on the
+  full vector, write back the model-dtype parameters.
+* stage 1 (``zero/stage1_optimizer.py:29-189``): optimizer state only for this rank's
+  shard; full all-reduce, clip on the full vector, AdamW on the shard, all-gather of the
+  updated model-dtype shards.
+* stage 2 (``zero/stage2_optimizer.py:29-311``): gradients are reduce-scattered after every
+  ``backward`` (once per micro-batch) and accumulated, averaged, into an fp32 shard; the
+  global norm is the all-reduced sum of squares of the shards; AdamW on the shard; all-gather.
+
+B200-first differences: parameters are views of one flat buffer and weight gradients
+accumulate in one flat fp32 buffer (``main_grad``) so no ``torch.cat`` flattening or
+per-parameter hooks are needed; the collectives work in place on those buffers, and an
+implementation with device kernels (``--collective-impl nvls``) fuses the averaging and
+accumulation into the reduction; the AdamW update is one fused kernel that also writes the
+model-dtype copy; clipping never synchronises with the host.
+"""
+
+from __future__ import annotations
+
+import time
+from typing import Dict, List, Optional, Tuple
+
+import torch
+import torch.nn as nn
+
+from .base import ZeROEngineBase
+from .common import (
+    FlatParamSpace,
+    build_flat_param_metadata,
+    bytes_to_mb,
+    tensor_num_bytes,
+    tensors_num_bytes,
+)
+from .optim import adamw_update_, clip_coefficient, global_norm_from_local_sq, sum_of_squares
+
+
+class _FlatEngine(ZeROEngineBase):
+    """Common structure for the stages whose parameters are replicated between steps."""
+
+    shard_optimizer = False
+
+    def __init__(self, model: nn.Module, **kwargs) -> None:
+        super().__init__(model, **kwargs)
+        self.meta = build_flat_param_metadata(model)
+        self.space = FlatParamSpace(self.meta, self.world_size, self.rank, with_grads=True)
+        if self.shard_optimizer:
+            master_src = self.space.shard(self.space.params)
+        else:
+            master_src = self.space.params
+        self._master = master_src.float().clone()
+        self._exp_avg = torch.zeros_like(self._master)
+        self._exp_avg_sq = torch.zeros_like(self._master)
+
+    # Names kept from the reference engines.
+    @property
+    def master_params(self) -> torch.Tensor:
+        return self._master
+
+    @property
+    def local_master_param_shard(self) -> torch.Tensor:
+        return self._master
+
+    @property
+    def exp_avg(self) -> torch.Tensor:
+        return self._exp_avg
+
+    @property
+    def exp_avg_sq(self) -> torch.Tensor:
+        return self._exp_avg_sq
+
+    def zero_grad(self) -> None:
+        self.clock.reset()
+        self.space.grads.zero_()
+        for p in self.meta.params:
+            p.grad = None
+
+    def _adamw(self, grads: torch.Tensor, scale: torch.Tensor) -> None:
+        with self.clock.measure("optimizer"):
+            adamw_update_(self._master, self._exp_avg, self._exp_avg_sq, grads, self.adam, self.step_count,
+                          grad_scale=scale, param_out=self._param_out())
+
+    def _param_out(self) -> torch.Tensor:
+        return self.space.shard(self.space.params) if self.shard_optimizer else self.space.params
+
+    def _allgather_params(self) -> None:
+        if self.world_size == 1:
+            return
+        with self.clock.measure("post_allgather", tensor_num_bytes(self.space.shard(self.space.params))):
+            self.collectives.allgather_into(self.space.params, self.space.shard(self.space.params))
+
+    # -- state dict ---------------------------------------------------------------------
+    def _hparams(self) -> Dict[str, object]:
+        return {"lr": self.lr, "betas": self.betas, "eps": self.eps, "weight_decay": self.weight_decay}
+
+    def memory_state_breakdown_mb(self) -> Dict[str, float]:
+        params_mb = bytes_to_mb(sum(p.numel() for p in self.meta.params) * self.space.params.element_size())
+        grads_mb = bytes_to_mb(self._logical_grad_bytes())
+        optimizer_mb = bytes_to_mb(tensors_num_bytes([self._master, self._exp_avg, self._exp_avg_sq]))
+        return {"params_mb": params_mb, "grads_mb": grads_mb, "optimizer_mb": optimizer_mb,
+                "total_mb": params_mb + grads_mb + optimizer_mb}
+
+    def _logical_grad_bytes(self) -> int:
+        return self.meta.total_numel * self.space.params.element_size()
+
+
+class ZeROStage0DDP(_FlatEngine):
+    """Full replication + gradient all-reduce + local AdamW."""
+
+    stage = 0
+
+    def _update(self, max_grad_norm: float) -> torch.Tensor:
+        self.space.fold_autograd_grads()
+        grads = self.space.grads
+        inv_w = 1.0 / self.world_size
+        if self.world_size > 1:
+            self._record_memory_event("measured_step_stage0_pre_allreduce")
+            with self.clock.measure("allreduce", tensor_num_bytes(grads)):
+                self.collectives.allreduce_scaled_(grads, inv_w)
+            self._record_memory_event("measured_step_stage0_post_allreduce")
+        norm = sum_of_squares(grads).sqrt()
+        self.step_count += 1
+        self._adamw(grads, clip_coefficient(norm, max_grad_norm))
+        self._record_memory_event("measured_step_stage0_post_optimizer")
+        return norm
+
+    def step_async(self, max_grad_norm: float = 0.0) -> torch.Tensor:
+        return self._update(max_grad_norm)
+
+    def step_with_stats(self, max_grad_norm: float = 0.0) -> Dict[str, float]:
+        t0 = time.perf_counter()
+        norm = self._update(max_grad_norm)
+        return self._stats(norm, t0, {"allreduce": "allreduce"})
+
+    def state_dict(self) -> Dict[str, object]:
+        return {
+            "rank": self.rank,
+            "world_size": self.world_size,
+            "step_count": self.step_count,
+            "master_params": self.space.padded_to_logical(self._master).cpu(),
+            "exp_avg": self.space.padded_to_logical(self._exp_avg).cpu(),
+            "exp_avg_sq": self.space.padded_to_logical(self._exp_avg_sq).cpu(),
+            "hparams": self._hparams(),
+        }
+
+    def load_state_dict(self, state: Dict[str, object]) -> None:
+        self.step_count = int(state["step_count"])
+        dev = self.device
+        self._master.copy_(self.space.logical_to_padded(state["master_params"].to(dev, torch.float32)))
+        self._exp_avg.copy_(self.space.logical_to_padded(state["exp_avg"].to(dev, torch.float32)))
+        self._exp_avg_sq.copy_(self.space.logical_to_padded(state["exp_avg_sq"].to(dev, torch.float32)))
+        self.space.params.copy_(self._master)
+
+
+class _ShardedStateMixin:
+    """state_dict/load_state_dict for the shard-holding stages (1 and 2)."""
+
+    def state_dict(self) -> Dict[str, object]:
+        state = {
+            "step_count": self.step_count,
+            "rank": self.rank,
+            "world_size": self.world_size,
+            "shard_start": self.space.shard_start,
+            "shard_end": self.space.shard_start + self.space.chunk,
+            "layout": "padded_flat_v1",
+            "local_master_param_shard": self._master.detach().cpu(),
+            "exp_avg": self._exp_avg.detach().cpu(),
+            "exp_avg_sq": self._exp_avg_sq.detach().cpu(),
+            "hparams": self._hparams(),
+        }
+        extra = getattr(self, "_extra_state", None)
+        if callable(extra):
+            state.update(extra())
+        return state
+
+    def load_state_dict(self, state: Dict[str, object]) -> None:
+        self.step_count = int(state["step_count"])
+        self._master.copy_(state["local_master_param_shard"].to(self.device, torch.float32))
+        self._exp_avg.copy_(state["exp_avg"].to(self.device, torch.float32))
+        self._exp_avg_sq.copy_(state["exp_avg_sq"].to(self.device, torch.float32))
+        self._param_out().copy_(self._master)
+        self._allgather_params()
+
+
+class ZeROStage1Optimizer(_ShardedStateMixin, _FlatEngine):
+    """Sharded optimizer state; full gradient all-reduce; all-gather of updated shards."""
+
+    stage = 1
+    shard_optimizer = True
+
+    def _update(self, max_grad_norm: float) -> torch.Tensor:
+        self.space.fold_autograd_grads()
+        grads = self.space.grads
+        if self.world_size > 1:
+            self._record_memory_event("measured_step_stage1_pre_allreduce")
+            with self.clock.measure("allreduce", tensor_num_bytes(grads)):
+                self.collectives.allreduce_scaled_(grads, 1.0 / self.world_size)
+            self._record_memory_event("measured_step_stage1_post_allreduce")
+        norm = sum_of_squares(grads).sqrt()
+        self.step_count += 1
+        self._adamw(self.space.shard(grads), clip_coefficient(norm, max_grad_norm))
+        self._record_memory_event("measured_step_stage1_pre_allgather")
+        self._allgather_params()
+        self._record_memory_event("measured_step_stage1_post_allgather")
+        return norm
+
+    def step_async(self, max_grad_norm: float = 0.0) -> torch.Tensor:
+        return self._update(max_grad_norm)
+
+    def step_with_stats(self, max_grad_norm: float = 0.0) -> Dict[str, float]:
+        t0 = time.perf_counter()
+        norm = self._update(max_grad_norm)
+        return self._stats(norm, t0, {"allreduce": "allreduce", "post_allgather": "post_allgather"})
+
+
+class ZeROStage2Optimizer(_ShardedStateMixin, _FlatEngine):
+    """Sharded optimizer state and gradients; replicated parameters."""
+
+    stage = 2
+    shard_optimizer = True
+
+    def __init__(self, model: nn.Module, grad_bucket_numel: int = 16 * 1024 * 1024, **kwargs) -> None:
+        super().__init__(model, **kwargs)
+        # Accepted for CLI compatibility; one reduce-scatter of the whole flat buffer per backward.
+        self.grad_bucket_numel = grad_bucket_numel
+        self.grad_shard = torch.zeros(self.space.chunk, dtype=torch.float32, device=self.device)
+        self._pending_flush = False
+
+    @property
+    def flat_grad_buffer(self) -> torch.Tensor:
+        return self.space.grads
+
+    def zero_grad(self) -> None:
+        super().zero_grad()
+        self.grad_shard.zero_()
+        self._pending_flush = True
+
+    def backward(self, loss: torch.Tensor) -> None:
+        loss.backward()
+        self._pending_flush = True
+        self._flush_flat_grad_buffer()
+
+    def _flush_flat_grad_buffer(self) -> None:
+        if not self._pending_flush:
+            return
+        self.space.fold_autograd_grads()
+        grads = self.space.grads
+        self._record_memory_event("measured_step_stage2_pre_reduce_scatter")
+        with self.clock.measure("backward_reduce_scatter", tensor_num_bytes(grads)):
+            with self.collectives.label_scope("stage2.backward.reduce_scatter.flat_grad_buffer"):
+                if self.world_size > 1:
+                    self.collectives.reduce_scatter_accumulate_(self.grad_shard, grads, 1.0 / self.world_size)
+                else:
+                    self.grad_shard.add_(grads)
+        self._record_memory_event("measured_step_stage2_post_reduce_scatter")
+        grads.zero_()
+        self._pending_flush = False
+
+    def _update(self, max_grad_norm: float) -> torch.Tensor:
+        if any(p.grad is not None for p in self.meta.params) and not hasattr(self.meta.params[0], "main_grad"):
+            raise RuntimeError("Stage 2 expects gradients in the flat buffer")
+        self._flush_flat_grad_buffer()
+        norm = global_norm_from_local_sq(sum_of_squares(self.grad_shard), sharded=self.world_size > 1)
+        self.step_count += 1
+        self._adamw(self.grad_shard, clip_coefficient(norm, max_grad_norm))
+        self._record_memory_event("measured_step_stage2_pre_allgather")
+        with self.collectives.label_scope("stage2.step.allgather.updated_param_shard"):
+            self._allgather_params()
+        self._record_memory_event("measured_step_stage2_post_allgather")
+        self._record_memory_event("measured_step_stage2_post_step_free_grad_shard")
+        return norm
+
+    def step_async(self, max_grad_norm: float = 0.0) -> torch.Tensor:
+        return self._update(max_grad_norm)
+
+    def step_with_stats(self, max_grad_norm: float = 0.0) -> Dict[str, float]:
+        t0 = time.perf_counter()
+        norm = self._update(max_grad_norm)
+        return self._stats(norm, t0, {"backward_reduce_scatter": "backward_reduce_scatter",
+                                      "post_allgather": "post_allgather"})
+
+    def _logical_grad_bytes(self) -> int:
+        return self.space.chunk * self.space.params.element_size()
+
+    def _debug_memory_components_mb(self) -> Dict[str, float]:
+        return {
+            "logical_params_mb": bytes_to_mb(sum(p.numel() for p in self.meta.params) * self.space.params.element_size()),
+            "logical_grads_mb": bytes_to_mb(self._logical_grad_bytes()),
+            "logical_optimizer_mb": bytes_to_mb(tensors_num_bytes([self._master, self._exp_avg, self._exp_avg_sq])),
+            "live_full_grads_mb": 0.0,
+            "live_flat_grad_buffer_mb": bytes_to_mb(tensor_num_bytes(self.space.grads)),
+            "live_grad_shard_mb": bytes_to_mb(tensor_num_bytes(self.grad_shard)),
+            "comm_temp_mb": 0.0,
+        }
+
+    def debug_memory_components_mb(self) -> Dict[str, float]:
+        return self._debug_memory_components_mb()
+
+    def live_model_state_breakdown_mb(self) -> Dict[str, float]:
+        base = self.memory_state_breakdown_mb()
+        grads_mb = bytes_to_mb(tensor_num_bytes(self.space.grads) + tensor_num_bytes(self.grad_shard))
+        base["total_mb"] += grads_mb - base["grads_mb"]
+        base["grads_mb"] = grads_mb
+        return base
+
+    def _extra_state(self) -> Dict[str, object]:
+        return {"grad_shard": self.grad_shard.detach().cpu()}

@@ -1,0 +1,383 @@
+"""ZeRO stage 3: parameters, gradients and optimizer state all sharded.
+
+Behaviour follows the reference (``zero/stage3_optimizer.py:1-576``): one handle per
+parametrised module (``tok_embeddings``, ``layers.i``, ``norm``, ``lm_head``; a tied head
+reuses the embedding handle); between module calls the parameters are empty
+(``numel() == 0``); the model's ``_call_parametrized_module`` hook routes each call through
+an autograd function that all-gathers the module's parameters, runs the module without
+building a graph, and releases the parameters; its backward all-gathers again, restores the
+saved RNG and autocast state, recomputes the module with gradients, and reduce-scatters the
+module's gradients into an fp32 shard (averaged over ranks).  The optimizer step computes the
+global norm from all shards, clips, and runs AdamW per handle.  ``summon_full_params()`` is a
+re-entrant context that materialises every handle.
+
+B200-first structure: each handle keeps a model-dtype copy of its shard (the all-gather source),
+the all-gather writes straight into one aligned full-size buffer whose slices become the
+parameters, and the recomputed backward accumulates weight gradients in a full-size fp32
+``main_grad`` buffer that is reduce-scattered (with the 1/W scale fused in implementations
+that support it) and released.
+"""
+
+from __future__ import annotations
+
+import time
+from contextlib import contextmanager
+from typing import Dict, Iterator, List, Optional, Sequence, Tuple
+
+import torch
+import torch.distributed as dist
+import torch.nn as nn
+
+from .base import ZeROEngineBase
+from .common import (
+    FlatParamMetadata,
+    aligned_layout,
+    build_flat_param_metadata_from_params,
+    bytes_to_mb,
+    grads_num_bytes,
+    params_num_bytes,
+    tensors_num_bytes,
+    unique_trainable_params,
+)
+from .optim import adamw_update_, clip_coefficient, sum_of_squares
+
+
+class Stage3ParamHandle:
+    def __init__(self, name: str, meta: FlatParamMetadata, engine: "ZeROStage3Optimizer") -> None:
+        self.name = name
+        self.meta = meta
+        self.engine = engine
+        self.module_names: List[str] = [name]
+        self.world_size = engine.world_size
+        self.rank = engine.rank
+        self.device = meta.device
+        self.param_dtype = meta.params[0].dtype
+        self.offsets, self.numel, self.chunk = aligned_layout(meta, self.world_size)
+        self.padded_numel = self.chunk * self.world_size
+        full = torch.zeros(self.padded_numel, dtype=torch.float32, device=self.device)
+        for p, off, shape in zip(meta.params, self.offsets, meta.shapes):
+            full[off : off + shape.numel()].copy_(p.data.reshape(-1))
+        start = self.rank * self.chunk
+        self.local_master_param_shard = full[start : start + self.chunk].clone()
+        self.param_shard = self.local_master_param_shard.to(self.param_dtype)
+        self.exp_avg = torch.zeros_like(self.local_master_param_shard)
+        self.exp_avg_sq = torch.zeros_like(self.local_master_param_shard)
+        self.grad_shard = torch.zeros_like(self.local_master_param_shard)
+        self.full_params: Optional[torch.Tensor] = None
+        self.materialized = True
+        self._bind(full.to(self.param_dtype))
+
+    # Reference-compatible shard bookkeeping.
+    @property
+    def shard_start(self) -> int:
+        return self.rank * self.chunk
+
+    @property
+    def shard_end(self) -> int:
+        return self.shard_start + self.chunk
+
+    @property
+    def full_param_bytes(self) -> int:
+        return self.meta.total_numel * torch.tensor([], dtype=self.param_dtype).element_size()
+
+    def _bind(self, full: torch.Tensor) -> None:
+        self.full_params = full
+        for p, off, shape in zip(self.meta.params, self.offsets, self.meta.shapes):
+            p.data = full[off : off + shape.numel()].view(shape)
+        self.materialized = True
+
+    def materialize(self, phase: str) -> None:
+        if self.materialized:
+            return
+        eng = self.engine
+        full = torch.empty(self.padded_numel, dtype=self.param_dtype, device=self.device)
+        category = {"forward": "forward_allgather", "backward": "backward_allgather"}.get(phase, "summon_allgather")
+        with eng.clock.measure(category, self.full_param_bytes):
+            with eng.collectives.label_scope(f"stage3.{phase}.allgather.{self.name}"):
+                if self.world_size > 1:
+                    eng.collectives.allgather_into(full, self.param_shard)
+                else:
+                    full.copy_(self.param_shard)
+        self._bind(full)
+
+    def reshard(self) -> None:
+        if not self.materialized:
+            return
+        for p in self.meta.params:
+            p.grad = None
+            p.data = torch.empty(0, dtype=p.dtype, device=p.device)
+        self.full_params = None
+        self.materialized = False
+
+    def reset_grad(self) -> None:
+        self.grad_shard.zero_()
+
+    def begin_grad(self) -> torch.Tensor:
+        """Full-size fp32 gradient buffer bound to every parameter's ``main_grad``."""
+        buf = torch.zeros(self.padded_numel, dtype=torch.float32, device=self.device)
+        for p, off, shape in zip(self.meta.params, self.offsets, self.meta.shapes):
+            p.main_grad = buf[off : off + shape.numel()].view(shape)
+        return buf
+
+    def end_grad(self, buf: torch.Tensor, param_grads: Sequence[Optional[torch.Tensor]]) -> None:
+        for p, g in zip(self.meta.params, param_grads):
+            if g is not None:
+                p.main_grad.add_(g.to(torch.float32))
+        for p in self.meta.params:
+            if hasattr(p, "main_grad"):
+                del p.main_grad
+        eng = self.engine
+        with eng.clock.measure("backward_reduce_scatter", self.full_param_bytes):
+            with eng.collectives.label_scope(f"stage3.backward.reduce_scatter.{self.name}"):
+                if self.world_size > 1:
+                    eng.collectives.reduce_scatter_accumulate_(self.grad_shard, buf, 1.0 / self.world_size)
+                else:
+                    self.grad_shard.add_(buf)
+
+
+class _ShardedModuleFunction(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, runner: "_ModuleRunner", token: torch.Tensor, *args):
+        del token
+        ctx.runner = runner
+        ctx.is_tensor = [torch.is_tensor(a) for a in args]
+        ctx.wants_grad = [
+            torch.is_tensor(a) and a.requires_grad and (a.is_floating_point() or a.is_complex()) for a in args
+        ]
+        ctx.constants = [None if torch.is_tensor(a) else a for a in args]
+        ctx.save_for_backward(*[a.detach() for a in args if torch.is_tensor(a)])
+        ctx.cpu_rng = torch.get_rng_state()
+        dev = runner.device
+        ctx.cuda_rng = torch.cuda.get_rng_state(dev) if dev.type == "cuda" else None
+        if dev.type == "cuda":
+            ctx.autocast = (torch.is_autocast_enabled("cuda"), torch.get_autocast_dtype("cuda"))
+        elif dev.type == "cpu":
+            ctx.autocast = (torch.is_autocast_enabled("cpu"), torch.get_autocast_dtype("cpu"))
+        else:
+            ctx.autocast = (False, torch.float32)
+        eng = runner.engine
+        eng._record_memory_event(f"measured_step_stage3_{runner.name}_pre_allgather_forward")
+        runner.handle.materialize("forward")
+        eng._record_memory_event(f"measured_step_stage3_{runner.name}_post_allgather_forward")
+        with torch.no_grad():
+            out = runner.module(*args)
+        eng._record_memory_event(f"measured_step_stage3_{runner.name}_after_forward")
+        runner.handle.reshard()
+        eng._record_memory_event(f"measured_step_stage3_{runner.name}_after_forward_discard")
+        return out
+
+    @staticmethod
+    def backward(ctx, grad_output: torch.Tensor):
+        runner = ctx.runner
+        eng = runner.engine
+        dev = runner.device
+        devices = [dev.index if dev.index is not None else torch.cuda.current_device()] if dev.type == "cuda" else []
+        saved = iter(ctx.saved_tensors)
+        with torch.random.fork_rng(devices=devices, enabled=True):
+            torch.set_rng_state(ctx.cpu_rng)
+            if ctx.cuda_rng is not None:
+                torch.cuda.set_rng_state(ctx.cuda_rng, device=devices[0])
+            eng._record_memory_event(f"measured_step_stage3_{runner.name}_pre_allgather_backward")
+            runner.handle.materialize("backward")
+            eng._record_memory_event(f"measured_step_stage3_{runner.name}_post_allgather_backward")
+            grad_buf = runner.handle.begin_grad()
+            rebuilt, inputs = [], []
+            with torch.enable_grad():
+                for is_t, wants, const in zip(ctx.is_tensor, ctx.wants_grad, ctx.constants):
+                    if not is_t:
+                        rebuilt.append(const)
+                        continue
+                    t = next(saved).detach()
+                    if wants:
+                        t.requires_grad_(True)
+                        inputs.append(t)
+                    rebuilt.append(t)
+                enabled, dtype = ctx.autocast
+                with torch.autocast(device_type=dev.type, dtype=dtype, enabled=enabled and dev.type in ("cpu", "cuda")):
+                    out = runner.module(*rebuilt)
+                params = list(runner.handle.meta.params)
+                grads = torch.autograd.grad(out, inputs + params, grad_outputs=grad_output, allow_unused=True)
+            input_grads, param_grads = grads[: len(inputs)], grads[len(inputs) :]
+            eng._record_memory_event(f"measured_step_stage3_{runner.name}_after_layer_backward")
+            runner.handle.end_grad(grad_buf, param_grads)
+            del grad_buf
+            runner.handle.reshard()
+            eng._record_memory_event(f"measured_step_stage3_{runner.name}_after_reduce_scatter_discard")
+        it = iter(input_grads)
+        out_grads = [next(it) if (is_t and wants) else None for is_t, wants in zip(ctx.is_tensor, ctx.wants_grad)]
+        return (None, None, *out_grads)
+
+
+class _ModuleRunner:
+    def __init__(self, name: str, module: nn.Module, handle: Stage3ParamHandle, engine: "ZeROStage3Optimizer") -> None:
+        self.name = name
+        self.module = module
+        self.handle = handle
+        self.engine = engine
+        self.device = handle.device
+        # A grad-requiring dummy input guarantees the autograd node exists even when the
+        # module's real input (token ids) does not require grad.
+        self.autograd_token = torch.zeros(1, dtype=torch.float32, device=self.device, requires_grad=True)
+
+    def call(self, *args):
+        return _ShardedModuleFunction.apply(self, self.autograd_token, *args)
+
+
+class ZeROStage3Optimizer(ZeROEngineBase):
+    stage = 3
+
+    def __init__(self, model: nn.Module, **kwargs) -> None:
+        super().__init__(model, **kwargs)
+        self._summon_depth = 0
+        self.handles: Dict[str, Stage3ParamHandle] = {}
+        self._handle_order: List[Stage3ParamHandle] = []
+        self._module_runners: Dict[str, _ModuleRunner] = {}
+        self._build_module_runners()
+        self.model._zero3_executor = self
+        self._reshard_all_params()
+
+    def _module_specs(self) -> List[Tuple[str, nn.Module]]:
+        specs = [("tok_embeddings", self.model.tok_embeddings)]
+        specs += [(f"layers.{i}", layer) for i, layer in enumerate(self.model.layers)]
+        specs += [("norm", self.model.norm), ("lm_head", self.model.lm_head)]
+        return specs
+
+    def _build_module_runners(self) -> None:
+        by_params: Dict[Tuple[int, ...], Stage3ParamHandle] = {}
+        for name, module in self._module_specs():
+            params = unique_trainable_params(list(module.parameters(recurse=True)))
+            if not params:
+                continue
+            key = tuple(sorted(id(p) for p in params))
+            handle = by_params.get(key)
+            if handle is None:
+                handle = Stage3ParamHandle(name, build_flat_param_metadata_from_params(params), self)
+                by_params[key] = handle
+                self.handles[name] = handle
+                self._handle_order.append(handle)
+            elif name not in handle.module_names:
+                handle.module_names.append(name)
+            self._module_runners[name] = _ModuleRunner(name, module, handle, self)
+
+    def call_module(self, module_name: str, module: nn.Module, *args):
+        runner = self._module_runners.get(module_name)
+        if runner is None or runner.module is not module:
+            return module(*args)
+        return runner.call(*args)
+
+    def _reshard_all_params(self) -> None:
+        if self._summon_depth > 0:
+            return
+        for h in self._handle_order:
+            h.reshard()
+
+    @contextmanager
+    def summon_full_params(self) -> Iterator[nn.Module]:
+        self._summon_depth += 1
+        if self._summon_depth == 1:
+            for h in self._handle_order:
+                h.materialize("summon")
+        try:
+            yield self.model
+        finally:
+            self._summon_depth -= 1
+            if self._summon_depth == 0:
+                self._reshard_all_params()
+
+    def prepare_forward(self) -> Dict[str, float]:
+        self._reshard_all_params()
+        return {"prepare_comm_ms": 0.0}
+
+    def zero_grad(self) -> None:
+        self.clock.reset()
+        for h in self._handle_order:
+            h.reset_grad()
+        for p in self.model.parameters():
+            p.grad = None
+        self._reshard_all_params()
+
+    def _global_norm(self) -> torch.Tensor:
+        total = torch.zeros(1, dtype=torch.float32, device=self.device)
+        for h in self._handle_order:
+            total += sum_of_squares(h.grad_shard)
+        if dist.is_available() and dist.is_initialized() and self.world_size > 1:
+            dist.all_reduce(total)
+        return total.sqrt().reshape(())
+
+    def _update(self, max_grad_norm: float) -> torch.Tensor:
+        norm = self._global_norm()
+        scale = clip_coefficient(norm, max_grad_norm)
+        self.step_count += 1
+        with self.clock.measure("optimizer"):
+            for h in self._handle_order:
+                adamw_update_(h.local_master_param_shard, h.exp_avg, h.exp_avg_sq, h.grad_shard, self.adam,
+                              self.step_count, grad_scale=scale, param_out=h.param_shard)
+        self._reshard_all_params()
+        return norm
+
+    def step_async(self, max_grad_norm: float = 0.0) -> torch.Tensor:
+        return self._update(max_grad_norm)
+
+    def step_with_stats(self, max_grad_norm: float = 0.0) -> Dict[str, float]:
+        t0 = time.perf_counter()
+        norm = self._update(max_grad_norm)
+        return self._stats(norm, t0, {
+            "forward_allgather": "forward_allgather",
+            "backward_allgather": "backward_allgather",
+            "backward_reduce_scatter": "backward_reduce_scatter",
+        })
+
+    # -- accounting -----------------------------------------------------------------------
+    def _logical_shard_bytes(self) -> int:
+        return sum(h.chunk * torch.tensor([], dtype=h.param_dtype).element_size() for h in self._handle_order)
+
+    def _optimizer_tensors(self) -> List[torch.Tensor]:
+        out: List[torch.Tensor] = []
+        for h in self._handle_order:
+            out += [h.local_master_param_shard, h.exp_avg, h.exp_avg_sq]
+        return out
+
+    def memory_state_breakdown_mb(self) -> Dict[str, float]:
+        shard = bytes_to_mb(self._logical_shard_bytes())
+        opt = bytes_to_mb(tensors_num_bytes(self._optimizer_tensors()))
+        return {"params_mb": shard, "grads_mb": shard, "optimizer_mb": opt, "total_mb": 2 * shard + opt}
+
+    def live_model_state_breakdown_mb(self) -> Dict[str, float]:
+        shard = self._logical_shard_bytes()
+        params_mb = bytes_to_mb(shard + params_num_bytes(self.model.parameters()))
+        grads_mb = bytes_to_mb(shard + grads_num_bytes(self.model.parameters()))
+        opt = bytes_to_mb(tensors_num_bytes(self._optimizer_tensors()))
+        return {"params_mb": params_mb, "grads_mb": grads_mb, "optimizer_mb": opt, "total_mb": params_mb + grads_mb + opt}
+
+    def state_dict(self) -> Dict[str, object]:
+        return {
+            "step_count": self.step_count,
+            "rank": self.rank,
+            "world_size": self.world_size,
+            "handles": {
+                h.name: {
+                    "module_names": list(h.module_names),
+                    "shard_start": h.shard_start,
+                    "shard_end": h.shard_end,
+                    "local_master_param_shard": h.local_master_param_shard.detach().cpu(),
+                    "exp_avg": h.exp_avg.detach().cpu(),
+                    "exp_avg_sq": h.exp_avg_sq.detach().cpu(),
+                }
+                for h in self._handle_order
+            },
+            "hparams": {"lr": self.lr, "betas": self.betas, "eps": self.eps, "weight_decay": self.weight_decay},
+        }
+
+    def load_state_dict(self, state: Dict[str, object]) -> None:
+        self.step_count = int(state["step_count"])
+        saved_handles = state["handles"]
+        for h in self._handle_order:
+            if h.name not in saved_handles:
+                raise KeyError(f"missing stage3 handle state for '{h.name}'")
+            saved = saved_handles[h.name]
+            h.local_master_param_shard.copy_(saved["local_master_param_shard"].to(h.device, torch.float32))
+            h.exp_avg.copy_(saved["exp_avg"].to(h.device, torch.float32))
+            h.exp_avg_sq.copy_(saved["exp_avg_sq"].to(h.device, torch.float32))
+            h.param_shard.copy_(h.local_master_param_shard)
+            h.grad_shard.zero_()
+        self._reshard_all_params()

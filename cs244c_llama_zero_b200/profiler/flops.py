@@ -1,0 +1,106 @@
+"""FLOP accounting (reference ``profiler/flops.py:15-100``).
+
+``estimate_transformer_train_flops`` keeps the reference's formula, including its
+3x training multiplier (4x for ZeRO-3, which recomputes the forward), so reported
+TFLOP/s values stay comparable.  ``executed_train_flops`` gives the FLOPs the
+B200 path really executes (causal attention counted once per pair, no 4x for
+recompute unless asked) for roofline fractions.
+"""
+
+from __future__ import annotations
+
+from dataclasses import asdict, dataclass
+from typing import TYPE_CHECKING, Callable, Dict, Generic, List, Optional, TypeVar
+
+import torch
+
+if TYPE_CHECKING:
+    from ..models.config import ModelConfig
+
+T = TypeVar("T")
+
+
+@dataclass
+class FlopSnapshot:
+    label: str
+    total_flops: float
+
+    def to_dict(self) -> Dict[str, float | str]:
+        return asdict(self)
+
+
+def flops_to_tflops_per_second(total_flops: float, step_time_s: float) -> float:
+    if total_flops < 0.0 or step_time_s <= 0.0:
+        raise ValueError("total_flops must be >= 0 and step_time_s must be > 0")
+    return float(total_flops) / 1e12 / float(step_time_s)
+
+
+def _forward_terms(cfg: "ModelConfig", batch_size: int, seq_len: int) -> Dict[str, float]:
+    tokens = float(batch_size * seq_len)
+    d, ffn, vocab = float(cfg.dim), float(cfg.ffn_dim), float(cfg.vocab_size)
+    kv = float(cfg.kv_dim)
+    return {
+        "attn_proj": 2.0 * tokens * (2.0 * d * d + 2.0 * d * kv),
+        "attn_score": 2.0 * batch_size * cfg.n_heads * float(seq_len) ** 2 * cfg.head_dim,
+        "mlp": 2.0 * tokens * d * ffn * 3.0,
+        "pointwise": tokens * (8.0 * d + 4.0 * ffn),
+        "lm_head": 2.0 * tokens * d * vocab,
+    }
+
+
+def estimate_transformer_train_flops(
+    cfg: "ModelConfig",
+    batch_size: int,
+    seq_len: int,
+    grad_accum_steps: int = 1,
+    world_size: int = 1,
+    stage: int = 0,
+) -> float:
+    if batch_size <= 0 or seq_len <= 0 or grad_accum_steps <= 0 or world_size <= 0:
+        raise ValueError("batch_size, seq_len, grad_accum_steps, and world_size must be positive")
+    t = _forward_terms(cfg, batch_size, seq_len)
+    per_layer = t["attn_proj"] + 2.0 * t["attn_score"] + t["mlp"] + t["pointwise"]
+    forward = cfg.n_layers * per_layer + t["lm_head"]
+    multiplier = 4.0 if stage == 3 else 3.0
+    return forward * multiplier * float(grad_accum_steps * world_size)
+
+
+def executed_train_flops(cfg: "ModelConfig", batch_size: int, seq_len: int, recompute_forward: bool = False) -> float:
+    """Tensor-core FLOPs of one training micro-step on one GPU (causal attention halved)."""
+    t = _forward_terms(cfg, batch_size, seq_len)
+    matmul = cfg.n_layers * (t["attn_proj"] + t["mlp"]) + t["lm_head"]
+    attention = cfg.n_layers * 2.0 * t["attn_score"] * 0.5
+    total = 3.0 * matmul + 3.5 * attention  # backward of attention recomputes P: 2.5x forward
+    if recompute_forward:
+        total += matmul + attention
+    return total
+
+
+@dataclass
+class FlopTracker(Generic[T]):
+    device: Optional[torch.device] = None
+    snapshots: List[FlopSnapshot] = None
+
+    def __post_init__(self) -> None:
+        if self.snapshots is None:
+            self.snapshots = []
+
+    def _activities(self):
+        acts = [torch.profiler.ProfilerActivity.CPU]
+        if self.device is not None and self.device.type == "cuda" and torch.cuda.is_available():
+            acts.append(torch.profiler.ProfilerActivity.CUDA)
+        return acts
+
+    def measure(self, label: str, fn: Callable[[], T]) -> tuple[T, float | None]:
+        with torch.profiler.profile(activities=self._activities(), with_flops=True, acc_events=True) as prof:
+            result = fn()
+            if self.device is not None and self.device.type == "cuda" and torch.cuda.is_available():
+                torch.cuda.synchronize(self.device)
+        total = float(sum(float(getattr(evt, "flops", 0.0) or 0.0) for evt in prof.key_averages()))
+        if total <= 0.0:
+            return result, None
+        self.snapshots.append(FlopSnapshot(label=label, total_flops=total))
+        return result, total
+
+    def as_dicts(self) -> List[Dict[str, float | str]]:
+        return [s.to_dict() for s in self.snapshots]
