@@ -1,0 +1,414 @@
+// Causal GQA flash-attention backward on the 5th-generation tensor cores (sm_100a).
+//
+// Grid: one CTA per (key/value block j of 128 rows, kv head, batch).  The CTA keeps K_j and V_j in
+// shared memory and loops over every query head of its group and every query block i >= j:
+//
+//   S^T  = K_j Q_i^T           (M = kv, N = q,  K = hd)   tensor memory
+//   dP^T = V_j dO_i^T          (M = kv, N = q,  K = hd)   tensor memory
+//   P^T  = exp2(S^T * scale*log2e - lse2[q]),  dS^T = P^T * (dP^T - delta[q])   (one kv row / thread)
+//   dV  += P^T dO_i            (M = kv, N = hd, K = q)    accumulated in tensor memory over the loop
+//   dK  += dS^T Q_i            (M = kv, N = hd, K = q)    accumulated in tensor memory over the loop
+//   dQ_i = dS K_j              (M = q,  N = hd, K = kv)   A operand = the same dS^T bytes read MN-major
+//   dq_acc[q rows] += scale * dQ_i                        fp32 vector atomics (summed over j)
+//
+// Epilogues: dK (times the softmax scale, RoPE backward applied) and dV are written as bf16 straight
+// into the k / v columns of the fused q|k|v gradient; a small kernel converts dq_acc into the q
+// columns with RoPE backward.  delta = rowsum(dO * O) comes from a pre-pass.
+#include <cuda.h>
+
+#include "common.cuh"
+#include "gemm.h"
+#include "kernels.h"
+
+namespace b200 {
+
+namespace {
+
+constexpr int BWD_THREADS = 192;
+
+template <int HD>
+struct AttnBwdCfg {
+  static constexpr int KB = HD / 64;
+  static constexpr int TILE = 128 * HD * 2;     // bytes of one 128-row tile
+  static constexpr int STAGES = (HD == 64) ? 2 : 1;
+  static constexpr int K_OFF = 0;
+  static constexpr int V_OFF = TILE;
+  static constexpr int QD_OFF = 2 * TILE;       // stages of (Q_i, dO_i)
+  static constexpr int PT_OFF = QD_OFF + STAGES * 2 * TILE;
+  static constexpr int DST_OFF = PT_OFF + 128 * 128 * 2;
+  static constexpr int VEC_OFF = DST_OFF + 128 * 128 * 2;  // lse2[128], delta[128]
+  static constexpr int BAR_OFF = VEC_OFF + 2 * 128 * 4;
+  static constexpr int SMEM_BYTES = BAR_OFF + 256 + 1024;
+  // tensor-memory columns
+  static constexpr int T_ST = 0, T_DPT = 128, T_DV = 256, T_DK = 256 + HD;
+  static constexpr int T_DQ = (HD == 64) ? 384 : 0;
+  static constexpr int TMEM_COLS = 512;
+};
+
+__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+__device__ __forceinline__ void compute_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+
+__device__ __forceinline__ void store_swizzled_row(uint8_t* base, int r, int c, const uint32_t (&pk)[16]) {
+  // 32 bf16 values (columns c .. c+31) of row r of a [128 x 128] K-major SW128 tile.
+  const int kblk = c >> 6;
+#pragma unroll
+  for (int ch = 0; ch < 4; ++ch) {
+    const int chunk = ((c & 63) >> 3) + ch;
+    const int sw = chunk ^ (r & 7);
+    *reinterpret_cast<uint4*>(base + kblk * 16384 + r * 128 + sw * 16) =
+        make_uint4(pk[4 * ch], pk[4 * ch + 1], pk[4 * ch + 2], pk[4 * ch + 3]);
+  }
+}
+
+template <int HD>
+__global__ void __launch_bounds__(BWD_THREADS, 1)
+    attn_bwd_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __grid_constant__ CUtensorMap tm_do,
+                    AttnBwdParams p, DeviceErrors* errs) {
+  using C = AttnBwdCfg<HD>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::BAR_OFF);
+  uint64_t* kv_full = bars;
+  uint64_t* q_full = bars + 1;
+  uint64_t* q_empty = q_full + C::STAGES;
+  uint64_t* st_full = q_empty + C::STAGES;
+  uint64_t* p_ready = st_full + 1;
+  uint64_t* dq_full = p_ready + 1;
+  uint64_t* dq_free = dq_full + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(dq_free + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  float* s_lse = reinterpret_cast<float*>(smem + C::VEC_OFF);
+  float* s_delta = s_lse + 128;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int j = blockIdx.x;  // kv block (j = 0 has the most work and starts first)
+  const int kvh = blockIdx.y, b = blockIdx.z;
+  const int n_qb = p.seq / 128;
+  const int group = p.heads / p.kv_heads;
+  const int n_q = n_qb - j;  // query blocks i = j .. n_qb-1
+  const int n_it = group * n_q;
+  const int row0 = b * p.seq;
+
+  if (threadIdx.x == 0) {
+    mbar_init(kv_full, 1);
+    for (int s = 0; s < C::STAGES; ++s) {
+      mbar_init(&q_full[s], 1);
+      mbar_init(&q_empty[s], 1);
+    }
+    mbar_init(st_full, 1);
+    mbar_init(p_ready, 4);
+    mbar_init(dq_full, 1);
+    mbar_init(dq_free, 4);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      tma_prefetch_desc(&tm_qkv);
+      tma_prefetch_desc(&tm_do);
+      mbar_expect_tx(kv_full, 2 * C::TILE);
+#pragma unroll
+      for (int kb = 0; kb < C::KB; ++kb) {
+        tma_load_2d(smem + C::K_OFF + kb * 16384, &tm_qkv, kv_full, p.k_col + kvh * HD + 64 * kb, row0 + j * 128);
+        tma_load_2d(smem + C::V_OFF + kb * 16384, &tm_qkv, kv_full, p.v_col + kvh * HD + 64 * kb, row0 + j * 128);
+      }
+      for (int it = 0; it < n_it; ++it) {
+        const int h = kvh * group + it / n_q;
+        const int i = j + it % n_q;
+        const int st = it % C::STAGES;
+        if (!mbar_wait_bounded(&q_empty[st], ((it / C::STAGES) & 1) ^ 1u, abort_flag, errs, kErrAttnWait, 10)) break;
+        uint8_t* qs = smem + C::QD_OFF + st * 2 * C::TILE;
+        uint8_t* ds = qs + C::TILE;
+        mbar_expect_tx(&q_full[st], 2 * C::TILE);
+#pragma unroll
+        for (int kb = 0; kb < C::KB; ++kb) {
+          tma_load_2d(qs + kb * 16384, &tm_qkv, &q_full[st], h * HD + 64 * kb, row0 + i * 128);
+          tma_load_2d(ds + kb * 16384, &tm_do, &q_full[st], h * HD + 64 * kb, row0 + i * 128);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t ID_S = idesc_bf16_f32(128, 128, false, false);
+      constexpr uint32_t ID_KV = idesc_bf16_f32(128, HD, false, true);
+      constexpr uint32_t ID_Q = idesc_bf16_f32(128, HD, true, true);
+      const uint32_t k_addr = smem_u32(smem + C::K_OFF);
+      const uint32_t v_addr = smem_u32(smem + C::V_OFF);
+      const uint32_t pt_addr = smem_u32(smem + C::PT_OFF);
+      const uint32_t dst_addr = smem_u32(smem + C::DST_OFF);
+      bool ok = mbar_wait_bounded(kv_full, 0, abort_flag, errs, kErrAttnWait, 11);
+      for (int it = 0; it < n_it && ok; ++it) {
+        const int st = it % C::STAGES;
+        if (!mbar_wait_bounded(&q_full[st], (it / C::STAGES) & 1, abort_flag, errs, kErrAttnWait, 12)) break;
+        if (HD == 128 && it > 0 &&
+            !mbar_wait_bounded(dq_free, (it - 1) & 1, abort_flag, errs, kErrAttnWait, 13))
+          break;
+        tc_fence_after();
+        const uint32_t q_addr = smem_u32(smem + C::QD_OFF + st * 2 * C::TILE);
+        const uint32_t do_addr = q_addr + C::TILE;
+#pragma unroll
+        for (int ks = 0; ks < HD / 16; ++ks) {
+          const uint32_t off = (ks >> 2) * 16384 + (ks & 3) * 32;
+          tc_mma_f16(tmem + C::T_ST, smem_desc_sw128(k_addr + off, 16, 1024), smem_desc_sw128(q_addr + off, 16, 1024),
+                     ID_S, ks > 0 ? 1u : 0u);
+        }
+#pragma unroll
+        for (int ks = 0; ks < HD / 16; ++ks) {
+          const uint32_t off = (ks >> 2) * 16384 + (ks & 3) * 32;
+          tc_mma_f16(tmem + C::T_DPT, smem_desc_sw128(v_addr + off, 16, 1024),
+                     smem_desc_sw128(do_addr + off, 16, 1024), ID_S, ks > 0 ? 1u : 0u);
+        }
+        tc_commit(st_full);
+        if (!mbar_wait_bounded(p_ready, it & 1, abort_flag, errs, kErrAttnWait, 14)) break;
+        if (HD == 64 && it > 0 && !mbar_wait_bounded(dq_free, (it - 1) & 1, abort_flag, errs, kErrAttnWait, 15)) break;
+        tc_fence_after();
+#pragma unroll
+        for (int ks = 0; ks < 8; ++ks) {  // K = 128 query rows
+          const uint32_t aoff = (ks >> 2) * 16384 + (ks & 3) * 32;
+          const uint32_t boff = ks * 2048;
+          const uint32_t acc = (it > 0 || ks > 0) ? 1u : 0u;
+          tc_mma_f16(tmem + C::T_DV, smem_desc_sw128(pt_addr + aoff, 16, 1024),
+                     smem_desc_sw128(do_addr + boff, 16384, 1024), ID_KV, acc);
+          tc_mma_f16(tmem + C::T_DK, smem_desc_sw128(dst_addr + aoff, 16, 1024),
+                     smem_desc_sw128(q_addr + boff, 16384, 1024), ID_KV, acc);
+        }
+#pragma unroll
+        for (int ks = 0; ks < 8; ++ks) {  // K = 128 kv rows
+          tc_mma_f16(tmem + C::T_DQ, smem_desc_sw128(dst_addr + ks * 2048, 16384, 1024),
+                     smem_desc_sw128(k_addr + ks * 2048, 16384, 1024), ID_Q, ks > 0 ? 1u : 0u);
+        }
+        tc_commit(dq_full);
+        tc_commit(&q_empty[st]);
+      }
+    }
+  } else {
+    const int q4 = warp & 3;
+    const int r = q4 * 32 + lane;  // kv row for S^T / dK / dV; query row for dQ
+    const int tid = threadIdx.x - 64;
+    const uint32_t lane_base = tmem + ((uint32_t)(q4 * 32) << 16);
+    const float scale2 = p.scale * 1.4426950408889634f;
+    uint8_t* pt = smem + C::PT_OFF;
+    uint8_t* dst = smem + C::DST_OFF;
+    bool ok = true;
+    for (int it = 0; it < n_it && ok; ++it) {
+      const int h = kvh * group + it / n_q;
+      const int i = j + it % n_q;
+      const size_t vec_base = ((size_t)b * p.heads + h) * p.seq + (size_t)i * 128;
+      s_lse[tid] = p.lse[vec_base + tid];
+      s_delta[tid] = p.delta[vec_base + tid];
+      compute_bar();
+      if (!mbar_wait_bounded(st_full, it & 1, abort_flag, errs, kErrAttnWait, 16)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const bool diag = (i == j);
+#pragma unroll 1
+      for (int c = 0; c < 128; c += 32) {
+        uint32_t sv[32], dpv[32];
+        tmem_ld_32x32b_x32(lane_base + C::T_ST + c, sv);
+        tmem_ld_32x32b_x32(lane_base + C::T_DPT + c, dpv);
+        tc_wait_ld();
+        uint32_t pk[16], dk[16];
+#pragma unroll
+        for (int e = 0; e < 32; e += 2) {
+          float pv[2], dv[2];
+#pragma unroll
+          for (int t = 0; t < 2; ++t) {
+            const int qc = c + e + t;
+            const bool masked = diag && (qc < r);
+            const float pr = masked ? 0.f : exp2f(__uint_as_float(sv[e + t]) * scale2 - s_lse[qc]);
+            pv[t] = pr;
+            dv[t] = pr * (__uint_as_float(dpv[e + t]) - s_delta[qc]);
+          }
+          pk[e >> 1] = pack_bf16(pv[0], pv[1]);
+          dk[e >> 1] = pack_bf16(dv[0], dv[1]);
+        }
+        store_swizzled_row(pt, r, c, pk);
+        store_swizzled_row(dst, r, c, dk);
+      }
+      fence_async_smem();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(p_ready);
+      // dQ_i rows (thread = query row r of block i)
+      if (!mbar_wait_bounded(dq_full, it & 1, abort_flag, errs, kErrAttnWait, 17)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      float* dq_row = p.dq_acc + (size_t)(row0 + i * 128 + r) * (p.heads * HD) + h * HD;
+#pragma unroll 1
+      for (int c = 0; c < HD; c += 32) {
+        uint32_t qv[32];
+        tmem_ld_32x32b_x32(lane_base + C::T_DQ + c, qv);
+        tc_wait_ld();
+#pragma unroll
+        for (int e = 0; e < 32; e += 4) {
+          atomicAdd(reinterpret_cast<float4*>(dq_row + c + e),
+                    make_float4(__uint_as_float(qv[e]) * p.scale, __uint_as_float(qv[e + 1]) * p.scale,
+                                __uint_as_float(qv[e + 2]) * p.scale, __uint_as_float(qv[e + 3]) * p.scale));
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(dq_free);
+      compute_bar();  // lse/delta of this iteration no longer needed
+    }
+    if (ok && n_it > 0) {
+      // The last dq_full also covers the final dV / dK accumulation.
+      tc_fence_after();
+      const int kv_row = row0 + j * 128 + r;
+      const int pos = j * 128 + r;
+      const int half = HD / 2;
+      __nv_bfloat16* dk_out = p.dqkv + (size_t)kv_row * p.ld + p.k_col + kvh * HD;
+      __nv_bfloat16* dv_out = p.dqkv + (size_t)kv_row * p.ld + p.v_col + kvh * HD;
+#pragma unroll 1
+      for (int c = 0; c < HD; c += 32) {
+        uint32_t vv[32];
+        tmem_ld_32x32b_x32(lane_base + C::T_DV + c, vv);
+        tc_wait_ld();
+#pragma unroll
+        for (int e = 0; e < 32; e += 8) {
+          uint4 w;
+          w.x = pack_bf16(__uint_as_float(vv[e]), __uint_as_float(vv[e + 1]));
+          w.y = pack_bf16(__uint_as_float(vv[e + 2]), __uint_as_float(vv[e + 3]));
+          w.z = pack_bf16(__uint_as_float(vv[e + 4]), __uint_as_float(vv[e + 5]));
+          w.w = pack_bf16(__uint_as_float(vv[e + 6]), __uint_as_float(vv[e + 7]));
+          *reinterpret_cast<uint4*>(dv_out + c + e) = w;
+        }
+      }
+#pragma unroll 1
+      for (int c = 0; c < half; c += 32) {
+        uint32_t lo[32], hi[32];
+        tmem_ld_32x32b_x32(lane_base + C::T_DK + c, lo);
+        tmem_ld_32x32b_x32(lane_base + C::T_DK + half + c, hi);
+        tc_wait_ld();
+        const float* cs = p.rope_cos + (size_t)pos * half + c;
+        const float* sn = p.rope_sin + (size_t)pos * half + c;
+#pragma unroll
+        for (int e = 0; e < 32; e += 8) {
+          float a[8], bb[8];
+#pragma unroll
+          for (int t = 0; t < 8; ++t) {
+            const float x0 = __uint_as_float(lo[e + t]) * p.scale;
+            const float x1 = __uint_as_float(hi[e + t]) * p.scale;
+            const float cv = cs[e + t], sv = sn[e + t];
+            a[t] = x0 * cv + x1 * sv;
+            bb[t] = x1 * cv - x0 * sv;
+          }
+          uint4 wa, wb;
+          wa.x = pack_bf16(a[0], a[1]); wa.y = pack_bf16(a[2], a[3]);
+          wa.z = pack_bf16(a[4], a[5]); wa.w = pack_bf16(a[6], a[7]);
+          wb.x = pack_bf16(bb[0], bb[1]); wb.y = pack_bf16(bb[2], bb[3]);
+          wb.z = pack_bf16(bb[4], bb[5]); wb.w = pack_bf16(bb[6], bb[7]);
+          *reinterpret_cast<uint4*>(dk_out + c + e) = wa;
+          *reinterpret_cast<uint4*>(dk_out + half + c + e) = wb;
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, C::TMEM_COLS);
+  }
+}
+
+// delta[b, h, s] = sum_c dO[row, h*hd + c] * O[row, h*hd + c]; one warp per (row, head).
+__global__ void attn_delta_kernel(const __nv_bfloat16* __restrict__ o, const __nv_bfloat16* __restrict__ dout, int ld,
+                                  float* __restrict__ delta, int rows, int seq, int heads, int hd) {
+  const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (gw >= rows * heads) return;
+  const int row = gw / heads, h = gw % heads;
+  const __nv_bfloat16* a = o + (size_t)row * ld + h * hd;
+  const __nv_bfloat16* g = dout + (size_t)row * ld + h * hd;
+  float acc = 0.f;
+  for (int c = lane * 8; c < hd; c += 256) {
+    const uint4 qa = *reinterpret_cast<const uint4*>(a + c);
+    const uint4 qg = *reinterpret_cast<const uint4*>(g + c);
+    const uint32_t wa[4] = {qa.x, qa.y, qa.z, qa.w}, wg[4] = {qg.x, qg.y, qg.z, qg.w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) acc += bf16lo(wa[e]) * bf16lo(wg[e]) + bf16hi(wa[e]) * bf16hi(wg[e]);
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+  if (lane == 0) {
+    const int b = row / seq, s = row % seq;
+    delta[((size_t)b * heads + h) * seq + s] = acc;
+  }
+}
+
+// q columns of dqkv = RoPE^T(dq_acc) in bf16.
+__global__ void attn_dq_convert_kernel(const float* __restrict__ dq_acc, __nv_bfloat16* __restrict__ dqkv, int ld,
+                                       int rows, int seq, int heads, int hd, const float* __restrict__ cosv,
+                                       const float* __restrict__ sinv) {
+  const int half = hd / 2;
+  const size_t total = (size_t)rows * heads * half;
+  for (size_t idx = blockIdx.x * (size_t)blockDim.x + threadIdx.x; idx < total; idx += (size_t)gridDim.x * blockDim.x) {
+    const int row = (int)(idx / (heads * half));
+    const int rem = (int)(idx % (heads * half));
+    const int h = rem / half, c = rem % half;
+    const int pos = row % seq;
+    const float* src = dq_acc + (size_t)row * heads * hd + h * hd;
+    const float x0 = src[c], x1 = src[c + half];
+    const float cv = cosv[(size_t)pos * half + c], sv = sinv[(size_t)pos * half + c];
+    __nv_bfloat16* out = dqkv + (size_t)row * ld + h * hd;
+    out[c] = __float2bfloat16_rn(x0 * cv + x1 * sv);
+    out[c + half] = __float2bfloat16_rn(x1 * cv - x0 * sv);
+  }
+}
+
+template <int HD>
+void launch_bwd(const AttnBwdParams& p, const CUtensorMap& tq, const CUtensorMap& tdo, cudaStream_t s) {
+  using C = AttnBwdCfg<HD>;
+  static bool cfg = false;
+  if (!cfg) {
+    B200_CUDA_CHECK(cudaFuncSetAttribute(attn_bwd_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES));
+    cfg = true;
+  }
+  dim3 grid(p.seq / 128, p.kv_heads, p.batch);
+  attn_bwd_kernel<HD><<<grid, BWD_THREADS, C::SMEM_BYTES, s>>>(tq, tdo, p, device_errors_ptr());
+}
+
+}  // namespace
+
+void attention_bwd(const AttnBwdParams& p, cudaStream_t s) {
+  B200_CHECK(p.head_dim == 64 || p.head_dim == 128, "attention_bwd: head_dim must be 64 or 128");
+  B200_CHECK(p.seq % 128 == 0, "attention_bwd: seq_len must be a multiple of 128");
+  B200_CHECK(p.rope_cos != nullptr && p.rope_sin != nullptr, "attention_bwd: RoPE tables required");
+  const int rows = p.batch * p.seq;
+  {
+    const int warps = rows * p.heads;
+    attn_delta_kernel<<<(warps * 32 + 255) / 256, 256, 0, s>>>(p.out, p.dout, p.ld_out, p.delta, rows, p.seq,
+                                                               p.heads, p.head_dim);
+    B200_CUDA_CHECK(cudaGetLastError());
+  }
+  CUtensorMap tq = make_tmap_bf16_2d(p.qkv, (uint64_t)p.ld, (uint64_t)rows, (uint64_t)p.ld, 64, 128);
+  CUtensorMap tdo = make_tmap_bf16_2d(p.dout, (uint64_t)p.ld_out, (uint64_t)rows, (uint64_t)p.ld_out, 64, 128);
+  if (p.head_dim == 64)
+    launch_bwd<64>(p, tq, tdo, s);
+  else
+    launch_bwd<128>(p, tq, tdo, s);
+  B200_CUDA_CHECK(cudaGetLastError());
+  const size_t work = (size_t)rows * p.heads * (p.head_dim / 2);
+  const int blocks = (int)std::min<size_t>((work + 255) / 256, (size_t)num_sms_cached() * 16);
+  attn_dq_convert_kernel<<<blocks, 256, 0, s>>>(p.dq_acc, p.dqkv, p.ld, rows, p.seq, p.heads, p.head_dim, p.rope_cos,
+                                                p.rope_sin);
+  B200_CUDA_CHECK(cudaGetLastError());
+  count_launch(3);
+}
+
+}  // namespace b200

@@ -1,0 +1,307 @@
+// Causal GQA flash-attention forward on the 5th-generation tensor cores (sm_100a).
+//
+// One CTA per (query block of 128 rows, query head, batch), 192 threads:
+//   warp 0      TMA producer: Q once, then K_j / V_j tiles into a STAGES-deep ring.  Q, K and V
+//               are column blocks of the fused [B*S, ld] q|k|v projection output, so one tensor
+//               map serves all three and K/V are never repeated for grouped heads: query head h
+//               reads kv head h / (H / KV).
+//   warp 1      allocates tensor memory; lane 0 issues S_j = Q K_j^T (M=128, N=128, K=hd) into a
+//               double-buffered S accumulator, and O_j = P_j V_j (M=128, N=hd, K=128) into a
+//               double-buffered O accumulator once the softmax warps have written P_j.
+//   warps 2..5  softmax (one query row per thread): read S_j from tensor memory, apply the causal
+//               mask on the diagonal block, online max / sum in the base-2 domain, write P_j (bf16)
+//               to shared memory in the 128-byte-swizzled K-major layout the MMA reads, and fold
+//               O_{j-1} into the register accumulator with the running rescale factor.
+// The log-sum-exp of every row is stored in base-2 units scaled by log2(e)/sqrt(hd) so the
+// backward pass can rebuild P with one exp2.
+#include <cuda.h>
+
+#include "common.cuh"
+#include "gemm.h"
+#include "kernels.h"
+
+namespace b200 {
+
+namespace {
+
+constexpr int ATT_THREADS = 192;
+constexpr float kLog2e = 1.4426950408889634f;
+
+template <int HD>
+struct AttnFwdCfg {
+  static constexpr int KB = HD / 64;                 // 64-column swizzle blocks per row
+  static constexpr int TILE_BYTES = 128 * HD * 2;    // one 128-row tile of Q, K or V
+  static constexpr int STAGES = (HD == 64) ? 3 : 2;
+  static constexpr int P_BYTES = 128 * 128 * 2;
+  static constexpr int P_BUFS = (HD == 64) ? 2 : 1;
+  static constexpr int Q_OFF = 0;
+  static constexpr int KV_OFF = TILE_BYTES;
+  static constexpr int P_OFF = KV_OFF + STAGES * 2 * TILE_BYTES;
+  static constexpr int BAR_OFF = P_OFF + P_BUFS * P_BYTES;
+  static constexpr int SMEM_BYTES = BAR_OFF + 256 + 1024;
+  static constexpr int TMEM_COLS = (2 * 128 + 2 * HD) <= 256 ? 256 : 512;
+  static constexpr int O_TMEM = 256;  // O accumulators start after the two S buffers
+};
+
+__device__ __forceinline__ void fence_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+template <int HD>
+__global__ void __launch_bounds__(ATT_THREADS, 1)
+    attn_fwd_kernel(const __grid_constant__ CUtensorMap tm, AttnParams p, DeviceErrors* errs) {
+  using C = AttnFwdCfg<HD>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::BAR_OFF);
+  uint64_t* q_full = bars;
+  uint64_t* kv_full = bars + 1;
+  uint64_t* kv_empty = kv_full + C::STAGES;
+  uint64_t* s_full = kv_empty + C::STAGES;
+  uint64_t* p_full = s_full + 2;
+  uint64_t* o_full = p_full + 2;
+  uint64_t* o_free = o_full + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_free + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n_qb = p.seq / 128;
+  const int qb = n_qb - 1 - blockIdx.x;  // heaviest (longest causal) blocks first
+  const int h = blockIdx.y, b = blockIdx.z;
+  const int kvh = h / (p.heads / p.kv_heads);
+  const int n_kv = qb + 1;
+  const int row0 = b * p.seq;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int s = 0; s < C::STAGES; ++s) {
+      mbar_init(&kv_full[s], 1);
+      mbar_init(&kv_empty[s], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s_full[i], 1);
+      mbar_init(&p_full[i], 4);
+      mbar_init(&o_full[i], 1);
+      mbar_init(&o_free[i], 4);
+    }
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      tma_prefetch_desc(&tm);
+      mbar_expect_tx(q_full, C::TILE_BYTES);
+#pragma unroll
+      for (int kb = 0; kb < C::KB; ++kb)
+        tma_load_2d(smem + C::Q_OFF + kb * 16384, &tm, q_full, h * HD + 64 * kb, row0 + qb * 128);
+      for (int j = 0; j < n_kv; ++j) {
+        const int st = j % C::STAGES;
+        const uint32_t ph = (j / C::STAGES) & 1;
+        if (!mbar_wait_bounded(&kv_empty[st], ph ^ 1u, abort_flag, errs, kErrAttnWait, 0)) break;
+        uint8_t* ks = smem + C::KV_OFF + st * 2 * C::TILE_BYTES;
+        uint8_t* vs = ks + C::TILE_BYTES;
+        mbar_expect_tx(&kv_full[st], 2 * C::TILE_BYTES);
+#pragma unroll
+        for (int kb = 0; kb < C::KB; ++kb) {
+          tma_load_2d(ks + kb * 16384, &tm, &kv_full[st], p.k_col + kvh * HD + 64 * kb, row0 + j * 128);
+          tma_load_2d(vs + kb * 16384, &tm, &kv_full[st], p.v_col + kvh * HD + 64 * kb, row0 + j * 128);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t IDESC_S = idesc_bf16_f32(128, 128, false, false);
+      constexpr uint32_t IDESC_O = idesc_bf16_f32(128, HD, false, true);
+      const uint32_t q_addr = smem_u32(smem + C::Q_OFF);
+      auto issue_s = [&](int j) -> bool {
+        const int st = j % C::STAGES;
+        if (!mbar_wait_bounded(&kv_full[st], (j / C::STAGES) & 1, abort_flag, errs, kErrAttnWait, 1)) return false;
+        tc_fence_after();
+        const uint32_t k_addr = smem_u32(smem + C::KV_OFF + st * 2 * C::TILE_BYTES);
+#pragma unroll
+        for (int ks = 0; ks < HD / 16; ++ks) {
+          const uint32_t off = (ks >> 2) * 16384 + (ks & 3) * 32;
+          tc_mma_f16(tmem + (j & 1) * 128, smem_desc_sw128(q_addr + off, 16, 1024),
+                     smem_desc_sw128(k_addr + off, 16, 1024), IDESC_S, ks > 0 ? 1u : 0u);
+        }
+        tc_commit(&s_full[j & 1]);
+        return true;
+      };
+      bool ok = mbar_wait_bounded(q_full, 0, abort_flag, errs, kErrAttnWait, 2);
+      if (ok) ok = issue_s(0);
+      for (int j = 0; j < n_kv && ok; ++j) {
+        if (j + 1 < n_kv && !issue_s(j + 1)) break;
+        if (!mbar_wait_bounded(&p_full[j & 1], (j >> 1) & 1, abort_flag, errs, kErrAttnWait, 3)) break;
+        if (j >= 2 && !mbar_wait_bounded(&o_free[j & 1], ((j - 2) >> 1) & 1, abort_flag, errs, kErrAttnWait, 4)) break;
+        tc_fence_after();
+        const int st = j % C::STAGES;
+        const uint32_t v_addr = smem_u32(smem + C::KV_OFF + st * 2 * C::TILE_BYTES + C::TILE_BYTES);
+        const uint32_t p_addr = smem_u32(smem + C::P_OFF + (j % C::P_BUFS) * C::P_BYTES);
+#pragma unroll
+        for (int ks = 0; ks < 8; ++ks) {
+          const uint32_t poff = (ks >> 2) * 16384 + (ks & 3) * 32;
+          tc_mma_f16(tmem + C::O_TMEM + (j & 1) * HD, smem_desc_sw128(p_addr + poff, 16, 1024),
+                     smem_desc_sw128(v_addr + ks * 2048, 16384, 1024), IDESC_O, ks > 0 ? 1u : 0u);
+        }
+        tc_commit(&o_full[j & 1]);
+        tc_commit(&kv_empty[st]);
+      }
+    }
+  } else {
+    const int q = warp & 3;
+    const int r = q * 32 + lane;  // row within the query block
+    const uint32_t lane_base = tmem + ((uint32_t)(q * 32) << 16);
+    const float scale2 = p.scale * kLog2e;
+    float m = -INFINITY, l = 0.f;
+    float o[HD];
+#pragma unroll
+    for (int i = 0; i < HD; ++i) o[i] = 0.f;
+    bool ok = true;
+    for (int j = 0; j < n_kv; ++j) {
+      if (!mbar_wait_bounded(&s_full[j & 1], (j >> 1) & 1, abort_flag, errs, kErrAttnWait, 5)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const uint32_t sbase = lane_base + (j & 1) * 128;
+      const bool diag = (j == qb);
+      // pass 1: row max of the scaled scores
+      float mx = m;
+#pragma unroll 1
+      for (int c = 0; c < 128; c += 32) {
+        uint32_t sv[32];
+        tmem_ld_32x32b_x32(sbase + c, sv);
+        tc_wait_ld();
+#pragma unroll
+        for (int e = 0; e < 32; ++e) {
+          const bool masked = diag && (c + e > r);
+          if (!masked) mx = fmaxf(mx, __uint_as_float(sv[e]) * scale2);
+        }
+      }
+      const float alpha = exp2f(m - mx);
+      // P buffer reuse: PV_{j-1} must have finished reading it.
+      if (j >= 1 && !mbar_wait_bounded(&o_full[(j - 1) & 1], ((j - 1) >> 1) & 1, abort_flag, errs, kErrAttnWait, 6)) {
+        ok = false;
+        break;
+      }
+      // pass 2: probabilities, row sum, bf16 P into swizzled shared memory
+      uint8_t* pbuf = smem + C::P_OFF + (j % C::P_BUFS) * C::P_BYTES;
+      float rs = 0.f;
+#pragma unroll 1
+      for (int c = 0; c < 128; c += 32) {
+        uint32_t sv[32];
+        tmem_ld_32x32b_x32(sbase + c, sv);
+        tc_wait_ld();
+        uint32_t pk[16];
+#pragma unroll
+        for (int e = 0; e < 32; e += 2) {
+          float p0 = (diag && (c + e > r)) ? 0.f : exp2f(__uint_as_float(sv[e]) * scale2 - mx);
+          float p1 = (diag && (c + e + 1 > r)) ? 0.f : exp2f(__uint_as_float(sv[e + 1]) * scale2 - mx);
+          rs += p0 + p1;
+          pk[e >> 1] = pack_bf16(p0, p1);
+        }
+        const int kblk = c >> 6;
+#pragma unroll
+        for (int ch = 0; ch < 4; ++ch) {
+          const int chunk = ((c & 63) >> 3) + ch;  // 16-byte chunk within the 128-byte row
+          const int sw = chunk ^ (r & 7);
+          uint4 val = make_uint4(pk[4 * ch], pk[4 * ch + 1], pk[4 * ch + 2], pk[4 * ch + 3]);
+          *reinterpret_cast<uint4*>(pbuf + kblk * 16384 + r * 128 + sw * 16) = val;
+        }
+      }
+      l = l * alpha + rs;
+      fence_async_smem();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&p_full[j & 1]);
+      if (j >= 1) {
+        tc_fence_after();
+        const uint32_t obase = lane_base + C::O_TMEM + ((j - 1) & 1) * HD;
+#pragma unroll
+        for (int c = 0; c < HD; c += 32) {
+          uint32_t ov[32];
+          tmem_ld_32x32b_x32(obase + c, ov);
+          tc_wait_ld();
+#pragma unroll
+          for (int e = 0; e < 32; ++e) o[c + e] = (o[c + e] + __uint_as_float(ov[e])) * alpha;
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&o_free[(j - 1) & 1]);
+      } else {
+#pragma unroll
+        for (int i = 0; i < HD; ++i) o[i] *= alpha;
+      }
+      m = mx;
+    }
+    if (ok && mbar_wait_bounded(&o_full[(n_kv - 1) & 1], ((n_kv - 1) >> 1) & 1, abort_flag, errs, kErrAttnWait, 7)) {
+      tc_fence_after();
+      const uint32_t obase = lane_base + C::O_TMEM + ((n_kv - 1) & 1) * HD;
+      const float inv_l = 1.0f / l;
+      __nv_bfloat16* dst = p.out + (size_t)(row0 + qb * 128 + r) * p.ld_out + h * HD;
+#pragma unroll
+      for (int c = 0; c < HD; c += 32) {
+        uint32_t ov[32];
+        tmem_ld_32x32b_x32(obase + c, ov);
+        tc_wait_ld();
+#pragma unroll
+        for (int e = 0; e < 32; e += 8) {
+          uint4 w;
+          w.x = pack_bf16((o[c + e] + __uint_as_float(ov[e])) * inv_l, (o[c + e + 1] + __uint_as_float(ov[e + 1])) * inv_l);
+          w.y = pack_bf16((o[c + e + 2] + __uint_as_float(ov[e + 2])) * inv_l, (o[c + e + 3] + __uint_as_float(ov[e + 3])) * inv_l);
+          w.z = pack_bf16((o[c + e + 4] + __uint_as_float(ov[e + 4])) * inv_l, (o[c + e + 5] + __uint_as_float(ov[e + 5])) * inv_l);
+          w.w = pack_bf16((o[c + e + 6] + __uint_as_float(ov[e + 6])) * inv_l, (o[c + e + 7] + __uint_as_float(ov[e + 7])) * inv_l);
+          *reinterpret_cast<uint4*>(dst + c + e) = w;
+        }
+      }
+      p.lse[((size_t)b * p.heads + h) * p.seq + qb * 128 + r] = m + log2f(l);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, C::TMEM_COLS);
+  }
+}
+
+}  // namespace
+
+void attention_fwd(const AttnParams& p, cudaStream_t s) {
+  B200_CHECK(p.head_dim == 64 || p.head_dim == 128, "attention: head_dim must be 64 or 128");
+  B200_CHECK(p.seq % 128 == 0, "attention: seq_len must be a multiple of 128");
+  B200_CHECK(p.heads % p.kv_heads == 0, "attention: heads must be a multiple of kv_heads");
+  CUtensorMap tm = make_tmap_bf16_2d(p.qkv, (uint64_t)p.ld, (uint64_t)p.batch * p.seq, (uint64_t)p.ld, 64, 128);
+  dim3 grid(p.seq / 128, p.heads, p.batch);
+  if (p.head_dim == 64) {
+    using C = AttnFwdCfg<64>;
+    static bool cfg = false;
+    if (!cfg) {
+      B200_CUDA_CHECK(cudaFuncSetAttribute(attn_fwd_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES));
+      cfg = true;
+    }
+    attn_fwd_kernel<64><<<grid, ATT_THREADS, C::SMEM_BYTES, s>>>(tm, p, device_errors_ptr());
+  } else {
+    using C = AttnFwdCfg<128>;
+    static bool cfg = false;
+    if (!cfg) {
+      B200_CUDA_CHECK(cudaFuncSetAttribute(attn_fwd_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES));
+      cfg = true;
+    }
+    attn_fwd_kernel<128><<<grid, ATT_THREADS, C::SMEM_BYTES, s>>>(tm, p, device_errors_ptr());
+  }
+  B200_CUDA_CHECK(cudaGetLastError());
+  count_launch();
+}
+
+}  // namespace b200

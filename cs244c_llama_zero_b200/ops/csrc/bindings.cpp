@@ -1,0 +1,427 @@
+// Python bindings of the sm_100a kernels.  Every entry point validates shapes, dtypes, devices
+// and alignment, then launches on the current PyTorch CUDA stream.
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/extension.h>
+
+#include <optional>
+
+#include "comm.h"
+#include "gemm.h"
+#include "kernels.h"
+
+namespace {
+
+using at::Tensor;
+
+cudaStream_t cur_stream() { return at::cuda::getCurrentCUDAStream().stream(); }
+
+void check_cuda(const Tensor& t, const char* name) {
+  TORCH_CHECK(t.is_cuda(), name, " must be a CUDA tensor");
+}
+void check_bf16_2d(const Tensor& t, const char* name) {
+  check_cuda(t, name);
+  TORCH_CHECK(t.scalar_type() == at::kBFloat16, name, " must be bfloat16");
+  TORCH_CHECK(t.dim() == 2 && t.stride(1) == 1, name, " must be 2-D with unit column stride");
+  TORCH_CHECK(t.stride(0) % 8 == 0, name, " row stride must be a multiple of 8 elements");
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(t.data_ptr()) % 16 == 0, name, " must be 16-byte aligned");
+}
+void check_f32(const Tensor& t, const char* name) {
+  check_cuda(t, name);
+  TORCH_CHECK(t.scalar_type() == at::kFloat, name, " must be float32");
+}
+
+b200::GemmParams base_params(int M, int N, int K) {
+  b200::GemmParams p{};
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.splits = 1;
+  return p;
+}
+
+int pick_bn(int n_cols) { return n_cols <= 128 ? 128 : 256; }
+
+// Number of K splits so that small-output weight-gradient GEMMs still fill every SM.
+int pick_splits(int M, int N, int K, int bn) {
+  const int tiles = ((M + 127) / 128) * ((N + bn - 1) / bn);
+  const int kblocks = (K + 63) / 64;
+  const int target = 2 * b200::num_sms();
+  int splits = std::max(1, target / std::max(1, tiles));
+  splits = std::min(splits, std::max(1, kblocks / 8));  // keep at least 8 k-blocks per split
+  return splits;
+}
+
+// y[M,N] = x[M,K] @ w[N,K]^T (+ residual)
+void linear_fwd(Tensor x, Tensor w, Tensor out, std::optional<Tensor> residual, int64_t bn) {
+  check_bf16_2d(x, "x");
+  check_bf16_2d(w, "w");
+  check_bf16_2d(out, "out");
+  const int M = x.size(0), K = x.size(1), N = w.size(0);
+  TORCH_CHECK(w.size(1) == K && out.size(0) == M && out.size(1) == N, "linear_fwd: shape mismatch");
+  c10::cuda::CUDAGuard g(x.device());
+  auto p = base_params(M, N, K);
+  p.C = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
+  p.ldc = out.stride(0);
+  int epi = b200::EPI_STORE;
+  if (residual.has_value()) {
+    check_bf16_2d(*residual, "residual");
+    TORCH_CHECK(residual->size(0) == M && residual->size(1) == N, "residual shape mismatch");
+    p.R = reinterpret_cast<const __nv_bfloat16*>(residual->data_ptr());
+    p.ldr = residual->stride(0);
+    epi = b200::EPI_RESIDUAL;
+  }
+  b200::GemmOperands op{x.data_ptr(), w.data_ptr(), (uint64_t)x.stride(0), (uint64_t)w.stride(0)};
+  b200::gemm_launch(op, p, epi, false, false, bn > 0 ? (int)bn : pick_bn(N), cur_stream());
+}
+
+void qkv_rope_fwd(Tensor x, Tensor w, Tensor out, Tensor cos, Tensor sin, int64_t seq_len, int64_t head_dim,
+                  int64_t rope_cols) {
+  check_bf16_2d(x, "x");
+  check_bf16_2d(w, "w");
+  check_bf16_2d(out, "out");
+  check_f32(cos, "cos");
+  check_f32(sin, "sin");
+  const int M = x.size(0), K = x.size(1), N = w.size(0);
+  TORCH_CHECK(w.size(1) == K && out.size(0) == M && out.size(1) == N, "qkv_rope_fwd: shape mismatch");
+  TORCH_CHECK(N % head_dim == 0 && 256 % head_dim == 0, "qkv_rope_fwd: head_dim must divide 256 and N");
+  TORCH_CHECK(cos.numel() >= seq_len * head_dim / 2, "rope table too small");
+  c10::cuda::CUDAGuard g(x.device());
+  auto p = base_params(M, N, K);
+  p.C = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
+  p.ldc = out.stride(0);
+  p.rope_cos = cos.data_ptr<float>();
+  p.rope_sin = sin.data_ptr<float>();
+  p.seq_len = seq_len;
+  p.head_dim = head_dim;
+  p.rope_cols = rope_cols;
+  b200::GemmOperands op{x.data_ptr(), w.data_ptr(), (uint64_t)x.stride(0), (uint64_t)w.stride(0)};
+  b200::gemm_launch(op, p, b200::EPI_ROPE, false, false, 256, cur_stream());
+}
+
+// h = silu(x @ Wg^T) * (x @ Wu^T); gu = [x @ Wg^T | x @ Wu^T].  w_gu = [Wg; Wu] of shape [2*ffn, K].
+void swiglu_fwd(Tensor x, Tensor w_gu, Tensor h, Tensor gu) {
+  check_bf16_2d(x, "x");
+  check_bf16_2d(w_gu, "w_gu");
+  check_bf16_2d(h, "h");
+  check_bf16_2d(gu, "gu");
+  const int M = x.size(0), K = x.size(1), ffn = w_gu.size(0) / 2;
+  TORCH_CHECK(w_gu.size(0) == 2 * ffn && w_gu.size(1) == K, "swiglu_fwd: weight shape");
+  TORCH_CHECK(h.size(0) == M && h.size(1) == ffn && gu.size(0) == M && gu.size(1) == 2 * ffn, "swiglu_fwd: outputs");
+  TORCH_CHECK(ffn % 8 == 0, "ffn must be a multiple of 8");
+  c10::cuda::CUDAGuard g(x.device());
+  auto p = base_params(M, ffn, K);
+  p.C = reinterpret_cast<__nv_bfloat16*>(h.data_ptr());
+  p.ldc = h.stride(0);
+  p.aux = reinterpret_cast<__nv_bfloat16*>(gu.data_ptr());
+  p.ld_aux = gu.stride(0);
+  p.ffn = ffn;
+  b200::GemmOperands op{x.data_ptr(), w_gu.data_ptr(), (uint64_t)x.stride(0), (uint64_t)w_gu.stride(0)};
+  b200::gemm_launch(op, p, b200::EPI_SWIGLU, false, false, 256, cur_stream());
+}
+
+// dx[M,K] = dy[M,N] @ w[N,K]
+void linear_dgrad(Tensor dy, Tensor w, Tensor dx, int64_t bn) {
+  check_bf16_2d(dy, "dy");
+  check_bf16_2d(w, "w");
+  check_bf16_2d(dx, "dx");
+  const int M = dy.size(0), N = dy.size(1), K = w.size(1);
+  TORCH_CHECK(w.size(0) == N && dx.size(0) == M && dx.size(1) == K, "linear_dgrad: shape mismatch");
+  c10::cuda::CUDAGuard g(dy.device());
+  auto p = base_params(M, K, N);
+  p.C = reinterpret_cast<__nv_bfloat16*>(dx.data_ptr());
+  p.ldc = dx.stride(0);
+  b200::GemmOperands op{dy.data_ptr(), w.data_ptr(), (uint64_t)dy.stride(0), (uint64_t)w.stride(0)};
+  b200::gemm_launch(op, p, b200::EPI_STORE, false, true, bn > 0 ? (int)bn : pick_bn(K), cur_stream());
+}
+
+// dgu = swiglu'(gu) * (dy @ w_down), with w_down [d, ffn] and gu/dgu [M, 2*ffn].
+void swiglu_dgrad(Tensor dy, Tensor w_down, Tensor gu, Tensor dgu) {
+  check_bf16_2d(dy, "dy");
+  check_bf16_2d(w_down, "w_down");
+  check_bf16_2d(gu, "gu");
+  check_bf16_2d(dgu, "dgu");
+  const int M = dy.size(0), d = dy.size(1), ffn = w_down.size(1);
+  TORCH_CHECK(w_down.size(0) == d && gu.size(1) == 2 * ffn && dgu.size(1) == 2 * ffn && gu.size(0) == M &&
+                  dgu.size(0) == M,
+              "swiglu_dgrad: shape mismatch");
+  c10::cuda::CUDAGuard g(dy.device());
+  auto p = base_params(M, ffn, d);
+  p.C = reinterpret_cast<__nv_bfloat16*>(dgu.data_ptr());
+  p.ldc = dgu.stride(0);
+  p.aux_in = reinterpret_cast<const __nv_bfloat16*>(gu.data_ptr());
+  p.ld_aux_in = gu.stride(0);
+  p.ffn = ffn;
+  b200::GemmOperands op{dy.data_ptr(), w_down.data_ptr(), (uint64_t)dy.stride(0), (uint64_t)w_down.stride(0)};
+  b200::gemm_launch(op, p, b200::EPI_SWIGLU_BWD, false, true, 256, cur_stream());
+}
+
+// dw[N,K] (fp32) += dy[M,N]^T @ x[M,K]
+void linear_wgrad(Tensor dy, Tensor x, Tensor dw, int64_t splits, int64_t bn) {
+  check_bf16_2d(dy, "dy");
+  check_bf16_2d(x, "x");
+  check_f32(dw, "dw");
+  const int M = dy.size(0), N = dy.size(1), K = x.size(1);
+  TORCH_CHECK(x.size(0) == M, "linear_wgrad: token counts differ");
+  TORCH_CHECK(dw.dim() == 2 && dw.size(0) == N && dw.size(1) == K && dw.stride(1) == 1, "linear_wgrad: dw shape");
+  TORCH_CHECK(dw.stride(0) % 4 == 0 && reinterpret_cast<uintptr_t>(dw.data_ptr()) % 16 == 0, "dw alignment");
+  c10::cuda::CUDAGuard g(dy.device());
+  const int b = bn > 0 ? (int)bn : pick_bn(K);
+  auto p = base_params(N, K, M);
+  p.C32 = dw.data_ptr<float>();
+  p.ldc32 = dw.stride(0);
+  p.splits = splits > 0 ? (int)splits : pick_splits(N, K, M, b);
+  b200::GemmOperands op{dy.data_ptr(), x.data_ptr(), (uint64_t)dy.stride(0), (uint64_t)x.stride(0)};
+  b200::gemm_launch(op, p, b200::EPI_ACC_F32, true, true, b, cur_stream());
+}
+
+// Generic entry for tests: C = A op B with explicit majors.
+void gemm_raw(Tensor A, Tensor B, Tensor C, int64_t M, int64_t N, int64_t K, bool a_mn, bool b_mn, int64_t bn,
+              int64_t splits) {
+  check_bf16_2d(A, "A");
+  check_bf16_2d(B, "B");
+  c10::cuda::CUDAGuard g(A.device());
+  auto p = base_params(M, N, K);
+  int epi = b200::EPI_STORE;
+  if (C.scalar_type() == at::kFloat) {
+    p.C32 = C.data_ptr<float>();
+    p.ldc32 = C.stride(0);
+    p.splits = splits > 0 ? (int)splits : 1;
+    epi = b200::EPI_ACC_F32;
+  } else {
+    check_bf16_2d(C, "C");
+    p.C = reinterpret_cast<__nv_bfloat16*>(C.data_ptr());
+    p.ldc = C.stride(0);
+  }
+  b200::GemmOperands op{A.data_ptr(), B.data_ptr(), (uint64_t)A.stride(0), (uint64_t)B.stride(0)};
+  b200::gemm_launch(op, p, epi, a_mn, b_mn, (int)bn, cur_stream());
+}
+
+void rmsnorm_fwd(Tensor x, Tensor w, Tensor y, std::optional<Tensor> rstd, double eps) {
+  check_bf16_2d(x, "x");
+  check_bf16_2d(y, "y");
+  check_cuda(w, "w");
+  TORCH_CHECK(w.scalar_type() == at::kBFloat16 && w.is_contiguous(), "w must be contiguous bf16");
+  TORCH_CHECK(x.stride(0) == x.size(1) && y.stride(0) == y.size(1), "rmsnorm: rows must be contiguous");
+  c10::cuda::CUDAGuard g(x.device());
+  float* r = nullptr;
+  if (rstd.has_value()) {
+    check_f32(*rstd, "rstd");
+    r = rstd->data_ptr<float>();
+  }
+  b200::rmsnorm_fwd(reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()),
+                    reinterpret_cast<const __nv_bfloat16*>(w.data_ptr()), reinterpret_cast<__nv_bfloat16*>(y.data_ptr()),
+                    r, x.size(0), x.size(1), (float)eps, cur_stream());
+}
+
+void rmsnorm_bwd(Tensor dy, Tensor x, Tensor w, Tensor rstd, std::optional<Tensor> dres, Tensor dx, Tensor dw) {
+  check_bf16_2d(dy, "dy");
+  check_bf16_2d(x, "x");
+  check_bf16_2d(dx, "dx");
+  check_f32(rstd, "rstd");
+  check_f32(dw, "dw");
+  TORCH_CHECK(dw.is_contiguous() && dw.numel() == x.size(1), "dw must be contiguous [d] fp32");
+  c10::cuda::CUDAGuard g(x.device());
+  const __nv_bfloat16* r = nullptr;
+  if (dres.has_value()) {
+    check_bf16_2d(*dres, "dres");
+    r = reinterpret_cast<const __nv_bfloat16*>(dres->data_ptr());
+  }
+  b200::rmsnorm_bwd(reinterpret_cast<const __nv_bfloat16*>(dy.data_ptr()),
+                    reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()),
+                    reinterpret_cast<const __nv_bfloat16*>(w.data_ptr()), rstd.data_ptr<float>(), r,
+                    reinterpret_cast<__nv_bfloat16*>(dx.data_ptr()), dw.data_ptr<float>(), x.size(0), x.size(1),
+                    cur_stream());
+}
+
+void embedding_fwd(Tensor ids, Tensor table, Tensor out) {
+  check_cuda(ids, "ids");
+  TORCH_CHECK(ids.scalar_type() == at::kLong && ids.is_contiguous(), "ids must be contiguous int64");
+  check_bf16_2d(table, "table");
+  check_bf16_2d(out, "out");
+  c10::cuda::CUDAGuard g(table.device());
+  b200::embedding_fwd(ids.data_ptr<int64_t>(), reinterpret_cast<const __nv_bfloat16*>(table.data_ptr()),
+                      reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), ids.numel(), table.size(1), table.size(0),
+                      cur_stream());
+}
+
+void embedding_bwd(Tensor ids, Tensor dy, Tensor dtable) {
+  check_cuda(ids, "ids");
+  check_bf16_2d(dy, "dy");
+  check_f32(dtable, "dtable");
+  TORCH_CHECK(dtable.is_contiguous() && reinterpret_cast<uintptr_t>(dtable.data_ptr()) % 16 == 0, "dtable layout");
+  c10::cuda::CUDAGuard g(dy.device());
+  b200::embedding_bwd(ids.data_ptr<int64_t>(), reinterpret_cast<const __nv_bfloat16*>(dy.data_ptr()),
+                      dtable.data_ptr<float>(), ids.numel(), dy.size(1), dtable.size(0), cur_stream());
+}
+
+void rope_bwd(Tensor g, int64_t rope_cols, int64_t head_dim, int64_t seq_len, Tensor cos, Tensor sin) {
+  check_bf16_2d(g, "g");
+  check_f32(cos, "cos");
+  check_f32(sin, "sin");
+  c10::cuda::CUDAGuard gd(g.device());
+  b200::rope_bwd(reinterpret_cast<__nv_bfloat16*>(g.data_ptr()), g.size(0), g.stride(0), rope_cols, head_dim,
+                 seq_len, cos.data_ptr<float>(), sin.data_ptr<float>(), cur_stream());
+}
+
+void adamw(Tensor master, Tensor m, Tensor v, Tensor grad, std::optional<Tensor> param_out,
+           std::optional<Tensor> scale, double scale_const, double lr, double beta1, double beta2, double eps,
+           double wd, int64_t step) {
+  check_f32(master, "master");
+  check_f32(m, "exp_avg");
+  check_f32(v, "exp_avg_sq");
+  check_f32(grad, "grad");
+  const size_t n = master.numel();
+  TORCH_CHECK(m.numel() == (int64_t)n && v.numel() == (int64_t)n && grad.numel() == (int64_t)n, "adamw: sizes");
+  TORCH_CHECK(master.is_contiguous() && m.is_contiguous() && v.is_contiguous() && grad.is_contiguous(),
+              "adamw: contiguous state required");
+  c10::cuda::CUDAGuard g(master.device());
+  void* out = nullptr;
+  bool out_bf16 = false;
+  if (param_out.has_value()) {
+    check_cuda(*param_out, "param_out");
+    TORCH_CHECK(param_out->numel() == (int64_t)n && param_out->is_contiguous(), "adamw: param_out");
+    out_bf16 = param_out->scalar_type() == at::kBFloat16;
+    TORCH_CHECK(out_bf16 || param_out->scalar_type() == at::kFloat, "adamw: param_out dtype");
+    out = param_out->data_ptr();
+  }
+  const float* sp = nullptr;
+  if (scale.has_value()) {
+    check_f32(*scale, "scale");
+    sp = scale->data_ptr<float>();
+  }
+  b200::adamw_step(master.data_ptr<float>(), m.data_ptr<float>(), v.data_ptr<float>(), grad.data_ptr<float>(), out,
+                   out_bf16, n, sp, (float)scale_const, (float)lr, (float)beta1, (float)beta2, (float)eps, (float)wd,
+                   (int)step, cur_stream());
+}
+
+void sum_squares(Tensor x, Tensor out) {
+  check_cuda(x, "x");
+  check_f32(out, "out");
+  TORCH_CHECK(x.is_contiguous(), "sum_squares: contiguous input required");
+  TORCH_CHECK(x.scalar_type() == at::kFloat || x.scalar_type() == at::kBFloat16, "sum_squares dtype");
+  c10::cuda::CUDAGuard g(x.device());
+  b200::sum_squares(x.data_ptr(), x.scalar_type() == at::kBFloat16, x.numel(), out.data_ptr<float>(), cur_stream());
+}
+
+void cross_entropy_fwd(Tensor logits, Tensor targets, Tensor lse, Tensor loss_sum, Tensor count, Tensor loss) {
+  check_bf16_2d(logits, "logits");
+  TORCH_CHECK(targets.scalar_type() == at::kLong && targets.numel() == logits.size(0), "targets");
+  c10::cuda::CUDAGuard g(logits.device());
+  b200::cross_entropy_fwd(reinterpret_cast<const __nv_bfloat16*>(logits.data_ptr()), logits.stride(0),
+                          targets.data_ptr<int64_t>(), logits.size(0), logits.size(1), lse.data_ptr<float>(),
+                          loss_sum.data_ptr<float>(), count.data_ptr<float>(), loss.data_ptr<float>(), cur_stream());
+}
+
+void cross_entropy_bwd(Tensor logits, Tensor targets, Tensor lse, Tensor grad_loss, Tensor count) {
+  check_bf16_2d(logits, "logits");
+  c10::cuda::CUDAGuard g(logits.device());
+  b200::cross_entropy_bwd(reinterpret_cast<__nv_bfloat16*>(logits.data_ptr()), logits.stride(0),
+                          targets.data_ptr<int64_t>(), logits.size(0), logits.size(1), lse.data_ptr<float>(),
+                          grad_loss.data_ptr<float>(), count.data_ptr<float>(), cur_stream());
+}
+
+void attention_fwd(Tensor qkv, int64_t k_col, int64_t v_col, Tensor out, Tensor lse, int64_t batch, int64_t seq,
+                   int64_t heads, int64_t kv_heads, int64_t head_dim, double scale) {
+  check_bf16_2d(qkv, "qkv");
+  check_bf16_2d(out, "out");
+  check_f32(lse, "lse");
+  TORCH_CHECK(qkv.size(0) == batch * seq && out.size(0) == batch * seq, "attention: row count");
+  TORCH_CHECK(lse.numel() == batch * heads * seq, "attention: lse size");
+  c10::cuda::CUDAGuard g(qkv.device());
+  b200::AttnParams p{};
+  p.qkv = reinterpret_cast<const __nv_bfloat16*>(qkv.data_ptr());
+  p.ld = qkv.stride(0);
+  p.k_col = k_col;
+  p.v_col = v_col;
+  p.out = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
+  p.ld_out = out.stride(0);
+  p.lse = lse.data_ptr<float>();
+  p.batch = batch;
+  p.seq = seq;
+  p.heads = heads;
+  p.kv_heads = kv_heads;
+  p.head_dim = head_dim;
+  p.scale = (float)scale;
+  b200::attention_fwd(p, cur_stream());
+}
+
+void attention_bwd(Tensor qkv, int64_t k_col, int64_t v_col, Tensor out, Tensor dout, Tensor lse, Tensor delta,
+                   Tensor dq_acc, Tensor dqkv, Tensor cos, Tensor sin, int64_t batch, int64_t seq, int64_t heads,
+                   int64_t kv_heads, int64_t head_dim, double scale) {
+  check_f32(cos, "cos");
+  check_f32(sin, "sin");
+  TORCH_CHECK(cos.numel() >= seq * head_dim / 2 && sin.numel() >= seq * head_dim / 2, "rope table too small");
+  check_bf16_2d(qkv, "qkv");
+  check_bf16_2d(out, "out");
+  check_bf16_2d(dout, "dout");
+  check_bf16_2d(dqkv, "dqkv");
+  check_f32(lse, "lse");
+  check_f32(delta, "delta");
+  check_f32(dq_acc, "dq_acc");
+  TORCH_CHECK(dq_acc.numel() >= batch * seq * heads * head_dim, "dq_acc too small");
+  TORCH_CHECK(dqkv.stride(0) == qkv.stride(0), "dqkv must share the qkv row stride");
+  c10::cuda::CUDAGuard g(qkv.device());
+  b200::AttnBwdParams p{};
+  p.qkv = reinterpret_cast<const __nv_bfloat16*>(qkv.data_ptr());
+  p.ld = qkv.stride(0);
+  p.k_col = k_col;
+  p.v_col = v_col;
+  p.out = reinterpret_cast<const __nv_bfloat16*>(out.data_ptr());
+  p.dout = reinterpret_cast<const __nv_bfloat16*>(dout.data_ptr());
+  p.ld_out = out.stride(0);
+  TORCH_CHECK(dout.stride(0) == out.stride(0), "dout must share the output row stride");
+  p.lse = lse.data_ptr<float>();
+  p.delta = delta.data_ptr<float>();
+  p.dq_acc = dq_acc.data_ptr<float>();
+  p.dqkv = reinterpret_cast<__nv_bfloat16*>(dqkv.data_ptr());
+  p.rope_cos = cos.data_ptr<float>();
+  p.rope_sin = sin.data_ptr<float>();
+  p.batch = batch;
+  p.seq = seq;
+  p.heads = heads;
+  p.kv_heads = kv_heads;
+  p.head_dim = head_dim;
+  p.scale = (float)scale;
+  b200::attention_bwd(p, cur_stream());
+}
+
+int64_t launch_count() { return b200::launch_counter().load(); }
+
+std::vector<int64_t> read_device_errors() {
+  b200::DeviceErrors e{};
+  B200_CUDA_CHECK(cudaMemcpy(&e, b200::device_errors_ptr(), sizeof(e), cudaMemcpyDeviceToHost));
+  return {e.code, e.where, e.block, e.count};
+}
+
+void reset_device_errors() { B200_CUDA_CHECK(cudaMemset(b200::device_errors_ptr(), 0, sizeof(b200::DeviceErrors))); }
+
+}  // namespace
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "sm_100a kernels: tcgen05 GEMMs with fused epilogues, flash attention, norms, optimizer, collectives";
+  m.def("linear_fwd", &linear_fwd, py::arg("x"), py::arg("w"), py::arg("out"), py::arg("residual") = py::none(),
+        py::arg("bn") = 0);
+  m.def("qkv_rope_fwd", &qkv_rope_fwd);
+  m.def("swiglu_fwd", &swiglu_fwd);
+  m.def("linear_dgrad", &linear_dgrad, py::arg("dy"), py::arg("w"), py::arg("dx"), py::arg("bn") = 0);
+  m.def("swiglu_dgrad", &swiglu_dgrad);
+  m.def("linear_wgrad", &linear_wgrad, py::arg("dy"), py::arg("x"), py::arg("dw"), py::arg("splits") = 0,
+        py::arg("bn") = 0);
+  m.def("gemm_raw", &gemm_raw);
+  m.def("rmsnorm_fwd", &rmsnorm_fwd);
+  m.def("rmsnorm_bwd", &rmsnorm_bwd);
+  m.def("embedding_fwd", &embedding_fwd);
+  m.def("embedding_bwd", &embedding_bwd);
+  m.def("rope_bwd", &rope_bwd);
+  m.def("adamw", &adamw);
+  m.def("sum_squares", &sum_squares);
+  m.def("cross_entropy_fwd", &cross_entropy_fwd);
+  m.def("cross_entropy_bwd", &cross_entropy_bwd);
+  m.def("attention_fwd", &attention_fwd);
+  m.def("attention_bwd", &attention_bwd);
+  m.def("launch_count", &launch_count);
+  m.def("read_device_errors", &read_device_errors);
+  m.def("reset_device_errors", &reset_device_errors);
+
+}

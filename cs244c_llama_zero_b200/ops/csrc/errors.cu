@@ -1,0 +1,32 @@
+// Process-wide launch counter and the per-device error record used by bounded waits.
+#include <cuda_runtime.h>
+
+#include <mutex>
+#include <vector>
+
+#include "common.cuh"
+
+namespace b200 {
+
+std::atomic<long long>& launch_counter() {
+  static std::atomic<long long> counter{0};
+  return counter;
+}
+
+DeviceErrors* device_errors_ptr() {
+  static std::mutex mu;
+  static std::vector<DeviceErrors*> per_device;
+  int dev = 0;
+  B200_CUDA_CHECK(cudaGetDevice(&dev));
+  std::lock_guard<std::mutex> lock(mu);
+  if ((int)per_device.size() <= dev) per_device.resize(dev + 1, nullptr);
+  if (per_device[dev] == nullptr) {
+    DeviceErrors* p = nullptr;
+    B200_CUDA_CHECK(cudaMalloc(&p, sizeof(DeviceErrors)));
+    B200_CUDA_CHECK(cudaMemset(p, 0, sizeof(DeviceErrors)));
+    per_device[dev] = p;
+  }
+  return per_device[dev];
+}
+
+}  // namespace b200

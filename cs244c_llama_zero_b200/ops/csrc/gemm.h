@@ -1,0 +1,56 @@
+// Host-visible interface of the tcgen05 GEMM (see gemm_tcgen05.cu).
+#pragma once
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "common.cuh"
+
+namespace b200 {
+
+enum GemmEpilogue : int {
+  EPI_STORE = 0,
+  EPI_RESIDUAL = 1,
+  EPI_ROPE = 2,
+  EPI_SWIGLU = 3,
+  EPI_SWIGLU_BWD = 4,
+  EPI_ACC_F32 = 5,
+};
+
+struct GemmOperands {
+  const void* A;  // bf16; K-major: [M, K] with row stride lda; MN-major: [K, M] with row stride lda
+  const void* B;  // bf16; K-major: [N, K] with row stride ldb; MN-major: [K, N] with row stride ldb
+  uint64_t lda;
+  uint64_t ldb;
+};
+
+struct GemmParams {
+  int M, N, K;
+  int tiles_m, tiles_n, splits, k_blocks_per_split, total_k_blocks;  // filled by the launcher
+  __nv_bfloat16* C;
+  int ldc;
+  const __nv_bfloat16* R;
+  int ldr;
+  float* C32;
+  int ldc32;
+  const float* rope_cos;  // [seq_len, head_dim/2]
+  const float* rope_sin;
+  int seq_len;
+  int head_dim;
+  int rope_cols;  // columns [0, rope_cols) are rotated (q and k)
+  __nv_bfloat16* aux;  // SwiGLU forward: [M, 2*ffn] pre-activations (g | u)
+  int ld_aux;
+  const __nv_bfloat16* aux_in;  // SwiGLU backward: [M, 2*ffn] saved (g | u)
+  int ld_aux_in;
+  int ffn;
+  DeviceErrors* errs;
+};
+
+int num_sms();
+CUtensorMap make_tmap_bf16_2d(const void* base, uint64_t inner, uint64_t outer, uint64_t row_stride_elems,
+                              uint32_t box_inner, uint32_t box_outer);
+void gemm_launch(const GemmOperands& op, GemmParams p, int epi, bool a_mn, bool b_mn, int bn, cudaStream_t stream);
+
+}  // namespace b200

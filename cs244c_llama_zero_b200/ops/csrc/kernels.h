@@ -1,0 +1,63 @@
+// Host launchers of the non-GEMM kernels.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+namespace b200 {
+
+int num_sms_cached();
+
+void rmsnorm_fwd(const __nv_bfloat16* x, const __nv_bfloat16* w, __nv_bfloat16* y, float* rstd, int rows, int d,
+                 float eps, cudaStream_t s);
+void rmsnorm_bwd(const __nv_bfloat16* dy, const __nv_bfloat16* x, const __nv_bfloat16* w, const float* rstd,
+                 const __nv_bfloat16* dres, __nv_bfloat16* dx, float* dw, int rows, int d, cudaStream_t s);
+void embedding_fwd(const int64_t* ids, const __nv_bfloat16* table, __nv_bfloat16* out, int rows, int d, int vocab,
+                   cudaStream_t s);
+void embedding_bwd(const int64_t* ids, const __nv_bfloat16* dy, float* dtable, int rows, int d, int vocab,
+                   cudaStream_t s);
+void rope_bwd(__nv_bfloat16* g, int rows, int ld, int rope_cols, int head_dim, int seq_len, const float* cosv,
+              const float* sinv, cudaStream_t s);
+
+void adamw_step(float* master, float* m, float* v, const float* g, void* param_out, bool param_bf16, size_t n,
+                const float* scale_ptr, float scale_const, float lr, float beta1, float beta2, float eps, float wd,
+                int step, cudaStream_t s);
+void sum_squares(const void* x, bool is_bf16, size_t n, float* out, cudaStream_t s);
+void cross_entropy_fwd(const __nv_bfloat16* logits, int ld, const int64_t* targets, int rows, int vocab, float* lse,
+                       float* loss_sum, float* count, float* loss, cudaStream_t s);
+void cross_entropy_bwd(__nv_bfloat16* logits, int ld, const int64_t* targets, int rows, int vocab, const float* lse,
+                       const float* grad_loss, const float* count, cudaStream_t s);
+
+// Flash attention (causal, GQA) on tcgen05.  q/k/v are column blocks of one [B*S, ld] matrix.
+struct AttnParams {
+  const __nv_bfloat16* qkv;  // [B*S, ld]; q at column 0, k at k_col, v at v_col
+  int ld;
+  int k_col, v_col;
+  __nv_bfloat16* out;  // [B*S, H*hd]
+  int ld_out;
+  float* lse;          // [B, H, S] (natural-log units)
+  int batch, seq, heads, kv_heads, head_dim;
+  float scale;
+};
+void attention_fwd(const AttnParams& p, cudaStream_t s);
+
+struct AttnBwdParams {
+  const __nv_bfloat16* qkv;
+  int ld, k_col, v_col;
+  const __nv_bfloat16* out;   // forward output O [B*S, H*hd]
+  const __nv_bfloat16* dout;  // dO
+  int ld_out;
+  const float* lse;           // [B, H, S]
+  float* delta;               // [B, H, S] scratch: rowsum(dO * O)
+  float* dq_acc;              // [B*S, H*hd] fp32 scratch (zeroed by the launcher)
+  __nv_bfloat16* dqkv;        // [B*S, ld] gradient of the fused qkv matrix (pre-RoPE q and k)
+  const float* rope_cos;      // [seq, head_dim/2]: RoPE backward is applied to dq and dk
+  const float* rope_sin;
+  int batch, seq, heads, kv_heads, head_dim;
+  float scale;
+};
+void attention_bwd(const AttnBwdParams& p, cudaStream_t s);
+
+}  // namespace b200

@@ -1,0 +1,290 @@
+// Memory-bound kernels of the transformer block: RMSNorm forward/backward (with the residual
+// gradient fused into the backward), token-embedding gather/scatter, RoPE backward.
+//
+// All of them move 16-byte vectors (8 bf16) per thread access and keep statistics in fp32.
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace b200 {
+
+namespace {
+
+constexpr int kWarpsPerBlock = 8;
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+__device__ __forceinline__ void unpack8(const uint4& q, float (&f)[8]) {
+  const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    f[2 * i] = bf16lo(w[i]);
+    f[2 * i + 1] = bf16hi(w[i]);
+  }
+}
+
+__device__ __forceinline__ uint4 pack8(const float (&f)[8]) {
+  uint4 q;
+  q.x = pack_bf16(f[0], f[1]);
+  q.y = pack_bf16(f[2], f[3]);
+  q.z = pack_bf16(f[4], f[5]);
+  q.w = pack_bf16(f[6], f[7]);
+  return q;
+}
+
+// One warp per row; each lane owns VEC groups of 8 columns (d = 256 * VEC).
+template <int VEC>
+__global__ void rmsnorm_fwd_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ w,
+                                   __nv_bfloat16* __restrict__ y, float* __restrict__ rstd, int rows, int d,
+                                   float eps) {
+  const int lane = threadIdx.x & 31;
+  const int row = blockIdx.x * kWarpsPerBlock + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  const __nv_bfloat16* xr = x + (size_t)row * d;
+  float v[VEC][8];
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < VEC; ++i) {
+    const int c = (i * 32 + lane) * 8;
+    if (c < d) {
+      unpack8(*reinterpret_cast<const uint4*>(xr + c), v[i]);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) ss += v[i][e] * v[i][e];
+    }
+  }
+  ss = warp_sum(ss);
+  const float r = rsqrtf(ss / (float)d + eps);
+  if (lane == 0 && rstd != nullptr) rstd[row] = r;
+  __nv_bfloat16* yr = y + (size_t)row * d;
+#pragma unroll
+  for (int i = 0; i < VEC; ++i) {
+    const int c = (i * 32 + lane) * 8;
+    if (c < d) {
+      float wf[8], o[8];
+      unpack8(*reinterpret_cast<const uint4*>(w + c), wf);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) o[e] = v[i][e] * r * wf[e];
+      *reinterpret_cast<uint4*>(yr + c) = pack8(o);
+    }
+  }
+}
+
+// dx = dres + rstd * (dy*w - xhat * mean(dy*w*xhat)); dw += sum_rows(dy * xhat) (fp32 atomics).
+template <int VEC>
+__global__ void rmsnorm_bwd_kernel(const __nv_bfloat16* __restrict__ dy, const __nv_bfloat16* __restrict__ x,
+                                   const __nv_bfloat16* __restrict__ w, const float* __restrict__ rstd,
+                                   const __nv_bfloat16* __restrict__ dres, __nv_bfloat16* __restrict__ dx,
+                                   float* __restrict__ dw, int rows, int d, int rows_per_block) {
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  float wf[VEC][8];
+  float acc[VEC][8];
+#pragma unroll
+  for (int i = 0; i < VEC; ++i) {
+    const int c = (i * 32 + lane) * 8;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) acc[i][e] = 0.f;
+    if (c < d) unpack8(*reinterpret_cast<const uint4*>(w + c), wf[i]);
+  }
+  const int row_begin = blockIdx.x * rows_per_block;
+  const int row_end = min(rows, row_begin + rows_per_block);
+  for (int row = row_begin + warp; row < row_end; row += kWarpsPerBlock) {
+    const float r = rstd[row];
+    float xh[VEC][8], g[VEC][8];
+    float dot = 0.f;
+#pragma unroll
+    for (int i = 0; i < VEC; ++i) {
+      const int c = (i * 32 + lane) * 8;
+      if (c < d) {
+        float xv[8], dyv[8];
+        unpack8(*reinterpret_cast<const uint4*>(x + (size_t)row * d + c), xv);
+        unpack8(*reinterpret_cast<const uint4*>(dy + (size_t)row * d + c), dyv);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          xh[i][e] = xv[e] * r;
+          g[i][e] = dyv[e] * wf[i][e];
+          dot += g[i][e] * xh[i][e];
+          acc[i][e] += dyv[e] * xh[i][e];
+        }
+      }
+    }
+    dot = warp_sum(dot) / (float)d;
+#pragma unroll
+    for (int i = 0; i < VEC; ++i) {
+      const int c = (i * 32 + lane) * 8;
+      if (c < d) {
+        float o[8];
+        float rv[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+        if (dres != nullptr) unpack8(*reinterpret_cast<const uint4*>(dres + (size_t)row * d + c), rv);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) o[e] = rv[e] + r * (g[i][e] - xh[i][e] * dot);
+        *reinterpret_cast<uint4*>(dx + (size_t)row * d + c) = pack8(o);
+      }
+    }
+  }
+  // Reduce the weight gradient across the warps of the block, then one atomic per column.
+  __shared__ float red[kWarpsPerBlock][32 * 8];
+#pragma unroll
+  for (int i = 0; i < VEC; ++i) {
+#pragma unroll
+    for (int e = 0; e < 8; ++e) red[warp][lane * 8 + e] = acc[i][e];
+    __syncthreads();
+    for (int t = threadIdx.x; t < 256; t += blockDim.x) {
+      float s = 0.f;
+#pragma unroll
+      for (int k = 0; k < kWarpsPerBlock; ++k) s += red[k][t];
+      const int c = i * 256 + t;
+      if (c < d) atomicAdd(dw + c, s);
+    }
+    __syncthreads();
+  }
+}
+
+__global__ void embedding_fwd_kernel(const int64_t* __restrict__ ids, const __nv_bfloat16* __restrict__ table,
+                                     __nv_bfloat16* __restrict__ out, int rows, int d, int vocab,
+                                     DeviceErrors* errs) {
+  const int vec_per_row = d / 8;
+  const size_t total = (size_t)rows * vec_per_row;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+    const int row = (int)(i / vec_per_row);
+    const int v = (int)(i % vec_per_row);
+    int64_t id = ids[row];
+    uint4 val = make_uint4(0, 0, 0, 0);
+    if (id >= 0 && id < vocab) val = *reinterpret_cast<const uint4*>(table + (size_t)id * d + v * 8);
+    *reinterpret_cast<uint4*>(out + (size_t)row * d + v * 8) = val;
+  }
+}
+
+__global__ void embedding_bwd_kernel(const int64_t* __restrict__ ids, const __nv_bfloat16* __restrict__ dy,
+                                     float* __restrict__ dtable, int rows, int d, int vocab) {
+  const int vec_per_row = d / 8;
+  const size_t total = (size_t)rows * vec_per_row;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+    const int row = (int)(i / vec_per_row);
+    const int v = (int)(i % vec_per_row);
+    const int64_t id = ids[row];
+    if (id < 0 || id >= vocab) continue;
+    float g[8];
+    unpack8(*reinterpret_cast<const uint4*>(dy + (size_t)row * d + v * 8), g);
+    float* dst = dtable + (size_t)id * d + v * 8;
+    atomicAdd(reinterpret_cast<float4*>(dst), make_float4(g[0], g[1], g[2], g[3]));
+    atomicAdd(reinterpret_cast<float4*>(dst + 4), make_float4(g[4], g[5], g[6], g[7]));
+  }
+}
+
+// In-place inverse rotation of the q and k columns of a [rows, ld] gradient.
+__global__ void rope_bwd_kernel(__nv_bfloat16* __restrict__ g, int rows, int ld, int rope_cols, int head_dim,
+                                int seq_len, const float* __restrict__ cosv, const float* __restrict__ sinv) {
+  const int half = head_dim / 2;
+  const int groups_per_row = rope_cols / head_dim * (half / 8);
+  const size_t total = (size_t)rows * groups_per_row;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+    const int row = (int)(i / groups_per_row);
+    const int gidx = (int)(i % groups_per_row);
+    const int head = gidx / (half / 8);
+    const int j = (gidx % (half / 8)) * 8;
+    const int pos = row % seq_len;
+    __nv_bfloat16* lo = g + (size_t)row * ld + head * head_dim + j;
+    __nv_bfloat16* hi = lo + half;
+    float a[8], b[8], oa[8], ob[8];
+    unpack8(*reinterpret_cast<const uint4*>(lo), a);
+    unpack8(*reinterpret_cast<const uint4*>(hi), b);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const float c = cosv[(size_t)pos * half + j + e], s = sinv[(size_t)pos * half + j + e];
+      oa[e] = a[e] * c + b[e] * s;
+      ob[e] = b[e] * c - a[e] * s;
+    }
+    *reinterpret_cast<uint4*>(lo) = pack8(oa);
+    *reinterpret_cast<uint4*>(hi) = pack8(ob);
+  }
+}
+
+int grid_for(size_t work, int threads) {
+  const size_t blocks = (work + threads - 1) / threads;
+  const size_t cap = (size_t)num_sms_cached() * 16;
+  return (int)std::max<size_t>(1, std::min(blocks, cap));
+}
+
+}  // namespace
+
+int num_sms_cached() {
+  static int n = 0;
+  if (n == 0) {
+    int dev;
+    B200_CUDA_CHECK(cudaGetDevice(&dev));
+    B200_CUDA_CHECK(cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev));
+  }
+  return n;
+}
+
+void rmsnorm_fwd(const __nv_bfloat16* x, const __nv_bfloat16* w, __nv_bfloat16* y, float* rstd, int rows, int d,
+                 float eps, cudaStream_t s) {
+  B200_CHECK(d % 8 == 0 && d <= 256 * 16, "rmsnorm: d must be a multiple of 8 and at most 4096");
+  const int blocks = (rows + kWarpsPerBlock - 1) / kWarpsPerBlock;
+  const int vec = (d + 255) / 256;
+  if (vec <= 1)
+    rmsnorm_fwd_kernel<1><<<blocks, 32 * kWarpsPerBlock, 0, s>>>(x, w, y, rstd, rows, d, eps);
+  else if (vec <= 2)
+    rmsnorm_fwd_kernel<2><<<blocks, 32 * kWarpsPerBlock, 0, s>>>(x, w, y, rstd, rows, d, eps);
+  else if (vec <= 4)
+    rmsnorm_fwd_kernel<4><<<blocks, 32 * kWarpsPerBlock, 0, s>>>(x, w, y, rstd, rows, d, eps);
+  else if (vec <= 8)
+    rmsnorm_fwd_kernel<8><<<blocks, 32 * kWarpsPerBlock, 0, s>>>(x, w, y, rstd, rows, d, eps);
+  else
+    rmsnorm_fwd_kernel<16><<<blocks, 32 * kWarpsPerBlock, 0, s>>>(x, w, y, rstd, rows, d, eps);
+  B200_CUDA_CHECK(cudaGetLastError());
+  count_launch();
+}
+
+void rmsnorm_bwd(const __nv_bfloat16* dy, const __nv_bfloat16* x, const __nv_bfloat16* w, const float* rstd,
+                 const __nv_bfloat16* dres, __nv_bfloat16* dx, float* dw, int rows, int d, cudaStream_t s) {
+  B200_CHECK(d % 8 == 0 && d <= 256 * 8, "rmsnorm_bwd: d must be a multiple of 8 and at most 2048");
+  const int blocks = std::max(1, std::min(num_sms_cached() * 2, (rows + kWarpsPerBlock - 1) / kWarpsPerBlock));
+  const int rows_per_block = (rows + blocks - 1) / blocks;
+  const int vec = (d + 255) / 256;
+  const int threads = 32 * kWarpsPerBlock;
+  if (vec <= 1)
+    rmsnorm_bwd_kernel<1><<<blocks, threads, 0, s>>>(dy, x, w, rstd, dres, dx, dw, rows, d, rows_per_block);
+  else if (vec <= 2)
+    rmsnorm_bwd_kernel<2><<<blocks, threads, 0, s>>>(dy, x, w, rstd, dres, dx, dw, rows, d, rows_per_block);
+  else if (vec <= 4)
+    rmsnorm_bwd_kernel<4><<<blocks, threads, 0, s>>>(dy, x, w, rstd, dres, dx, dw, rows, d, rows_per_block);
+  else
+    rmsnorm_bwd_kernel<8><<<blocks, threads, 0, s>>>(dy, x, w, rstd, dres, dx, dw, rows, d, rows_per_block);
+  B200_CUDA_CHECK(cudaGetLastError());
+  count_launch();
+}
+
+void embedding_fwd(const int64_t* ids, const __nv_bfloat16* table, __nv_bfloat16* out, int rows, int d, int vocab,
+                   cudaStream_t s) {
+  B200_CHECK(d % 8 == 0, "embedding: d must be a multiple of 8");
+  embedding_fwd_kernel<<<grid_for((size_t)rows * d / 8, 256), 256, 0, s>>>(ids, table, out, rows, d, vocab,
+                                                                            device_errors_ptr());
+  B200_CUDA_CHECK(cudaGetLastError());
+  count_launch();
+}
+
+void embedding_bwd(const int64_t* ids, const __nv_bfloat16* dy, float* dtable, int rows, int d, int vocab,
+                   cudaStream_t s) {
+  embedding_bwd_kernel<<<grid_for((size_t)rows * d / 8, 256), 256, 0, s>>>(ids, dy, dtable, rows, d, vocab);
+  B200_CUDA_CHECK(cudaGetLastError());
+  count_launch();
+}
+
+void rope_bwd(__nv_bfloat16* g, int rows, int ld, int rope_cols, int head_dim, int seq_len, const float* cosv,
+              const float* sinv, cudaStream_t s) {
+  B200_CHECK(head_dim % 16 == 0 && rope_cols % head_dim == 0, "rope_bwd: bad head layout");
+  const size_t work = (size_t)rows * (rope_cols / head_dim) * (head_dim / 16);
+  rope_bwd_kernel<<<grid_for(work, 256), 256, 0, s>>>(g, rows, ld, rope_cols, head_dim, seq_len, cosv, sinv);
+  B200_CUDA_CHECK(cudaGetLastError());
+  count_launch();
+}
+
+}  // namespace b200

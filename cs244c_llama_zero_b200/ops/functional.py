@@ -1,0 +1,354 @@
+"""Autograd functions of the B200 backend, built on the sm_100a kernels in ``_C``.
+
+Weight gradients are accumulated in fp32 directly into ``param.main_grad`` when the ZeRO
+engine has bound one (the flat gradient buffer); the function then returns ``None`` for that
+parameter so autograd never materialises a separate ``.grad`` tensor.  Without a bound
+``main_grad`` (plain model use) the gradient is returned to autograd as usual.
+
+Every function here requires CUDA tensors and the compiled extension; there is no eager
+fallback on this path.
+"""
+
+from __future__ import annotations
+
+import math
+from typing import Dict, List, Optional, Sequence, Tuple
+
+import torch
+
+from . import load_extension
+
+_C = None
+
+
+def _ext():
+    global _C
+    if _C is None:
+        _C = load_extension()
+    return _C
+
+
+def _require_cuda(*tensors: torch.Tensor) -> None:
+    for t in tensors:
+        if not t.is_cuda:
+            raise RuntimeError("the b200 backend runs on CUDA tensors only; use backend='torch' on CPU")
+
+
+# ------------------------------------------------------------------------------ helpers
+def fused_view(params: Sequence[torch.Tensor]) -> Optional[torch.Tensor]:
+    """A single [sum(rows), cols] view over row-concatenated 2-D tensors that are adjacent in memory."""
+    first = params[0]
+    cols = first.shape[1]
+    expected = first.data_ptr()
+    storage = first.untyped_storage().data_ptr()
+    for p in params:
+        if p.dim() != 2 or p.shape[1] != cols or not p.is_contiguous() or p.data_ptr() != expected:
+            return None
+        if p.untyped_storage().data_ptr() != storage:
+            return None
+        expected += p.numel() * p.element_size()
+    rows = sum(p.shape[0] for p in params)
+    return torch.as_strided(first, (rows, cols), (cols, 1))
+
+
+def fused_weight(params: Sequence[torch.Tensor]) -> torch.Tensor:
+    view = fused_view([p.detach() for p in params])
+    if view is not None:
+        return view
+    return torch.cat([p.detach() for p in params], dim=0)
+
+
+class _GradSink:
+    """fp32 accumulation target for the gradient of one (possibly fused) weight."""
+
+    def __init__(self, params: Sequence[torch.nn.Parameter]) -> None:
+        self.params = list(params)
+        self.buffer: Optional[torch.Tensor] = None
+        mains = [getattr(p, "main_grad", None) for p in self.params]
+        if all(m is not None for m in mains):
+            self.buffer = fused_view(mains) if len(mains) > 1 else mains[0].view(self.params[0].shape)
+            self.direct = self.buffer is not None
+        else:
+            self.direct = False
+        if self.buffer is None:
+            rows = sum(p.shape[0] for p in self.params)
+            shape = (rows,) + tuple(self.params[0].shape[1:])
+            self.buffer = torch.zeros(shape, dtype=torch.float32, device=self.params[0].device)
+
+    def finish(self) -> List[Optional[torch.Tensor]]:
+        """Per-parameter gradients to hand back to autograd (None when accumulated in place)."""
+        if self.direct:
+            return [None] * len(self.params)
+        out: List[Optional[torch.Tensor]] = []
+        row = 0
+        for p in self.params:
+            part = self.buffer[row : row + p.shape[0]] if self.buffer.dim() > 1 else self.buffer
+            row += p.shape[0] if self.buffer.dim() > 1 else 0
+            main = getattr(p, "main_grad", None)
+            if main is not None:
+                main.add_(part.view(p.shape))
+                out.append(None)
+            else:
+                out.append(part.view(p.shape).to(p.dtype))
+        return out
+
+
+_ROPE_CACHE: Dict[Tuple, Tuple[torch.Tensor, torch.Tensor]] = {}
+
+
+def rope_tables(seq_len: int, head_dim: int, theta: float, device: torch.device) -> Tuple[torch.Tensor, torch.Tensor]:
+    """fp32 ``cos``/``sin`` of ``pos * theta^(-2i/hd)`` with shape ``[seq_len, head_dim/2]``."""
+    key = (seq_len, head_dim, float(theta), str(device))
+    if key not in _ROPE_CACHE:
+        inv_freq = 1.0 / (theta ** (torch.arange(0, head_dim, 2, dtype=torch.float32) / head_dim))
+        angles = torch.outer(torch.arange(seq_len, dtype=torch.float32), inv_freq)
+        _ROPE_CACHE[key] = (angles.cos().to(device).contiguous(), angles.sin().to(device).contiguous())
+    return _ROPE_CACHE[key]
+
+
+# ------------------------------------------------------------------------------ RMSNorm
+class _RMSNormFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x: torch.Tensor, weight: torch.nn.Parameter, eps: float):
+        _require_cuda(x)
+        shape = x.shape
+        x2 = x.reshape(-1, shape[-1]).contiguous()
+        y = torch.empty_like(x2)
+        rstd = torch.empty(x2.shape[0], dtype=torch.float32, device=x.device)
+        _ext().rmsnorm_fwd(x2, weight.detach().contiguous(), y, rstd, eps)
+        ctx.save_for_backward(x2, rstd)
+        ctx.weight = weight
+        ctx.shape = shape
+        return y.view(shape)
+
+    @staticmethod
+    def backward(ctx, dy: torch.Tensor):
+        x2, rstd = ctx.saved_tensors
+        w = ctx.weight
+        dy2 = dy.reshape(x2.shape).contiguous()
+        dx = torch.empty_like(x2)
+        sink = _GradSink([w])
+        _ext().rmsnorm_bwd(dy2, x2, w.detach().contiguous(), rstd, None, dx, sink.buffer.view(-1))
+        return dx.view(ctx.shape), sink.finish()[0], None
+
+
+def rms_norm(x: torch.Tensor, weight: torch.nn.Parameter, eps: float) -> torch.Tensor:
+    return _RMSNormFn.apply(x, weight, eps)
+
+
+# ------------------------------------------------------------------------------ embedding
+class _EmbeddingFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, ids: torch.Tensor, weight: torch.nn.Parameter):
+        _require_cuda(ids, weight)
+        flat = ids.reshape(-1).contiguous()
+        out = torch.empty(flat.numel(), weight.shape[1], dtype=weight.dtype, device=weight.device)
+        _ext().embedding_fwd(flat, weight.detach(), out)
+        ctx.save_for_backward(flat)
+        ctx.weight = weight
+        return out.view(*ids.shape, weight.shape[1])
+
+    @staticmethod
+    def backward(ctx, dy: torch.Tensor):
+        (flat,) = ctx.saved_tensors
+        sink = _GradSink([ctx.weight])
+        _ext().embedding_bwd(flat, dy.reshape(flat.numel(), -1).contiguous(), sink.buffer)
+        return None, sink.finish()[0]
+
+
+def embedding(ids: torch.Tensor, weight: torch.nn.Parameter) -> torch.Tensor:
+    return _EmbeddingFn.apply(ids, weight)
+
+
+# ------------------------------------------------------------------------------ attention
+def attention_forward(qkv: torch.Tensor, batch: int, seq: int, heads: int, kv_heads: int, head_dim: int,
+                      out: Optional[torch.Tensor] = None) -> Tuple[torch.Tensor, torch.Tensor]:
+    """Causal GQA attention over the fused projection ``qkv = [q | k | v]`` -> (o [T, H*hd], lse2)."""
+    T = batch * seq
+    if out is None:
+        out = torch.empty(T, heads * head_dim, dtype=qkv.dtype, device=qkv.device)
+    lse = torch.empty(batch * heads * seq, dtype=torch.float32, device=qkv.device)
+    _ext().attention_fwd(qkv, heads * head_dim, (heads + kv_heads) * head_dim, out, lse, batch, seq, heads,
+                         kv_heads, head_dim, 1.0 / math.sqrt(head_dim))
+    return out, lse
+
+
+def attention_backward(qkv: torch.Tensor, out: torch.Tensor, dout: torch.Tensor, lse: torch.Tensor, batch: int,
+                       seq: int, heads: int, kv_heads: int, head_dim: int, dqkv: torch.Tensor,
+                       cos: torch.Tensor, sin: torch.Tensor) -> None:
+    """dqkv = gradient w.r.t. the *pre-RoPE* q|k|v projection (RoPE backward is fused)."""
+    T = batch * seq
+    delta = torch.empty(batch * heads * seq, dtype=torch.float32, device=qkv.device)
+    dq_acc = torch.zeros(T, heads * head_dim, dtype=torch.float32, device=qkv.device)
+    _ext().attention_bwd(qkv, heads * head_dim, (heads + kv_heads) * head_dim, out, dout.contiguous(), lse, delta,
+                         dq_acc, dqkv, cos, sin, batch, seq, heads, kv_heads, head_dim, 1.0 / math.sqrt(head_dim))
+
+
+# ------------------------------------------------------------------------------ transformer block
+class _BlockFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, w_in, wq, wk, wv, wo, w_post, wg, wu, wd, meta):
+        _require_cuda(x)
+        cfg, params = meta
+        B, S, d = x.shape
+        T = B * S
+        H, KV, hd, ffn = cfg.n_heads, cfg.n_kv_heads, cfg.head_dim, cfg.ffn_dim
+        eps = cfg.rms_norm_eps
+        C = _ext()
+        xf = x.reshape(T, d).contiguous()
+        w_qkv = fused_weight([wq, wk, wv])
+        w_gu = fused_weight([wg, wu])
+        cos, sin = rope_tables(S, hd, cfg.rope_theta, x.device)
+
+        h1 = torch.empty_like(xf)
+        rstd1 = torch.empty(T, dtype=torch.float32, device=x.device)
+        C.rmsnorm_fwd(xf, w_in.detach(), h1, rstd1, eps)
+        qkv = torch.empty(T, (H + 2 * KV) * hd, dtype=x.dtype, device=x.device)
+        C.qkv_rope_fwd(h1, w_qkv, qkv, cos, sin, S, hd, (H + KV) * hd)
+        attn, lse = attention_forward(qkv, B, S, H, KV, hd)
+        x2 = torch.empty_like(xf)
+        C.linear_fwd(attn, wo.detach(), x2, xf)
+        h2 = torch.empty_like(xf)
+        rstd2 = torch.empty(T, dtype=torch.float32, device=x.device)
+        C.rmsnorm_fwd(x2, w_post.detach(), h2, rstd2, eps)
+        act = torch.empty(T, ffn, dtype=x.dtype, device=x.device)
+        gu = torch.empty(T, 2 * ffn, dtype=x.dtype, device=x.device)
+        C.swiglu_fwd(h2, w_gu, act, gu)
+        x3 = torch.empty_like(xf)
+        C.linear_fwd(act, wd.detach(), x3, x2)
+
+        ctx.save_for_backward(xf, h1, rstd1, qkv, attn, lse, x2, h2, rstd2, gu, act)
+        ctx.cfg = cfg
+        ctx.params = params
+        ctx.shape = (B, S, d)
+        return x3.view(B, S, d)
+
+    @staticmethod
+    def backward(ctx, dy):
+        xf, h1, rstd1, qkv, attn, lse, x2, h2, rstd2, gu, act = ctx.saved_tensors
+        cfg = ctx.cfg
+        w_in, wq, wk, wv, wo, w_post, wg, wu, wd = ctx.params
+        B, S, d = ctx.shape
+        T = B * S
+        H, KV, hd, ffn = cfg.n_heads, cfg.n_kv_heads, cfg.head_dim, cfg.ffn_dim
+        C = _ext()
+        dy3 = dy.reshape(T, d).contiguous()
+        w_qkv = fused_weight([wq, wk, wv])
+        w_gu = fused_weight([wg, wu])
+        cos, sin = rope_tables(S, hd, cfg.rope_theta, dy.device)
+
+        # MLP: down projection (SwiGLU backward fused into its data-gradient epilogue)
+        dgu = torch.empty_like(gu)
+        C.swiglu_dgrad(dy3, wd.detach(), gu, dgu)
+        sink_d = _GradSink([wd])
+        C.linear_wgrad(dy3, act, sink_d.buffer)
+        dh2 = torch.empty_like(xf)
+        C.linear_dgrad(dgu, w_gu, dh2)
+        sink_gu = _GradSink([wg, wu])
+        C.linear_wgrad(dgu, h2, sink_gu.buffer)
+        del dgu
+        dx2 = torch.empty_like(xf)
+        sink_post = _GradSink([w_post])
+        C.rmsnorm_bwd(dh2, x2, w_post.detach(), rstd2, dy3, dx2, sink_post.buffer.view(-1))
+        # attention
+        dattn = torch.empty_like(attn)
+        C.linear_dgrad(dx2, wo.detach(), dattn)
+        sink_o = _GradSink([wo])
+        C.linear_wgrad(dx2, attn, sink_o.buffer)
+        dqkv = torch.empty_like(qkv)
+        attention_backward(qkv, attn, dattn, lse, B, S, H, KV, hd, dqkv, cos, sin)
+        dh1 = torch.empty_like(xf)
+        C.linear_dgrad(dqkv, w_qkv, dh1)
+        sink_qkv = _GradSink([wq, wk, wv])
+        C.linear_wgrad(dqkv, h1, sink_qkv.buffer)
+        dx = torch.empty_like(xf)
+        sink_in = _GradSink([w_in])
+        C.rmsnorm_bwd(dh1, xf, w_in.detach(), rstd1, dx2, dx, sink_in.buffer.view(-1))
+
+        g_qkv = sink_qkv.finish()
+        g_gu = sink_gu.finish()
+        return (dx.view(B, S, d), sink_in.finish()[0], g_qkv[0], g_qkv[1], g_qkv[2], sink_o.finish()[0],
+                sink_post.finish()[0], g_gu[0], g_gu[1], sink_d.finish()[0], None)
+
+
+def transformer_block(x: torch.Tensor, block) -> torch.Tensor:
+    a, m = block.attn, block.mlp
+    params = (block.input_norm.weight, a.q_proj.weight, a.k_proj.weight, a.v_proj.weight, a.o_proj.weight,
+              block.post_attn_norm.weight, m.gate_proj.weight, m.up_proj.weight, m.down_proj.weight)
+    return _BlockFn.apply(x, *params, (block.cfg, params))
+
+
+# ------------------------------------------------------------------------------ LM head + CE
+def shifted_targets(labels: torch.Tensor) -> torch.Tensor:
+    """``targets[b, s] = labels[b, s+1]`` and ``-100`` at the last position of every row."""
+    tgt = torch.full_like(labels, -100)
+    tgt[:, :-1] = labels[:, 1:]
+    return tgt.reshape(-1).contiguous()
+
+
+class _LMHeadCEFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x: torch.Tensor, weight: torch.nn.Parameter, labels: torch.Tensor):
+        _require_cuda(x, weight)
+        B, S, d = x.shape
+        T = B * S
+        V = weight.shape[0]
+        C = _ext()
+        xf = x.reshape(T, d).contiguous()
+        targets = shifted_targets(labels)
+        logits = torch.empty(T, V, dtype=x.dtype, device=x.device)
+        C.linear_fwd(xf, weight.detach(), logits, None)
+        lse = torch.empty(T, dtype=torch.float32, device=x.device)
+        scratch = torch.empty(3, dtype=torch.float32, device=x.device)
+        loss_sum, count, loss = scratch[0:1], scratch[1:2], scratch[2:3]
+        C.cross_entropy_fwd(logits, targets, lse, loss_sum, count, loss)
+        ctx.save_for_backward(xf, logits, targets, lse, scratch)
+        ctx.weight = weight
+        ctx.shape = (B, S, d)
+        return loss.view(())
+
+    @staticmethod
+    def backward(ctx, grad_loss: torch.Tensor):
+        xf, logits, targets, lse, scratch = ctx.saved_tensors
+        C = _ext()
+        g = grad_loss.reshape(1).to(torch.float32).contiguous()
+        C.cross_entropy_bwd(logits, targets, lse, g, scratch[1:2])
+        w = ctx.weight
+        dx = torch.empty_like(xf)
+        C.linear_dgrad(logits, w.detach(), dx)
+        sink = _GradSink([w])
+        C.linear_wgrad(logits, xf, sink.buffer)
+        return dx.view(ctx.shape), sink.finish()[0], None
+
+
+def lm_head_cross_entropy(x: torch.Tensor, weight: torch.nn.Parameter, labels: torch.Tensor) -> torch.Tensor:
+    return _LMHeadCEFn.apply(x, weight, labels)
+
+
+# ------------------------------------------------------------------------------ optimizer
+def adamw_step(master, exp_avg, exp_avg_sq, grad, param_out, lr, beta1, beta2, eps, weight_decay, step,
+               grad_scale=None) -> None:
+    scale_t, scale_c = None, 1.0
+    if isinstance(grad_scale, torch.Tensor):
+        scale_t = grad_scale.reshape(1).to(torch.float32)
+    elif grad_scale is not None:
+        scale_c = float(grad_scale)
+    out = param_out.reshape(-1) if param_out is not None else None
+    _ext().adamw(master.reshape(-1), exp_avg.reshape(-1), exp_avg_sq.reshape(-1), grad.reshape(-1).float()
+                 if grad.dtype != torch.float32 else grad.reshape(-1), out, scale_t, scale_c, lr, beta1, beta2,
+                 eps, weight_decay, step)
+
+
+def sum_squares(t: torch.Tensor) -> torch.Tensor:
+    out = torch.empty(1, dtype=torch.float32, device=t.device)
+    _ext().sum_squares(t.reshape(-1).contiguous(), out)
+    return out.reshape(())
+
+
+def device_errors() -> List[int]:
+    """[code, where, block, count] recorded by kernels whose bounded waits expired."""
+    return list(_ext().read_device_errors())
+
+
+def reset_device_errors() -> None:
+    _ext().reset_device_errors()

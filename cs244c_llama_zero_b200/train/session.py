@@ -1,0 +1,153 @@
+"""Training-session API: one object that owns the process group, model, collectives and
+ZeRO engine, and runs one optimizer step per call.
+
+This is the public entry point a user (and the benchmark) calls::
+
+    from cs244c_llama_zero_b200.train import TrainSession, SessionConfig
+    sess = TrainSession(SessionConfig(model_size="baseline-small", zero_stage=2, batch_size=8, seq_len=1024))
+    loss = sess.train_step(input_ids)          # input_ids: int64 [B, S] on the host or the device
+    print(float(loss))
+
+Semantics follow the reference's ``train_zero.py`` step (``train_zero.py:416-589``):
+zero_grad -> prepare_forward -> for each micro-batch: forward under bf16 autocast with labels ==
+inputs (the model shifts them), backward(loss / grad_accum) -> optimizer step.  Inputs given on
+the host are copied with a non-blocking H2D transfer from pinned memory.
+"""
+
+from __future__ import annotations
+
+import os
+from dataclasses import dataclass, field
+from datetime import timedelta
+from typing import Optional, Sequence, Tuple
+
+import torch
+import torch.distributed as dist
+
+from ..models import BASELINE_VOCAB_SIZE, LlamaForCausalLM, ModelConfig, build_config
+from ..parallel.collectives import TracingCollectives, pick_collectives
+from ..parallel.zero import ENGINES
+
+
+@dataclass
+class SessionConfig:
+    model_size: str = "baseline-small"
+    vocab_size: int = BASELINE_VOCAB_SIZE
+    seq_len: int = 1024
+    batch_size: int = 8
+    grad_accum_steps: int = 1
+    zero_stage: int = 0
+    collective_impl: str = "torch"
+    dtype: str = "bfloat16"
+    backend: str = "auto"  # "b200" on CUDA, "torch" on CPU
+    learning_rate: float = 3e-4
+    weight_decay: float = 0.1
+    betas: Tuple[float, float] = (0.9, 0.95)
+    eps: float = 1e-8
+    max_grad_norm: float = 0.0
+    seed: int = 1337
+    loss_chunk_size: int = 128
+    activation_checkpointing: bool = False
+    profile_collectives: bool = False
+    model_overrides: dict = field(default_factory=dict)
+    pg_timeout_s: float = 600.0
+
+
+def init_distributed(timeout_s: float = 600.0) -> Tuple[int, int, torch.device]:
+    """torchrun environment -> (rank, world, device); NCCL on CUDA, Gloo on CPU."""
+    if "RANK" not in os.environ or "WORLD_SIZE" not in os.environ:
+        return 0, 1, torch.device("cuda" if torch.cuda.is_available() else "cpu")
+    rank = int(os.environ["RANK"])
+    world = int(os.environ["WORLD_SIZE"])
+    local_rank = int(os.environ.get("LOCAL_RANK", rank))
+    if torch.cuda.is_available():
+        torch.cuda.set_device(local_rank)
+        device = torch.device("cuda", local_rank)
+        if not dist.is_initialized():
+            dist.init_process_group(backend="nccl", timeout=timedelta(seconds=timeout_s), device_id=device)
+    else:
+        device = torch.device("cpu")
+        if not dist.is_initialized():
+            dist.init_process_group(backend="gloo", timeout=timedelta(seconds=timeout_s))
+    return rank, world, device
+
+
+def model_param_dtype(device: torch.device, dtype_name: str) -> torch.dtype:
+    if device.type != "cuda" or dtype_name == "float32":
+        return torch.float32
+    return torch.bfloat16
+
+
+def broadcast_model(model: torch.nn.Module) -> None:
+    if dist.is_available() and dist.is_initialized() and dist.get_world_size() > 1:
+        for p in model.parameters():
+            dist.broadcast(p.data, src=0)
+
+
+class TrainSession:
+    def __init__(self, cfg: SessionConfig, model_cfg: Optional[ModelConfig] = None) -> None:
+        self.cfg = cfg
+        self.rank, self.world_size, self.device = init_distributed(cfg.pg_timeout_s)
+        torch.manual_seed(cfg.seed)
+        if self.device.type == "cuda":
+            torch.cuda.manual_seed_all(cfg.seed)
+            torch.backends.cuda.matmul.allow_tf32 = True
+            torch.backends.cudnn.allow_tf32 = True
+        self.model_cfg = model_cfg or build_config(cfg.model_size, vocab_size=cfg.vocab_size, max_seq_len=cfg.seq_len,
+                                                   **cfg.model_overrides)
+        backend = cfg.backend
+        if backend == "auto":
+            backend = "b200" if self.device.type == "cuda" else "torch"
+        self.backend = backend
+        dtype = model_param_dtype(self.device, cfg.dtype)
+        self.model = LlamaForCausalLM(self.model_cfg).to(device=self.device, dtype=dtype)
+        self.model.set_loss_chunk_size(cfg.loss_chunk_size)
+        self.model.set_activation_checkpointing(cfg.activation_checkpointing)
+        self.model.set_backend(backend)
+        broadcast_model(self.model)
+        collectives = pick_collectives(self.world_size, cfg.collective_impl, self.device)
+        if cfg.profile_collectives:
+            collectives = TracingCollectives(collectives)
+        self.collectives = collectives
+        self.engine = ENGINES[cfg.zero_stage](
+            model=self.model, lr=cfg.learning_rate, betas=cfg.betas, eps=cfg.eps, weight_decay=cfg.weight_decay,
+            collectives=collectives,
+        )
+        self._staging: Optional[torch.Tensor] = None
+        self.autocast = dtype == torch.bfloat16
+
+    # ----------------------------------------------------------------------------- steps
+    def _to_device(self, input_ids: torch.Tensor) -> torch.Tensor:
+        if input_ids.device == self.device:
+            return input_ids
+        if self._staging is None or self._staging.shape != input_ids.shape:
+            self._staging = torch.empty(input_ids.shape, dtype=torch.long, device=self.device)
+        self._staging.copy_(input_ids, non_blocking=True)
+        return self._staging
+
+    def forward_backward(self, micro_batches: Sequence[torch.Tensor]) -> torch.Tensor:
+        """Run every micro-batch; returns the mean loss as a device scalar (no host sync)."""
+        total = torch.zeros((), dtype=torch.float32, device=self.device)
+        n = len(micro_batches)
+        for ids in micro_batches:
+            ids = self._to_device(ids)
+            with torch.autocast(device_type=self.device.type, dtype=torch.bfloat16, enabled=self.autocast):
+                loss = self.model(input_ids=ids, labels=ids, return_logits=False).loss
+            self.engine.backward(loss / n)
+            total = total + loss.detach().float()
+        return total / n
+
+    def train_step(self, input_ids: torch.Tensor) -> torch.Tensor:
+        """One optimizer step on ``input_ids`` ([grad_accum * B, S] or [B, S]); returns the loss (device)."""
+        micro = list(input_ids.chunk(self.cfg.grad_accum_steps, dim=0)) if self.cfg.grad_accum_steps > 1 else [input_ids]
+        self.model.train()
+        self.engine.zero_grad()
+        self.engine.prepare_forward()
+        loss = self.forward_backward(micro)
+        self.engine.step_async(max_grad_norm=self.cfg.max_grad_norm)
+        return loss
+
+    def close(self) -> None:
+        if dist.is_available() and dist.is_initialized():
+            dist.barrier()
+            dist.destroy_process_group()

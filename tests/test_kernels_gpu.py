@@ -1,0 +1,235 @@
+"""Numerics of every sm_100a kernel against a plain PyTorch fp32 reference of the same op."""
+
+from __future__ import annotations
+
+import math
+
+import pytest
+import torch
+import torch.nn.functional as F
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def C():
+    from cs244c_llama_zero_b200 import ops
+
+    ext = ops.load_extension()
+    ext.reset_device_errors()
+    yield ext
+    assert list(ext.read_device_errors()) == [0, 0, 0, 0], "a kernel's bounded wait expired"
+
+
+def _bf(*shape, scale=1.0, seed=0):
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    return (torch.randn(*shape, device="cuda", generator=g) * scale).to(torch.bfloat16)
+
+
+def _close(a, b, tol):
+    a32, b32 = a.float(), b.float()
+    err = (a32 - b32).abs().max().item()
+    ref = b32.abs().max().item() + 1e-6
+    assert err <= tol * ref, f"max abs err {err:.4g} vs ref scale {ref:.4g}"
+
+
+@pytest.mark.parametrize("M,N,K,bn", [(256, 512, 128, 256), (300, 264, 136, 128), (1024, 1280, 768, 256),
+                                      (128, 768, 2048, 256)])
+def test_linear_fwd(C, M, N, K, bn):
+    x, w = _bf(M, K, seed=1), _bf(N, K, scale=0.05, seed=2)
+    out = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+    C.linear_fwd(x, w, out, None, bn)
+    _close(out, x.float() @ w.float().t(), 2e-2)
+    res = _bf(M, N, seed=3)
+    C.linear_fwd(x, w, out, res, bn)
+    _close(out, res.float() + x.float() @ w.float().t(), 2e-2)
+
+
+@pytest.mark.parametrize("M,N,K", [(256, 768, 512), (200, 136, 264), (1024, 768, 2048)])
+def test_linear_dgrad(C, M, N, K):
+    dy, w = _bf(M, N, seed=4), _bf(N, K, scale=0.05, seed=5)
+    dx = torch.empty(M, K, device="cuda", dtype=torch.bfloat16)
+    C.linear_dgrad(dy, w, dx, 0)
+    _close(dx, dy.float() @ w.float(), 2e-2)
+
+
+@pytest.mark.parametrize("M,N,K,splits", [(512, 384, 256, 1), (1024, 768, 1280, 4), (300, 136, 200, 0)])
+def test_linear_wgrad_accumulates(C, M, N, K, splits):
+    dy, x = _bf(M, N, seed=6), _bf(M, K, seed=7)
+    dw = torch.ones(N, K, device="cuda", dtype=torch.float32)
+    C.linear_wgrad(dy, x, dw, splits, 0)
+    _close(dw, 1.0 + dy.float().t() @ x.float(), 1e-2)
+
+
+def _rope_ref(t, S, hd, theta):
+    inv = 1.0 / (theta ** (torch.arange(0, hd, 2, device="cuda").float() / hd))
+    ang = torch.outer(torch.arange(S, device="cuda").float(), inv)
+    cos, sin = torch.cat([ang.cos()] * 2, -1), torch.cat([ang.sin()] * 2, -1)
+    B = t.shape[0] // S
+    tt = t.view(B, S, -1, hd)
+    rot = torch.cat([-tt[..., hd // 2:], tt[..., : hd // 2]], -1)
+    return (tt * cos[None, :, None] + rot * sin[None, :, None]).view_as(t)
+
+
+@pytest.mark.parametrize("hd,H,KV", [(64, 4, 2), (128, 4, 2)])
+def test_qkv_rope_epilogue(C, hd, H, KV):
+    from cs244c_llama_zero_b200.ops.functional import rope_tables
+
+    B, S, d = 2, 256, 256
+    x, w = _bf(B * S, d, seed=8), _bf((H + 2 * KV) * hd, d, scale=0.05, seed=9)
+    cos, sin = rope_tables(S, hd, 10000.0, x.device)
+    out = torch.empty(B * S, (H + 2 * KV) * hd, device="cuda", dtype=torch.bfloat16)
+    C.qkv_rope_fwd(x, w, out, cos, sin, S, hd, (H + KV) * hd)
+    full = x.float() @ w.float().t()
+    qk = full[:, : (H + KV) * hd]
+    ref = torch.cat([_rope_ref(qk.contiguous(), S, hd, 10000.0), full[:, (H + KV) * hd:]], 1)
+    _close(out, ref, 2e-2)
+    # RoPE backward kernel = exact inverse rotation
+    g = out.clone()
+    C.rope_bwd(g, (H + KV) * hd, hd, S, cos, sin)
+    _close(g, full, 3e-2)
+
+
+def test_swiglu_forward_and_backward_epilogues(C):
+    M, d, ffn = 384, 256, 512
+    x, w_gu, w_down = _bf(M, d, seed=10), _bf(2 * ffn, d, scale=0.05, seed=11), _bf(d, ffn, scale=0.05, seed=12)
+    h = torch.empty(M, ffn, device="cuda", dtype=torch.bfloat16)
+    gu = torch.empty(M, 2 * ffn, device="cuda", dtype=torch.bfloat16)
+    C.swiglu_fwd(x, w_gu, h, gu)
+    g_ref = x.float() @ w_gu[:ffn].float().t()
+    u_ref = x.float() @ w_gu[ffn:].float().t()
+    _close(gu[:, :ffn], g_ref, 2e-2)
+    _close(gu[:, ffn:], u_ref, 2e-2)
+    _close(h, F.silu(g_ref) * u_ref, 3e-2)
+    dy = _bf(M, d, seed=13)
+    dgu = torch.empty_like(gu)
+    C.swiglu_dgrad(dy, w_down, gu, dgu)
+    g, u = gu[:, :ffn].float(), gu[:, ffn:].float()
+    da = dy.float() @ w_down.float()
+    sig = torch.sigmoid(g)
+    _close(dgu[:, :ffn], da * u * sig * (1 + g * (1 - sig)), 3e-2)
+    _close(dgu[:, ffn:], da * g * sig, 3e-2)
+
+
+@pytest.mark.parametrize("d", [256, 768, 2048])
+def test_rmsnorm(C, d):
+    T = 333
+    x, w = _bf(T, d, seed=14), (1 + 0.1 * _bf(d, seed=15).float()).to(torch.bfloat16)
+    y = torch.empty_like(x)
+    rstd = torch.empty(T, device="cuda")
+    C.rmsnorm_fwd(x, w, y, rstd, 1e-5)
+    xf = x.float().requires_grad_()
+    wf = w.float().requires_grad_()
+    ref = xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + 1e-5) * wf
+    _close(y, ref, 1e-2)
+    dy, dres = _bf(T, d, seed=16), _bf(T, d, seed=17)
+    ref.backward(dy.float())
+    dx = torch.empty_like(x)
+    dw = torch.zeros(d, device="cuda")
+    C.rmsnorm_bwd(dy, x, w, rstd, dres, dx, dw)
+    _close(dx, xf.grad + dres.float(), 2e-2)
+    _close(dw, wf.grad, 1e-2)
+
+
+def test_embedding(C):
+    V, d, T = 1000, 256, 777
+    table = _bf(V, d, seed=18)
+    ids = torch.randint(0, V, (T,), device="cuda")
+    out = torch.empty(T, d, device="cuda", dtype=torch.bfloat16)
+    C.embedding_fwd(ids, table, out)
+    assert torch.equal(out, table[ids])
+    dy = _bf(T, d, seed=19)
+    dt = torch.zeros(V, d, device="cuda")
+    C.embedding_bwd(ids, dy, dt)
+    ref = torch.zeros(V, d, device="cuda").index_add_(0, ids, dy.float())
+    _close(dt, ref, 1e-5)
+
+
+def test_adamw_matches_reference_math(C):
+    n = 10_003
+    g = torch.Generator(device="cuda").manual_seed(20)
+    master = torch.randn(n, device="cuda", generator=g)
+    m, v = torch.randn(n, device="cuda", generator=g) * 0.1, torch.rand(n, device="cuda", generator=g) * 0.01
+    grad = torch.randn(n, device="cuda", generator=g)
+    ref = [t.clone() for t in (master, m, v)]
+    out = torch.empty(n, device="cuda", dtype=torch.bfloat16)
+    scale = torch.tensor([0.5], device="cuda")
+    lr, b1, b2, eps, wd, step = 1e-3, 0.9, 0.95, 1e-8, 0.1, 3
+    C.adamw(master, m, v, grad, out, scale, 1.0, lr, b1, b2, eps, wd, step)
+    pm, mm, vv = ref
+    gg = grad * 0.5
+    mm.mul_(b1).add_(gg, alpha=1 - b1)
+    vv.mul_(b2).addcmul_(gg, gg, value=1 - b2)
+    pm.mul_(1 - lr * wd)
+    denom = vv.sqrt() / math.sqrt(1 - b2 ** step) + eps
+    pm.addcdiv_(mm, denom, value=-lr / (1 - b1 ** step))
+    torch.testing.assert_close(master, pm, atol=1e-6, rtol=1e-5)
+    torch.testing.assert_close(m, mm, atol=1e-7, rtol=1e-6)
+    torch.testing.assert_close(v, vv, atol=1e-7, rtol=1e-6)
+    torch.testing.assert_close(out.float(), pm, atol=1e-2, rtol=1e-2)
+
+
+def test_sum_squares(C):
+    x = torch.randn(1_000_001, device="cuda")
+    out = torch.empty(1, device="cuda")
+    C.sum_squares(x, out)
+    torch.testing.assert_close(out[0], (x.double() ** 2).sum().float(), rtol=1e-4, atol=1e-3)
+
+
+def test_cross_entropy(C):
+    T, V = 300, 4000
+    logits = _bf(T, V, scale=2.0, seed=21)
+    targets = torch.randint(0, V, (T,), device="cuda")
+    targets[::7] = -100
+    lse = torch.empty(T, device="cuda")
+    scratch = torch.empty(3, device="cuda")
+    C.cross_entropy_fwd(logits, targets, lse, scratch[0:1], scratch[1:2], scratch[2:3])
+    lf = logits.float().requires_grad_()
+    ref = F.cross_entropy(lf, targets, ignore_index=-100)
+    torch.testing.assert_close(scratch[2], ref.detach(), rtol=1e-4, atol=1e-4)
+    ref.backward()
+    g = torch.tensor([1.0], device="cuda")
+    work = logits.clone()
+    C.cross_entropy_bwd(work, targets, lse, g, scratch[1:2])
+    _close(work, lf.grad, 1e-2)
+
+
+def _attn_ref(qkv, B, S, H, KV, hd):
+    q = qkv[:, : H * hd].view(B, S, H, hd).transpose(1, 2)
+    k = qkv[:, H * hd : (H + KV) * hd].view(B, S, KV, hd).transpose(1, 2)
+    v = qkv[:, (H + KV) * hd :].view(B, S, KV, hd).transpose(1, 2)
+    rep = H // KV
+    k, v = k.repeat_interleave(rep, 1), v.repeat_interleave(rep, 1)
+    s = (q @ k.transpose(-1, -2)) / math.sqrt(hd)
+    s = s.masked_fill(torch.ones(S, S, device=qkv.device, dtype=torch.bool).triu(1), float("-inf"))
+    o = torch.softmax(s, -1) @ v
+    return o.transpose(1, 2).reshape(B * S, H * hd)
+
+
+@pytest.mark.parametrize("B,S,H,KV,hd", [(2, 256, 4, 2, 64), (1, 512, 4, 4, 128), (2, 384, 6, 2, 64),
+                                         (1, 256, 4, 2, 128)])
+def test_attention_forward_and_backward(C, B, S, H, KV, hd):
+    from cs244c_llama_zero_b200.ops.functional import attention_backward, attention_forward, rope_tables
+
+    qkv = _bf(B * S, (H + 2 * KV) * hd, seed=22)
+    out, lse = attention_forward(qkv, B, S, H, KV, hd)
+    qf = qkv.float().requires_grad_()
+    ref = _attn_ref(qf, B, S, H, KV, hd)
+    _close(out, ref, 2e-2)
+    dout = _bf(B * S, H * hd, seed=23)
+    ref.backward(dout.float())
+    # The backward kernel also applies RoPE backward to dq/dk: compare through an identity rotation.
+    cos = torch.ones(S, hd // 2, device="cuda")
+    sin = torch.zeros(S, hd // 2, device="cuda")
+    dqkv = torch.empty_like(qkv)
+    attention_backward(qkv, out, dout, lse, B, S, H, KV, hd, dqkv, cos, sin)
+    _close(dqkv[:, : H * hd], qf.grad[:, : H * hd], 3e-2)
+    _close(dqkv[:, H * hd : (H + KV) * hd], qf.grad[:, H * hd : (H + KV) * hd], 3e-2)
+    _close(dqkv[:, (H + KV) * hd :], qf.grad[:, (H + KV) * hd :], 3e-2)
+    # With a real rotation the result equals R^T applied to the identity-rotation gradient.
+    cos, sin = rope_tables(S, hd, 10000.0, qkv.device)
+    dqkv_rot = torch.empty_like(qkv)
+    attention_backward(qkv, out, dout, lse, B, S, H, KV, hd, dqkv_rot, cos, sin)
+    expect = dqkv.clone()
+    C.rope_bwd(expect, (H + KV) * hd, hd, S, cos, sin)
+    _close(dqkv_rot[:, : (H + KV) * hd], expect[:, : (H + KV) * hd], 2e-2)
