@@ -5,15 +5,20 @@
 //
 //   S^T  = K_j Q_i^T           (M = kv, N = q,  K = hd)   tensor memory
 //   dP^T = V_j dO_i^T          (M = kv, N = q,  K = hd)   tensor memory
-//   P^T  = exp2(S^T * scale*log2e - lse2[q]),  dS^T = P^T * (dP^T - delta[q])   (one kv row / thread)
+//   P^T  = exp2(S^T * scale*log2e - lse2[q]),  dS^T = P^T * (dP^T - delta[q])
 //   dV  += P^T dO_i            (M = kv, N = hd, K = q)    accumulated in tensor memory over the loop
 //   dK  += dS^T Q_i            (M = kv, N = hd, K = q)    accumulated in tensor memory over the loop
 //   dQ_i = dS K_j              (M = q,  N = hd, K = kv)   A operand = the same dS^T bytes read MN-major
 //   dq_acc[q rows] += scale * dQ_i                        fp32 vector atomics (summed over j)
 //
-// Epilogues: dK (times the softmax scale, RoPE backward applied) and dV are written as bf16 straight
-// into the k / v columns of the fused q|k|v gradient; a small kernel converts dq_acc into the q
-// columns with RoPE backward.  delta = rowsum(dO * O) comes from a pre-pass.
+// 320 threads: warp 0 TMA, warp 1 tensor-memory allocation + MMA issue, warps 2..9 two compute
+// warpgroups.  Thread (wg, r) owns kv row r and the query columns [64*wg, 64*wg+64) of S^T / dP^T,
+// then the output columns [wg*hd/2, (wg+1)*hd/2) of dQ / dV and its half of the RoPE pairs of dK.
+// lse2 / delta are read with warp-uniform (broadcast) vector loads, so the compute warps never
+// need a block-level barrier.  Epilogues: dK (times the softmax scale, RoPE backward applied) and
+// dV are written as bf16 straight into the k / v columns of the fused q|k|v gradient; a small
+// kernel converts dq_acc into the q columns with RoPE backward.  delta = rowsum(dO * O) comes
+// from a pre-pass.
 #include <cuda.h>
 
 #include "common.cuh"
@@ -24,7 +29,7 @@ namespace b200 {
 
 namespace {
 
-constexpr int BWD_THREADS = 192;
+constexpr int BWD_THREADS = 320;
 
 template <int HD>
 struct AttnBwdCfg {
@@ -36,17 +41,16 @@ struct AttnBwdCfg {
   static constexpr int QD_OFF = 2 * TILE;       // stages of (Q_i, dO_i)
   static constexpr int PT_OFF = QD_OFF + STAGES * 2 * TILE;
   static constexpr int DST_OFF = PT_OFF + 128 * 128 * 2;
-  static constexpr int VEC_OFF = DST_OFF + 128 * 128 * 2;  // lse2[128], delta[128]
-  static constexpr int BAR_OFF = VEC_OFF + 2 * 128 * 4;
+  static constexpr int BAR_OFF = DST_OFF + 128 * 128 * 2;
   static constexpr int SMEM_BYTES = BAR_OFF + 256 + 1024;
   // tensor-memory columns
   static constexpr int T_ST = 0, T_DPT = 128, T_DV = 256, T_DK = 256 + HD;
   static constexpr int T_DQ = (HD == 64) ? 384 : 0;
   static constexpr int TMEM_COLS = 512;
+  static constexpr int HALF = HD / 2;
 };
 
 __device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
-__device__ __forceinline__ void compute_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
 
 __device__ __forceinline__ void store_swizzled_row(uint8_t* base, int r, int c, const uint32_t (&pk)[16]) {
   // 32 bf16 values (columns c .. c+31) of row r of a [128 x 128] K-major SW128 tile.
@@ -57,6 +61,16 @@ __device__ __forceinline__ void store_swizzled_row(uint8_t* base, int r, int c, 
     const int sw = chunk ^ (r & 7);
     *reinterpret_cast<uint4*>(base + kblk * 16384 + r * 128 + sw * 16) =
         make_uint4(pk[4 * ch], pk[4 * ch + 1], pk[4 * ch + 2], pk[4 * ch + 3]);
+  }
+}
+
+template <int N>
+__device__ __forceinline__ void tmem_ld_cols(uint32_t taddr, uint32_t (&r)[N]) {
+  if constexpr (N == 32) {
+    tmem_ld_32x32b_x32(taddr, r);
+  } else {
+    static_assert(N == 16, "16 or 32 columns");
+    tmem_ld_32x32b_x16(taddr, r);
   }
 }
 
@@ -77,8 +91,6 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
   uint64_t* dq_free = dq_full + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(dq_free + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  float* s_lse = reinterpret_cast<float*>(smem + C::VEC_OFF);
-  float* s_delta = s_lse + 128;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int j = blockIdx.x;  // kv block (j = 0 has the most work and starts first)
@@ -96,9 +108,9 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
       mbar_init(&q_empty[s], 1);
     }
     mbar_init(st_full, 1);
-    mbar_init(p_ready, 4);
+    mbar_init(p_ready, 8);
     mbar_init(dq_full, 1);
-    mbar_init(dq_free, 4);
+    mbar_init(dq_free, 8);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -191,9 +203,10 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
       }
     }
   } else {
+    const int wg = (warp - 2) >> 2;  // columns [64*wg, 64*wg + 64) of S^T / dP^T
     const int q4 = warp & 3;
-    const int r = q4 * 32 + lane;  // kv row for S^T / dK / dV; query row for dQ
-    const int tid = threadIdx.x - 64;
+    const int r = q4 * 32 + lane;    // kv row for S^T / dK / dV; query row for dQ
+    const int col0 = wg * 64;
     const uint32_t lane_base = tmem + ((uint32_t)(q4 * 32) << 16);
     const float scale2 = p.scale * 1.4426950408889634f;
     uint8_t* pt = smem + C::PT_OFF;
@@ -202,21 +215,27 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
     for (int it = 0; it < n_it && ok; ++it) {
       const int h = kvh * group + it / n_q;
       const int i = j + it % n_q;
-      const size_t vec_base = ((size_t)b * p.heads + h) * p.seq + (size_t)i * 128;
-      s_lse[tid] = p.lse[vec_base + tid];
-      s_delta[tid] = p.delta[vec_base + tid];
-      compute_bar();
+      const size_t vec_base = ((size_t)b * p.heads + h) * p.seq + (size_t)i * 128 + col0;
       if (!mbar_wait_bounded(st_full, it & 1, abort_flag, errs, kErrAttnWait, 16)) {
         ok = false;
         break;
       }
       tc_fence_after();
       const bool diag = (i == j);
-#pragma unroll 1
-      for (int c = 0; c < 128; c += 32) {
+#pragma unroll
+      for (int c = 0; c < 64; c += 32) {
         uint32_t sv[32], dpv[32];
-        tmem_ld_32x32b_x32(lane_base + C::T_ST + c, sv);
-        tmem_ld_32x32b_x32(lane_base + C::T_DPT + c, dpv);
+        tmem_ld_32x32b_x32(lane_base + C::T_ST + col0 + c, sv);
+        tmem_ld_32x32b_x32(lane_base + C::T_DPT + col0 + c, dpv);
+        float lse_v[32], del_v[32];
+        const float4* l4 = reinterpret_cast<const float4*>(p.lse + vec_base + c);
+        const float4* d4 = reinterpret_cast<const float4*>(p.delta + vec_base + c);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const float4 a = __ldg(l4 + e), dd = __ldg(d4 + e);
+          lse_v[4 * e] = a.x; lse_v[4 * e + 1] = a.y; lse_v[4 * e + 2] = a.z; lse_v[4 * e + 3] = a.w;
+          del_v[4 * e] = dd.x; del_v[4 * e + 1] = dd.y; del_v[4 * e + 2] = dd.z; del_v[4 * e + 3] = dd.w;
+        }
         tc_wait_ld();
         uint32_t pk[16], dk[16];
 #pragma unroll
@@ -224,33 +243,32 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
           float pv[2], dv[2];
 #pragma unroll
           for (int t = 0; t < 2; ++t) {
-            const int qc = c + e + t;
-            const bool masked = diag && (qc < r);
-            const float pr = masked ? 0.f : exp2f(__uint_as_float(sv[e + t]) * scale2 - s_lse[qc]);
+            float pr = ex2_approx(fmaf(__uint_as_float(sv[e + t]), scale2, -lse_v[e + t]));
+            if (diag && (col0 + c + e + t < r)) pr = 0.f;
             pv[t] = pr;
-            dv[t] = pr * (__uint_as_float(dpv[e + t]) - s_delta[qc]);
+            dv[t] = pr * (__uint_as_float(dpv[e + t]) - del_v[e + t]);
           }
           pk[e >> 1] = pack_bf16(pv[0], pv[1]);
           dk[e >> 1] = pack_bf16(dv[0], dv[1]);
         }
-        store_swizzled_row(pt, r, c, pk);
-        store_swizzled_row(dst, r, c, dk);
+        store_swizzled_row(pt, r, col0 + c, pk);
+        store_swizzled_row(dst, r, col0 + c, dk);
       }
       fence_async_smem();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(p_ready);
-      // dQ_i rows (thread = query row r of block i)
+      // dQ_i rows (thread = query row r of block i), this warpgroup's half of the columns
       if (!mbar_wait_bounded(dq_full, it & 1, abort_flag, errs, kErrAttnWait, 17)) {
         ok = false;
         break;
       }
       tc_fence_after();
-      float* dq_row = p.dq_acc + (size_t)(row0 + i * 128 + r) * (p.heads * HD) + h * HD;
-#pragma unroll 1
-      for (int c = 0; c < HD; c += 32) {
+      float* dq_row = p.dq_acc + (size_t)(row0 + i * 128 + r) * (p.heads * HD) + h * HD + wg * C::HALF;
+#pragma unroll
+      for (int c = 0; c < C::HALF; c += 32) {
         uint32_t qv[32];
-        tmem_ld_32x32b_x32(lane_base + C::T_DQ + c, qv);
+        tmem_ld_32x32b_x32(lane_base + C::T_DQ + wg * C::HALF + c, qv);
         tc_wait_ld();
 #pragma unroll
         for (int e = 0; e < 32; e += 4) {
@@ -262,20 +280,20 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(dq_free);
-      compute_bar();  // lse/delta of this iteration no longer needed
     }
     if (ok && n_it > 0) {
       // The last dq_full also covers the final dV / dK accumulation.
       tc_fence_after();
       const int kv_row = row0 + j * 128 + r;
       const int pos = j * 128 + r;
-      const int half = HD / 2;
+      constexpr int HALF = C::HALF;
+      constexpr int QTR = HALF / 2;  // RoPE pairs per warpgroup
       __nv_bfloat16* dk_out = p.dqkv + (size_t)kv_row * p.ld + p.k_col + kvh * HD;
-      __nv_bfloat16* dv_out = p.dqkv + (size_t)kv_row * p.ld + p.v_col + kvh * HD;
-#pragma unroll 1
-      for (int c = 0; c < HD; c += 32) {
+      __nv_bfloat16* dv_out = p.dqkv + (size_t)kv_row * p.ld + p.v_col + kvh * HD + wg * HALF;
+#pragma unroll
+      for (int c = 0; c < HALF; c += 32) {
         uint32_t vv[32];
-        tmem_ld_32x32b_x32(lane_base + C::T_DV + c, vv);
+        tmem_ld_32x32b_x32(lane_base + C::T_DV + wg * HALF + c, vv);
         tc_wait_ld();
 #pragma unroll
         for (int e = 0; e < 32; e += 8) {
@@ -287,16 +305,16 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
           *reinterpret_cast<uint4*>(dv_out + c + e) = w;
         }
       }
-#pragma unroll 1
-      for (int c = 0; c < half; c += 32) {
-        uint32_t lo[32], hi[32];
-        tmem_ld_32x32b_x32(lane_base + C::T_DK + c, lo);
-        tmem_ld_32x32b_x32(lane_base + C::T_DK + half + c, hi);
+      {
+        const int c0 = wg * QTR;  // this warpgroup's RoPE pair range [c0, c0 + QTR)
+        uint32_t lo[QTR], hi[QTR];
+        tmem_ld_cols<QTR>(lane_base + C::T_DK + c0, lo);
+        tmem_ld_cols<QTR>(lane_base + C::T_DK + HALF + c0, hi);
         tc_wait_ld();
-        const float* cs = p.rope_cos + (size_t)pos * half + c;
-        const float* sn = p.rope_sin + (size_t)pos * half + c;
+        const float* cs = p.rope_cos + (size_t)pos * HALF + c0;
+        const float* sn = p.rope_sin + (size_t)pos * HALF + c0;
 #pragma unroll
-        for (int e = 0; e < 32; e += 8) {
+        for (int e = 0; e < QTR; e += 8) {
           float a[8], bb[8];
 #pragma unroll
           for (int t = 0; t < 8; ++t) {
@@ -311,8 +329,8 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
           wa.z = pack_bf16(a[4], a[5]); wa.w = pack_bf16(a[6], a[7]);
           wb.x = pack_bf16(bb[0], bb[1]); wb.y = pack_bf16(bb[2], bb[3]);
           wb.z = pack_bf16(bb[4], bb[5]); wb.w = pack_bf16(bb[6], bb[7]);
-          *reinterpret_cast<uint4*>(dk_out + c + e) = wa;
-          *reinterpret_cast<uint4*>(dk_out + half + c + e) = wb;
+          *reinterpret_cast<uint4*>(dk_out + c0 + e) = wa;
+          *reinterpret_cast<uint4*>(dk_out + HALF + c0 + e) = wb;
         }
       }
     }
@@ -351,23 +369,39 @@ __global__ void attn_delta_kernel(const __nv_bfloat16* __restrict__ o, const __n
   }
 }
 
-// q columns of dqkv = RoPE^T(dq_acc) in bf16.
+// q columns of dqkv = RoPE^T(dq_acc) in bf16; 8 consecutive pairs per thread.
 __global__ void attn_dq_convert_kernel(const float* __restrict__ dq_acc, __nv_bfloat16* __restrict__ dqkv, int ld,
                                        int rows, int seq, int heads, int hd, const float* __restrict__ cosv,
                                        const float* __restrict__ sinv) {
   const int half = hd / 2;
-  const size_t total = (size_t)rows * heads * half;
+  const int groups = half / 8;
+  const size_t total = (size_t)rows * heads * groups;
   for (size_t idx = blockIdx.x * (size_t)blockDim.x + threadIdx.x; idx < total; idx += (size_t)gridDim.x * blockDim.x) {
-    const int row = (int)(idx / (heads * half));
-    const int rem = (int)(idx % (heads * half));
-    const int h = rem / half, c = rem % half;
+    const int row = (int)(idx / (heads * groups));
+    const int rem = (int)(idx % (heads * groups));
+    const int h = rem / groups, c = (rem % groups) * 8;
     const int pos = row % seq;
     const float* src = dq_acc + (size_t)row * heads * hd + h * hd;
-    const float x0 = src[c], x1 = src[c + half];
-    const float cv = cosv[(size_t)pos * half + c], sv = sinv[(size_t)pos * half + c];
+    const float4 a0 = *reinterpret_cast<const float4*>(src + c), a1 = *reinterpret_cast<const float4*>(src + c + 4);
+    const float4 b0 = *reinterpret_cast<const float4*>(src + half + c);
+    const float4 b1 = *reinterpret_cast<const float4*>(src + half + c + 4);
+    const float x0[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+    const float x1[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+    float lo[8], hi[8];
+#pragma unroll
+    for (int t = 0; t < 8; ++t) {
+      const float cv = cosv[(size_t)pos * half + c + t], sv = sinv[(size_t)pos * half + c + t];
+      lo[t] = x0[t] * cv + x1[t] * sv;
+      hi[t] = x1[t] * cv - x0[t] * sv;
+    }
     __nv_bfloat16* out = dqkv + (size_t)row * ld + h * hd;
-    out[c] = __float2bfloat16_rn(x0 * cv + x1 * sv);
-    out[c + half] = __float2bfloat16_rn(x1 * cv - x0 * sv);
+    uint4 wl, wh;
+    wl.x = pack_bf16(lo[0], lo[1]); wl.y = pack_bf16(lo[2], lo[3]);
+    wl.z = pack_bf16(lo[4], lo[5]); wl.w = pack_bf16(lo[6], lo[7]);
+    wh.x = pack_bf16(hi[0], hi[1]); wh.y = pack_bf16(hi[2], hi[3]);
+    wh.z = pack_bf16(hi[4], hi[5]); wh.w = pack_bf16(hi[6], hi[7]);
+    *reinterpret_cast<uint4*>(out + c) = wl;
+    *reinterpret_cast<uint4*>(out + half + c) = wh;
   }
 }
 
@@ -403,7 +437,7 @@ void attention_bwd(const AttnBwdParams& p, cudaStream_t s) {
   else
     launch_bwd<128>(p, tq, tdo, s);
   B200_CUDA_CHECK(cudaGetLastError());
-  const size_t work = (size_t)rows * p.heads * (p.head_dim / 2);
+  const size_t work = (size_t)rows * p.heads * (p.head_dim / 16);
   const int blocks = (int)std::min<size_t>((work + 255) / 256, (size_t)num_sms_cached() * 16);
   attn_dq_convert_kernel<<<blocks, 256, 0, s>>>(p.dq_acc, p.dqkv, p.ld, rows, p.seq, p.heads, p.head_dim, p.rope_cos,
                                                 p.rope_sin);

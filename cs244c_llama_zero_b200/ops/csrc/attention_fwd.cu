@@ -1,6 +1,6 @@
 // Causal GQA flash-attention forward on the 5th-generation tensor cores (sm_100a).
 //
-// One CTA per (query block of 128 rows, query head, batch), 192 threads:
+// One CTA per (query block of 128 rows, query head, batch), 320 threads:
 //   warp 0      TMA producer: Q once, then K_j / V_j tiles into a STAGES-deep ring.  Q, K and V
 //               are column blocks of the fused [B*S, ld] q|k|v projection output, so one tensor
 //               map serves all three and K/V are never repeated for grouped heads: query head h
@@ -8,10 +8,13 @@
 //   warp 1      allocates tensor memory; lane 0 issues S_j = Q K_j^T (M=128, N=128, K=hd) into a
 //               double-buffered S accumulator, and O_j = P_j V_j (M=128, N=hd, K=128) into a
 //               double-buffered O accumulator once the softmax warps have written P_j.
-//   warps 2..5  softmax (one query row per thread): read S_j from tensor memory, apply the causal
-//               mask on the diagonal block, online max / sum in the base-2 domain, write P_j (bf16)
-//               to shared memory in the 128-byte-swizzled K-major layout the MMA reads, and fold
-//               O_{j-1} into the register accumulator with the running rescale factor.
+//   warps 2..9  softmax, two warpgroups.  Thread (wg, r) owns query row r and the 64 score columns
+//               [64*wg, 64*wg+64) and the output columns [wg*hd/2, (wg+1)*hd/2).  Row maxima are
+//               combined through shared memory once per block (one named barrier); row sums stay
+//               per warpgroup until the end.  Scores are read from tensor memory, masked only on
+//               the diagonal block, exponentiated with one FFMA + ex2.approx in the base-2 domain,
+//               written as bf16 P in the 128-byte-swizzled K-major layout the MMA reads, and
+//               O_{j-1} is folded into registers with the running rescale factor.
 // The log-sum-exp of every row is stored in base-2 units scaled by log2(e)/sqrt(hd) so the
 // backward pass can rebuild P with one exp2.
 #include <cuda.h>
@@ -24,7 +27,7 @@ namespace b200 {
 
 namespace {
 
-constexpr int ATT_THREADS = 192;
+constexpr int ATT_THREADS = 320;
 constexpr float kLog2e = 1.4426950408889634f;
 
 template <int HD>
@@ -37,10 +40,12 @@ struct AttnFwdCfg {
   static constexpr int Q_OFF = 0;
   static constexpr int KV_OFF = TILE_BYTES;
   static constexpr int P_OFF = KV_OFF + STAGES * 2 * TILE_BYTES;
-  static constexpr int BAR_OFF = P_OFF + P_BUFS * P_BYTES;
+  static constexpr int RED_OFF = P_OFF + P_BUFS * P_BYTES;  // row-max exchange [2 parity][2 wg][128]
+  static constexpr int BAR_OFF = RED_OFF + 3 * 2 * 128 * 4;
   static constexpr int SMEM_BYTES = BAR_OFF + 256 + 1024;
-  static constexpr int TMEM_COLS = (2 * 128 + 2 * HD) <= 256 ? 256 : 512;
+  static constexpr int TMEM_COLS = 512;
   static constexpr int O_TMEM = 256;  // O accumulators start after the two S buffers
+  static constexpr int HALF_O = HD / 2;
 };
 
 __device__ __forceinline__ void fence_async_smem() {
@@ -61,8 +66,10 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
   uint64_t* p_full = s_full + 2;
   uint64_t* o_full = p_full + 2;
   uint64_t* o_free = o_full + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_free + 2);
+  uint64_t* red_bar = o_free + 2;  // [0..1]: row-max exchange per parity, [2]: final row-sum exchange
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(red_bar + 3);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  float* red = reinterpret_cast<float*>(smem + C::RED_OFF);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n_qb = p.seq / 128;
@@ -80,10 +87,11 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
-      mbar_init(&p_full[i], 4);
+      mbar_init(&p_full[i], 8);
       mbar_init(&o_full[i], 1);
-      mbar_init(&o_free[i], 4);
+      mbar_init(&o_free[i], 8);
     }
+    for (int i = 0; i < 3; ++i) mbar_init(&red_bar[i], 8);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -157,14 +165,17 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
       }
     }
   } else {
-    const int q = warp & 3;
-    const int r = q * 32 + lane;  // row within the query block
+    const int wg = (warp - 2) >> 2;   // warpgroup: score columns [64*wg, 64*wg+64)
+    const int q = warp & 3;            // tensor-memory lane quarter
+    const int r = q * 32 + lane;       // query row within the block
+    const int col0 = wg * 64;
+    const int ocol0 = wg * C::HALF_O;
     const uint32_t lane_base = tmem + ((uint32_t)(q * 32) << 16);
     const float scale2 = p.scale * kLog2e;
     float m = -INFINITY, l = 0.f;
-    float o[HD];
+    float o[C::HALF_O];
 #pragma unroll
-    for (int i = 0; i < HD; ++i) o[i] = 0.f;
+    for (int i = 0; i < C::HALF_O; ++i) o[i] = 0.f;
     bool ok = true;
     for (int j = 0; j < n_kv; ++j) {
       if (!mbar_wait_bounded(&s_full[j & 1], (j >> 1) & 1, abort_flag, errs, kErrAttnWait, 5)) {
@@ -172,50 +183,68 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
         break;
       }
       tc_fence_after();
-      const uint32_t sbase = lane_base + (j & 1) * 128;
+      const uint32_t sbase = lane_base + (j & 1) * 128 + col0;
       const bool diag = (j == qb);
-      // pass 1: row max of the scaled scores
-      float mx = m;
-#pragma unroll 1
-      for (int c = 0; c < 128; c += 32) {
+      // pass 1: partial row max of the raw scores over this warpgroup's 64 columns
+      float pmx = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < 64; c += 32) {
         uint32_t sv[32];
         tmem_ld_32x32b_x32(sbase + c, sv);
         tc_wait_ld();
+        if (diag) {
 #pragma unroll
-        for (int e = 0; e < 32; ++e) {
-          const bool masked = diag && (c + e > r);
-          if (!masked) mx = fmaxf(mx, __uint_as_float(sv[e]) * scale2);
+          for (int e = 0; e < 32; ++e)
+            if (col0 + c + e <= r) pmx = fmaxf(pmx, __uint_as_float(sv[e]));
+        } else {
+#pragma unroll
+          for (int e = 0; e < 32; ++e) pmx = fmaxf(pmx, __uint_as_float(sv[e]));
         }
       }
-      const float alpha = exp2f(m - mx);
+      float* red_slot = red + (j & 1) * 256;
+      red_slot[wg * 128 + r] = pmx;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&red_bar[j & 1]);
+      if (!mbar_wait_bounded(&red_bar[j & 1], (j >> 1) & 1, abort_flag, errs, kErrAttnWait, 8)) {
+        ok = false;
+        break;
+      }
+      const float other = red_slot[(wg ^ 1) * 128 + r];
+      const float mx = fmaxf(m, fmaxf(pmx, other) * scale2);  // scaled, base-2 domain
+      const float alpha = ex2_approx(m - mx);
       // P buffer reuse: PV_{j-1} must have finished reading it.
       if (j >= 1 && !mbar_wait_bounded(&o_full[(j - 1) & 1], ((j - 1) >> 1) & 1, abort_flag, errs, kErrAttnWait, 6)) {
         ok = false;
         break;
       }
-      // pass 2: probabilities, row sum, bf16 P into swizzled shared memory
+      // pass 2: probabilities, partial row sum, bf16 P into swizzled shared memory
       uint8_t* pbuf = smem + C::P_OFF + (j % C::P_BUFS) * C::P_BYTES;
       float rs = 0.f;
-#pragma unroll 1
-      for (int c = 0; c < 128; c += 32) {
+#pragma unroll
+      for (int c = 0; c < 64; c += 32) {
         uint32_t sv[32];
         tmem_ld_32x32b_x32(sbase + c, sv);
         tc_wait_ld();
         uint32_t pk[16];
 #pragma unroll
         for (int e = 0; e < 32; e += 2) {
-          float p0 = (diag && (c + e > r)) ? 0.f : exp2f(__uint_as_float(sv[e]) * scale2 - mx);
-          float p1 = (diag && (c + e + 1 > r)) ? 0.f : exp2f(__uint_as_float(sv[e + 1]) * scale2 - mx);
+          float p0 = ex2_approx(fmaf(__uint_as_float(sv[e]), scale2, -mx));
+          float p1 = ex2_approx(fmaf(__uint_as_float(sv[e + 1]), scale2, -mx));
+          if (diag) {
+            if (col0 + c + e > r) p0 = 0.f;
+            if (col0 + c + e + 1 > r) p1 = 0.f;
+          }
           rs += p0 + p1;
           pk[e >> 1] = pack_bf16(p0, p1);
         }
-        const int kblk = c >> 6;
+        const int cc = col0 + c;
+        const int kblk = cc >> 6;
 #pragma unroll
         for (int ch = 0; ch < 4; ++ch) {
-          const int chunk = ((c & 63) >> 3) + ch;  // 16-byte chunk within the 128-byte row
+          const int chunk = ((cc & 63) >> 3) + ch;  // 16-byte chunk within the 128-byte row
           const int sw = chunk ^ (r & 7);
-          uint4 val = make_uint4(pk[4 * ch], pk[4 * ch + 1], pk[4 * ch + 2], pk[4 * ch + 3]);
-          *reinterpret_cast<uint4*>(pbuf + kblk * 16384 + r * 128 + sw * 16) = val;
+          *reinterpret_cast<uint4*>(pbuf + kblk * 16384 + r * 128 + sw * 16) =
+              make_uint4(pk[4 * ch], pk[4 * ch + 1], pk[4 * ch + 2], pk[4 * ch + 3]);
         }
       }
       l = l * alpha + rs;
@@ -225,9 +254,9 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
       if (lane == 0) mbar_arrive(&p_full[j & 1]);
       if (j >= 1) {
         tc_fence_after();
-        const uint32_t obase = lane_base + C::O_TMEM + ((j - 1) & 1) * HD;
+        const uint32_t obase = lane_base + C::O_TMEM + ((j - 1) & 1) * HD + ocol0;
 #pragma unroll
-        for (int c = 0; c < HD; c += 32) {
+        for (int c = 0; c < C::HALF_O; c += 32) {
           uint32_t ov[32];
           tmem_ld_32x32b_x32(obase + c, ov);
           tc_wait_ld();
@@ -239,17 +268,24 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
         if (lane == 0) mbar_arrive(&o_free[(j - 1) & 1]);
       } else {
 #pragma unroll
-        for (int i = 0; i < HD; ++i) o[i] *= alpha;
+        for (int i = 0; i < C::HALF_O; ++i) o[i] *= alpha;
       }
       m = mx;
     }
+    // Combine the two warpgroups' partial row sums.
+    float* lred = red + 512;  // separate slot: no reader of the loop's slots is disturbed
+    lred[wg * 128 + r] = l;
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&red_bar[2]);
+    ok = ok && mbar_wait_bounded(&red_bar[2], 0, abort_flag, errs, kErrAttnWait, 9);
+    const float l_total = l + lred[(wg ^ 1) * 128 + r];
     if (ok && mbar_wait_bounded(&o_full[(n_kv - 1) & 1], ((n_kv - 1) >> 1) & 1, abort_flag, errs, kErrAttnWait, 7)) {
       tc_fence_after();
-      const uint32_t obase = lane_base + C::O_TMEM + ((n_kv - 1) & 1) * HD;
-      const float inv_l = 1.0f / l;
-      __nv_bfloat16* dst = p.out + (size_t)(row0 + qb * 128 + r) * p.ld_out + h * HD;
+      const uint32_t obase = lane_base + C::O_TMEM + ((n_kv - 1) & 1) * HD + ocol0;
+      const float inv_l = 1.0f / l_total;
+      __nv_bfloat16* dst = p.out + (size_t)(row0 + qb * 128 + r) * p.ld_out + h * HD + ocol0;
 #pragma unroll
-      for (int c = 0; c < HD; c += 32) {
+      for (int c = 0; c < C::HALF_O; c += 32) {
         uint32_t ov[32];
         tmem_ld_32x32b_x32(obase + c, ov);
         tc_wait_ld();
@@ -263,7 +299,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
           *reinterpret_cast<uint4*>(dst + c + e) = w;
         }
       }
-      p.lse[((size_t)b * p.heads + h) * p.seq + qb * 128 + r] = m + log2f(l);
+      if (wg == 0) p.lse[((size_t)b * p.heads + h) * p.seq + qb * 128 + r] = m + log2f(l_total);
     }
   }
 
@@ -275,6 +311,18 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
   }
 }
 
+template <int HD>
+void launch_fwd(const AttnParams& p, const CUtensorMap& tm, cudaStream_t s) {
+  using C = AttnFwdCfg<HD>;
+  static bool cfg = false;
+  if (!cfg) {
+    B200_CUDA_CHECK(cudaFuncSetAttribute(attn_fwd_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES));
+    cfg = true;
+  }
+  dim3 grid(p.seq / 128, p.heads, p.batch);
+  attn_fwd_kernel<HD><<<grid, ATT_THREADS, C::SMEM_BYTES, s>>>(tm, p, device_errors_ptr());
+}
+
 }  // namespace
 
 void attention_fwd(const AttnParams& p, cudaStream_t s) {
@@ -282,24 +330,10 @@ void attention_fwd(const AttnParams& p, cudaStream_t s) {
   B200_CHECK(p.seq % 128 == 0, "attention: seq_len must be a multiple of 128");
   B200_CHECK(p.heads % p.kv_heads == 0, "attention: heads must be a multiple of kv_heads");
   CUtensorMap tm = make_tmap_bf16_2d(p.qkv, (uint64_t)p.ld, (uint64_t)p.batch * p.seq, (uint64_t)p.ld, 64, 128);
-  dim3 grid(p.seq / 128, p.heads, p.batch);
-  if (p.head_dim == 64) {
-    using C = AttnFwdCfg<64>;
-    static bool cfg = false;
-    if (!cfg) {
-      B200_CUDA_CHECK(cudaFuncSetAttribute(attn_fwd_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES));
-      cfg = true;
-    }
-    attn_fwd_kernel<64><<<grid, ATT_THREADS, C::SMEM_BYTES, s>>>(tm, p, device_errors_ptr());
-  } else {
-    using C = AttnFwdCfg<128>;
-    static bool cfg = false;
-    if (!cfg) {
-      B200_CUDA_CHECK(cudaFuncSetAttribute(attn_fwd_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES));
-      cfg = true;
-    }
-    attn_fwd_kernel<128><<<grid, ATT_THREADS, C::SMEM_BYTES, s>>>(tm, p, device_errors_ptr());
-  }
+  if (p.head_dim == 64)
+    launch_fwd<64>(p, tm, s);
+  else
+    launch_fwd<128>(p, tm, s);
   B200_CUDA_CHECK(cudaGetLastError());
   count_launch();
 }

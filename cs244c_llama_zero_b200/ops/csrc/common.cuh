@@ -256,6 +256,18 @@ __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
 
 __device__ __forceinline__ int elect_one_lane() { return (threadIdx.x & 31) == 0; }
 
+// 2^x with the hardware approximation (PTX ex2.approx.ftz.f32; ~2 ulp, flushes denormals).
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// Named barrier over `count` threads (id 0 is __syncthreads).
+__device__ __forceinline__ void named_bar(int id, int count) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+
 #endif  // __CUDACC__
 
 }  // namespace b200

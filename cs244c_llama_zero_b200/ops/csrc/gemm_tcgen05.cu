@@ -2,14 +2,15 @@
 //
 //   C[M, N] (op)= sum_k A(m, k) * B(n, k)         fp32 accumulation in tensor memory
 //
-// Structure (one CTA per SM, 192 threads):
+// Structure (one CTA per SM, 320 threads):
 //   warp 0      : TMA producer. Loads A (128 x 64) and B (BN x 64) bf16 tiles per k-block into a
 //                 STAGES-deep shared-memory ring (128-byte swizzle, no multicast).
 //   warp 1      : allocates 2*BN tensor-memory columns (double-buffered accumulator); lane 0 issues
 //                 tcgen05.mma (M=128, N=BN, K=16) and tcgen05.commit to release smem stages and to
 //                 hand a finished accumulator to the epilogue.
-//   warps 2..5  : epilogue. tcgen05.ld the accumulator (one row per thread), apply the fused
-//                 operation, write to global memory, release the accumulator buffer.
+//   warps 2..9  : epilogue, two warpgroups splitting the tile columns. tcgen05.ld the accumulator
+//                 (one row per thread), apply the fused operation, write to global memory,
+//                 release the accumulator buffer.
 // The epilogue of tile t overlaps the main loop of tile t+1.  Operands may be K-major or
 // MN-major (the descriptor's major bit), so forward, data-gradient and weight-gradient GEMMs of a
 // row-major nn.Linear weight all run without transposes.
@@ -41,7 +42,7 @@ namespace {
 constexpr int BM = 128;
 constexpr int BK = 64;  // 64 bf16 = 128 bytes = one swizzle row
 constexpr int A_STAGE_BYTES = BM * BK * 2;
-constexpr int NUM_THREADS = 192;
+constexpr int NUM_THREADS = 320;
 
 template <int BN>
 struct GemmCfg {
@@ -80,7 +81,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull_bar[a], 1);
-      mbar_init(&tempty_bar[a], 4);
+      mbar_init(&tempty_bar[a], 8);
     }
     *abort_flag = 0;
     fence_mbar_init();
@@ -186,6 +187,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   } else {
     // ------------------------------------------------------------------ epilogue warps
     const int q = warp & 3;  // tensor-memory lane quarter this warp may access
+    const int wg = (warp - 2) >> 2;  // epilogue warpgroup: columns [wg*BN/2, (wg+1)*BN/2)
     const int row = q * 32 + lane;
     int t = 0;
     for (int u = blockIdx.x; u < total_units; u += gridDim.x, ++t) {
@@ -202,7 +204,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       if constexpr (EPI == EPI_STORE || EPI == EPI_RESIDUAL || EPI == EPI_ACC_F32) {
         const int n0 = tn * BN;
 #pragma unroll 1
-        for (int c = 0; c < BN; c += 32) {
+        for (int c = wg * (BN / 2); c < (wg + 1) * (BN / 2); c += 32) {
           uint32_t r[32];
           tmem_ld_32x32b_x32(tbase + c, r);
           tc_wait_ld();
@@ -250,7 +252,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         const int half = p.head_dim >> 1;
         const int pos = row_ok ? (m % p.seq_len) : 0;
 #pragma unroll 1
-        for (int h0 = 0; h0 < BN; h0 += p.head_dim) {
+        for (int h0 = wg * (BN / 2); h0 < (wg + 1) * (BN / 2); h0 += p.head_dim) {
           const int col = n0 + h0;
           const bool rotate = col < p.rope_cols;
 #pragma unroll 1
@@ -293,7 +295,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       } else if constexpr (EPI == EPI_SWIGLU) {
         const int n0 = tn * (BN / 2);
 #pragma unroll 1
-        for (int c = 0; c < BN / 2; c += 32) {
+        for (int c = wg * (BN / 4); c < (wg + 1) * (BN / 4); c += 32) {
           uint32_t g[32], uu[32];
           tmem_ld_32x32b_x32(tbase + c, g);
           tmem_ld_32x32b_x32(tbase + BN / 2 + c, uu);
@@ -327,7 +329,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       } else if constexpr (EPI == EPI_SWIGLU_BWD) {
         const int n0 = tn * BN;
 #pragma unroll 1
-        for (int c = 0; c < BN; c += 32) {
+        for (int c = wg * (BN / 2); c < (wg + 1) * (BN / 2); c += 32) {
           uint32_t r[32];
           tmem_ld_32x32b_x32(tbase + c, r);
           tc_wait_ld();

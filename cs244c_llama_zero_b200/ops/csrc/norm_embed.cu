@@ -233,6 +233,8 @@ void rmsnorm_fwd(const __nv_bfloat16* x, const __nv_bfloat16* w, __nv_bfloat16* 
     rmsnorm_fwd_kernel<1><<<blocks, 32 * kWarpsPerBlock, 0, s>>>(x, w, y, rstd, rows, d, eps);
   else if (vec <= 2)
     rmsnorm_fwd_kernel<2><<<blocks, 32 * kWarpsPerBlock, 0, s>>>(x, w, y, rstd, rows, d, eps);
+  else if (vec <= 3)
+    rmsnorm_fwd_kernel<3><<<blocks, 32 * kWarpsPerBlock, 0, s>>>(x, w, y, rstd, rows, d, eps);
   else if (vec <= 4)
     rmsnorm_fwd_kernel<4><<<blocks, 32 * kWarpsPerBlock, 0, s>>>(x, w, y, rstd, rows, d, eps);
   else if (vec <= 8)
@@ -246,7 +248,9 @@ void rmsnorm_fwd(const __nv_bfloat16* x, const __nv_bfloat16* w, __nv_bfloat16* 
 void rmsnorm_bwd(const __nv_bfloat16* dy, const __nv_bfloat16* x, const __nv_bfloat16* w, const float* rstd,
                  const __nv_bfloat16* dres, __nv_bfloat16* dx, float* dw, int rows, int d, cudaStream_t s) {
   B200_CHECK(d % 8 == 0 && d <= 256 * 8, "rmsnorm_bwd: d must be a multiple of 8 and at most 2048");
-  const int blocks = std::max(1, std::min(num_sms_cached() * 2, (rows + kWarpsPerBlock - 1) / kWarpsPerBlock));
+  // ~32 rows per block: enough blocks for several resident per SM (latency hiding) while the
+  // per-block weight-gradient atomics stay a small fraction of the traffic.
+  const int blocks = std::max(1, (rows + 31) / 32);
   const int rows_per_block = (rows + blocks - 1) / blocks;
   const int vec = (d + 255) / 256;
   const int threads = 32 * kWarpsPerBlock;
@@ -254,6 +258,8 @@ void rmsnorm_bwd(const __nv_bfloat16* dy, const __nv_bfloat16* x, const __nv_bfl
     rmsnorm_bwd_kernel<1><<<blocks, threads, 0, s>>>(dy, x, w, rstd, dres, dx, dw, rows, d, rows_per_block);
   else if (vec <= 2)
     rmsnorm_bwd_kernel<2><<<blocks, threads, 0, s>>>(dy, x, w, rstd, dres, dx, dw, rows, d, rows_per_block);
+  else if (vec <= 3)
+    rmsnorm_bwd_kernel<3><<<blocks, threads, 0, s>>>(dy, x, w, rstd, dres, dx, dw, rows, d, rows_per_block);
   else if (vec <= 4)
     rmsnorm_bwd_kernel<4><<<blocks, threads, 0, s>>>(dy, x, w, rstd, dres, dx, dw, rows, d, rows_per_block);
   else
