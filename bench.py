@@ -205,7 +205,9 @@ def run_mine(args) -> None:
     rank, world, local = dist_env()
     if world != args.gpus and rank == 0:
         print(f"[bench] note: --gpus {args.gpus} but WORLD_SIZE={world}; using {world}", file=sys.stderr)
-    impl = args.collective_impl if args.collective_impl != "auto" else "torch"
+    impl = args.collective_impl
+    if impl == "auto":
+        impl = "nvls" if world > 1 else "torch"
     per_stage = {}
     e2e = None
     launches = None
@@ -238,7 +240,9 @@ def run_mine(args) -> None:
         stage_launches = (ops.launch_count() - launches_before) // args.steps
         entry ={"tokens_per_s": tokens_per_step / (ms / 1000.0), "ms_per_step": ms,
                  "gpu_launches_per_step": stage_launches}
-        # comm time of one extra instrumented step (device events around each collective)
+        # comm time of one extra instrumented step (device events around each collective); the
+        # barrier keeps host-side skew between ranks out of the measured intervals
+        barrier_sync()
         sess.engine.zero_grad()
         sess.engine.prepare_forward()
         sess.forward_backward([dev[0]])

@@ -19,6 +19,8 @@ def load_extension():
     global _EXT, _EXT_ERROR
     if _EXT is not None:
         return _EXT
+    import torch  # noqa: F401  (loads libc10 / libtorch that the extension links against)
+
     try:
         _EXT = importlib.import_module(f"{__name__}._C")
     except ImportError as exc:  # pragma: no cover - depends on the build

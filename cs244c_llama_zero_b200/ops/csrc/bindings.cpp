@@ -386,6 +386,102 @@ void attention_bwd(Tensor qkv, int64_t k_col, int64_t v_col, Tensor out, Tensor 
   b200::attention_bwd(p, cur_stream());
 }
 
+// ----------------------------------------------------------------------------------- comm
+// Python-side handle for one symmetric buffer: peer / multicast / signal-pad addresses come from
+// the symmetric-memory rendezvous; the per-block epoch counters are a small local int32 tensor.
+class CommContext {
+ public:
+  CommContext(int64_t rank, int64_t world, std::vector<int64_t> peers, int64_t mc, std::vector<int64_t> pads,
+              Tensor epochs, int64_t blocks, int64_t timeout_ns)
+      : epochs_(epochs), device_(epochs.device()) {
+    TORCH_CHECK(world >= 1 && world <= b200::kCommMaxWorld, "comm: world size 1..8");
+    TORCH_CHECK((int64_t)peers.size() == world && (int64_t)pads.size() == world, "comm: one peer/pad per rank");
+    TORCH_CHECK(epochs.is_cuda() && epochs.scalar_type() == at::kInt && epochs.numel() >= b200::kCommMaxBlocks,
+                "comm: epochs must be a CUDA int32 tensor of at least 64 elements");
+    TORCH_CHECK(blocks >= 1 && blocks < b200::kCommMaxBlocks, "comm: blocks 1..63");
+    c_ = b200::CommCtx{};
+    c_.rank = rank;
+    c_.world = world;
+    for (int i = 0; i < world; ++i) {
+      c_.peers[i] = (uint64_t)peers[i];
+      c_.pads[i] = (uint64_t)pads[i];
+    }
+    c_.mc = (uint64_t)mc;
+    c_.epochs = reinterpret_cast<uint32_t*>(epochs.data_ptr<int32_t>());
+    c_.timeout_ns = (uint64_t)timeout_ns;
+    c_.blocks = blocks;
+  }
+  void allreduce_f32(int64_t off, int64_t n, double scale) {
+    c10::cuda::CUDAGuard g(device_);
+    prepare();
+    b200::comm_allreduce_f32(c_, off, n, (float)scale, cur_stream());
+  }
+  void allreduce_bf16(int64_t off, int64_t n, double scale) {
+    c10::cuda::CUDAGuard g(device_);
+    prepare();
+    b200::comm_allreduce_bf16(c_, off, n, (float)scale, cur_stream());
+  }
+  void reduce_scatter_acc_f32(int64_t off, int64_t chunk, Tensor acc, double scale) {
+    check_acc(acc, chunk);
+    c10::cuda::CUDAGuard g(device_);
+    prepare();
+    b200::comm_reduce_scatter_acc_f32(c_, off, chunk, acc.data_ptr<float>(), (float)scale, cur_stream());
+  }
+  void reduce_scatter_acc_bf16(int64_t off, int64_t chunk, Tensor acc, double scale) {
+    check_acc(acc, chunk);
+    c10::cuda::CUDAGuard g(device_);
+    prepare();
+    b200::comm_reduce_scatter_acc_bf16(c_, off, chunk, acc.data_ptr<float>(), (float)scale, cur_stream());
+  }
+  void allgather(int64_t off, int64_t chunk_bytes, Tensor shard) {
+    check_cuda(shard, "shard");
+    TORCH_CHECK(shard.is_contiguous() && shard.numel() * shard.element_size() >= chunk_bytes, "shard too small");
+    c10::cuda::CUDAGuard g(device_);
+    prepare();
+    b200::comm_allgather(c_, off, chunk_bytes, shard.data_ptr(), cur_stream());
+  }
+  void adamw_allgather(int64_t param_off, int64_t chunk, Tensor master, Tensor m, Tensor v, Tensor grad,
+                       std::optional<Tensor> scale, double scale_const, double lr, double beta1, double beta2,
+                       double eps, double wd, int64_t step) {
+    for (auto* t : {&master, &m, &v, &grad}) {
+      check_f32(*t, "adam state");
+      TORCH_CHECK(t->is_contiguous() && t->numel() >= chunk, "adam state too small");
+    }
+    const float* sp = nullptr;
+    if (scale.has_value()) {
+      check_f32(*scale, "scale");
+      sp = scale->data_ptr<float>();
+    }
+    c10::cuda::CUDAGuard g(device_);
+    prepare();
+    b200::comm_adamw_allgather(c_, param_off, chunk, master.data_ptr<float>(), m.data_ptr<float>(),
+                               v.data_ptr<float>(), grad.data_ptr<float>(), sp, (float)scale_const, (float)lr,
+                               (float)beta1, (float)beta2, (float)eps, (float)wd, (int)step, cur_stream());
+  }
+  void barrier() {
+    c10::cuda::CUDAGuard g(device_);
+    prepare();
+    b200::comm_barrier(c_, cur_stream());
+  }
+  void wait_unsignalled(int64_t timeout_ns) {
+    c10::cuda::CUDAGuard g(device_);
+    prepare();
+    b200::comm_wait_unsignalled(c_, (uint64_t)timeout_ns, cur_stream());
+  }
+  bool multicast() const { return c_.mc != 0; }
+  int64_t blocks() const { return c_.blocks; }
+
+ private:
+  void prepare() { c_.errs = b200::device_errors_ptr(); }
+  static void check_acc(const Tensor& acc, int64_t chunk) {
+    check_f32(acc, "acc");
+    TORCH_CHECK(acc.numel() >= chunk && acc.is_contiguous(), "acc too small or not contiguous");
+  }
+  b200::CommCtx c_;
+  Tensor epochs_;
+  c10::Device device_;
+};
+
 int64_t launch_count() { return b200::launch_counter().load(); }
 
 std::vector<int64_t> read_device_errors() {
@@ -423,5 +519,17 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("launch_count", &launch_count);
   m.def("read_device_errors", &read_device_errors);
   m.def("reset_device_errors", &reset_device_errors);
+  py::class_<CommContext>(m, "CommContext")
+      .def(py::init<int64_t, int64_t, std::vector<int64_t>, int64_t, std::vector<int64_t>, Tensor, int64_t, int64_t>())
+      .def("allreduce_f32", &CommContext::allreduce_f32)
+      .def("allreduce_bf16", &CommContext::allreduce_bf16)
+      .def("reduce_scatter_acc_f32", &CommContext::reduce_scatter_acc_f32)
+      .def("reduce_scatter_acc_bf16", &CommContext::reduce_scatter_acc_bf16)
+      .def("allgather", &CommContext::allgather)
+      .def("adamw_allgather", &CommContext::adamw_allgather)
+      .def("barrier", &CommContext::barrier)
+      .def("wait_unsignalled", &CommContext::wait_unsignalled)
+      .def_property_readonly("multicast", &CommContext::multicast)
+      .def_property_readonly("blocks", &CommContext::blocks);
 
 }

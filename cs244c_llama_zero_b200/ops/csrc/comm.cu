@@ -1,2 +1,466 @@
-// NVLink / NVSwitch collective kernels.
+// NVLink 5 / NVSwitch collective kernels for the ZeRO engines.
+//
+// Data moves through symmetric memory: each rank's buffer is mapped on every GPU (peer pointers)
+// and, when the NVSwitch supports it, bound to a multicast object.  With multicast the switch
+// does the arithmetic: `multimem.ld_reduce` returns the sum over all ranks of one 16-byte vector
+// and `multimem.st` writes one vector to every rank.  Without multicast the same kernels use
+// plain peer loads and stores.
+//
+//   allreduce            each rank reduces its 1/W slice (ld_reduce) and broadcasts it (st), with
+//                        the 1/W gradient averaging fused in
+//   reduce_scatter_acc   each rank ld_reduces its own chunk and accumulates scale * sum into its
+//                        local fp32 gradient shard (ZeRO-2/3 gradient reduce-scatter + averaging)
+//   allgather            each rank multicasts its shard into every rank's buffer
+//   adamw_allgather      AdamW on the local fp32 shard; the bf16 result is multicast straight into
+//                        every rank's parameter buffer (ZeRO-1/2 update + parameter all-gather)
+//
+// Ordering: every block of every rank runs the same grid, and block b synchronises with block b of
+// every peer at kernel start (all inputs written) and at kernel end (all outputs delivered).  The
+// barrier writes a per-block epoch into the peer's signal pad with st.release.sys and polls its own
+// pad with ld.acquire.sys; the epochs live in device memory.  Every poll is bounded by a
+// %globaltimer deadline; on expiry the block records an error in the device error record and returns.
+#include <cuda_bf16.h>
+
+#include <algorithm>
+#include <cmath>
+
 #include "comm.h"
+#include "common.cuh"
+
+namespace b200 {
+
+namespace {
+
+constexpr int kThreads = 512;
+constexpr int kUnroll = 4;  // independent 16-byte vectors in flight per thread
+
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void fence_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
+
+__device__ __forceinline__ float4 mc_ld_reduce_f32x4(uint64_t addr) {
+  float4 v;
+  asm volatile("multimem.ld_reduce.relaxed.sys.global.add.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "l"(addr)
+               : "memory");
+  return v;
+}
+__device__ __forceinline__ void mc_st_f32x4(uint64_t addr, float4 v) {
+  asm volatile("multimem.st.relaxed.sys.global.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(addr), "f"(v.x), "f"(v.y),
+               "f"(v.z), "f"(v.w)
+               : "memory");
+}
+__device__ __forceinline__ void mc_st_b128(uint64_t addr, uint4 v) {
+  mc_st_f32x4(addr, make_float4(__uint_as_float(v.x), __uint_as_float(v.y), __uint_as_float(v.z), __uint_as_float(v.w)));
+}
+// Sum over ranks of 8 bf16 values, accumulated in fp32 inside the switch, returned as bf16x2 words.
+__device__ __forceinline__ uint4 mc_ld_reduce_bf16x8(uint64_t addr) {
+  uint4 v;
+  asm volatile("multimem.ld_reduce.relaxed.sys.global.add.acc::f32.v4.bf16x2 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(addr)
+               : "memory");
+  return v;
+}
+__device__ __forceinline__ void bf16x8_to_f32(uint4 q, float (&f)[8]) {
+  const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    f[2 * i] = bf16lo(w[i]);
+    f[2 * i + 1] = bf16hi(w[i]);
+  }
+}
+__device__ __forceinline__ uint4 f32_to_bf16x8(const float (&f)[8]) {
+  return make_uint4(pack_bf16(f[0], f[1]), pack_bf16(f[2], f[3]), pack_bf16(f[4], f[5]), pack_bf16(f[6], f[7]));
+}
+
+// Returns this block's epoch for this call (same value on every rank: same call sequence, same grid).
+__device__ __forceinline__ uint32_t next_epoch(const CommCtx& c) {
+  __shared__ uint32_t e;
+  if (threadIdx.x == 0) {
+    e = c.epochs[blockIdx.x] + 1;
+    c.epochs[blockIdx.x] = e;
+  }
+  __syncthreads();
+  return e;
+}
+
+__device__ bool block_barrier(const CommCtx& c, uint32_t value) {
+  __shared__ int ok;
+  if (threadIdx.x == 0) ok = 1;
+  fence_sys();
+  __syncthreads();
+  if (threadIdx.x < c.world) {
+    const int peer = threadIdx.x;
+    uint32_t* remote = reinterpret_cast<uint32_t*>(c.pads[peer]) + blockIdx.x * kCommMaxWorld + c.rank;
+    st_release_sys(remote, value);
+    const uint32_t* mine = reinterpret_cast<const uint32_t*>(c.pads[c.rank]) + blockIdx.x * kCommMaxWorld + peer;
+    const uint64_t t0 = globaltimer_ns();
+    while ((int)(ld_acquire_sys(mine) - value) < 0) {
+      if (globaltimer_ns() - t0 > c.timeout_ns) {
+        report_error(c.errs, kErrCommBarrier, peer);
+        ok = 0;
+        break;
+      }
+    }
+  }
+  __syncthreads();
+  return ok != 0;
+}
+
+__device__ __forceinline__ size_t gtid() { return (size_t)blockIdx.x * blockDim.x + threadIdx.x; }
+__device__ __forceinline__ size_t gstride() { return (size_t)gridDim.x * blockDim.x; }
+
+template <bool MC>
+__global__ void __launch_bounds__(kThreads) allreduce_f32_kernel(CommCtx c, size_t off, size_t n4, float scale) {
+  const uint32_t e = next_epoch(c);
+  if (!block_barrier(c, 2 * e)) return;
+  const size_t per = (n4 + c.world - 1) / c.world;
+  const size_t lo = (size_t)c.rank * per, hi = min(n4, lo + per);
+  const size_t stride = gstride();
+  for (size_t i0 = lo + gtid(); i0 < hi; i0 += stride * kUnroll) {
+    float4 v[kUnroll];
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+      const size_t i = i0 + u * stride;
+      if (i >= hi) break;
+      const size_t b = off + i * 16;
+      if constexpr (MC) {
+        v[u] = mc_ld_reduce_f32x4(c.mc + b);
+      } else {
+        v[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int w = 0; w < c.world; ++w) {
+          const float4 x = __ldcg(reinterpret_cast<const float4*>(c.peers[w] + b));
+          v[u].x += x.x; v[u].y += x.y; v[u].z += x.z; v[u].w += x.w;
+        }
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+      const size_t i = i0 + u * stride;
+      if (i >= hi) break;
+      const size_t b = off + i * 16;
+      float4 x = v[u];
+      x.x *= scale; x.y *= scale; x.z *= scale; x.w *= scale;
+      if constexpr (MC) {
+        mc_st_f32x4(c.mc + b, x);
+      } else {
+        for (int w = 0; w < c.world; ++w) __stcg(reinterpret_cast<float4*>(c.peers[w] + b), x);
+      }
+    }
+  }
+  block_barrier(c, 2 * e + 1);
+}
+
+template <bool MC>
+__global__ void __launch_bounds__(kThreads) reduce_scatter_acc_f32_kernel(CommCtx c, size_t off, size_t chunk4,
+                                                                          float4* acc, float scale) {
+  const uint32_t e = next_epoch(c);
+  if (!block_barrier(c, 2 * e)) return;
+  const size_t base = off + (size_t)c.rank * chunk4 * 16;
+  const size_t stride = gstride();
+  for (size_t i0 = gtid(); i0 < chunk4; i0 += stride * kUnroll) {
+    float4 v[kUnroll];
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+      const size_t i = i0 + u * stride;
+      if (i >= chunk4) break;
+      const size_t b = base + i * 16;
+      if constexpr (MC) {
+        v[u] = mc_ld_reduce_f32x4(c.mc + b);
+      } else {
+        v[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int w = 0; w < c.world; ++w) {
+          const float4 x = __ldcg(reinterpret_cast<const float4*>(c.peers[w] + b));
+          v[u].x += x.x; v[u].y += x.y; v[u].z += x.z; v[u].w += x.w;
+        }
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+      const size_t i = i0 + u * stride;
+      if (i >= chunk4) break;
+      float4 a = acc[i];
+      a.x += scale * v[u].x; a.y += scale * v[u].y; a.z += scale * v[u].z; a.w += scale * v[u].w;
+      acc[i] = a;
+    }
+  }
+  block_barrier(c, 2 * e + 1);
+}
+
+// bf16 variants: 16-byte vectors of 8 values; sums accumulate in fp32 (switch-side with multicast,
+// in registers with peer loads) and are rounded once.
+template <bool MC>
+__global__ void __launch_bounds__(kThreads) allreduce_bf16_kernel(CommCtx c, size_t off, size_t n8, float scale) {
+  const uint32_t e = next_epoch(c);
+  if (!block_barrier(c, 2 * e)) return;
+  const size_t per = (n8 + c.world - 1) / c.world;
+  const size_t lo = (size_t)c.rank * per, hi = min(n8, lo + per);
+  const size_t stride = gstride();
+  for (size_t i0 = lo + gtid(); i0 < hi; i0 += stride * kUnroll) {
+    float v[kUnroll][8];
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+      const size_t i = i0 + u * stride;
+      if (i >= hi) break;
+      const size_t b = off + i * 16;
+      if constexpr (MC) {
+        bf16x8_to_f32(mc_ld_reduce_bf16x8(c.mc + b), v[u]);
+      } else {
+#pragma unroll
+        for (int t = 0; t < 8; ++t) v[u][t] = 0.f;
+        for (int w = 0; w < c.world; ++w) {
+          float x[8];
+          bf16x8_to_f32(__ldcg(reinterpret_cast<const uint4*>(c.peers[w] + b)), x);
+#pragma unroll
+          for (int t = 0; t < 8; ++t) v[u][t] += x[t];
+        }
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+      const size_t i = i0 + u * stride;
+      if (i >= hi) break;
+      const size_t b = off + i * 16;
+#pragma unroll
+      for (int t = 0; t < 8; ++t) v[u][t] *= scale;
+      const uint4 o = f32_to_bf16x8(v[u]);
+      if constexpr (MC) {
+        mc_st_b128(c.mc + b, o);
+      } else {
+        for (int w = 0; w < c.world; ++w) __stcg(reinterpret_cast<uint4*>(c.peers[w] + b), o);
+      }
+    }
+  }
+  block_barrier(c, 2 * e + 1);
+}
+
+template <bool MC>
+__global__ void __launch_bounds__(kThreads) reduce_scatter_acc_bf16_kernel(CommCtx c, size_t off, size_t chunk8,
+                                                                           float* acc, float scale) {
+  const uint32_t e = next_epoch(c);
+  if (!block_barrier(c, 2 * e)) return;
+  const size_t base = off + (size_t)c.rank * chunk8 * 16;
+  for (size_t i = gtid(); i < chunk8; i += gstride()) {
+    const size_t b = base + i * 16;
+    float v[8];
+    if constexpr (MC) {
+      bf16x8_to_f32(mc_ld_reduce_bf16x8(c.mc + b), v);
+    } else {
+#pragma unroll
+      for (int t = 0; t < 8; ++t) v[t] = 0.f;
+      for (int w = 0; w < c.world; ++w) {
+        float x[8];
+        bf16x8_to_f32(__ldcg(reinterpret_cast<const uint4*>(c.peers[w] + b)), x);
+#pragma unroll
+        for (int t = 0; t < 8; ++t) v[t] += x[t];
+      }
+    }
+    float4* a4 = reinterpret_cast<float4*>(acc + i * 8);
+    float4 a0 = a4[0], a1 = a4[1];
+    a0.x += scale * v[0]; a0.y += scale * v[1]; a0.z += scale * v[2]; a0.w += scale * v[3];
+    a1.x += scale * v[4]; a1.y += scale * v[5]; a1.z += scale * v[6]; a1.w += scale * v[7];
+    a4[0] = a0;
+    a4[1] = a1;
+  }
+  block_barrier(c, 2 * e + 1);
+}
+
+template <bool MC>
+__global__ void __launch_bounds__(kThreads) allgather_kernel(CommCtx c, size_t off, size_t chunk16,
+                                                             const uint4* shard) {
+  const uint32_t e = next_epoch(c);
+  if (!block_barrier(c, 2 * e)) return;
+  const size_t base = off + (size_t)c.rank * chunk16 * 16;
+  for (size_t i = gtid(); i < chunk16; i += gstride()) {
+    const uint4 v = shard[i];
+    const size_t b = base + i * 16;
+    if constexpr (MC) {
+      mc_st_b128(c.mc + b, v);
+    } else {
+      for (int w = 0; w < c.world; ++w) __stcg(reinterpret_cast<uint4*>(c.peers[w] + b), v);
+    }
+  }
+  block_barrier(c, 2 * e + 1);
+}
+
+struct AdamScalars {
+  float lr, beta1, beta2, eps, decay, step, inv_sqrt_bc2, scale_const;
+};
+
+template <bool MC>
+__global__ void __launch_bounds__(kThreads) adamw_allgather_kernel(CommCtx c, size_t param_off, size_t chunk8,
+                                                                   float4* master, float4* m, float4* v,
+                                                                   const float4* g, const float* scale_ptr,
+                                                                   AdamScalars a) {
+  const uint32_t e = next_epoch(c);
+  if (!block_barrier(c, 2 * e)) return;
+  const float scale = (scale_ptr != nullptr ? *scale_ptr : 1.0f) * a.scale_const;
+  const size_t base = param_off + (size_t)c.rank * chunk8 * 16;  // chunk8 groups of 8 bf16 = 16 bytes
+  for (size_t i = gtid(); i < chunk8; i += gstride()) {
+    float out[8];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const size_t k = 2 * i + h;
+      float4 gp = g[k], mp = m[k], vp = v[k], pp = master[k];
+      float gg[4] = {gp.x * scale, gp.y * scale, gp.z * scale, gp.w * scale};
+      float mm[4] = {mp.x, mp.y, mp.z, mp.w}, vv[4] = {vp.x, vp.y, vp.z, vp.w}, pw[4] = {pp.x, pp.y, pp.z, pp.w};
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        mm[t] = a.beta1 * mm[t] + (1.0f - a.beta1) * gg[t];
+        vv[t] = a.beta2 * vv[t] + (1.0f - a.beta2) * gg[t] * gg[t];
+        pw[t] = pw[t] * a.decay - a.step * mm[t] / (sqrtf(vv[t]) * a.inv_sqrt_bc2 + a.eps);
+        out[4 * h + t] = pw[t];
+      }
+      m[k] = make_float4(mm[0], mm[1], mm[2], mm[3]);
+      v[k] = make_float4(vv[0], vv[1], vv[2], vv[3]);
+      master[k] = make_float4(pw[0], pw[1], pw[2], pw[3]);
+    }
+    const uint4 o = f32_to_bf16x8(out);
+    const size_t b = base + i * 16;
+    if constexpr (MC) {
+      mc_st_b128(c.mc + b, o);
+    } else {
+      for (int w = 0; w < c.world; ++w) __stcg(reinterpret_cast<uint4*>(c.peers[w] + b), o);
+    }
+  }
+  block_barrier(c, 2 * e + 1);
+}
+
+__global__ void barrier_kernel(CommCtx c) {
+  const uint32_t e = next_epoch(c);
+  block_barrier(c, 2 * e);
+  block_barrier(c, 2 * e + 1);
+}
+
+// Waits on a signal-pad slot that no peer writes; returns once the deadline passes.
+__global__ void wait_unsignalled_kernel(CommCtx c, uint64_t timeout_ns) {
+  if (threadIdx.x != 0) return;
+  const uint32_t* slot =
+      reinterpret_cast<const uint32_t*>(c.pads[c.rank]) + (kCommMaxBlocks - 1) * kCommMaxWorld + (kCommMaxWorld - 1);
+  const uint64_t t0 = globaltimer_ns();
+  while (ld_acquire_sys(slot) != 0xFFFFFFFFu) {
+    if (globaltimer_ns() - t0 > timeout_ns) {
+      report_error(c.errs, kErrCommWait, -1);
+      return;
+    }
+  }
+}
+
+void check_ctx(const CommCtx& c) {
+  B200_CHECK(c.world >= 1 && c.world <= kCommMaxWorld, "comm: world size out of range");
+  B200_CHECK(c.blocks >= 1 && c.blocks < kCommMaxBlocks, "comm: block count out of range");
+}
+
+}  // namespace
+
+// All collectives of one communicator use the same grid size (c.blocks) so that per-block epochs
+// advance identically on every rank whatever the message size.
+void comm_allreduce_f32(const CommCtx& c, size_t off, size_t n, float scale, cudaStream_t s) {
+  check_ctx(c);
+  B200_CHECK(n % 4 == 0 && off % 16 == 0, "comm_allreduce_f32: n must be a multiple of 4 and offset 16-aligned");
+  if (c.mc)
+    allreduce_f32_kernel<true><<<c.blocks, kThreads, 0, s>>>(c, off, n / 4, scale);
+  else
+    allreduce_f32_kernel<false><<<c.blocks, kThreads, 0, s>>>(c, off, n / 4, scale);
+  B200_CUDA_CHECK(cudaGetLastError());
+  count_launch();
+}
+
+void comm_reduce_scatter_acc_f32(const CommCtx& c, size_t off, size_t chunk, float* acc, float scale, cudaStream_t s) {
+  check_ctx(c);
+  B200_CHECK(chunk % 4 == 0 && off % 16 == 0 && (reinterpret_cast<uintptr_t>(acc) & 15) == 0,
+             "comm_reduce_scatter: chunk must be a multiple of 4, offset and acc 16-aligned");
+  auto* a4 = reinterpret_cast<float4*>(acc);
+  if (c.mc)
+    reduce_scatter_acc_f32_kernel<true><<<c.blocks, kThreads, 0, s>>>(c, off, chunk / 4, a4, scale);
+  else
+    reduce_scatter_acc_f32_kernel<false><<<c.blocks, kThreads, 0, s>>>(c, off, chunk / 4, a4, scale);
+  B200_CUDA_CHECK(cudaGetLastError());
+  count_launch();
+}
+
+void comm_allreduce_bf16(const CommCtx& c, size_t off, size_t n, float scale, cudaStream_t s) {
+  check_ctx(c);
+  B200_CHECK(n % 8 == 0 && off % 16 == 0, "comm_allreduce_bf16: n must be a multiple of 8 and offset 16-aligned");
+  if (c.mc)
+    allreduce_bf16_kernel<true><<<c.blocks, kThreads, 0, s>>>(c, off, n / 8, scale);
+  else
+    allreduce_bf16_kernel<false><<<c.blocks, kThreads, 0, s>>>(c, off, n / 8, scale);
+  B200_CUDA_CHECK(cudaGetLastError());
+  count_launch();
+}
+
+void comm_reduce_scatter_acc_bf16(const CommCtx& c, size_t off, size_t chunk, float* acc, float scale,
+                                  cudaStream_t s) {
+  check_ctx(c);
+  B200_CHECK(chunk % 8 == 0 && off % 16 == 0 && (reinterpret_cast<uintptr_t>(acc) & 15) == 0,
+             "comm_reduce_scatter_bf16: chunk must be a multiple of 8, offset and acc 16-aligned");
+  if (c.mc)
+    reduce_scatter_acc_bf16_kernel<true><<<c.blocks, kThreads, 0, s>>>(c, off, chunk / 8, acc, scale);
+  else
+    reduce_scatter_acc_bf16_kernel<false><<<c.blocks, kThreads, 0, s>>>(c, off, chunk / 8, acc, scale);
+  B200_CUDA_CHECK(cudaGetLastError());
+  count_launch();
+}
+
+void comm_allgather(const CommCtx& c, size_t off, size_t chunk_bytes, const void* shard, cudaStream_t s) {
+  check_ctx(c);
+  B200_CHECK(chunk_bytes % 16 == 0 && off % 16 == 0 && (reinterpret_cast<uintptr_t>(shard) & 15) == 0,
+             "comm_allgather: 16-byte granularity required");
+  const auto* src = reinterpret_cast<const uint4*>(shard);
+  if (c.mc)
+    allgather_kernel<true><<<c.blocks, kThreads, 0, s>>>(c, off, chunk_bytes / 16, src);
+  else
+    allgather_kernel<false><<<c.blocks, kThreads, 0, s>>>(c, off, chunk_bytes / 16, src);
+  B200_CUDA_CHECK(cudaGetLastError());
+  count_launch();
+}
+
+void comm_adamw_allgather(const CommCtx& c, size_t param_off, size_t chunk, float* master, float* m, float* v,
+                          const float* grad, const float* scale_ptr, float scale_const, float lr, float beta1,
+                          float beta2, float eps, float wd, int step, cudaStream_t s) {
+  check_ctx(c);
+  B200_CHECK(chunk % 8 == 0 && param_off % 16 == 0, "comm_adamw_allgather: chunk must be a multiple of 8");
+  AdamScalars a;
+  a.lr = lr;
+  a.beta1 = beta1;
+  a.beta2 = beta2;
+  a.eps = eps;
+  a.decay = 1.0f - lr * wd;
+  a.step = (float)(lr / (1.0 - std::pow((double)beta1, (double)step)));
+  a.inv_sqrt_bc2 = (float)(1.0 / std::sqrt(1.0 - std::pow((double)beta2, (double)step)));
+  a.scale_const = scale_const;
+  auto* M = reinterpret_cast<float4*>(master);
+  auto* Mm = reinterpret_cast<float4*>(m);
+  auto* Vv = reinterpret_cast<float4*>(v);
+  auto* G = reinterpret_cast<const float4*>(grad);
+  if (c.mc)
+    adamw_allgather_kernel<true><<<c.blocks, kThreads, 0, s>>>(c, param_off, chunk / 8, M, Mm, Vv, G, scale_ptr, a);
+  else
+    adamw_allgather_kernel<false><<<c.blocks, kThreads, 0, s>>>(c, param_off, chunk / 8, M, Mm, Vv, G, scale_ptr, a);
+  B200_CUDA_CHECK(cudaGetLastError());
+  count_launch();
+}
+
+void comm_barrier(const CommCtx& c, cudaStream_t s) {
+  check_ctx(c);
+  barrier_kernel<<<c.blocks, 32, 0, s>>>(c);
+  B200_CUDA_CHECK(cudaGetLastError());
+  count_launch();
+}
+
+void comm_wait_unsignalled(const CommCtx& c, uint64_t timeout_ns, cudaStream_t s) {
+  wait_unsignalled_kernel<<<1, 32, 0, s>>>(c, timeout_ns);
+  B200_CUDA_CHECK(cudaGetLastError());
+  count_launch();
+}
+
+}  // namespace b200

@@ -1,9 +1,53 @@
 // NVLink / NVSwitch collective kernels over symmetric memory (see comm.cu).
+//
+// Every rank owns one buffer of a symmetric allocation; `peers[r]` is rank r's buffer as a
+// pointer valid on this GPU (NVLink peer mapping), `mc` the NVSwitch multicast address of the
+// same allocation (0 when the switch cannot multicast).  Offsets are in bytes from the buffer
+// base and identical on every rank.
 #pragma once
 
 #include <cuda_runtime.h>
 #include <stddef.h>
 #include <stdint.h>
 
+#include "common.cuh"
+
 namespace b200 {
+
+constexpr int kCommMaxWorld = 8;
+constexpr int kCommMaxBlocks = 64;
+
+struct CommCtx {
+  int rank;
+  int world;
+  uint64_t peers[kCommMaxWorld];  // rank r's buffer base, mapped on this GPU
+  uint64_t mc;                     // multicast base (0 = none)
+  uint64_t pads[kCommMaxWorld];   // rank r's signal pad base, mapped on this GPU
+  uint32_t* epochs;                // [kCommMaxBlocks] per-block barrier epochs (local memory)
+  DeviceErrors* errs;
+  uint64_t timeout_ns;
+  int blocks;                      // grid size used by every collective of this communicator
+};
+
+// In place: region[0, n) = scale * sum_ranks(region); fp32.
+void comm_allreduce_f32(const CommCtx& c, size_t off_bytes, size_t n, float scale, cudaStream_t s);
+// acc[0, chunk) += scale * sum_ranks(region[rank*chunk, (rank+1)*chunk)); fp32 region and acc.
+void comm_reduce_scatter_acc_f32(const CommCtx& c, size_t off_bytes, size_t chunk, float* acc, float scale,
+                                 cudaStream_t s);
+// bf16 variants (fp32 accumulation of the sum; the reduce-scatter accumulates into an fp32 shard).
+void comm_allreduce_bf16(const CommCtx& c, size_t off_bytes, size_t n, float scale, cudaStream_t s);
+void comm_reduce_scatter_acc_bf16(const CommCtx& c, size_t off_bytes, size_t chunk, float* acc, float scale,
+                                  cudaStream_t s);
+// Every rank's `shard` (chunk_bytes, 16-byte multiple) lands at region[rank*chunk_bytes] on all ranks.
+void comm_allgather(const CommCtx& c, size_t off_bytes, size_t chunk_bytes, const void* shard, cudaStream_t s);
+// AdamW on this rank's fp32 shard, then the bf16 result is written into every rank's parameter
+// region at [rank*chunk] (fused update + all-gather).
+void comm_adamw_allgather(const CommCtx& c, size_t param_off_bytes, size_t chunk, float* master, float* m, float* v,
+                          const float* grad, const float* scale_ptr, float scale_const, float lr, float beta1,
+                          float beta2, float eps, float wd, int step, cudaStream_t s);
+// Standalone barrier among the ranks (every block of the communicator's grid).
+void comm_barrier(const CommCtx& c, cudaStream_t s);
+// A wait that nobody satisfies: used by tests to exercise the bounded-wait error path.
+void comm_wait_unsignalled(const CommCtx& c, uint64_t timeout_ns, cudaStream_t s);
+
 }  // namespace b200

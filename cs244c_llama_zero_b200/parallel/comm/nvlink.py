@@ -1,0 +1,179 @@
+"""NVLink / NVSwitch collectives over symmetric memory (``--collective-impl nvls`` / ``p2p``).
+
+Buffers that the ZeRO engines reduce or gather (the flat fp32 gradient buffer, the flat model-dtype
+parameter buffer, ZeRO-3 staging buffers) are allocated as symmetric memory: torch's symmetric-memory
+rendezvous maps every rank's buffer on every GPU and, when the NVSwitch supports it, binds the
+allocation to a multicast object.  The collectives on those buffers are this package's own sm_100a
+kernels (``ops/csrc/comm.cu``):
+
+* ``allreduce_scaled_``          NVLS ``multimem.ld_reduce`` + ``multimem.st`` with the 1/W scale fused
+* ``reduce_scatter_accumulate_`` ``multimem.ld_reduce`` of this rank's chunk, scaled and accumulated into
+                                 the fp32 gradient shard in the same kernel
+* ``allgather_into``             ``multimem.st`` of the shard into every rank's buffer
+* ``adamw_allgather``            AdamW on the shard fused with the multicast all-gather of the bf16 result
+
+``impl="p2p"`` runs the same kernels with plain peer loads/stores instead of multicast.  Calls on
+tensors that are not part of a registered symmetric buffer (and the reference-compatible
+``allreduce`` / ``reduce_scatter`` / ``allgather`` API) fall back to NCCL, like ``TorchCollectives``.
+
+Every device-side wait is bounded (``ZB_COMM_TIMEOUT_S``, default 30 s); an expired wait is recorded in
+the device error record, which :meth:`NvlinkCollectives.check_errors` turns into a ``CommTimeoutError``.
+"""
+
+from __future__ import annotations
+
+import os
+from typing import List, Optional, Tuple
+
+import torch
+import torch.distributed as dist
+
+from ..collectives import TorchCollectives, _maybe_simulate_collective_delay, _world
+
+
+class CommTimeoutError(RuntimeError):
+    """A device-side wait of a collective kernel expired (a peer never arrived)."""
+
+
+def _timeout_ns() -> int:
+    return int(float(os.environ.get("ZB_COMM_TIMEOUT_S", "30")) * 1e9)
+
+
+class SymmetricBuffer:
+    """One symmetric allocation + the kernel context that addresses it on every rank."""
+
+    def __init__(self, numel: int, dtype: torch.dtype, device: torch.device, use_multicast: bool,
+                 group=None, blocks: int = 48) -> None:
+        import torch.distributed._symmetric_memory as symm_mem
+
+        from ... import ops
+
+        group = group or dist.group.WORLD
+        self.tensor = symm_mem.empty(numel, dtype=dtype, device=device)
+        self.tensor.zero_()
+        self.handle = symm_mem.rendezvous(self.tensor, group)
+        self.rank = self.handle.rank
+        self.world = self.handle.world_size
+        mc = int(self.handle.multicast_ptr) if use_multicast else 0
+        pad_bytes = int(self.handle.signal_pad_size)
+        # barrier slots: 8 uint32 per block; the last block's slots are reserved for tests
+        blocks = max(1, min(blocks, pad_bytes // (4 * 8) - 1, 63))
+        self.epochs = torch.zeros(64, dtype=torch.int32, device=device)
+        self.ctx = ops.load_extension().CommContext(
+            self.rank, self.world, [int(p) for p in self.handle.buffer_ptrs], mc,
+            [int(p) for p in self.handle.signal_pad_ptrs], self.epochs, blocks, _timeout_ns())
+        self.multicast = mc != 0
+        self.base = self.tensor.data_ptr()
+        self.nbytes = self.tensor.numel() * self.tensor.element_size()
+
+    def offset_of(self, t: torch.Tensor) -> Optional[int]:
+        ptr = t.data_ptr()
+        if self.base <= ptr and ptr + t.numel() * t.element_size() <= self.base + self.nbytes:
+            return ptr - self.base
+        return None
+
+
+class NvlinkCollectives(TorchCollectives):
+    """ZeRO collectives as NVLink/NVSwitch kernels on symmetric buffers; NCCL for everything else."""
+
+    supports_fused = True
+
+    def __init__(self, device: Optional[torch.device] = None, use_multicast: bool = True) -> None:
+        self.name = "nvls" if use_multicast else "p2p"
+        self.device = device or torch.device("cuda", torch.cuda.current_device())
+        self.use_multicast = use_multicast
+        self.buffers: List[SymmetricBuffer] = []
+
+    # -- allocation --------------------------------------------------------------------------
+    def alloc(self, numel: int, dtype: torch.dtype) -> torch.Tensor:
+        """A zero-filled symmetric buffer (collective call: every rank must allocate the same sizes)."""
+        buf = SymmetricBuffer(int(numel), dtype, self.device, self.use_multicast)
+        self.buffers.append(buf)
+        return buf.tensor
+
+    def _locate(self, t: torch.Tensor) -> Optional[Tuple[SymmetricBuffer, int]]:
+        if not t.is_cuda or not t.is_contiguous():
+            return None
+        for buf in self.buffers:
+            off = buf.offset_of(t)
+            if off is not None and buf.tensor.dtype == t.dtype:
+                return buf, off
+        return None
+
+    def check_errors(self) -> None:
+        from ... import ops
+
+        code, where, block, count = ops.load_extension().read_device_errors()
+        if code:
+            raise CommTimeoutError(f"device wait expired (code {code}, peer/role {where}, block {block}, {count} reports)")
+
+    # -- fused entry points ------------------------------------------------------------------------
+    def allreduce_scaled_(self, flat: torch.Tensor, scale: float) -> torch.Tensor:
+        hit = self._locate(flat)
+        if hit is None or flat.dtype not in (torch.float32, torch.bfloat16) or flat.numel() % 8:
+            return super().allreduce_scaled_(flat, scale)
+        buf, off = hit
+        if flat.dtype == torch.float32:
+            buf.ctx.allreduce_f32(off, flat.numel(), scale)
+        else:
+            buf.ctx.allreduce_bf16(off, flat.numel(), scale)
+        _maybe_simulate_collective_delay(flat.numel() * flat.element_size(), self._w())
+        return flat
+
+    def reduce_scatter_accumulate_(self, acc: torch.Tensor, flat: torch.Tensor, scale: float) -> torch.Tensor:
+        hit = self._locate(flat)
+        world = self._w()
+        if (hit is None or flat.dtype not in (torch.float32, torch.bfloat16) or flat.numel() % (8 * world)
+                or acc.dtype != torch.float32):
+            return super().reduce_scatter_accumulate_(acc, flat, scale)
+        buf, off = hit
+        if flat.dtype == torch.float32:
+            buf.ctx.reduce_scatter_acc_f32(off, flat.numel() // world, acc, scale)
+        else:
+            buf.ctx.reduce_scatter_acc_bf16(off, flat.numel() // world, acc, scale)
+        _maybe_simulate_collective_delay(acc.numel() * flat.element_size(), world)
+        return acc
+
+    def reduce_scatter_into(self, out: torch.Tensor, flat: torch.Tensor) -> torch.Tensor:
+        if out.dtype == torch.float32 and self._locate(flat) is not None:
+            out.zero_()
+            return self.reduce_scatter_accumulate_(out, flat, 1.0)
+        return super().reduce_scatter_into(out, flat)
+
+    def allgather_into(self, out: torch.Tensor, shard: torch.Tensor) -> torch.Tensor:
+        hit = self._locate(out)
+        world = self._w()
+        chunk_bytes = shard.numel() * shard.element_size()
+        if (hit is None or out.numel() != shard.numel() * world or chunk_bytes % 16 or not shard.is_contiguous()
+                or shard.dtype != out.dtype):
+            return super().allgather_into(out, shard)
+        buf, off = hit
+        buf.ctx.allgather(off, chunk_bytes, shard)
+        _maybe_simulate_collective_delay(chunk_bytes, world)
+        return out
+
+    def adamw_allgather(self, params_flat: torch.Tensor, master: torch.Tensor, exp_avg: torch.Tensor,
+                        exp_avg_sq: torch.Tensor, grad: torch.Tensor, scale, cfg, step: int) -> bool:
+        """AdamW on the shard + multicast all-gather of the bf16 result; False if not applicable."""
+        hit = self._locate(params_flat)
+        world = self._w()
+        chunk = master.numel()
+        if (hit is None or params_flat.dtype != torch.bfloat16 or params_flat.numel() != chunk * world
+                or chunk % 8 or grad.dtype != torch.float32):
+            return False
+        buf, off = hit
+        scale_t = scale.reshape(1).float() if isinstance(scale, torch.Tensor) else None
+        scale_c = 1.0 if isinstance(scale, torch.Tensor) else float(scale if scale is not None else 1.0)
+        buf.ctx.adamw_allgather(off, chunk, master, exp_avg, exp_avg_sq, grad.contiguous(), scale_t, scale_c, cfg.lr,
+                                cfg.betas[0], cfg.betas[1], cfg.eps, cfg.weight_decay, step)
+        return True
+
+    def barrier(self) -> None:
+        if self.buffers:
+            self.buffers[0].ctx.barrier()
+        else:
+            dist.barrier()
+
+    @staticmethod
+    def _w() -> int:
+        return _world()

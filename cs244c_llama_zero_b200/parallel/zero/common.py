@@ -192,7 +192,7 @@ class FlatParamSpace:
 
     def __init__(self, meta: FlatParamMetadata, world_size: int, rank: int, with_grads: bool = True,
                  param_dtype: Optional[torch.dtype] = None, device: Optional[torch.device] = None,
-                 alignment: int = 64) -> None:
+                 alignment: int = 64, allocator=None) -> None:
         self.meta = meta
         self.world_size = world_size
         self.rank = rank
@@ -200,13 +200,18 @@ class FlatParamSpace:
         self.param_dtype = param_dtype or model_param_dtype(meta)
         self.offsets, self.numel, self.chunk = aligned_layout(meta, world_size, alignment)
         self.padded_numel = self.chunk * world_size
-        self.params = torch.zeros(self.padded_numel, dtype=self.param_dtype, device=self.device)
+        # ``allocator(numel, dtype)`` lets a collectives implementation place the buffers in memory
+        # its kernels can address on every rank (symmetric memory); default: ordinary device memory.
+        alloc = allocator or (lambda n, dt: torch.zeros(n, dtype=dt, device=self.device))
+        self.params = alloc(self.padded_numel, self.param_dtype)
+        self.params.zero_()
         for p, off in zip(meta.params, self.offsets):
             self.params[off : off + p.numel()].copy_(p.data.reshape(-1))
         self.grads: Optional[torch.Tensor] = None
         self.bind_params()
         if with_grads:
-            self.grads = torch.zeros(self.padded_numel, dtype=torch.float32, device=self.device)
+            self.grads = alloc(self.padded_numel, torch.float32)
+            self.grads.zero_()
             self.bind_grads()
 
     # -- views ------------------------------------------------------------------------

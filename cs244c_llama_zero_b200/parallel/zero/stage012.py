@@ -47,7 +47,8 @@ class _FlatEngine(ZeROEngineBase):
     def __init__(self, model: nn.Module, **kwargs) -> None:
         super().__init__(model, **kwargs)
         self.meta = build_flat_param_metadata(model)
-        self.space = FlatParamSpace(self.meta, self.world_size, self.rank, with_grads=True)
+        allocator = getattr(self.collectives, "alloc", None) if self.world_size > 1 and self.device.type == "cuda" else None
+        self.space = FlatParamSpace(self.meta, self.world_size, self.rank, with_grads=True, allocator=allocator)
         if self.shard_optimizer:
             master_src = self.space.shard(self.space.params)
         else:
@@ -83,6 +84,18 @@ class _FlatEngine(ZeROEngineBase):
         with self.clock.measure("optimizer"):
             adamw_update_(self._master, self._exp_avg, self._exp_avg_sq, grads, self.adam, self.step_count,
                           grad_scale=scale, param_out=self._param_out())
+
+    def _adamw_and_gather(self, grads: torch.Tensor, scale: torch.Tensor) -> None:
+        """Sharded update followed by the parameter all-gather; one fused kernel when available."""
+        fused = getattr(self.collectives, "adamw_allgather", None) if self.world_size > 1 else None
+        if fused is not None and self.device.type == "cuda":
+            with self.clock.measure("post_allgather", tensor_num_bytes(self.space.shard(self.space.params))):
+                done = fused(self.space.params, self._master, self._exp_avg, self._exp_avg_sq, grads, scale, self.adam,
+                             self.step_count)
+            if done:
+                return
+        self._adamw(grads, scale)
+        self._allgather_params()
 
     def _param_out(self) -> torch.Tensor:
         return self.space.shard(self.space.params) if self.shard_optimizer else self.space.params
@@ -202,9 +215,8 @@ class ZeROStage1Optimizer(_ShardedStateMixin, _FlatEngine):
             self._record_memory_event("measured_step_stage1_post_allreduce")
         norm = sum_of_squares(grads).sqrt()
         self.step_count += 1
-        self._adamw(self.space.shard(grads), clip_coefficient(norm, max_grad_norm))
         self._record_memory_event("measured_step_stage1_pre_allgather")
-        self._allgather_params()
+        self._adamw_and_gather(self.space.shard(grads), clip_coefficient(norm, max_grad_norm))
         self._record_memory_event("measured_step_stage1_post_allgather")
         return norm
 
@@ -266,10 +278,9 @@ class ZeROStage2Optimizer(_ShardedStateMixin, _FlatEngine):
         self._flush_flat_grad_buffer()
         norm = global_norm_from_local_sq(sum_of_squares(self.grad_shard), sharded=self.world_size > 1)
         self.step_count += 1
-        self._adamw(self.grad_shard, clip_coefficient(norm, max_grad_norm))
         self._record_memory_event("measured_step_stage2_pre_allgather")
         with self.collectives.label_scope("stage2.step.allgather.updated_param_shard"):
-            self._allgather_params()
+            self._adamw_and_gather(self.grad_shard, clip_coefficient(norm, max_grad_norm))
         self._record_memory_event("measured_step_stage2_post_allgather")
         self._record_memory_event("measured_step_stage2_post_step_free_grad_shard")
         return norm

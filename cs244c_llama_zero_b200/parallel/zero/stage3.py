@@ -90,7 +90,9 @@ class Stage3ParamHandle:
         if self.materialized:
             return
         eng = self.engine
-        full = torch.empty(self.padded_numel, dtype=self.param_dtype, device=self.device)
+        staging = eng._staging_params(self.padded_numel, self.param_dtype) if phase in ("forward", "backward") else None
+        full = staging if staging is not None else torch.empty(self.padded_numel, dtype=self.param_dtype,
+                                                              device=self.device)
         category = {"forward": "forward_allgather", "backward": "backward_allgather"}.get(phase, "summon_allgather")
         with eng.clock.measure(category, self.full_param_bytes):
             with eng.collectives.label_scope(f"stage3.{phase}.allgather.{self.name}"):
@@ -114,7 +116,11 @@ class Stage3ParamHandle:
 
     def begin_grad(self) -> torch.Tensor:
         """Full-size fp32 gradient buffer bound to every parameter's ``main_grad``."""
-        buf = torch.zeros(self.padded_numel, dtype=torch.float32, device=self.device)
+        buf = self.engine._staging_grads(self.padded_numel)
+        if buf is None:
+            buf = torch.zeros(self.padded_numel, dtype=torch.float32, device=self.device)
+        else:
+            buf.zero_()
         for p, off, shape in zip(self.meta.params, self.offsets, self.meta.shapes):
             p.main_grad = buf[off : off + shape.numel()].view(shape)
         return buf
@@ -235,6 +241,26 @@ class ZeROStage3Optimizer(ZeROEngineBase):
         self._build_module_runners()
         self.model._zero3_executor = self
         self._reshard_all_params()
+        # Symmetric staging for the per-module all-gather (two slots, so one module can be gathered
+        # while the previous one is still in use) and for the backward reduce-scatter input.
+        self._stage_params: List[torch.Tensor] = []
+        self._stage_slot = 0
+        self._stage_grads: Optional[torch.Tensor] = None
+        alloc = getattr(self.collectives, "alloc", None)
+        if alloc is not None and self.world_size > 1 and self.device.type == "cuda":
+            largest = max(h.padded_numel for h in self._handle_order)
+            self._stage_params = [alloc(largest, self.param_dtype) for _ in range(2)]
+            self._stage_grads = alloc(largest, torch.float32)
+
+    def _staging_params(self, numel: int, dtype: torch.dtype) -> Optional[torch.Tensor]:
+        if not self._stage_params or dtype != self._stage_params[0].dtype:
+            return None
+        buf = self._stage_params[self._stage_slot]
+        self._stage_slot ^= 1
+        return buf[:numel]
+
+    def _staging_grads(self, numel: int) -> Optional[torch.Tensor]:
+        return None if self._stage_grads is None else self._stage_grads[:numel]
 
     def _module_specs(self) -> List[Tuple[str, nn.Module]]:
         specs = [("tok_embeddings", self.model.tok_embeddings)]
