@@ -21,6 +21,10 @@
 // from a pre-pass.
 #include <cuda.h>
 
+#include <cstdio>
+#include <mutex>
+
+#include "attention_bwd_noalloc.h"
 #include "common.cuh"
 #include "gemm.h"
 #include "kernels.h"
@@ -445,4 +449,132 @@ void attention_bwd(const AttnBwdParams& p, cudaStream_t s) {
   count_launch(3);
 }
 
+// ---------------------------------------------------------------------------------------------
+// Allocation-free variant (declared in attention_bwd_noalloc.h, which documents the contract).
+// The scratch that the regular path takes from its caller (error record, delta, dQ accumulator)
+// lives in one fixed device array; host code reaches it only through the address returned by
+// cudaGetSymbolAddress, because the array's name in host code is a host-side stand-in.
+// ---------------------------------------------------------------------------------------------
+namespace {
+
+static __device__ __align__(256) unsigned char g_attn_bwd_scratch[B200_ATTN_BWD_NOALLOC_SCRATCH_BYTES];
+
+constexpr int kNoAllocMaxDevices = 64;
+std::mutex g_noalloc_mu;
+unsigned char* g_noalloc_scratch_addr[kNoAllocMaxDevices] = {};  // device address of the array, per device
+
+constexpr size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+
+// Once per device, with that device current: resolve the array's device address and raise the
+// bwd kernels' dynamic shared-memory limit.  Returns nullptr (after printing why) on failure.
+unsigned char* noalloc_scratch_for_current_device() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kNoAllocMaxDevices) return nullptr;
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (g_noalloc_scratch_addr[dev] != nullptr) return g_noalloc_scratch_addr[dev];
+  void* addr = nullptr;
+  cudaError_t e = cudaGetSymbolAddress(&addr, g_attn_bwd_scratch);
+  if (e != cudaSuccess || addr == nullptr) {
+    std::fprintf(stderr, "b200_attention_bwd_noalloc: cudaGetSymbolAddress failed on device %d: %s\n", dev,
+                 cudaGetErrorString(e));
+    return nullptr;
+  }
+  e = cudaFuncSetAttribute(attn_bwd_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, AttnBwdCfg<64>::SMEM_BYTES);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(attn_bwd_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             AttnBwdCfg<128>::SMEM_BYTES);
+  if (e != cudaSuccess) {
+    std::fprintf(stderr, "b200_attention_bwd_noalloc: cudaFuncSetAttribute failed: %s\n", cudaGetErrorString(e));
+    return nullptr;
+  }
+  g_noalloc_scratch_addr[dev] = static_cast<unsigned char*>(addr);
+  return g_noalloc_scratch_addr[dev];
+}
+
+}  // namespace
+
 }  // namespace b200
+
+extern "C" int b200_attention_bwd_noalloc(const void* qkv, int ld, int k_col, int v_col, const void* out,
+                                          const void* dout, int ld_out, const float* lse, void* dqkv,
+                                          const float* rope_cos, const float* rope_sin, int batch, int seq, int heads,
+                                          int kv_heads, int head_dim, float scale, cudaStream_t stream) {
+  using namespace b200;
+  const auto aligned16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+  if (qkv == nullptr || out == nullptr || dout == nullptr || lse == nullptr || dqkv == nullptr ||
+      rope_cos == nullptr || rope_sin == nullptr || !aligned16(qkv) || !aligned16(out) || !aligned16(dout) ||
+      !aligned16(dqkv) || !aligned16(lse) || (head_dim != 64 && head_dim != 128) || batch <= 0 || seq <= 0 ||
+      seq % 128 != 0 || heads <= 0 || kv_heads <= 0 || heads % kv_heads != 0 || ld % 8 != 0 || ld_out % 8 != 0 ||
+      k_col % 64 != 0 || v_col % 64 != 0) {
+    std::fprintf(stderr, "b200_attention_bwd_noalloc: invalid arguments (head_dim must be 64 or 128, seq a multiple "
+                         "of 128, heads a multiple of kv_heads, pointers 16-byte aligned)\n");
+    return B200_NOALLOC_ERR_INVALID;
+  }
+  const size_t rows = (size_t)batch * seq;
+  const size_t err_bytes = align256(sizeof(DeviceErrors));
+  const size_t delta_bytes = align256((size_t)batch * heads * seq * sizeof(float));
+  const size_t dq_bytes = align256(rows * heads * head_dim * sizeof(float));
+  const size_t need = err_bytes + delta_bytes + dq_bytes;
+  if (need > B200_ATTN_BWD_NOALLOC_SCRATCH_BYTES) {
+    std::fprintf(stderr,
+                 "b200_attention_bwd_noalloc: problem needs %zu bytes of scratch but the fixed array holds %u "
+                 "(batch=%d seq=%d heads=%d head_dim=%d); use the regular attention backward instead\n",
+                 need, (unsigned)B200_ATTN_BWD_NOALLOC_SCRATCH_BYTES, batch, seq, heads, head_dim);
+    return B200_NOALLOC_ERR_TOO_LARGE;
+  }
+  unsigned char* scratch = noalloc_scratch_for_current_device();
+  if (scratch == nullptr) return B200_NOALLOC_ERR_CUDA;
+  auto* errs = reinterpret_cast<DeviceErrors*>(scratch);
+  float* delta = reinterpret_cast<float*>(scratch + err_bytes);
+  float* dq_acc = reinterpret_cast<float*>(scratch + err_bytes + delta_bytes);
+  try {
+    // The error record and the dQ accumulator must start at zero; delta is fully overwritten.
+    if (cudaMemsetAsync(errs, 0, sizeof(DeviceErrors), stream) != cudaSuccess ||
+        cudaMemsetAsync(dq_acc, 0, rows * heads * head_dim * sizeof(float), stream) != cudaSuccess)
+      return B200_NOALLOC_ERR_CUDA;
+    AttnBwdParams p{};
+    p.qkv = static_cast<const __nv_bfloat16*>(qkv);
+    p.ld = ld;
+    p.k_col = k_col;
+    p.v_col = v_col;
+    p.out = static_cast<const __nv_bfloat16*>(out);
+    p.dout = static_cast<const __nv_bfloat16*>(dout);
+    p.ld_out = ld_out;
+    p.lse = lse;
+    p.delta = delta;
+    p.dq_acc = dq_acc;
+    p.dqkv = static_cast<__nv_bfloat16*>(dqkv);
+    p.rope_cos = rope_cos;
+    p.rope_sin = rope_sin;
+    p.batch = batch;
+    p.seq = seq;
+    p.heads = heads;
+    p.kv_heads = kv_heads;
+    p.head_dim = head_dim;
+    p.scale = scale;
+    const int warps = (int)rows * heads;
+    attn_delta_kernel<<<(warps * 32 + 255) / 256, 256, 0, stream>>>(p.out, p.dout, p.ld_out, p.delta, (int)rows, seq,
+                                                                    heads, head_dim);
+    const CUtensorMap tq = make_tmap_bf16_2d(p.qkv, (uint64_t)ld, (uint64_t)rows, (uint64_t)ld, 64, 128);
+    const CUtensorMap tdo = make_tmap_bf16_2d(p.dout, (uint64_t)ld_out, (uint64_t)rows, (uint64_t)ld_out, 64, 128);
+    const dim3 grid(seq / 128, kv_heads, batch);
+    if (head_dim == 64)
+      attn_bwd_kernel<64><<<grid, BWD_THREADS, AttnBwdCfg<64>::SMEM_BYTES, stream>>>(tq, tdo, p, errs);
+    else
+      attn_bwd_kernel<128><<<grid, BWD_THREADS, AttnBwdCfg<128>::SMEM_BYTES, stream>>>(tq, tdo, p, errs);
+    const size_t work = rows * heads * (head_dim / 16);
+    const int blocks = (int)std::min<size_t>((work + 255) / 256, (size_t)num_sms_cached() * 16);
+    attn_dq_convert_kernel<<<blocks, 256, 0, stream>>>(dq_acc, p.dqkv, ld, (int)rows, seq, heads, head_dim, rope_cos,
+                                                       rope_sin);
+    count_launch(3);
+  } catch (const std::exception& ex) {
+    std::fprintf(stderr, "b200_attention_bwd_noalloc: %s\n", ex.what());
+    return B200_NOALLOC_ERR_INVALID;
+  }
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    std::fprintf(stderr, "b200_attention_bwd_noalloc: launch failed: %s\n", cudaGetErrorString(e));
+    return B200_NOALLOC_ERR_CUDA;
+  }
+  return B200_NOALLOC_OK;
+}
