@@ -84,11 +84,11 @@ def main(args, ClockSampler, base_record, emit, time_device, time_wall, random_b
             step(dev[it["i"] % len(dev)])
             it["i"] += 1
 
-        for _ in range(args.warmup):
-            device_step()
         sampler = ClockSampler([local]) if stage == args.headline_stage and rank == 0 else None
         if sampler:
             sampler.__enter__()
+        for _ in range(args.warmup):
+            device_step()
         ms = time_device(device_step, args.steps)
         if sampler:
             sampler.__exit__(None, None, None)

@@ -69,7 +69,7 @@ class ClockSampler:
             os.makedirs(os.path.dirname(self.path), exist_ok=True)
             self.fh = open(self.path, "w")
             self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                                          "-lms", "200"], stdout=self.fh, stderr=subprocess.DEVNULL)
+                                          "-lms", "100"], stdout=self.fh, stderr=subprocess.DEVNULL)
         except (OSError, FileNotFoundError):
             self.proc = None
         return self
@@ -226,13 +226,15 @@ def run_mine(args) -> None:
             sess.train_step(dev[it["i"] % len(dev)])
             it["i"] += 1
 
+        # The sampler starts before the warm-up so that short timed regions still get samples taken
+        # under steady load; it stops right after the timed steps.
+        sampler = ClockSampler([local]) if stage == args.headline_stage and rank == 0 else None
+        if sampler:
+            sampler.__enter__()
         for _ in range(args.warmup):
             device_step()
         torch.cuda.synchronize()
         launches_before = ops.launch_count()
-        sampler = ClockSampler([local]) if stage == args.headline_stage and rank == 0 else None
-        if sampler:
-            sampler.__enter__()
         ms = time_device(device_step, args.steps)
         if sampler:
             sampler.__exit__(None, None, None)
