@@ -1,0 +1,46 @@
+"""Operational scripts on CPU: gloo sanity / all-reduce benchmark (2 ranks), loopback shaper check, repo bundle."""
+
+from __future__ import annotations
+
+import json
+import subprocess
+import sys
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parents[1]
+
+
+def _torchrun(script: str, port: int, *args: str) -> str:
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nproc-per-node", "2", "--master-addr", "127.0.0.1",
+           "--master-port", str(port), str(ROOT / "scripts" / script), *args]
+    return subprocess.run(cmd, check=True, capture_output=True, text=True, timeout=300, cwd=ROOT).stdout
+
+
+def test_distributed_sanity_gloo():
+    assert "all_reduce_sum=3.0" in _torchrun("distributed_sanity.py", 29631)
+
+
+def test_benchmark_allreduce_gloo():
+    line = [ln for ln in _torchrun("benchmark_allreduce.py", 29632, "--numel", "4096", "--iters", "2").splitlines()
+            if ln.startswith("{")][-1]
+    rec = json.loads(line)
+    assert rec["world_size"] == 2 and rec["payload_mb"] == 4096 * 4 / 1e6 and rec["mean_ms"] > 0
+
+
+def test_validate_socket_shaper(tmp_path):
+    out = tmp_path / "v.json"
+    subprocess.run([sys.executable, str(ROOT / "scripts" / "validate_bandwidth.py"), "socket", "--bw-gbps", "0.2",
+                    "--bytes", "4000000", "--tolerance", "0.5", "--json-output", str(out)], check=True,
+                   capture_output=True, timeout=300)
+    rec = json.loads(out.read_text())
+    assert rec["passed"] and rec["shaped_gbps"] < rec["unshaped_gbps"]
+
+
+def test_repo_bundle_roundtrip(tmp_path):
+    archive = tmp_path / "b.tar.gz"
+    subprocess.run(["bash", str(ROOT / "scripts" / "repo_bundle.sh"), "pack", str(archive)], check=True,
+                   capture_output=True)
+    dest = tmp_path / "unpacked"
+    subprocess.run(["bash", str(ROOT / "scripts" / "repo_bundle.sh"), "unpack", str(archive), str(dest)], check=True,
+                   capture_output=True)
+    assert (dest / "bench.py").exists() and not (dest / ".git").exists()
