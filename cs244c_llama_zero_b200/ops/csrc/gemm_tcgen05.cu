@@ -44,31 +44,84 @@ constexpr int BK = 64;  // 64 bf16 = 128 bytes = one swizzle row
 constexpr int A_STAGE_BYTES = BM * BK * 2;
 constexpr int NUM_THREADS = 320;
 
+constexpr int kEpiWarps = 8;
+constexpr int kChunkBytes = 2048;  // epilogue staging chunk: 32 rows x 64 B (32 bf16 or 16 fp32 columns)
+
 template <int BN>
 struct GemmCfg {
   static constexpr int B_STAGE_BYTES = BN * BK * 2;
   static constexpr int STAGE_BYTES = A_STAGE_BYTES + B_STAGE_BYTES;
   static constexpr int STAGES = (BN == 256) ? 4 : 6;
   static constexpr int TMEM_COLS = 2 * BN;
-  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+  static constexpr int STAGING_BYTES = kEpiWarps * 2 * kChunkBytes;
+  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + STAGING_BYTES + 1024 /*align*/ + 512 /*barriers*/;
+  static_assert(SMEM_BYTES <= 232448, "GEMM shared memory exceeds the 227 KB per-block limit");
 };
 
 __device__ __forceinline__ float silu_f(float g) { return g / (1.0f + __expf(-g)); }
 
+// Byte offset of 16-byte column group j of row `row` inside a staging chunk.  The TMA maps of the
+// outputs use the 64-byte swizzle (16-byte group index XOR bits 1..2 of the row); the chunk base is
+// 2 KB aligned, so this is the layout TMA reads, and a warp writing one row per lane hits 32
+// distinct banks per quarter-warp.
+__device__ __forceinline__ uint32_t chunk_off(int row, int j) { return row * 64 + ((j ^ ((row >> 1) & 3)) << 4); }
+
+__device__ __forceinline__ uint4 pack8f(const float (&v)[8]) {
+  return make_uint4(pack_bf16(v[0], v[1]), pack_bf16(v[2], v[3]), pack_bf16(v[4], v[5]), pack_bf16(v[6], v[7]));
+}
+
+// This lane's 32 fp32 values (bit patterns) -> 32 bf16 of its row in the chunk.
+__device__ __forceinline__ void write_chunk_bf16(uint8_t* buf, const uint32_t (&r)[32]) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    float v[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) v[e] = __uint_as_float(r[8 * j + e]);
+    *reinterpret_cast<uint4*>(buf + chunk_off(lane, j)) = pack8f(v);
+  }
+}
+
+// Next chunk of this warp's two-deep ring, once the TMA store issued from it two chunks ago has
+// finished reading it.
+__device__ __forceinline__ uint8_t* acquire_chunk(uint8_t* stg, int& bsel) {
+  if ((threadIdx.x & 31) == 0) bulk_wait_group_read<1>();
+  __syncwarp();
+  uint8_t* buf = stg + bsel * kChunkBytes;
+  bsel ^= 1;
+  return buf;
+}
+
+// Hand a filled chunk to TMA: store (or fp32 add-reduce) it at (column c0, row c1) of `map`.
+__device__ __forceinline__ void publish_chunk(const CUtensorMap* map, uint8_t* buf, int c0, int c1, bool reduce) {
+  fence_proxy_async_smem();
+  __syncwarp();
+  if ((threadIdx.x & 31) == 0) {
+    if (reduce)
+      tma_reduce_add_2d(map, buf, c0, c1);
+    else
+      tma_store_2d(map, buf, c0, c1);
+    bulk_commit_group();
+  }
+}
+
 template <int BN, bool A_MN, bool B_MN, int EPI>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
-    gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, GemmParams p) {
+    gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmX,
+                const __grid_constant__ CUtensorMap tmY, GemmParams p) {
   using Cfg = GemmCfg<BN>;
   constexpr int STAGES = Cfg::STAGES;
   constexpr uint32_t IDESC = idesc_bf16_f32(BM, BN, A_MN, B_MN);
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + STAGES * Cfg::STAGE_BYTES);
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + STAGES * Cfg::STAGE_BYTES + Cfg::STAGING_BYTES);
   uint64_t* empty_bar = full_bar + STAGES;
   uint64_t* tfull_bar = empty_bar + STAGES;
   uint64_t* tempty_bar = tfull_bar + 2;
-  uint32_t* tmem_base_slot = reinterpret_cast<uint32_t*>(tempty_bar + 2);
+  uint64_t* load_bar = tempty_bar + 2;  // two per epilogue warp (residual tiles)
+  uint32_t* tmem_base_slot = reinterpret_cast<uint32_t*>(load_bar + 2 * kEpiWarps);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_base_slot + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -81,8 +134,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull_bar[a], 1);
-      mbar_init(&tempty_bar[a], 8);
+      mbar_init(&tempty_bar[a], kEpiWarps);
     }
+    for (int b = 0; b < 2 * kEpiWarps; ++b) mbar_init(&load_bar[b], 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -186,66 +240,102 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     }
   } else {
     // ------------------------------------------------------------------ epilogue warps
-    const int q = warp & 3;  // tensor-memory lane quarter this warp may access
-    const int wg = (warp - 2) >> 2;  // epilogue warpgroup: columns [wg*BN/2, (wg+1)*BN/2)
-    const int row = q * 32 + lane;
+    // Warp (q, wg) owns tile rows [32q, 32q+32) and columns [wg*BN/2, (wg+1)*BN/2).  Results go
+    // through this warp's two 2 KB staging chunks (32 rows x 64 B, 64-byte swizzle) and leave with
+    // TMA stores (fp32 weight gradients: TMA add-reductions), so global writes are full-line and
+    // asynchronous; the ring of two chunks lets the next chunk fill while the previous one drains.
+    const int q = warp & 3;
+    const int wg = (warp - 2) >> 2;
+    const int ew = warp - 2;
+    uint8_t* stg = smem + STAGES * Cfg::STAGE_BYTES + ew * 2 * kChunkBytes;
+    uint64_t* lbar = load_bar + ew * 2;
+    uint32_t lphase[2] = {0u, 0u};
+    int bsel = 0;
     int t = 0;
-    for (int u = blockIdx.x; u < total_units; u += gridDim.x, ++t) {
+    bool ok = true;
+    for (int u = blockIdx.x; u < total_units && ok; u += gridDim.x, ++t) {
       const int tile = u / p.splits;
       const int tm = tile % p.tiles_m, tn = tile / p.tiles_m;
       const int acc = t & 1;
       const uint32_t acc_phase = (t >> 1) & 1;
+      const int row0 = tm * BM + q * 32;  // TMA row coordinate of this warp's chunk
+      const int m = row0 + lane;
+      const bool row_ok = m < p.M;
+
+      if constexpr (EPI == EPI_RESIDUAL) {
+        // Prefetch the residual for the first two chunks while the main loop still runs.
+        if (lane == 0) {
+          bulk_wait_group_read<0>();
+          for (int i = 0; i < 2 && i < BN / 64; ++i) {
+            mbar_expect_tx(&lbar[i], kChunkBytes);
+            tma_load_2d(stg + i * kChunkBytes, &tmX, &lbar[i], tn * BN + wg * (BN / 2) + 32 * i, row0);
+          }
+        }
+        __syncwarp();
+      }
       if (!mbar_wait_bounded(&tfull_bar[acc], acc_phase, abort_flag, p.errs, kErrGemmWait, 3)) break;
       tc_fence_after();
       const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + acc * BN;
-      const int m = tm * BM + row;
-      const bool row_ok = m < p.M;
 
-      if constexpr (EPI == EPI_STORE || EPI == EPI_RESIDUAL || EPI == EPI_ACC_F32) {
-        const int n0 = tn * BN;
+      if constexpr (EPI == EPI_STORE || EPI == EPI_RESIDUAL) {
+        const int n0 = tn * BN + wg * (BN / 2);
 #pragma unroll 1
-        for (int c = wg * (BN / 2); c < (wg + 1) * (BN / 2); c += 32) {
+        for (int i = 0; i < BN / 64; ++i) {
           uint32_t r[32];
-          tmem_ld_32x32b_x32(tbase + c, r);
+          tmem_ld_32x32b_x32(tbase + wg * (BN / 2) + 32 * i, r);
           tc_wait_ld();
-          if (!row_ok) continue;
-          const int nb = n0 + c;
-          if constexpr (EPI == EPI_ACC_F32) {
-            float* dst = p.C32 + (size_t)m * p.ldc32 + nb;
+          uint8_t* buf;
+          if constexpr (EPI == EPI_RESIDUAL) {
+            const int b = i & 1;
+            buf = stg + b * kChunkBytes;
+            if (!mbar_wait_bounded(&lbar[b], lphase[b], abort_flag, p.errs, kErrGemmWait, 4)) { ok = false; break; }
+            lphase[b] ^= 1u;
 #pragma unroll
-            for (int j = 0; j < 32; j += 4) {
-              if (nb + j < p.N) {
-                float4 v = make_float4(__uint_as_float(r[j]), __uint_as_float(r[j + 1]), __uint_as_float(r[j + 2]),
-                                       __uint_as_float(r[j + 3]));
-                atomicAdd(reinterpret_cast<float4*>(dst + j), v);
-              }
-            }
-          } else {
-            __nv_bfloat16* dst = p.C + (size_t)m * p.ldc + nb;
-            const __nv_bfloat16* res = (EPI == EPI_RESIDUAL) ? p.R + (size_t)m * p.ldr + nb : nullptr;
-#pragma unroll
-            for (int j = 0; j < 32; j += 8) {
-              if (nb + j >= p.N) break;
+            for (int j = 0; j < 4; ++j) {
+              const uint4 rv = *reinterpret_cast<const uint4*>(buf + chunk_off(lane, j));
+              const uint32_t rw[4] = {rv.x, rv.y, rv.z, rv.w};
               float v[8];
 #pragma unroll
-              for (int e = 0; e < 8; ++e) v[e] = __uint_as_float(r[j + e]);
-              if constexpr (EPI == EPI_RESIDUAL) {
-                uint4 rv = *reinterpret_cast<const uint4*>(res + j);
-                const uint32_t rw[4] = {rv.x, rv.y, rv.z, rv.w};
-#pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                  v[2 * e] += bf16lo(rw[e]);
-                  v[2 * e + 1] += bf16hi(rw[e]);
-                }
+              for (int e = 0; e < 4; ++e) {
+                v[2 * e] = __uint_as_float(r[8 * j + 2 * e]) + bf16lo(rw[e]);
+                v[2 * e + 1] = __uint_as_float(r[8 * j + 2 * e + 1]) + bf16hi(rw[e]);
               }
-              uint4 o;
-              o.x = pack_bf16(v[0], v[1]);
-              o.y = pack_bf16(v[2], v[3]);
-              o.z = pack_bf16(v[4], v[5]);
-              o.w = pack_bf16(v[6], v[7]);
-              *reinterpret_cast<uint4*>(dst + j) = o;
+              *reinterpret_cast<uint4*>(buf + chunk_off(lane, j)) = pack8f(v);
             }
+            publish_chunk(&tmC, buf, n0 + 32 * i, row0, false);
+            if (i + 2 < BN / 64) {  // refill this buffer with the residual of chunk i + 2
+              if (lane == 0) {
+                bulk_wait_group_read<0>();
+                mbar_expect_tx(&lbar[b], kChunkBytes);
+                tma_load_2d(buf, &tmX, &lbar[b], n0 + 32 * (i + 2), row0);
+              }
+              __syncwarp();
+            }
+          } else {
+            buf = acquire_chunk(stg, bsel);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              float v[8];
+#pragma unroll
+              for (int e = 0; e < 8; ++e) v[e] = __uint_as_float(r[8 * j + e]);
+              *reinterpret_cast<uint4*>(buf + chunk_off(lane, j)) = pack8f(v);
+            }
+            publish_chunk(&tmC, buf, n0 + 32 * i, row0, false);
           }
+        }
+      } else if constexpr (EPI == EPI_ACC_F32) {
+        const int n0 = tn * BN + wg * (BN / 2);
+#pragma unroll 1
+        for (int c = 0; c < BN / 2; c += 16) {
+          uint32_t r[16];
+          tmem_ld_32x32b_x16(tbase + wg * (BN / 2) + c, r);
+          tc_wait_ld();
+          uint8_t* buf = acquire_chunk(stg, bsel);
+#pragma unroll
+          for (int j = 0; j < 4; ++j)
+            *reinterpret_cast<uint4*>(buf + chunk_off(lane, j)) =
+                make_uint4(r[4 * j], r[4 * j + 1], r[4 * j + 2], r[4 * j + 3]);
+          publish_chunk(&tmC, buf, n0 + c, row0, true);
         }
       } else if constexpr (EPI == EPI_ROPE) {
         const int n0 = tn * BN;
@@ -256,40 +346,33 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           const int col = n0 + h0;
           const bool rotate = col < p.rope_cols;
 #pragma unroll 1
-          for (int j = 0; j < half; j += 32) {
+          for (int j0 = 0; j0 < half; j0 += 32) {
             uint32_t lo[32], hi[32];
-            tmem_ld_32x32b_x32(tbase + h0 + j, lo);
-            tmem_ld_32x32b_x32(tbase + h0 + half + j, hi);
+            tmem_ld_32x32b_x32(tbase + h0 + j0, lo);
+            tmem_ld_32x32b_x32(tbase + h0 + half + j0, hi);
             tc_wait_ld();
-            if (!row_ok || col >= p.N) continue;
-            __nv_bfloat16* dlo = p.C + (size_t)m * p.ldc + col + j;
-            __nv_bfloat16* dhi = dlo + half;
-            const float* cs = p.rope_cos + (size_t)pos * half + j;
-            const float* sn = p.rope_sin + (size_t)pos * half + j;
+            if (rotate) {
+              const float4* c4 = reinterpret_cast<const float4*>(p.rope_cos + (size_t)pos * half + j0);
+              const float4* s4 = reinterpret_cast<const float4*>(p.rope_sin + (size_t)pos * half + j0);
 #pragma unroll
-            for (int e = 0; e < 32; e += 8) {
-              float a[8], b[8];
+              for (int e4 = 0; e4 < 8; ++e4) {
+                const float4 cv = c4[e4], sv = s4[e4];
+                const float cs[4] = {cv.x, cv.y, cv.z, cv.w}, sn[4] = {sv.x, sv.y, sv.z, sv.w};
 #pragma unroll
-              for (int i = 0; i < 8; ++i) {
-                const float x0 = __uint_as_float(lo[e + i]);
-                const float x1 = __uint_as_float(hi[e + i]);
-                if (rotate) {
-                  const float c = cs[e + i], s = sn[e + i];
-                  a[i] = x0 * c - x1 * s;
-                  b[i] = x1 * c + x0 * s;
-                } else {
-                  a[i] = x0;
-                  b[i] = x1;
+                for (int k = 0; k < 4; ++k) {
+                  const int e = 4 * e4 + k;
+                  const float x0 = __uint_as_float(lo[e]), x1 = __uint_as_float(hi[e]);
+                  lo[e] = __float_as_uint(x0 * cs[k] - x1 * sn[k]);
+                  hi[e] = __float_as_uint(x1 * cs[k] + x0 * sn[k]);
                 }
               }
-              uint4 oa, ob;
-              oa.x = pack_bf16(a[0], a[1]); oa.y = pack_bf16(a[2], a[3]);
-              oa.z = pack_bf16(a[4], a[5]); oa.w = pack_bf16(a[6], a[7]);
-              ob.x = pack_bf16(b[0], b[1]); ob.y = pack_bf16(b[2], b[3]);
-              ob.z = pack_bf16(b[4], b[5]); ob.w = pack_bf16(b[6], b[7]);
-              *reinterpret_cast<uint4*>(dlo + e) = oa;
-              *reinterpret_cast<uint4*>(dhi + e) = ob;
             }
+            uint8_t* ba = acquire_chunk(stg, bsel);
+            write_chunk_bf16(ba, lo);
+            publish_chunk(&tmC, ba, col + j0, row0, false);
+            uint8_t* bb = acquire_chunk(stg, bsel);
+            write_chunk_bf16(bb, hi);
+            publish_chunk(&tmC, bb, col + half + j0, row0, false);
           }
         }
       } else if constexpr (EPI == EPI_SWIGLU) {
@@ -301,78 +384,71 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           tmem_ld_32x32b_x32(tbase + BN / 2 + c, uu);
           tc_wait_ld();
           const int nb = n0 + c;
-          if (!row_ok || nb >= p.N) continue;
-          __nv_bfloat16* dh = p.C + (size_t)m * p.ldc + nb;
-          __nv_bfloat16* dg = p.aux + (size_t)m * p.ld_aux + nb;
-          __nv_bfloat16* du = dg + p.ffn;
+          uint8_t* bg = acquire_chunk(stg, bsel);
+          write_chunk_bf16(bg, g);
+          publish_chunk(&tmX, bg, nb, row0, false);
+          uint8_t* bu = acquire_chunk(stg, bsel);
+          write_chunk_bf16(bu, uu);
+          publish_chunk(&tmY, bu, nb, row0, false);
 #pragma unroll
-          for (int j = 0; j < 32; j += 8) {
-            float hv[8], gv[8], uv[8];
-#pragma unroll
-            for (int i = 0; i < 8; ++i) {
-              gv[i] = __uint_as_float(g[j + i]);
-              uv[i] = __uint_as_float(uu[j + i]);
-              hv[i] = silu_f(gv[i]) * uv[i];
-            }
-            uint4 oh, og, ou;
-            oh.x = pack_bf16(hv[0], hv[1]); oh.y = pack_bf16(hv[2], hv[3]);
-            oh.z = pack_bf16(hv[4], hv[5]); oh.w = pack_bf16(hv[6], hv[7]);
-            og.x = pack_bf16(gv[0], gv[1]); og.y = pack_bf16(gv[2], gv[3]);
-            og.z = pack_bf16(gv[4], gv[5]); og.w = pack_bf16(gv[6], gv[7]);
-            ou.x = pack_bf16(uv[0], uv[1]); ou.y = pack_bf16(uv[2], uv[3]);
-            ou.z = pack_bf16(uv[4], uv[5]); ou.w = pack_bf16(uv[6], uv[7]);
-            *reinterpret_cast<uint4*>(dh + j) = oh;
-            *reinterpret_cast<uint4*>(dg + j) = og;
-            *reinterpret_cast<uint4*>(du + j) = ou;
+          for (int e = 0; e < 32; ++e) {
+            const float gv = __uint_as_float(g[e]);
+            g[e] = __float_as_uint(silu_f(gv) * __uint_as_float(uu[e]));
           }
+          uint8_t* bh = acquire_chunk(stg, bsel);
+          write_chunk_bf16(bh, g);
+          publish_chunk(&tmC, bh, nb, row0, false);
         }
       } else if constexpr (EPI == EPI_SWIGLU_BWD) {
-        const int n0 = tn * BN;
-#pragma unroll 1
-        for (int c = wg * (BN / 2); c < (wg + 1) * (BN / 2); c += 32) {
-          uint32_t r[32];
-          tmem_ld_32x32b_x32(tbase + c, r);
-          tc_wait_ld();
-          const int nb = n0 + c;
-          if (!row_ok || nb >= p.N) continue;
-          const __nv_bfloat16* gsrc = p.aux_in + (size_t)m * p.ld_aux_in + nb;
-          const __nv_bfloat16* usrc = gsrc + p.ffn;
-          __nv_bfloat16* dg = p.C + (size_t)m * p.ldc + nb;
-          __nv_bfloat16* du = dg + p.ffn;
+        const int n0 = tn * BN + wg * (BN / 2);
+        // Saved pre-activations of this row for chunk i (64 B of g and of u), prefetched one chunk ahead.
+        uint4 gq[4], uq[4];
+        auto load_gu = [&](int i) {
+          const __nv_bfloat16* gsrc = p.aux_in + (size_t)(row_ok ? m : 0) * p.ld_aux_in + n0 + 32 * i;
 #pragma unroll
-          for (int j = 0; j < 32; j += 8) {
-            const uint4 gq = *reinterpret_cast<const uint4*>(gsrc + j);
-            const uint4 uq = *reinterpret_cast<const uint4*>(usrc + j);
-            const uint32_t gw[4] = {gq.x, gq.y, gq.z, gq.w};
-            const uint32_t uw[4] = {uq.x, uq.y, uq.z, uq.w};
-            float dgv[8], duv[8];
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-#pragma unroll
-              for (int h = 0; h < 2; ++h) {
-                const float gval = h ? bf16hi(gw[i]) : bf16lo(gw[i]);
-                const float uval = h ? bf16hi(uw[i]) : bf16lo(uw[i]);
-                const float da = __uint_as_float(r[j + 2 * i + h]);
-                const float sig = 1.0f / (1.0f + __expf(-gval));
-                const float s = gval * sig;
-                duv[2 * i + h] = da * s;
-                dgv[2 * i + h] = da * uval * sig * (1.0f + gval * (1.0f - sig));
-              }
-            }
-            uint4 og, ou;
-            og.x = pack_bf16(dgv[0], dgv[1]); og.y = pack_bf16(dgv[2], dgv[3]);
-            og.z = pack_bf16(dgv[4], dgv[5]); og.w = pack_bf16(dgv[6], dgv[7]);
-            ou.x = pack_bf16(duv[0], duv[1]); ou.y = pack_bf16(duv[2], duv[3]);
-            ou.z = pack_bf16(duv[4], duv[5]); ou.w = pack_bf16(duv[6], duv[7]);
-            *reinterpret_cast<uint4*>(dg + j) = og;
-            *reinterpret_cast<uint4*>(du + j) = ou;
+          for (int j = 0; j < 4; ++j) {
+            const bool in = n0 + 32 * i + 8 * j < p.N;
+            gq[j] = in ? *reinterpret_cast<const uint4*>(gsrc + 8 * j) : make_uint4(0u, 0u, 0u, 0u);
+            uq[j] = in ? *reinterpret_cast<const uint4*>(gsrc + p.ffn + 8 * j) : make_uint4(0u, 0u, 0u, 0u);
           }
+        };
+        load_gu(0);
+#pragma unroll 1
+        for (int i = 0; i < BN / 64; ++i) {
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(tbase + wg * (BN / 2) + 32 * i, r);
+          tc_wait_ld();
+          uint32_t dg[32], du[32];
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const uint32_t gw[4] = {gq[j].x, gq[j].y, gq[j].z, gq[j].w};
+            const uint32_t uw[4] = {uq[j].x, uq[j].y, uq[j].z, uq[j].w};
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+              const float gval = (e & 1) ? bf16hi(gw[e >> 1]) : bf16lo(gw[e >> 1]);
+              const float uval = (e & 1) ? bf16hi(uw[e >> 1]) : bf16lo(uw[e >> 1]);
+              const float da = __uint_as_float(r[8 * j + e]);
+              const float sig = 1.0f / (1.0f + __expf(-gval));
+              du[8 * j + e] = __float_as_uint(da * gval * sig);
+              dg[8 * j + e] = __float_as_uint(da * uval * sig * (1.0f + gval * (1.0f - sig)));
+            }
+          }
+          if (i + 1 < BN / 64) load_gu(i + 1);
+          uint8_t* bg = acquire_chunk(stg, bsel);
+          write_chunk_bf16(bg, dg);
+          publish_chunk(&tmC, bg, n0 + 32 * i, row0, false);
+          uint8_t* bu = acquire_chunk(stg, bsel);
+          write_chunk_bf16(bu, du);
+          publish_chunk(&tmY, bu, n0 + 32 * i, row0, false);
         }
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty_bar[acc]);
     }
+    // Every staged chunk must have landed before the CTA's shared memory goes away.
+    if (lane == 0) bulk_wait_group<0>();
+    __syncwarp();
   }
 
   tc_fence_before();
@@ -401,20 +477,37 @@ PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
 
 }  // namespace
 
-CUtensorMap make_tmap_bf16_2d(const void* base, uint64_t inner, uint64_t outer, uint64_t row_stride_elems,
-                              uint32_t box_inner, uint32_t box_outer) {
+static CUtensorMap encode_2d(CUtensorMapDataType dtype, int elem_bytes, const void* base, uint64_t inner,
+                             uint64_t outer, uint64_t row_stride_elems, uint32_t box_inner, uint32_t box_outer,
+                             CUtensorMapSwizzle swizzle) {
   B200_CHECK((reinterpret_cast<uintptr_t>(base) & 15) == 0, "TMA base address must be 16-byte aligned");
-  B200_CHECK((row_stride_elems * 2) % 16 == 0, "TMA row stride must be a multiple of 16 bytes");
+  B200_CHECK((row_stride_elems * elem_bytes) % 16 == 0, "TMA row stride must be a multiple of 16 bytes");
   CUtensorMap map;
   cuuint64_t dims[2] = {inner, outer};
-  cuuint64_t strides[1] = {row_stride_elems * 2};
+  cuuint64_t strides[1] = {row_stride_elems * (uint64_t)elem_bytes};
   cuuint32_t box[2] = {box_inner, box_outer};
   cuuint32_t estr[2] = {1, 1};
-  CUresult r = get_encode_fn()(&map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides,
-                               box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  CUresult r = get_encode_fn()(&map, dtype, 2, const_cast<void*>(base), dims, strides, box, estr,
+                               CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   B200_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled failed (code " + std::to_string((int)r) + ")");
   return map;
+}
+
+CUtensorMap make_tmap_bf16_2d(const void* base, uint64_t inner, uint64_t outer, uint64_t row_stride_elems,
+                              uint32_t box_inner, uint32_t box_outer) {
+  return encode_2d(CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, base, inner, outer, row_stride_elems, box_inner, box_outer,
+                   CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
+// Epilogue output / residual maps: one staging chunk (32 rows x 64 B) per box, 64-byte swizzle.
+static CUtensorMap epi_map_bf16(const void* base, int rows, int cols, int ld) {
+  return encode_2d(CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, base, (uint64_t)cols, (uint64_t)rows, (uint64_t)ld, 32, 32,
+                   CU_TENSOR_MAP_SWIZZLE_64B);
+}
+static CUtensorMap epi_map_f32(const void* base, int rows, int cols, int ld) {
+  return encode_2d(CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, base, (uint64_t)cols, (uint64_t)rows, (uint64_t)ld, 16, 32,
+                   CU_TENSOR_MAP_SWIZZLE_64B);
 }
 
 int num_sms() {
@@ -447,6 +540,21 @@ static void launch_impl(const GemmOperands& op, GemmParams p, cudaStream_t strea
   } else {
     tmB = make_tmap_bf16_2d(op.B, (uint64_t)p.K, (uint64_t)p.N, op.ldb, 64, BN);
   }
+  // Output side.  Maps that an epilogue does not use repeat tmA (never dereferenced).
+  CUtensorMap tmC = tmA, tmX = tmA, tmY = tmA;
+  if (EPI == EPI_ACC_F32) {
+    tmC = epi_map_f32(p.C32, p.M, p.N, p.ldc32);
+  } else if (EPI == EPI_SWIGLU) {
+    tmC = epi_map_bf16(p.C, p.M, p.ffn, p.ldc);
+    tmX = epi_map_bf16(p.aux, p.M, p.ffn, p.ld_aux);
+    tmY = epi_map_bf16(p.aux + p.ffn, p.M, p.ffn, p.ld_aux);
+  } else if (EPI == EPI_SWIGLU_BWD) {
+    tmC = epi_map_bf16(p.C, p.M, p.ffn, p.ldc);
+    tmY = epi_map_bf16(p.C + p.ffn, p.M, p.ffn, p.ldc);
+  } else {
+    tmC = epi_map_bf16(p.C, p.M, p.N, p.ldc);
+    if (EPI == EPI_RESIDUAL) tmX = epi_map_bf16(p.R, p.M, p.N, p.ldr);
+  }
   const int out_cols_per_tile = (EPI == EPI_SWIGLU) ? BN / 2 : BN;
   p.tiles_m = (p.M + BM - 1) / BM;
   p.tiles_n = (p.N + out_cols_per_tile - 1) / out_cols_per_tile;
@@ -458,7 +566,7 @@ static void launch_impl(const GemmOperands& op, GemmParams p, cudaStream_t strea
   p.errs = device_errors_ptr();
   const int units = p.tiles_m * p.tiles_n * p.splits;
   const int grid = std::max(1, std::min(units, num_sms()));
-  kernel<<<grid, NUM_THREADS, Cfg::SMEM_BYTES, stream>>>(tmA, tmB, p);
+  kernel<<<grid, NUM_THREADS, Cfg::SMEM_BYTES, stream>>>(tmA, tmB, tmC, tmX, tmY, p);
   B200_CUDA_CHECK(cudaGetLastError());
   count_launch();
 }

@@ -76,54 +76,77 @@ __global__ void rmsnorm_fwd_kernel(const __nv_bfloat16* __restrict__ x, const __
 }
 
 // dx = dres + rstd * (dy*w - xhat * mean(dy*w*xhat)); dw += sum_rows(dy * xhat) (fp32 atomics).
-template <int VEC>
-__global__ void rmsnorm_bwd_kernel(const __nv_bfloat16* __restrict__ dy, const __nv_bfloat16* __restrict__ x,
-                                   const __nv_bfloat16* __restrict__ w, const float* __restrict__ rstd,
-                                   const __nv_bfloat16* __restrict__ dres, __nv_bfloat16* __restrict__ dx,
-                                   float* __restrict__ dw, int rows, int d, int rows_per_block) {
+//
+// Each warp owns ROWS rows and issues the x, dy and dres loads of all of them before any arithmetic,
+// so a warp keeps several 16-byte loads per lane in flight (the kernel is bound by HBM latency x
+// bytes in flight, not by arithmetic).  ROWS = 2 up to d = 1024 and 1 above (register budget).  The
+// block's weight-gradient partials are summed in shared memory and added with one fp32 atomic per
+// column per block.
+template <int VEC, int ROWS>
+__global__ void __launch_bounds__(32 * kWarpsPerBlock)
+    rmsnorm_bwd_kernel(const __nv_bfloat16* __restrict__ dy, const __nv_bfloat16* __restrict__ x,
+                       const __nv_bfloat16* __restrict__ w, const float* __restrict__ rstd,
+                       const __nv_bfloat16* __restrict__ dres, __nv_bfloat16* __restrict__ dx,
+                       float* __restrict__ dw, int rows, int d) {
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
-  float wf[VEC][8];
+  const int row0 = (blockIdx.x * kWarpsPerBlock + warp) * ROWS;
+  uint4 xq[ROWS][VEC], gq[ROWS][VEC], rq[ROWS][VEC];
+  float r[ROWS];
+  const uint4 zero = make_uint4(0u, 0u, 0u, 0u);
+#pragma unroll
+  for (int k = 0; k < ROWS; ++k) {
+    const int row = row0 + k;
+    const bool ok = row < rows;
+    r[k] = ok ? rstd[row] : 0.f;
+#pragma unroll
+    for (int i = 0; i < VEC; ++i) {
+      const int c = (i * 32 + lane) * 8;
+      const bool in = ok && c < d;
+      const size_t off = (size_t)row * d + c;
+      xq[k][i] = in ? *reinterpret_cast<const uint4*>(x + off) : zero;
+      gq[k][i] = in ? *reinterpret_cast<const uint4*>(dy + off) : zero;
+      rq[k][i] = (in && dres != nullptr) ? *reinterpret_cast<const uint4*>(dres + off) : zero;
+    }
+  }
   float acc[VEC][8];
 #pragma unroll
-  for (int i = 0; i < VEC; ++i) {
-    const int c = (i * 32 + lane) * 8;
+  for (int i = 0; i < VEC; ++i)
 #pragma unroll
     for (int e = 0; e < 8; ++e) acc[i][e] = 0.f;
-    if (c < d) unpack8(*reinterpret_cast<const uint4*>(w + c), wf[i]);
-  }
-  const int row_begin = blockIdx.x * rows_per_block;
-  const int row_end = min(rows, row_begin + rows_per_block);
-  for (int row = row_begin + warp; row < row_end; row += kWarpsPerBlock) {
-    const float r = rstd[row];
-    float xh[VEC][8], g[VEC][8];
+#pragma unroll
+  for (int k = 0; k < ROWS; ++k) {
+    const int row = row0 + k;
     float dot = 0.f;
 #pragma unroll
     for (int i = 0; i < VEC; ++i) {
       const int c = (i * 32 + lane) * 8;
       if (c < d) {
-        float xv[8], dyv[8];
-        unpack8(*reinterpret_cast<const uint4*>(x + (size_t)row * d + c), xv);
-        unpack8(*reinterpret_cast<const uint4*>(dy + (size_t)row * d + c), dyv);
+        float xv[8], dyv[8], wf[8];
+        unpack8(xq[k][i], xv);
+        unpack8(gq[k][i], dyv);
+        unpack8(*reinterpret_cast<const uint4*>(w + c), wf);
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
-          xh[i][e] = xv[e] * r;
-          g[i][e] = dyv[e] * wf[i][e];
-          dot += g[i][e] * xh[i][e];
-          acc[i][e] += dyv[e] * xh[i][e];
+          const float xh = xv[e] * r[k];
+          dot += dyv[e] * wf[e] * xh;
+          acc[i][e] += dyv[e] * xh;
         }
       }
     }
     dot = warp_sum(dot) / (float)d;
+    if (row >= rows) continue;
 #pragma unroll
     for (int i = 0; i < VEC; ++i) {
       const int c = (i * 32 + lane) * 8;
       if (c < d) {
-        float o[8];
-        float rv[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-        if (dres != nullptr) unpack8(*reinterpret_cast<const uint4*>(dres + (size_t)row * d + c), rv);
+        float xv[8], dyv[8], wf[8], rv[8], o[8];
+        unpack8(xq[k][i], xv);
+        unpack8(gq[k][i], dyv);
+        unpack8(rq[k][i], rv);
+        unpack8(*reinterpret_cast<const uint4*>(w + c), wf);
 #pragma unroll
-        for (int e = 0; e < 8; ++e) o[e] = rv[e] + r * (g[i][e] - xh[i][e] * dot);
+        for (int e = 0; e < 8; ++e) o[e] = rv[e] + r[k] * (dyv[e] * wf[e] - xv[e] * r[k] * dot);
         *reinterpret_cast<uint4*>(dx + (size_t)row * d + c) = pack8(o);
       }
     }
@@ -248,22 +271,20 @@ void rmsnorm_fwd(const __nv_bfloat16* x, const __nv_bfloat16* w, __nv_bfloat16* 
 void rmsnorm_bwd(const __nv_bfloat16* dy, const __nv_bfloat16* x, const __nv_bfloat16* w, const float* rstd,
                  const __nv_bfloat16* dres, __nv_bfloat16* dx, float* dw, int rows, int d, cudaStream_t s) {
   B200_CHECK(d % 8 == 0 && d <= 256 * 8, "rmsnorm_bwd: d must be a multiple of 8 and at most 2048");
-  // ~32 rows per block: enough blocks for several resident per SM (latency hiding) while the
-  // per-block weight-gradient atomics stay a small fraction of the traffic.
-  const int blocks = std::max(1, (rows + 31) / 32);
-  const int rows_per_block = (rows + blocks - 1) / blocks;
   const int vec = (d + 255) / 256;
+  const int per_block = kWarpsPerBlock * (vec <= 4 ? 2 : 1);
+  const int blocks = std::max(1, (rows + per_block - 1) / per_block);
   const int threads = 32 * kWarpsPerBlock;
   if (vec <= 1)
-    rmsnorm_bwd_kernel<1><<<blocks, threads, 0, s>>>(dy, x, w, rstd, dres, dx, dw, rows, d, rows_per_block);
+    rmsnorm_bwd_kernel<1, 2><<<blocks, threads, 0, s>>>(dy, x, w, rstd, dres, dx, dw, rows, d);
   else if (vec <= 2)
-    rmsnorm_bwd_kernel<2><<<blocks, threads, 0, s>>>(dy, x, w, rstd, dres, dx, dw, rows, d, rows_per_block);
+    rmsnorm_bwd_kernel<2, 2><<<blocks, threads, 0, s>>>(dy, x, w, rstd, dres, dx, dw, rows, d);
   else if (vec <= 3)
-    rmsnorm_bwd_kernel<3><<<blocks, threads, 0, s>>>(dy, x, w, rstd, dres, dx, dw, rows, d, rows_per_block);
+    rmsnorm_bwd_kernel<3, 2><<<blocks, threads, 0, s>>>(dy, x, w, rstd, dres, dx, dw, rows, d);
   else if (vec <= 4)
-    rmsnorm_bwd_kernel<4><<<blocks, threads, 0, s>>>(dy, x, w, rstd, dres, dx, dw, rows, d, rows_per_block);
+    rmsnorm_bwd_kernel<4, 2><<<blocks, threads, 0, s>>>(dy, x, w, rstd, dres, dx, dw, rows, d);
   else
-    rmsnorm_bwd_kernel<8><<<blocks, threads, 0, s>>>(dy, x, w, rstd, dres, dx, dw, rows, d, rows_per_block);
+    rmsnorm_bwd_kernel<8, 1><<<blocks, threads, 0, s>>>(dy, x, w, rstd, dres, dx, dw, rows, d);
   B200_CUDA_CHECK(cudaGetLastError());
   count_launch();
 }
