@@ -1,6 +1,6 @@
 // Causal GQA flash-attention backward on the 5th-generation tensor cores (sm_100a).
 //
-// Grid: one CTA per (key/value block j of 128 rows, kv head, batch).  The CTA keeps K_j and V_j in
+// Work item: one (key/value block j of 128 rows, kv head, batch).  The item keeps K_j and V_j in
 // shared memory and loops over every query head of its group and every query block i >= j:
 //
 //   S^T  = K_j Q_i^T           (M = kv, N = q,  K = hd)   tensor memory
@@ -9,16 +9,20 @@
 //   dV  += P^T dO_i            (M = kv, N = hd, K = q)    accumulated in tensor memory over the loop
 //   dK  += dS^T Q_i            (M = kv, N = hd, K = q)    accumulated in tensor memory over the loop
 //   dQ_i = dS K_j              (M = q,  N = hd, K = kv)   A operand = the same dS^T bytes read MN-major
-//   dq_acc[q rows] += scale * dQ_i                        fp32 vector atomics (summed over j)
+//   dq_acc[q rows] += scale * dQ_i                        TMA add-reductions (hd 64) / fp32 vector atomics
 //
-// 320 threads: warp 0 TMA, warp 1 tensor-memory allocation + MMA issue, warps 2..9 two compute
-// warpgroups.  Thread (wg, r) owns kv row r and the query columns [64*wg, 64*wg+64) of S^T / dP^T,
-// then the output columns [wg*hd/2, (wg+1)*hd/2) of dQ / dV and its half of the RoPE pairs of dK.
-// lse2 / delta are read with warp-uniform (broadcast) vector loads, so the compute warps never
-// need a block-level barrier.  Epilogues: dK (times the softmax scale, RoPE backward applied) and
-// dV are written as bf16 straight into the k / v columns of the fused q|k|v gradient; a small
-// kernel converts dq_acc into the q columns with RoPE backward.  delta = rowsum(dO * O) comes
-// from a pre-pass.
+// Scheduling: a persistent grid of min(items, SMs) CTAs.  Items are ordered by cost (block j costs
+// group * (S/128 - j) iterations, so j = 0 first) and dealt to CTAs boustrophedon-style (CTA c takes
+// items c, 2G-1-c, 2G+c, ...), which pairs long items with short ones.
+//
+// 320 threads: warp 0 TMA (K/V per item; Q, dO, lse and delta per iteration), warp 1 tensor-memory
+// allocation + MMA issue, warps 2..9 two compute warpgroups.  Thread (wg, r) owns kv row r and the
+// query columns [64*wg, 64*wg+64) of S^T / dP^T, then the output columns [wg*hd/2, (wg+1)*hd/2) of
+// dQ / dV and its half of the RoPE pairs of dK.  lse / delta of the current query block arrive in
+// shared memory with the Q / dO tiles and are read as broadcasts.  Epilogues: dK (times the softmax
+// scale, RoPE backward applied) and dV are written as bf16 into the k / v columns of the fused
+// q|k|v gradient; a small kernel converts dq_acc into the q columns with RoPE backward.
+// delta = rowsum(dO * O) comes from a pre-pass.
 #include <cuda.h>
 
 #include <cstdio>
@@ -34,19 +38,25 @@ namespace b200 {
 namespace {
 
 constexpr int BWD_THREADS = 320;
+constexpr int kBwdChunk = 2048;  // dQ staging chunk: 32 rows x 16 fp32 (64 B rows, 64-byte swizzle)
 
 template <int HD>
 struct AttnBwdCfg {
   static constexpr int KB = HD / 64;
   static constexpr int TILE = 128 * HD * 2;     // bytes of one 128-row tile
   static constexpr int STAGES = (HD == 64) ? 2 : 1;
+  static constexpr bool TMA_DQ = (HD == 64);    // dQ through TMA reductions (staging fits in smem)
   static constexpr int K_OFF = 0;
   static constexpr int V_OFF = TILE;
   static constexpr int QD_OFF = 2 * TILE;       // stages of (Q_i, dO_i)
   static constexpr int PT_OFF = QD_OFF + STAGES * 2 * TILE;
   static constexpr int DST_OFF = PT_OFF + 128 * 128 * 2;
-  static constexpr int BAR_OFF = DST_OFF + 128 * 128 * 2;
+  static constexpr int LD_OFF = DST_OFF + 128 * 128 * 2;  // per stage: lse2[128] | delta[128]
+  static constexpr int STG_OFF = LD_OFF + STAGES * 1024;
+  static constexpr int STG_BYTES = TMA_DQ ? 8 * 2 * kBwdChunk : 0;
+  static constexpr int BAR_OFF = STG_OFF + STG_BYTES;
   static constexpr int SMEM_BYTES = BAR_OFF + 256 + 1024;
+  static_assert(SMEM_BYTES <= 232448, "attention backward shared memory exceeds 227 KB");
   // tensor-memory columns
   static constexpr int T_ST = 0, T_DPT = 128, T_DV = 256, T_DK = 256 + HD;
   static constexpr int T_DQ = (HD == 64) ? 384 : 0;
@@ -55,6 +65,13 @@ struct AttnBwdCfg {
 };
 
 __device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+// Untiled bulk copy global -> shared (16-byte aligned addresses, size a multiple of 16).
+__device__ __forceinline__ void bulk_load(void* smem_dst, const void* gsrc, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+               ::"r"(smem_u32(smem_dst)), "l"(reinterpret_cast<uint64_t>(gsrc)), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
 
 __device__ __forceinline__ void store_swizzled_row(uint8_t* base, int r, int c, const uint32_t (&pk)[16]) {
   // 32 bf16 values (columns c .. c+31) of row r of a [128 x 128] K-major SW128 tile.
@@ -78,35 +95,50 @@ __device__ __forceinline__ void tmem_ld_cols(uint32_t taddr, uint32_t (&r)[N]) {
   }
 }
 
+// Work item u of the cost-ordered list -> (kv block j, kv head, batch).
+struct BwdItem {
+  int j, kvh, b;
+};
+__device__ __forceinline__ BwdItem bwd_item(int u, int batch, int kv_heads) {
+  const int per_j = batch * kv_heads;
+  const int r = u % per_j;
+  return {u / per_j, r % kv_heads, r / kv_heads};
+}
+// k-th item of CTA c in a grid of G CTAs (boustrophedon deal), or -1 past the end.
+__device__ __forceinline__ int bwd_item_index(int k, int c, int G, int n_items) {
+  const int u = k * G + ((k & 1) ? (G - 1 - c) : c);
+  return u < n_items ? u : -1;
+}
+
 template <int HD>
 __global__ void __launch_bounds__(BWD_THREADS, 1)
     attn_bwd_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __grid_constant__ CUtensorMap tm_do,
-                    AttnBwdParams p, DeviceErrors* errs) {
+                    const __grid_constant__ CUtensorMap tm_dq, AttnBwdParams p, DeviceErrors* errs) {
   using C = AttnBwdCfg<HD>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::BAR_OFF);
   uint64_t* kv_full = bars;
-  uint64_t* q_full = bars + 1;
+  uint64_t* kv_empty = bars + 1;
+  uint64_t* q_full = bars + 2;
   uint64_t* q_empty = q_full + C::STAGES;
   uint64_t* st_full = q_empty + C::STAGES;
   uint64_t* p_ready = st_full + 1;
   uint64_t* dq_full = p_ready + 1;
   uint64_t* dq_free = dq_full + 1;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(dq_free + 1);
+  uint64_t* epi_done = dq_free + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(epi_done + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int j = blockIdx.x;  // kv block (j = 0 has the most work and starts first)
-  const int kvh = blockIdx.y, b = blockIdx.z;
   const int n_qb = p.seq / 128;
   const int group = p.heads / p.kv_heads;
-  const int n_q = n_qb - j;  // query blocks i = j .. n_qb-1
-  const int n_it = group * n_q;
-  const int row0 = b * p.seq;
+  const int n_items = p.batch * p.kv_heads * n_qb;
+  const int G = gridDim.x, cta = blockIdx.x;
 
   if (threadIdx.x == 0) {
     mbar_init(kv_full, 1);
+    mbar_init(kv_empty, 1);
     for (int s = 0; s < C::STAGES; ++s) {
       mbar_init(&q_full[s], 1);
       mbar_init(&q_empty[s], 1);
@@ -115,6 +147,7 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
     mbar_init(p_ready, 8);
     mbar_init(dq_full, 1);
     mbar_init(dq_free, 8);
+    mbar_init(epi_done, 8);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -131,24 +164,41 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
     if (lane == 0) {
       tma_prefetch_desc(&tm_qkv);
       tma_prefetch_desc(&tm_do);
-      mbar_expect_tx(kv_full, 2 * C::TILE);
-#pragma unroll
-      for (int kb = 0; kb < C::KB; ++kb) {
-        tma_load_2d(smem + C::K_OFF + kb * 16384, &tm_qkv, kv_full, p.k_col + kvh * HD + 64 * kb, row0 + j * 128);
-        tma_load_2d(smem + C::V_OFF + kb * 16384, &tm_qkv, kv_full, p.v_col + kvh * HD + 64 * kb, row0 + j * 128);
-      }
-      for (int it = 0; it < n_it; ++it) {
-        const int h = kvh * group + it / n_q;
-        const int i = j + it % n_q;
-        const int st = it % C::STAGES;
-        if (!mbar_wait_bounded(&q_empty[st], ((it / C::STAGES) & 1) ^ 1u, abort_flag, errs, kErrAttnWait, 10)) break;
-        uint8_t* qs = smem + C::QD_OFF + st * 2 * C::TILE;
-        uint8_t* ds = qs + C::TILE;
-        mbar_expect_tx(&q_full[st], 2 * C::TILE);
+      int g = 0;  // global iteration counter (stage ring position)
+      bool ok = true;
+      for (int k = 0, u; ok && (u = bwd_item_index(k, cta, G, n_items)) >= 0; ++k) {
+        const BwdItem w = bwd_item(u, p.batch, p.kv_heads);
+        const int row0 = w.b * p.seq;
+        const int n_q = n_qb - w.j;
+        if (!mbar_wait_bounded(kv_empty, (k & 1) ^ 1u, abort_flag, errs, kErrAttnWait, 9)) break;
+        mbar_expect_tx(kv_full, 2 * C::TILE);
 #pragma unroll
         for (int kb = 0; kb < C::KB; ++kb) {
-          tma_load_2d(qs + kb * 16384, &tm_qkv, &q_full[st], h * HD + 64 * kb, row0 + i * 128);
-          tma_load_2d(ds + kb * 16384, &tm_do, &q_full[st], h * HD + 64 * kb, row0 + i * 128);
+          tma_load_2d(smem + C::K_OFF + kb * 16384, &tm_qkv, kv_full, p.k_col + w.kvh * HD + 64 * kb,
+                      row0 + w.j * 128);
+          tma_load_2d(smem + C::V_OFF + kb * 16384, &tm_qkv, kv_full, p.v_col + w.kvh * HD + 64 * kb,
+                      row0 + w.j * 128);
+        }
+        for (int it = 0; it < group * n_q; ++it, ++g) {
+          const int h = w.kvh * group + it / n_q;
+          const int i = w.j + it % n_q;
+          const int st = g % C::STAGES;
+          if (!mbar_wait_bounded(&q_empty[st], ((g / C::STAGES) & 1) ^ 1u, abort_flag, errs, kErrAttnWait, 10)) {
+            ok = false;
+            break;
+          }
+          uint8_t* qs = smem + C::QD_OFF + st * 2 * C::TILE;
+          uint8_t* ds = qs + C::TILE;
+          uint8_t* ls = smem + C::LD_OFF + st * 1024;
+          const size_t vec = ((size_t)w.b * p.heads + h) * p.seq + (size_t)i * 128;
+          mbar_expect_tx(&q_full[st], 2 * C::TILE + 1024);
+#pragma unroll
+          for (int kb = 0; kb < C::KB; ++kb) {
+            tma_load_2d(qs + kb * 16384, &tm_qkv, &q_full[st], h * HD + 64 * kb, row0 + i * 128);
+            tma_load_2d(ds + kb * 16384, &tm_do, &q_full[st], h * HD + 64 * kb, row0 + i * 128);
+          }
+          bulk_load(ls, p.lse + vec, 512, &q_full[st]);
+          bulk_load(ls + 512, p.delta + vec, 512, &q_full[st]);
         }
       }
     }
@@ -161,49 +211,72 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
       const uint32_t v_addr = smem_u32(smem + C::V_OFF);
       const uint32_t pt_addr = smem_u32(smem + C::PT_OFF);
       const uint32_t dst_addr = smem_u32(smem + C::DST_OFF);
-      bool ok = mbar_wait_bounded(kv_full, 0, abort_flag, errs, kErrAttnWait, 11);
-      for (int it = 0; it < n_it && ok; ++it) {
-        const int st = it % C::STAGES;
-        if (!mbar_wait_bounded(&q_full[st], (it / C::STAGES) & 1, abort_flag, errs, kErrAttnWait, 12)) break;
-        if (HD == 128 && it > 0 &&
-            !mbar_wait_bounded(dq_free, (it - 1) & 1, abort_flag, errs, kErrAttnWait, 13))
-          break;
-        tc_fence_after();
-        const uint32_t q_addr = smem_u32(smem + C::QD_OFF + st * 2 * C::TILE);
-        const uint32_t do_addr = q_addr + C::TILE;
+      int g = 0;
+      bool ok = true;
+      for (int k = 0, u; ok && (u = bwd_item_index(k, cta, G, n_items)) >= 0; ++k) {
+        const BwdItem w = bwd_item(u, p.batch, p.kv_heads);
+        const int n_it = group * (n_qb - w.j);
+        if (!mbar_wait_bounded(kv_full, k & 1, abort_flag, errs, kErrAttnWait, 11)) break;
+        for (int it = 0; it < n_it; ++it, ++g) {
+          const int st = g % C::STAGES;
+          if (!mbar_wait_bounded(&q_full[st], (g / C::STAGES) & 1, abort_flag, errs, kErrAttnWait, 12)) {
+            ok = false;
+            break;
+          }
+          if (HD == 128 && g > 0 && !mbar_wait_bounded(dq_free, (g - 1) & 1, abort_flag, errs, kErrAttnWait, 13)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t q_addr = smem_u32(smem + C::QD_OFF + st * 2 * C::TILE);
+          const uint32_t do_addr = q_addr + C::TILE;
 #pragma unroll
-        for (int ks = 0; ks < HD / 16; ++ks) {
-          const uint32_t off = (ks >> 2) * 16384 + (ks & 3) * 32;
-          tc_mma_f16(tmem + C::T_ST, smem_desc_sw128(k_addr + off, 16, 1024), smem_desc_sw128(q_addr + off, 16, 1024),
-                     ID_S, ks > 0 ? 1u : 0u);
-        }
+          for (int ks = 0; ks < HD / 16; ++ks) {
+            const uint32_t off = (ks >> 2) * 16384 + (ks & 3) * 32;
+            tc_mma_f16(tmem + C::T_ST, smem_desc_sw128(k_addr + off, 16, 1024),
+                       smem_desc_sw128(q_addr + off, 16, 1024), ID_S, ks > 0 ? 1u : 0u);
+          }
 #pragma unroll
-        for (int ks = 0; ks < HD / 16; ++ks) {
-          const uint32_t off = (ks >> 2) * 16384 + (ks & 3) * 32;
-          tc_mma_f16(tmem + C::T_DPT, smem_desc_sw128(v_addr + off, 16, 1024),
-                     smem_desc_sw128(do_addr + off, 16, 1024), ID_S, ks > 0 ? 1u : 0u);
-        }
-        tc_commit(st_full);
-        if (!mbar_wait_bounded(p_ready, it & 1, abort_flag, errs, kErrAttnWait, 14)) break;
-        if (HD == 64 && it > 0 && !mbar_wait_bounded(dq_free, (it - 1) & 1, abort_flag, errs, kErrAttnWait, 15)) break;
-        tc_fence_after();
+          for (int ks = 0; ks < HD / 16; ++ks) {
+            const uint32_t off = (ks >> 2) * 16384 + (ks & 3) * 32;
+            tc_mma_f16(tmem + C::T_DPT, smem_desc_sw128(v_addr + off, 16, 1024),
+                       smem_desc_sw128(do_addr + off, 16, 1024), ID_S, ks > 0 ? 1u : 0u);
+          }
+          tc_commit(st_full);
+          if (!mbar_wait_bounded(p_ready, g & 1, abort_flag, errs, kErrAttnWait, 14)) {
+            ok = false;
+            break;
+          }
+          if (HD == 64 && g > 0 && !mbar_wait_bounded(dq_free, (g - 1) & 1, abort_flag, errs, kErrAttnWait, 15)) {
+            ok = false;
+            break;
+          }
+          // The previous item's dK / dV must be read out before this item's first MMA overwrites them.
+          if (it == 0 && k > 0 && !mbar_wait_bounded(epi_done, (k - 1) & 1, abort_flag, errs, kErrAttnWait, 18)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
 #pragma unroll
-        for (int ks = 0; ks < 8; ++ks) {  // K = 128 query rows
-          const uint32_t aoff = (ks >> 2) * 16384 + (ks & 3) * 32;
-          const uint32_t boff = ks * 2048;
-          const uint32_t acc = (it > 0 || ks > 0) ? 1u : 0u;
-          tc_mma_f16(tmem + C::T_DV, smem_desc_sw128(pt_addr + aoff, 16, 1024),
-                     smem_desc_sw128(do_addr + boff, 16384, 1024), ID_KV, acc);
-          tc_mma_f16(tmem + C::T_DK, smem_desc_sw128(dst_addr + aoff, 16, 1024),
-                     smem_desc_sw128(q_addr + boff, 16384, 1024), ID_KV, acc);
-        }
+          for (int ks = 0; ks < 8; ++ks) {  // K = 128 query rows
+            const uint32_t aoff = (ks >> 2) * 16384 + (ks & 3) * 32;
+            const uint32_t boff = ks * 2048;
+            const uint32_t acc = (it > 0 || ks > 0) ? 1u : 0u;
+            tc_mma_f16(tmem + C::T_DV, smem_desc_sw128(pt_addr + aoff, 16, 1024),
+                       smem_desc_sw128(do_addr + boff, 16384, 1024), ID_KV, acc);
+            tc_mma_f16(tmem + C::T_DK, smem_desc_sw128(dst_addr + aoff, 16, 1024),
+                       smem_desc_sw128(q_addr + boff, 16384, 1024), ID_KV, acc);
+          }
 #pragma unroll
-        for (int ks = 0; ks < 8; ++ks) {  // K = 128 kv rows
-          tc_mma_f16(tmem + C::T_DQ, smem_desc_sw128(dst_addr + ks * 2048, 16384, 1024),
-                     smem_desc_sw128(k_addr + ks * 2048, 16384, 1024), ID_Q, ks > 0 ? 1u : 0u);
+          for (int ks = 0; ks < 8; ++ks) {  // K = 128 kv rows
+            tc_mma_f16(tmem + C::T_DQ, smem_desc_sw128(dst_addr + ks * 2048, 16384, 1024),
+                       smem_desc_sw128(k_addr + ks * 2048, 16384, 1024), ID_Q, ks > 0 ? 1u : 0u);
+          }
+          tc_commit(dq_full);
+          tc_commit(&q_empty[st]);
         }
-        tc_commit(dq_full);
-        tc_commit(&q_empty[st]);
+        if (!ok) break;
+        tc_commit(kv_empty);  // K_j / V_j no longer read once this item's MMAs complete
       }
     }
   } else {
@@ -215,85 +288,124 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
     const float scale2 = p.scale * 1.4426950408889634f;
     uint8_t* pt = smem + C::PT_OFF;
     uint8_t* dst = smem + C::DST_OFF;
+    uint8_t* stg = smem + C::STG_OFF + (warp - 2) * 2 * kBwdChunk;
+    int g = 0;
     bool ok = true;
-    for (int it = 0; it < n_it && ok; ++it) {
-      const int h = kvh * group + it / n_q;
-      const int i = j + it % n_q;
-      const size_t vec_base = ((size_t)b * p.heads + h) * p.seq + (size_t)i * 128 + col0;
-      if (!mbar_wait_bounded(st_full, it & 1, abort_flag, errs, kErrAttnWait, 16)) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
-      const bool diag = (i == j);
-#pragma unroll
-      for (int c = 0; c < 64; c += 32) {
-        uint32_t sv[32], dpv[32];
-        tmem_ld_32x32b_x32(lane_base + C::T_ST + col0 + c, sv);
-        tmem_ld_32x32b_x32(lane_base + C::T_DPT + col0 + c, dpv);
-        float lse_v[32], del_v[32];
-        const float4* l4 = reinterpret_cast<const float4*>(p.lse + vec_base + c);
-        const float4* d4 = reinterpret_cast<const float4*>(p.delta + vec_base + c);
-#pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          const float4 a = __ldg(l4 + e), dd = __ldg(d4 + e);
-          lse_v[4 * e] = a.x; lse_v[4 * e + 1] = a.y; lse_v[4 * e + 2] = a.z; lse_v[4 * e + 3] = a.w;
-          del_v[4 * e] = dd.x; del_v[4 * e + 1] = dd.y; del_v[4 * e + 2] = dd.z; del_v[4 * e + 3] = dd.w;
+    for (int k = 0, u; ok && (u = bwd_item_index(k, cta, G, n_items)) >= 0; ++k) {
+      const BwdItem w = bwd_item(u, p.batch, p.kv_heads);
+      const int n_q = n_qb - w.j;
+      const int n_it = group * n_q;
+      const int row0 = w.b * p.seq;
+      for (int it = 0; it < n_it; ++it, ++g) {
+        const int h = w.kvh * group + it / n_q;
+        const int i = w.j + it % n_q;
+        if (!mbar_wait_bounded(st_full, g & 1, abort_flag, errs, kErrAttnWait, 16)) {
+          ok = false;
+          break;
         }
-        tc_wait_ld();
-        uint32_t pk[16], dk[16];
+        tc_fence_after();
+        const bool diag = (i == w.j);
+        const float* lds = reinterpret_cast<const float*>(smem + C::LD_OFF + (g % C::STAGES) * 1024);
 #pragma unroll
-        for (int e = 0; e < 32; e += 2) {
-          float pv[2], dv[2];
+        for (int c = 0; c < 64; c += 32) {
+          uint32_t sv[32], dpv[32];
+          tmem_ld_32x32b_x32(lane_base + C::T_ST + col0 + c, sv);
+          tmem_ld_32x32b_x32(lane_base + C::T_DPT + col0 + c, dpv);
+          float lse_v[32], del_v[32];
+          const float4* l4 = reinterpret_cast<const float4*>(lds + col0 + c);
+          const float4* d4 = reinterpret_cast<const float4*>(lds + 128 + col0 + c);
 #pragma unroll
-          for (int t = 0; t < 2; ++t) {
-            float pr = ex2_approx(fmaf(__uint_as_float(sv[e + t]), scale2, -lse_v[e + t]));
-            if (diag && (col0 + c + e + t < r)) pr = 0.f;
-            pv[t] = pr;
-            dv[t] = pr * (__uint_as_float(dpv[e + t]) - del_v[e + t]);
+          for (int e = 0; e < 8; ++e) {
+            const float4 a = l4[e], dd = d4[e];
+            lse_v[4 * e] = a.x; lse_v[4 * e + 1] = a.y; lse_v[4 * e + 2] = a.z; lse_v[4 * e + 3] = a.w;
+            del_v[4 * e] = dd.x; del_v[4 * e + 1] = dd.y; del_v[4 * e + 2] = dd.z; del_v[4 * e + 3] = dd.w;
           }
-          pk[e >> 1] = pack_bf16(pv[0], pv[1]);
-          dk[e >> 1] = pack_bf16(dv[0], dv[1]);
-        }
-        store_swizzled_row(pt, r, col0 + c, pk);
-        store_swizzled_row(dst, r, col0 + c, dk);
-      }
-      fence_async_smem();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(p_ready);
-      // dQ_i rows (thread = query row r of block i), this warpgroup's half of the columns
-      if (!mbar_wait_bounded(dq_full, it & 1, abort_flag, errs, kErrAttnWait, 17)) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
-      float* dq_row = p.dq_acc + (size_t)(row0 + i * 128 + r) * (p.heads * HD) + h * HD + wg * C::HALF;
+          tc_wait_ld();
+          uint32_t pk[16], dk[16];
 #pragma unroll
-      for (int c = 0; c < C::HALF; c += 32) {
-        uint32_t qv[32];
-        tmem_ld_32x32b_x32(lane_base + C::T_DQ + wg * C::HALF + c, qv);
-        tc_wait_ld();
+          for (int e = 0; e < 32; e += 2) {
+            float pv[2], dv[2];
 #pragma unroll
-        for (int e = 0; e < 32; e += 4) {
-          atomicAdd(reinterpret_cast<float4*>(dq_row + c + e),
-                    make_float4(__uint_as_float(qv[e]) * p.scale, __uint_as_float(qv[e + 1]) * p.scale,
-                                __uint_as_float(qv[e + 2]) * p.scale, __uint_as_float(qv[e + 3]) * p.scale));
+            for (int t = 0; t < 2; ++t) {
+              float pr = ex2_approx(fmaf(__uint_as_float(sv[e + t]), scale2, -lse_v[e + t]));
+              if (diag && (col0 + c + e + t < r)) pr = 0.f;
+              pv[t] = pr;
+              dv[t] = pr * (__uint_as_float(dpv[e + t]) - del_v[e + t]);
+            }
+            pk[e >> 1] = pack_bf16(pv[0], pv[1]);
+            dk[e >> 1] = pack_bf16(dv[0], dv[1]);
+          }
+          store_swizzled_row(pt, r, col0 + c, pk);
+          store_swizzled_row(dst, r, col0 + c, dk);
+        }
+        fence_async_smem();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(p_ready);
+        // dQ_i rows (thread = query row r of block i), this warpgroup's half of the columns
+        if (!mbar_wait_bounded(dq_full, g & 1, abort_flag, errs, kErrAttnWait, 17)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        if constexpr (C::TMA_DQ) {
+          // 32 columns = two 16-column fp32 chunks; both staging chunks of this warp are free once
+          // the previous iteration's reductions have read them.
+          if (lane == 0) bulk_wait_group_read<0>();
+          __syncwarp();
+#pragma unroll
+          for (int hc = 0; hc < 2; ++hc) {
+            uint32_t qv[16];
+            tmem_ld_32x32b_x16(lane_base + C::T_DQ + wg * C::HALF + 16 * hc, qv);
+            tc_wait_ld();
+            uint8_t* buf = stg + hc * kBwdChunk;
+#pragma unroll
+            for (int jj = 0; jj < 4; ++jj) {
+              const int off = lane * 64 + ((jj ^ ((lane >> 1) & 3)) << 4);
+              *reinterpret_cast<float4*>(buf + off) =
+                  make_float4(__uint_as_float(qv[4 * jj]) * p.scale, __uint_as_float(qv[4 * jj + 1]) * p.scale,
+                              __uint_as_float(qv[4 * jj + 2]) * p.scale, __uint_as_float(qv[4 * jj + 3]) * p.scale);
+            }
+          }
+          fence_async_smem();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) {
+            mbar_arrive(dq_free);
+#pragma unroll
+            for (int hc = 0; hc < 2; ++hc)
+              tma_reduce_add_2d(&tm_dq, stg + hc * kBwdChunk, h * HD + wg * C::HALF + 16 * hc,
+                                row0 + i * 128 + q4 * 32);
+            bulk_commit_group();
+          }
+        } else {
+          float* dq_row = p.dq_acc + (size_t)(row0 + i * 128 + r) * (p.heads * HD) + h * HD + wg * C::HALF;
+#pragma unroll
+          for (int c = 0; c < C::HALF; c += 32) {
+            uint32_t qv[32];
+            tmem_ld_32x32b_x32(lane_base + C::T_DQ + wg * C::HALF + c, qv);
+            tc_wait_ld();
+#pragma unroll
+            for (int e = 0; e < 32; e += 4) {
+              atomicAdd(reinterpret_cast<float4*>(dq_row + c + e),
+                        make_float4(__uint_as_float(qv[e]) * p.scale, __uint_as_float(qv[e + 1]) * p.scale,
+                                    __uint_as_float(qv[e + 2]) * p.scale, __uint_as_float(qv[e + 3]) * p.scale));
+            }
+          }
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(dq_free);
         }
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(dq_free);
-    }
-    if (ok && n_it > 0) {
-      // The last dq_full also covers the final dV / dK accumulation.
+      if (!ok) break;
+      // The item's last dq_full also covers its final dV / dK accumulation.
       tc_fence_after();
-      const int kv_row = row0 + j * 128 + r;
-      const int pos = j * 128 + r;
+      const int kv_row = row0 + w.j * 128 + r;
+      const int pos = w.j * 128 + r;
       constexpr int HALF = C::HALF;
       constexpr int QTR = HALF / 2;  // RoPE pairs per warpgroup
-      __nv_bfloat16* dk_out = p.dqkv + (size_t)kv_row * p.ld + p.k_col + kvh * HD;
-      __nv_bfloat16* dv_out = p.dqkv + (size_t)kv_row * p.ld + p.v_col + kvh * HD + wg * HALF;
+      __nv_bfloat16* dk_out = p.dqkv + (size_t)kv_row * p.ld + p.k_col + w.kvh * HD;
+      __nv_bfloat16* dv_out = p.dqkv + (size_t)kv_row * p.ld + p.v_col + w.kvh * HD + wg * HALF;
 #pragma unroll
       for (int c = 0; c < HALF; c += 32) {
         uint32_t vv[32];
@@ -301,12 +413,12 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
         tc_wait_ld();
 #pragma unroll
         for (int e = 0; e < 32; e += 8) {
-          uint4 w;
-          w.x = pack_bf16(__uint_as_float(vv[e]), __uint_as_float(vv[e + 1]));
-          w.y = pack_bf16(__uint_as_float(vv[e + 2]), __uint_as_float(vv[e + 3]));
-          w.z = pack_bf16(__uint_as_float(vv[e + 4]), __uint_as_float(vv[e + 5]));
-          w.w = pack_bf16(__uint_as_float(vv[e + 6]), __uint_as_float(vv[e + 7]));
-          *reinterpret_cast<uint4*>(dv_out + c + e) = w;
+          uint4 o;
+          o.x = pack_bf16(__uint_as_float(vv[e]), __uint_as_float(vv[e + 1]));
+          o.y = pack_bf16(__uint_as_float(vv[e + 2]), __uint_as_float(vv[e + 3]));
+          o.z = pack_bf16(__uint_as_float(vv[e + 4]), __uint_as_float(vv[e + 5]));
+          o.w = pack_bf16(__uint_as_float(vv[e + 6]), __uint_as_float(vv[e + 7]));
+          *reinterpret_cast<uint4*>(dv_out + c + e) = o;
         }
       }
       {
@@ -337,7 +449,12 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
           *reinterpret_cast<uint4*>(dk_out + HALF + c0 + e) = wb;
         }
       }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(epi_done);
     }
+    if (C::TMA_DQ && lane == 0) bulk_wait_group<0>();
+    __syncwarp();
   }
 
   tc_fence_before();
@@ -409,16 +526,23 @@ __global__ void attn_dq_convert_kernel(const float* __restrict__ dq_acc, __nv_bf
   }
 }
 
+// dq_acc as a TMA target: fp32 [rows, heads*hd], one 32-row x 16-column chunk per box.
+CUtensorMap make_dq_map(const AttnBwdParams& p) {
+  const int rows = p.batch * p.seq, cols = p.heads * p.head_dim;
+  return make_tmap_2d(CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, p.dq_acc, (uint64_t)cols, (uint64_t)rows, (uint64_t)cols, 16,
+                      32, CU_TENSOR_MAP_SWIZZLE_64B);
+}
+
+int bwd_grid(const AttnBwdParams& p) {
+  const int items = p.batch * p.kv_heads * (p.seq / 128);
+  return std::max(1, std::min(items, num_sms_cached()));
+}
+
 template <int HD>
-void launch_bwd(const AttnBwdParams& p, const CUtensorMap& tq, const CUtensorMap& tdo, cudaStream_t s) {
+void launch_bwd(const AttnBwdParams& p, const CUtensorMap& tq, const CUtensorMap& tdo, const CUtensorMap& tdq,
+                DeviceErrors* errs, cudaStream_t s) {
   using C = AttnBwdCfg<HD>;
-  static bool cfg = false;
-  if (!cfg) {
-    B200_CUDA_CHECK(cudaFuncSetAttribute(attn_bwd_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES));
-    cfg = true;
-  }
-  dim3 grid(p.seq / 128, p.kv_heads, p.batch);
-  attn_bwd_kernel<HD><<<grid, BWD_THREADS, C::SMEM_BYTES, s>>>(tq, tdo, p, device_errors_ptr());
+  attn_bwd_kernel<HD><<<bwd_grid(p), BWD_THREADS, C::SMEM_BYTES, s>>>(tq, tdo, tdq, p, errs);
 }
 
 }  // namespace
@@ -436,10 +560,19 @@ void attention_bwd(const AttnBwdParams& p, cudaStream_t s) {
   }
   CUtensorMap tq = make_tmap_bf16_2d(p.qkv, (uint64_t)p.ld, (uint64_t)rows, (uint64_t)p.ld, 64, 128);
   CUtensorMap tdo = make_tmap_bf16_2d(p.dout, (uint64_t)p.ld_out, (uint64_t)rows, (uint64_t)p.ld_out, 64, 128);
+  CUtensorMap tdq = make_dq_map(p);
+  static bool cfg = false;
+  if (!cfg) {
+    B200_CUDA_CHECK(cudaFuncSetAttribute(attn_bwd_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         AttnBwdCfg<64>::SMEM_BYTES));
+    B200_CUDA_CHECK(cudaFuncSetAttribute(attn_bwd_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         AttnBwdCfg<128>::SMEM_BYTES));
+    cfg = true;
+  }
   if (p.head_dim == 64)
-    launch_bwd<64>(p, tq, tdo, s);
+    launch_bwd<64>(p, tq, tdo, tdq, device_errors_ptr(), s);
   else
-    launch_bwd<128>(p, tq, tdo, s);
+    launch_bwd<128>(p, tq, tdo, tdq, device_errors_ptr(), s);
   B200_CUDA_CHECK(cudaGetLastError());
   const size_t work = (size_t)rows * p.heads * (p.head_dim / 16);
   const int blocks = (int)std::min<size_t>((work + 255) / 256, (size_t)num_sms_cached() * 16);
@@ -557,11 +690,11 @@ extern "C" int b200_attention_bwd_noalloc(const void* qkv, int ld, int k_col, in
                                                                     heads, head_dim);
     const CUtensorMap tq = make_tmap_bf16_2d(p.qkv, (uint64_t)ld, (uint64_t)rows, (uint64_t)ld, 64, 128);
     const CUtensorMap tdo = make_tmap_bf16_2d(p.dout, (uint64_t)ld_out, (uint64_t)rows, (uint64_t)ld_out, 64, 128);
-    const dim3 grid(seq / 128, kv_heads, batch);
+    const CUtensorMap tdq = make_dq_map(p);
     if (head_dim == 64)
-      attn_bwd_kernel<64><<<grid, BWD_THREADS, AttnBwdCfg<64>::SMEM_BYTES, stream>>>(tq, tdo, p, errs);
+      launch_bwd<64>(p, tq, tdo, tdq, errs, stream);
     else
-      attn_bwd_kernel<128><<<grid, BWD_THREADS, AttnBwdCfg<128>::SMEM_BYTES, stream>>>(tq, tdo, p, errs);
+      launch_bwd<128>(p, tq, tdo, tdq, errs, stream);
     const size_t work = rows * heads * (head_dim / 16);
     const int blocks = (int)std::min<size_t>((work + 255) / 256, (size_t)num_sms_cached() * 16);
     attn_dq_convert_kernel<<<blocks, 256, 0, stream>>>(dq_acc, p.dqkv, ld, (int)rows, seq, heads, head_dim, rope_cos,

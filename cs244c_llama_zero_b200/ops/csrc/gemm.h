@@ -49,6 +49,11 @@ struct GemmParams {
 };
 
 int num_sms();
+// Generic 2D tiled tensor map (dims {inner, outer}, row stride in elements); throws on misaligned
+// base or stride.
+CUtensorMap make_tmap_2d(CUtensorMapDataType dtype, int elem_bytes, const void* base, uint64_t inner, uint64_t outer,
+                         uint64_t row_stride_elems, uint32_t box_inner, uint32_t box_outer,
+                         CUtensorMapSwizzle swizzle);
 CUtensorMap make_tmap_bf16_2d(const void* base, uint64_t inner, uint64_t outer, uint64_t row_stride_elems,
                               uint32_t box_inner, uint32_t box_outer);
 void gemm_launch(const GemmOperands& op, GemmParams p, int epi, bool a_mn, bool b_mn, int bn, cudaStream_t stream);

@@ -477,9 +477,9 @@ PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
 
 }  // namespace
 
-static CUtensorMap encode_2d(CUtensorMapDataType dtype, int elem_bytes, const void* base, uint64_t inner,
-                             uint64_t outer, uint64_t row_stride_elems, uint32_t box_inner, uint32_t box_outer,
-                             CUtensorMapSwizzle swizzle) {
+CUtensorMap make_tmap_2d(CUtensorMapDataType dtype, int elem_bytes, const void* base, uint64_t inner, uint64_t outer,
+                         uint64_t row_stride_elems, uint32_t box_inner, uint32_t box_outer,
+                         CUtensorMapSwizzle swizzle) {
   B200_CHECK((reinterpret_cast<uintptr_t>(base) & 15) == 0, "TMA base address must be 16-byte aligned");
   B200_CHECK((row_stride_elems * elem_bytes) % 16 == 0, "TMA row stride must be a multiple of 16 bytes");
   CUtensorMap map;
@@ -496,17 +496,17 @@ static CUtensorMap encode_2d(CUtensorMapDataType dtype, int elem_bytes, const vo
 
 CUtensorMap make_tmap_bf16_2d(const void* base, uint64_t inner, uint64_t outer, uint64_t row_stride_elems,
                               uint32_t box_inner, uint32_t box_outer) {
-  return encode_2d(CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, base, inner, outer, row_stride_elems, box_inner, box_outer,
+  return make_tmap_2d(CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, base, inner, outer, row_stride_elems, box_inner, box_outer,
                    CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
 // Epilogue output / residual maps: one staging chunk (32 rows x 64 B) per box, 64-byte swizzle.
 static CUtensorMap epi_map_bf16(const void* base, int rows, int cols, int ld) {
-  return encode_2d(CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, base, (uint64_t)cols, (uint64_t)rows, (uint64_t)ld, 32, 32,
+  return make_tmap_2d(CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, base, (uint64_t)cols, (uint64_t)rows, (uint64_t)ld, 32, 32,
                    CU_TENSOR_MAP_SWIZZLE_64B);
 }
 static CUtensorMap epi_map_f32(const void* base, int rows, int cols, int ld) {
-  return encode_2d(CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, base, (uint64_t)cols, (uint64_t)rows, (uint64_t)ld, 16, 32,
+  return make_tmap_2d(CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, base, (uint64_t)cols, (uint64_t)rows, (uint64_t)ld, 16, 32,
                    CU_TENSOR_MAP_SWIZZLE_64B);
 }
 
