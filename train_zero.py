@@ -39,6 +39,7 @@ from cs244c_llama_zero_b200.profiler import (
     flops_to_tflops_per_second,
     overlap_efficiency,
 )
+from cs244c_llama_zero_b200.train.faults import FaultInjector
 from cs244c_llama_zero_b200.train.session import init_distributed
 from train import (
     add_data_args,
@@ -109,6 +110,8 @@ def parse_args(argv=None) -> argparse.Namespace:
     p.add_argument("--tflops-mode", type=str, default="estimate", choices=["estimate", "profile", "off"])
     p.add_argument("--verbose", action="store_true")
     p.add_argument("--verbose-memory", action="store_true")
+    p.add_argument("--pg-timeout-s", type=float, default=600.0,
+                   help="Process-group timeout: a collective waiting longer than this on a missing rank fails")
     p.set_defaults(activation_checkpointing=False)
     return p.parse_args(argv)
 
@@ -213,7 +216,8 @@ class MemoryRecorder:
 
 
 def train(args: argparse.Namespace) -> None:
-    rank, world_size, device = init_distributed()
+    rank, world_size, device = init_distributed(args.pg_timeout_s)
+    faults = FaultInjector(rank)
     verbose = bool(args.verbose)
     configure_runtime(device)
     set_seed(args.seed)
@@ -279,6 +283,8 @@ def train(args: argparse.Namespace) -> None:
     t_start = time.perf_counter()
 
     for step in range(start_step, args.max_steps + 1):
+        if faults:
+            faults.at_step(step)
         sample = args.profile_memory_interval > 0 and (step == 1 or step == args.max_steps
                                                        or step % args.profile_memory_interval == 0)
         is_measured = measured_step is not None and step == measured_step
