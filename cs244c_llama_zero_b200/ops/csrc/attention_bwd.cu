@@ -465,35 +465,38 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
   }
 }
 
-// delta[b, h, s] = sum_c dO[row, h*hd + c] * O[row, h*hd + c]; one warp per (row, head).
+// delta[b, h, s] = sum_c dO[row, h*hd + c] * O[row, h*hd + c].  One warp per row: lane l takes the
+// 16-byte column groups l, l+32, ...; a head spans hd/8 consecutive groups (8 or 16 lanes), reduced
+// with butterfly shuffles inside that lane group, so every lane loads on every round.
+template <int HD>
 __global__ void attn_delta_kernel(const __nv_bfloat16* __restrict__ o, const __nv_bfloat16* __restrict__ dout, int ld,
-                                  float* __restrict__ delta, int rows, int seq, int heads, int hd) {
-  const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+                                  float* __restrict__ delta, int rows, int seq, int heads) {
+  constexpr int G = HD / 8;  // lanes per head
+  const int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
-  if (gw >= rows * heads) return;
-  const int row = gw / heads, h = gw % heads;
-  const __nv_bfloat16* a = o + (size_t)row * ld + h * hd;
-  const __nv_bfloat16* g = dout + (size_t)row * ld + h * hd;
-  float acc = 0.f;
-  for (int c = lane * 8; c < hd; c += 256) {
-    const uint4 qa = *reinterpret_cast<const uint4*>(a + c);
-    const uint4 qg = *reinterpret_cast<const uint4*>(g + c);
-    const uint32_t wa[4] = {qa.x, qa.y, qa.z, qa.w}, wg[4] = {qg.x, qg.y, qg.z, qg.w};
+  if (row >= rows) return;
+  const int groups = heads * G;
+  const int b = row / seq, s = row % seq;
+  for (int c0 = 0; c0 < groups; c0 += 32) {
+    const int c = c0 + lane;
+    float acc = 0.f;
+    if (c < groups) {
+      const uint4 qa = *reinterpret_cast<const uint4*>(o + (size_t)row * ld + c * 8);
+      const uint4 qg = *reinterpret_cast<const uint4*>(dout + (size_t)row * ld + c * 8);
+      const uint32_t wa[4] = {qa.x, qa.y, qa.z, qa.w}, wg[4] = {qg.x, qg.y, qg.z, qg.w};
 #pragma unroll
-    for (int e = 0; e < 4; ++e) acc += bf16lo(wa[e]) * bf16lo(wg[e]) + bf16hi(wa[e]) * bf16hi(wg[e]);
-  }
+      for (int e = 0; e < 4; ++e) acc += bf16lo(wa[e]) * bf16lo(wg[e]) + bf16hi(wa[e]) * bf16hi(wg[e]);
+    }
 #pragma unroll
-  for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
-  if (lane == 0) {
-    const int b = row / seq, s = row % seq;
-    delta[((size_t)b * heads + h) * seq + s] = acc;
+    for (int off = G / 2; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+    if (c < groups && (lane % G) == 0) delta[((size_t)b * heads + c / G) * seq + s] = acc;
   }
 }
 
 // q columns of dqkv = RoPE^T(dq_acc) in bf16; 8 consecutive pairs per thread.
-__global__ void attn_dq_convert_kernel(const float* __restrict__ dq_acc, __nv_bfloat16* __restrict__ dqkv, int ld,
-                                       int rows, int seq, int heads, int hd, const float* __restrict__ cosv,
-                                       const float* __restrict__ sinv) {
+__global__ void attn_dq_convert_kernel(const float* dq_acc, __nv_bfloat16* __restrict__ dqkv, int ld, int rows,
+                                       int seq, int heads, int hd, const float* __restrict__ cosv,
+                                       const float* __restrict__ sinv, bool rezero) {
   const int half = hd / 2;
   const int groups = half / 8;
   const size_t total = (size_t)rows * heads * groups;
@@ -508,6 +511,14 @@ __global__ void attn_dq_convert_kernel(const float* __restrict__ dq_acc, __nv_bf
     const float4 b1 = *reinterpret_cast<const float4*>(src + half + c + 4);
     const float x0[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
     const float x1[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+    if (rezero) {  // leave the accumulator zeroed for the next backward that reuses it
+      float* w = const_cast<float*>(src);
+      const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
+      *reinterpret_cast<float4*>(w + c) = z;
+      *reinterpret_cast<float4*>(w + c + 4) = z;
+      *reinterpret_cast<float4*>(w + half + c) = z;
+      *reinterpret_cast<float4*>(w + half + c + 4) = z;
+    }
     float lo[8], hi[8];
 #pragma unroll
     for (int t = 0; t < 8; ++t) {
@@ -524,6 +535,16 @@ __global__ void attn_dq_convert_kernel(const float* __restrict__ dq_acc, __nv_bf
     *reinterpret_cast<uint4*>(out + c) = wl;
     *reinterpret_cast<uint4*>(out + half + c) = wh;
   }
+}
+
+void launch_delta(const __nv_bfloat16* o, const __nv_bfloat16* dout, int ld, float* delta, int rows, int seq, int heads,
+                  int hd, cudaStream_t s) {
+  const int blocks = (rows * 32 + 255) / 256;
+  if (hd == 64)
+    attn_delta_kernel<64><<<blocks, 256, 0, s>>>(o, dout, ld, delta, rows, seq, heads);
+  else
+    attn_delta_kernel<128><<<blocks, 256, 0, s>>>(o, dout, ld, delta, rows, seq, heads);
+  B200_CUDA_CHECK(cudaGetLastError());
 }
 
 // dq_acc as a TMA target: fp32 [rows, heads*hd], one 32-row x 16-column chunk per box.
@@ -552,12 +573,7 @@ void attention_bwd(const AttnBwdParams& p, cudaStream_t s) {
   B200_CHECK(p.seq % 128 == 0, "attention_bwd: seq_len must be a multiple of 128");
   B200_CHECK(p.rope_cos != nullptr && p.rope_sin != nullptr, "attention_bwd: RoPE tables required");
   const int rows = p.batch * p.seq;
-  {
-    const int warps = rows * p.heads;
-    attn_delta_kernel<<<(warps * 32 + 255) / 256, 256, 0, s>>>(p.out, p.dout, p.ld_out, p.delta, rows, p.seq,
-                                                               p.heads, p.head_dim);
-    B200_CUDA_CHECK(cudaGetLastError());
-  }
+  launch_delta(p.out, p.dout, p.ld_out, p.delta, rows, p.seq, p.heads, p.head_dim, s);
   CUtensorMap tq = make_tmap_bf16_2d(p.qkv, (uint64_t)p.ld, (uint64_t)rows, (uint64_t)p.ld, 64, 128);
   CUtensorMap tdo = make_tmap_bf16_2d(p.dout, (uint64_t)p.ld_out, (uint64_t)rows, (uint64_t)p.ld_out, 64, 128);
   CUtensorMap tdq = make_dq_map(p);
@@ -577,7 +593,7 @@ void attention_bwd(const AttnBwdParams& p, cudaStream_t s) {
   const size_t work = (size_t)rows * p.heads * (p.head_dim / 16);
   const int blocks = (int)std::min<size_t>((work + 255) / 256, (size_t)num_sms_cached() * 16);
   attn_dq_convert_kernel<<<blocks, 256, 0, s>>>(p.dq_acc, p.dqkv, p.ld, rows, p.seq, p.heads, p.head_dim, p.rope_cos,
-                                                p.rope_sin);
+                                                p.rope_sin, p.rezero_dq_acc);
   B200_CUDA_CHECK(cudaGetLastError());
   count_launch(3);
 }
@@ -685,9 +701,7 @@ extern "C" int b200_attention_bwd_noalloc(const void* qkv, int ld, int k_col, in
     p.kv_heads = kv_heads;
     p.head_dim = head_dim;
     p.scale = scale;
-    const int warps = (int)rows * heads;
-    attn_delta_kernel<<<(warps * 32 + 255) / 256, 256, 0, stream>>>(p.out, p.dout, p.ld_out, p.delta, (int)rows, seq,
-                                                                    heads, head_dim);
+    launch_delta(p.out, p.dout, p.ld_out, p.delta, (int)rows, seq, heads, head_dim, stream);
     const CUtensorMap tq = make_tmap_bf16_2d(p.qkv, (uint64_t)ld, (uint64_t)rows, (uint64_t)ld, 64, 128);
     const CUtensorMap tdo = make_tmap_bf16_2d(p.dout, (uint64_t)ld_out, (uint64_t)rows, (uint64_t)ld_out, 64, 128);
     const CUtensorMap tdq = make_dq_map(p);
@@ -698,7 +712,7 @@ extern "C" int b200_attention_bwd_noalloc(const void* qkv, int ld, int k_col, in
     const size_t work = rows * heads * (head_dim / 16);
     const int blocks = (int)std::min<size_t>((work + 255) / 256, (size_t)num_sms_cached() * 16);
     attn_dq_convert_kernel<<<blocks, 256, 0, stream>>>(dq_acc, p.dqkv, ld, (int)rows, seq, heads, head_dim, rope_cos,
-                                                       rope_sin);
+                                                       rope_sin, false);
     count_launch(3);
   } catch (const std::exception& ex) {
     std::fprintf(stderr, "b200_attention_bwd_noalloc: %s\n", ex.what());

@@ -40,18 +40,6 @@ b200::GemmParams base_params(int M, int N, int K) {
   return p;
 }
 
-int pick_bn(int n_cols) { return n_cols <= 128 ? 128 : 256; }
-
-// Number of K splits so that small-output weight-gradient GEMMs still fill every SM.
-int pick_splits(int M, int N, int K, int bn) {
-  const int tiles = ((M + 127) / 128) * ((N + bn - 1) / bn);
-  const int kblocks = (K + 63) / 64;
-  const int target = 2 * b200::num_sms();
-  int splits = std::max(1, target / std::max(1, tiles));
-  splits = std::min(splits, std::max(1, kblocks / 8));  // keep at least 8 k-blocks per split
-  return splits;
-}
-
 // y[M,N] = x[M,K] @ w[N,K]^T (+ residual)
 void linear_fwd(Tensor x, Tensor w, Tensor out, std::optional<Tensor> residual, int64_t bn) {
   check_bf16_2d(x, "x");
@@ -72,7 +60,7 @@ void linear_fwd(Tensor x, Tensor w, Tensor out, std::optional<Tensor> residual, 
     epi = b200::EPI_RESIDUAL;
   }
   b200::GemmOperands op{x.data_ptr(), w.data_ptr(), (uint64_t)x.stride(0), (uint64_t)w.stride(0)};
-  b200::gemm_launch(op, p, epi, false, false, bn > 0 ? (int)bn : pick_bn(N), cur_stream());
+  b200::gemm_launch(op, p, epi, false, false, (int)bn, cur_stream());
 }
 
 void qkv_rope_fwd(Tensor x, Tensor w, Tensor out, Tensor cos, Tensor sin, int64_t seq_len, int64_t head_dim,
@@ -96,7 +84,7 @@ void qkv_rope_fwd(Tensor x, Tensor w, Tensor out, Tensor cos, Tensor sin, int64_
   p.head_dim = head_dim;
   p.rope_cols = rope_cols;
   b200::GemmOperands op{x.data_ptr(), w.data_ptr(), (uint64_t)x.stride(0), (uint64_t)w.stride(0)};
-  b200::gemm_launch(op, p, b200::EPI_ROPE, false, false, 256, cur_stream());
+  b200::gemm_launch(op, p, b200::EPI_ROPE, false, false, 0, cur_stream());
 }
 
 // h = silu(x @ Wg^T) * (x @ Wu^T); gu = [x @ Wg^T | x @ Wu^T].  w_gu = [Wg; Wu] of shape [2*ffn, K].
@@ -117,7 +105,7 @@ void swiglu_fwd(Tensor x, Tensor w_gu, Tensor h, Tensor gu) {
   p.ld_aux = gu.stride(0);
   p.ffn = ffn;
   b200::GemmOperands op{x.data_ptr(), w_gu.data_ptr(), (uint64_t)x.stride(0), (uint64_t)w_gu.stride(0)};
-  b200::gemm_launch(op, p, b200::EPI_SWIGLU, false, false, 256, cur_stream());
+  b200::gemm_launch(op, p, b200::EPI_SWIGLU, false, false, 0, cur_stream());
 }
 
 // dx[M,K] = dy[M,N] @ w[N,K]
@@ -132,7 +120,7 @@ void linear_dgrad(Tensor dy, Tensor w, Tensor dx, int64_t bn) {
   p.C = reinterpret_cast<__nv_bfloat16*>(dx.data_ptr());
   p.ldc = dx.stride(0);
   b200::GemmOperands op{dy.data_ptr(), w.data_ptr(), (uint64_t)dy.stride(0), (uint64_t)w.stride(0)};
-  b200::gemm_launch(op, p, b200::EPI_STORE, false, true, bn > 0 ? (int)bn : pick_bn(K), cur_stream());
+  b200::gemm_launch(op, p, b200::EPI_STORE, false, true, (int)bn, cur_stream());
 }
 
 // dgu = swiglu'(gu) * (dy @ w_down), with w_down [d, ffn] and gu/dgu [M, 2*ffn].
@@ -153,7 +141,7 @@ void swiglu_dgrad(Tensor dy, Tensor w_down, Tensor gu, Tensor dgu) {
   p.ld_aux_in = gu.stride(0);
   p.ffn = ffn;
   b200::GemmOperands op{dy.data_ptr(), w_down.data_ptr(), (uint64_t)dy.stride(0), (uint64_t)w_down.stride(0)};
-  b200::gemm_launch(op, p, b200::EPI_SWIGLU_BWD, false, true, 256, cur_stream());
+  b200::gemm_launch(op, p, b200::EPI_SWIGLU_BWD, false, true, 0, cur_stream());
 }
 
 // dw[N,K] (fp32) += dy[M,N]^T @ x[M,K]
@@ -166,13 +154,12 @@ void linear_wgrad(Tensor dy, Tensor x, Tensor dw, int64_t splits, int64_t bn) {
   TORCH_CHECK(dw.dim() == 2 && dw.size(0) == N && dw.size(1) == K && dw.stride(1) == 1, "linear_wgrad: dw shape");
   TORCH_CHECK(dw.stride(0) % 4 == 0 && reinterpret_cast<uintptr_t>(dw.data_ptr()) % 16 == 0, "dw alignment");
   c10::cuda::CUDAGuard g(dy.device());
-  const int b = bn > 0 ? (int)bn : pick_bn(K);
   auto p = base_params(N, K, M);
   p.C32 = dw.data_ptr<float>();
   p.ldc32 = dw.stride(0);
-  p.splits = splits > 0 ? (int)splits : pick_splits(N, K, M, b);
+  p.splits = splits > 0 ? (int)splits : 0;  // 0: chosen with the tile width
   b200::GemmOperands op{dy.data_ptr(), x.data_ptr(), (uint64_t)dy.stride(0), (uint64_t)x.stride(0)};
-  b200::gemm_launch(op, p, b200::EPI_ACC_F32, true, true, b, cur_stream());
+  b200::gemm_launch(op, p, b200::EPI_ACC_F32, true, true, (int)bn, cur_stream());
 }
 
 // Generic entry for tests: C = A op B with explicit majors.
@@ -348,7 +335,7 @@ void attention_fwd(Tensor qkv, int64_t k_col, int64_t v_col, Tensor out, Tensor 
 
 void attention_bwd(Tensor qkv, int64_t k_col, int64_t v_col, Tensor out, Tensor dout, Tensor lse, Tensor delta,
                    Tensor dq_acc, Tensor dqkv, Tensor cos, Tensor sin, int64_t batch, int64_t seq, int64_t heads,
-                   int64_t kv_heads, int64_t head_dim, double scale) {
+                   int64_t kv_heads, int64_t head_dim, double scale, bool rezero_dq_acc) {
   check_f32(cos, "cos");
   check_f32(sin, "sin");
   TORCH_CHECK(cos.numel() >= seq * head_dim / 2 && sin.numel() >= seq * head_dim / 2, "rope table too small");
@@ -383,6 +370,7 @@ void attention_bwd(Tensor qkv, int64_t k_col, int64_t v_col, Tensor out, Tensor 
   p.kv_heads = kv_heads;
   p.head_dim = head_dim;
   p.scale = (float)scale;
+  p.rezero_dq_acc = rezero_dq_acc;
   b200::attention_bwd(p, cur_stream());
 }
 
@@ -515,7 +503,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("cross_entropy_fwd", &cross_entropy_fwd);
   m.def("cross_entropy_bwd", &cross_entropy_bwd);
   m.def("attention_fwd", &attention_fwd);
-  m.def("attention_bwd", &attention_bwd);
+  m.def("attention_bwd", &attention_bwd, py::arg("qkv"), py::arg("k_col"), py::arg("v_col"), py::arg("out"),
+        py::arg("dout"), py::arg("lse"), py::arg("delta"), py::arg("dq_acc"), py::arg("dqkv"), py::arg("cos"),
+        py::arg("sin"), py::arg("batch"), py::arg("seq"), py::arg("heads"), py::arg("kv_heads"), py::arg("head_dim"),
+        py::arg("scale"), py::arg("rezero_dq_acc") = false);
   m.def("launch_count", &launch_count);
   m.def("read_device_errors", &read_device_errors);
   m.def("reset_device_errors", &reset_device_errors);

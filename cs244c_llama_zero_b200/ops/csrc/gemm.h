@@ -48,6 +48,12 @@ struct GemmParams {
   DeviceErrors* errs;
 };
 
+struct GemmTile {
+  int bn, splits;
+};
+// Tile width (128 / 192 / 256) and K-split minimising the modelled time on `sms` persistent CTAs.
+GemmTile choose_gemm_tile(int M, int N, int K, int epi, int head_dim, bool allow_split, int sms);
+
 int num_sms();
 // Generic 2D tiled tensor map (dims {inner, outer}, row stride in elements); throws on misaligned
 // base or stride.

@@ -51,8 +51,8 @@ template <int BN>
 struct GemmCfg {
   static constexpr int B_STAGE_BYTES = BN * BK * 2;
   static constexpr int STAGE_BYTES = A_STAGE_BYTES + B_STAGE_BYTES;
-  static constexpr int STAGES = (BN == 256) ? 4 : 6;
-  static constexpr int TMEM_COLS = 2 * BN;
+  static constexpr int STAGES = (BN == 128) ? 6 : 4;
+  static constexpr int TMEM_COLS = (BN == 128) ? 256 : 512;  // power of two >= 2 * BN
   static constexpr int STAGING_BYTES = kEpiWarps * 2 * kChunkBytes;
   static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + STAGING_BYTES + 1024 /*align*/ + 512 /*barriers*/;
   static_assert(SMEM_BYTES <= 232448, "GEMM shared memory exceeds the 227 KB per-block limit");
@@ -571,16 +571,62 @@ static void launch_impl(const GemmOperands& op, GemmParams p, cudaStream_t strea
   count_launch();
 }
 
+// Tile widths each epilogue supports: ROPE needs whole heads per epilogue warpgroup half and SWIGLU
+// 32-column chunks of gate and up per half, so neither takes 192.
+constexpr bool epi_supports_bn(int epi, int bn) {
+  return bn == 128 || bn == 256 || (bn == 192 && epi != EPI_ROPE && epi != EPI_SWIGLU);
+}
+
 template <bool A_MN, bool B_MN, int EPI>
 static void dispatch_bn(int bn, const GemmOperands& op, const GemmParams& p, cudaStream_t stream) {
   if (bn == 256)
     launch_impl<256, A_MN, B_MN, EPI>(op, p, stream);
-  else
+  else if (bn == 192) {
+    if constexpr (epi_supports_bn(EPI, 192)) launch_impl<192, A_MN, B_MN, EPI>(op, p, stream);
+  } else
     launch_impl<128, A_MN, B_MN, EPI>(op, p, stream);
 }
 
+// Tile width and K-split for a persistent grid of `sms` CTAs.  Cost of one work unit = its k-blocks
+// times the time of one k-block, which is the larger of the MMA time (2*BN clocks for 128 x BN x 64)
+// and the operand feed time ((128 + BN) * 128 bytes at ~110 B/clock from L2), plus a pipeline fill of
+// two k-blocks; units run in ceil(units / sms) rounds and the last epilogue is exposed.
+GemmTile choose_gemm_tile(int M, int N, int K, int epi, int head_dim, bool allow_split, int sms) {
+  const int kb = (K + BK - 1) / BK;
+  const double epi_cost = (epi == EPI_SWIGLU || epi == EPI_SWIGLU_BWD || epi == EPI_ROPE) ? 24.0 : 8.0;
+  GemmTile best{256, 1};
+  double best_cost = 1e30;
+  for (int bn : {256, 192, 128}) {
+    if (!epi_supports_bn(epi, bn)) continue;
+    if (epi == EPI_ROPE && ((bn / 2) % head_dim) != 0) continue;
+    const int out_cols = (epi == EPI_SWIGLU) ? bn / 2 : bn;
+    const long tiles = (long)((M + BM - 1) / BM) * ((N + out_cols - 1) / out_cols);
+    const double t_kb = std::max(2.0 * bn, (16384.0 + 128.0 * bn) / 110.0);
+    const int max_split = allow_split ? std::max(1, std::min(32, kb / 4)) : 1;
+    for (int s = 1; s <= max_split; ++s) {
+      const int kbs = (kb + s - 1) / s;
+      const long units = tiles * ((kb + kbs - 1) / kbs);
+      const long rounds = (units + sms - 1) / sms;
+      const double cost = rounds * (kbs + 2.0) * t_kb + epi_cost * bn + (s > 1 ? 4.0 * bn : 0.0);
+      if (cost < best_cost * 0.97) {
+        best_cost = cost;
+        best = {bn, s};
+      }
+    }
+  }
+  return best;
+}
+
 void gemm_launch(const GemmOperands& op, GemmParams p, int epi, bool a_mn, bool b_mn, int bn, cudaStream_t stream) {
-  B200_CHECK(bn == 128 || bn == 256, "BN must be 128 or 256");
+  if (bn <= 0) {  // automatic tile width (and K-split for the fp32-accumulating epilogue)
+    const GemmTile t = choose_gemm_tile(p.M, p.N, p.K, epi, p.head_dim > 0 ? p.head_dim : 64,
+                                        epi == EPI_ACC_F32 && p.splits <= 0, num_sms());
+    bn = t.bn;
+    if (epi == EPI_ACC_F32 && p.splits <= 0) p.splits = t.splits;
+  }
+  if (p.splits <= 0) p.splits = 1;
+  B200_CHECK(bn == 128 || bn == 192 || bn == 256, "BN must be 128, 192 or 256");
+  B200_CHECK(epi_supports_bn(epi, bn), "this epilogue does not support BN = 192");
   B200_CHECK(p.N % 8 == 0, "GEMM output width N must be a multiple of 8");
   B200_CHECK((a_mn || p.K % 8 == 0) && (b_mn || p.K % 8 == 0), "GEMM K must be a multiple of 8 for K-major operands");
   B200_CHECK(!a_mn || p.M % 8 == 0, "GEMM M must be a multiple of 8 for an MN-major A operand");

@@ -51,7 +51,8 @@ struct AttnBwdParams {
   int ld_out;
   const float* lse;           // [B, H, S]
   float* delta;               // [B, H, S] scratch: rowsum(dO * O)
-  float* dq_acc;              // [B*S, H*hd] fp32 scratch (zeroed by the launcher)
+  float* dq_acc;              // [B*S, H*hd] fp32 scratch, all zero on entry
+  bool rezero_dq_acc;         // leave dq_acc zeroed on exit (the caller keeps one zeroed buffer)
   __nv_bfloat16* dqkv;        // [B*S, ld] gradient of the fused qkv matrix (pre-RoPE q and k)
   const float* rope_cos;      // [seq, head_dim/2]: RoPE backward is applied to dq and dk
   const float* rope_sin;

@@ -173,15 +173,31 @@ def attention_forward(qkv: torch.Tensor, batch: int, seq: int, heads: int, kv_he
     return out, lse
 
 
+_DQ_ACC: Dict[Tuple[int, int], torch.Tensor] = {}
+
+
+def _zeroed_dq_accumulator(numel: int, device: torch.device) -> torch.Tensor:
+    """One fp32 dQ accumulator per (device, size), zeroed once: the backward's dQ conversion kernel
+    writes it back to zero after reading it, so no per-call fill is needed.  Backwards run one at a
+    time on a device's stream, which is what makes the sharing safe."""
+    key = (device.index if device.index is not None else torch.cuda.current_device(), numel)
+    buf = _DQ_ACC.get(key)
+    if buf is None:
+        buf = torch.zeros(numel, dtype=torch.float32, device=device)
+        _DQ_ACC[key] = buf
+    return buf
+
+
 def attention_backward(qkv: torch.Tensor, out: torch.Tensor, dout: torch.Tensor, lse: torch.Tensor, batch: int,
                        seq: int, heads: int, kv_heads: int, head_dim: int, dqkv: torch.Tensor,
                        cos: torch.Tensor, sin: torch.Tensor) -> None:
     """dqkv = gradient w.r.t. the *pre-RoPE* q|k|v projection (RoPE backward is fused)."""
     T = batch * seq
     delta = torch.empty(batch * heads * seq, dtype=torch.float32, device=qkv.device)
-    dq_acc = torch.zeros(T, heads * head_dim, dtype=torch.float32, device=qkv.device)
+    dq_acc = _zeroed_dq_accumulator(T * heads * head_dim, qkv.device)
     _ext().attention_bwd(qkv, heads * head_dim, (heads + kv_heads) * head_dim, out, dout.contiguous(), lse, delta,
-                         dq_acc, dqkv, cos, sin, batch, seq, heads, kv_heads, head_dim, 1.0 / math.sqrt(head_dim))
+                         dq_acc, dqkv, cos, sin, batch, seq, heads, kv_heads, head_dim, 1.0 / math.sqrt(head_dim),
+                         True)
 
 
 # ------------------------------------------------------------------------------ transformer block

@@ -34,7 +34,7 @@ def _close(a, b, tol):
 
 
 @pytest.mark.parametrize("M,N,K,bn", [(256, 512, 128, 256), (300, 264, 136, 128), (1024, 1280, 768, 256),
-                                      (128, 768, 2048, 256)])
+                                      (128, 768, 2048, 256), (520, 776, 264, 192), (1024, 768, 768, 0)])
 def test_linear_fwd(C, M, N, K, bn):
     x, w = _bf(M, K, seed=1), _bf(N, K, scale=0.05, seed=2)
     out = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
@@ -45,19 +45,21 @@ def test_linear_fwd(C, M, N, K, bn):
     _close(out, res.float() + x.float() @ w.float().t(), 2e-2)
 
 
-@pytest.mark.parametrize("M,N,K", [(256, 768, 512), (200, 136, 264), (1024, 768, 2048)])
-def test_linear_dgrad(C, M, N, K):
+@pytest.mark.parametrize("M,N,K,bn", [(256, 768, 512, 0), (200, 136, 264, 0), (1024, 768, 2048, 0),
+                                      (384, 512, 776, 192), (256, 640, 384, 128)])
+def test_linear_dgrad(C, M, N, K, bn):
     dy, w = _bf(M, N, seed=4), _bf(N, K, scale=0.05, seed=5)
     dx = torch.empty(M, K, device="cuda", dtype=torch.bfloat16)
-    C.linear_dgrad(dy, w, dx, 0)
+    C.linear_dgrad(dy, w, dx, bn)
     _close(dx, dy.float() @ w.float(), 2e-2)
 
 
-@pytest.mark.parametrize("M,N,K,splits", [(512, 384, 256, 1), (1024, 768, 1280, 4), (300, 136, 200, 0)])
-def test_linear_wgrad_accumulates(C, M, N, K, splits):
+@pytest.mark.parametrize("M,N,K,splits,bn", [(512, 384, 256, 1, 0), (1024, 768, 1280, 4, 0), (300, 136, 200, 0, 0),
+                                             (4096, 1280, 768, 0, 0), (1024, 384, 776, 3, 192)])
+def test_linear_wgrad_accumulates(C, M, N, K, splits, bn):
     dy, x = _bf(M, N, seed=6), _bf(M, K, seed=7)
     dw = torch.ones(N, K, device="cuda", dtype=torch.float32)
-    C.linear_wgrad(dy, x, dw, splits, 0)
+    C.linear_wgrad(dy, x, dw, splits, bn)
     _close(dw, 1.0 + dy.float().t() @ x.float(), 1e-2)
 
 
