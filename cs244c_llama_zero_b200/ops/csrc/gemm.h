@@ -49,10 +49,12 @@ struct GemmParams {
 };
 
 struct GemmTile {
-  int bn, splits;
+  int bn, splits, cg;
 };
-// Tile width (128 / 192 / 256) and K-split minimising the modelled time on `sms` persistent CTAs.
-GemmTile choose_gemm_tile(int M, int N, int K, int epi, int head_dim, bool allow_split, int sms);
+// Tile width (128 / 192 / 256), CTA group (1 or a pair) and K-split minimising the modelled time.
+// only_bn / only_cg > 0 restrict the search to that tile width / CTA group.
+GemmTile choose_gemm_tile(int M, int N, int K, int epi, int head_dim, bool allow_split, bool b_mn, int sms,
+                          int only_bn = 0, int only_cg = 0);
 
 int num_sms();
 // Generic 2D tiled tensor map (dims {inner, outer}, row stride in elements); throws on misaligned

@@ -47,11 +47,13 @@ constexpr int NUM_THREADS = 320;
 constexpr int kEpiWarps = 8;
 constexpr int kChunkBytes = 2048;  // epilogue staging chunk: 32 rows x 64 B (32 bf16 or 16 fp32 columns)
 
-template <int BN>
+// CG = 1: one CTA computes a 128 x BN tile.  CG = 2: a CTA pair (cluster of 2) computes a 256 x BN
+// tile with cta_group::2 MMAs; each CTA stages its own 128 rows of A and half (BN / 2 rows) of B.
+template <int BN, int CG = 1>
 struct GemmCfg {
-  static constexpr int B_STAGE_BYTES = BN * BK * 2;
+  static constexpr int B_STAGE_BYTES = (BN / CG) * BK * 2;
   static constexpr int STAGE_BYTES = A_STAGE_BYTES + B_STAGE_BYTES;
-  static constexpr int STAGES = (BN == 128) ? 6 : 4;
+  static constexpr int STAGES = (CG == 2 || BN == 128) ? 6 : 4;
   static constexpr int TMEM_COLS = (BN == 128) ? 256 : 512;  // power of two >= 2 * BN
   static constexpr int STAGING_BYTES = kEpiWarps * 2 * kChunkBytes;
   static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + STAGING_BYTES + 1024 /*align*/ + 512 /*barriers*/;
@@ -105,14 +107,16 @@ __device__ __forceinline__ void publish_chunk(const CUtensorMap* map, uint8_t* b
   }
 }
 
-template <int BN, bool A_MN, bool B_MN, int EPI>
+template <int BN, bool A_MN, bool B_MN, int EPI, int CG>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                 const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmX,
                 const __grid_constant__ CUtensorMap tmY, GemmParams p) {
-  using Cfg = GemmCfg<BN>;
+  using Cfg = GemmCfg<BN, CG>;
   constexpr int STAGES = Cfg::STAGES;
-  constexpr uint32_t IDESC = idesc_bf16_f32(BM, BN, A_MN, B_MN);
+  constexpr uint32_t IDESC = idesc_bf16_f32(BM * CG, BN, A_MN, B_MN);
+  static_assert(CG == 1 || CG == 2, "CTA group of 1 or 2");
+  static_assert(CG == 1 || !B_MN || (BN / 2) % 64 == 0, "pair tiles with an MN-major B need BN/2 % 64 == 0");
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -126,6 +130,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  // Pair bookkeeping: `rank` 0 is the leader that issues the MMAs; units are dealt per pair.
+  const int rank = (CG == 2) ? (int)cluster_ctarank() : 0;
+  const int group_id = blockIdx.x / CG, n_groups = gridDim.x / CG;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -134,18 +141,24 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull_bar[a], 1);
-      mbar_init(&tempty_bar[a], kEpiWarps);
+      mbar_init(&tempty_bar[a], kEpiWarps * CG);  // both CTAs' epilogue warps release the pair accumulator
     }
     for (int b = 0; b < 2 * kEpiWarps; ++b) mbar_init(&load_bar[b], 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
   if (warp == 1) {
-    tmem_alloc(tmem_base_slot, Cfg::TMEM_COLS);
-    tmem_relinquish();
+    if constexpr (CG == 2) {
+      tmem_alloc_pair(tmem_base_slot, Cfg::TMEM_COLS);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(tmem_base_slot, Cfg::TMEM_COLS);
+      tmem_relinquish();
+    }
   }
   tc_fence_before();
   __syncthreads();
+  if constexpr (CG == 2) cluster_sync();  // the peer's barriers are initialised before any remote arrive
   tc_fence_after();
   const uint32_t tmem_base = *tmem_base_slot;
 
@@ -158,11 +171,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
-      for (int u = blockIdx.x; u < total_units && ok; u += gridDim.x) {
+      for (int u = group_id; u < total_units && ok; u += n_groups) {
         const int split = u % p.splits;
         const int tile = u / p.splits;
         const int tm = tile % p.tiles_m, tn = tile / p.tiles_m;
-        const int m0 = tm * BM;
+        const int m0 = tm * BM * CG + rank * BM;
         const int kb0 = split * p.k_blocks_per_split;
         const int kb1 = min(p.total_k_blocks, kb0 + p.k_blocks_per_split);
         for (int kb = kb0; kb < kb1; ++kb) {
@@ -172,23 +185,35 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           }
           uint8_t* sA = smem + stage * Cfg::STAGE_BYTES;
           uint8_t* sB = sA + A_STAGE_BYTES;
-          mbar_expect_tx(&full_bar[stage], Cfg::STAGE_BYTES);
           const int k0 = kb * BK;
+          // All of a stage's bytes (both CTAs of a pair) count on the leader's full barrier.
+          if (rank == 0) mbar_expect_tx(&full_bar[stage], Cfg::STAGE_BYTES * CG);
+          const uint32_t fb = (CG == 2) ? leader_bar_addr(&full_bar[stage]) : 0u;
+          auto load = [&](void* dst, const CUtensorMap* map, int c0, int c1) {
+            if constexpr (CG == 2)
+              tma_load_2d_pair(dst, map, fb, c0, c1);
+            else
+              tma_load_2d(dst, map, &full_bar[stage], c0, c1);
+          };
           if constexpr (!A_MN) {
-            tma_load_2d(sA, &tmA, &full_bar[stage], k0, m0);
+            load(sA, &tmA, k0, m0);
           } else {
-            tma_load_2d(sA, &tmA, &full_bar[stage], m0, k0);
-            tma_load_2d(sA + 8192, &tmA, &full_bar[stage], m0 + 64, k0);
+            load(sA, &tmA, m0, k0);
+            load(sA + 8192, &tmA, m0 + 64, k0);
           }
           if constexpr (EPI == EPI_SWIGLU) {
             const int g0 = tn * (BN / 2);
-            tma_load_2d(sB, &tmB, &full_bar[stage], k0, g0);
-            tma_load_2d(sB + (BN / 2) * 128, &tmB, &full_bar[stage], k0, p.ffn + g0);
+            if constexpr (CG == 2) {
+              load(sB, &tmB, k0, rank == 0 ? g0 : p.ffn + g0);  // leader: gate rows, peer: up rows
+            } else {
+              load(sB, &tmB, k0, g0);
+              load(sB + (BN / 2) * 128, &tmB, k0, p.ffn + g0);
+            }
           } else if constexpr (!B_MN) {
-            tma_load_2d(sB, &tmB, &full_bar[stage], k0, tn * BN);
+            load(sB, &tmB, k0, tn * BN + rank * (BN / CG));
           } else {
 #pragma unroll
-            for (int j = 0; j < BN / 64; ++j) tma_load_2d(sB + j * 8192, &tmB, &full_bar[stage], tn * BN + 64 * j, k0);
+            for (int j = 0; j < BN / CG / 64; ++j) load(sB + j * 8192, &tmB, tn * BN + rank * (BN / CG) + 64 * j, k0);
           }
           if (++stage == STAGES) {
             stage = 0;
@@ -198,12 +223,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       }
     }
   } else if (warp == 1) {
-    if (lane == 0) {
+    if (lane == 0 && rank == 0) {
       int stage = 0;
       uint32_t phase = 0;
       int t = 0;
       bool ok = true;
-      for (int u = blockIdx.x; u < total_units && ok; u += gridDim.x, ++t) {
+      for (int u = group_id; u < total_units && ok; u += n_groups, ++t) {
         const int split = u % p.splits;
         const int kb0 = split * p.k_blocks_per_split;
         const int kb1 = min(p.total_k_blocks, kb0 + p.k_blocks_per_split);
@@ -226,16 +251,25 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                                         : smem_desc_sw128(a_addr + k * 32, 16, 1024);
             const uint64_t bdesc = B_MN ? smem_desc_sw128(b_addr + k * 2048, 8192, 1024)
                                         : smem_desc_sw128(b_addr + k * 32, 16, 1024);
-            tc_mma_f16(d_tmem, adesc, bdesc, IDESC, (kb > kb0 || k > 0) ? 1u : 0u);
+            if constexpr (CG == 2)
+              tc_mma_f16_pair(d_tmem, adesc, bdesc, IDESC, (kb > kb0 || k > 0) ? 1u : 0u);
+            else
+              tc_mma_f16(d_tmem, adesc, bdesc, IDESC, (kb > kb0 || k > 0) ? 1u : 0u);
           }
-          tc_commit(&empty_bar[stage]);
+          if constexpr (CG == 2)
+            tc_commit_pair(&empty_bar[stage], 0x3);  // frees the stage in both CTAs
+          else
+            tc_commit(&empty_bar[stage]);
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1u;
           }
         }
         if (!ok) break;
-        tc_commit(&tfull_bar[acc]);
+        if constexpr (CG == 2)
+          tc_commit_pair(&tfull_bar[acc], 0x3);
+        else
+          tc_commit(&tfull_bar[acc]);
       }
     }
   } else {
@@ -253,12 +287,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     int bsel = 0;
     int t = 0;
     bool ok = true;
-    for (int u = blockIdx.x; u < total_units && ok; u += gridDim.x, ++t) {
+    for (int u = group_id; u < total_units && ok; u += n_groups, ++t) {
       const int tile = u / p.splits;
       const int tm = tile % p.tiles_m, tn = tile / p.tiles_m;
       const int acc = t & 1;
       const uint32_t acc_phase = (t >> 1) & 1;
-      const int row0 = tm * BM + q * 32;  // TMA row coordinate of this warp's chunk
+      const int row0 = tm * BM * CG + rank * BM + q * 32;  // TMA row coordinate of this warp's chunk
       const int m = row0 + lane;
       const bool row_ok = m < p.M;
 
@@ -444,7 +478,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&tempty_bar[acc]);
+      if (lane == 0) {
+        if constexpr (CG == 2)
+          mbar_arrive_cluster(&tempty_bar[acc], 0);  // the leader's MMA owns the pair accumulator
+        else
+          mbar_arrive(&tempty_bar[acc]);
+      }
     }
     // Every staged chunk must have landed before the CTA's shared memory goes away.
     if (lane == 0) bulk_wait_group<0>();
@@ -453,9 +492,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 
   tc_fence_before();
   __syncthreads();
+  if constexpr (CG == 2) cluster_sync();  // no remote arrive or pair MMA may target a departed peer
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, Cfg::TMEM_COLS);
+    if constexpr (CG == 2)
+      tmem_dealloc_pair(tmem_base, Cfg::TMEM_COLS);
+    else
+      tmem_dealloc(tmem_base, Cfg::TMEM_COLS);
   }
 }
 
@@ -520,10 +563,10 @@ int num_sms() {
   return n;
 }
 
-template <int BN, bool A_MN, bool B_MN, int EPI>
+template <int BN, bool A_MN, bool B_MN, int EPI, int CG>
 static void launch_impl(const GemmOperands& op, GemmParams p, cudaStream_t stream) {
-  using Cfg = GemmCfg<BN>;
-  auto kernel = gemm_kernel<BN, A_MN, B_MN, EPI>;
+  using Cfg = GemmCfg<BN, CG>;
+  auto kernel = gemm_kernel<BN, A_MN, B_MN, EPI, CG>;
   static bool configured = false;
   if (!configured) {
     B200_CUDA_CHECK(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_BYTES));
@@ -538,7 +581,7 @@ static void launch_impl(const GemmOperands& op, GemmParams p, cudaStream_t strea
   } else if (B_MN) {
     tmB = make_tmap_bf16_2d(op.B, (uint64_t)p.N, (uint64_t)p.K, op.ldb, 64, 64);
   } else {
-    tmB = make_tmap_bf16_2d(op.B, (uint64_t)p.K, (uint64_t)p.N, op.ldb, 64, BN);
+    tmB = make_tmap_bf16_2d(op.B, (uint64_t)p.K, (uint64_t)p.N, op.ldb, 64, BN / CG);
   }
   // Output side.  Maps that an epilogue does not use repeat tmA (never dereferenced).
   CUtensorMap tmC = tmA, tmX = tmA, tmY = tmA;
@@ -556,7 +599,7 @@ static void launch_impl(const GemmOperands& op, GemmParams p, cudaStream_t strea
     if (EPI == EPI_RESIDUAL) tmX = epi_map_bf16(p.R, p.M, p.N, p.ldr);
   }
   const int out_cols_per_tile = (EPI == EPI_SWIGLU) ? BN / 2 : BN;
-  p.tiles_m = (p.M + BM - 1) / BM;
+  p.tiles_m = (p.M + BM * CG - 1) / (BM * CG);
   p.tiles_n = (p.N + out_cols_per_tile - 1) / out_cols_per_tile;
   p.total_k_blocks = (p.K + BK - 1) / BK;
   if (p.splits < 1) p.splits = 1;
@@ -565,8 +608,24 @@ static void launch_impl(const GemmOperands& op, GemmParams p, cudaStream_t strea
   p.splits = (p.total_k_blocks + p.k_blocks_per_split - 1) / p.k_blocks_per_split;
   p.errs = device_errors_ptr();
   const int units = p.tiles_m * p.tiles_n * p.splits;
-  const int grid = std::max(1, std::min(units, num_sms()));
-  kernel<<<grid, NUM_THREADS, Cfg::SMEM_BYTES, stream>>>(tmA, tmB, tmC, tmX, tmY, p);
+  const int groups = std::max(1, std::min(units, num_sms() / CG));
+  if constexpr (CG == 1) {
+    kernel<<<groups, NUM_THREADS, Cfg::SMEM_BYTES, stream>>>(tmA, tmB, tmC, tmX, tmY, p);
+  } else {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(groups * CG, 1, 1);
+    cfg.blockDim = dim3(NUM_THREADS, 1, 1);
+    cfg.dynamicSmemBytes = Cfg::SMEM_BYTES;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = CG;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    B200_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kernel, tmA, tmB, tmC, tmX, tmY, p));
+  }
   B200_CUDA_CHECK(cudaGetLastError());
   count_launch();
 }
@@ -577,40 +636,67 @@ constexpr bool epi_supports_bn(int epi, int bn) {
   return bn == 128 || bn == 256 || (bn == 192 && epi != EPI_ROPE && epi != EPI_SWIGLU);
 }
 
-template <bool A_MN, bool B_MN, int EPI>
-static void dispatch_bn(int bn, const GemmOperands& op, const GemmParams& p, cudaStream_t stream) {
+// CTA pairs with an MN-major B split B into halves of whole 64-column TMA boxes.
+constexpr bool pair_supports(bool b_mn, int bn) { return !b_mn || (bn / 2) % 64 == 0; }
+
+template <int CG, bool A_MN, bool B_MN, int EPI>
+static void dispatch_bn_cg(int bn, const GemmOperands& op, const GemmParams& p, cudaStream_t stream) {
   if (bn == 256)
-    launch_impl<256, A_MN, B_MN, EPI>(op, p, stream);
+    launch_impl<256, A_MN, B_MN, EPI, CG>(op, p, stream);
   else if (bn == 192) {
-    if constexpr (epi_supports_bn(EPI, 192)) launch_impl<192, A_MN, B_MN, EPI>(op, p, stream);
+    if constexpr (epi_supports_bn(EPI, 192) && (CG == 1 || pair_supports(B_MN, 192)))
+      launch_impl<192, A_MN, B_MN, EPI, CG>(op, p, stream);
+    else
+      B200_CHECK(false, "BN = 192 is not available for this epilogue / operand layout / CTA group");
   } else
-    launch_impl<128, A_MN, B_MN, EPI>(op, p, stream);
+    launch_impl<128, A_MN, B_MN, EPI, CG>(op, p, stream);
 }
 
-// Tile width and K-split for a persistent grid of `sms` CTAs.  Cost of one work unit = its k-blocks
-// times the time of one k-block, which is the larger of the MMA time (2*BN clocks for 128 x BN x 64)
-// and the operand feed time ((128 + BN) * 128 bytes at ~110 B/clock from L2), plus a pipeline fill of
-// two k-blocks; units run in ceil(units / sms) rounds and the last epilogue is exposed.
-GemmTile choose_gemm_tile(int M, int N, int K, int epi, int head_dim, bool allow_split, int sms) {
+template <bool A_MN, bool B_MN, int EPI>
+static void dispatch_bn(int bn, int cg, const GemmOperands& op, const GemmParams& p, cudaStream_t stream) {
+  if (cg == 2)
+    dispatch_bn_cg<2, A_MN, B_MN, EPI>(bn, op, p, stream);
+  else
+    dispatch_bn_cg<1, A_MN, B_MN, EPI>(bn, op, p, stream);
+}
+
+// Tile width, CTA group and K-split for a persistent grid on `sms` SMs.  A work unit runs in rounds of
+// sms / CG concurrent units; its time is (k-blocks + 3 for the pipeline fill) x the per-SM time of one
+// 64-deep k-block, measured on B200 for each variant (microseconds; the bigger the per-SM tile, the
+// better the time per FLOP, pairs better than single CTAs), plus the exposed last epilogue.
+GemmTile choose_gemm_tile(int M, int N, int K, int epi, int head_dim, bool allow_split, bool b_mn, int sms,
+                          int only_bn, int only_cg) {
+  struct Variant {
+    int cg, bn;
+    double us_per_kblock;
+  };
+  static const Variant kVariants[] = {{2, 256, 0.418}, {2, 192, 0.400}, {1, 256, 0.465},
+                                      {1, 192, 0.450}, {2, 128, 0.362}, {1, 128, 0.350}};
   const int kb = (K + BK - 1) / BK;
-  const double epi_cost = (epi == EPI_SWIGLU || epi == EPI_SWIGLU_BWD || epi == EPI_ROPE) ? 24.0 : 8.0;
-  GemmTile best{256, 1};
+  const bool heavy = (epi == EPI_SWIGLU || epi == EPI_SWIGLU_BWD || epi == EPI_ROPE);
+  GemmTile best{256, 1, 1};
   double best_cost = 1e30;
-  for (int bn : {256, 192, 128}) {
-    if (!epi_supports_bn(epi, bn)) continue;
-    if (epi == EPI_ROPE && ((bn / 2) % head_dim) != 0) continue;
-    const int out_cols = (epi == EPI_SWIGLU) ? bn / 2 : bn;
-    const long tiles = (long)((M + BM - 1) / BM) * ((N + out_cols - 1) / out_cols);
-    const double t_kb = std::max(2.0 * bn, (16384.0 + 128.0 * bn) / 110.0);
+  for (const Variant& v : kVariants) {
+    if (!epi_supports_bn(epi, v.bn) || (v.cg == 2 && !pair_supports(b_mn, v.bn))) continue;
+    if ((only_bn > 0 && v.bn != only_bn) || (only_cg > 0 && v.cg != only_cg)) continue;
+    // Measured in the model's step: epilogues that read or write several tiles per output tile
+    // (residual, SwiGLU forward / backward) ran slower as pairs, whose two CTAs release the shared
+    // accumulator together.
+    if (only_cg == 0 && v.cg == 2 && (epi == EPI_RESIDUAL || epi == EPI_SWIGLU || epi == EPI_SWIGLU_BWD)) continue;
+    if (epi == EPI_ROPE && ((v.bn / 2) % head_dim) != 0) continue;
+    const int out_cols = (epi == EPI_SWIGLU) ? v.bn / 2 : v.bn;
+    const long tiles = (long)((M + BM * v.cg - 1) / (BM * v.cg)) * ((N + out_cols - 1) / out_cols);
     const int max_split = allow_split ? std::max(1, std::min(32, kb / 4)) : 1;
+    const int slots = std::max(1, sms / v.cg);
+    const double epi_us = (heavy ? 3.0 : 0.5) * v.bn / 256.0;
     for (int s = 1; s <= max_split; ++s) {
       const int kbs = (kb + s - 1) / s;
       const long units = tiles * ((kb + kbs - 1) / kbs);
-      const long rounds = (units + sms - 1) / sms;
-      const double cost = rounds * (kbs + 2.0) * t_kb + epi_cost * bn + (s > 1 ? 4.0 * bn : 0.0);
-      if (cost < best_cost * 0.97) {
+      const long rounds = (units + slots - 1) / slots;
+      const double cost = rounds * (kbs + 3.0) * v.us_per_kblock + epi_us;
+      if (cost < best_cost * 0.98) {
         best_cost = cost;
-        best = {bn, s};
+        best = {v.bn, s, v.cg};
       }
     }
   }
@@ -618,11 +704,21 @@ GemmTile choose_gemm_tile(int M, int N, int K, int epi, int head_dim, bool allow
 }
 
 void gemm_launch(const GemmOperands& op, GemmParams p, int epi, bool a_mn, bool b_mn, int bn, cudaStream_t stream) {
-  if (bn <= 0) {  // automatic tile width (and K-split for the fp32-accumulating epilogue)
+  int cg = 1;
+  if (bn <= 0) {  // automatic tile width, CTA group (and K-split for the fp32-accumulating epilogue)
     const GemmTile t = choose_gemm_tile(p.M, p.N, p.K, epi, p.head_dim > 0 ? p.head_dim : 64,
-                                        epi == EPI_ACC_F32 && p.splits <= 0, num_sms());
+                                        epi == EPI_ACC_F32 && p.splits <= 0, b_mn, num_sms(), 0, 0);
     bn = t.bn;
+    cg = t.cg;
     if (epi == EPI_ACC_F32 && p.splits <= 0) p.splits = t.splits;
+  } else {
+    if (bn >= 1000) {  // explicit CTA-pair request (tests, benchmarks): 1000 + tile width
+      bn -= 1000;
+      cg = 2;
+      B200_CHECK(pair_supports(b_mn, bn), "CTA pairs with an MN-major B need BN / 2 to be a multiple of 64");
+    }
+    if (epi == EPI_ACC_F32 && p.splits <= 0)  // explicit tile, automatic K-split
+      p.splits = choose_gemm_tile(p.M, p.N, p.K, epi, 64, true, b_mn, num_sms(), bn, cg).splits;
   }
   if (p.splits <= 0) p.splits = 1;
   B200_CHECK(bn == 128 || bn == 192 || bn == 256, "BN must be 128, 192 or 256");
@@ -632,22 +728,22 @@ void gemm_launch(const GemmOperands& op, GemmParams p, int epi, bool a_mn, bool 
   B200_CHECK(!a_mn || p.M % 8 == 0, "GEMM M must be a multiple of 8 for an MN-major A operand");
   if (!a_mn && !b_mn) {
     switch (epi) {
-      case EPI_STORE: return dispatch_bn<false, false, EPI_STORE>(bn, op, p, stream);
-      case EPI_RESIDUAL: return dispatch_bn<false, false, EPI_RESIDUAL>(bn, op, p, stream);
-      case EPI_ROPE: return dispatch_bn<false, false, EPI_ROPE>(bn, op, p, stream);
-      case EPI_SWIGLU: return dispatch_bn<false, false, EPI_SWIGLU>(bn, op, p, stream);
-      case EPI_ACC_F32: return dispatch_bn<false, false, EPI_ACC_F32>(bn, op, p, stream);
+      case EPI_STORE: return dispatch_bn<false, false, EPI_STORE>(bn, cg, op, p, stream);
+      case EPI_RESIDUAL: return dispatch_bn<false, false, EPI_RESIDUAL>(bn, cg, op, p, stream);
+      case EPI_ROPE: return dispatch_bn<false, false, EPI_ROPE>(bn, cg, op, p, stream);
+      case EPI_SWIGLU: return dispatch_bn<false, false, EPI_SWIGLU>(bn, cg, op, p, stream);
+      case EPI_ACC_F32: return dispatch_bn<false, false, EPI_ACC_F32>(bn, cg, op, p, stream);
     }
   } else if (!a_mn && b_mn) {
     switch (epi) {
-      case EPI_STORE: return dispatch_bn<false, true, EPI_STORE>(bn, op, p, stream);
-      case EPI_SWIGLU_BWD: return dispatch_bn<false, true, EPI_SWIGLU_BWD>(bn, op, p, stream);
-      case EPI_ACC_F32: return dispatch_bn<false, true, EPI_ACC_F32>(bn, op, p, stream);
+      case EPI_STORE: return dispatch_bn<false, true, EPI_STORE>(bn, cg, op, p, stream);
+      case EPI_SWIGLU_BWD: return dispatch_bn<false, true, EPI_SWIGLU_BWD>(bn, cg, op, p, stream);
+      case EPI_ACC_F32: return dispatch_bn<false, true, EPI_ACC_F32>(bn, cg, op, p, stream);
     }
   } else if (a_mn && b_mn) {
     switch (epi) {
-      case EPI_ACC_F32: return dispatch_bn<true, true, EPI_ACC_F32>(bn, op, p, stream);
-      case EPI_STORE: return dispatch_bn<true, true, EPI_STORE>(bn, op, p, stream);
+      case EPI_ACC_F32: return dispatch_bn<true, true, EPI_ACC_F32>(bn, cg, op, p, stream);
+      case EPI_STORE: return dispatch_bn<true, true, EPI_STORE>(bn, cg, op, p, stream);
     }
   }
   B200_CHECK(false, "unsupported GEMM operand-major / epilogue combination");

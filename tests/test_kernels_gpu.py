@@ -34,8 +34,10 @@ def _close(a, b, tol):
 
 
 @pytest.mark.parametrize("M,N,K,bn", [(256, 512, 128, 256), (300, 264, 136, 128), (1024, 1280, 768, 256),
-                                      (128, 768, 2048, 256), (520, 776, 264, 192), (1024, 768, 768, 0)])
+                                      (128, 768, 2048, 256), (520, 776, 264, 192), (1024, 768, 768, 0),
+                                      (512, 512, 256, 1256), (600, 392, 200, 1128), (384, 776, 264, 1192)])
 def test_linear_fwd(C, M, N, K, bn):
+    """bn >= 1000 requests a CTA-pair (cta_group::2) tile of width bn - 1000; 0 = automatic choice."""
     x, w = _bf(M, K, seed=1), _bf(N, K, scale=0.05, seed=2)
     out = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
     C.linear_fwd(x, w, out, None, bn)
@@ -46,7 +48,8 @@ def test_linear_fwd(C, M, N, K, bn):
 
 
 @pytest.mark.parametrize("M,N,K,bn", [(256, 768, 512, 0), (200, 136, 264, 0), (1024, 768, 2048, 0),
-                                      (384, 512, 776, 192), (256, 640, 384, 128)])
+                                      (384, 512, 776, 192), (256, 640, 384, 128), (600, 256, 392, 1128),
+                                      (512, 384, 1024, 1256)])
 def test_linear_dgrad(C, M, N, K, bn):
     dy, w = _bf(M, N, seed=4), _bf(N, K, scale=0.05, seed=5)
     dx = torch.empty(M, K, device="cuda", dtype=torch.bfloat16)
@@ -55,7 +58,8 @@ def test_linear_dgrad(C, M, N, K, bn):
 
 
 @pytest.mark.parametrize("M,N,K,splits,bn", [(512, 384, 256, 1, 0), (1024, 768, 1280, 4, 0), (300, 136, 200, 0, 0),
-                                             (4096, 1280, 768, 0, 0), (1024, 384, 776, 3, 192)])
+                                             (4096, 1280, 768, 0, 0), (1024, 384, 776, 3, 192),
+                                             (1024, 640, 512, 2, 1128), (512, 384, 1024, 1, 1256)])
 def test_linear_wgrad_accumulates(C, M, N, K, splits, bn):
     dy, x = _bf(M, N, seed=6), _bf(M, K, seed=7)
     dw = torch.ones(N, K, device="cuda", dtype=torch.float32)
