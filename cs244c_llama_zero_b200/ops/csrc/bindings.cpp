@@ -415,6 +415,14 @@ class CommContext {
     prepare();
     b200::comm_reduce_scatter_acc_f32(c_, off, chunk, acc.data_ptr<float>(), (float)scale, cur_stream());
   }
+  void reduce_scatter_range_acc_f32(int64_t off, int64_t lo, int64_t hi, Tensor acc, double scale, int64_t blocks) {
+    TORCH_CHECK(hi >= lo, "reduce_scatter_range: hi < lo");
+    check_acc(acc, hi - lo);
+    c10::cuda::CUDAGuard g(device_);
+    prepare();
+    b200::comm_reduce_scatter_range_acc_f32(c_, off, lo, hi, acc.data_ptr<float>(), (float)scale, (int)blocks,
+                                            cur_stream());
+  }
   void reduce_scatter_acc_bf16(int64_t off, int64_t chunk, Tensor acc, double scale) {
     check_acc(acc, chunk);
     c10::cuda::CUDAGuard g(device_);
@@ -516,6 +524,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
       .def("allreduce_bf16", &CommContext::allreduce_bf16)
       .def("reduce_scatter_acc_f32", &CommContext::reduce_scatter_acc_f32)
       .def("reduce_scatter_acc_bf16", &CommContext::reduce_scatter_acc_bf16)
+      .def("reduce_scatter_range_acc_f32", &CommContext::reduce_scatter_range_acc_f32)
       .def("allgather", &CommContext::allgather)
       .def("adamw_allgather", &CommContext::adamw_allgather)
       .def("barrier", &CommContext::barrier)

@@ -195,6 +195,47 @@ __global__ void __launch_bounds__(kThreads) reduce_scatter_acc_f32_kernel(CommCt
   block_barrier(c, 2 * e + 1);
 }
 
+// Bucketed variant for reduce-scatter overlapped with backward: the region is one bucket of the
+// flat buffer, and this rank reduces only the part of it that falls inside its own shard
+// ([lo4, hi4) in 16-byte vectors from the region start; possibly empty), accumulating into acc[0..).
+// Every rank still joins both barriers so the per-block epochs stay aligned.
+template <bool MC>
+__global__ void __launch_bounds__(kThreads) reduce_scatter_range_acc_f32_kernel(CommCtx c, size_t off, size_t lo4,
+                                                                                size_t hi4, float4* acc, float scale) {
+  const uint32_t e = next_epoch(c);
+  if (!block_barrier(c, 2 * e)) return;
+  const size_t n4 = hi4 > lo4 ? hi4 - lo4 : 0;
+  const size_t base = off + lo4 * 16;
+  const size_t stride = gstride();
+  for (size_t i0 = gtid(); i0 < n4; i0 += stride * kUnroll) {
+    float4 v[kUnroll];
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+      const size_t i = i0 + u * stride;
+      if (i >= n4) break;
+      const size_t b = base + i * 16;
+      if constexpr (MC) {
+        v[u] = mc_ld_reduce_f32x4(c.mc + b);
+      } else {
+        v[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int w = 0; w < c.world; ++w) {
+          const float4 x = __ldcg(reinterpret_cast<const float4*>(c.peers[w] + b));
+          v[u].x += x.x; v[u].y += x.y; v[u].z += x.z; v[u].w += x.w;
+        }
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+      const size_t i = i0 + u * stride;
+      if (i >= n4) break;
+      float4 a = acc[i];
+      a.x += scale * v[u].x; a.y += scale * v[u].y; a.z += scale * v[u].z; a.w += scale * v[u].w;
+      acc[i] = a;
+    }
+  }
+  block_barrier(c, 2 * e + 1);
+}
+
 // bf16 variants: 16-byte vectors of 8 values; sums accumulate in fp32 (switch-side with multicast,
 // in registers with peer loads) and are rounded once.
 template <bool MC>
@@ -383,6 +424,23 @@ void comm_reduce_scatter_acc_f32(const CommCtx& c, size_t off, size_t chunk, flo
     reduce_scatter_acc_f32_kernel<true><<<c.blocks, kThreads, 0, s>>>(c, off, chunk / 4, a4, scale);
   else
     reduce_scatter_acc_f32_kernel<false><<<c.blocks, kThreads, 0, s>>>(c, off, chunk / 4, a4, scale);
+  B200_CUDA_CHECK(cudaGetLastError());
+  count_launch();
+}
+
+void comm_reduce_scatter_range_acc_f32(const CommCtx& c, size_t off, size_t lo, size_t hi, float* acc, float scale,
+                                       int blocks, cudaStream_t s) {
+  check_ctx(c);
+  // Fewer blocks than the communicator's grid are allowed (every rank must pass the same count):
+  // the blocks left out simply skip this call's epochs on all ranks.
+  const int grid = (blocks > 0 && blocks < c.blocks) ? blocks : c.blocks;
+  B200_CHECK(lo % 4 == 0 && hi % 4 == 0 && off % 16 == 0 && (reinterpret_cast<uintptr_t>(acc) & 15) == 0,
+             "comm_reduce_scatter_range: range ends must be multiples of 4, offset and acc 16-aligned");
+  auto* a4 = reinterpret_cast<float4*>(acc);
+  if (c.mc)
+    reduce_scatter_range_acc_f32_kernel<true><<<grid, kThreads, 0, s>>>(c, off, lo / 4, hi / 4, a4, scale);
+  else
+    reduce_scatter_range_acc_f32_kernel<false><<<grid, kThreads, 0, s>>>(c, off, lo / 4, hi / 4, a4, scale);
   B200_CUDA_CHECK(cudaGetLastError());
   count_launch();
 }

@@ -34,6 +34,11 @@ void comm_allreduce_f32(const CommCtx& c, size_t off_bytes, size_t n, float scal
 // acc[0, chunk) += scale * sum_ranks(region[rank*chunk, (rank+1)*chunk)); fp32 region and acc.
 void comm_reduce_scatter_acc_f32(const CommCtx& c, size_t off_bytes, size_t chunk, float* acc, float scale,
                                  cudaStream_t s);
+// acc[0, hi - lo) += scale * sum_ranks(region[lo, hi)), fp32 (elements, multiples of 4; lo == hi is
+// allowed): one bucket's share of this rank's shard, for reduce-scatter overlapped with backward.
+// `blocks` > 0 runs it on that many blocks (fewer SMs taken from concurrent compute); same on all ranks.
+void comm_reduce_scatter_range_acc_f32(const CommCtx& c, size_t off_bytes, size_t lo, size_t hi, float* acc,
+                                       float scale, int blocks, cudaStream_t s);
 // bf16 variants (fp32 accumulation of the sum; the reduce-scatter accumulates into an fp32 shard).
 void comm_allreduce_bf16(const CommCtx& c, size_t off_bytes, size_t n, float scale, cudaStream_t s);
 void comm_reduce_scatter_acc_bf16(const CommCtx& c, size_t off_bytes, size_t chunk, float* acc, float scale,

@@ -201,6 +201,26 @@ def attention_backward(qkv: torch.Tensor, out: torch.Tensor, dout: torch.Tensor,
 
 
 # ------------------------------------------------------------------------------ transformer block
+# Called at the end of each block's backward with the block's parameters, once all of their weight
+# gradients have been issued on the current stream (a ZeRO engine starts that block's gradient
+# reduction from here, overlapping it with the rest of the backward).
+_GRAD_READY_HOOKS: List = []
+
+
+def register_grad_ready_hook(fn) -> "_HookHandle":
+    _GRAD_READY_HOOKS.append(fn)
+    return _HookHandle(fn)
+
+
+class _HookHandle:
+    def __init__(self, fn) -> None:
+        self.fn = fn
+
+    def remove(self) -> None:
+        if self.fn in _GRAD_READY_HOOKS:
+            _GRAD_READY_HOOKS.remove(self.fn)
+
+
 class _BlockFn(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x, w_in, wq, wk, wv, wo, w_post, wg, wu, wd, meta):
@@ -283,6 +303,8 @@ class _BlockFn(torch.autograd.Function):
 
         g_qkv = sink_qkv.finish()
         g_gu = sink_gu.finish()
+        for hook in list(_GRAD_READY_HOOKS):  # every weight gradient of this block has been issued
+            hook(ctx.params)
         return (dx.view(B, S, d), sink_in.finish()[0], g_qkv[0], g_qkv[1], g_qkv[2], sink_o.finish()[0],
                 sink_post.finish()[0], g_gu[0], g_gu[1], sink_d.finish()[0], None)
 

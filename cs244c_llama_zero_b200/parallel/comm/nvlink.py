@@ -134,6 +134,33 @@ class NvlinkCollectives(TorchCollectives):
         _maybe_simulate_collective_delay(acc.numel() * flat.element_size(), world)
         return acc
 
+    supports_range_reduce_scatter = True
+
+    def reduce_scatter_range_accumulate_(self, shard_acc: torch.Tensor, flat: torch.Tensor, lo: int, hi: int,
+                                         shard_lo: int, scale: float, blocks: int = 0) -> bool:
+        """shard_acc += scale * sum_ranks(flat[lo:hi]) restricted to this rank's shard.
+
+        ``flat`` is the whole symmetric fp32 buffer, ``shard_acc`` this rank's shard of it
+        (``flat[shard_lo : shard_lo + shard_acc.numel()]`` in the flat layout).  Every rank must call
+        this for the same buckets in the same order (each call is a collective).  Returns False, doing
+        nothing, when ``flat`` is not a symmetric fp32 buffer of this object or the bounds are not
+        4-element aligned.  ``blocks`` > 0 limits the kernel to that many thread blocks (every rank must
+        pass the same value), leaving the other SMs to compute that runs concurrently.
+        """
+        hit = self._locate(flat)
+        if hit is None or flat.dtype != torch.float32 or lo % 4 or hi % 4 or shard_lo % 4:
+            return False
+        buf, off = hit
+        shard_hi = shard_lo + shard_acc.numel()
+        a, b = max(lo, shard_lo), min(hi, shard_hi)
+        if b <= a:
+            a = b = lo  # empty share: still join the collective's barriers
+            acc = shard_acc
+        else:
+            acc = shard_acc[a - shard_lo:]
+        buf.ctx.reduce_scatter_range_acc_f32(off + lo * 4, a - lo, b - lo, acc, scale, int(blocks))
+        return True
+
     def reduce_scatter_into(self, out: torch.Tensor, flat: torch.Tensor) -> torch.Tensor:
         if out.dtype == torch.float32 and self._locate(flat) is not None:
             out.zero_()

@@ -22,6 +22,7 @@ model-dtype copy; clipping never synchronises with the host.
 
 from __future__ import annotations
 
+import os
 import time
 from typing import Dict, List, Optional, Tuple
 
@@ -237,10 +238,84 @@ class ZeROStage2Optimizer(_ShardedStateMixin, _FlatEngine):
 
     def __init__(self, model: nn.Module, grad_bucket_numel: int = 16 * 1024 * 1024, **kwargs) -> None:
         super().__init__(model, **kwargs)
-        # Accepted for CLI compatibility; one reduce-scatter of the whole flat buffer per backward.
+        # Accepted for CLI compatibility: buckets are transformer blocks (see _setup_overlap).
         self.grad_bucket_numel = grad_bucket_numel
         self.grad_shard = torch.zeros(self.space.chunk, dtype=torch.float32, device=self.device)
         self._pending_flush = False
+        self._setup_overlap()
+
+    # -- reduce-scatter overlapped with backward -------------------------------------------
+    def _setup_overlap(self) -> None:
+        """Per-block gradient buckets reduced on a high-priority stream while backward continues.
+
+        Enabled with ``ZB_OVERLAP_REDUCE_SCATTER=1`` when the collectives offer a bucketed
+        reduce-scatter on the flat gradient buffer (the NVLink kernels).  Each transformer block's parameters occupy one contiguous range of the
+        flat space; when the block's backward has issued its weight gradients, that range is
+        reduce-scattered (each rank reduces the part inside its shard) on the side stream.  The
+        ranges no block covers (embedding / head / final norm) are reduced when backward ends.
+        """
+        self._overlap = False
+        self._buckets: List[Tuple[int, int]] = []
+        self._bucket_of: Dict[int, int] = {}
+        if not (self.world_size > 1 and self.device.type == "cuda"
+                and getattr(self.collectives, "supports_range_reduce_scatter", False)):
+            return
+        # Opt-in.  Measured on 2 B200 (small model, stage 2): 10.32 ms/step without, 13.07 ms with (8-block
+        # buckets) and 11.13 ms (full-grid buckets): a bucket kernel that waits at its cross-rank barrier
+        # holds SMs that the statically scheduled persistent GEMM CTAs need, so its wait lands on the
+        # critical path.  Worth revisiting with dynamically scheduled (work-counter) compute kernels.
+        if os.environ.get("ZB_OVERLAP_REDUCE_SCATTER", "0") != "1":
+            return
+        offset = {id(p): off for p, off in zip(self.meta.params, self.space.offsets)}
+        for module in self.model.modules():
+            if type(module).__name__ != "TransformerBlock":
+                continue
+            ps = [p for p in module.parameters() if id(p) in offset]
+            if not ps:
+                continue
+            lo = min(offset[id(p)] for p in ps)
+            hi = max(offset[id(p)] + p.numel() for p in ps)
+            hi = (hi + 3) // 4 * 4
+            if lo % 4:
+                return  # layout not bucketable; keep the single reduce-scatter
+            for p in ps:
+                self._bucket_of[id(p)] = len(self._buckets)
+            self._buckets.append((lo, hi))
+        if not self._buckets:
+            return
+        from ...ops import functional as F
+
+        self._comm_stream = torch.cuda.Stream(device=self.device, priority=-1)
+        self._launched: List[int] = []
+        self._overlap_active = False
+        self._hook = F.register_grad_ready_hook(self._on_block_grads_ready)
+        self._overlap = True
+
+    # Thread blocks for buckets reduced while backward runs: few, so that the persistent compute
+    # kernels keep almost every SM; the final flush runs alone and uses the full grid.
+    OVERLAP_BLOCKS = 8
+
+    def _reduce_range(self, lo: int, hi: int, blocks: int = 0) -> None:
+        grads = self.space.grads
+        with self.clock.measure("backward_reduce_scatter", (hi - lo) * grads.element_size()):
+            ok = self.collectives.reduce_scatter_range_accumulate_(self.grad_shard, grads, lo, hi,
+                                                                   self.space.shard_start, 1.0 / self.world_size,
+                                                                   blocks)
+        if not ok:
+            raise RuntimeError("bucketed reduce-scatter unavailable for the flat gradient buffer")
+
+    def _on_block_grads_ready(self, params) -> None:
+        if not self._overlap_active or not params:
+            return
+        b = self._bucket_of.get(id(params[0]))
+        if b is None or b in self._launched:
+            return
+        ready = torch.cuda.Event()
+        ready.record()
+        with torch.cuda.stream(self._comm_stream):
+            self._comm_stream.wait_event(ready)
+            self._reduce_range(*self._buckets[b], blocks=self.OVERLAP_BLOCKS)
+        self._launched.append(b)
 
     @property
     def flat_grad_buffer(self) -> torch.Tensor:
@@ -252,15 +327,49 @@ class ZeROStage2Optimizer(_ShardedStateMixin, _FlatEngine):
         self._pending_flush = True
 
     def backward(self, loss: torch.Tensor) -> None:
-        loss.backward()
+        if self._overlap:
+            self._launched = []
+            self._overlap_active = True
+        try:
+            loss.backward()
+        finally:
+            if self._overlap:
+                self._overlap_active = False
         self._pending_flush = True
         self._flush_flat_grad_buffer()
+
+    def _flush_overlapped(self) -> None:
+        """Reduce what the per-block buckets did not cover, then join the side stream."""
+        grads = self.space.grads
+        covered = sorted(self._buckets[b] for b in self._launched)
+        rest, cursor = [], 0
+        for lo, hi in covered:
+            if lo > cursor:
+                rest.append((cursor, lo))
+            cursor = max(cursor, hi)
+        if cursor < grads.numel():
+            rest.append((cursor, grads.numel()))
+        ready = torch.cuda.Event()
+        ready.record()
+        with torch.cuda.stream(self._comm_stream):
+            self._comm_stream.wait_event(ready)
+            for lo, hi in rest:
+                self._reduce_range(lo, hi)
+        torch.cuda.current_stream().wait_stream(self._comm_stream)
+        grads.zero_()
+        self._pending_flush = False
 
     def _flush_flat_grad_buffer(self) -> None:
         if not self._pending_flush:
             return
         self.space.fold_autograd_grads()
         grads = self.space.grads
+        if self._overlap and self._launched:
+            self._record_memory_event("measured_step_stage2_pre_reduce_scatter")
+            with self.collectives.label_scope("stage2.backward.reduce_scatter.flat_grad_buffer"):
+                self._flush_overlapped()
+            self._record_memory_event("measured_step_stage2_post_reduce_scatter")
+            return
         self._record_memory_event("measured_step_stage2_pre_reduce_scatter")
         with self.clock.measure("backward_reduce_scatter", tensor_num_bytes(grads)):
             with self.collectives.label_scope("stage2.backward.reduce_scatter.flat_grad_buffer"):
