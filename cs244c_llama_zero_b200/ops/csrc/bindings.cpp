@@ -436,6 +436,12 @@ class CommContext {
     prepare();
     b200::comm_allgather(c_, off, chunk_bytes, shard.data_ptr(), cur_stream());
   }
+  void gather_ce(int64_t off, int64_t chunk_bytes, Tensor dst) {
+    TORCH_CHECK(dst.is_cuda() && dst.is_contiguous(), "gather_ce: contiguous CUDA destination required");
+    TORCH_CHECK(dst.numel() * dst.element_size() >= chunk_bytes * c_.world, "gather_ce: destination too small");
+    c10::cuda::CUDAGuard g(device_);
+    b200::comm_gather_ce(c_, off, chunk_bytes, dst.data_ptr(), cur_stream());
+  }
   void adamw_allgather(int64_t param_off, int64_t chunk, Tensor master, Tensor m, Tensor v, Tensor grad,
                        std::optional<Tensor> scale, double scale_const, double lr, double beta1, double beta2,
                        double eps, double wd, int64_t step) {
@@ -526,6 +532,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
       .def("reduce_scatter_acc_bf16", &CommContext::reduce_scatter_acc_bf16)
       .def("reduce_scatter_range_acc_f32", &CommContext::reduce_scatter_range_acc_f32)
       .def("allgather", &CommContext::allgather)
+      .def("gather_ce", &CommContext::gather_ce)
       .def("adamw_allgather", &CommContext::adamw_allgather)
       .def("barrier", &CommContext::barrier)
       .def("wait_unsignalled", &CommContext::wait_unsignalled)

@@ -482,6 +482,17 @@ void comm_allgather(const CommCtx& c, size_t off, size_t chunk_bytes, const void
   count_launch();
 }
 
+void comm_gather_ce(const CommCtx& c, size_t off, size_t chunk_bytes, void* dst, cudaStream_t s) {
+  check_ctx(c);
+  // Start with the next rank so that at any moment the W ranks read from W different peers.
+  for (int i = 0; i < c.world; ++i) {
+    const int r = (c.rank + 1 + i) % c.world;
+    const void* src = reinterpret_cast<const void*>(c.peers[r] + off);
+    B200_CUDA_CHECK(cudaMemcpyAsync(static_cast<char*>(dst) + (size_t)r * chunk_bytes, src, chunk_bytes,
+                                    cudaMemcpyDeviceToDevice, s));
+  }
+}
+
 void comm_adamw_allgather(const CommCtx& c, size_t param_off, size_t chunk, float* master, float* m, float* v,
                           const float* grad, const float* scale_ptr, float scale_const, float lr, float beta1,
                           float beta2, float eps, float wd, int step, cudaStream_t s) {

@@ -45,6 +45,10 @@ void comm_reduce_scatter_acc_bf16(const CommCtx& c, size_t off_bytes, size_t chu
                                   cudaStream_t s);
 // Every rank's `shard` (chunk_bytes, 16-byte multiple) lands at region[rank*chunk_bytes] on all ranks.
 void comm_allgather(const CommCtx& c, size_t off_bytes, size_t chunk_bytes, const void* shard, cudaStream_t s);
+// Pull-mode all-gather on the copy engines: dst[r*chunk_bytes, (r+1)*chunk_bytes) = rank r's
+// region[0, chunk_bytes) for every r, as one peer-to-device copy per rank on stream s (no kernel, no
+// SMs, no barrier).  The caller guarantees every rank's source region is stable while it is read.
+void comm_gather_ce(const CommCtx& c, size_t off_bytes, size_t chunk_bytes, void* dst, cudaStream_t s);
 // AdamW on this rank's fp32 shard, then the bf16 result is written into every rank's parameter
 // region at [rank*chunk] (fused update + all-gather).
 void comm_adamw_allgather(const CommCtx& c, size_t param_off_bytes, size_t chunk, float* master, float* m, float* v,

@@ -11,6 +11,8 @@ kernels (``ops/csrc/comm.cu``):
                                  the fp32 gradient shard in the same kernel
 * ``allgather_into``             ``multimem.st`` of the shard into every rank's buffer
 * ``adamw_allgather``            AdamW on the shard fused with the multicast all-gather of the bf16 result
+* ``pull_allgather_into``        copy-engine pulls of every rank's shard (no kernel, no barrier): the ZeRO-3
+                                 per-module parameter gather, prefetched on a side stream
 
 ``impl="p2p"`` runs the same kernels with plain peer loads/stores instead of multicast.  Calls on
 tensors that are not part of a registered symmetric buffer (and the reference-compatible
@@ -178,6 +180,27 @@ class NvlinkCollectives(TorchCollectives):
         buf.ctx.allgather(off, chunk_bytes, shard)
         _maybe_simulate_collective_delay(chunk_bytes, world)
         return out
+
+    supports_pull_gather = True
+
+    def pull_allgather_into(self, out: torch.Tensor, shard: torch.Tensor) -> bool:
+        """out[r*n : (r+1)*n] = rank r's ``shard`` (n elements) for every r, read by the copy engines.
+
+        ``shard`` must lie in a symmetric buffer of this object (same offset on every rank).  No kernel
+        and no barrier: one peer-to-device copy per rank on the current stream, so the caller must
+        guarantee that no rank rewrites its shard while another may be reading it.  Returns False,
+        doing nothing, when the tensors do not qualify.
+        """
+        hit = self._locate(shard)
+        world = self._w()
+        nbytes = shard.numel() * shard.element_size()
+        if (hit is None or out.dtype != shard.dtype or out.numel() < shard.numel() * world or nbytes % 16
+                or not out.is_contiguous() or not out.is_cuda):
+            return False
+        buf, off = hit
+        buf.ctx.gather_ce(off, nbytes, out)
+        _maybe_simulate_collective_delay(nbytes, world)
+        return True
 
     def adamw_allgather(self, params_flat: torch.Tensor, master: torch.Tensor, exp_avg: torch.Tensor,
                         exp_avg_sq: torch.Tensor, grad: torch.Tensor, scale, cfg, step: int) -> bool:

@@ -20,6 +20,7 @@ that support it) and released.
 
 from __future__ import annotations
 
+import os
 import time
 from contextlib import contextmanager
 from typing import Dict, Iterator, List, Optional, Sequence, Tuple
@@ -90,6 +91,11 @@ class Stage3ParamHandle:
         if self.materialized:
             return
         eng = self.engine
+        if eng._pull is not None and phase in ("forward", "backward"):
+            full = eng._pull.materialize(self, phase)
+            if full is not None:
+                self._bind(full)
+                return
         staging = eng._staging_params(self.padded_numel, self.param_dtype) if phase in ("forward", "backward") else None
         full = staging if staging is not None else torch.empty(self.padded_numel, dtype=self.param_dtype,
                                                               device=self.device)
@@ -105,6 +111,8 @@ class Stage3ParamHandle:
     def reshard(self) -> None:
         if not self.materialized:
             return
+        if self.engine._pull is not None:
+            self.engine._pull.release(self)
         for p in self.meta.params:
             p.grad = None
             p.data = torch.empty(0, dtype=p.dtype, device=p.device)
@@ -165,8 +173,25 @@ class _ShardedModuleFunction(torch.autograd.Function):
         eng._record_memory_event(f"measured_step_stage3_{runner.name}_pre_allgather_forward")
         runner.handle.materialize("forward")
         eng._record_memory_event(f"measured_step_stage3_{runner.name}_post_allgather_forward")
-        with torch.no_grad():
-            out = runner.module(*args)
+        ctx.graph = None
+        keep, runner.keep_next = runner.keep_next, False
+        if keep:
+            # Keep this module's autograd graph (its activations) instead of recomputing it in
+            # backward; its backward reads the parameters only when it runs, after re-gathering.
+            with torch.enable_grad():
+                inputs, rebuilt = [], []
+                for a, wants in zip(args, ctx.wants_grad):
+                    if torch.is_tensor(a):
+                        a = a.detach().requires_grad_(wants)
+                        if wants:
+                            inputs.append(a)
+                    rebuilt.append(a)
+                out = runner.module(*rebuilt)
+            ctx.graph = (out, inputs)
+            out = out.detach()
+        else:
+            with torch.no_grad():
+                out = runner.module(*args)
         eng._record_memory_event(f"measured_step_stage3_{runner.name}_after_forward")
         runner.handle.reshard()
         eng._record_memory_event(f"measured_step_stage3_{runner.name}_after_forward_discard")
@@ -179,6 +204,22 @@ class _ShardedModuleFunction(torch.autograd.Function):
         dev = runner.device
         devices = [dev.index if dev.index is not None else torch.cuda.current_device()] if dev.type == "cuda" else []
         saved = iter(ctx.saved_tensors)
+        if ctx.graph is not None:
+            graph_out, inputs = ctx.graph
+            ctx.graph = None
+            runner.handle.materialize("backward")
+            grad_buf = runner.handle.begin_grad()
+            params = list(runner.handle.meta.params)
+            grads = torch.autograd.grad(graph_out, inputs + params, grad_outputs=grad_output, allow_unused=True)
+            del graph_out
+            input_grads, param_grads = grads[: len(inputs)], grads[len(inputs) :]
+            eng._record_memory_event(f"measured_step_stage3_{runner.name}_after_layer_backward")
+            runner.handle.end_grad(grad_buf, param_grads)
+            del grad_buf
+            runner.handle.reshard()
+            it = iter(input_grads)
+            return (None, None, *[next(it) if (is_t and wants) else None
+                                  for is_t, wants in zip(ctx.is_tensor, ctx.wants_grad)])
         with torch.random.fork_rng(devices=devices, enabled=True):
             torch.set_rng_state(ctx.cpu_rng)
             if ctx.cuda_rng is not None:
@@ -224,16 +265,176 @@ class _ModuleRunner:
         # A grad-requiring dummy input guarantees the autograd node exists even when the
         # module's real input (token ids) does not require grad.
         self.autograd_token = torch.zeros(1, dtype=torch.float32, device=self.device, requires_grad=True)
+        self.keep_next = False
+
+    def keeps_graph(self, args) -> bool:
+        """True when this call can keep its graph instead of being recomputed in backward.
+
+        Only the B200 kernels' autograd functions qualify: they save activations and read the
+        parameters at backward time (so re-gathered parameters are seen), while eager PyTorch ops save
+        the parameter tensors themselves, which are released between calls.
+        """
+        if self.engine.recompute or not torch.is_grad_enabled():
+            return False
+        m = self.module
+        kind = type(m).__name__
+        if kind == "TransformerBlock":
+            return (getattr(m, "use_b200", False) and (len(args) < 2 or args[1] is None)
+                    and not (m.training and m.cfg.dropout > 0))
+        if kind == "LMHead":  # labels given: the fused LM-head + cross-entropy function
+            return getattr(m, "use_b200", False) and len(args) > 1 and args[1] is not None
+        return False
 
     def call(self, *args):
+        # Decided here: grad mode is always off inside an autograd Function's forward.
+        self.keep_next = self.keeps_graph(args)
         return _ShardedModuleFunction.apply(self, self.autograd_token, *args)
+
+
+class _PullGather:
+    """Per-module parameter all-gathers as copy-engine pulls, prefetched one module ahead.
+
+    Every rank keeps its model-dtype parameter shards in one symmetric buffer (the store, identical
+    layout on every rank).  Gathering a module is one peer-to-device copy per rank into a staging
+    slot: no kernel (the GEMMs keep every SM) and no barrier (ranks do not wait for one another
+    module by module).  While module ``i`` computes, module ``i+1``'s copies run on a side stream; the
+    order is predicted from the previous step's sequence of (module, forward/backward) gathers, and
+    prefetching stops for the step at the first gather that does not match.
+
+    Safety of the barrier-free reads: a rank rewrites its store only in the optimizer step, which
+    comes after the global-norm all-reduce, and every rank joins that all-reduce only after all of
+    its copies of the step have finished (the compute stream waits for the side stream first);
+    the next step's reads start only after a device barrier that follows every rank's update.
+    """
+
+    def __init__(self, engine: "ZeROStage3Optimizer", store: torch.Tensor, slots: List[torch.Tensor]) -> None:
+        self.engine = engine
+        self.store = store
+        self.slots = slots
+        self.stream = torch.cuda.Stream(device=engine.device)
+        self.use_done: List[Optional[torch.cuda.Event]] = [None] * len(slots)   # last reader finished
+        self.write_done: List[Optional[torch.cuda.Event]] = [None] * len(slots)  # last side-stream gather
+        self.bound: List[Optional[Stage3ParamHandle]] = [None] * len(slots)
+        self.pending: Dict[int, int] = {}  # id(handle) -> slot holding its prefetched parameters
+        self.ring = 0
+        self.plan: Optional[List[Tuple[Stage3ParamHandle, str]]] = None
+        self.pos = 0
+        self.trace: List[Tuple[Stage3ParamHandle, str]] = []
+        self.trace_cap = 64 * (len(engine._handle_order) + 1)
+        self.ready: Optional[torch.cuda.Event] = None
+        self.prefetches = 0
+
+    # -- slots ---------------------------------------------------------------------------------
+    def _take_slot(self) -> Optional[int]:
+        s = self.ring
+        if self.bound[s] is not None:
+            return None
+        self.ring = (s + 1) % len(self.slots)
+        for key, slot in list(self.pending.items()):
+            if slot == s:
+                del self.pending[key]
+        return s
+
+    def _gather(self, handle: Stage3ParamHandle, slot: int, phase: str) -> None:
+        full = self.slots[slot][: handle.padded_numel]
+        eng = self.engine
+        category = "forward_allgather" if phase == "forward" else "backward_allgather"
+        with eng.clock.measure(category, handle.full_param_bytes):
+            if not eng.collectives.pull_allgather_into(full, handle.param_shard):
+                raise RuntimeError(f"stage 3 pull gather does not apply to handle {handle.name}")
+
+    def _prefetch(self, handle: Stage3ParamHandle, phase: str) -> None:
+        # A handle that is bound right now (the last forward module is the first backward one) is
+        # gathered again into the other slot, which it takes over when it is next materialised.
+        if id(handle) in self.pending:
+            return
+        s = self._take_slot()
+        if s is None:
+            return
+        st = self.stream
+        for ev in (self.use_done[s], self.ready):
+            if ev is not None:
+                st.wait_event(ev)
+        with torch.cuda.stream(st):
+            self._gather(handle, s, phase)
+            ev = torch.cuda.Event()
+            ev.record(st)
+        self.write_done[s] = ev
+        self.pending[id(handle)] = s
+        self.prefetches += 1
+
+    # -- module calls --------------------------------------------------------------------------
+    def materialize(self, handle: Stage3ParamHandle, phase: str) -> Optional[torch.Tensor]:
+        cur = torch.cuda.current_stream(self.engine.device)
+        s = self.pending.pop(id(handle), None)
+        if s is not None:
+            cur.wait_event(self.write_done[s])
+        else:
+            s = self._take_slot()
+            if s is None:
+                return None
+            if self.write_done[s] is not None:  # a dropped prefetch may still be writing this slot
+                cur.wait_event(self.write_done[s])
+            self._gather(handle, s, phase)
+        self.bound[s] = handle
+        self._advance(handle, phase)
+        return self.slots[s][: handle.padded_numel]
+
+    def release(self, handle: Stage3ParamHandle) -> None:
+        for s, h in enumerate(self.bound):
+            if h is handle:
+                ev = torch.cuda.Event()
+                ev.record(torch.cuda.current_stream(self.engine.device))
+                self.use_done[s] = ev
+                self.bound[s] = None
+
+    def _advance(self, handle: Stage3ParamHandle, phase: str) -> None:
+        if len(self.trace) < self.trace_cap:
+            self.trace.append((handle, phase))
+        plan = self.plan
+        if plan is None:
+            return
+        if self.pos < len(plan) and plan[self.pos][0] is handle and plan[self.pos][1] == phase:
+            self.pos += 1
+            if self.pos < len(plan):
+                self._prefetch(*plan[self.pos])
+        else:
+            self.plan = None
+
+    # -- step boundaries -----------------------------------------------------------------------
+    def begin_forward(self) -> None:
+        self.trace = []
+        self.pos = 0
+
+    def before_store_write(self) -> None:
+        """Every copy issued so far has finished before the compute stream goes on."""
+        torch.cuda.current_stream(self.engine.device).wait_stream(self.stream)
+        self.pending.clear()
+
+    def after_store_write(self, next_plan: bool) -> None:
+        """Barrier so that no rank reads a shard before its owner has rewritten it; then prefetch the
+        first module of the next step."""
+        self.engine.collectives.barrier()
+        ev = torch.cuda.Event()
+        ev.record(torch.cuda.current_stream(self.engine.device))
+        self.ready = ev
+        if next_plan:
+            self.plan = list(self.trace) if 0 < len(self.trace) < self.trace_cap else None
+        self.trace = []
+        self.pos = 0
+        if self.plan:
+            self._prefetch(*self.plan[0])
 
 
 class ZeROStage3Optimizer(ZeROEngineBase):
     stage = 3
 
-    def __init__(self, model: nn.Module, **kwargs) -> None:
+    def __init__(self, model: nn.Module, recompute: bool = False, **kwargs) -> None:
         super().__init__(model, **kwargs)
+        # recompute=True: every module is re-run in backward (the reference's behaviour).  False:
+        # modules running on the B200 kernels keep their activations; the others still recompute.
+        self.recompute = bool(recompute)
+        self._pull: Optional[_PullGather] = None
         self._summon_depth = 0
         self.handles: Dict[str, Stage3ParamHandle] = {}
         self._handle_order: List[Stage3ParamHandle] = []
@@ -251,9 +452,23 @@ class ZeROStage3Optimizer(ZeROEngineBase):
             largest = max(h.padded_numel for h in self._handle_order)
             self._stage_params = [alloc(largest, self.param_dtype) for _ in range(2)]
             self._stage_grads = alloc(largest, torch.float32)
+            if getattr(self.collectives, "supports_pull_gather", False) and os.environ.get("ZB_STAGE3_PULL", "1") != "0":
+                self._setup_pull_gather(alloc)
+
+    def _setup_pull_gather(self, alloc) -> None:
+        """Move every handle's model-dtype shard into one symmetric store read by the peers' copy engines."""
+        store = alloc(sum(h.chunk for h in self._handle_order), self.param_dtype)
+        off = 0
+        for h in self._handle_order:
+            view = store[off : off + h.chunk]
+            view.copy_(h.param_shard)
+            h.param_shard = view
+            off += h.chunk
+        self._pull = _PullGather(self, store, self._stage_params)
+        self._pull.after_store_write(next_plan=False)
 
     def _staging_params(self, numel: int, dtype: torch.dtype) -> Optional[torch.Tensor]:
-        if not self._stage_params or dtype != self._stage_params[0].dtype:
+        if not self._stage_params or dtype != self._stage_params[0].dtype or self._pull is not None:
             return None
         buf = self._stage_params[self._stage_slot]
         self._stage_slot ^= 1
@@ -312,6 +527,8 @@ class ZeROStage3Optimizer(ZeROEngineBase):
 
     def prepare_forward(self) -> Dict[str, float]:
         self._reshard_all_params()
+        if self._pull is not None:
+            self._pull.begin_forward()
         return {"prepare_comm_ms": 0.0}
 
     def zero_grad(self) -> None:
@@ -331,6 +548,9 @@ class ZeROStage3Optimizer(ZeROEngineBase):
         return total.sqrt().reshape(())
 
     def _update(self, max_grad_norm: float) -> torch.Tensor:
+        if self._pull is not None:
+            # before the global-norm all-reduce: a peer rewrites its store only after that all-reduce
+            self._pull.before_store_write()
         norm = self._global_norm()
         scale = clip_coefficient(norm, max_grad_norm)
         self.step_count += 1
@@ -339,6 +559,8 @@ class ZeROStage3Optimizer(ZeROEngineBase):
                 adamw_update_(h.local_master_param_shard, h.exp_avg, h.exp_avg_sq, h.grad_shard, self.adam,
                               self.step_count, grad_scale=scale, param_out=h.param_shard)
         self._reshard_all_params()
+        if self._pull is not None:
+            self._pull.after_store_write(next_plan=True)
         return norm
 
     def step_async(self, max_grad_norm: float = 0.0) -> torch.Tensor:
@@ -395,6 +617,8 @@ class ZeROStage3Optimizer(ZeROEngineBase):
         }
 
     def load_state_dict(self, state: Dict[str, object]) -> None:
+        if self._pull is not None:
+            self._pull.before_store_write()
         self.step_count = int(state["step_count"])
         saved_handles = state["handles"]
         for h in self._handle_order:
@@ -407,3 +631,5 @@ class ZeROStage3Optimizer(ZeROEngineBase):
             h.param_shard.copy_(h.local_master_param_shard)
             h.grad_shard.zero_()
         self._reshard_all_params()
+        if self._pull is not None:
+            self._pull.after_store_write(next_plan=False)

@@ -56,6 +56,14 @@ def _collectives_worker(rank: int, world: int, port: int, impl: str) -> None:
         parts = [torch.empty_like(shard) for _ in range(world)]
         dist.all_gather(parts, shard)
         torch.testing.assert_close(pbuf, torch.cat(parts))
+        # copy-engine pull gather: every rank's shard at the same offset of a symmetric store
+        store = coll.alloc(chunk + 64, torch.bfloat16)
+        store[64:].copy_(shard)
+        coll.barrier()
+        pulled = torch.full((n,), -1.0, device="cuda", dtype=torch.bfloat16)
+        assert coll.pull_allgather_into(pulled, store[64:])
+        torch.testing.assert_close(pulled, torch.cat(parts))
+        coll.barrier()
         # fused AdamW + all-gather vs update + NCCL all-gather
         master = torch.randn(chunk, device="cuda", generator=g)
         m, v = torch.zeros(chunk, device="cuda"), torch.zeros(chunk, device="cuda")

@@ -65,3 +65,43 @@ def test_b200_engine_trains(tmp_path):
         engine.step()
         losses.append(float(loss))
     assert losses[-1] < 0.8 * losses[0], losses
+
+
+def test_stage3_keep_graph_matches_recompute_and_stage0():
+    """ZeRO-3 keeping the B200 modules' activations gives the same training as re-running them in
+    backward and as the unsharded engine (one GPU, so sharding is the identity)."""
+    from cs244c_llama_zero_b200.parallel.zero import ZeROStage0DDP, ZeROStage3Optimizer
+
+    cfg = _cfg(64, tied=False)
+    models, engines = [], []
+    for make in (lambda m: ZeROStage0DDP(model=m, lr=1e-3),
+                 lambda m: ZeROStage3Optimizer(model=m, lr=1e-3, recompute=True),
+                 lambda m: ZeROStage3Optimizer(model=m, lr=1e-3, recompute=False)):
+        torch.manual_seed(0)
+        model = LlamaForCausalLM(cfg).cuda().to(torch.bfloat16)
+        model.set_backend("b200")
+        models.append(model)
+        engines.append(make(model))
+    ids = torch.randint(0, cfg.vocab_size, (2, cfg.max_seq_len), device="cuda",
+                        generator=torch.Generator(device="cuda").manual_seed(1))
+    kept = []
+    for runner in engines[2]._module_runners.values():
+        decide = runner.keeps_graph
+        runner.keeps_graph = lambda args, decide=decide: kept.append(decide(args)) or kept[-1]
+    losses = [[] for _ in engines]
+    for _ in range(3):
+        for i, (model, engine) in enumerate(zip(models, engines)):
+            engine.zero_grad()
+            engine.prepare_forward()
+            with torch.autocast("cuda", dtype=torch.bfloat16):
+                loss = model(input_ids=ids, labels=ids, return_logits=False).loss
+            engine.backward(loss)
+            engine.step(max_grad_norm=1.0)
+            losses[i].append(float(loss))
+    assert sum(kept) == 3 * (cfg.n_layers + 1), kept  # every block and the LM head kept their graphs
+    assert losses[1] == pytest.approx(losses[0], rel=1e-3) and losses[2] == pytest.approx(losses[0], rel=1e-3)
+    with engines[1].summon_full_params(), engines[2].summon_full_params():
+        for (n, a), (_, b), (_, c) in zip(models[0].named_parameters(), models[1].named_parameters(),
+                                          models[2].named_parameters()):
+            torch.testing.assert_close(c.float(), b.float(), rtol=2e-2, atol=2e-3, msg=n)
+            torch.testing.assert_close(c.float(), a.float(), rtol=2e-2, atol=2e-3, msg=n)

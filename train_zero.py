@@ -110,6 +110,9 @@ def parse_args(argv=None) -> argparse.Namespace:
     p.add_argument("--tflops-mode", type=str, default="estimate", choices=["estimate", "profile", "off"])
     p.add_argument("--verbose", action="store_true")
     p.add_argument("--verbose-memory", action="store_true")
+    p.add_argument("--stage3-recompute", action="store_true",
+                   help="ZeRO-3: re-run every module in backward (the reference's behaviour) instead of keeping "
+                        "the activations of modules on the B200 kernels")
     p.add_argument("--pg-timeout-s", type=float, default=600.0,
                    help="Process-group timeout: a collective waiting longer than this on a missing rank fails")
     p.set_defaults(activation_checkpointing=False)
@@ -139,7 +142,7 @@ def build_engine(args: argparse.Namespace, model, collectives):
         return ZeROStage1Optimizer(**kwargs)
     if args.zero_stage == 2:
         return ZeROStage2Optimizer(**kwargs, grad_bucket_numel=max(1, int(args.stage2_grad_bucket_mb * 1024 * 1024 / 4)))
-    return ZeROStage3Optimizer(**kwargs)
+    return ZeROStage3Optimizer(**kwargs, recompute=args.stage3_recompute)
 
 
 def global_mean_scalar(value: float, device: torch.device, world_size: int) -> float:
