@@ -472,6 +472,12 @@ class CommContext {
   }
   bool multicast() const { return c_.mc != 0; }
   int64_t blocks() const { return c_.blocks; }
+  // Copy-engine pull of every rank's region[off, off + chunk_bytes) into dst on stream s.
+  void gather_ce_on(int64_t off, int64_t chunk_bytes, void* dst, cudaStream_t s) const {
+    b200::comm_gather_ce(c_, off, chunk_bytes, dst, s);
+  }
+  int64_t world() const { return c_.world; }
+  const c10::Device& device() const { return device_; }
 
  private:
   void prepare() { c_.errs = b200::device_errors_ptr(); }
@@ -482,6 +488,150 @@ class CommContext {
   b200::CommCtx c_;
   Tensor epochs_;
   c10::Device device_;
+};
+
+// Stream/event plumbing of the ZeRO-3 prefetching parameter gather, kept native so that one module's
+// prefetch costs one call from Python.  Slots are staging buffers; for each slot the object keeps
+// the event that the last gather into it finished (`written`) and the event that its last reader
+// on the compute stream finished (`used`).  Gathers are copy-engine pulls (no kernel).  Each gather
+// can be timed with a pair of events into one of a few categories.
+class PullGather {
+ public:
+  PullGather(int64_t slots, int64_t categories, int64_t device_index)
+      : device_(c10::Device(c10::DeviceType::CUDA, (c10::DeviceIndex)device_index)),
+        side_(at::cuda::getStreamFromPool(false, (c10::DeviceIndex)device_index)) {
+    TORCH_CHECK(slots >= 1 && slots <= 16 && categories >= 1, "PullGather: 1..16 slots");
+    c10::cuda::CUDAGuard g(device_);
+    written_.resize(slots);
+    used_.resize(slots);
+    has_written_.assign(slots, false);
+    has_used_.assign(slots, false);
+    for (int64_t i = 0; i < slots; ++i) {
+      B200_CUDA_CHECK(cudaEventCreateWithFlags(&written_[i], cudaEventDisableTiming));
+      B200_CUDA_CHECK(cudaEventCreateWithFlags(&used_[i], cudaEventDisableTiming));
+    }
+    B200_CUDA_CHECK(cudaEventCreateWithFlags(&ready_, cudaEventDisableTiming));
+    B200_CUDA_CHECK(cudaEventCreateWithFlags(&join_, cudaEventDisableTiming));
+    ms_.assign(categories, 0.0);
+    calls_.assign(categories, 0);
+  }
+  ~PullGather() {
+    for (auto e : written_) cudaEventDestroy(e);
+    for (auto e : used_) cudaEventDestroy(e);
+    for (auto& t : timed_) {
+      cudaEventDestroy(t.start);
+      cudaEventDestroy(t.end);
+    }
+    for (auto e : free_timing_) cudaEventDestroy(e);
+    cudaEventDestroy(ready_);
+    cudaEventDestroy(join_);
+  }
+
+  // Gather into `slot` on the side stream, after the slot's last reader and after the last
+  // mark_ready(); the compute stream picks it up with acquire(slot).
+  void prefetch(const CommContext& ctx, int64_t slot, int64_t off, int64_t chunk_bytes, int64_t dst,
+                int64_t category, bool timed) {
+    c10::cuda::CUDAGuard g(device_);
+    cudaStream_t s = side_.stream();
+    if (has_used_.at(slot)) B200_CUDA_CHECK(cudaStreamWaitEvent(s, used_[slot], 0));
+    if (has_ready_) B200_CUDA_CHECK(cudaStreamWaitEvent(s, ready_, 0));
+    copy(ctx, off, chunk_bytes, dst, category, timed, s);
+    B200_CUDA_CHECK(cudaEventRecord(written_[slot], s));
+    has_written_[slot] = true;
+  }
+  // Gather into `slot` on the current stream (after any side-stream gather still writing it).
+  void gather_now(const CommContext& ctx, int64_t slot, int64_t off, int64_t chunk_bytes, int64_t dst,
+                  int64_t category, bool timed) {
+    c10::cuda::CUDAGuard g(device_);
+    cudaStream_t s = cur_stream();
+    if (has_written_.at(slot)) B200_CUDA_CHECK(cudaStreamWaitEvent(s, written_[slot], 0));
+    copy(ctx, off, chunk_bytes, dst, category, timed, s);
+  }
+  // The current stream waits for the side-stream gather into `slot`.
+  void acquire(int64_t slot) {
+    c10::cuda::CUDAGuard g(device_);
+    if (has_written_.at(slot)) B200_CUDA_CHECK(cudaStreamWaitEvent(cur_stream(), written_[slot], 0));
+  }
+  // The slot's reader (queued on the current stream so far) is done with it once this point is reached.
+  void release(int64_t slot) {
+    c10::cuda::CUDAGuard g(device_);
+    B200_CUDA_CHECK(cudaEventRecord(used_.at(slot), cur_stream()));
+    has_used_[slot] = true;
+  }
+  // Later gathers start after the work queued on the current stream so far (the barrier that
+  // follows the stores' rewrite).
+  void mark_ready() {
+    c10::cuda::CUDAGuard g(device_);
+    B200_CUDA_CHECK(cudaEventRecord(ready_, cur_stream()));
+    has_ready_ = true;
+  }
+  // The current stream waits for every gather issued so far.
+  void join() {
+    c10::cuda::CUDAGuard g(device_);
+    B200_CUDA_CHECK(cudaEventRecord(join_, side_.stream()));
+    B200_CUDA_CHECK(cudaStreamWaitEvent(cur_stream(), join_, 0));
+  }
+  // Per-category totals (ms) and call counts of the timed gathers since the last call; waits for them.
+  std::pair<std::vector<double>, std::vector<int64_t>> take_times() {
+    c10::cuda::CUDAGuard g(device_);
+    for (auto& t : timed_) {
+      B200_CUDA_CHECK(cudaEventSynchronize(t.end));
+      float ms = 0.f;
+      B200_CUDA_CHECK(cudaEventElapsedTime(&ms, t.start, t.end));
+      ms_[t.category] += ms;
+      calls_[t.category] += 1;
+      free_timing_.push_back(t.start);
+      free_timing_.push_back(t.end);
+    }
+    timed_.clear();
+    auto out = std::make_pair(ms_, calls_);
+    std::fill(ms_.begin(), ms_.end(), 0.0);
+    std::fill(calls_.begin(), calls_.end(), 0);
+    return out;
+  }
+  void reset_times() { take_times(); }
+  int64_t side_stream() const { return (int64_t)side_.stream(); }
+
+ private:
+  struct Timed {
+    cudaEvent_t start, end;
+    int64_t category;
+  };
+  cudaEvent_t timing_event() {
+    if (!free_timing_.empty()) {
+      cudaEvent_t e = free_timing_.back();
+      free_timing_.pop_back();
+      return e;
+    }
+    cudaEvent_t e;
+    B200_CUDA_CHECK(cudaEventCreate(&e));
+    return e;
+  }
+  void copy(const CommContext& ctx, int64_t off, int64_t chunk_bytes, int64_t dst, int64_t category, bool timed,
+            cudaStream_t s) {
+    TORCH_CHECK(ctx.device() == device_, "PullGather: communicator on another device");
+    TORCH_CHECK(category >= 0 && category < (int64_t)ms_.size(), "PullGather: bad category");
+    Timed t{nullptr, nullptr, category};
+    if (timed) {
+      t.start = timing_event();
+      t.end = timing_event();
+      B200_CUDA_CHECK(cudaEventRecord(t.start, s));
+    }
+    ctx.gather_ce_on(off, chunk_bytes, reinterpret_cast<void*>(dst), s);
+    if (timed) {
+      B200_CUDA_CHECK(cudaEventRecord(t.end, s));
+      timed_.push_back(t);
+    }
+  }
+  c10::Device device_;
+  at::cuda::CUDAStream side_;
+  std::vector<cudaEvent_t> written_, used_, free_timing_;
+  std::vector<bool> has_written_, has_used_;
+  bool has_ready_ = false;
+  cudaEvent_t ready_, join_;
+  std::vector<Timed> timed_;
+  std::vector<double> ms_;
+  std::vector<int64_t> calls_;
 };
 
 int64_t launch_count() { return b200::launch_counter().load(); }
@@ -538,5 +688,16 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
       .def("wait_unsignalled", &CommContext::wait_unsignalled)
       .def_property_readonly("multicast", &CommContext::multicast)
       .def_property_readonly("blocks", &CommContext::blocks);
+  py::class_<PullGather>(m, "PullGather")
+      .def(py::init<int64_t, int64_t, int64_t>(), py::arg("slots"), py::arg("categories"), py::arg("device_index"))
+      .def("prefetch", &PullGather::prefetch)
+      .def("gather_now", &PullGather::gather_now)
+      .def("acquire", &PullGather::acquire)
+      .def("release", &PullGather::release)
+      .def("mark_ready", &PullGather::mark_ready)
+      .def("join", &PullGather::join)
+      .def("take_times", &PullGather::take_times)
+      .def("reset_times", &PullGather::reset_times)
+      .def_property_readonly("side_stream", &PullGather::side_stream);
 
 }

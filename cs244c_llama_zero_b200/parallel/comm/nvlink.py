@@ -102,6 +102,11 @@ class NvlinkCollectives(TorchCollectives):
                 return buf, off
         return None
 
+    def locate_symmetric(self, t: torch.Tensor) -> Optional[Tuple[object, int]]:
+        """(kernel context, byte offset) of a tensor inside one of this object's symmetric buffers."""
+        hit = self._locate(t)
+        return None if hit is None else (hit[0].ctx, hit[1])
+
     def check_errors(self) -> None:
         from ... import ops
 

@@ -36,8 +36,24 @@ class CommClock:
         self._host_ms: Dict[str, float] = {}
         self.calls: Dict[str, int] = {}
         self.bytes: Dict[str, int] = {}
+        # callables returning {category: ms} for intervals timed elsewhere (native code) since their last call
+        self._sources: List[object] = []
+
+    def add_source(self, fn) -> None:
+        self._sources.append(fn)
+
+    def count(self, category: str, num_bytes: int = 0) -> None:
+        """Count one call whose interval a registered source times."""
+        self.calls[category] = self.calls.get(category, 0) + 1
+        self.bytes[category] = self.bytes.get(category, 0) + int(num_bytes)
+
+    def _drain(self) -> None:
+        for fn in self._sources:
+            for category, ms in fn().items():
+                self._host_ms[category] = self._host_ms.get(category, 0.0) + ms
 
     def reset(self) -> None:
+        self._drain()
         self._pending.clear()
         self._host_ms.clear()
         self.calls.clear()
@@ -60,6 +76,7 @@ class CommClock:
             self._host_ms[category] = self._host_ms.get(category, 0.0) + (time.perf_counter() - t0) * 1000.0
 
     def ms(self, category: str) -> float:
+        self._drain()
         total = self._host_ms.get(category, 0.0)
         for start, end in self._pending.get(category, []):
             end.synchronize()
@@ -67,6 +84,7 @@ class CommClock:
         return total
 
     def total_ms(self, categories: Optional[List[str]] = None) -> float:
+        self._drain()
         cats = categories if categories is not None else sorted(set(self._pending) | set(self._host_ms))
         return sum(self.ms(c) for c in cats)
 

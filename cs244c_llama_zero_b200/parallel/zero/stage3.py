@@ -40,6 +40,7 @@ from .common import (
     tensors_num_bytes,
     unique_trainable_params,
 )
+from ..collectives import _maybe_simulate_collective_delay
 from .optim import adamw_update_, clip_coefficient, sum_of_squares
 
 
@@ -66,6 +67,8 @@ class Stage3ParamHandle:
         self.grad_shard = torch.zeros_like(self.local_master_param_shard)
         self.full_params: Optional[torch.Tensor] = None
         self.materialized = True
+        self._view_cache: Dict[Tuple[int, torch.dtype], List[torch.Tensor]] = {}
+        self._empty = torch.empty(0, dtype=self.param_dtype, device=self.device)  # released parameters' data
         self._bind(full.to(self.param_dtype))
 
     # Reference-compatible shard bookkeeping.
@@ -81,10 +84,20 @@ class Stage3ParamHandle:
     def full_param_bytes(self) -> int:
         return self.meta.total_numel * torch.tensor([], dtype=self.param_dtype).element_size()
 
-    def _bind(self, full: torch.Tensor) -> None:
+    def _views(self, full: torch.Tensor, cache: bool) -> List[torch.Tensor]:
+        """Per-parameter views of a full-size buffer; cached for the engine's persistent buffers."""
+        key = (full.data_ptr(), full.dtype)
+        views = self._view_cache.get(key) if cache else None
+        if views is None:
+            views = [full[off : off + shape.numel()].view(shape) for off, shape in zip(self.offsets, self.meta.shapes)]
+            if cache:
+                self._view_cache[key] = views
+        return views
+
+    def _bind(self, full: torch.Tensor, cache: bool = False) -> None:
         self.full_params = full
-        for p, off, shape in zip(self.meta.params, self.offsets, self.meta.shapes):
-            p.data = full[off : off + shape.numel()].view(shape)
+        for p, v in zip(self.meta.params, self._views(full, cache)):
+            p.data = v
         self.materialized = True
 
     def materialize(self, phase: str) -> None:
@@ -94,7 +107,7 @@ class Stage3ParamHandle:
         if eng._pull is not None and phase in ("forward", "backward"):
             full = eng._pull.materialize(self, phase)
             if full is not None:
-                self._bind(full)
+                self._bind(full, cache=True)
                 return
         staging = eng._staging_params(self.padded_numel, self.param_dtype) if phase in ("forward", "backward") else None
         full = staging if staging is not None else torch.empty(self.padded_numel, dtype=self.param_dtype,
@@ -106,16 +119,18 @@ class Stage3ParamHandle:
                     eng.collectives.allgather_into(full, self.param_shard)
                 else:
                     full.copy_(self.param_shard)
-        self._bind(full)
+        self._bind(full, cache=staging is not None)
 
     def reshard(self) -> None:
         if not self.materialized:
             return
         if self.engine._pull is not None:
             self.engine._pull.release(self)
+        empty = self._empty
         for p in self.meta.params:
-            p.grad = None
-            p.data = torch.empty(0, dtype=p.dtype, device=p.device)
+            if p.grad is not None:
+                p.grad = None
+            p.data = empty
         self.full_params = None
         self.materialized = False
 
@@ -125,12 +140,13 @@ class Stage3ParamHandle:
     def begin_grad(self) -> torch.Tensor:
         """Full-size fp32 gradient buffer bound to every parameter's ``main_grad``."""
         buf = self.engine._staging_grads(self.padded_numel)
+        persistent = buf is not None
         if buf is None:
             buf = torch.zeros(self.padded_numel, dtype=torch.float32, device=self.device)
         else:
             buf.zero_()
-        for p, off, shape in zip(self.meta.params, self.offsets, self.meta.shapes):
-            p.main_grad = buf[off : off + shape.numel()].view(shape)
+        for p, v in zip(self.meta.params, self._views(buf, persistent)):
+            p.main_grad = v
         return buf
 
     def end_grad(self, buf: torch.Tensor, param_grads: Sequence[Optional[torch.Tensor]]) -> None:
@@ -173,25 +189,8 @@ class _ShardedModuleFunction(torch.autograd.Function):
         eng._record_memory_event(f"measured_step_stage3_{runner.name}_pre_allgather_forward")
         runner.handle.materialize("forward")
         eng._record_memory_event(f"measured_step_stage3_{runner.name}_post_allgather_forward")
-        ctx.graph = None
-        keep, runner.keep_next = runner.keep_next, False
-        if keep:
-            # Keep this module's autograd graph (its activations) instead of recomputing it in
-            # backward; its backward reads the parameters only when it runs, after re-gathering.
-            with torch.enable_grad():
-                inputs, rebuilt = [], []
-                for a, wants in zip(args, ctx.wants_grad):
-                    if torch.is_tensor(a):
-                        a = a.detach().requires_grad_(wants)
-                        if wants:
-                            inputs.append(a)
-                    rebuilt.append(a)
-                out = runner.module(*rebuilt)
-            ctx.graph = (out, inputs)
-            out = out.detach()
-        else:
-            with torch.no_grad():
-                out = runner.module(*args)
+        with torch.no_grad():
+            out = runner.module(*args)
         eng._record_memory_event(f"measured_step_stage3_{runner.name}_after_forward")
         runner.handle.reshard()
         eng._record_memory_event(f"measured_step_stage3_{runner.name}_after_forward_discard")
@@ -204,22 +203,6 @@ class _ShardedModuleFunction(torch.autograd.Function):
         dev = runner.device
         devices = [dev.index if dev.index is not None else torch.cuda.current_device()] if dev.type == "cuda" else []
         saved = iter(ctx.saved_tensors)
-        if ctx.graph is not None:
-            graph_out, inputs = ctx.graph
-            ctx.graph = None
-            runner.handle.materialize("backward")
-            grad_buf = runner.handle.begin_grad()
-            params = list(runner.handle.meta.params)
-            grads = torch.autograd.grad(graph_out, inputs + params, grad_outputs=grad_output, allow_unused=True)
-            del graph_out
-            input_grads, param_grads = grads[: len(inputs)], grads[len(inputs) :]
-            eng._record_memory_event(f"measured_step_stage3_{runner.name}_after_layer_backward")
-            runner.handle.end_grad(grad_buf, param_grads)
-            del grad_buf
-            runner.handle.reshard()
-            it = iter(input_grads)
-            return (None, None, *[next(it) if (is_t and wants) else None
-                                  for is_t, wants in zip(ctx.is_tensor, ctx.wants_grad)])
         with torch.random.fork_rng(devices=devices, enabled=True):
             torch.set_rng_state(ctx.cpu_rng)
             if ctx.cuda_rng is not None:
@@ -265,7 +248,6 @@ class _ModuleRunner:
         # A grad-requiring dummy input guarantees the autograd node exists even when the
         # module's real input (token ids) does not require grad.
         self.autograd_token = torch.zeros(1, dtype=torch.float32, device=self.device, requires_grad=True)
-        self.keep_next = False
 
     def keeps_graph(self, args) -> bool:
         """True when this call can keep its graph instead of being recomputed in backward.
@@ -286,9 +268,41 @@ class _ModuleRunner:
         return False
 
     def call(self, *args):
-        # Decided here: grad mode is always off inside an autograd Function's forward.
-        self.keep_next = self.keeps_graph(args)
+        if self.keeps_graph(args):
+            return self._call_keeping_graph(args)
         return _ShardedModuleFunction.apply(self, self.autograd_token, *args)
+
+    # backward nodes of the B200 functions that take the whole module (activations saved, parameters
+    # read through the Parameter objects when the node runs)
+    _KEPT_NODES = ("_BlockFnBackward", "_LMHeadCEFnBackward")
+
+    def _call_keeping_graph(self, args):
+        """Run the module in the caller's graph; hooks on its single backward node re-gather the
+        parameters and bind the gradient buffer before the node runs, and reduce-scatter and release
+        them after it."""
+        handle, eng, name = self.handle, self.engine, self.name
+        eng._record_memory_event(f"measured_step_stage3_{name}_pre_allgather_forward")
+        handle.materialize("forward")
+        out = self.module(*args)
+        eng._record_memory_event(f"measured_step_stage3_{name}_after_forward")
+        handle.reshard()
+        node = out.grad_fn
+        if node is None or type(node).__name__ not in self._KEPT_NODES:
+            raise RuntimeError(f"stage 3: {name} was expected to end in one of {self._KEPT_NODES}, got {node}")
+        state = {}
+
+        def before(grad_outputs):
+            handle.materialize("backward")
+            state["buf"] = handle.begin_grad()
+
+        def after(grad_inputs, grad_outputs):
+            eng._record_memory_event(f"measured_step_stage3_{name}_after_layer_backward")
+            handle.end_grad(state.pop("buf"), ())
+            handle.reshard()
+
+        node.register_prehook(before)
+        node.register_hook(after)
+        return out
 
 
 class _PullGather:
@@ -299,7 +313,8 @@ class _PullGather:
     slot: no kernel (the GEMMs keep every SM) and no barrier (ranks do not wait for one another
     module by module).  While module ``i`` computes, module ``i+1``'s copies run on a side stream; the
     order is predicted from the previous step's sequence of (module, forward/backward) gathers, and
-    prefetching stops for the step at the first gather that does not match.
+    prefetching stops for the step at the first gather that does not match.  The streams, events
+    and copies live in the native ``PullGather`` object, so a module's gather costs one call.
 
     Safety of the barrier-free reads: a rank rewrites its store only in the optimizer step, which
     comes after the global-norm all-reduce, and every rank joins that all-reduce only after all of
@@ -307,13 +322,25 @@ class _PullGather:
     the next step's reads start only after a device barrier that follows every rank's update.
     """
 
+    CATEGORIES = ("forward_allgather", "backward_allgather")
+
     def __init__(self, engine: "ZeROStage3Optimizer", store: torch.Tensor, slots: List[torch.Tensor]) -> None:
+        from ... import ops
+        from ..collectives import simulated_collective_delay_s
+
         self.engine = engine
         self.store = store
         self.slots = slots
-        self.stream = torch.cuda.Stream(device=engine.device)
-        self.use_done: List[Optional[torch.cuda.Event]] = [None] * len(slots)   # last reader finished
-        self.write_done: List[Optional[torch.cuda.Event]] = [None] * len(slots)  # last side-stream gather
+        self.slot_ptrs = [t.data_ptr() for t in slots]
+        dev = engine.device.index if engine.device.index is not None else torch.cuda.current_device()
+        self.native = ops.load_extension().PullGather(len(slots), len(self.CATEGORIES), dev)
+        coll = engine.collectives
+        elsize = store.element_size()
+        self.where: Dict[int, Tuple[object, int, int]] = {}  # id(handle) -> (comm context, byte offset, chunk bytes)
+        for h in engine._handle_order:
+            ctx, off = coll.locate_symmetric(h.param_shard)
+            self.where[id(h)] = (ctx, off, h.chunk * elsize)
+        self.simulate = simulated_collective_delay_s(1 << 20, engine.world_size) > 0
         self.bound: List[Optional[Stage3ParamHandle]] = [None] * len(slots)
         self.pending: Dict[int, int] = {}  # id(handle) -> slot holding its prefetched parameters
         self.ring = 0
@@ -321,8 +348,12 @@ class _PullGather:
         self.pos = 0
         self.trace: List[Tuple[Stage3ParamHandle, str]] = []
         self.trace_cap = 64 * (len(engine._handle_order) + 1)
-        self.ready: Optional[torch.cuda.Event] = None
         self.prefetches = 0
+        engine.clock.add_source(self._times)
+
+    def _times(self) -> Dict[str, float]:
+        ms, _ = self.native.take_times()
+        return {c: m for c, m in zip(self.CATEGORIES, ms) if m}
 
     # -- slots ---------------------------------------------------------------------------------
     def _take_slot(self) -> Optional[int]:
@@ -335,13 +366,14 @@ class _PullGather:
                 del self.pending[key]
         return s
 
-    def _gather(self, handle: Stage3ParamHandle, slot: int, phase: str) -> None:
-        full = self.slots[slot][: handle.padded_numel]
-        eng = self.engine
-        category = "forward_allgather" if phase == "forward" else "backward_allgather"
-        with eng.clock.measure(category, handle.full_param_bytes):
-            if not eng.collectives.pull_allgather_into(full, handle.param_shard):
-                raise RuntimeError(f"stage 3 pull gather does not apply to handle {handle.name}")
+    def _issue(self, handle: Stage3ParamHandle, slot: int, phase: str, prefetch: bool) -> None:
+        cat = 0 if phase == "forward" else 1
+        self.engine.clock.count(self.CATEGORIES[cat], handle.full_param_bytes)
+        ctx, off, nbytes = self.where[id(handle)]
+        issue = self.native.prefetch if prefetch else self.native.gather_now
+        issue(ctx, slot, off, nbytes, self.slot_ptrs[slot], cat, True)
+        if self.simulate:
+            _maybe_simulate_collective_delay(nbytes, self.engine.world_size)
 
     def _prefetch(self, handle: Stage3ParamHandle, phase: str) -> None:
         # A handle that is bound right now (the last forward module is the first backward one) is
@@ -351,31 +383,20 @@ class _PullGather:
         s = self._take_slot()
         if s is None:
             return
-        st = self.stream
-        for ev in (self.use_done[s], self.ready):
-            if ev is not None:
-                st.wait_event(ev)
-        with torch.cuda.stream(st):
-            self._gather(handle, s, phase)
-            ev = torch.cuda.Event()
-            ev.record(st)
-        self.write_done[s] = ev
+        self._issue(handle, s, phase, prefetch=True)
         self.pending[id(handle)] = s
         self.prefetches += 1
 
     # -- module calls --------------------------------------------------------------------------
     def materialize(self, handle: Stage3ParamHandle, phase: str) -> Optional[torch.Tensor]:
-        cur = torch.cuda.current_stream(self.engine.device)
         s = self.pending.pop(id(handle), None)
         if s is not None:
-            cur.wait_event(self.write_done[s])
+            self.native.acquire(s)
         else:
             s = self._take_slot()
             if s is None:
                 return None
-            if self.write_done[s] is not None:  # a dropped prefetch may still be writing this slot
-                cur.wait_event(self.write_done[s])
-            self._gather(handle, s, phase)
+            self._issue(handle, s, phase, prefetch=False)
         self.bound[s] = handle
         self._advance(handle, phase)
         return self.slots[s][: handle.padded_numel]
@@ -383,9 +404,7 @@ class _PullGather:
     def release(self, handle: Stage3ParamHandle) -> None:
         for s, h in enumerate(self.bound):
             if h is handle:
-                ev = torch.cuda.Event()
-                ev.record(torch.cuda.current_stream(self.engine.device))
-                self.use_done[s] = ev
+                self.native.release(s)
                 self.bound[s] = None
 
     def _advance(self, handle: Stage3ParamHandle, phase: str) -> None:
@@ -408,16 +427,14 @@ class _PullGather:
 
     def before_store_write(self) -> None:
         """Every copy issued so far has finished before the compute stream goes on."""
-        torch.cuda.current_stream(self.engine.device).wait_stream(self.stream)
+        self.native.join()
         self.pending.clear()
 
     def after_store_write(self, next_plan: bool) -> None:
         """Barrier so that no rank reads a shard before its owner has rewritten it; then prefetch the
         first module of the next step."""
         self.engine.collectives.barrier()
-        ev = torch.cuda.Event()
-        ev.record(torch.cuda.current_stream(self.engine.device))
-        self.ready = ev
+        self.native.mark_ready()
         if next_plan:
             self.plan = list(self.trace) if 0 < len(self.trace) < self.trace_cap else None
         self.trace = []
