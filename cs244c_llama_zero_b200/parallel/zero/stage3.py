@@ -465,24 +465,39 @@ class ZeROStage3Optimizer(ZeROEngineBase):
         self._stage_slot = 0
         self._stage_grads: Optional[torch.Tensor] = None
         alloc = getattr(self.collectives, "alloc", None)
+        use_pull = False
         if alloc is not None and self.world_size > 1 and self.device.type == "cuda":
             largest = max(h.padded_numel for h in self._handle_order)
             self._stage_params = [alloc(largest, self.param_dtype) for _ in range(2)]
             self._stage_grads = alloc(largest, torch.float32)
-            if getattr(self.collectives, "supports_pull_gather", False) and os.environ.get("ZB_STAGE3_PULL", "1") != "0":
-                self._setup_pull_gather(alloc)
+            use_pull = (getattr(self.collectives, "supports_pull_gather", False)
+                        and os.environ.get("ZB_STAGE3_PULL", "1") != "0")
+        self._flat: Optional[Dict[str, torch.Tensor]] = None
+        if all(h.param_dtype == self.param_dtype for h in self._handle_order):
+            self._flatten_shards(alloc if use_pull else None)
+            if use_pull:
+                self._pull = _PullGather(self, self._flat["param_shard"], self._stage_params)
+                self._pull.after_store_write(next_plan=False)
 
-    def _setup_pull_gather(self, alloc) -> None:
-        """Move every handle's model-dtype shard into one symmetric store read by the peers' copy engines."""
-        store = alloc(sum(h.chunk for h in self._handle_order), self.param_dtype)
+    def _flatten_shards(self, alloc) -> None:
+        """Put every handle's shards (fp32 master, moments, gradient; model-dtype parameters) at the
+        same offsets of one flat buffer each, so that the norm, AdamW and zeroing run once per step
+        over all handles.  With ``alloc`` the parameter buffer is symmetric memory: the store that the
+        peers' copy engines read in the per-module gathers."""
+        total = sum(h.chunk for h in self._handle_order)
+        dev = self.device
+        flat = {name: torch.zeros(total, dtype=torch.float32, device=dev)
+                for name in ("local_master_param_shard", "exp_avg", "exp_avg_sq", "grad_shard")}
+        flat["param_shard"] = (alloc(total, self.param_dtype) if alloc is not None
+                               else torch.empty(total, dtype=self.param_dtype, device=dev))
         off = 0
         for h in self._handle_order:
-            view = store[off : off + h.chunk]
-            view.copy_(h.param_shard)
-            h.param_shard = view
+            for name, buf in flat.items():
+                view = buf[off : off + h.chunk]
+                view.copy_(getattr(h, name))
+                setattr(h, name, view)
             off += h.chunk
-        self._pull = _PullGather(self, store, self._stage_params)
-        self._pull.after_store_write(next_plan=False)
+        self._flat = flat
 
     def _staging_params(self, numel: int, dtype: torch.dtype) -> Optional[torch.Tensor]:
         if not self._stage_params or dtype != self._stage_params[0].dtype or self._pull is not None:
@@ -550,16 +565,22 @@ class ZeROStage3Optimizer(ZeROEngineBase):
 
     def zero_grad(self) -> None:
         self.clock.reset()
-        for h in self._handle_order:
-            h.reset_grad()
+        if self._flat is not None:
+            self._flat["grad_shard"].zero_()
+        else:
+            for h in self._handle_order:
+                h.reset_grad()
         for p in self.model.parameters():
             p.grad = None
         self._reshard_all_params()
 
     def _global_norm(self) -> torch.Tensor:
-        total = torch.zeros(1, dtype=torch.float32, device=self.device)
-        for h in self._handle_order:
-            total += sum_of_squares(h.grad_shard)
+        if self._flat is not None:
+            total = sum_of_squares(self._flat["grad_shard"]).reshape(1)
+        else:
+            total = torch.zeros(1, dtype=torch.float32, device=self.device)
+            for h in self._handle_order:
+                total += sum_of_squares(h.grad_shard)
         if dist.is_available() and dist.is_initialized() and self.world_size > 1:
             dist.all_reduce(total)
         return total.sqrt().reshape(())
@@ -572,9 +593,14 @@ class ZeROStage3Optimizer(ZeROEngineBase):
         scale = clip_coefficient(norm, max_grad_norm)
         self.step_count += 1
         with self.clock.measure("optimizer"):
-            for h in self._handle_order:
-                adamw_update_(h.local_master_param_shard, h.exp_avg, h.exp_avg_sq, h.grad_shard, self.adam,
-                              self.step_count, grad_scale=scale, param_out=h.param_shard)
+            if self._flat is not None:
+                f = self._flat
+                adamw_update_(f["local_master_param_shard"], f["exp_avg"], f["exp_avg_sq"], f["grad_shard"], self.adam,
+                              self.step_count, grad_scale=scale, param_out=f["param_shard"])
+            else:
+                for h in self._handle_order:
+                    adamw_update_(h.local_master_param_shard, h.exp_avg, h.exp_avg_sq, h.grad_shard, self.adam,
+                                  self.step_count, grad_scale=scale, param_out=h.param_shard)
         self._reshard_all_params()
         if self._pull is not None:
             self._pull.after_store_write(next_plan=True)
