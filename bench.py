@@ -43,6 +43,8 @@ def parse_args(argv=None) -> argparse.Namespace:
     p.add_argument("--seq-len", type=int, default=1024)
     p.add_argument("--collective-impl", type=str, default="auto", help="auto | torch | nvls | p2p")
     p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--model-size", type=str, default="baseline-small",
+                   help="model preset: baseline-small (the headline config), baseline-1.3b, baseline-7b, ...")
     args = p.parse_args(argv)
     args.warmup = max(3, args.warmup)
     args.stage_list = [int(s) for s in args.stages.split(",") if s.strip()]
@@ -115,6 +117,17 @@ class ClockSampler:
 
 
 # ----------------------------------------------------------------------------------- helpers
+def model_desc(size: str) -> str:
+    if size == "baseline-small":
+        return MODEL_DESC
+    from cs244c_llama_zero_b200.models import BASELINE_VOCAB_SIZE
+    from cs244c_llama_zero_b200.models.config import build_config
+
+    c = build_config(size, vocab_size=BASELINE_VOCAB_SIZE)
+    return (f"{size} LLaMA d{c.dim}/L{c.n_layers}/H{c.n_heads}/KV{c.n_kv_heads}/ffn{c.ffn_dim}/V{c.vocab_size}"
+            f" ({'tied' if c.tie_word_embeddings else 'untied'} embeddings)")
+
+
 def dist_env():
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -215,7 +228,7 @@ def run_mine(args) -> None:
     headline_ms = None
     tokens_per_step = args.batch_size * args.seq_len * world
     for stage in args.stage_list:
-        sess = TrainSession(SessionConfig(model_size="baseline-small", vocab_size=BASELINE_VOCAB_SIZE,
+        sess = TrainSession(SessionConfig(model_size=args.model_size, vocab_size=BASELINE_VOCAB_SIZE,
                                           seq_len=args.seq_len, batch_size=args.batch_size, zero_stage=stage,
                                           collective_impl=impl, backend="b200"))
         host = random_batches(4, args.batch_size, args.seq_len, BASELINE_VOCAB_SIZE, seed=1234 + rank * 100 + stage)
@@ -276,7 +289,7 @@ def run_mine(args) -> None:
     rec.update({
         "value": head["tokens_per_s"],
         "ms_per_step": headline_ms,
-        "config": {"model": MODEL_DESC, "global_batch": args.batch_size * world, "micro_batch_per_gpu": args.batch_size,
+        "config": {"model": model_desc(args.model_size), "global_batch": args.batch_size * world, "micro_batch_per_gpu": args.batch_size,
                    "seq_len": args.seq_len, "grad_accum": 1, "parallelism": f"dp{world}",
                    "zero_stage": args.headline_stage, "collective_impl": impl,
                    "l2": "no flush: each step touches >2 GB (activations, 1.2 GB fp32 optimizer state) vs 126 MB L2"},
