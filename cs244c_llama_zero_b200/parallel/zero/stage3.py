@@ -150,6 +150,10 @@ class Stage3ParamHandle:
         return buf
 
     def end_grad(self, buf: torch.Tensor, param_grads: Sequence[Optional[torch.Tensor]]) -> None:
+        if self.device.type == "cuda":
+            from ...ops import functional as B
+
+            B.join_weight_grads(self.device)  # weight-gradient GEMMs may still run on their side stream
         for p, g in zip(self.meta.params, param_grads):
             if g is not None:
                 p.main_grad.add_(g.to(torch.float32))
