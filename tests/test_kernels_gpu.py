@@ -213,7 +213,9 @@ def _attn_ref(qkv, B, S, H, KV, hd):
 
 
 @pytest.mark.parametrize("B,S,H,KV,hd", [(2, 256, 4, 2, 64), (1, 512, 4, 4, 128), (2, 384, 6, 2, 64),
-                                         (1, 256, 4, 2, 128)])
+                                         (1, 256, 4, 2, 128),
+                                         # more work items than SMs: each persistent CTA walks several
+                                         (4, 1024, 12, 4, 64), (2, 1024, 16, 8, 128)])
 def test_attention_forward_and_backward(C, B, S, H, KV, hd):
     from cs244c_llama_zero_b200.ops.functional import attention_backward, attention_forward, rope_tables
 
