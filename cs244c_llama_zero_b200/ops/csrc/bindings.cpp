@@ -162,6 +162,32 @@ void linear_wgrad(Tensor dy, Tensor x, Tensor dw, int64_t splits, int64_t bn) {
   b200::gemm_launch(op, p, b200::EPI_ACC_F32, true, true, (int)bn, cur_stream());
 }
 
+// dx = dy @ w and dw += dy^T @ x in one persistent launch (the two GEMMs of a linear layer's
+// backward pass share dy and are independent of each other).
+void linear_dgrad_wgrad(Tensor dy, Tensor w, Tensor x, Tensor dx, Tensor dw, int64_t splits) {
+  check_bf16_2d(dy, "dy");
+  check_bf16_2d(w, "w");
+  check_bf16_2d(x, "x");
+  check_bf16_2d(dx, "dx");
+  check_f32(dw, "dw");
+  const int T = dy.size(0), out = dy.size(1), in = w.size(1);
+  TORCH_CHECK(w.size(0) == out && dx.size(0) == T && dx.size(1) == in, "linear_dgrad_wgrad: dgrad shape mismatch");
+  TORCH_CHECK(x.size(0) == T && x.size(1) == in, "linear_dgrad_wgrad: x shape mismatch");
+  TORCH_CHECK(dw.dim() == 2 && dw.size(0) == out && dw.size(1) == in && dw.stride(1) == 1, "linear_dgrad_wgrad: dw shape");
+  TORCH_CHECK(dw.stride(0) % 4 == 0 && reinterpret_cast<uintptr_t>(dw.data_ptr()) % 16 == 0, "dw alignment");
+  c10::cuda::CUDAGuard g(dy.device());
+  auto p0 = base_params(T, in, out);
+  p0.C = reinterpret_cast<__nv_bfloat16*>(dx.data_ptr());
+  p0.ldc = dx.stride(0);
+  b200::GemmOperands op0{dy.data_ptr(), w.data_ptr(), (uint64_t)dy.stride(0), (uint64_t)w.stride(0)};
+  auto p1 = base_params(out, in, T);
+  p1.C32 = dw.data_ptr<float>();
+  p1.ldc32 = dw.stride(0);
+  p1.splits = splits > 0 ? (int)splits : 0;
+  b200::GemmOperands op1{dy.data_ptr(), x.data_ptr(), (uint64_t)dy.stride(0), (uint64_t)x.stride(0)};
+  b200::gemm_launch_dgrad_wgrad(op0, p0, op1, p1, cur_stream());
+}
+
 // Generic entry for tests: C = A op B with explicit majors.
 void gemm_raw(Tensor A, Tensor B, Tensor C, int64_t M, int64_t N, int64_t K, bool a_mn, bool b_mn, int64_t bn,
               int64_t splits) {
@@ -653,6 +679,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("qkv_rope_fwd", &qkv_rope_fwd);
   m.def("swiglu_fwd", &swiglu_fwd);
   m.def("linear_dgrad", &linear_dgrad, py::arg("dy"), py::arg("w"), py::arg("dx"), py::arg("bn") = 0);
+  m.def("linear_dgrad_wgrad", &linear_dgrad_wgrad, py::arg("dy"), py::arg("w"), py::arg("x"), py::arg("dx"),
+        py::arg("dw"), py::arg("splits") = 0);
   m.def("swiglu_dgrad", &swiglu_dgrad);
   m.def("linear_wgrad", &linear_wgrad, py::arg("dy"), py::arg("x"), py::arg("dw"), py::arg("splits") = 0,
         py::arg("bn") = 0);

@@ -46,6 +46,9 @@ struct GemmParams {
   int ld_aux_in;
   int ffn;
   DeviceErrors* errs;
+  // Grouped launches (gemm_launch_dgrad_wgrad): units [0, grp_units_first) belong to problem
+  // grp_first, the rest (up to grp_units_total) to the other one.
+  int grp_first, grp_units_first, grp_units_total;
 };
 
 struct GemmTile {
@@ -65,5 +68,12 @@ CUtensorMap make_tmap_2d(CUtensorMapDataType dtype, int elem_bytes, const void* 
 CUtensorMap make_tmap_bf16_2d(const void* base, uint64_t inner, uint64_t outer, uint64_t row_stride_elems,
                               uint32_t box_inner, uint32_t box_outer);
 void gemm_launch(const GemmOperands& op, GemmParams p, int epi, bool a_mn, bool b_mn, int bn, cudaStream_t stream);
+// One persistent launch computing two independent GEMMs of a linear layer's backward pass:
+//   problem 0: dX[M0, N0] = dY[M0, K0] @ W[K0, N0]          (A K-major, B MN-major, bf16 store)
+//   problem 1: dW[M1, N1] += dY^T[M1, K1] @ X[K1, N1]       (A MN-major, B MN-major, fp32 add-reduce)
+// Their tiles are dealt together, longest first, so neither one's partial last wave idles SMs.
+// splits1 <= 0 chooses problem 1's K-split for the combined schedule.
+void gemm_launch_dgrad_wgrad(const GemmOperands& op0, GemmParams p0, const GemmOperands& op1, GemmParams p1,
+                             cudaStream_t stream);
 
 }  // namespace b200

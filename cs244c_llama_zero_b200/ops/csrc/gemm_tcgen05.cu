@@ -31,6 +31,7 @@
 
 #include <algorithm>
 #include <mutex>
+#include <vector>
 
 #include "common.cuh"
 #include "gemm.h"
@@ -107,14 +108,59 @@ __device__ __forceinline__ void publish_chunk(const CUtensorMap* map, uint8_t* b
   }
 }
 
-template <int BN, bool A_MN, bool B_MN, int EPI, int CG>
+// One work unit: a (tile, K-range) of problem `prob` (always 0 outside grouped launches).
+struct Unit {
+  int prob, tm, tn, kb0, kb1;
+};
+
+// The k-th unit of CTA group g out of G: strided for single problems; boustrophedon for grouped
+// launches, whose unit list runs from the longest units to the shortest.
+template <bool GROUPED>
+__device__ __forceinline__ int unit_index(int k, int g, int G) {
+  if constexpr (GROUPED)
+    return k * G + ((k & 1) ? (G - 1 - g) : g);
+  else
+    return g + k * G;
+}
+
+template <bool GROUPED>
+__device__ __forceinline__ Unit decode_unit(int u, const GemmParams& p, const GemmParams& p1) {
+  int prob = 0, v = u;
+  if constexpr (GROUPED) {
+    if (u < p.grp_units_first) {
+      prob = p.grp_first;
+    } else {
+      prob = 1 - p.grp_first;
+      v = u - p.grp_units_first;
+    }
+  }
+  const int splits = prob ? p1.splits : p.splits;
+  const int tiles_m = prob ? p1.tiles_m : p.tiles_m;
+  const int kbs = prob ? p1.k_blocks_per_split : p.k_blocks_per_split;
+  const int total_kb = prob ? p1.total_k_blocks : p.total_k_blocks;
+  const int split = v % splits, tile = v / splits;
+  Unit d;
+  d.prob = prob;
+  d.tm = tile % tiles_m;
+  d.tn = tile / tiles_m;
+  d.kb0 = split * kbs;
+  d.kb1 = min(total_kb, d.kb0 + kbs);
+  return d;
+}
+
+// GROUPED: problem 0 is described by the template (A_MN, EPI = EPI_STORE, maps tmA/tmB/tmC, params
+// p) and problem 1 is a weight gradient (MN-major A, EPI_ACC_F32, maps tmX/tmY/tmZ, params p1).
+template <int BN, bool A_MN, bool B_MN, int EPI, int CG, bool GROUPED = false>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                 const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmX,
-                const __grid_constant__ CUtensorMap tmY, GemmParams p) {
+                const __grid_constant__ CUtensorMap tmY, const __grid_constant__ CUtensorMap tmZ,
+                const __grid_constant__ GemmParams p, const __grid_constant__ GemmParams p1) {
   using Cfg = GemmCfg<BN, CG>;
   constexpr int STAGES = Cfg::STAGES;
   constexpr uint32_t IDESC = idesc_bf16_f32(BM * CG, BN, A_MN, B_MN);
+  constexpr uint32_t IDESC_AMN = idesc_bf16_f32(BM * CG, BN, true, B_MN);  // grouped problem 1
+  static_assert(!GROUPED || (EPI == EPI_STORE && !A_MN && B_MN), "grouped launches pair a dgrad with a wgrad");
   static_assert(CG == 1 || CG == 2, "CTA group of 1 or 2");
   static_assert(CG == 1 || !B_MN || (BN / 2) % 64 == 0, "pair tiles with an MN-major B need BN/2 % 64 == 0");
 
@@ -162,7 +208,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_base_slot;
 
-  const int total_units = p.tiles_m * p.tiles_n * p.splits;
+  const int total_units = GROUPED ? p.grp_units_total : p.tiles_m * p.tiles_n * p.splits;
 
   if (warp == 0) {
     if (lane == 0) {
@@ -171,14 +217,17 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
-      for (int u = group_id; u < total_units && ok; u += n_groups) {
-        const int split = u % p.splits;
-        const int tile = u / p.splits;
-        const int tm = tile % p.tiles_m, tn = tile / p.tiles_m;
-        const int m0 = tm * BM * CG + rank * BM;
-        const int kb0 = split * p.k_blocks_per_split;
-        const int kb1 = min(p.total_k_blocks, kb0 + p.k_blocks_per_split);
-        for (int kb = kb0; kb < kb1; ++kb) {
+      for (int ku = 0; ok; ++ku) {
+        const int u = unit_index<GROUPED>(ku, group_id, n_groups);
+        if (u >= total_units) break;
+        const Unit d = decode_unit<GROUPED>(u, p, p1);
+        const int tn = d.tn;
+        const int m0 = d.tm * BM * CG + rank * BM;
+        const bool p1u = GROUPED && d.prob == 1;
+        const bool a_mn = GROUPED ? p1u : A_MN;
+        const CUtensorMap* mapA = p1u ? &tmX : &tmA;
+        const CUtensorMap* mapB = p1u ? &tmY : &tmB;
+        for (int kb = d.kb0; kb < d.kb1; ++kb) {
           if (!mbar_wait_bounded(&empty_bar[stage], phase ^ 1u, abort_flag, p.errs, kErrGemmWait, 0)) {
             ok = false;
             break;
@@ -195,11 +244,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             else
               tma_load_2d(dst, map, &full_bar[stage], c0, c1);
           };
-          if constexpr (!A_MN) {
-            load(sA, &tmA, k0, m0);
+          if (!a_mn) {
+            load(sA, mapA, k0, m0);
           } else {
-            load(sA, &tmA, m0, k0);
-            load(sA + 8192, &tmA, m0 + 64, k0);
+            load(sA, mapA, m0, k0);
+            load(sA + 8192, mapA, m0 + 64, k0);
           }
           if constexpr (EPI == EPI_SWIGLU) {
             const int g0 = tn * (BN / 2);
@@ -210,10 +259,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
               load(sB + (BN / 2) * 128, &tmB, k0, p.ffn + g0);
             }
           } else if constexpr (!B_MN) {
-            load(sB, &tmB, k0, tn * BN + rank * (BN / CG));
+            load(sB, mapB, k0, tn * BN + rank * (BN / CG));
           } else {
 #pragma unroll
-            for (int j = 0; j < BN / CG / 64; ++j) load(sB + j * 8192, &tmB, tn * BN + rank * (BN / CG) + 64 * j, k0);
+            for (int j = 0; j < BN / CG / 64; ++j) load(sB + j * 8192, mapB, tn * BN + rank * (BN / CG) + 64 * j, k0);
           }
           if (++stage == STAGES) {
             stage = 0;
@@ -228,10 +277,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       uint32_t phase = 0;
       int t = 0;
       bool ok = true;
-      for (int u = group_id; u < total_units && ok; u += n_groups, ++t) {
-        const int split = u % p.splits;
-        const int kb0 = split * p.k_blocks_per_split;
-        const int kb1 = min(p.total_k_blocks, kb0 + p.k_blocks_per_split);
+      for (int ku = 0; ok; ++ku, ++t) {
+        const int u = unit_index<GROUPED>(ku, group_id, n_groups);
+        if (u >= total_units) break;
+        const Unit d = decode_unit<GROUPED>(u, p, p1);
+        const int kb0 = d.kb0, kb1 = d.kb1;
+        const bool a_mn = GROUPED ? d.prob == 1 : A_MN;
+        const uint32_t idesc = GROUPED ? (a_mn ? IDESC_AMN : IDESC) : IDESC;
         const int acc = t & 1;
         const uint32_t acc_phase = (t >> 1) & 1;
         if (!mbar_wait_bounded(&tempty_bar[acc], acc_phase ^ 1u, abort_flag, p.errs, kErrGemmWait, 1)) break;
@@ -247,14 +299,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           const uint32_t b_addr = a_addr + A_STAGE_BYTES;
 #pragma unroll
           for (int k = 0; k < BK / 16; ++k) {
-            const uint64_t adesc = A_MN ? smem_desc_sw128(a_addr + k * 2048, 8192, 1024)
+            const uint64_t adesc = a_mn ? smem_desc_sw128(a_addr + k * 2048, 8192, 1024)
                                         : smem_desc_sw128(a_addr + k * 32, 16, 1024);
             const uint64_t bdesc = B_MN ? smem_desc_sw128(b_addr + k * 2048, 8192, 1024)
                                         : smem_desc_sw128(b_addr + k * 32, 16, 1024);
             if constexpr (CG == 2)
-              tc_mma_f16_pair(d_tmem, adesc, bdesc, IDESC, (kb > kb0 || k > 0) ? 1u : 0u);
+              tc_mma_f16_pair(d_tmem, adesc, bdesc, idesc, (kb > kb0 || k > 0) ? 1u : 0u);
             else
-              tc_mma_f16(d_tmem, adesc, bdesc, IDESC, (kb > kb0 || k > 0) ? 1u : 0u);
+              tc_mma_f16(d_tmem, adesc, bdesc, idesc, (kb > kb0 || k > 0) ? 1u : 0u);
           }
           if constexpr (CG == 2)
             tc_commit_pair(&empty_bar[stage], 0x3);  // frees the stage in both CTAs
@@ -287,14 +339,16 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     int bsel = 0;
     int t = 0;
     bool ok = true;
-    for (int u = group_id; u < total_units && ok; u += n_groups, ++t) {
-      const int tile = u / p.splits;
-      const int tm = tile % p.tiles_m, tn = tile / p.tiles_m;
+    for (int ku = 0; ok; ++ku, ++t) {
+      const int u = unit_index<GROUPED>(ku, group_id, n_groups);
+      if (u >= total_units) break;
+      const Unit d = decode_unit<GROUPED>(u, p, p1);
+      const int tm = d.tm, tn = d.tn;
       const int acc = t & 1;
       const uint32_t acc_phase = (t >> 1) & 1;
       const int row0 = tm * BM * CG + rank * BM + q * 32;  // TMA row coordinate of this warp's chunk
       const int m = row0 + lane;
-      const bool row_ok = m < p.M;
+      const bool row_ok = m < ((GROUPED && d.prob == 1) ? p1.M : p.M);
 
       if constexpr (EPI == EPI_RESIDUAL) {
         // Prefetch the residual for the first two chunks while the main loop still runs.
@@ -311,7 +365,25 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       tc_fence_after();
       const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + acc * BN;
 
-      if constexpr (EPI == EPI_STORE || EPI == EPI_RESIDUAL) {
+      // fp32 add-reduction of the accumulator (weight gradients; grouped problem 1)
+      auto acc_f32_epilogue = [&](const CUtensorMap* map) {
+        const int n0 = tn * BN + wg * (BN / 2);
+#pragma unroll 1
+        for (int c = 0; c < BN / 2; c += 16) {
+          uint32_t r[16];
+          tmem_ld_32x32b_x16(tbase + wg * (BN / 2) + c, r);
+          tc_wait_ld();
+          uint8_t* buf = acquire_chunk(stg, bsel);
+#pragma unroll
+          for (int j = 0; j < 4; ++j)
+            *reinterpret_cast<uint4*>(buf + chunk_off(lane, j)) =
+                make_uint4(r[4 * j], r[4 * j + 1], r[4 * j + 2], r[4 * j + 3]);
+          publish_chunk(map, buf, n0 + c, row0, true);
+        }
+      };
+      if (GROUPED && d.prob == 1) {
+        if constexpr (GROUPED) acc_f32_epilogue(&tmZ);
+      } else if constexpr (EPI == EPI_STORE || EPI == EPI_RESIDUAL) {
         const int n0 = tn * BN + wg * (BN / 2);
 #pragma unroll 1
         for (int i = 0; i < BN / 64; ++i) {
@@ -358,19 +430,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           }
         }
       } else if constexpr (EPI == EPI_ACC_F32) {
-        const int n0 = tn * BN + wg * (BN / 2);
-#pragma unroll 1
-        for (int c = 0; c < BN / 2; c += 16) {
-          uint32_t r[16];
-          tmem_ld_32x32b_x16(tbase + wg * (BN / 2) + c, r);
-          tc_wait_ld();
-          uint8_t* buf = acquire_chunk(stg, bsel);
-#pragma unroll
-          for (int j = 0; j < 4; ++j)
-            *reinterpret_cast<uint4*>(buf + chunk_off(lane, j)) =
-                make_uint4(r[4 * j], r[4 * j + 1], r[4 * j + 2], r[4 * j + 3]);
-          publish_chunk(&tmC, buf, n0 + c, row0, true);
-        }
+        acc_f32_epilogue(&tmC);
       } else if constexpr (EPI == EPI_ROPE) {
         const int n0 = tn * BN;
         const int half = p.head_dim >> 1;
@@ -610,7 +670,7 @@ static void launch_impl(const GemmOperands& op, GemmParams p, cudaStream_t strea
   const int units = p.tiles_m * p.tiles_n * p.splits;
   const int groups = std::max(1, std::min(units, num_sms() / CG));
   if constexpr (CG == 1) {
-    kernel<<<groups, NUM_THREADS, Cfg::SMEM_BYTES, stream>>>(tmA, tmB, tmC, tmX, tmY, p);
+    kernel<<<groups, NUM_THREADS, Cfg::SMEM_BYTES, stream>>>(tmA, tmB, tmC, tmX, tmY, tmA, p, p);
   } else {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(groups * CG, 1, 1);
@@ -624,7 +684,7 @@ static void launch_impl(const GemmOperands& op, GemmParams p, cudaStream_t strea
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    B200_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kernel, tmA, tmB, tmC, tmX, tmY, p));
+    B200_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kernel, tmA, tmB, tmC, tmX, tmY, tmA, p, p));
   }
   B200_CUDA_CHECK(cudaGetLastError());
   count_launch();
@@ -747,6 +807,102 @@ void gemm_launch(const GemmOperands& op, GemmParams p, int epi, bool a_mn, bool 
     }
   }
   B200_CHECK(false, "unsupported GEMM operand-major / epilogue combination");
+}
+
+// Tile / split bookkeeping of one problem for a given tile shape (the launcher's fields).
+static void fill_schedule(GemmParams& q, int bn, int cg, int splits) {
+  q.tiles_m = (q.M + BM * cg - 1) / (BM * cg);
+  q.tiles_n = (q.N + bn - 1) / bn;
+  q.total_k_blocks = (q.K + BK - 1) / BK;
+  q.splits = std::max(1, std::min(splits, q.total_k_blocks));
+  q.k_blocks_per_split = (q.total_k_blocks + q.splits - 1) / q.splits;
+  q.splits = (q.total_k_blocks + q.k_blocks_per_split - 1) / q.k_blocks_per_split;
+}
+
+// Makespan (in k-blocks, +3 per unit for the pipeline fill) of the grouped boustrophedon deal.
+static long grouped_makespan(const GemmParams& p0, const GemmParams& p1, int G, int* first_out) {
+  const long units0 = (long)p0.tiles_m * p0.tiles_n * p0.splits, units1 = (long)p1.tiles_m * p1.tiles_n * p1.splits;
+  const int c0 = p0.k_blocks_per_split + 3, c1 = p1.k_blocks_per_split + 3;
+  const int first = c1 > c0 ? 1 : 0;
+  const long n_first = first ? units1 : units0;
+  const int cost_first = first ? c1 : c0, cost_second = first ? c0 : c1;
+  std::vector<long> load(G, 0);
+  const long total = units0 + units1;
+  for (long u = 0; u < total; ++u) {
+    const long k = u / G, r = u % G;
+    const long g = (k & 1) ? (G - 1 - r) : r;
+    load[g] += (u < n_first) ? cost_first : cost_second;
+  }
+  *first_out = first;
+  return *std::max_element(load.begin(), load.end());
+}
+
+void gemm_launch_dgrad_wgrad(const GemmOperands& op0, GemmParams p0, const GemmOperands& op1, GemmParams p1,
+                             cudaStream_t stream) {
+  constexpr int BNG = 256, CGG = 2;
+  using Cfg = GemmCfg<BNG, CGG>;
+  B200_CHECK(p0.N % 8 == 0 && p1.N % 8 == 0 && p0.K % 8 == 0 && p1.M % 8 == 0,
+             "grouped dgrad/wgrad: N, K (dgrad) and M (wgrad) must be multiples of 8");
+  const int G = std::max(1, num_sms() / CGG);
+  fill_schedule(p0, BNG, CGG, 1);
+  int first = 0;
+  if (p1.splits > 0) {
+    fill_schedule(p1, BNG, CGG, p1.splits);
+    grouped_makespan(p0, p1, G, &first);
+  } else {
+    long best = -1;
+    int best_split = 1;
+    const int kb1 = (p1.K + BK - 1) / BK;
+    for (int s : {1, 2, 3, 4, 6, 8, 12, 16}) {
+      if (s > 1 && kb1 / s < 4) break;
+      GemmParams q = p1;
+      fill_schedule(q, BNG, CGG, s);
+      int f = 0;
+      const long span = grouped_makespan(p0, q, G, &f);
+      if (best < 0 || span < best) {
+        best = span;
+        best_split = s;
+      }
+    }
+    fill_schedule(p1, BNG, CGG, best_split);
+    grouped_makespan(p0, p1, G, &first);
+  }
+  const long units0 = (long)p0.tiles_m * p0.tiles_n * p0.splits, units1 = (long)p1.tiles_m * p1.tiles_n * p1.splits;
+  p0.grp_first = first;
+  p0.grp_units_first = (int)(first ? units1 : units0);
+  p0.grp_units_total = (int)(units0 + units1);
+  p0.errs = p1.errs = device_errors_ptr();
+
+  auto kernel = gemm_kernel<BNG, false, true, EPI_STORE, CGG, true>;
+  static bool configured = false;
+  if (!configured) {
+    B200_CUDA_CHECK(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_BYTES));
+    configured = true;
+  }
+  // problem 0: A = dY [M0, K0] K-major, B = W [K0, N0] MN-major, C = dX (bf16)
+  const CUtensorMap tmA = make_tmap_bf16_2d(op0.A, (uint64_t)p0.K, (uint64_t)p0.M, op0.lda, 64, BM);
+  const CUtensorMap tmB = make_tmap_bf16_2d(op0.B, (uint64_t)p0.N, (uint64_t)p0.K, op0.ldb, 64, 64);
+  const CUtensorMap tmC = epi_map_bf16(p0.C, p0.M, p0.N, p0.ldc);
+  // problem 1: A = dY^T as [K1, M1] MN-major, B = X [K1, N1] MN-major, C = dW (fp32, accumulated)
+  const CUtensorMap tmX = make_tmap_bf16_2d(op1.A, (uint64_t)p1.M, (uint64_t)p1.K, op1.lda, 64, 64);
+  const CUtensorMap tmY = make_tmap_bf16_2d(op1.B, (uint64_t)p1.N, (uint64_t)p1.K, op1.ldb, 64, 64);
+  const CUtensorMap tmZ = epi_map_f32(p1.C32, p1.M, p1.N, p1.ldc32);
+  const int groups = std::max(1, std::min(p0.grp_units_total, G));
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(groups * CGG, 1, 1);
+  cfg.blockDim = dim3(NUM_THREADS, 1, 1);
+  cfg.dynamicSmemBytes = Cfg::SMEM_BYTES;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = CGG;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  B200_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kernel, tmA, tmB, tmC, tmX, tmY, tmZ, p0, p1));
+  B200_CUDA_CHECK(cudaGetLastError());
+  count_launch();
 }
 
 }  // namespace b200

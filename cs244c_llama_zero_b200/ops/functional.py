@@ -273,6 +273,24 @@ class _WgradLauncher:
             _WGRAD_CALLBACK_QUEUED[0] = True
 
 
+def _grouped_backward_enabled() -> bool:
+    import os
+
+    return os.environ.get("ZB_GROUPED_BWD", "1") != "0"
+
+
+def _dgrad_and_wgrad(dy: torch.Tensor, w: torch.Tensor, x: torch.Tensor, dx: torch.Tensor, dw: torch.Tensor,
+                     wgrad: "_WgradLauncher") -> None:
+    """dx = dy @ w and dw += dy^T @ x: one grouped persistent GEMM launch (both problems' tiles dealt
+    together), or two launches when the weight gradient runs on its own stream."""
+    C = _ext()
+    if wgrad.side is None and _grouped_backward_enabled():
+        C.linear_dgrad_wgrad(dy, w, x, dx, dw)
+        return
+    C.linear_dgrad(dy, w, dx)
+    wgrad(dy, x, dw)
+
+
 _GRAD_READY_HOOKS: List = []
 
 
@@ -349,24 +367,21 @@ class _BlockFn(torch.autograd.Function):
         sink_d = _GradSink([wd])
         wgrad(dy3, act, sink_d.buffer)
         dh2 = torch.empty_like(xf)
-        C.linear_dgrad(dgu, w_gu, dh2)
         sink_gu = _GradSink([wg, wu])
-        wgrad(dgu, h2, sink_gu.buffer)
+        _dgrad_and_wgrad(dgu, w_gu, h2, dh2, sink_gu.buffer, wgrad)
         del dgu
         dx2 = torch.empty_like(xf)
         sink_post = _GradSink([w_post])
         C.rmsnorm_bwd(dh2, x2, w_post.detach(), rstd2, dy3, dx2, sink_post.buffer.view(-1))
         # attention
         dattn = torch.empty_like(attn)
-        C.linear_dgrad(dx2, wo.detach(), dattn)
         sink_o = _GradSink([wo])
-        wgrad(dx2, attn, sink_o.buffer)
+        _dgrad_and_wgrad(dx2, wo.detach(), attn, dattn, sink_o.buffer, wgrad)
         dqkv = torch.empty_like(qkv)
         attention_backward(qkv, attn, dattn, lse, B, S, H, KV, hd, dqkv, cos, sin)
         dh1 = torch.empty_like(xf)
-        C.linear_dgrad(dqkv, w_qkv, dh1)
         sink_qkv = _GradSink([wq, wk, wv])
-        wgrad(dqkv, h1, sink_qkv.buffer)
+        _dgrad_and_wgrad(dqkv, w_qkv, h1, dh1, sink_qkv.buffer, wgrad)
         dx = torch.empty_like(xf)
         sink_in = _GradSink([w_in])
         C.rmsnorm_bwd(dh1, xf, w_in.detach(), rstd1, dx2, dx, sink_in.buffer.view(-1))
@@ -425,9 +440,8 @@ class _LMHeadCEFn(torch.autograd.Function):
         C.cross_entropy_bwd(logits, targets, lse, g, scratch[1:2])
         w = ctx.weight
         dx = torch.empty_like(xf)
-        C.linear_dgrad(logits, w.detach(), dx)
         sink = _GradSink([w])
-        _WgradLauncher(xf.device)(logits, xf, sink.buffer)
+        _dgrad_and_wgrad(logits, w.detach(), xf, dx, sink.buffer, _WgradLauncher(xf.device))
         if not sink.direct:
             join_weight_grads(xf.device)
         return dx.view(ctx.shape), sink.finish()[0], None

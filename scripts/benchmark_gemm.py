@@ -8,6 +8,12 @@ of the operands.  It prints TFLOP/s per variant and the fraction of the measured
 variants keep the automatic K-split for their tile.
 
     python scripts/benchmark_gemm.py --shapes 8192x768x4096:dgrad 8192x2048x768:fwd 1280x768x8192:wgrad
+
+`T x out x in:pair` shapes time a linear layer's backward pair (dx = dy @ w and dw += dy^T @ x):
+the two automatic launches one after the other vs the grouped launch that deals both problems'
+tiles together (`linear_dgrad_wgrad`).
+
+    python scripts/benchmark_gemm.py --shapes 8192x4096x768:pair 8192x768x768:pair 8192x1280x768:pair
 """
 
 from __future__ import annotations
@@ -80,6 +86,22 @@ def main(argv=None) -> None:
             dy, x, dw = rnd(K, M), rnd(K, N), torch.zeros(M, N, device="cuda", dtype=torch.float32)
             run = lambda bn: C.linear_wgrad(dy, x, dw, 0, bn)  # noqa: E731
             ref = lambda: torch.matmul(dy.t(), x)  # noqa: E731
+        if kind == "pair":  # T x out x in: dx[T,in] = dy[T,out] w[out,in]; dw[out,in] += dy^T x[T,in]
+            T, out, inp = M, N, K
+            dy, w, x = rnd(T, out), rnd(out, inp), rnd(T, inp)
+            dx = torch.empty(T, inp, device="cuda", dtype=torch.bfloat16)
+            dw = torch.zeros(out, inp, device="cuda", dtype=torch.float32)
+            flops = 4.0 * T * out * inp
+            row = {"shape": spec, "gflop": flops / 1e9}
+            for name, fn in (("separate", lambda: (C.linear_dgrad(dy, w, dx, 0), C.linear_wgrad(dy, x, dw, 0, 0))),
+                             ("grouped", lambda: C.linear_dgrad_wgrad(dy, w, x, dx, dw, 0)),
+                             ("cublas", lambda: (torch.matmul(dy, w), torch.matmul(dy.t(), x)))):
+                ms = _time(fn, a.iters, flush)
+                row[name] = {"ms": ms, "tflops": flops / ms / 1e9, "frac_of_measured": flops / ms / 1e9 / peak}
+            rows.append(row)
+            print(f"{spec:22s} " + " ".join(f"{k}={v['tflops']:.0f}" for k, v in row.items() if isinstance(v, dict)),
+                  flush=True)
+            continue
         row = {"shape": spec, "gflop": flops / 1e9}
         for name, bn in VARIANTS:
             try:

@@ -67,6 +67,18 @@ def test_linear_wgrad_accumulates(C, M, N, K, splits, bn):
     _close(dw, 1.0 + dy.float().t() @ x.float(), 1e-2)
 
 
+@pytest.mark.parametrize("T,out,inp,splits", [(1024, 768, 768, 0), (4096, 4096, 768, 0), (1000, 264, 392, 0),
+                                               (2048, 4000, 768, 3), (8192, 1280, 768, 0)])
+def test_grouped_dgrad_wgrad(C, T, out, inp, splits):
+    """One launch computing dx = dy @ w and dw += dy^T @ x (both problems' tiles dealt together)."""
+    dy, w, x = _bf(T, out, seed=31), _bf(out, inp, scale=0.05, seed=32), _bf(T, inp, seed=33)
+    dx = torch.full((T, inp), 7.0, device="cuda", dtype=torch.bfloat16)
+    dw = torch.ones(out, inp, device="cuda", dtype=torch.float32)
+    C.linear_dgrad_wgrad(dy, w, x, dx, dw, splits)
+    _close(dx, dy.float() @ w.float(), 2e-2)
+    _close(dw, 1.0 + dy.float().t() @ x.float(), 1e-2)
+
+
 def _rope_ref(t, S, hd, theta):
     inv = 1.0 / (theta ** (torch.arange(0, hd, 2, device="cuda").float() / hd))
     ang = torch.outer(torch.arange(S, device="cuda").float(), inv)
