@@ -61,7 +61,10 @@ struct GemmCfg {
   static_assert(SMEM_BYTES <= 232448, "GEMM shared memory exceeds the 227 KB per-block limit");
 };
 
-__device__ __forceinline__ float silu_f(float g) { return g / (1.0f + __expf(-g)); }
+// Fast division (the `__fdividef` intrinsic): the denominator 1 + e^-g is >= 1, and where it
+// overflows the result is the limit 0 either way.
+__device__ __forceinline__ float sigmoid_f(float g) { return __fdividef(1.0f, 1.0f + __expf(-g)); }
+__device__ __forceinline__ float silu_f(float g) { return __fdividef(g, 1.0f + __expf(-g)); }
 
 // Byte offset of 16-byte column group j of row `row` inside a staging chunk.  The TMA maps of the
 // outputs use the 64-byte swizzle (16-byte group index XOR bits 1..2 of the row); the chunk base is
@@ -361,6 +364,21 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         }
         __syncwarp();
       }
+      // SwiGLU backward: saved pre-activations of this row for chunk i (64 B of g and of u), loaded
+      // one chunk ahead; the first chunk's loads are issued before the accumulator wait so that
+      // their latency overlaps the main loop.
+      uint4 gq[4], uq[4];
+      auto load_gu = [&](int i) {
+        const int n0 = tn * BN + wg * (BN / 2);
+        const __nv_bfloat16* gsrc = p.aux_in + (size_t)(row_ok ? m : 0) * p.ld_aux_in + n0 + 32 * i;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const bool in = n0 + 32 * i + 8 * j < p.N;
+          gq[j] = in ? *reinterpret_cast<const uint4*>(gsrc + 8 * j) : make_uint4(0u, 0u, 0u, 0u);
+          uq[j] = in ? *reinterpret_cast<const uint4*>(gsrc + p.ffn + 8 * j) : make_uint4(0u, 0u, 0u, 0u);
+        }
+      };
+      if constexpr (EPI == EPI_SWIGLU_BWD) load_gu(0);
       if (!mbar_wait_bounded(&tfull_bar[acc], acc_phase, abort_flag, p.errs, kErrGemmWait, 3)) break;
       tc_fence_after();
       const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + acc * BN;
@@ -495,18 +513,6 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         }
       } else if constexpr (EPI == EPI_SWIGLU_BWD) {
         const int n0 = tn * BN + wg * (BN / 2);
-        // Saved pre-activations of this row for chunk i (64 B of g and of u), prefetched one chunk ahead.
-        uint4 gq[4], uq[4];
-        auto load_gu = [&](int i) {
-          const __nv_bfloat16* gsrc = p.aux_in + (size_t)(row_ok ? m : 0) * p.ld_aux_in + n0 + 32 * i;
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            const bool in = n0 + 32 * i + 8 * j < p.N;
-            gq[j] = in ? *reinterpret_cast<const uint4*>(gsrc + 8 * j) : make_uint4(0u, 0u, 0u, 0u);
-            uq[j] = in ? *reinterpret_cast<const uint4*>(gsrc + p.ffn + 8 * j) : make_uint4(0u, 0u, 0u, 0u);
-          }
-        };
-        load_gu(0);
 #pragma unroll 1
         for (int i = 0; i < BN / 64; ++i) {
           uint32_t r[32];
@@ -522,7 +528,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
               const float gval = (e & 1) ? bf16hi(gw[e >> 1]) : bf16lo(gw[e >> 1]);
               const float uval = (e & 1) ? bf16hi(uw[e >> 1]) : bf16lo(uw[e >> 1]);
               const float da = __uint_as_float(r[8 * j + e]);
-              const float sig = 1.0f / (1.0f + __expf(-gval));
+              const float sig = sigmoid_f(gval);
               du[8 * j + e] = __float_as_uint(da * gval * sig);
               dg[8 * j + e] = __float_as_uint(da * uval * sig * (1.0f + gval * (1.0f - sig)));
             }
