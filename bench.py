@@ -20,6 +20,7 @@ from __future__ import annotations
 
 import argparse
 import json
+import math
 import os
 import statistics
 import subprocess
@@ -169,11 +170,13 @@ def time_device(step_fn, steps: int) -> float:
     return max_over_ranks(start.elapsed_time(end) / steps)
 
 
-def time_wall(step_fn, steps: int) -> float:
+def time_wall(step_fn, steps: int, finish=None) -> float:
     barrier_sync()
     t0 = time.perf_counter()
     for _ in range(steps):
         step_fn()
+    if finish is not None:
+        finish()
     barrier_sync()
     return max_over_ranks((time.perf_counter() - t0) * 1000.0 / steps)
 
@@ -269,17 +272,32 @@ def run_mine(args) -> None:
             if not args.no_e2e:
                 h2d = host[0].numel() * host[0].element_size()
 
-                def e2e_step():
-                    loss = sess.train_step(host[it["i"] % len(host)])
-                    it["i"] += 1
-                    float(loss)  # device -> host read of the step's loss
+                pending = []
 
+                def e2e_step():
+                    # pinned host batch -> device inside train_step; the step's loss is copied to
+                    # pinned host memory and read (.item()) after the next step has been queued
+                    pending.append(sess.train_step_async(host[it["i"] % len(host)]))
+                    it["i"] += 1
+                    if len(pending) > 1:
+                        losses.append(pending.pop(0).item())
+
+                def e2e_finish():  # the last step's loss is read inside the timed region too
+                    while pending:
+                        losses.append(pending.pop(0).item())
+
+                losses = []
                 for _ in range(2):
                     e2e_step()
-                e2e_ms = time_wall(e2e_step, args.steps)
+                e2e_finish()
+                losses.clear()
+                e2e_ms = time_wall(e2e_step, args.steps, finish=e2e_finish)
+                if len(losses) != args.steps or not all(math.isfinite(x) for x in losses):
+                    raise RuntimeError(f"e2e: expected {args.steps} finite losses, got {losses}")
                 e2e = {"value": tokens_per_step / (e2e_ms / 1000.0), "unit": "tokens/s",
                        "ms_per_step": e2e_ms, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 4,
-                       "api": "cs244c_llama_zero_b200.train.TrainSession.train_step(pinned host int64 [B,S]) + float(loss)"}
+                       "api": "cs244c_llama_zero_b200.train.TrainSession.train_step_async(pinned host int64 [B,S])"
+                              " + AsyncLoss.item() one step later (every step's loss read on the host)"}
         per_stage[str(stage)] = entry
         del sess
         torch.cuda.empty_cache()

@@ -1,5 +1,5 @@
 """Training-session API shared by ``train_zero.py`` and ``bench.py``."""
 
-from .session import SessionConfig, TrainSession, broadcast_model, init_distributed, model_param_dtype
+from .session import AsyncLoss, SessionConfig, TrainSession, broadcast_model, init_distributed, model_param_dtype
 
-__all__ = ["SessionConfig", "TrainSession", "broadcast_model", "init_distributed", "model_param_dtype"]
+__all__ = ["AsyncLoss", "SessionConfig", "TrainSession", "broadcast_model", "init_distributed", "model_param_dtype"]

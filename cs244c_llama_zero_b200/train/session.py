@@ -19,7 +19,7 @@ from __future__ import annotations
 import os
 from dataclasses import dataclass, field
 from datetime import timedelta
-from typing import Optional, Sequence, Tuple
+from typing import List, Optional, Sequence, Tuple
 
 import torch
 import torch.distributed as dist
@@ -84,6 +84,23 @@ def broadcast_model(model: torch.nn.Module) -> None:
             dist.broadcast(p.data, src=0)
 
 
+class AsyncLoss:
+    """A step's loss on its way to the host (see ``TrainSession.train_step_async``).
+
+    The session reuses its pinned slots round-robin (4 of them), so read a handle within three
+    further steps.
+    """
+
+    def __init__(self, host: torch.Tensor, event: Optional["torch.cuda.Event"]) -> None:
+        self._host = host
+        self._event = event
+
+    def item(self) -> float:
+        if self._event is not None:
+            self._event.synchronize()
+        return float(self._host[0])
+
+
 class TrainSession:
     def __init__(self, cfg: SessionConfig, model_cfg: Optional[ModelConfig] = None) -> None:
         self.cfg = cfg
@@ -114,6 +131,8 @@ class TrainSession:
             collectives=collectives,
         )
         self._staging: Optional[torch.Tensor] = None
+        self._loss_ring: Optional[List[torch.Tensor]] = None  # pinned host slots of train_step_async
+        self._loss_slot = 0
         self.autocast = dtype == torch.bfloat16
 
     # ----------------------------------------------------------------------------- steps
@@ -146,6 +165,25 @@ class TrainSession:
         loss = self.forward_backward(micro)
         self.engine.step_async(max_grad_norm=self.cfg.max_grad_norm)
         return loss
+
+    def train_step_async(self, input_ids: torch.Tensor) -> "AsyncLoss":
+        """``train_step`` whose loss comes back to the host without stalling the launch queue.
+
+        The loss is copied into pinned host memory on the compute stream (non-blocking); read it with
+        ``.item()`` one step later, by which time the copy has normally landed, so the host keeps
+        queuing the next step while the GPU finishes this one.
+        """
+        loss = self.train_step(input_ids)
+        if self.device.type != "cuda":
+            return AsyncLoss(loss.detach().float().reshape(1), None)
+        if self._loss_ring is None:
+            self._loss_ring = [torch.empty(1, dtype=torch.float32).pin_memory() for _ in range(4)]
+        buf = self._loss_ring[self._loss_slot]
+        self._loss_slot = (self._loss_slot + 1) % len(self._loss_ring)
+        buf.copy_(loss.detach().float().reshape(1), non_blocking=True)
+        ev = torch.cuda.Event()
+        ev.record()
+        return AsyncLoss(buf, ev)
 
     def close(self) -> None:
         if dist.is_available() and dist.is_initialized():
