@@ -378,7 +378,30 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           uq[j] = in ? *reinterpret_cast<const uint4*>(gsrc + p.ffn + 8 * j) : make_uint4(0u, 0u, 0u, 0u);
         }
       };
-      if constexpr (EPI == EPI_SWIGLU_BWD) load_gu(0);
+      if constexpr (EPI == EPI_SWIGLU_BWD) {
+        // The saved pre-activations were written long ago (forward pass) and sit in DRAM; each lane
+        // reads its own row, so eight warps cannot hide the latency.  Pull this row's g and u slices
+        // of the current (first unit) and the next tile into L2 while the main loop runs.
+        auto prefetch_row = [&](int unit_k) {
+          const int uu = unit_index<GROUPED>(unit_k, group_id, n_groups);
+          if (uu >= total_units) return;
+          const Unit dn = decode_unit<GROUPED>(uu, p, p1);
+          const int rown = dn.tm * BM * CG + rank * BM + q * 32 + lane;
+          if (rown >= p.M) return;
+          const int col = dn.tn * BN + wg * (BN / 2);
+          const __nv_bfloat16* src = p.aux_in + (size_t)rown * p.ld_aux_in + col;
+#pragma unroll
+          for (int b = 0; b < BN / 2; b += 64) {  // BN / 2 columns = BN bytes = BN / 128 lines
+            if (col + b < p.N) {
+              prefetch_l2(src + b);
+              prefetch_l2(src + p.ffn + b);
+            }
+          }
+        };
+        if (ku == 0) prefetch_row(0);
+        prefetch_row(ku + 1);
+        load_gu(0);
+      }
       if (!mbar_wait_bounded(&tfull_bar[acc], acc_phase, abort_flag, p.errs, kErrGemmWait, 3)) break;
       tc_fence_after();
       const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + acc * BN;
