@@ -159,6 +159,7 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  pdl_wait_and_release();  // q|k|v, O, dO, lse, delta come from earlier kernels of the stream
 
   if (warp == 0) {
     if (lane == 0) {
@@ -471,6 +472,7 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
 template <int HD>
 __global__ void attn_delta_kernel(const __nv_bfloat16* __restrict__ o, const __nv_bfloat16* __restrict__ dout, int ld,
                                   float* __restrict__ delta, int rows, int seq, int heads) {
+  pdl_wait_and_release();
   constexpr int G = HD / 8;  // lanes per head
   const int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
@@ -497,6 +499,7 @@ __global__ void attn_delta_kernel(const __nv_bfloat16* __restrict__ o, const __n
 __global__ void attn_dq_convert_kernel(const float* dq_acc, __nv_bfloat16* __restrict__ dqkv, int ld, int rows,
                                        int seq, int heads, int hd, const float* __restrict__ cosv,
                                        const float* __restrict__ sinv, bool rezero) {
+  pdl_wait_and_release();
   const int half = hd / 2;
   const int groups = half / 8;
   const size_t total = (size_t)rows * heads * groups;
@@ -541,9 +544,9 @@ void launch_delta(const __nv_bfloat16* o, const __nv_bfloat16* dout, int ld, flo
                   int hd, cudaStream_t s) {
   const int blocks = (rows * 32 + 255) / 256;
   if (hd == 64)
-    attn_delta_kernel<64><<<blocks, 256, 0, s>>>(o, dout, ld, delta, rows, seq, heads);
+    launch_k(attn_delta_kernel<64>, dim3(blocks), dim3(256), 0, s, 1, o, dout, ld, delta, rows, seq, heads);
   else
-    attn_delta_kernel<128><<<blocks, 256, 0, s>>>(o, dout, ld, delta, rows, seq, heads);
+    launch_k(attn_delta_kernel<128>, dim3(blocks), dim3(256), 0, s, 1, o, dout, ld, delta, rows, seq, heads);
   B200_CUDA_CHECK(cudaGetLastError());
 }
 
@@ -563,7 +566,7 @@ template <int HD>
 void launch_bwd(const AttnBwdParams& p, const CUtensorMap& tq, const CUtensorMap& tdo, const CUtensorMap& tdq,
                 DeviceErrors* errs, cudaStream_t s) {
   using C = AttnBwdCfg<HD>;
-  attn_bwd_kernel<HD><<<bwd_grid(p), BWD_THREADS, C::SMEM_BYTES, s>>>(tq, tdo, tdq, p, errs);
+  launch_k(attn_bwd_kernel<HD>, dim3(bwd_grid(p)), dim3(BWD_THREADS), C::SMEM_BYTES, s, 1, tq, tdo, tdq, p, errs);
 }
 
 }  // namespace
@@ -592,8 +595,8 @@ void attention_bwd(const AttnBwdParams& p, cudaStream_t s) {
   B200_CUDA_CHECK(cudaGetLastError());
   const size_t work = (size_t)rows * p.heads * (p.head_dim / 16);
   const int blocks = (int)std::min<size_t>((work + 255) / 256, (size_t)num_sms_cached() * 16);
-  attn_dq_convert_kernel<<<blocks, 256, 0, s>>>(p.dq_acc, p.dqkv, p.ld, rows, p.seq, p.heads, p.head_dim, p.rope_cos,
-                                                p.rope_sin, p.rezero_dq_acc);
+  launch_k(attn_dq_convert_kernel, dim3(blocks), dim3(256), 0, s, 1, (const float*)p.dq_acc, p.dqkv, p.ld, rows, p.seq,
+           p.heads, p.head_dim, p.rope_cos, p.rope_sin, p.rezero_dq_acc);
   B200_CUDA_CHECK(cudaGetLastError());
   count_launch(3);
 }
@@ -711,8 +714,8 @@ extern "C" int b200_attention_bwd_noalloc(const void* qkv, int ld, int k_col, in
       launch_bwd<128>(p, tq, tdo, tdq, errs, stream);
     const size_t work = rows * heads * (head_dim / 16);
     const int blocks = (int)std::min<size_t>((work + 255) / 256, (size_t)num_sms_cached() * 16);
-    attn_dq_convert_kernel<<<blocks, 256, 0, stream>>>(dq_acc, p.dqkv, ld, (int)rows, seq, heads, head_dim, rope_cos,
-                                                       rope_sin, false);
+    launch_k(attn_dq_convert_kernel, dim3(blocks), dim3(256), 0, stream, 1, (const float*)dq_acc, p.dqkv, ld, (int)rows,
+             seq, heads, head_dim, rope_cos, rope_sin, false);
     count_launch(3);
   } catch (const std::exception& ex) {
     std::fprintf(stderr, "b200_attention_bwd_noalloc: %s\n", ex.what());

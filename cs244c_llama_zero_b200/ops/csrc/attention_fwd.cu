@@ -129,6 +129,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  pdl_wait_and_release();  // q|k|v come from the previous kernel of the stream
 
   if (warp == 0) {
     if (lane == 0) {
@@ -396,7 +397,7 @@ void launch_fwd(const AttnParams& p, const CUtensorMap& tm, cudaStream_t s) {
   }
   const int items = (p.seq / 128) * p.heads * p.batch;
   const int grid = std::max(1, std::min(items, num_sms_cached()));
-  attn_fwd_kernel<HD><<<grid, ATT_THREADS, C::SMEM_BYTES, s>>>(tm, p, device_errors_ptr());
+  launch_k(attn_fwd_kernel<HD>, dim3(grid), dim3(ATT_THREADS), C::SMEM_BYTES, s, 1, tm, p, device_errors_ptr());
 }
 
 }  // namespace

@@ -15,6 +15,7 @@
 #include <atomic>
 #include <stdexcept>
 #include <string>
+#include <utility>
 
 namespace b200 {
 
@@ -37,6 +38,40 @@ inline void count_launch(int n = 1) { launch_counter().fetch_add(n, std::memory_
     if (!(cond)) throw std::runtime_error(std::string("b200 ops: ") + (msg));      \
   } while (0)
 
+// Programmatic dependent launch: a kernel launched with launch_k() may start (and run its setup:
+// barrier init, tensor-memory allocation, descriptor prefetch) while the previous kernel of the
+// stream is still finishing; it must call pdl_wait() before touching any global memory that an
+// earlier kernel reads or writes.  ZB_PDL=0 launches without the attribute (pdl_wait is then a
+// no-op).  Communication kernels, whose blocks wait on peers, are not launched this way.
+bool pdl_enabled();
+
+template <typename... KArgs, typename... Args>
+void launch_k(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream, int cluster_x,
+              Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  int n = 0;
+  if (pdl_enabled()) {
+    attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[n].val.programmaticStreamSerializationAllowed = 1;
+    ++n;
+  }
+  if (cluster_x > 1) {
+    attr[n].id = cudaLaunchAttributeClusterDimension;
+    attr[n].val.clusterDim.x = cluster_x;
+    attr[n].val.clusterDim.y = 1;
+    attr[n].val.clusterDim.z = 1;
+    ++n;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = n;
+  B200_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...));
+}
+
 // Device error record written by kernels whose bounded waits expired.
 struct DeviceErrors {
   int code;      // 0 = ok; otherwise a kernel-specific code
@@ -58,6 +93,13 @@ enum : int {
 // ---------------------------------------------------------------------------------------
 // Device side
 // ---------------------------------------------------------------------------------------
+// Wait until the previous kernel of the stream has completed and its memory is visible (returns at
+// once when this kernel was not launched as a programmatic dependent), then let the next kernel of
+// the stream start launching.
+__device__ __forceinline__ void pdl_wait_and_release() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
 #if defined(__CUDACC__)
 
 // Deadline for any single wait: generous against normal latencies, short enough that a

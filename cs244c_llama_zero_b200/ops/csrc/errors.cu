@@ -1,7 +1,9 @@
 // Process-wide launch counter and the per-device error record used by bounded waits.
 #include <cuda_runtime.h>
 
+#include <cstdlib>
 #include <mutex>
+#include <string>
 #include <vector>
 
 #include "common.cuh"
@@ -11,6 +13,14 @@ namespace b200 {
 std::atomic<long long>& launch_counter() {
   static std::atomic<long long> counter{0};
   return counter;
+}
+
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* v = std::getenv("ZB_PDL");
+    return v == nullptr || std::string(v) != "0";
+  }();
+  return on;
 }
 
 DeviceErrors* device_errors_ptr() {

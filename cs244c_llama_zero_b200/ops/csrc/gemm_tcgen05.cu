@@ -210,6 +210,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   if constexpr (CG == 2) cluster_sync();  // the peer's barriers are initialised before any remote arrive
   tc_fence_after();
   const uint32_t tmem_base = *tmem_base_slot;
+  pdl_wait_and_release();  // operands / outputs are shared with the previous kernels of the stream
 
   const int total_units = GROUPED ? p.grp_units_total : p.tiles_m * p.tiles_n * p.splits;
 
@@ -698,23 +699,8 @@ static void launch_impl(const GemmOperands& op, GemmParams p, cudaStream_t strea
   p.errs = device_errors_ptr();
   const int units = p.tiles_m * p.tiles_n * p.splits;
   const int groups = std::max(1, std::min(units, num_sms() / CG));
-  if constexpr (CG == 1) {
-    kernel<<<groups, NUM_THREADS, Cfg::SMEM_BYTES, stream>>>(tmA, tmB, tmC, tmX, tmY, tmA, p, p);
-  } else {
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(groups * CG, 1, 1);
-    cfg.blockDim = dim3(NUM_THREADS, 1, 1);
-    cfg.dynamicSmemBytes = Cfg::SMEM_BYTES;
-    cfg.stream = stream;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = CG;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    B200_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kernel, tmA, tmB, tmC, tmX, tmY, tmA, p, p));
-  }
+  launch_k(kernel, dim3(groups * CG), dim3(NUM_THREADS), Cfg::SMEM_BYTES, stream, CG, tmA, tmB, tmC, tmX, tmY, tmA, p,
+           p);
   B200_CUDA_CHECK(cudaGetLastError());
   count_launch();
 }
@@ -917,19 +903,8 @@ void gemm_launch_dgrad_wgrad(const GemmOperands& op0, GemmParams p0, const GemmO
   const CUtensorMap tmY = make_tmap_bf16_2d(op1.B, (uint64_t)p1.N, (uint64_t)p1.K, op1.ldb, 64, 64);
   const CUtensorMap tmZ = epi_map_f32(p1.C32, p1.M, p1.N, p1.ldc32);
   const int groups = std::max(1, std::min(p0.grp_units_total, G));
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(groups * CGG, 1, 1);
-  cfg.blockDim = dim3(NUM_THREADS, 1, 1);
-  cfg.dynamicSmemBytes = Cfg::SMEM_BYTES;
-  cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = CGG;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  B200_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kernel, tmA, tmB, tmC, tmX, tmY, tmZ, p0, p1));
+  launch_k(kernel, dim3(groups * CGG), dim3(NUM_THREADS), Cfg::SMEM_BYTES, stream, CGG, tmA, tmB, tmC, tmX, tmY, tmZ,
+           p0, p1);
   B200_CUDA_CHECK(cudaGetLastError());
   count_launch();
 }

@@ -43,6 +43,7 @@ template <int VEC>
 __global__ void rmsnorm_fwd_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ w,
                                    __nv_bfloat16* __restrict__ y, float* __restrict__ rstd, int rows, int d,
                                    float eps) {
+  pdl_wait_and_release();
   const int lane = threadIdx.x & 31;
   const int row = blockIdx.x * kWarpsPerBlock + (threadIdx.x >> 5);
   if (row >= rows) return;
@@ -88,6 +89,7 @@ __global__ void __launch_bounds__(32 * kWarpsPerBlock)
                        const __nv_bfloat16* __restrict__ w, const float* __restrict__ rstd,
                        const __nv_bfloat16* __restrict__ dres, __nv_bfloat16* __restrict__ dx,
                        float* __restrict__ dw, int rows, int d) {
+  pdl_wait_and_release();
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
   const int row0 = (blockIdx.x * kWarpsPerBlock + warp) * ROWS;
@@ -172,6 +174,7 @@ __global__ void __launch_bounds__(32 * kWarpsPerBlock)
 __global__ void embedding_fwd_kernel(const int64_t* __restrict__ ids, const __nv_bfloat16* __restrict__ table,
                                      __nv_bfloat16* __restrict__ out, int rows, int d, int vocab,
                                      DeviceErrors* errs) {
+  pdl_wait_and_release();
   const int vec_per_row = d / 8;
   const size_t total = (size_t)rows * vec_per_row;
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
@@ -186,6 +189,7 @@ __global__ void embedding_fwd_kernel(const int64_t* __restrict__ ids, const __nv
 
 __global__ void embedding_bwd_kernel(const int64_t* __restrict__ ids, const __nv_bfloat16* __restrict__ dy,
                                      float* __restrict__ dtable, int rows, int d, int vocab) {
+  pdl_wait_and_release();
   const int vec_per_row = d / 8;
   const size_t total = (size_t)rows * vec_per_row;
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
@@ -204,6 +208,7 @@ __global__ void embedding_bwd_kernel(const int64_t* __restrict__ ids, const __nv
 // In-place inverse rotation of the q and k columns of a [rows, ld] gradient.
 __global__ void rope_bwd_kernel(__nv_bfloat16* __restrict__ g, int rows, int ld, int rope_cols, int head_dim,
                                 int seq_len, const float* __restrict__ cosv, const float* __restrict__ sinv) {
+  pdl_wait_and_release();
   const int half = head_dim / 2;
   const int groups_per_row = rope_cols / head_dim * (half / 8);
   const size_t total = (size_t)rows * groups_per_row;
@@ -253,17 +258,17 @@ void rmsnorm_fwd(const __nv_bfloat16* x, const __nv_bfloat16* w, __nv_bfloat16* 
   const int blocks = (rows + kWarpsPerBlock - 1) / kWarpsPerBlock;
   const int vec = (d + 255) / 256;
   if (vec <= 1)
-    rmsnorm_fwd_kernel<1><<<blocks, 32 * kWarpsPerBlock, 0, s>>>(x, w, y, rstd, rows, d, eps);
+    launch_k(rmsnorm_fwd_kernel<1>, dim3(blocks), dim3(32 * kWarpsPerBlock), 0, s, 1, x, w, y, rstd, rows, d, eps);
   else if (vec <= 2)
-    rmsnorm_fwd_kernel<2><<<blocks, 32 * kWarpsPerBlock, 0, s>>>(x, w, y, rstd, rows, d, eps);
+    launch_k(rmsnorm_fwd_kernel<2>, dim3(blocks), dim3(32 * kWarpsPerBlock), 0, s, 1, x, w, y, rstd, rows, d, eps);
   else if (vec <= 3)
-    rmsnorm_fwd_kernel<3><<<blocks, 32 * kWarpsPerBlock, 0, s>>>(x, w, y, rstd, rows, d, eps);
+    launch_k(rmsnorm_fwd_kernel<3>, dim3(blocks), dim3(32 * kWarpsPerBlock), 0, s, 1, x, w, y, rstd, rows, d, eps);
   else if (vec <= 4)
-    rmsnorm_fwd_kernel<4><<<blocks, 32 * kWarpsPerBlock, 0, s>>>(x, w, y, rstd, rows, d, eps);
+    launch_k(rmsnorm_fwd_kernel<4>, dim3(blocks), dim3(32 * kWarpsPerBlock), 0, s, 1, x, w, y, rstd, rows, d, eps);
   else if (vec <= 8)
-    rmsnorm_fwd_kernel<8><<<blocks, 32 * kWarpsPerBlock, 0, s>>>(x, w, y, rstd, rows, d, eps);
+    launch_k(rmsnorm_fwd_kernel<8>, dim3(blocks), dim3(32 * kWarpsPerBlock), 0, s, 1, x, w, y, rstd, rows, d, eps);
   else
-    rmsnorm_fwd_kernel<16><<<blocks, 32 * kWarpsPerBlock, 0, s>>>(x, w, y, rstd, rows, d, eps);
+    launch_k(rmsnorm_fwd_kernel<16>, dim3(blocks), dim3(32 * kWarpsPerBlock), 0, s, 1, x, w, y, rstd, rows, d, eps);
   B200_CUDA_CHECK(cudaGetLastError());
   count_launch();
 }
@@ -276,15 +281,15 @@ void rmsnorm_bwd(const __nv_bfloat16* dy, const __nv_bfloat16* x, const __nv_bfl
   const int blocks = std::max(1, (rows + per_block - 1) / per_block);
   const int threads = 32 * kWarpsPerBlock;
   if (vec <= 1)
-    rmsnorm_bwd_kernel<1, 2><<<blocks, threads, 0, s>>>(dy, x, w, rstd, dres, dx, dw, rows, d);
+    launch_k(rmsnorm_bwd_kernel<1, 2>, dim3(blocks), dim3(threads), 0, s, 1, dy, x, w, rstd, dres, dx, dw, rows, d);
   else if (vec <= 2)
-    rmsnorm_bwd_kernel<2, 2><<<blocks, threads, 0, s>>>(dy, x, w, rstd, dres, dx, dw, rows, d);
+    launch_k(rmsnorm_bwd_kernel<2, 2>, dim3(blocks), dim3(threads), 0, s, 1, dy, x, w, rstd, dres, dx, dw, rows, d);
   else if (vec <= 3)
-    rmsnorm_bwd_kernel<3, 2><<<blocks, threads, 0, s>>>(dy, x, w, rstd, dres, dx, dw, rows, d);
+    launch_k(rmsnorm_bwd_kernel<3, 2>, dim3(blocks), dim3(threads), 0, s, 1, dy, x, w, rstd, dres, dx, dw, rows, d);
   else if (vec <= 4)
-    rmsnorm_bwd_kernel<4, 2><<<blocks, threads, 0, s>>>(dy, x, w, rstd, dres, dx, dw, rows, d);
+    launch_k(rmsnorm_bwd_kernel<4, 2>, dim3(blocks), dim3(threads), 0, s, 1, dy, x, w, rstd, dres, dx, dw, rows, d);
   else
-    rmsnorm_bwd_kernel<8, 1><<<blocks, threads, 0, s>>>(dy, x, w, rstd, dres, dx, dw, rows, d);
+    launch_k(rmsnorm_bwd_kernel<8, 1>, dim3(blocks), dim3(threads), 0, s, 1, dy, x, w, rstd, dres, dx, dw, rows, d);
   B200_CUDA_CHECK(cudaGetLastError());
   count_launch();
 }
@@ -292,7 +297,7 @@ void rmsnorm_bwd(const __nv_bfloat16* dy, const __nv_bfloat16* x, const __nv_bfl
 void embedding_fwd(const int64_t* ids, const __nv_bfloat16* table, __nv_bfloat16* out, int rows, int d, int vocab,
                    cudaStream_t s) {
   B200_CHECK(d % 8 == 0, "embedding: d must be a multiple of 8");
-  embedding_fwd_kernel<<<grid_for((size_t)rows * d / 8, 256), 256, 0, s>>>(ids, table, out, rows, d, vocab,
+  launch_k(embedding_fwd_kernel, dim3(grid_for((size_t)rows * d / 8, 256)), dim3(256), 0, s, 1, ids, table, out, rows, d, vocab,
                                                                             device_errors_ptr());
   B200_CUDA_CHECK(cudaGetLastError());
   count_launch();
@@ -300,7 +305,7 @@ void embedding_fwd(const int64_t* ids, const __nv_bfloat16* table, __nv_bfloat16
 
 void embedding_bwd(const int64_t* ids, const __nv_bfloat16* dy, float* dtable, int rows, int d, int vocab,
                    cudaStream_t s) {
-  embedding_bwd_kernel<<<grid_for((size_t)rows * d / 8, 256), 256, 0, s>>>(ids, dy, dtable, rows, d, vocab);
+  launch_k(embedding_bwd_kernel, dim3(grid_for((size_t)rows * d / 8, 256)), dim3(256), 0, s, 1, ids, dy, dtable, rows, d, vocab);
   B200_CUDA_CHECK(cudaGetLastError());
   count_launch();
 }
@@ -309,7 +314,7 @@ void rope_bwd(__nv_bfloat16* g, int rows, int ld, int rope_cols, int head_dim, i
               const float* sinv, cudaStream_t s) {
   B200_CHECK(head_dim % 16 == 0 && rope_cols % head_dim == 0, "rope_bwd: bad head layout");
   const size_t work = (size_t)rows * (rope_cols / head_dim) * (head_dim / 16);
-  rope_bwd_kernel<<<grid_for(work, 256), 256, 0, s>>>(g, rows, ld, rope_cols, head_dim, seq_len, cosv, sinv);
+  launch_k(rope_bwd_kernel, dim3(grid_for(work, 256)), dim3(256), 0, s, 1, g, rows, ld, rope_cols, head_dim, seq_len, cosv, sinv);
   B200_CUDA_CHECK(cudaGetLastError());
   count_launch();
 }

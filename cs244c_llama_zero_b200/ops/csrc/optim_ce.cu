@@ -39,6 +39,7 @@ template <bool BF16_OUT>
 __global__ void adamw_kernel(float* __restrict__ master, float* __restrict__ m, float* __restrict__ v,
                              const float* __restrict__ g, void* __restrict__ param_out, size_t n,
                              const float* __restrict__ scale_ptr, float scale_const, AdamArgs a) {
+  pdl_wait_and_release();
   const float scale = (scale_ptr != nullptr ? *scale_ptr : 1.0f) * scale_const;
   const float decay = 1.0f - a.lr * a.wd;
   const float step = a.lr * a.inv_bc1;
@@ -98,6 +99,7 @@ __device__ __forceinline__ float to_float(__nv_bfloat16 v) { return __bfloat162f
 
 template <typename T>
 __global__ void sum_squares_kernel(const T* __restrict__ x, size_t n, float* __restrict__ out) {
+  pdl_wait_and_release();
   float acc = 0.f;
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
     const float v = to_float(x[i]);
@@ -116,6 +118,7 @@ __global__ void sum_squares_kernel(const T* __restrict__ x, size_t n, float* __r
 }
 
 __global__ void sum_squares_f4_kernel(const float4* __restrict__ x, size_t n4, float* __restrict__ out) {
+  pdl_wait_and_release();
   float acc = 0.f;
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n4; i += (size_t)gridDim.x * blockDim.x) {
     const float4 v = x[i];
@@ -137,6 +140,7 @@ __global__ void sum_squares_f4_kernel(const float4* __restrict__ x, size_t n4, f
 __global__ void ce_fwd_kernel(const __nv_bfloat16* __restrict__ logits, int ld, const int64_t* __restrict__ targets,
                               int rows, int vocab, float* __restrict__ lse_out, float* __restrict__ loss_sum,
                               float* __restrict__ count) {
+  pdl_wait_and_release();
   const int row = blockIdx.x;
   if (row >= rows) return;
   const int64_t tgt = targets[row];
@@ -201,6 +205,7 @@ __global__ void ce_fwd_kernel(const __nv_bfloat16* __restrict__ logits, int ld, 
 __global__ void ce_bwd_kernel(__nv_bfloat16* __restrict__ logits, int ld, const int64_t* __restrict__ targets,
                               int rows, int vocab, const float* __restrict__ lse, const float* __restrict__ grad_loss,
                               const float* __restrict__ count) {
+  pdl_wait_and_release();
   const int row = blockIdx.x;
   if (row >= rows) return;
   const int64_t tgt = targets[row];
@@ -228,6 +233,7 @@ __global__ void ce_bwd_kernel(__nv_bfloat16* __restrict__ logits, int ld, const 
 }
 
 __global__ void finalize_loss_kernel(const float* loss_sum, const float* count, float* loss) {
+  pdl_wait_and_release();
   *loss = *loss_sum / fmaxf(*count, 1.0f);
 }
 
@@ -255,9 +261,9 @@ void adamw_step(float* master, float* m, float* v, const float* g, void* param_o
   const size_t work = std::max<size_t>(1, n / 4);
   const int blocks = (int)std::min<size_t>((work + threads - 1) / threads, (size_t)num_sms_cached() * 8);
   if (param_bf16)
-    adamw_kernel<true><<<blocks, threads, 0, s>>>(master, m, v, g, param_out, n, scale_ptr, scale_const, a);
+    launch_k(adamw_kernel<true>, dim3(blocks), dim3(threads), 0, s, 1, master, m, v, g, param_out, n, scale_ptr, scale_const, a);
   else
-    adamw_kernel<false><<<blocks, threads, 0, s>>>(master, m, v, g, param_out, n, scale_ptr, scale_const, a);
+    launch_k(adamw_kernel<false>, dim3(blocks), dim3(threads), 0, s, 1, master, m, v, g, param_out, n, scale_ptr, scale_const, a);
   B200_CUDA_CHECK(cudaGetLastError());
   count_launch();
 }
@@ -267,11 +273,11 @@ void sum_squares(const void* x, bool is_bf16, size_t n, float* out, cudaStream_t
   const int threads = 512;
   const int blocks = (int)std::max<size_t>(1, std::min<size_t>((n + threads - 1) / threads, (size_t)num_sms_cached() * 4));
   if (is_bf16) {
-    sum_squares_kernel<__nv_bfloat16><<<blocks, threads, 0, s>>>(reinterpret_cast<const __nv_bfloat16*>(x), n, out);
+    launch_k(sum_squares_kernel<__nv_bfloat16>, dim3(blocks), dim3(threads), 0, s, 1, reinterpret_cast<const __nv_bfloat16*>(x), n, out);
   } else if ((reinterpret_cast<uintptr_t>(x) & 15) == 0 && n % 4 == 0) {
-    sum_squares_f4_kernel<<<blocks, threads, 0, s>>>(reinterpret_cast<const float4*>(x), n / 4, out);
+    launch_k(sum_squares_f4_kernel, dim3(blocks), dim3(threads), 0, s, 1, reinterpret_cast<const float4*>(x), n / 4, out);
   } else {
-    sum_squares_kernel<float><<<blocks, threads, 0, s>>>(reinterpret_cast<const float*>(x), n, out);
+    launch_k(sum_squares_kernel<float>, dim3(blocks), dim3(threads), 0, s, 1, reinterpret_cast<const float*>(x), n, out);
   }
   B200_CUDA_CHECK(cudaGetLastError());
   count_launch();
@@ -282,16 +288,16 @@ void cross_entropy_fwd(const __nv_bfloat16* logits, int ld, const int64_t* targe
   B200_CHECK(ld % 8 == 0, "cross_entropy: logits row stride must be a multiple of 8");
   B200_CUDA_CHECK(cudaMemsetAsync(loss_sum, 0, sizeof(float), s));
   B200_CUDA_CHECK(cudaMemsetAsync(count, 0, sizeof(float), s));
-  ce_fwd_kernel<<<rows, 256, 0, s>>>(logits, ld, targets, rows, vocab, lse, loss_sum, count);
+  launch_k(ce_fwd_kernel, dim3(rows), dim3(256), 0, s, 1, logits, ld, targets, rows, vocab, lse, loss_sum, count);
   B200_CUDA_CHECK(cudaGetLastError());
-  finalize_loss_kernel<<<1, 1, 0, s>>>(loss_sum, count, loss);
+  launch_k(finalize_loss_kernel, dim3(1), dim3(1), 0, s, 1, loss_sum, count, loss);
   B200_CUDA_CHECK(cudaGetLastError());
   count_launch(2);
 }
 
 void cross_entropy_bwd(__nv_bfloat16* logits, int ld, const int64_t* targets, int rows, int vocab, const float* lse,
                        const float* grad_loss, const float* count, cudaStream_t s) {
-  ce_bwd_kernel<<<rows, 256, 0, s>>>(logits, ld, targets, rows, vocab, lse, grad_loss, count);
+  launch_k(ce_bwd_kernel, dim3(rows), dim3(256), 0, s, 1, logits, ld, targets, rows, vocab, lse, grad_loss, count);
   B200_CUDA_CHECK(cudaGetLastError());
   count_launch();
 }
