@@ -188,6 +188,27 @@ void linear_dgrad_wgrad(Tensor dy, Tensor w, Tensor x, Tensor dx, Tensor dw, int
   b200::gemm_launch_dgrad_wgrad(op0, p0, op1, p1, cur_stream());
 }
 
+// Host-only views of the GEMM schedulers (no GPU needed), for tests and tooling.
+// (bn, splits, cg) that the automatic tile choice picks for one GEMM on `sms` SMs.
+std::vector<int64_t> gemm_tile_choice(int64_t M, int64_t N, int64_t K, int64_t epi, int64_t head_dim, bool allow_split,
+                                      bool b_mn, int64_t sms) {
+  const b200::GemmTile t = b200::choose_gemm_tile((int)M, (int)N, (int)K, (int)epi, (int)head_dim, allow_split, b_mn,
+                                                  (int)sms);
+  return {t.bn, t.splits, t.cg};
+}
+
+// The grouped dgrad + wgrad schedule of a linear layer [T tokens, out x in weight] on `sms` SMs:
+// (wgrad splits, wgrad k-blocks per split, problem dealt first, units of that problem, all units,
+//  modelled makespan in k-blocks, dgrad tiles, wgrad tiles).
+std::vector<int64_t> grouped_dgrad_wgrad_plan(int64_t T, int64_t out, int64_t in, int64_t sms, int64_t splits) {
+  auto p0 = base_params((int)T, (int)in, (int)out);
+  auto p1 = base_params((int)out, (int)in, (int)T);
+  p1.splits = splits > 0 ? (int)splits : 0;
+  const long span = b200::plan_dgrad_wgrad(p0, p1, (int)sms);
+  return {p1.splits, p1.k_blocks_per_split, p0.grp_first, p0.grp_units_first, p0.grp_units_total, span,
+          (int64_t)p0.tiles_m * p0.tiles_n, (int64_t)p1.tiles_m * p1.tiles_n};
+}
+
 // Generic entry for tests: C = A op B with explicit majors.
 void gemm_raw(Tensor A, Tensor B, Tensor C, int64_t M, int64_t N, int64_t K, bool a_mn, bool b_mn, int64_t bn,
               int64_t splits) {
@@ -679,6 +700,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("qkv_rope_fwd", &qkv_rope_fwd);
   m.def("swiglu_fwd", &swiglu_fwd);
   m.def("linear_dgrad", &linear_dgrad, py::arg("dy"), py::arg("w"), py::arg("dx"), py::arg("bn") = 0);
+  m.def("gemm_tile_choice", &gemm_tile_choice, py::arg("M"), py::arg("N"), py::arg("K"), py::arg("epi"),
+        py::arg("head_dim"), py::arg("allow_split"), py::arg("b_mn"), py::arg("sms"));
+  m.def("grouped_dgrad_wgrad_plan", &grouped_dgrad_wgrad_plan, py::arg("T"), py::arg("out"), py::arg("inp"),
+        py::arg("sms"), py::arg("splits") = 0);
   m.def("linear_dgrad_wgrad", &linear_dgrad_wgrad, py::arg("dy"), py::arg("w"), py::arg("x"), py::arg("dx"),
         py::arg("dw"), py::arg("splits") = 0);
   m.def("swiglu_dgrad", &swiglu_dgrad);

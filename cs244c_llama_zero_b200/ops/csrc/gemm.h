@@ -75,5 +75,8 @@ void gemm_launch(const GemmOperands& op, GemmParams p, int epi, bool a_mn, bool 
 // splits1 <= 0 chooses problem 1's K-split for the combined schedule.
 void gemm_launch_dgrad_wgrad(const GemmOperands& op0, GemmParams p0, const GemmOperands& op1, GemmParams p1,
                              cudaStream_t stream);
+// The grouped launch's schedule (host only): fills both problems' tile / split fields and the
+// grouping fields of p0 for `sms` SMs and returns the modelled makespan in k-blocks per CTA pair.
+long plan_dgrad_wgrad(GemmParams& p0, GemmParams& p1, int sms);
 
 }  // namespace b200

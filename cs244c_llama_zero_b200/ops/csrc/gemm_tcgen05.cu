@@ -852,13 +852,11 @@ static long grouped_makespan(const GemmParams& p0, const GemmParams& p1, int G, 
   return *std::max_element(load.begin(), load.end());
 }
 
-void gemm_launch_dgrad_wgrad(const GemmOperands& op0, GemmParams p0, const GemmOperands& op1, GemmParams p1,
-                             cudaStream_t stream) {
-  constexpr int BNG = 256, CGG = 2;
-  using Cfg = GemmCfg<BNG, CGG>;
-  B200_CHECK(p0.N % 8 == 0 && p1.N % 8 == 0 && p0.K % 8 == 0 && p1.M % 8 == 0,
-             "grouped dgrad/wgrad: N, K (dgrad) and M (wgrad) must be multiples of 8");
-  const int G = std::max(1, num_sms() / CGG);
+constexpr int kGroupedBN = 256, kGroupedCG = 2;
+
+long plan_dgrad_wgrad(GemmParams& p0, GemmParams& p1, int sms) {
+  constexpr int BNG = kGroupedBN, CGG = kGroupedCG;
+  const int G = std::max(1, sms / CGG);
   fill_schedule(p0, BNG, CGG, 1);
   int first = 0;
   if (p1.splits > 0) {
@@ -886,6 +884,17 @@ void gemm_launch_dgrad_wgrad(const GemmOperands& op0, GemmParams p0, const GemmO
   p0.grp_first = first;
   p0.grp_units_first = (int)(first ? units1 : units0);
   p0.grp_units_total = (int)(units0 + units1);
+  return grouped_makespan(p0, p1, G, &first);
+}
+
+void gemm_launch_dgrad_wgrad(const GemmOperands& op0, GemmParams p0, const GemmOperands& op1, GemmParams p1,
+                             cudaStream_t stream) {
+  constexpr int BNG = kGroupedBN, CGG = kGroupedCG;
+  using Cfg = GemmCfg<BNG, CGG>;
+  B200_CHECK(p0.N % 8 == 0 && p1.N % 8 == 0 && p0.K % 8 == 0 && p1.M % 8 == 0,
+             "grouped dgrad/wgrad: N, K (dgrad) and M (wgrad) must be multiples of 8");
+  const int G = std::max(1, num_sms() / CGG);
+  plan_dgrad_wgrad(p0, p1, num_sms());
   p0.errs = p1.errs = device_errors_ptr();
 
   auto kernel = gemm_kernel<BNG, false, true, EPI_STORE, CGG, true>;
