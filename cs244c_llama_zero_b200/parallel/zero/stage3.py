@@ -328,16 +328,20 @@ class _PullGather:
 
     CATEGORIES = ("forward_allgather", "backward_allgather")
 
-    def __init__(self, engine: "ZeROStage3Optimizer", store: torch.Tensor, slots: List[torch.Tensor]) -> None:
-        from ... import ops
+    def __init__(self, engine: "ZeROStage3Optimizer", store: torch.Tensor, slots: List[torch.Tensor],
+                 native=None) -> None:
         from ..collectives import simulated_collective_delay_s
 
         self.engine = engine
         self.store = store
         self.slots = slots
         self.slot_ptrs = [t.data_ptr() for t in slots]
-        dev = engine.device.index if engine.device.index is not None else torch.cuda.current_device()
-        self.native = ops.load_extension().PullGather(len(slots), len(self.CATEGORIES), dev)
+        if native is None:  # the streams / events / copies object (a stand-in can be passed in tests)
+            from ... import ops
+
+            dev = engine.device.index if engine.device.index is not None else torch.cuda.current_device()
+            native = ops.load_extension().PullGather(len(slots), len(self.CATEGORIES), dev)
+        self.native = native
         coll = engine.collectives
         elsize = store.element_size()
         self.where: Dict[int, Tuple[object, int, int]] = {}  # id(handle) -> (comm context, byte offset, chunk bytes)
