@@ -28,7 +28,7 @@ def _unavailable(reason: str) -> None:
 def main(args, ClockSampler, base_record, emit, time_device, time_wall, random_batches, max_over_ranks, metric,
          model_desc) -> None:
     if not os.path.isdir(os.path.join(REF, "zero")):
-        _unavailable("reference not installed in baseline/_ref (run the pip install recorded in DESIGN.md)")
+        _unavailable("reference not installed in baseline/_ref (install: python -m pip install --no-index --no-build-isolation --find-links /opt/wheelhouse --no-deps --target baseline/_ref <copy of the reference tree with a pyproject.toml>)")
         return
     sys.path.insert(0, REF)
     from datetime import timedelta
@@ -84,7 +84,7 @@ def main(args, ClockSampler, base_record, emit, time_device, time_wall, random_b
             step(dev[it["i"] % len(dev)])
             it["i"] += 1
 
-        sampler = ClockSampler([local]) if stage == args.headline_stage and rank == 0 else None
+        sampler = ClockSampler([local], getattr(args, "clocks_csv", None)) if stage == args.headline_stage and rank == 0 else None
         if sampler:
             sampler.__enter__()
         for _ in range(args.warmup):

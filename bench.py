@@ -25,6 +25,7 @@ import os
 import statistics
 import subprocess
 import sys
+import tempfile
 import time
 
 HERE = os.path.dirname(os.path.abspath(__file__))
@@ -44,6 +45,7 @@ def parse_args(argv=None) -> argparse.Namespace:
     p.add_argument("--seq-len", type=int, default=1024)
     p.add_argument("--collective-impl", type=str, default="auto", help="auto | torch | nvls | p2p")
     p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--clocks-csv", type=str, default=None, help="keep the raw nvidia-smi clock samples here")
     p.add_argument("--model-size", type=str, default="baseline-small",
                    help="model preset: baseline-small (the headline config), baseline-1.3b, baseline-7b, ...")
     args = p.parse_args(argv)
@@ -62,10 +64,12 @@ class ClockSampler:
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, gpu_indices):
+    def __init__(self, gpu_indices, path=None):
         self.gpu_indices = set(gpu_indices)
         self.proc = None
-        self.path = os.path.join(HERE, "gpurun_out", f"clocks_{os.getpid()}.csv")
+        # The raw samples go to --clocks-csv when given (kept), else to a temporary file; the JSON
+        # line carries the summary either way.
+        self.path = path or os.path.join(tempfile.gettempdir(), f"zb_clocks_{os.getpid()}.csv")
 
     def __enter__(self):
         try:
@@ -244,7 +248,7 @@ def run_mine(args) -> None:
 
         # The sampler starts before the warm-up so that short timed regions still get samples taken
         # under steady load; it stops right after the timed steps.
-        sampler = ClockSampler([local]) if stage == args.headline_stage and rank == 0 else None
+        sampler = ClockSampler([local], args.clocks_csv) if stage == args.headline_stage and rank == 0 else None
         if sampler:
             sampler.__enter__()
         for _ in range(args.warmup):

@@ -349,6 +349,8 @@ class _PullGather:
             ctx, off = coll.locate_symmetric(h.param_shard)
             self.where[id(h)] = (ctx, off, h.chunk * elsize)
         self.simulate = simulated_collective_delay_s(1 << 20, engine.world_size) > 0
+        self.record_gather = getattr(coll, "record_external", None)
+        self.elsize = elsize
         self.bound: List[Optional[Stage3ParamHandle]] = [None] * len(slots)
         self.pending: Dict[int, int] = {}  # id(handle) -> slot holding its prefetched parameters
         self.ring = 0
@@ -379,9 +381,14 @@ class _PullGather:
         self.engine.clock.count(self.CATEGORIES[cat], handle.full_param_bytes)
         ctx, off, nbytes = self.where[id(handle)]
         issue = self.native.prefetch if prefetch else self.native.gather_now
+        t0 = time.perf_counter()
         issue(ctx, slot, off, nbytes, self.slot_ptrs[slot], cat, True)
         if self.simulate:
             _maybe_simulate_collective_delay(nbytes, self.engine.world_size)
+        if self.record_gather is not None:  # the collective-trace wrapper: one "allgather" record per gather
+            self.record_gather("allgather", f"stage3.{phase}.allgather.{handle.name}", nbytes,
+                       handle.padded_numel * self.elsize, (time.perf_counter() - t0) * 1000.0, str(self.store.device),
+                       str(self.store.dtype).replace("torch.", ""))
 
     def _prefetch(self, handle: Stage3ParamHandle, phase: str) -> None:
         # A handle that is bound right now (the last forward module is the first backward one) is

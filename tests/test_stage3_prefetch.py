@@ -142,3 +142,15 @@ def test_store_write_joins_and_drops_pending_prefetches():
     assert pg.pending  # first module prefetched
     pg.before_store_write()  # e.g. load_state_dict rewrites the store
     assert not pg.pending and native.log[-1] == ("join",)
+
+
+def test_gathers_appear_in_the_collective_trace():
+    eng, pg, native, h = _setup(("emb", "l0"))
+    records = []
+    pg.record_gather = lambda *rec: records.append(rec)  # what TracingCollectives.record_external receives
+    pg.after_store_write(next_plan=False)
+    _step(pg, h, ["emb", "l0"])
+    labels = [r[1] for r in records]
+    assert labels == ["stage3.forward.allgather.emb", "stage3.forward.allgather.l0",
+                      "stage3.backward.allgather.l0", "stage3.backward.allgather.emb"]
+    assert all(r[0] == "allgather" and r[2] == 64 and r[3] == 128 for r in records)
