@@ -59,7 +59,7 @@ def add_training_args(p: argparse.ArgumentParser, *, model_size: str, steps: int
 
 
 def add_bandwidth_args(p: argparse.ArgumentParser, *, mode: str = "socket") -> None:
-    p.add_argument("--bandwidth-mode", type=str, default=mode, choices=["simulated", "none", "tc", "socket"])
+    p.add_argument("--bandwidth-mode", type=str, default=mode, choices=["simulated", "none", "tc", "socket", "nvlink"])
     p.add_argument("--sim-latency-ms", type=float, default=0.0)
     p.add_argument("--tc-interface", type=str, default="eth0")
     p.add_argument("--socket-interface", type=str, default="lo")

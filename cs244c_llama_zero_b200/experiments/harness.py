@@ -142,7 +142,9 @@ def _build_parser() -> argparse.ArgumentParser:
     p.add_argument("--profile-memory-interval", type=int, default=0)
     p.add_argument("--metrics-warmup-steps", type=int, default=0,
                    help="Ignore this many logged training steps when computing mean step metrics.")
-    p.add_argument("--bandwidth-mode", type=str, default="simulated", choices=["simulated", "none", "tc", "socket"])
+    p.add_argument("--bandwidth-mode", type=str, default="simulated",
+                   choices=["simulated", "none", "tc", "socket", "nvlink"],
+                   help="nvlink: device-paced emulated link for --collective-impl nvls|p2p (Gbit/s)")
     p.add_argument("--sim-latency-ms", type=float, default=0.0)
     p.add_argument("--tc-interface", type=str, default="eth0")
     p.add_argument("--socket-interface", type=str, default="lo")
@@ -325,13 +327,20 @@ def _build_launch_env(case: CaseConfig, socket_shaper_path: Optional[Path] = Non
     env["PYTHONUNBUFFERED"] = "1"
     env["ZERO_COLLECTIVE_CUDA_SYNC"] = "1"
     for key in ("ZERO_SIM_BW_GBPS", "ZERO_SIM_LATENCY_MS", "ZERO_SOCKET_SHAPER_BW_GBPS", "ZERO_SOCKET_SHAPER_LATENCY_MS",
-                "ZERO_SOCKET_SHAPER_BURST_BYTES", "ZERO_SOCKET_SHAPER_SHARED_NAME"):
+                "ZERO_SOCKET_SHAPER_BURST_BYTES", "ZERO_SOCKET_SHAPER_SHARED_NAME", "ZERO_NVLINK_BW_GBPS",
+                "ZERO_NVLINK_LATENCY_MS"):
         env.pop(key, None)
     if case.bandwidth_mode == "simulated":
         if case.bandwidth_gbps > 0:
             env["ZERO_SIM_BW_GBPS"] = str(case.bandwidth_gbps)
         if case.sim_latency_ms > 0:
             env["ZERO_SIM_LATENCY_MS"] = str(case.sim_latency_ms)
+    if case.bandwidth_mode == "nvlink":
+        # Paced on the device by the NVLink collective runtime (parallel/comm/pacing.py).
+        if case.bandwidth_gbps > 0:
+            env["ZERO_NVLINK_BW_GBPS"] = str(case.bandwidth_gbps)
+        if case.sim_latency_ms > 0:
+            env["ZERO_NVLINK_LATENCY_MS"] = str(case.sim_latency_ms)
     if case.bandwidth_mode == "socket":
         if socket_shaper_path is None:
             raise ValueError("socket shaper path is required for bandwidth-mode=socket")
@@ -467,6 +476,8 @@ def run_matrix(args: argparse.Namespace) -> Dict[str, object]:
     launch = _launch_config_from_args(args)
     if args.bandwidth_mode == "tc" and shutil.which("tc") is None:
         raise FileNotFoundError("bandwidth mode 'tc' requires the 'tc' command to be installed")
+    if args.bandwidth_mode == "nvlink" and args.collective_impl not in ("nvls", "p2p"):
+        raise ValueError("bandwidth mode 'nvlink' paces the NVLink collective kernels: use --collective-impl nvls or p2p")
     run_dir = Path(args.results_dir) / args.name
     run_dir.mkdir(parents=True, exist_ok=True)
     cases = _build_cases(args)

@@ -4,6 +4,8 @@
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/extension.h>
 
+#include <cmath>
+#include <memory>
 #include <optional>
 
 #include "comm.h"
@@ -537,6 +539,59 @@ class CommContext {
   c10::Device device_;
 };
 
+// Cost in ns of `link_bytes` bytes on an emulated link of `gbps` Gbit/s plus a fixed latency
+// (bits / (Gbit/s) = ns).  gbps <= 0 means no bandwidth term.
+int64_t pace_cost_ns(int64_t link_bytes, double gbps, double latency_ms) {
+  double ns = latency_ms > 0 ? latency_ms * 1e6 : 0.0;
+  if (gbps > 0) ns += 8.0 * (double)link_bytes / gbps;
+  return (int64_t)std::llround(ns);
+}
+
+// One GPU's emulated link for the `nvlink` bandwidth mode: owns the device state of the paced
+// transfers (link free time + start stamps) and hands out stamp slots round-robin.  Shared by the
+// collectives on the compute stream and the ZeRO-3 gathers on their side stream, so both queue on
+// the same link.
+class LinkPacer {
+ public:
+  LinkPacer(int64_t device_index, double gbps, double latency_ms, int64_t timeout_ns)
+      : device_(c10::Device(c10::DeviceType::CUDA, (c10::DeviceIndex)device_index)),
+        gbps_(gbps), latency_ms_(latency_ms), timeout_ns_(timeout_ns) {
+    c10::cuda::CUDAGuard g(device_);
+    state_ = at::zeros({1 + b200::kPaceSlots}, at::TensorOptions().dtype(at::kLong).device(device_));
+  }
+  int64_t cost_ns(int64_t link_bytes) const { return pace_cost_ns(link_bytes, gbps_, latency_ms_); }
+  int64_t begin_on(cudaStream_t s) {
+    c10::cuda::CUDAGuard g(device_);
+    const int slot = (int)(next_++ % b200::kPaceSlots);
+    b200::comm_pace_begin(state(), slot, s);
+    return slot;
+  }
+  void end_on(int64_t slot, int64_t link_bytes, cudaStream_t s) {
+    c10::cuda::CUDAGuard g(device_);
+    b200::comm_pace_end(state(), (int)slot, (uint64_t)cost_ns(link_bytes), (uint64_t)timeout_ns_,
+                        b200::device_errors_ptr(), s);
+  }
+  int64_t begin() {
+    c10::cuda::CUDAGuard g(device_);
+    return begin_on(cur_stream());
+  }
+  void end(int64_t slot, int64_t link_bytes) {
+    c10::cuda::CUDAGuard g(device_);
+    end_on(slot, link_bytes, cur_stream());
+  }
+  double gbps() const { return gbps_; }
+  double latency_ms() const { return latency_ms_; }
+  Tensor state_tensor() const { return state_; }
+
+ private:
+  uint64_t* state() { return reinterpret_cast<uint64_t*>(state_.data_ptr<int64_t>()); }
+  c10::Device device_;
+  double gbps_, latency_ms_;
+  int64_t timeout_ns_;
+  Tensor state_;
+  uint64_t next_ = 0;
+};
+
 // Stream/event plumbing of the ZeRO-3 prefetching parameter gather, kept native so that one module's
 // prefetch costs one call from Python.  Slots are staging buffers; for each slot the object keeps
 // the event that the last gather into it finished (`written`) and the event that its last reader
@@ -638,6 +693,9 @@ class PullGather {
   }
   void reset_times() { take_times(); }
   int64_t side_stream() const { return (int64_t)side_.stream(); }
+  // Pace every later gather on `pacer`'s emulated link (None: stop pacing).  A gather moves
+  // (world - 1) shards across this GPU's link.
+  void set_pacer(std::shared_ptr<LinkPacer> pacer) { pacer_ = std::move(pacer); }
 
  private:
   struct Timed {
@@ -664,7 +722,9 @@ class PullGather {
       t.end = timing_event();
       B200_CUDA_CHECK(cudaEventRecord(t.start, s));
     }
+    const int64_t slot = pacer_ ? pacer_->begin_on(s) : -1;
     ctx.gather_ce_on(off, chunk_bytes, reinterpret_cast<void*>(dst), s);
+    if (pacer_) pacer_->end_on(slot, (ctx.world() - 1) * chunk_bytes, s);
     if (timed) {
       B200_CUDA_CHECK(cudaEventRecord(t.end, s));
       timed_.push_back(t);
@@ -679,6 +739,7 @@ class PullGather {
   std::vector<Timed> timed_;
   std::vector<double> ms_;
   std::vector<int64_t> calls_;
+  std::shared_ptr<LinkPacer> pacer_;
 };
 
 int64_t launch_count() { return b200::launch_counter().load(); }
@@ -741,6 +802,16 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
       .def("wait_unsignalled", &CommContext::wait_unsignalled)
       .def_property_readonly("multicast", &CommContext::multicast)
       .def_property_readonly("blocks", &CommContext::blocks);
+  m.def("pace_cost_ns", &pace_cost_ns, py::arg("link_bytes"), py::arg("gbps"), py::arg("latency_ms"));
+  py::class_<LinkPacer, std::shared_ptr<LinkPacer>>(m, "LinkPacer")
+      .def(py::init<int64_t, double, double, int64_t>(), py::arg("device_index"), py::arg("gbps"),
+           py::arg("latency_ms"), py::arg("timeout_ns"))
+      .def("cost_ns", &LinkPacer::cost_ns)
+      .def("begin", &LinkPacer::begin)
+      .def("end", &LinkPacer::end)
+      .def_property_readonly("gbps", &LinkPacer::gbps)
+      .def_property_readonly("latency_ms", &LinkPacer::latency_ms)
+      .def_property_readonly("state", &LinkPacer::state_tensor);
   py::class_<PullGather>(m, "PullGather")
       .def(py::init<int64_t, int64_t, int64_t>(), py::arg("slots"), py::arg("categories"), py::arg("device_index"))
       .def("prefetch", &PullGather::prefetch)
@@ -751,6 +822,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
       .def("join", &PullGather::join)
       .def("take_times", &PullGather::take_times)
       .def("reset_times", &PullGather::reset_times)
+      .def("set_pacer", &PullGather::set_pacer, py::arg("pacer").none(true))
       .def_property_readonly("side_stream", &PullGather::side_stream);
 
 }

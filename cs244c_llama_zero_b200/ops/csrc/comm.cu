@@ -395,6 +395,38 @@ __global__ void wait_unsignalled_kernel(CommCtx c, uint64_t timeout_ns) {
   }
 }
 
+__global__ void pace_begin_kernel(uint64_t* state, int slot) {
+  if (threadIdx.x == 0) state[1 + slot] = globaltimer_ns();
+}
+
+// One thread books the link with a compare-and-swap on state[0], then sleeps until the booking ends.
+__global__ void pace_end_kernel(uint64_t* state, int slot, uint64_t cost_ns, uint64_t timeout_ns,
+                                DeviceErrors* errs) {
+  if (threadIdx.x != 0) return;
+  auto* link = reinterpret_cast<unsigned long long*>(state);
+  const uint64_t stamp = *reinterpret_cast<volatile uint64_t*>(state + 1 + slot);
+  unsigned long long seen = *reinterpret_cast<volatile unsigned long long*>(link);
+  unsigned long long done;
+  while (true) {
+    done = (unsigned long long)max((uint64_t)seen, stamp) + cost_ns;
+    const unsigned long long prev = atomicCAS(link, seen, done);
+    if (prev == seen) break;
+    seen = prev;
+  }
+  const uint64_t t0 = globaltimer_ns();
+  if (done > t0 && done - t0 > timeout_ns) {  // a booking beyond the bound: report it instead of waiting
+    report_error(errs, kErrPaceWait, slot);
+    return;
+  }
+  for (uint64_t now = t0; now < done; now = globaltimer_ns()) {
+    if (now - t0 > timeout_ns) {
+      report_error(errs, kErrPaceWait, slot);
+      return;
+    }
+    __nanosleep(done - now > 20000 ? 10000u : 500u);
+  }
+}
+
 void check_ctx(const CommCtx& c) {
   B200_CHECK(c.world >= 1 && c.world <= kCommMaxWorld, "comm: world size out of range");
   B200_CHECK(c.blocks >= 1 && c.blocks < kCommMaxBlocks, "comm: block count out of range");
@@ -522,6 +554,21 @@ void comm_adamw_allgather(const CommCtx& c, size_t param_off, size_t chunk, floa
 void comm_barrier(const CommCtx& c, cudaStream_t s) {
   check_ctx(c);
   barrier_kernel<<<c.blocks, 32, 0, s>>>(c);
+  B200_CUDA_CHECK(cudaGetLastError());
+  count_launch();
+}
+
+void comm_pace_begin(uint64_t* state, int slot, cudaStream_t s) {
+  B200_CHECK(slot >= 0 && slot < kPaceSlots, "comm_pace_begin: slot out of range");
+  pace_begin_kernel<<<1, 32, 0, s>>>(state, slot);
+  B200_CUDA_CHECK(cudaGetLastError());
+  count_launch();
+}
+
+void comm_pace_end(uint64_t* state, int slot, uint64_t cost_ns, uint64_t timeout_ns, DeviceErrors* errs,
+                   cudaStream_t s) {
+  B200_CHECK(slot >= 0 && slot < kPaceSlots, "comm_pace_end: slot out of range");
+  pace_end_kernel<<<1, 32, 0, s>>>(state, slot, cost_ns, timeout_ns, errs);
   B200_CUDA_CHECK(cudaGetLastError());
   count_launch();
 }

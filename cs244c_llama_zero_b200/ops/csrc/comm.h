@@ -59,4 +59,17 @@ void comm_barrier(const CommCtx& c, cudaStream_t s);
 // A wait that nobody satisfies: used by tests to exercise the bounded-wait error path.
 void comm_wait_unsignalled(const CommCtx& c, uint64_t timeout_ns, cudaStream_t s);
 
+// Device-paced link emulation (the `nvlink` bandwidth mode of the experiment harness): every paced
+// transfer of one GPU books one emulated link.  `state` is a device array of 1 + kPaceSlots words:
+// state[0] is the %globaltimer time at which the link is next free, state[1 + slot] the start stamp
+// of the transfer using `slot`.  pace_begin stamps the clock on stream s before the transfer;
+// pace_end, after it, books the link for cost_ns starting at max(stamp, link free time) and holds
+// the stream until that booking ends, so the transfer takes max(its own time, its share of the
+// link).  Transfers on several streams queue on the same link.  The hold is bounded by timeout_ns
+// (the error record gets kErrPaceWait when it runs out).
+constexpr int kPaceSlots = 1024;
+void comm_pace_begin(uint64_t* state, int slot, cudaStream_t s);
+void comm_pace_end(uint64_t* state, int slot, uint64_t cost_ns, uint64_t timeout_ns, DeviceErrors* errs,
+                   cudaStream_t s);
+
 }  // namespace b200

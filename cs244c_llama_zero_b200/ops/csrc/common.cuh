@@ -88,6 +88,7 @@ enum : int {
   kErrAttnWait = 2,
   kErrCommWait = 3,
   kErrCommBarrier = 4,
+  kErrPaceWait = 5,
 };
 
 // ---------------------------------------------------------------------------------------

@@ -20,6 +20,9 @@ tensors that are not part of a registered symmetric buffer (and the reference-co
 
 Every device-side wait is bounded (``ZB_COMM_TIMEOUT_S``, default 30 s); an expired wait is recorded in
 the device error record, which :meth:`NvlinkCollectives.check_errors` turns into a ``CommTimeoutError``.
+
+With ``ZERO_NVLINK_BW_GBPS`` / ``ZERO_NVLINK_LATENCY_MS`` set, every transfer above is paced on the
+device to an emulated link of that bandwidth (:mod:`.pacing`; the harness's ``nvlink`` bandwidth mode).
 """
 
 from __future__ import annotations
@@ -31,6 +34,7 @@ import torch
 import torch.distributed as dist
 
 from ..collectives import TorchCollectives, _maybe_simulate_collective_delay, _world
+from .pacing import link_bytes, make_pacer
 
 
 class CommTimeoutError(RuntimeError):
@@ -39,6 +43,11 @@ class CommTimeoutError(RuntimeError):
 
 def _timeout_ns() -> int:
     return int(float(os.environ.get("ZB_COMM_TIMEOUT_S", "30")) * 1e9)
+
+
+def _pace_timeout_ns() -> int:
+    """Bound on one paced hold (it also waits out the transfers queued before it on the link)."""
+    return int(float(os.environ.get("ZB_PACE_TIMEOUT_S", "120")) * 1e9)
 
 
 class SymmetricBuffer:
@@ -85,6 +94,14 @@ class NvlinkCollectives(TorchCollectives):
         self.device = device or torch.device("cuda", torch.cuda.current_device())
         self.use_multicast = use_multicast
         self.buffers: List[SymmetricBuffer] = []
+        self.pacer = make_pacer(self.device, _pace_timeout_ns())  # None unless the nvlink bandwidth mode is on
+
+    def _pace_begin(self) -> int:
+        return self.pacer.begin() if self.pacer is not None else -1
+
+    def _pace_end(self, slot: int, op: str, full_bytes: int) -> None:
+        if self.pacer is not None:
+            self.pacer.end(slot, link_bytes(op, full_bytes, self._w()))
 
     # -- allocation --------------------------------------------------------------------------
     def alloc(self, numel: int, dtype: torch.dtype) -> torch.Tensor:
@@ -120,10 +137,12 @@ class NvlinkCollectives(TorchCollectives):
         if hit is None or flat.dtype not in (torch.float32, torch.bfloat16) or flat.numel() % 8:
             return super().allreduce_scaled_(flat, scale)
         buf, off = hit
+        slot = self._pace_begin()
         if flat.dtype == torch.float32:
             buf.ctx.allreduce_f32(off, flat.numel(), scale)
         else:
             buf.ctx.allreduce_bf16(off, flat.numel(), scale)
+        self._pace_end(slot, "allreduce", flat.numel() * flat.element_size())
         _maybe_simulate_collective_delay(flat.numel() * flat.element_size(), self._w())
         return flat
 
@@ -134,10 +153,12 @@ class NvlinkCollectives(TorchCollectives):
                 or acc.dtype != torch.float32):
             return super().reduce_scatter_accumulate_(acc, flat, scale)
         buf, off = hit
+        slot = self._pace_begin()
         if flat.dtype == torch.float32:
             buf.ctx.reduce_scatter_acc_f32(off, flat.numel() // world, acc, scale)
         else:
             buf.ctx.reduce_scatter_acc_bf16(off, flat.numel() // world, acc, scale)
+        self._pace_end(slot, "reduce_scatter", flat.numel() * flat.element_size())
         _maybe_simulate_collective_delay(acc.numel() * flat.element_size(), world)
         return acc
 
@@ -165,7 +186,9 @@ class NvlinkCollectives(TorchCollectives):
             acc = shard_acc
         else:
             acc = shard_acc[a - shard_lo:]
+        slot = self._pace_begin()
         buf.ctx.reduce_scatter_range_acc_f32(off + lo * 4, a - lo, b - lo, acc, scale, int(blocks))
+        self._pace_end(slot, "reduce_scatter", (hi - lo) * 4)
         return True
 
     def reduce_scatter_into(self, out: torch.Tensor, flat: torch.Tensor) -> torch.Tensor:
@@ -182,7 +205,9 @@ class NvlinkCollectives(TorchCollectives):
                 or shard.dtype != out.dtype):
             return super().allgather_into(out, shard)
         buf, off = hit
+        slot = self._pace_begin()
         buf.ctx.allgather(off, chunk_bytes, shard)
+        self._pace_end(slot, "allgather", chunk_bytes * world)
         _maybe_simulate_collective_delay(chunk_bytes, world)
         return out
 
@@ -203,7 +228,9 @@ class NvlinkCollectives(TorchCollectives):
                 or not out.is_contiguous() or not out.is_cuda):
             return False
         buf, off = hit
+        slot = self._pace_begin()
         buf.ctx.gather_ce(off, nbytes, out)
+        self._pace_end(slot, "allgather", nbytes * world)
         _maybe_simulate_collective_delay(nbytes, world)
         return True
 
@@ -219,8 +246,10 @@ class NvlinkCollectives(TorchCollectives):
         buf, off = hit
         scale_t = scale.reshape(1).float() if isinstance(scale, torch.Tensor) else None
         scale_c = 1.0 if isinstance(scale, torch.Tensor) else float(scale if scale is not None else 1.0)
+        slot = self._pace_begin()
         buf.ctx.adamw_allgather(off, chunk, master, exp_avg, exp_avg_sq, grad.contiguous(), scale_t, scale_c, cfg.lr,
                                 cfg.betas[0], cfg.betas[1], cfg.eps, cfg.weight_decay, step)
+        self._pace_end(slot, "allgather", chunk * 2 * world)
         return True
 
     def barrier(self) -> None:

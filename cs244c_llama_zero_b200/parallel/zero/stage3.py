@@ -343,6 +343,9 @@ class _PullGather:
             native = ops.load_extension().PullGather(len(slots), len(self.CATEGORIES), dev)
         self.native = native
         coll = engine.collectives
+        pacer = getattr(coll, "pacer", None)  # nvlink bandwidth mode: gathers queue on the emulated link
+        if pacer is not None:
+            native.set_pacer(pacer)
         elsize = store.element_size()
         self.where: Dict[int, Tuple[object, int, int]] = {}  # id(handle) -> (comm context, byte offset, chunk bytes)
         for h in engine._handle_order:
