@@ -41,6 +41,7 @@ from .common import (
     unique_trainable_params,
 )
 from ..collectives import _maybe_simulate_collective_delay
+from ...profiler import nvtx
 from .optim import adamw_update_, clip_coefficient, sum_of_squares
 
 
@@ -384,6 +385,8 @@ class _PullGather:
         self.engine.clock.count(self.CATEGORIES[cat], handle.full_param_bytes)
         ctx, off, nbytes = self.where[id(handle)]
         issue = self.native.prefetch if prefetch else self.native.gather_now
+        if nvtx.enabled():
+            nvtx.mark(f"stage3.{phase}.{'prefetch' if prefetch else 'gather'}.{handle.name}")
         t0 = time.perf_counter()
         issue(ctx, slot, off, nbytes, self.slot_ptrs[slot], cat, True)
         if self.simulate:

@@ -5,6 +5,7 @@ from .flops import (
     executed_train_flops,
     flops_to_tflops_per_second,
 )
+from . import nvtx
 from .memory import MemorySnapshot, MemoryTracker, take_memory_snapshot
 from .overlap import overlap_efficiency
 from .timer import NamedTimer, TimerRegistry, TimerSummary
@@ -22,4 +23,5 @@ __all__ = [
     "NamedTimer",
     "TimerRegistry",
     "TimerSummary",
+    "nvtx",
 ]

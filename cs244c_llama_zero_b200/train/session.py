@@ -27,6 +27,7 @@ import torch.distributed as dist
 from ..models import BASELINE_VOCAB_SIZE, LlamaForCausalLM, ModelConfig, build_config
 from ..parallel.collectives import TracingCollectives, pick_collectives
 from ..parallel.zero import ENGINES
+from ..profiler.nvtx import nvtx_range
 
 
 @dataclass
@@ -150,9 +151,11 @@ class TrainSession:
         n = len(micro_batches)
         for ids in micro_batches:
             ids = self._to_device(ids)
-            with torch.autocast(device_type=self.device.type, dtype=torch.bfloat16, enabled=self.autocast):
+            with nvtx_range("forward"), torch.autocast(device_type=self.device.type, dtype=torch.bfloat16,
+                                                       enabled=self.autocast):
                 loss = self.model(input_ids=ids, labels=ids, return_logits=False).loss
-            self.engine.backward(loss / n)
+            with nvtx_range("backward"):
+                self.engine.backward(loss / n)
             total = total + loss.detach().float()
         return total / n
 
@@ -163,7 +166,8 @@ class TrainSession:
         self.engine.zero_grad()
         self.engine.prepare_forward()
         loss = self.forward_backward(micro)
-        self.engine.step_async(max_grad_norm=self.cfg.max_grad_norm)
+        with nvtx_range("optimizer"):
+            self.engine.step_async(max_grad_norm=self.cfg.max_grad_norm)
         return loss
 
     def train_step_async(self, input_ids: torch.Tensor) -> "AsyncLoss":

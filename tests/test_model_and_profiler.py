@@ -177,3 +177,29 @@ def test_tracing_collectives_and_aggregation():
         {"op": "allgather", "label": "l0", "calls": 2, "elapsed_ms": 5.0, "input_bytes": 8.0, "output_bytes": 32.0},
         {"op": "reduce_scatter", "label": "l1", "calls": 1, "elapsed_ms": 1.5, "input_bytes": 16.0,
          "output_bytes": 4.0}]
+
+
+def test_nvtx_ranges_are_balanced_and_off_by_default(monkeypatch):
+    from cs244c_llama_zero_b200.profiler import nvtx
+
+    calls = []
+    monkeypatch.setattr(torch.cuda.nvtx, "range_push", lambda name: calls.append(("push", name)))
+    monkeypatch.setattr(torch.cuda.nvtx, "range_pop", lambda: calls.append(("pop",)))
+    monkeypatch.setattr(torch.cuda.nvtx, "mark", lambda name: calls.append(("mark", name)))
+    was = nvtx.enabled()
+    try:
+        nvtx.enable(False)
+        with nvtx.nvtx_range("off"):
+            nvtx.mark("off")
+        assert calls == []
+        nvtx.enable(True)
+        with nvtx.nvtx_range("step"):
+            with nvtx.nvtx_range("forward"):
+                nvtx.mark("m")
+        with pytest.raises(RuntimeError):
+            with nvtx.nvtx_range("raises"):
+                raise RuntimeError("x")
+        assert calls == [("push", "step"), ("push", "forward"), ("mark", "m"), ("pop",), ("pop",),
+                         ("push", "raises"), ("pop",)]
+    finally:
+        nvtx.enable(was)

@@ -39,6 +39,8 @@ from cs244c_llama_zero_b200.profiler import (
     flops_to_tflops_per_second,
     overlap_efficiency,
 )
+from cs244c_llama_zero_b200.profiler import nvtx
+from cs244c_llama_zero_b200.profiler.nvtx import nvtx_range
 from cs244c_llama_zero_b200.train.faults import FaultInjector
 from cs244c_llama_zero_b200.train.session import init_distributed
 from train import (
@@ -108,6 +110,7 @@ def parse_args(argv=None) -> argparse.Namespace:
     p.add_argument("--measure-memory-step", action="store_true")
     p.add_argument("--memory-warmup-steps", type=int, default=0)
     p.add_argument("--tflops-mode", type=str, default="estimate", choices=["estimate", "profile", "off"])
+    p.add_argument("--nvtx", action="store_true", help="name the step phases with NVTX ranges (Nsight timelines)")
     p.add_argument("--verbose", action="store_true")
     p.add_argument("--verbose-memory", action="store_true")
     p.add_argument("--stage3-recompute", action="store_true",
@@ -222,6 +225,8 @@ def train(args: argparse.Namespace) -> None:
     rank, world_size, device = init_distributed(args.pg_timeout_s)
     faults = FaultInjector(rank)
     verbose = bool(args.verbose)
+    if getattr(args, "nvtx", False):
+        nvtx.enable(True)
     configure_runtime(device)
     set_seed(args.seed)
     log_event(rank, f"initialized distributed world_size={world_size} device={device} pid={os.getpid()}", force=verbose)
@@ -305,7 +310,9 @@ def train(args: argparse.Namespace) -> None:
             memory.reset_peak_stats()
             engine.memory_trace_active = recorder.enabled
         snap("start")
-        prepare_comm_ms = float(engine.prepare_forward().get("prepare_comm_ms", 0.0))
+        nvtx.mark(f"step {step}")
+        with nvtx_range("prepare_forward"):
+            prepare_comm_ms = float(engine.prepare_forward().get("prepare_comm_ms", 0.0))
         snap("post_prepare")
         fb_timer = timers.timer("forward_backward")
         fb_timer.start()
@@ -322,11 +329,12 @@ def train(args: argparse.Namespace) -> None:
                 batch = batch_from_chunk(chunk)
                 ids = batch.input_ids.to(device, non_blocking=True)
                 labels = batch.labels.to(device, non_blocking=True)
-                with autocast_context(device, args.dtype):
+                with nvtx_range(f"forward.micro{micro + 1}"), autocast_context(device, args.dtype):
                     loss = model(input_ids=ids, labels=labels, return_logits=False).loss
                 snap(f"micro_{micro + 1}_after_forward")
                 losses.append(loss.detach().float())
-                engine.backward(loss / args.grad_accum_steps)
+                with nvtx_range(f"backward.micro{micro + 1}"):
+                    engine.backward(loss / args.grad_accum_steps)
                 snap(f"micro_{micro + 1}_after_backward")
             return losses
 
@@ -340,7 +348,8 @@ def train(args: argparse.Namespace) -> None:
         snap("post_backward")
         opt_timer = timers.timer("optimizer_step")
         opt_timer.start()
-        stats = engine.step_with_stats(max_grad_norm=args.max_grad_norm)
+        with nvtx_range("optimizer"):
+            stats = engine.step_with_stats(max_grad_norm=args.max_grad_norm)
         opt_timer.stop()
         grad_norm = float(stats["grad_norm"])
         comm_ms = float(stats["comm_ms"]) + prepare_comm_ms
