@@ -277,11 +277,14 @@ def run_mine(args) -> None:
                 h2d = host[0].numel() * host[0].element_size()
 
                 pending = []
+                d2h = 0
 
                 def e2e_step():
                     # pinned host batch -> device inside train_step; the step's loss is copied to
                     # pinned host memory and read (.item()) after the next step has been queued
+                    nonlocal d2h
                     pending.append(sess.train_step_async(host[it["i"] % len(host)]))
+                    d2h = pending[-1].nbytes  # loss + the kernels' error record
                     it["i"] += 1
                     if len(pending) > 1:
                         losses.append(pending.pop(0).item())
@@ -299,9 +302,9 @@ def run_mine(args) -> None:
                 if len(losses) != args.steps or not all(math.isfinite(x) for x in losses):
                     raise RuntimeError(f"e2e: expected {args.steps} finite losses, got {losses}")
                 e2e = {"value": tokens_per_step / (e2e_ms / 1000.0), "unit": "tokens/s",
-                       "ms_per_step": e2e_ms, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 4,
+                       "ms_per_step": e2e_ms, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                        "api": "cs244c_llama_zero_b200.train.TrainSession.train_step_async(pinned host int64 [B,S])"
-                              " + AsyncLoss.item() one step later (every step's loss read on the host)"}
+                              " + AsyncLoss.item() one step later (every step's loss and error record read on the host)"}
         per_stage[str(stage)] = entry
         del sess
         torch.cuda.empty_cache()

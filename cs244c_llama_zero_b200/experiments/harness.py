@@ -102,6 +102,9 @@ class CaseResult:
     theoretical_param_count: int
     theoretical_memory_mb: Dict[str, float]
     notes: str = ""
+    # Extra (not in the reference's record): the same idealised state memory with the run's dtype
+    # (bf16 params and grads plus an fp32 master copy next to the Adam moments).
+    theoretical_memory_dtype_mb: Optional[Dict[str, float]] = None
 
 
 @dataclass(frozen=True)
@@ -236,6 +239,18 @@ def _theoretical_memory(case: CaseConfig) -> tuple:
     mb = 1024.0 * 1024.0
     params, grads, opt = 4.0 * n / dp / mb, 4.0 * n / dg / mb, 8.0 * n / do / mb
     return n, {"params_mb": params, "grads_mb": grads, "optimizer_mb": opt, "total_mb": params + grads + opt}
+
+
+def _theoretical_memory_dtype(case: CaseConfig, n_params: int) -> Dict[str, float]:
+    """State memory with the run's dtype: params and grads at its element size, Adam moments fp32 (8 B)
+    plus an fp32 master copy (4 B) when the params are not fp32; ideal 1/W sharding per stage."""
+    elem = {"float32": 4, "bfloat16": 2, "float16": 2}.get(case.dtype, 4)
+    w = max(1, case.nproc_per_node)
+    dp, dg, do = {0: (1, 1, 1), 1: (1, 1, w), 2: (1, w, w), 3: (w, w, w)}[case.stage]
+    mb = 1024.0 * 1024.0
+    opt_bytes = 8.0 + (4.0 if elem != 4 else 0.0)
+    params, grads, opt = elem * n_params / dp / mb, elem * n_params / dg / mb, opt_bytes * n_params / do / mb
+    return {"params_mb": params, "grads_mb": grads, "optimizer_mb": opt, "total_mb": params + grads + opt}
 
 
 def _parse_step_metrics(log_text: str, metrics_warmup_steps: int = 0) -> Dict[str, object]:
@@ -420,7 +435,8 @@ def _run_case(case: CaseConfig, run_dir: Path, skip_existing: bool, dry_run: boo
     def finish(rc: int, elapsed: float, metrics: Dict[str, object], mem: Dict[str, object], notes: str) -> CaseResult:
         result = CaseResult(case_id=case_id, config=asdict(case), command=command, return_code=rc, elapsed_s=elapsed,
                             log_path=str(log_path), profile_path=str(profile_path), **metrics, **mem,
-                            theoretical_param_count=n_params, theoretical_memory_mb=theory, notes=notes)
+                            theoretical_param_count=n_params, theoretical_memory_mb=theory, notes=notes,
+                            theoretical_memory_dtype_mb=_theoretical_memory_dtype(case, n_params))
         result_path.write_text(json.dumps(asdict(result), indent=2))
         return result
 

@@ -44,6 +44,45 @@ def require_extension():
     return load_extension()
 
 
+class DeviceWaitError(RuntimeError):
+    """A bounded device-side wait of one of this package's kernels ran out and the kernel gave up.
+
+    Every spin in the kernels (GEMM / attention pipeline barriers, collective barriers, paced link
+    holds) has a deadline; on expiry the kernel writes ``(code, where, block, count)`` into the
+    device's error record and returns instead of hanging, so the context stays usable and the host
+    raises this error at its next check.  Index inputs that are out of range (a token id >= vocab)
+    are recorded the same way, with the access skipped instead of faulting.
+    """
+
+
+class CommTimeoutError(DeviceWaitError):
+    """A collective kernel's wait for a peer expired (the peer never arrived or never signalled)."""
+
+
+ERROR_NAMES = {1: "gemm pipeline wait", 2: "attention pipeline wait", 3: "collective wait",
+               4: "collective barrier", 5: "paced link hold", 6: "index out of range (access skipped)"}
+COMM_CODES = (3, 4)
+
+
+def raise_for_device_errors(words) -> None:
+    """Raise for an error record ``(code, where, block, count)``; no-op when ``code`` is 0."""
+    code, where, block, count = (int(w) for w in list(words)[:4])
+    if code == 0:
+        return
+    cls = CommTimeoutError if code in COMM_CODES else DeviceWaitError
+    raise cls(f"device error record: {ERROR_NAMES.get(code, f'code {code}')} "
+              f"(code {code}, peer/role {where}, block {block}, {count} reports)")
+
+
+def check_device_errors(reset: bool = False) -> None:
+    """Read the current device's error record (synchronising) and raise if a wait expired."""
+    ext = load_extension()
+    words = ext.read_device_errors()
+    if reset and words[0]:
+        ext.reset_device_errors()
+    raise_for_device_errors(words)
+
+
 def launch_count() -> int:
     """Number of kernels this process has launched through the extension."""
     return int(load_extension().launch_count())

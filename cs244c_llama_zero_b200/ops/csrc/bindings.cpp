@@ -752,6 +752,16 @@ std::vector<int64_t> read_device_errors() {
 
 void reset_device_errors() { B200_CUDA_CHECK(cudaMemset(b200::device_errors_ptr(), 0, sizeof(b200::DeviceErrors))); }
 
+// Copies this device's error record into `host` (pinned int32[4]: code, where, block, count) on the
+// current stream, without synchronising: read it once an event recorded after this call completes.
+void device_errors_to_host(Tensor host) {
+  TORCH_CHECK(!host.is_cuda() && host.is_pinned() && host.scalar_type() == at::kInt && host.numel() >= 4 &&
+                  host.is_contiguous(),
+              "device_errors_to_host: pinned contiguous int32 host tensor of >= 4 elements required");
+  B200_CUDA_CHECK(cudaMemcpyAsync(host.data_ptr<int32_t>(), b200::device_errors_ptr(), sizeof(b200::DeviceErrors),
+                                  cudaMemcpyDeviceToHost, cur_stream()));
+}
+
 }  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -788,6 +798,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("launch_count", &launch_count);
   m.def("read_device_errors", &read_device_errors);
   m.def("reset_device_errors", &reset_device_errors);
+  m.def("device_errors_to_host", &device_errors_to_host);
   py::class_<CommContext>(m, "CommContext")
       .def(py::init<int64_t, int64_t, std::vector<int64_t>, int64_t, std::vector<int64_t>, Tensor, int64_t, int64_t>())
       .def("allreduce_f32", &CommContext::allreduce_f32)

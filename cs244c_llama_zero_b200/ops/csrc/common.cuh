@@ -89,6 +89,7 @@ enum : int {
   kErrCommWait = 3,
   kErrCommBarrier = 4,
   kErrPaceWait = 5,
+  kErrBadIndex = 6,  // an index input out of range (e.g. a token id >= vocab); the access was skipped
 };
 
 // ---------------------------------------------------------------------------------------

@@ -182,7 +182,10 @@ __global__ void embedding_fwd_kernel(const int64_t* __restrict__ ids, const __nv
     const int v = (int)(i % vec_per_row);
     int64_t id = ids[row];
     uint4 val = make_uint4(0, 0, 0, 0);
-    if (id >= 0 && id < vocab) val = *reinterpret_cast<const uint4*>(table + (size_t)id * d + v * 8);
+    if (id >= 0 && id < vocab)
+      val = *reinterpret_cast<const uint4*>(table + (size_t)id * d + v * 8);
+    else if (v == 0)
+      report_error(errs, kErrBadIndex, row);  // the row reads as zeros; the host raises at its next check
     *reinterpret_cast<uint4*>(out + (size_t)row * d + v * 8) = val;
   }
 }

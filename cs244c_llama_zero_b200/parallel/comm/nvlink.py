@@ -33,12 +33,9 @@ from typing import List, Optional, Tuple
 import torch
 import torch.distributed as dist
 
+from ...ops import CommTimeoutError  # re-exported: raised for expired collective waits
 from ..collectives import TorchCollectives, _maybe_simulate_collective_delay, _world
 from .pacing import link_bytes, make_pacer
-
-
-class CommTimeoutError(RuntimeError):
-    """A device-side wait of a collective kernel expired (a peer never arrived)."""
 
 
 def _timeout_ns() -> int:
@@ -95,6 +92,21 @@ class NvlinkCollectives(TorchCollectives):
         self.use_multicast = use_multicast
         self.buffers: List[SymmetricBuffer] = []
         self.pacer = make_pacer(self.device, _pace_timeout_ns())  # None unless the nvlink bandwidth mode is on
+        self._skip = 0  # fault injection: barrier-synchronised collectives left out on purpose
+
+    def skip_next_collective(self, count: int = 1) -> None:
+        """Fault injection: leave out (do not launch) the next ``count`` barrier-synchronised collective
+        kernels of this rank, so the peers' bounded barrier waits expire (``ZB_FAULT=skip_signal``)."""
+        self._skip += int(count)
+
+    def _skipped(self, op: str) -> bool:
+        if self._skip <= 0:
+            return False
+        self._skip -= 1
+        import sys
+
+        print(f"[fault] {op}: kernel left out, no barrier signal posted", file=sys.stderr, flush=True)
+        return True
 
     def _pace_begin(self) -> int:
         return self.pacer.begin() if self.pacer is not None else -1
@@ -125,11 +137,10 @@ class NvlinkCollectives(TorchCollectives):
         return None if hit is None else (hit[0].ctx, hit[1])
 
     def check_errors(self) -> None:
+        """Raise ``CommTimeoutError`` (or ``DeviceWaitError``) if any kernel's bounded wait expired."""
         from ... import ops
 
-        code, where, block, count = ops.load_extension().read_device_errors()
-        if code:
-            raise CommTimeoutError(f"device wait expired (code {code}, peer/role {where}, block {block}, {count} reports)")
+        ops.raise_for_device_errors(ops.load_extension().read_device_errors())
 
     # -- fused entry points ------------------------------------------------------------------------
     def allreduce_scaled_(self, flat: torch.Tensor, scale: float) -> torch.Tensor:
@@ -137,6 +148,8 @@ class NvlinkCollectives(TorchCollectives):
         if hit is None or flat.dtype not in (torch.float32, torch.bfloat16) or flat.numel() % 8:
             return super().allreduce_scaled_(flat, scale)
         buf, off = hit
+        if self._skipped("allreduce"):
+            return flat
         slot = self._pace_begin()
         if flat.dtype == torch.float32:
             buf.ctx.allreduce_f32(off, flat.numel(), scale)
@@ -153,6 +166,8 @@ class NvlinkCollectives(TorchCollectives):
                 or acc.dtype != torch.float32):
             return super().reduce_scatter_accumulate_(acc, flat, scale)
         buf, off = hit
+        if self._skipped("reduce_scatter"):
+            return acc
         slot = self._pace_begin()
         if flat.dtype == torch.float32:
             buf.ctx.reduce_scatter_acc_f32(off, flat.numel() // world, acc, scale)
@@ -186,6 +201,8 @@ class NvlinkCollectives(TorchCollectives):
             acc = shard_acc
         else:
             acc = shard_acc[a - shard_lo:]
+        if self._skipped("reduce_scatter_range"):
+            return True
         slot = self._pace_begin()
         buf.ctx.reduce_scatter_range_acc_f32(off + lo * 4, a - lo, b - lo, acc, scale, int(blocks))
         self._pace_end(slot, "reduce_scatter", (hi - lo) * 4)
@@ -205,6 +222,8 @@ class NvlinkCollectives(TorchCollectives):
                 or shard.dtype != out.dtype):
             return super().allgather_into(out, shard)
         buf, off = hit
+        if self._skipped("allgather"):
+            return out
         slot = self._pace_begin()
         buf.ctx.allgather(off, chunk_bytes, shard)
         self._pace_end(slot, "allgather", chunk_bytes * world)
@@ -246,6 +265,8 @@ class NvlinkCollectives(TorchCollectives):
         buf, off = hit
         scale_t = scale.reshape(1).float() if isinstance(scale, torch.Tensor) else None
         scale_c = 1.0 if isinstance(scale, torch.Tensor) else float(scale if scale is not None else 1.0)
+        if self._skipped("adamw_allgather"):
+            return True
         slot = self._pace_begin()
         buf.ctx.adamw_allgather(off, chunk, master, exp_avg, exp_avg_sq, grad.contiguous(), scale_t, scale_c, cfg.lr,
                                 cfg.betas[0], cfg.betas[1], cfg.eps, cfg.weight_decay, step)
@@ -254,7 +275,8 @@ class NvlinkCollectives(TorchCollectives):
 
     def barrier(self) -> None:
         if self.buffers:
-            self.buffers[0].ctx.barrier()
+            if not self._skipped("barrier"):
+                self.buffers[0].ctx.barrier()
         else:
             dist.barrier()
 

@@ -12,6 +12,10 @@ their next collective (gloo: connection closed; NCCL: the process-group timeout)
 * ``raise_rank:R@S`` - rank R raises :class:`FaultInjected` at the start of step S,
 * ``stall_rank:R@S`` - rank R stops joining: it sleeps ``ZB_FAULT_STALL_S`` seconds (default 3600) at the
   start of step S, so the others' process-group timeout (``--pg-timeout-s``) ends their next collective.
+* ``skip_signal:R@S`` - rank R omits (does not launch) its next NVLink collective kernel after the start of
+  step S, so it never posts that kernel's barrier signal.  The other ranks' barrier waits expire after
+  ``ZB_COMM_TIMEOUT_S``, their kernels record the expiry and return, and the host raises
+  ``CommTimeoutError`` at its next error check.  Needs ``--collective-impl nvls|p2p``.
 """
 
 from __future__ import annotations
@@ -22,7 +26,7 @@ import time
 from dataclasses import dataclass
 from typing import List, Optional
 
-KINDS = ("kill_rank", "raise_rank", "stall_rank")
+KINDS = ("kill_rank", "raise_rank", "stall_rank", "skip_signal")
 
 
 class FaultInjected(RuntimeError):
@@ -64,11 +68,17 @@ class FaultInjector:
     def __bool__(self) -> bool:
         return bool(self.faults)
 
-    def at_step(self, step: int) -> None:
+    def at_step(self, step: int, collectives=None) -> None:
         for f in self.faults:
             if f.step != step:
                 continue
             print(f"[fault] rank {self.rank}: injecting {f.kind} at step {step}", file=sys.stderr, flush=True)
+            if f.kind == "skip_signal":
+                arm = getattr(collectives, "skip_next_collective", None)
+                if arm is None:
+                    raise ValueError("skip_signal needs the NVLink collectives (--collective-impl nvls|p2p)")
+                arm()
+                continue
             if f.kind == "kill_rank":
                 os._exit(int(os.environ.get("ZB_FAULT_EXIT_CODE", "43")))
             if f.kind == "raise_rank":

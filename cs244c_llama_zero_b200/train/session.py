@@ -92,14 +92,27 @@ class AsyncLoss:
     further steps.
     """
 
-    def __init__(self, host: torch.Tensor, event: Optional["torch.cuda.Event"]) -> None:
+    def __init__(self, host: torch.Tensor, event: Optional["torch.cuda.Event"],
+                 errors: Optional[torch.Tensor] = None) -> None:
         self._host = host
         self._event = event
+        self._errors = errors  # pinned copy of the device error record taken with the loss
 
     def item(self) -> float:
+        """The loss; raises ``DeviceWaitError`` if a kernel's bounded wait expired up to this step."""
         if self._event is not None:
             self._event.synchronize()
+        if self._errors is not None:
+            from ..ops import raise_for_device_errors
+
+            raise_for_device_errors(self._errors.tolist())
         return float(self._host[0])
+
+    @property
+    def nbytes(self) -> int:
+        """Bytes this handle brings back to the host (loss + error record)."""
+        extra = 0 if self._errors is None else self._errors.numel() * self._errors.element_size()
+        return self._host.numel() * self._host.element_size() + extra
 
 
 class TrainSession:
@@ -182,12 +195,27 @@ class TrainSession:
             return AsyncLoss(loss.detach().float().reshape(1), None)
         if self._loss_ring is None:
             self._loss_ring = [torch.empty(1, dtype=torch.float32).pin_memory() for _ in range(4)]
-        buf = self._loss_ring[self._loss_slot]
-        self._loss_slot = (self._loss_slot + 1) % len(self._loss_ring)
+            self._error_ring = [torch.zeros(4, dtype=torch.int32).pin_memory() for _ in range(4)]
+        slot = self._loss_slot
+        buf = self._loss_ring[slot]
+        self._loss_slot = (slot + 1) % len(self._loss_ring)
         buf.copy_(loss.detach().float().reshape(1), non_blocking=True)
+        errors = None
+        if self.backend == "b200":  # the kernels' error record rides along with the loss (16 bytes)
+            from .. import ops
+
+            errors = self._error_ring[slot]
+            ops.load_extension().device_errors_to_host(errors)
         ev = torch.cuda.Event()
         ev.record()
-        return AsyncLoss(buf, ev)
+        return AsyncLoss(buf, ev, errors)
+
+    def check_device_errors(self) -> None:
+        """Synchronously read the kernels' error record; raises ``DeviceWaitError`` if a wait expired."""
+        if self.device.type == "cuda" and self.backend == "b200":
+            from .. import ops
+
+            ops.check_device_errors()
 
     def close(self) -> None:
         if dist.is_available() and dist.is_initialized():

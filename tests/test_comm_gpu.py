@@ -173,3 +173,38 @@ def _timeout_worker(rank: int, world: int, port: int) -> None:
 def test_bounded_wait_expires_and_reports():
     _need(1)
     mp.spawn(_timeout_worker, args=(1, find_free_port()), nprocs=1, join=True)
+
+
+def _skip_signal_worker(rank: int, world: int, port: int) -> None:
+    os.environ["ZB_COMM_TIMEOUT_S"] = "1"  # read when the communicator is built: expiries end within a second
+    _init(rank, world, port)
+    try:
+        from cs244c_llama_zero_b200 import ops
+        from cs244c_llama_zero_b200.parallel.comm.nvlink import CommTimeoutError, NvlinkCollectives
+
+        C = ops.load_extension()
+        C.reset_device_errors()
+        coll = NvlinkCollectives(device=torch.device("cuda", rank), use_multicast=False)  # plain peer loads
+        buf = coll.alloc(4096, torch.float32)
+        buf.fill_(1.0)
+        coll.barrier()
+        torch.cuda.synchronize()
+        if rank == world - 1:
+            coll.skip_next_collective()  # ZB_FAULT=skip_signal: this rank launches nothing, posts no signal
+        coll.allreduce_scaled_(buf, 1.0)
+        torch.cuda.synchronize()
+        if rank == world - 1:
+            coll.check_errors()  # it waited on nothing
+        else:
+            with pytest.raises(CommTimeoutError):
+                coll.check_errors()
+        C.reset_device_errors()
+    finally:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def test_peer_that_skips_its_signal_is_detected():
+    """A rank leaves its collective kernel out; the others' bounded barrier waits expire and report."""
+    _need(2)
+    mp.spawn(_skip_signal_worker, args=(2, find_free_port()), nprocs=2, join=True)

@@ -132,3 +132,20 @@ def test_dry_run_writes_summary(tmp_path):
 def test_simulated_env_only_when_limited(tmp_path, bw, expect):
     case = harness._build_cases(_args(tmp_path, "--bandwidth-gbps", str(bw)))[0]
     assert harness._build_launch_env(case).get("ZERO_SIM_BW_GBPS") == expect
+
+
+def test_dtype_aware_theoretical_memory_sits_beside_the_fp32_one(tmp_path):
+    args = _args(tmp_path, "--stages", "0", "3", "--dtype", "bfloat16", "--nproc-per-node", "4")
+    s0, s3 = harness._build_cases(args)
+    n, fp32 = harness._theoretical_memory(s0)
+    bf = harness._theoretical_memory_dtype(s0, n)
+    mb = 1024.0 * 1024.0
+    assert bf["params_mb"] == 2 * n / mb and bf["grads_mb"] == 2 * n / mb and bf["optimizer_mb"] == 12 * n / mb
+    assert fp32["params_mb"] == 4 * n / mb  # the reference's fp32 definition is kept unchanged
+    bf3 = harness._theoretical_memory_dtype(s3, n)
+    assert bf3["total_mb"] == bf["total_mb"] / 4
+    res = harness._run_case(s0, tmp_path / "run", False, True, harness._launch_config_from_args(args), 0)
+    assert res.theoretical_memory_dtype_mb == bf
+    legacy = {k: v for k, v in json.loads((tmp_path / "run" / "cases" / f"{res.case_id}.json").read_text()).items()
+              if k != "theoretical_memory_dtype_mb"}
+    assert harness.CaseResult(**legacy).theoretical_memory_dtype_mb is None  # older records still load

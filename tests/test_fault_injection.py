@@ -69,3 +69,61 @@ def test_harness_records_failed_case(tmp_path, monkeypatch):
     launch = harness._launch_config_from_args(args)
     result = harness._run_case(case, tmp_path / "run", False, False, launch, 0)
     assert result.return_code != 0 and result.logged_steps >= 1
+
+
+def test_skip_signal_directive_arms_the_nvlink_collectives(monkeypatch):
+    import torch
+
+    from cs244c_llama_zero_b200.parallel.comm import nvlink
+
+    assert [(f.kind, f.rank, f.step) for f in parse_faults("skip_signal:1@4")] == [("skip_signal", 1, 4)]
+    monkeypatch.setattr(nvlink, "_world", lambda: 2)
+    coll = nvlink.NvlinkCollectives(device=torch.device("cpu"))
+    launched = []
+
+    class Ctx:
+        def __getattr__(self, name):
+            return lambda *a: launched.append(name)
+
+    class Buf:
+        ctx = Ctx()
+
+    monkeypatch.setattr(coll, "_locate", lambda t: (Buf(), 0))
+    inj = FaultInjector(rank=1, spec="skip_signal:1@4")
+    inj.at_step(3, coll)
+    assert coll._skip == 0
+    inj.at_step(4, coll)
+    flat = torch.ones(16)
+    assert coll.allreduce_scaled_(flat, 0.5) is flat and launched == []  # left out: no kernel, data untouched
+    assert torch.equal(flat, torch.ones(16))
+    coll.allreduce_scaled_(flat, 0.5)
+    assert launched == ["allreduce_f32"]
+    with pytest.raises(ValueError, match="nvls"):
+        FaultInjector(rank=0, spec="skip_signal:0@1").at_step(1, object())
+
+
+def test_device_error_record_maps_to_exceptions():
+    from cs244c_llama_zero_b200 import ops
+    from cs244c_llama_zero_b200.parallel.comm.nvlink import CommTimeoutError
+
+    ops.raise_for_device_errors([0, 0, 0, 0])
+    with pytest.raises(CommTimeoutError, match="collective barrier"):
+        ops.raise_for_device_errors([4, 1, 7, 48])
+    with pytest.raises(ops.DeviceWaitError, match="gemm pipeline wait") as info:
+        ops.raise_for_device_errors([1, 2, 3, 1])
+    assert not isinstance(info.value, CommTimeoutError)
+    with pytest.raises(ops.DeviceWaitError, match="paced link hold"):
+        ops.raise_for_device_errors([5, 0, 0, 1])
+
+
+def test_async_loss_raises_on_a_recorded_expiry():
+    import torch
+
+    from cs244c_llama_zero_b200.ops import DeviceWaitError
+    from cs244c_llama_zero_b200.train.session import AsyncLoss
+
+    ok = AsyncLoss(torch.tensor([1.5]), None, torch.zeros(4, dtype=torch.int32))
+    assert ok.item() == 1.5 and ok.nbytes == 20
+    bad = AsyncLoss(torch.tensor([1.5]), None, torch.tensor([3, 0, 0, 1], dtype=torch.int32))
+    with pytest.raises(DeviceWaitError):
+        bad.item()

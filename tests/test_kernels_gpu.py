@@ -163,6 +163,27 @@ def test_embedding(C):
     _close(dt, ref, 1e-5)
 
 
+def test_embedding_out_of_range_id_is_recorded_not_read(C):
+    from cs244c_llama_zero_b200 import ops
+
+    V, d, T = 64, 128, 16
+    table = _bf(V, d, seed=21)
+    ids = torch.randint(0, V, (T,), device="cuda")
+    ids[5] = V + 3  # a bad token id: the row is skipped (zeros) and the error record names it
+    out = torch.full((T, d), 7.0, device="cuda", dtype=torch.bfloat16)
+    C.reset_device_errors()
+    C.embedding_fwd(ids, table, out)
+    torch.cuda.synchronize()
+    code, where, _, _ = C.read_device_errors()
+    C.reset_device_errors()
+    assert (code, where) == (6, 5)
+    assert torch.equal(out[5], torch.zeros(d, device="cuda", dtype=torch.bfloat16))
+    keep = torch.arange(T, device="cuda") != 5
+    assert torch.equal(out[keep], table[ids[keep]])
+    with pytest.raises(ops.DeviceWaitError, match="index out of range"):
+        ops.raise_for_device_errors([code, where, 0, 1])
+
+
 def test_adamw_matches_reference_math(C):
     n = 10_003
     g = torch.Generator(device="cuda").manual_seed(20)

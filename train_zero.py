@@ -23,6 +23,7 @@ from typing import Dict, Iterator, List, Optional
 import torch
 import torch.distributed as dist
 
+from cs244c_llama_zero_b200 import ops
 from cs244c_llama_zero_b200.models import LlamaForCausalLM, estimate_num_parameters, human_readable_count
 from cs244c_llama_zero_b200.parallel.collectives import TracingCollectives, aggregate_collective_trace, pick_collectives
 from cs244c_llama_zero_b200.parallel.zero import (
@@ -247,6 +248,7 @@ def train(args: argparse.Namespace) -> None:
     model.set_activation_checkpointing(args.activation_checkpointing)
     backend = resolve_backend(args, device, dtype)
     model.set_backend(backend)
+    check_device_waits = device.type == "cuda" and (backend == "b200" or args.collective_impl in ("nvls", "p2p"))
     broadcast_model(model)
     collectives = pick_collectives(world_size, args.collective_impl, device)
     if args.profile_collectives:
@@ -292,7 +294,7 @@ def train(args: argparse.Namespace) -> None:
 
     for step in range(start_step, args.max_steps + 1):
         if faults:
-            faults.at_step(step)
+            faults.at_step(step, collectives)
         sample = args.profile_memory_interval > 0 and (step == 1 or step == args.max_steps
                                                        or step % args.profile_memory_interval == 0)
         is_measured = measured_step is not None and step == measured_step
@@ -355,6 +357,8 @@ def train(args: argparse.Namespace) -> None:
         comm_ms = float(stats["comm_ms"]) + prepare_comm_ms
         snap("post_optimizer")
         local_loss = float(torch.stack(micro_losses).mean())
+        if check_device_waits:  # a kernel whose bounded wait expired (e.g. a peer never signalled) ends the run
+            ops.check_device_errors()
         step_loss = global_mean_scalar(local_loss, device, world_size)
         recent = (recent + [step_loss])[-100:]
         iter_ms = iter_timer.stop()
