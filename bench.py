@@ -46,6 +46,8 @@ def parse_args(argv=None) -> argparse.Namespace:
     p.add_argument("--collective-impl", type=str, default="auto", help="auto | torch | nvls | p2p")
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--clocks-csv", type=str, default=None, help="keep the raw nvidia-smi clock samples here")
+    p.add_argument("--cuda-graph", action="store_true",
+                   help="run stages 0-2 as one captured CUDA graph per step (TrainSession cuda_graph mode)")
     p.add_argument("--model-size", type=str, default="baseline-small",
                    help="model preset: baseline-small (the headline config), baseline-1.3b, baseline-7b, ...")
     args = p.parse_args(argv)
@@ -237,7 +239,8 @@ def run_mine(args) -> None:
     for stage in args.stage_list:
         sess = TrainSession(SessionConfig(model_size=args.model_size, vocab_size=BASELINE_VOCAB_SIZE,
                                           seq_len=args.seq_len, batch_size=args.batch_size, zero_stage=stage,
-                                          collective_impl=impl, backend="b200"))
+                                          collective_impl=impl, backend="b200",
+                                          cuda_graph=args.cuda_graph and stage != 3))
         host = random_batches(4, args.batch_size, args.seq_len, BASELINE_VOCAB_SIZE, seed=1234 + rank * 100 + stage)
         dev = [h.to(sess.device) for h in host]
         it = {"i": 0}
@@ -265,6 +268,7 @@ def run_mine(args) -> None:
         # comm time of one extra instrumented step (device events around each collective); the
         # barrier keeps host-side skew between ranks out of the measured intervals
         barrier_sync()
+        sess.engine.clock.timing = True  # an eager instrumented step, also in graph mode
         sess.engine.zero_grad()
         sess.engine.prepare_forward()
         sess.forward_backward([dev[0]])
@@ -317,6 +321,7 @@ def run_mine(args) -> None:
         "config": {"model": model_desc(args.model_size), "global_batch": args.batch_size * world, "micro_batch_per_gpu": args.batch_size,
                    "seq_len": args.seq_len, "grad_accum": 1, "parallelism": f"dp{world}",
                    "zero_stage": args.headline_stage, "collective_impl": impl,
+                   "cuda_graph": bool(args.cuda_graph and args.headline_stage != 3),
                    "l2": "no flush: each step touches >2 GB (activations, 1.2 GB fp32 optimizer state) vs 126 MB L2"},
         "per_stage": per_stage,
         "e2e": e2e,

@@ -81,7 +81,9 @@ def _methodology(run_args: Dict[str, object], tuning: Optional[Dict[str, object]
     mode = str(run_args.get("bandwidth_mode", "unknown"))
     lines.append({"socket": "- communication is forced over NCCL NET/Socket and throttled at the socket layer",
                   "simulated": "- bandwidth is simulated inside the collective interface",
-                  "tc": "- bandwidth is throttled with Linux tc on the configured interface"}.get(
+                  "tc": "- bandwidth is throttled with Linux tc on the configured interface",
+                  "nvlink": "- every NVLink collective and ZeRO-3 gather is paced on the device to an emulated link "
+                            "of the case bandwidth (ring volumes per GPU, Gbit/s)"}.get(
         mode, "- no bandwidth throttling is applied when bandwidth is unlimited"))
     lines.append(f"- per-case metrics are averaged over logged steps after skipping "
                  f"{run_args.get('metrics_warmup_steps', 0)} warmup step(s); nominal step count is "

@@ -84,5 +84,11 @@ def check_device_errors(reset: bool = False) -> None:
 
 
 def launch_count() -> int:
-    """Number of kernels this process has launched through the extension."""
+    """Number of kernels this process has launched through the extension (graph replays included)."""
     return int(load_extension().launch_count())
+
+
+def count_graph_kernels(n: int) -> None:
+    """Count ``n`` kernel launches made by replaying a CUDA graph of this extension's kernels."""
+    if n > 0:
+        load_extension().add_launch_count(int(n))

@@ -300,9 +300,17 @@ void rope_bwd(Tensor g, int64_t rope_cols, int64_t head_dim, int64_t seq_len, Te
                  seq_len, cos.data_ptr<float>(), sin.data_ptr<float>(), cur_stream());
 }
 
+// Device scalars of adam_advance: float32 [2] on the device of the optimizer state.
+const float* dev_scalars_ptr(const std::optional<Tensor>& sc) {
+  if (!sc.has_value()) return nullptr;
+  check_f32(*sc, "dev_scalars");
+  TORCH_CHECK(sc->numel() >= 2, "dev_scalars: 2 elements required");
+  return sc->data_ptr<float>();
+}
+
 void adamw(Tensor master, Tensor m, Tensor v, Tensor grad, std::optional<Tensor> param_out,
            std::optional<Tensor> scale, double scale_const, double lr, double beta1, double beta2, double eps,
-           double wd, int64_t step) {
+           double wd, int64_t step, std::optional<Tensor> dev_scalars) {
   check_f32(master, "master");
   check_f32(m, "exp_avg");
   check_f32(v, "exp_avg_sq");
@@ -328,7 +336,18 @@ void adamw(Tensor master, Tensor m, Tensor v, Tensor grad, std::optional<Tensor>
   }
   b200::adamw_step(master.data_ptr<float>(), m.data_ptr<float>(), v.data_ptr<float>(), grad.data_ptr<float>(), out,
                    out_bf16, n, sp, (float)scale_const, (float)lr, (float)beta1, (float)beta2, (float)eps, (float)wd,
-                   (int)step, cur_stream());
+                   (int)step, cur_stream(), dev_scalars_ptr(dev_scalars));
+}
+
+// step_count (int32 [1]) += 1 and dev_scalars (float32 [2]) = the bias corrections of the new step, on
+// the current stream: the optimizer's step number lives on the device, so a captured step replays.
+void adam_advance(Tensor step_count, Tensor dev_scalars, double lr, double beta1, double beta2) {
+  check_cuda(step_count, "step_count");
+  TORCH_CHECK(step_count.scalar_type() == at::kInt && step_count.numel() >= 1, "adam_advance: int32 step counter");
+  const float* sc = dev_scalars_ptr(dev_scalars);
+  c10::cuda::CUDAGuard g(step_count.device());
+  b200::adam_advance(step_count.data_ptr<int32_t>(), const_cast<float*>(sc), (float)lr, (float)beta1, (float)beta2,
+                     cur_stream());
 }
 
 void sum_squares(Tensor x, Tensor out) {
@@ -493,7 +512,7 @@ class CommContext {
   }
   void adamw_allgather(int64_t param_off, int64_t chunk, Tensor master, Tensor m, Tensor v, Tensor grad,
                        std::optional<Tensor> scale, double scale_const, double lr, double beta1, double beta2,
-                       double eps, double wd, int64_t step) {
+                       double eps, double wd, int64_t step, std::optional<Tensor> dev_scalars) {
     for (auto* t : {&master, &m, &v, &grad}) {
       check_f32(*t, "adam state");
       TORCH_CHECK(t->is_contiguous() && t->numel() >= chunk, "adam state too small");
@@ -507,7 +526,8 @@ class CommContext {
     prepare();
     b200::comm_adamw_allgather(c_, param_off, chunk, master.data_ptr<float>(), m.data_ptr<float>(),
                                v.data_ptr<float>(), grad.data_ptr<float>(), sp, (float)scale_const, (float)lr,
-                               (float)beta1, (float)beta2, (float)eps, (float)wd, (int)step, cur_stream());
+                               (float)beta1, (float)beta2, (float)eps, (float)wd, (int)step, cur_stream(),
+                               dev_scalars_ptr(dev_scalars));
   }
   void barrier() {
     c10::cuda::CUDAGuard g(device_);
@@ -743,6 +763,8 @@ class PullGather {
 };
 
 int64_t launch_count() { return b200::launch_counter().load(); }
+// A CUDA-graph replay launches the kernels it captured as graph nodes: count them as launches.
+void add_launch_count(int64_t n) { b200::count_launch((int)n); }
 
 std::vector<int64_t> read_device_errors() {
   b200::DeviceErrors e{};
@@ -786,7 +808,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("embedding_fwd", &embedding_fwd);
   m.def("embedding_bwd", &embedding_bwd);
   m.def("rope_bwd", &rope_bwd);
-  m.def("adamw", &adamw);
+  m.def("adamw", &adamw, py::arg("master"), py::arg("m"), py::arg("v"), py::arg("grad"), py::arg("param_out"),
+        py::arg("scale"), py::arg("scale_const"), py::arg("lr"), py::arg("beta1"), py::arg("beta2"), py::arg("eps"),
+        py::arg("wd"), py::arg("step"), py::arg("dev_scalars") = py::none());
+  m.def("adam_advance", &adam_advance);
   m.def("sum_squares", &sum_squares);
   m.def("cross_entropy_fwd", &cross_entropy_fwd);
   m.def("cross_entropy_bwd", &cross_entropy_bwd);
@@ -796,6 +821,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("sin"), py::arg("batch"), py::arg("seq"), py::arg("heads"), py::arg("kv_heads"), py::arg("head_dim"),
         py::arg("scale"), py::arg("rezero_dq_acc") = false);
   m.def("launch_count", &launch_count);
+  m.def("add_launch_count", &add_launch_count);
   m.def("read_device_errors", &read_device_errors);
   m.def("reset_device_errors", &reset_device_errors);
   m.def("device_errors_to_host", &device_errors_to_host);
@@ -808,7 +834,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
       .def("reduce_scatter_range_acc_f32", &CommContext::reduce_scatter_range_acc_f32)
       .def("allgather", &CommContext::allgather)
       .def("gather_ce", &CommContext::gather_ce)
-      .def("adamw_allgather", &CommContext::adamw_allgather)
+      .def("adamw_allgather", &CommContext::adamw_allgather, py::arg("param_off"), py::arg("chunk"),
+           py::arg("master"), py::arg("m"), py::arg("v"), py::arg("grad"), py::arg("scale"), py::arg("scale_const"),
+           py::arg("lr"), py::arg("beta1"), py::arg("beta2"), py::arg("eps"), py::arg("wd"), py::arg("step"),
+           py::arg("dev_scalars") = py::none())
       .def("barrier", &CommContext::barrier)
       .def("wait_unsignalled", &CommContext::wait_unsignalled)
       .def_property_readonly("multicast", &CommContext::multicast)

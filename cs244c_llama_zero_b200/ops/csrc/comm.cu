@@ -340,10 +340,14 @@ template <bool MC>
 __global__ void __launch_bounds__(kThreads) adamw_allgather_kernel(CommCtx c, size_t param_off, size_t chunk8,
                                                                    float4* master, float4* m, float4* v,
                                                                    const float4* g, const float* scale_ptr,
-                                                                   AdamScalars a) {
+                                                                   AdamScalars a, const float* dev_sc) {
   const uint32_t e = next_epoch(c);
   if (!block_barrier(c, 2 * e)) return;
   const float scale = (scale_ptr != nullptr ? *scale_ptr : 1.0f) * a.scale_const;
+  if (dev_sc != nullptr) {  // bias corrections from the device step counter (replayable graphs)
+    a.step = dev_sc[0];
+    a.inv_sqrt_bc2 = dev_sc[1];
+  }
   const size_t base = param_off + (size_t)c.rank * chunk8 * 16;  // chunk8 groups of 8 bf16 = 16 bytes
   for (size_t i = gtid(); i < chunk8; i += gstride()) {
     float out[8];
@@ -527,7 +531,7 @@ void comm_gather_ce(const CommCtx& c, size_t off, size_t chunk_bytes, void* dst,
 
 void comm_adamw_allgather(const CommCtx& c, size_t param_off, size_t chunk, float* master, float* m, float* v,
                           const float* grad, const float* scale_ptr, float scale_const, float lr, float beta1,
-                          float beta2, float eps, float wd, int step, cudaStream_t s) {
+                          float beta2, float eps, float wd, int step, cudaStream_t s, const float* dev_sc) {
   check_ctx(c);
   B200_CHECK(chunk % 8 == 0 && param_off % 16 == 0, "comm_adamw_allgather: chunk must be a multiple of 8");
   AdamScalars a;
@@ -544,9 +548,11 @@ void comm_adamw_allgather(const CommCtx& c, size_t param_off, size_t chunk, floa
   auto* Vv = reinterpret_cast<float4*>(v);
   auto* G = reinterpret_cast<const float4*>(grad);
   if (c.mc)
-    adamw_allgather_kernel<true><<<c.blocks, kThreads, 0, s>>>(c, param_off, chunk / 8, M, Mm, Vv, G, scale_ptr, a);
+    adamw_allgather_kernel<true><<<c.blocks, kThreads, 0, s>>>(c, param_off, chunk / 8, M, Mm, Vv, G, scale_ptr, a,
+                                                                dev_sc);
   else
-    adamw_allgather_kernel<false><<<c.blocks, kThreads, 0, s>>>(c, param_off, chunk / 8, M, Mm, Vv, G, scale_ptr, a);
+    adamw_allgather_kernel<false><<<c.blocks, kThreads, 0, s>>>(c, param_off, chunk / 8, M, Mm, Vv, G, scale_ptr, a,
+                                                                 dev_sc);
   B200_CUDA_CHECK(cudaGetLastError());
   count_launch();
 }

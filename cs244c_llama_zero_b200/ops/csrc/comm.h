@@ -50,10 +50,10 @@ void comm_allgather(const CommCtx& c, size_t off_bytes, size_t chunk_bytes, cons
 // SMs, no barrier).  The caller guarantees every rank's source region is stable while it is read.
 void comm_gather_ce(const CommCtx& c, size_t off_bytes, size_t chunk_bytes, void* dst, cudaStream_t s);
 // AdamW on this rank's fp32 shard, then the bf16 result is written into every rank's parameter
-// region at [rank*chunk] (fused update + all-gather).
+// region at [rank*chunk] (fused update + all-gather).  `dev_sc` as in adamw_step (kernels.h).
 void comm_adamw_allgather(const CommCtx& c, size_t param_off_bytes, size_t chunk, float* master, float* m, float* v,
                           const float* grad, const float* scale_ptr, float scale_const, float lr, float beta1,
-                          float beta2, float eps, float wd, int step, cudaStream_t s);
+                          float beta2, float eps, float wd, int step, cudaStream_t s, const float* dev_sc = nullptr);
 // Standalone barrier among the ranks (every block of the communicator's grid).
 void comm_barrier(const CommCtx& c, cudaStream_t s);
 // A wait that nobody satisfies: used by tests to exercise the bounded-wait error path.

@@ -21,9 +21,13 @@ void embedding_bwd(const int64_t* ids, const __nv_bfloat16* dy, float* dtable, i
 void rope_bwd(__nv_bfloat16* g, int rows, int ld, int rope_cols, int head_dim, int seq_len, const float* cosv,
               const float* sinv, cudaStream_t s);
 
+// `dev_sc` (nullable): device scalars {lr / (1 - beta1^t), 1 / sqrt(1 - beta2^t)} written by adam_advance;
+// when given they replace the host-computed bias corrections of `step` (replayable CUDA graphs).
 void adamw_step(float* master, float* m, float* v, const float* g, void* param_out, bool param_bf16, size_t n,
                 const float* scale_ptr, float scale_const, float lr, float beta1, float beta2, float eps, float wd,
-                int step, cudaStream_t s);
+                int step, cudaStream_t s, const float* dev_sc = nullptr);
+// step_count[0] += 1 on the device, then dev_sc = {lr / (1 - beta1^t), 1 / sqrt(1 - beta2^t)} for the new t.
+void adam_advance(int* step_count, float* dev_sc, float lr, float beta1, float beta2, cudaStream_t s);
 void sum_squares(const void* x, bool is_bf16, size_t n, float* out, cudaStream_t s);
 void cross_entropy_fwd(const __nv_bfloat16* logits, int ld, const int64_t* targets, int rows, int vocab, float* lse,
                        float* loss_sum, float* count, float* loss, cudaStream_t s);

@@ -38,11 +38,13 @@ struct AdamArgs {
 template <bool BF16_OUT>
 __global__ void adamw_kernel(float* __restrict__ master, float* __restrict__ m, float* __restrict__ v,
                              const float* __restrict__ g, void* __restrict__ param_out, size_t n,
-                             const float* __restrict__ scale_ptr, float scale_const, AdamArgs a) {
+                             const float* __restrict__ scale_ptr, float scale_const, AdamArgs a,
+                             const float* __restrict__ dev_sc) {
   pdl_wait_and_release();
   const float scale = (scale_ptr != nullptr ? *scale_ptr : 1.0f) * scale_const;
   const float decay = 1.0f - a.lr * a.wd;
-  const float step = a.lr * a.inv_bc1;
+  const float step = dev_sc != nullptr ? dev_sc[0] : a.lr * a.inv_bc1;
+  if (dev_sc != nullptr) a.inv_sqrt_bc2 = dev_sc[1];
   const size_t n4 = n / 4;
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n4; i += (size_t)gridDim.x * blockDim.x) {
     float4 gp = reinterpret_cast<const float4*>(g)[i];
@@ -237,11 +239,26 @@ __global__ void finalize_loss_kernel(const float* loss_sum, const float* count, 
   *loss = *loss_sum / fmaxf(*count, 1.0f);
 }
 
+// Advances the device step counter and writes the bias-corrected scalars for it (one thread).
+__global__ void adam_advance_kernel(int* step_count, float* dev_sc, float lr, float beta1, float beta2) {
+  if (threadIdx.x != 0 || blockIdx.x != 0) return;
+  const int t = step_count[0] + 1;
+  step_count[0] = t;
+  dev_sc[0] = lr / (1.0f - powf(beta1, (float)t));
+  dev_sc[1] = 1.0f / sqrtf(1.0f - powf(beta2, (float)t));
+}
+
 }  // namespace
+
+void adam_advance(int* step_count, float* dev_sc, float lr, float beta1, float beta2, cudaStream_t s) {
+  adam_advance_kernel<<<1, 32, 0, s>>>(step_count, dev_sc, lr, beta1, beta2);
+  B200_CUDA_CHECK(cudaGetLastError());
+  count_launch();
+}
 
 void adamw_step(float* master, float* m, float* v, const float* g, void* param_out, bool param_bf16, size_t n,
                 const float* scale_ptr, float scale_const, float lr, float beta1, float beta2, float eps, float wd,
-                int step, cudaStream_t s) {
+                int step, cudaStream_t s, const float* dev_sc) {
   B200_CHECK((reinterpret_cast<uintptr_t>(master) & 15) == 0 && (reinterpret_cast<uintptr_t>(m) & 15) == 0 &&
                  (reinterpret_cast<uintptr_t>(v) & 15) == 0 && (reinterpret_cast<uintptr_t>(g) & 15) == 0,
              "adamw: fp32 buffers must be 16-byte aligned");
@@ -261,9 +278,11 @@ void adamw_step(float* master, float* m, float* v, const float* g, void* param_o
   const size_t work = std::max<size_t>(1, n / 4);
   const int blocks = (int)std::min<size_t>((work + threads - 1) / threads, (size_t)num_sms_cached() * 8);
   if (param_bf16)
-    launch_k(adamw_kernel<true>, dim3(blocks), dim3(threads), 0, s, 1, master, m, v, g, param_out, n, scale_ptr, scale_const, a);
+    launch_k(adamw_kernel<true>, dim3(blocks), dim3(threads), 0, s, 1, master, m, v, g, param_out, n, scale_ptr, scale_const, a,
+             dev_sc);
   else
-    launch_k(adamw_kernel<false>, dim3(blocks), dim3(threads), 0, s, 1, master, m, v, g, param_out, n, scale_ptr, scale_const, a);
+    launch_k(adamw_kernel<false>, dim3(blocks), dim3(threads), 0, s, 1, master, m, v, g, param_out, n, scale_ptr, scale_const, a,
+             dev_sc);
   B200_CUDA_CHECK(cudaGetLastError());
   count_launch();
 }

@@ -453,7 +453,8 @@ def lm_head_cross_entropy(x: torch.Tensor, weight: torch.nn.Parameter, labels: t
 
 # ------------------------------------------------------------------------------ optimizer
 def adamw_step(master, exp_avg, exp_avg_sq, grad, param_out, lr, beta1, beta2, eps, weight_decay, step,
-               grad_scale=None) -> None:
+               grad_scale=None, dev_scalars=None) -> None:
+    """Fused AdamW; ``dev_scalars`` (from :func:`adam_advance`) replaces the host step's bias corrections."""
     scale_t, scale_c = None, 1.0
     if isinstance(grad_scale, torch.Tensor):
         scale_t = grad_scale.reshape(1).to(torch.float32)
@@ -462,7 +463,12 @@ def adamw_step(master, exp_avg, exp_avg_sq, grad, param_out, lr, beta1, beta2, e
     out = param_out.reshape(-1) if param_out is not None else None
     _ext().adamw(master.reshape(-1), exp_avg.reshape(-1), exp_avg_sq.reshape(-1), grad.reshape(-1).float()
                  if grad.dtype != torch.float32 else grad.reshape(-1), out, scale_t, scale_c, lr, beta1, beta2,
-                 eps, weight_decay, step)
+                 eps, weight_decay, step, dev_scalars)
+
+
+def adam_advance(step_count: torch.Tensor, dev_scalars: torch.Tensor, lr: float, beta1: float, beta2: float) -> None:
+    """Device step counter += 1 and the bias-corrected scalars of the new step (one tiny kernel)."""
+    _ext().adam_advance(step_count, dev_scalars, lr, beta1, beta2)
 
 
 def sum_squares(t: torch.Tensor) -> torch.Tensor:

@@ -254,7 +254,8 @@ class NvlinkCollectives(TorchCollectives):
         return True
 
     def adamw_allgather(self, params_flat: torch.Tensor, master: torch.Tensor, exp_avg: torch.Tensor,
-                        exp_avg_sq: torch.Tensor, grad: torch.Tensor, scale, cfg, step: int) -> bool:
+                        exp_avg_sq: torch.Tensor, grad: torch.Tensor, scale, cfg, step: int,
+                        dev_scalars: Optional[torch.Tensor] = None) -> bool:
         """AdamW on the shard + multicast all-gather of the bf16 result; False if not applicable."""
         hit = self._locate(params_flat)
         world = self._w()
@@ -269,7 +270,7 @@ class NvlinkCollectives(TorchCollectives):
             return True
         slot = self._pace_begin()
         buf.ctx.adamw_allgather(off, chunk, master, exp_avg, exp_avg_sq, grad.contiguous(), scale_t, scale_c, cfg.lr,
-                                cfg.betas[0], cfg.betas[1], cfg.eps, cfg.weight_decay, step)
+                                cfg.betas[0], cfg.betas[1], cfg.eps, cfg.weight_decay, step, dev_scalars)
         self._pace_end(slot, "allgather", chunk * 2 * world)
         return True
 

@@ -32,6 +32,9 @@ class CommClock:
 
     def __init__(self, device: torch.device) -> None:
         self.cuda = device.type == "cuda" and torch.cuda.is_available()
+        # False while a step is captured into a CUDA graph: events recorded during capture are graph
+        # dependencies, not timestamps, so intervals are neither recorded nor read then.
+        self.timing = True
         self._pending: Dict[str, List[Tuple[object, object]]] = {}
         self._host_ms: Dict[str, float] = {}
         self.calls: Dict[str, int] = {}
@@ -63,7 +66,9 @@ class CommClock:
     def measure(self, category: str, num_bytes: int = 0) -> Iterator[None]:
         self.calls[category] = self.calls.get(category, 0) + 1
         self.bytes[category] = self.bytes.get(category, 0) + int(num_bytes)
-        if self.cuda:
+        if not self.timing:
+            yield
+        elif self.cuda:
             start = torch.cuda.Event(enable_timing=True)
             end = torch.cuda.Event(enable_timing=True)
             start.record()

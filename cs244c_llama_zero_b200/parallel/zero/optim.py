@@ -41,10 +41,12 @@ def adamw_update_(
     step: int,
     grad_scale: Optional[Scale] = None,
     param_out: Optional[torch.Tensor] = None,
+    dev_scalars: Optional[torch.Tensor] = None,
 ) -> None:
     """One AdamW step over flat fp32 state; ``grad`` is multiplied by ``grad_scale`` first.
 
     ``param_out`` (model dtype, same length) receives the updated master cast to its dtype.
+    ``dev_scalars`` (CUDA only): the step's bias corrections on the device, from ``adam_advance``.
     """
     if master.numel() == 0:
         return
@@ -52,7 +54,7 @@ def adamw_update_(
         from ...ops import functional as B
 
         B.adamw_step(master, exp_avg, exp_avg_sq, grad, param_out, cfg.lr, cfg.betas[0], cfg.betas[1], cfg.eps,
-                     cfg.weight_decay, step, grad_scale)
+                     cfg.weight_decay, step, grad_scale, dev_scalars)
         return
     beta1, beta2 = cfg.betas
     g = grad if grad.dtype == torch.float32 else grad.float()

@@ -81,21 +81,44 @@ class _FlatEngine(ZeROEngineBase):
         for p in self.meta.params:
             p.grad = None
 
-    def _adamw(self, grads: torch.Tensor, scale: torch.Tensor) -> None:
+    # -- device-side step counter (replayable CUDA graphs of the whole step) ----------------------
+    def use_device_step(self, on: bool = True) -> None:
+        """Keep the optimizer's step number on the device: each update first advances a device
+        counter (one tiny kernel) and the AdamW kernels take their bias corrections from it, so a
+        captured step replays correctly.  The host ``step_count`` is still kept by the caller."""
+        if not on or self.device.type != "cuda":
+            self._dev_step = None
+            return
+        self._dev_step = (torch.full((1,), int(self.step_count), dtype=torch.int32, device=self.device),
+                          torch.zeros(2, dtype=torch.float32, device=self.device))
+
+    def _device_scalars(self) -> Optional[torch.Tensor]:
+        dev = getattr(self, "_dev_step", None)
+        if dev is None:
+            return None
+        from ...ops import functional as B
+
+        B.adam_advance(dev[0], dev[1], self.adam.lr, self.adam.betas[0], self.adam.betas[1])
+        return dev[1]
+
+    def _adamw(self, grads: torch.Tensor, scale: torch.Tensor, dev_scalars: Optional[torch.Tensor] = None) -> None:
+        if dev_scalars is None:
+            dev_scalars = self._device_scalars()
         with self.clock.measure("optimizer"):
             adamw_update_(self._master, self._exp_avg, self._exp_avg_sq, grads, self.adam, self.step_count,
-                          grad_scale=scale, param_out=self._param_out())
+                          grad_scale=scale, param_out=self._param_out(), dev_scalars=dev_scalars)
 
     def _adamw_and_gather(self, grads: torch.Tensor, scale: torch.Tensor) -> None:
         """Sharded update followed by the parameter all-gather; one fused kernel when available."""
+        dev_scalars = self._device_scalars()
         fused = getattr(self.collectives, "adamw_allgather", None) if self.world_size > 1 else None
         if fused is not None and self.device.type == "cuda":
             with self.clock.measure("post_allgather", tensor_num_bytes(self.space.shard(self.space.params))):
                 done = fused(self.space.params, self._master, self._exp_avg, self._exp_avg_sq, grads, scale, self.adam,
-                             self.step_count)
+                             self.step_count, dev_scalars)
             if done:
                 return
-        self._adamw(grads, scale)
+        self._adamw(grads, scale, dev_scalars)
         self._allgather_params()
 
     def _param_out(self) -> torch.Tensor:

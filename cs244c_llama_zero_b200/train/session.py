@@ -12,6 +12,14 @@ Semantics follow the reference's ``train_zero.py`` step (``train_zero.py:416-589
 zero_grad -> prepare_forward -> for each micro-batch: forward under bf16 autocast with labels ==
 inputs (the model shifts them), backward(loss / grad_accum) -> optimizer step.  Inputs given on
 the host are copied with a non-blocking H2D transfer from pinned memory.
+
+``SessionConfig(cuda_graph=True)`` (ZeRO stages 0-2 on CUDA) runs the first ``graph_warmup_steps``
+steps eagerly on a side stream, then captures one whole step (H2D-staged input buffer -> zero_grad ->
+forward -> backward -> collectives -> optimizer) into a CUDA graph and replays it for every later
+step: the host issues one launch per step instead of several hundred.  The optimizer's step number
+lives on the device then (``use_device_step``), so the captured AdamW bias corrections advance on
+each replay.  Per-collective timing is off in graph mode.  Call ``reset_graph()`` after anything
+that replaces the engine's buffers (``load_state_dict``); the next step captures again.
 """
 
 from __future__ import annotations
@@ -52,12 +60,16 @@ class SessionConfig:
     profile_collectives: bool = False
     model_overrides: dict = field(default_factory=dict)
     pg_timeout_s: float = 600.0
+    cuda_graph: bool = False  # capture the whole step once and replay it (stages 0-2, CUDA)
+    graph_warmup_steps: int = 3
 
 
 def init_distributed(timeout_s: float = 600.0) -> Tuple[int, int, torch.device]:
     """torchrun environment -> (rank, world, device); NCCL on CUDA, Gloo on CPU."""
     if "RANK" not in os.environ or "WORLD_SIZE" not in os.environ:
-        return 0, 1, torch.device("cuda" if torch.cuda.is_available() else "cpu")
+        if torch.cuda.is_available():
+            return 0, 1, torch.device("cuda", torch.cuda.current_device())
+        return 0, 1, torch.device("cpu")
     rank = int(os.environ["RANK"])
     world = int(os.environ["WORLD_SIZE"])
     local_rank = int(os.environ.get("LOCAL_RANK", rank))
@@ -148,6 +160,18 @@ class TrainSession:
         self._loss_ring: Optional[List[torch.Tensor]] = None  # pinned host slots of train_step_async
         self._loss_slot = 0
         self.autocast = dtype == torch.bfloat16
+        self._autocast_cache = True
+        # CUDA-graph mode state
+        self._graph: Optional["torch.cuda.CUDAGraph"] = None
+        self._graph_ids: Optional[torch.Tensor] = None
+        self._graph_loss: Optional[torch.Tensor] = None
+        self._graph_warm = 0
+        self._warm_stream: Optional["torch.cuda.Stream"] = None
+        self.graph_kernels_per_step = 0
+        if cfg.cuda_graph:
+            reason = self.graph_unsupported_reason()
+            if reason:
+                raise ValueError(f"cuda_graph: {reason}")
 
     # ----------------------------------------------------------------------------- steps
     def _to_device(self, input_ids: torch.Tensor) -> torch.Tensor:
@@ -165,7 +189,7 @@ class TrainSession:
         for ids in micro_batches:
             ids = self._to_device(ids)
             with nvtx_range("forward"), torch.autocast(device_type=self.device.type, dtype=torch.bfloat16,
-                                                       enabled=self.autocast):
+                                                       enabled=self.autocast, cache_enabled=self._autocast_cache):
                 loss = self.model(input_ids=ids, labels=ids, return_logits=False).loss
             with nvtx_range("backward"):
                 self.engine.backward(loss / n)
@@ -173,7 +197,79 @@ class TrainSession:
         return total / n
 
     def train_step(self, input_ids: torch.Tensor) -> torch.Tensor:
-        """One optimizer step on ``input_ids`` ([grad_accum * B, S] or [B, S]); returns the loss (device)."""
+        """One optimizer step on ``input_ids`` ([grad_accum * B, S] or [B, S]); returns the loss (device).
+
+        In graph mode the returned tensor is the graph's static output: read (or copy) it before the
+        next step overwrites it.
+        """
+        if self.cfg.cuda_graph and self.device.type == "cuda":
+            return self._train_step_graphed(input_ids)
+        return self._train_step_eager(input_ids)
+
+    # ----------------------------------------------------------------------------- CUDA graph
+    def graph_unsupported_reason(self) -> Optional[str]:
+        """Why this session cannot run its step as a CUDA graph (None when it can)."""
+        if self.device.type != "cuda":
+            return None  # graph mode is a no-op on CPU
+        if self.cfg.zero_stage == 3:
+            return "ZeRO-3 gathers parameters on a side stream with host-managed events; use stages 0-2"
+        if self.cfg.activation_checkpointing:
+            return "activation checkpointing replays the forward with host RNG bookkeeping"
+        if self.cfg.profile_collectives:
+            return "the collective trace times calls on the host"
+        if os.environ.get("ZERO_SIM_BW_GBPS") or os.environ.get("ZERO_SIM_LATENCY_MS"):
+            return "the simulated bandwidth mode sleeps on the host (use the nvlink mode, which paces on the device)"
+        return None
+
+    def reset_graph(self) -> None:
+        """Drop the captured step (the next step captures again, after no further warm-up)."""
+        self._graph = None
+        self._graph_loss = None
+        self.engine.use_device_step(False)
+        self.engine.clock.timing = True
+
+    def _train_step_graphed(self, input_ids: torch.Tensor) -> torch.Tensor:
+        if self._graph is None:
+            if self._graph_warm < self.cfg.graph_warmup_steps:
+                # Eager warm-up on a side stream: lazy initialisation (extension buffers, tensor maps,
+                # NCCL communicators, allocator pools) happens before capture, off the capture stream.
+                self._graph_warm += 1
+                if self._warm_stream is None:
+                    self._warm_stream = torch.cuda.Stream(device=self.device)
+                cur = torch.cuda.current_stream(self.device)
+                self._warm_stream.wait_stream(cur)
+                with torch.cuda.stream(self._warm_stream):
+                    loss = self._train_step_eager(input_ids)
+                cur.wait_stream(self._warm_stream)
+                return loss
+            return self._capture(input_ids)
+        self._graph_ids.copy_(input_ids, non_blocking=True)
+        self._graph.replay()
+        self.engine.step_count += 1
+        from .. import ops
+
+        ops.count_graph_kernels(self.graph_kernels_per_step)
+        return self._graph_loss
+
+    def _capture(self, input_ids: torch.Tensor) -> torch.Tensor:
+        from .. import ops
+
+        self._graph_ids = torch.empty(input_ids.shape, dtype=torch.long, device=self.device)
+        self._graph_ids.copy_(input_ids, non_blocking=True)
+        self.engine.use_device_step(True)  # device counter = host step_count; the replay advances it
+        self.engine.clock.timing = False
+        self._autocast_cache = False
+        torch.cuda.synchronize(self.device)
+        before = ops.launch_count()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            loss = self._train_step_eager(self._graph_ids)  # host step_count advances once, for this call
+        self.graph_kernels_per_step = ops.launch_count() - before
+        self._graph, self._graph_loss = graph, loss
+        graph.replay()  # capture only records: this runs the call's step
+        return loss
+
+    def _train_step_eager(self, input_ids: torch.Tensor) -> torch.Tensor:
         micro = list(input_ids.chunk(self.cfg.grad_accum_steps, dim=0)) if self.cfg.grad_accum_steps > 1 else [input_ids]
         self.model.train()
         self.engine.zero_grad()
@@ -218,6 +314,7 @@ class TrainSession:
             ops.check_device_errors()
 
     def close(self) -> None:
+        self._graph = None  # a graph holding NCCL calls must go before the process group does
         if dist.is_available() and dist.is_initialized():
             dist.barrier()
             dist.destroy_process_group()

@@ -208,6 +208,26 @@ def test_adamw_matches_reference_math(C):
     torch.testing.assert_close(out.float(), pm, atol=1e-2, rtol=1e-2)
 
 
+def test_adamw_device_step_matches_host_step(C):
+    """The device step counter (CUDA-graph mode) gives the host step's bias corrections."""
+    n = 4096
+    g = torch.Generator(device="cuda").manual_seed(24)
+    state = [torch.randn(n, device="cuda", generator=g) for _ in range(2)] + [torch.rand(n, device="cuda", generator=g)]
+    grad = torch.randn(n, device="cuda", generator=g)
+    a, b = [t.clone() for t in state], [t.clone() for t in state]
+    lr, b1, b2, eps, wd = 1e-3, 0.9, 0.95, 1e-8, 0.1
+    step_t = torch.tensor([4], dtype=torch.int32, device="cuda")
+    sc = torch.zeros(2, device="cuda")
+    C.adam_advance(step_t, sc, lr, b1, b2)
+    assert int(step_t.item()) == 5
+    torch.testing.assert_close(sc.cpu(), torch.tensor([lr / (1 - b1 ** 5), 1 / math.sqrt(1 - b2 ** 5)]), rtol=1e-5,
+                               atol=0.0)
+    C.adamw(*a, grad, None, None, 1.0, lr, b1, b2, eps, wd, 5)
+    C.adamw(*b, grad, None, None, 1.0, lr, b1, b2, eps, wd, 999, sc)  # the host step is ignored
+    for x, y in zip(a, b):
+        torch.testing.assert_close(x, y, rtol=1e-5, atol=1e-7)
+
+
 def test_sum_squares(C):
     x = torch.randn(1_000_001, device="cuda")
     out = torch.empty(1, device="cuda")

@@ -1,0 +1,43 @@
+"""TrainSession CUDA-graph mode: after its eager warm-up steps, one captured step replayed per call
+must train exactly like the eager session (same weights, same batches)."""
+
+from __future__ import annotations
+
+import pytest
+import torch
+
+from cs244c_llama_zero_b200.train import SessionConfig, TrainSession
+
+pytestmark = pytest.mark.gpu
+
+
+def _session(stage: int, graph: bool) -> TrainSession:
+    cfg = SessionConfig(model_size="baseline-small", vocab_size=1024, seq_len=256, batch_size=2, zero_stage=stage,
+                        backend="b200", cuda_graph=graph, graph_warmup_steps=2, model_overrides={"n_layers": 2})
+    return TrainSession(cfg)
+
+
+@pytest.mark.parametrize("stage", [0, 2])
+def test_graph_replay_trains_like_eager(stage):
+    from cs244c_llama_zero_b200 import ops
+
+    g = torch.Generator().manual_seed(5)
+    batches = [torch.randint(0, 1024, (2, 256), generator=g) for _ in range(7)]
+    eager = _session(stage, False)
+    want = [float(eager.train_step(b)) for b in batches]
+    graphed = _session(stage, True)
+    got = []
+    for i, b in enumerate(batches):
+        before = ops.launch_count()
+        got.append(float(graphed.train_step(b)))
+        if i >= 3:  # steps 0-1 warm up, step 2 captures, later steps replay
+            assert ops.launch_count() - before == graphed.graph_kernels_per_step > 0
+    assert graphed._graph is not None
+    assert graphed.engine.step_count == eager.engine.step_count == len(batches)
+    torch.testing.assert_close(torch.tensor(got), torch.tensor(want), rtol=2e-3, atol=2e-3)
+    torch.testing.assert_close(graphed.engine.master_params, eager.engine.master_params, rtol=1e-3, atol=1e-5)
+    assert got[-1] < got[0]
+    ops.check_device_errors()
+    graphed.reset_graph()  # the next step captures again
+    float(graphed.train_step(batches[0]))
+    assert graphed._graph is not None and graphed.engine.step_count == len(batches) + 1
