@@ -44,3 +44,29 @@ def test_repo_bundle_roundtrip(tmp_path):
     subprocess.run(["bash", str(ROOT / "scripts" / "repo_bundle.sh"), "unpack", str(archive), str(dest)], check=True,
                    capture_output=True)
     assert (dest / "bench.py").exists() and not (dest / ".git").exists()
+
+
+def test_reference_suite_runner_maps_imports_and_stages(tmp_path):
+    sys.path.insert(0, str(ROOT / "scripts"))
+    try:
+        import run_reference_tests as rrt
+    finally:
+        sys.path.pop(0)
+    src = ("from model.config import ModelConfig\nfrom zero import ZeROStage2Optimizer\nimport analysis.visualize\n"
+           "from data.fineweb import PackedFineWebDataset\nfrom experiments import harness\nimport torch\n"
+           "cmd = [sys.executable, \"experiments/merge_run_summaries.py\"]\n")
+    out = rrt.rewrite(src)
+    assert "from cs244c_llama_zero_b200.models.config import ModelConfig" in out
+    assert "from cs244c_llama_zero_b200.parallel.zero import ZeROStage2Optimizer" in out
+    assert "import cs244c_llama_zero_b200.analysis.visualize" in out
+    assert "from cs244c_llama_zero_b200.data.datasets import PackedFineWebDataset" in out
+    assert "from cs244c_llama_zero_b200.experiments import harness" in out and "import torch\n" in out
+    assert '"-m", "cs244c_llama_zero_b200.experiments.merge_run_summaries"' in out
+    fake = tmp_path / "ref"
+    (fake / "tests").mkdir(parents=True)
+    (fake / "tests" / "test_x.py").write_text("from model import build_tiny_config\n\ndef test_ok():\n    assert build_tiny_config()\n")
+    (fake / "tests" / "conftest.py").write_text("")
+    staged = rrt.stage(fake, tmp_path / "staged")
+    assert [p.name for p in staged] == ["test_x.py"]
+    assert "cs244c_llama_zero_b200.models" in staged[0].read_text()
+    assert (tmp_path / "staged" / "train_zero.py").exists()
