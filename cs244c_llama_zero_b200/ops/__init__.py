@@ -8,10 +8,17 @@ it: there is no silent eager fallback for CUDA tensors.
 from __future__ import annotations
 
 import importlib
+import os
 from typing import Optional
 
 _EXT = None
 _EXT_ERROR: Optional[BaseException] = None
+
+
+def extension_module_name() -> str:
+    """``_C``, or the debug-bounds build ``_C_debug`` when ``ZB_DEBUG_BOUNDS=1`` (range-checked
+    hand-indexed accesses; see ``setup.py``)."""
+    return "_C_debug" if os.environ.get("ZB_DEBUG_BOUNDS", "0") not in ("", "0") else "_C"
 
 
 def load_extension():
@@ -21,13 +28,15 @@ def load_extension():
         return _EXT
     import torch  # noqa: F401  (loads libc10 / libtorch that the extension links against)
 
+    name = extension_module_name()
     try:
-        _EXT = importlib.import_module(f"{__name__}._C")
+        _EXT = importlib.import_module(f"{__name__}.{name}")
     except ImportError as exc:  # pragma: no cover - depends on the build
         _EXT_ERROR = exc
+        hint = ("ZB_DEBUG_BOUNDS=1 python setup.py build_ext --inplace --build-temp build/debug_bounds"
+                if name == "_C_debug" else "python setup.py build_ext --inplace")
         raise ImportError(
-            "cs244c_llama_zero_b200.ops._C is not built; run `python setup.py build_ext --inplace` "
-            f"in the repository root ({exc})"
+            f"cs244c_llama_zero_b200.ops.{name} is not built; run `{hint}` in the repository root ({exc})"
         ) from exc
     return _EXT
 
@@ -60,7 +69,8 @@ class CommTimeoutError(DeviceWaitError):
 
 
 ERROR_NAMES = {1: "gemm pipeline wait", 2: "attention pipeline wait", 3: "collective wait",
-               4: "collective barrier", 5: "paced link hold", 6: "index out of range (access skipped)"}
+               4: "collective barrier", 5: "paced link hold", 6: "index out of range (access skipped)",
+               7: "out-of-bounds access caught by the debug-bounds build (skipped)"}
 COMM_CODES = (3, 4)
 
 

@@ -198,8 +198,13 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
             tma_load_2d(qs + kb * 16384, &tm_qkv, &q_full[st], h * HD + 64 * kb, row0 + i * 128);
             tma_load_2d(ds + kb * 16384, &tm_do, &q_full[st], h * HD + 64 * kb, row0 + i * 128);
           }
-          bulk_load(ls, p.lse + vec, 512, &q_full[st]);
-          bulk_load(ls + 512, p.delta + vec, 512, &q_full[st]);
+          if (B200_IN_BOUNDS(errs, vec, 128, (long long)p.batch * p.heads * p.seq, 110)) {
+            bulk_load(ls, p.lse + vec, 512, &q_full[st]);
+            bulk_load(ls + 512, p.delta + vec, 512, &q_full[st]);
+          } else {  // the 1024 skipped bytes were announced above: mark them complete without an arrival
+            asm volatile("mbarrier.complete_tx.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(&q_full[st])), "r"(1024)
+                         : "memory");
+          }
         }
       }
     }
@@ -380,7 +385,9 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
             bulk_commit_group();
           }
         } else {
-          float* dq_row = p.dq_acc + (size_t)(row0 + i * 128 + r) * (p.heads * HD) + h * HD + wg * C::HALF;
+          const size_t dq_idx = (size_t)(row0 + i * 128 + r) * (p.heads * HD) + h * HD + wg * C::HALF;
+          float* dq_row = p.dq_acc + dq_idx;
+          const bool dq_in = B200_IN_BOUNDS(errs, dq_idx, C::HALF, (long long)p.batch * p.seq * p.heads * HD, 111);
 #pragma unroll
           for (int c = 0; c < C::HALF; c += 32) {
             uint32_t qv[32];
@@ -388,7 +395,8 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
             tc_wait_ld();
 #pragma unroll
             for (int e = 0; e < 32; e += 4) {
-              atomicAdd(reinterpret_cast<float4*>(dq_row + c + e),
+              if (dq_in)
+                atomicAdd(reinterpret_cast<float4*>(dq_row + c + e),
                         make_float4(__uint_as_float(qv[e]) * p.scale, __uint_as_float(qv[e + 1]) * p.scale,
                                     __uint_as_float(qv[e + 2]) * p.scale, __uint_as_float(qv[e + 3]) * p.scale));
             }

@@ -355,7 +355,10 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
       tc_fence_after();
       const uint32_t obase = lane_base + C::O_TMEM + (gl & 1) * HD + ocol0;
       const float inv_l = 1.0f / l_total;
-      __nv_bfloat16* dst = p.out + (size_t)(row0 + it.qb * 128 + r) * p.ld_out + it.h * HD + ocol0;
+      const size_t out_idx = (size_t)(row0 + it.qb * 128 + r) * p.ld_out + it.h * HD + ocol0;
+      __nv_bfloat16* dst = p.out + out_idx;
+      const bool out_in =
+          B200_IN_BOUNDS(errs, out_idx, C::HALF_O, (long long)p.batch * p.seq * p.ld_out, 120);
 #pragma unroll
       for (int cc = 0; cc < C::HALF_O; cc += 32) {
         uint32_t ov[32];
@@ -368,14 +371,16 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
           w.y = pack_bf16((o[cc + e + 2] + __uint_as_float(ov[e + 2])) * inv_l, (o[cc + e + 3] + __uint_as_float(ov[e + 3])) * inv_l);
           w.z = pack_bf16((o[cc + e + 4] + __uint_as_float(ov[e + 4])) * inv_l, (o[cc + e + 5] + __uint_as_float(ov[e + 5])) * inv_l);
           w.w = pack_bf16((o[cc + e + 6] + __uint_as_float(ov[e + 6])) * inv_l, (o[cc + e + 7] + __uint_as_float(ov[e + 7])) * inv_l);
-          *reinterpret_cast<uint4*>(dst + cc + e) = w;
+          if (out_in) *reinterpret_cast<uint4*>(dst + cc + e) = w;
         }
       }
       // The last O buffer of the item is free for the PV two blocks later.
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&o_free[gl & 1]);
-      if (wg == 0) p.lse[((size_t)it.b * p.heads + it.h) * p.seq + it.qb * 128 + r] = m + log2f(l_total);
+      const size_t lse_idx = ((size_t)it.b * p.heads + it.h) * p.seq + it.qb * 128 + r;
+      if (wg == 0 && B200_IN_BOUNDS(errs, lse_idx, 1, (long long)p.batch * p.heads * p.seq, 121))
+        p.lse[lse_idx] = m + log2f(l_total);
     }
   }
 

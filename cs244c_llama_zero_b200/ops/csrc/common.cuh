@@ -90,6 +90,7 @@ enum : int {
   kErrCommBarrier = 4,
   kErrPaceWait = 5,
   kErrBadIndex = 6,  // an index input out of range (e.g. a token id >= vocab); the access was skipped
+  kErrBounds = 7,    // debug bounds build: a hand-indexed global access fell outside its buffer (skipped)
 };
 
 // ---------------------------------------------------------------------------------------
@@ -124,6 +125,24 @@ __device__ __forceinline__ void report_error(DeviceErrors* errs, int code, int w
   }
   atomicAdd(&errs->count, 1);
 }
+
+// Debug bounds build (the `_C_debug` extension, built with -DB200_DEBUG_BOUNDS): the hand-indexed
+// global accesses of the kernels (the ones TMA tensor maps do not clip) check that elements
+// [idx, idx + len) lie inside [0, extent); an access that does not is recorded (kErrBounds, where =
+// the site number) and skipped instead of reading or writing outside its buffer.  In the release
+// build the check is the constant `true` and compiles away.
+__device__ __forceinline__ bool bounds_ok(DeviceErrors* errs, long long idx, long long len, long long extent,
+                                          int site) {
+  if (idx >= 0 && idx + len <= extent) return true;
+  report_error(errs, kErrBounds, site);
+  return false;
+}
+#ifdef B200_DEBUG_BOUNDS
+#define B200_IN_BOUNDS(errs, idx, len, extent, site) \
+  (::b200::bounds_ok((errs), (long long)(idx), (long long)(len), (long long)(extent), (site)))
+#else
+#define B200_IN_BOUNDS(errs, idx, len, extent, site) (true)
+#endif
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));

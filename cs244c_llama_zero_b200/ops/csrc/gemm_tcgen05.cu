@@ -371,12 +371,16 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       uint4 gq[4], uq[4];
       auto load_gu = [&](int i) {
         const int n0 = tn * BN + wg * (BN / 2);
-        const __nv_bfloat16* gsrc = p.aux_in + (size_t)(row_ok ? m : 0) * p.ld_aux_in + n0 + 32 * i;
+        const size_t gidx = (size_t)(row_ok ? m : 0) * p.ld_aux_in + n0 + 32 * i;
+        const __nv_bfloat16* gsrc = p.aux_in + gidx;
+        const long long aux_extent = (long long)p.M * p.ld_aux_in;
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
           const bool in = n0 + 32 * i + 8 * j < p.N;
-          gq[j] = in ? *reinterpret_cast<const uint4*>(gsrc + 8 * j) : make_uint4(0u, 0u, 0u, 0u);
-          uq[j] = in ? *reinterpret_cast<const uint4*>(gsrc + p.ffn + 8 * j) : make_uint4(0u, 0u, 0u, 0u);
+          const bool gin = in && B200_IN_BOUNDS(p.errs, gidx + 8 * j, 8, aux_extent, 100);
+          const bool uin = in && B200_IN_BOUNDS(p.errs, gidx + p.ffn + 8 * j, 8, aux_extent, 101);
+          gq[j] = gin ? *reinterpret_cast<const uint4*>(gsrc + 8 * j) : make_uint4(0u, 0u, 0u, 0u);
+          uq[j] = uin ? *reinterpret_cast<const uint4*>(gsrc + p.ffn + 8 * j) : make_uint4(0u, 0u, 0u, 0u);
         }
       };
       if constexpr (EPI == EPI_SWIGLU_BWD) {
@@ -487,7 +491,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             tmem_ld_32x32b_x32(tbase + h0 + j0, lo);
             tmem_ld_32x32b_x32(tbase + h0 + half + j0, hi);
             tc_wait_ld();
-            if (rotate) {
+            if (rotate && B200_IN_BOUNDS(p.errs, (long long)pos * half + j0, 32, (long long)p.seq_len * half, 102)) {
               const float4* c4 = reinterpret_cast<const float4*>(p.rope_cos + (size_t)pos * half + j0);
               const float4* s4 = reinterpret_cast<const float4*>(p.rope_sin + (size_t)pos * half + j0);
 #pragma unroll
