@@ -529,6 +529,29 @@ class CommContext {
                                (float)beta1, (float)beta2, (float)eps, (float)wd, (int)step, cur_stream(),
                                dev_scalars_ptr(dev_scalars));
   }
+  // The ZeRO-2 step without clipping in one kernel (see comm.h): `grads` is the context of the flat
+  // fp32 gradient buffer, this context the bf16 parameter buffer.
+  void rs_adamw_allgather(CommContext& grads, int64_t g_off, int64_t param_off, int64_t chunk, Tensor master,
+                          Tensor m, Tensor v, double grad_scale, double lr, double beta1, double beta2, double eps,
+                          double wd, int64_t step, std::optional<Tensor> dev_scalars, std::optional<Tensor> sq_out) {
+    for (auto* t : {&master, &m, &v}) {
+      check_f32(*t, "adam state");
+      TORCH_CHECK(t->is_contiguous() && t->numel() >= chunk, "adam state too small");
+    }
+    TORCH_CHECK(grads.device() == device_, "rs_adamw_allgather: buffers on different devices");
+    float* sq = nullptr;
+    if (sq_out.has_value()) {
+      check_f32(*sq_out, "sq_out");
+      sq = sq_out->data_ptr<float>();
+    }
+    c10::cuda::CUDAGuard g(device_);
+    prepare();
+    grads.prepare();
+    b200::comm_rs_adamw_allgather(c_, grads.c_, g_off, param_off, chunk, master.data_ptr<float>(),
+                                  m.data_ptr<float>(), v.data_ptr<float>(), (float)grad_scale, (float)lr, (float)beta1,
+                                  (float)beta2, (float)eps, (float)wd, (int)step, dev_scalars_ptr(dev_scalars), sq,
+                                  cur_stream());
+  }
   void barrier() {
     c10::cuda::CUDAGuard g(device_);
     prepare();
@@ -838,6 +861,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
            py::arg("master"), py::arg("m"), py::arg("v"), py::arg("grad"), py::arg("scale"), py::arg("scale_const"),
            py::arg("lr"), py::arg("beta1"), py::arg("beta2"), py::arg("eps"), py::arg("wd"), py::arg("step"),
            py::arg("dev_scalars") = py::none())
+      .def("rs_adamw_allgather", &CommContext::rs_adamw_allgather, py::arg("grads"), py::arg("g_off"),
+           py::arg("param_off"), py::arg("chunk"), py::arg("master"), py::arg("m"), py::arg("v"),
+           py::arg("grad_scale"), py::arg("lr"), py::arg("beta1"), py::arg("beta2"), py::arg("eps"), py::arg("wd"),
+           py::arg("step"), py::arg("dev_scalars") = py::none(), py::arg("sq_out") = py::none())
       .def("barrier", &CommContext::barrier)
       .def("wait_unsignalled", &CommContext::wait_unsignalled)
       .def_property_readonly("multicast", &CommContext::multicast)

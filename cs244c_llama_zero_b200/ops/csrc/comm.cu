@@ -13,6 +13,9 @@
 //   allgather            each rank multicasts its shard into every rank's buffer
 //   adamw_allgather      AdamW on the local fp32 shard; the bf16 result is multicast straight into
 //                        every rank's parameter buffer (ZeRO-1/2 update + parameter all-gather)
+//   rs_adamw_allgather   the whole ZeRO-2 step without clipping in one kernel: each rank ld_reduces
+//                        its chunk of the flat fp32 gradients, averages it, adds its squares to the
+//                        norm, runs AdamW and multicasts the bf16 result (no gradient shard in HBM)
 //
 // Ordering: every block of every rank runs the same grid, and block b synchronises with block b of
 // every peer at kernel start (all inputs written) and at kernel end (all outputs delivered).  The
@@ -379,6 +382,78 @@ __global__ void __launch_bounds__(kThreads) adamw_allgather_kernel(CommCtx c, si
   block_barrier(c, 2 * e + 1);
 }
 
+// Reduce-scatter of the gradients (context g) + sum of squares + AdamW + parameter all-gather
+// (context c, whose barriers order the whole step).  Element k of this rank's chunk: gradient at
+// g region [rank*chunk + k], optimizer state at master/m/v[k], parameter at c region [rank*chunk + k].
+template <bool MC>
+__global__ void __launch_bounds__(kThreads) rs_adamw_allgather_kernel(CommCtx c, CommCtx g, size_t g_off,
+                                                                      size_t param_off, size_t chunk8,
+                                                                      float4* master, float4* m, float4* v,
+                                                                      float grad_scale, AdamScalars a,
+                                                                      const float* dev_sc, float* sq_out) {
+  const uint32_t e = next_epoch(c);
+  if (!block_barrier(c, 2 * e)) return;
+  if (dev_sc != nullptr) {
+    a.step = dev_sc[0];
+    a.inv_sqrt_bc2 = dev_sc[1];
+  }
+  const size_t gbase = g_off + (size_t)c.rank * chunk8 * 32;  // chunk8 groups of 8 fp32 = 32 bytes
+  const size_t pbase = param_off + (size_t)c.rank * chunk8 * 16;
+  float sq = 0.f;
+  for (size_t i = gtid(); i < chunk8; i += gstride()) {
+    float out[8];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const size_t gb = gbase + i * 32 + h * 16;
+      float4 gp;
+      if constexpr (MC) {
+        gp = mc_ld_reduce_f32x4(g.mc + gb);
+      } else {
+        gp = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int w = 0; w < g.world; ++w) {
+          const float4 x = __ldcg(reinterpret_cast<const float4*>(g.peers[w] + gb));
+          gp.x += x.x; gp.y += x.y; gp.z += x.z; gp.w += x.w;
+        }
+      }
+      const size_t k = 2 * i + h;
+      float4 mp = m[k], vp = v[k], pp = master[k];
+      float gg[4] = {gp.x * grad_scale, gp.y * grad_scale, gp.z * grad_scale, gp.w * grad_scale};
+      float mm[4] = {mp.x, mp.y, mp.z, mp.w}, vv[4] = {vp.x, vp.y, vp.z, vp.w}, pw[4] = {pp.x, pp.y, pp.z, pp.w};
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        sq += gg[t] * gg[t];
+        mm[t] = a.beta1 * mm[t] + (1.0f - a.beta1) * gg[t];
+        vv[t] = a.beta2 * vv[t] + (1.0f - a.beta2) * gg[t] * gg[t];
+        pw[t] = pw[t] * a.decay - a.step * mm[t] / (sqrtf(vv[t]) * a.inv_sqrt_bc2 + a.eps);
+        out[4 * h + t] = pw[t];
+      }
+      m[k] = make_float4(mm[0], mm[1], mm[2], mm[3]);
+      v[k] = make_float4(vv[0], vv[1], vv[2], vv[3]);
+      master[k] = make_float4(pw[0], pw[1], pw[2], pw[3]);
+    }
+    const uint4 o = f32_to_bf16x8(out);
+    const size_t b = pbase + i * 16;
+    if constexpr (MC) {
+      mc_st_b128(c.mc + b, o);
+    } else {
+      for (int w = 0; w < c.world; ++w) __stcg(reinterpret_cast<uint4*>(c.peers[w] + b), o);
+    }
+  }
+  // this rank's share of the squared norm of the averaged gradient
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
+  __shared__ float part[kThreads / 32];
+  if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = sq;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float t = threadIdx.x < kThreads / 32 ? part[threadIdx.x] : 0.f;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+    if (threadIdx.x == 0 && sq_out != nullptr) atomicAdd(sq_out, t);
+  }
+  block_barrier(c, 2 * e + 1);
+}
+
 __global__ void barrier_kernel(CommCtx c) {
   const uint32_t e = next_epoch(c);
   block_barrier(c, 2 * e);
@@ -553,6 +628,41 @@ void comm_adamw_allgather(const CommCtx& c, size_t param_off, size_t chunk, floa
   else
     adamw_allgather_kernel<false><<<c.blocks, kThreads, 0, s>>>(c, param_off, chunk / 8, M, Mm, Vv, G, scale_ptr, a,
                                                                  dev_sc);
+  B200_CUDA_CHECK(cudaGetLastError());
+  count_launch();
+}
+
+void comm_rs_adamw_allgather(const CommCtx& c, const CommCtx& g, size_t g_off, size_t param_off, size_t chunk,
+                             float* master, float* m, float* v, float grad_scale, float lr, float beta1, float beta2,
+                             float eps, float wd, int step, const float* dev_sc, float* sq_out, cudaStream_t s) {
+  check_ctx(c);
+  check_ctx(g);
+  B200_CHECK(c.world == g.world && c.rank == g.rank, "comm_rs_adamw_allgather: contexts of different groups");
+  B200_CHECK((c.mc != 0) == (g.mc != 0), "comm_rs_adamw_allgather: both buffers multicast or neither");
+  B200_CHECK(chunk % 8 == 0 && param_off % 16 == 0 && g_off % 16 == 0,
+             "comm_rs_adamw_allgather: chunk must be a multiple of 8, offsets 16-aligned");
+  B200_CHECK(((reinterpret_cast<uintptr_t>(master) | reinterpret_cast<uintptr_t>(m) | reinterpret_cast<uintptr_t>(v)) &
+              15) == 0,
+             "comm_rs_adamw_allgather: optimizer state must be 16-byte aligned");
+  AdamScalars a;
+  a.lr = lr;
+  a.beta1 = beta1;
+  a.beta2 = beta2;
+  a.eps = eps;
+  a.decay = 1.0f - lr * wd;
+  a.step = (float)(lr / (1.0 - std::pow((double)beta1, (double)step)));
+  a.inv_sqrt_bc2 = (float)(1.0 / std::sqrt(1.0 - std::pow((double)beta2, (double)step)));
+  a.scale_const = 1.0f;
+  if (sq_out != nullptr) B200_CUDA_CHECK(cudaMemsetAsync(sq_out, 0, sizeof(float), s));
+  auto* M = reinterpret_cast<float4*>(master);
+  auto* Mm = reinterpret_cast<float4*>(m);
+  auto* Vv = reinterpret_cast<float4*>(v);
+  if (c.mc)
+    rs_adamw_allgather_kernel<true><<<c.blocks, kThreads, 0, s>>>(c, g, g_off, param_off, chunk / 8, M, Mm, Vv,
+                                                                  grad_scale, a, dev_sc, sq_out);
+  else
+    rs_adamw_allgather_kernel<false><<<c.blocks, kThreads, 0, s>>>(c, g, g_off, param_off, chunk / 8, M, Mm, Vv,
+                                                                   grad_scale, a, dev_sc, sq_out);
   B200_CUDA_CHECK(cudaGetLastError());
   count_launch();
 }

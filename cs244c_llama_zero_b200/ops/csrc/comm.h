@@ -54,6 +54,13 @@ void comm_gather_ce(const CommCtx& c, size_t off_bytes, size_t chunk_bytes, void
 void comm_adamw_allgather(const CommCtx& c, size_t param_off_bytes, size_t chunk, float* master, float* m, float* v,
                           const float* grad, const float* scale_ptr, float scale_const, float lr, float beta1,
                           float beta2, float eps, float wd, int step, cudaStream_t s, const float* dev_sc = nullptr);
+// The ZeRO-2 step without clipping as one kernel: g's region [g_off + rank*chunk*4, +chunk*4) summed
+// over ranks (fp32) and scaled by grad_scale is this rank's averaged gradient shard; its squared norm
+// is added to *sq_out (zeroed first; nullable); AdamW updates master/m/v [chunk]; the bf16 result
+// lands in every rank's parameter region of c at [param_off + rank*chunk*2].  Barriers use c.
+void comm_rs_adamw_allgather(const CommCtx& c, const CommCtx& g, size_t g_off, size_t param_off, size_t chunk,
+                             float* master, float* m, float* v, float grad_scale, float lr, float beta1, float beta2,
+                             float eps, float wd, int step, const float* dev_sc, float* sq_out, cudaStream_t s);
 // Standalone barrier among the ranks (every block of the communicator's grid).
 void comm_barrier(const CommCtx& c, cudaStream_t s);
 // A wait that nobody satisfies: used by tests to exercise the bounded-wait error path.

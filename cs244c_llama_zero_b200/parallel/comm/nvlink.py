@@ -274,6 +274,53 @@ class NvlinkCollectives(TorchCollectives):
         self._pace_end(slot, "allgather", chunk * 2 * world)
         return True
 
+    def allreduce_sum_small_(self, t: torch.Tensor) -> bool:
+        """``t`` (at most 8 fp32 values on this GPU) = its sum over ranks, with this package's all-reduce
+        kernel on a small symmetric buffer instead of an NCCL call (the gradient-norm scalar).  The
+        buffer is allocated at the first call, which is therefore a collective: every rank must make
+        the same calls in the same order, as with every collective.  False if ``t`` does not qualify."""
+        if t.dtype != torch.float32 or t.numel() > 8 or not t.is_cuda or self._w() == 1:
+            return False
+        if getattr(self, "_scalars", None) is None:
+            self._scalars = self.alloc(8, torch.float32)
+        buf = self._scalars
+        buf.zero_()
+        buf[: t.numel()].copy_(t.reshape(-1))
+        if self._skipped("allreduce_small"):
+            return True
+        self._locate(buf)[0].ctx.allreduce_f32(0, 8, 1.0)
+        t.reshape(-1).copy_(buf[: t.numel()])
+        return True
+
+    supports_fused_step = True
+
+    def reduce_scatter_adamw_allgather(self, params_flat: torch.Tensor, grads_flat: torch.Tensor, master: torch.Tensor,
+                                       exp_avg: torch.Tensor, exp_avg_sq: torch.Tensor, grad_scale: float, cfg,
+                                       step: int, dev_scalars: Optional[torch.Tensor] = None,
+                                       sq_out: Optional[torch.Tensor] = None) -> bool:
+        """The whole unclipped ZeRO-2 update in one kernel: reduce-scatter of ``grads_flat`` (fp32,
+        symmetric) times ``grad_scale``, its squared norm added to ``sq_out``, AdamW on this rank's
+        shard state and the bf16 all-gather into ``params_flat`` (symmetric).  No fp32 gradient shard
+        is written.  Returns False, doing nothing, when the buffers do not qualify."""
+        hp, hg = self._locate(params_flat), self._locate(grads_flat)
+        world = self._w()
+        chunk = master.numel()
+        if (hp is None or hg is None or params_flat.dtype != torch.bfloat16 or grads_flat.dtype != torch.float32
+                or params_flat.numel() != chunk * world or grads_flat.numel() != chunk * world or chunk % 8
+                or hp[0].multicast != hg[0].multicast):
+            return False
+        if self._skipped("rs_adamw_allgather"):
+            return True
+        (pbuf, poff), (gbuf, goff) = hp, hg
+        slot = self._pace_begin()
+        pbuf.ctx.rs_adamw_allgather(gbuf.ctx, goff, poff, chunk, master, exp_avg, exp_avg_sq, float(grad_scale), cfg.lr,
+                                    cfg.betas[0], cfg.betas[1], cfg.eps, cfg.weight_decay, step, dev_scalars, sq_out)
+        # reduce-scatter of the fp32 gradients, then all-gather of the bf16 shards
+        self._pace_end(slot, "reduce_scatter", grads_flat.numel() * 4)
+        slot = self._pace_begin()
+        self._pace_end(slot, "allgather", params_flat.numel() * 2)
+        return True
+
     def barrier(self) -> None:
         if self.buffers:
             if not self._skipped("barrier"):

@@ -91,9 +91,12 @@ def clip_coefficient(norm: torch.Tensor, max_grad_norm: float) -> torch.Tensor:
     return torch.where(norm > max_grad_norm, max_grad_norm / (norm + 1e-6), torch.ones_like(norm))
 
 
-def global_norm_from_local_sq(local_sq: torch.Tensor, sharded: bool) -> torch.Tensor:
-    """sqrt of the (all-reduced when sharded) sum of squares; stays on device."""
+def global_norm_from_local_sq(local_sq: torch.Tensor, sharded: bool, collectives=None) -> torch.Tensor:
+    """sqrt of the (all-reduced when sharded) sum of squares; stays on device.  Collectives with a
+    small-vector all-reduce kernel (the NVLink ones) reduce the scalar themselves; otherwise NCCL/gloo."""
     total = local_sq.reshape(1).clone()
     if sharded and dist.is_available() and dist.is_initialized() and dist.get_world_size() > 1:
-        dist.all_reduce(total)
+        small = getattr(collectives, "allreduce_sum_small_", None)
+        if small is None or not small(total):
+            dist.all_reduce(total)
     return total.sqrt().reshape(())

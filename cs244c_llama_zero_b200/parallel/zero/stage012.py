@@ -266,6 +266,47 @@ class ZeROStage2Optimizer(_ShardedStateMixin, _FlatEngine):
         self.grad_shard = torch.zeros(self.space.chunk, dtype=torch.float32, device=self.device)
         self._pending_flush = False
         self._setup_overlap()
+        self._setup_fused_step()
+
+    # -- the unclipped step as one kernel ----------------------------------------------------------
+    def _setup_fused_step(self) -> None:
+        """``ZB_FUSED_STEP=1``: with the NVLink collectives and no clipping, the step is ONE kernel
+        (reduce-scatter of the flat fp32 gradients -> averaged shard -> squared norm -> AdamW ->
+        bf16 all-gather, ``rs_adamw_allgather``): no fp32 gradient shard is written and read back,
+        and the separate norm kernel and one launch + barrier pair go away.  The reduce-scatter then
+        happens once per step (after the last micro-batch) instead of after every backward; the sum
+        is the same.  Steps with clipping take the two-kernel path."""
+        coll = self.collectives
+        self._fused_step = bool(
+            os.environ.get("ZB_FUSED_STEP", "0") == "1" and self.world_size > 1 and self.device.type == "cuda"
+            and not self._overlap and getattr(coll, "supports_fused_step", False)
+            and coll.locate_symmetric(self.space.params) is not None
+            and coll.locate_symmetric(self.space.grads) is not None
+            and self.space.params.numel() == self.space.chunk * self.world_size)
+        self._fused_sq = torch.zeros(1, dtype=torch.float32, device=self.device) if self._fused_step else None
+
+    def _fused_update(self) -> Optional[torch.Tensor]:
+        """The unclipped step in one kernel; None (nothing done) if the collectives decline."""
+        self.space.fold_autograd_grads()
+        step = self.step_count + 1
+        dev_scalars = self._device_scalars()
+        nbytes = tensor_num_bytes(self.space.grads)
+        self._record_memory_event("measured_step_stage2_pre_reduce_scatter")
+        with self.clock.measure("backward_reduce_scatter", nbytes):
+            with self.collectives.label_scope("stage2.step.reduce_scatter_adamw_allgather"):
+                ok = self.collectives.reduce_scatter_adamw_allgather(
+                    self.space.params, self.space.grads, self._master, self._exp_avg, self._exp_avg_sq,
+                    1.0 / self.world_size, self.adam, step, dev_scalars, self._fused_sq)
+        if not ok:
+            if dev_scalars is not None:  # give back the device step taken for the declined kernel
+                self._dev_step[0].sub_(1)
+            return None
+        self.step_count = step
+        self.clock.count("post_allgather", tensor_num_bytes(self.space.shard(self.space.params)))
+        self._pending_flush = False
+        for label in ("post_reduce_scatter", "pre_allgather", "post_allgather", "post_step_free_grad_shard"):
+            self._record_memory_event(f"measured_step_stage2_{label}")
+        return global_norm_from_local_sq(self._fused_sq, sharded=True, collectives=self.collectives)
 
     # -- reduce-scatter overlapped with backward -------------------------------------------
     def _setup_overlap(self) -> None:
@@ -359,7 +400,8 @@ class ZeROStage2Optimizer(_ShardedStateMixin, _FlatEngine):
             if self._overlap:
                 self._overlap_active = False
         self._pending_flush = True
-        self._flush_flat_grad_buffer()
+        if not self._fused_step:  # the fused step reduces once, inside the optimizer kernel
+            self._flush_flat_grad_buffer()
 
     def _flush_overlapped(self) -> None:
         """Reduce what the per-block buckets did not cover, then join the side stream."""
@@ -407,6 +449,10 @@ class ZeROStage2Optimizer(_ShardedStateMixin, _FlatEngine):
     def _update(self, max_grad_norm: float) -> torch.Tensor:
         if any(p.grad is not None for p in self.meta.params) and not hasattr(self.meta.params[0], "main_grad"):
             raise RuntimeError("Stage 2 expects gradients in the flat buffer")
+        if self._fused_step and max_grad_norm <= 0 and self._pending_flush:
+            norm = self._fused_update()
+            if norm is not None:
+                return norm
         self._flush_flat_grad_buffer()
         norm = global_norm_from_local_sq(sum_of_squares(self.grad_shard), sharded=self.world_size > 1)
         self.step_count += 1

@@ -268,3 +268,84 @@ def _memory_worker(rank: int, world: int, port: int) -> None:
 
 def test_stage2_memory_accounting_and_trace_order() -> None:
     _spawn(_memory_worker, 2)
+
+
+class _FusedStepCollectives(TorchCollectives):
+    """Stands in for the NVLink kernel of the one-kernel stage-2 step with the same maths in torch."""
+
+    supports_fused_step = True
+
+    def __init__(self):
+        self.fused_calls = 0
+        self.rs_calls = 0
+
+    def locate_symmetric(self, t):
+        return ("ctx", 0)
+
+    def reduce_scatter_accumulate_(self, acc, flat, scale):
+        self.rs_calls += 1
+        return super().reduce_scatter_accumulate_(acc, flat, scale)
+
+    def reduce_scatter_adamw_allgather(self, params_flat, grads_flat, master, exp_avg, exp_avg_sq, grad_scale, cfg,
+                                       step, dev_scalars=None, sq_out=None):
+        from cs244c_llama_zero_b200.parallel.zero.optim import adamw_update_
+
+        self.fused_calls += 1
+        shard = torch.zeros(master.numel())
+        self.reduce_scatter_into(shard, grads_flat)
+        shard.mul_(grad_scale)
+        if sq_out is not None:
+            sq_out.zero_().add_(shard.pow(2).sum())
+        out = torch.empty(master.numel(), dtype=params_flat.dtype)
+        adamw_update_(master, exp_avg, exp_avg_sq, shard, cfg, step, param_out=out)
+        self.allgather_into(params_flat, out)
+        return True
+
+
+def _fused_step_worker(rank: int, world: int, port: int, grad_accum: int) -> None:
+    init_gloo(rank, world, port)
+    try:
+        cfg = _cfg()
+        torch.manual_seed(1234)
+        model = LlamaForCausalLM(cfg)
+        for p in model.parameters():
+            dist.broadcast(p.data, src=0)
+        ref = LlamaForCausalLM(cfg)
+        ref.load_state_dict(model.state_dict())
+        hp = dict(lr=1e-3, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.05)
+        coll = _FusedStepCollectives()
+        engine = ZeROStage2Optimizer(model=model, collectives=coll, **hp)
+        engine._fused_step, engine._fused_sq = True, torch.zeros(1)  # what the NVLink setup enables on GPUs
+        opt = torch.optim.AdamW(ref.parameters(), **hp)
+        for step in range(3):
+            micro = [_local_batch(step * 10 + m, rank, 3, cfg.max_seq_len, cfg.vocab_size) for m in range(grad_accum)]
+            engine.zero_grad()
+            engine.prepare_forward()
+            for ids in micro:
+                engine.backward(model(input_ids=ids, labels=ids).loss / grad_accum)
+            stats = engine.step_with_stats(max_grad_norm=0.0)
+            opt.zero_grad(set_to_none=True)
+            for ids in micro:
+                parts = [torch.empty_like(ids) for _ in range(world)]
+                dist.all_gather(parts, ids)
+                g = torch.cat(parts)
+                (ref(input_ids=g, labels=g).loss / grad_accum).backward()
+            want_norm = torch.sqrt(sum(p.grad.float().pow(2).sum() for p in ref.parameters()))
+            opt.step()
+            _assert_close(model, ref, f"fused step={step} rank={rank}")
+            torch.testing.assert_close(torch.tensor(stats["grad_norm"]), want_norm, rtol=1e-4, atol=1e-6)
+        assert coll.fused_calls == 3 and coll.rs_calls == 0  # one fused collective per step, whatever grad_accum
+        assert engine.step_count == 3
+        engine.zero_grad()
+        ids = _local_batch(99, rank, 3, cfg.max_seq_len, cfg.vocab_size)
+        engine.backward(model(input_ids=ids, labels=ids).loss)
+        engine.step(max_grad_norm=0.5)  # clipping takes the two-kernel path
+        assert coll.fused_calls == 3 and coll.rs_calls == 1 and engine.step_count == 4
+    finally:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("grad_accum", [1, 2])
+def test_stage2_fused_step_plumbing_matches_reference(grad_accum: int) -> None:
+    _spawn(_fused_step_worker, 2, grad_accum)
