@@ -46,6 +46,8 @@ def parse_args(argv=None) -> argparse.Namespace:
     p.add_argument("--collective-impl", type=str, default="auto", help="auto | torch | nvls | p2p")
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--clocks-csv", type=str, default=None, help="keep the raw nvidia-smi clock samples here")
+    p.add_argument("--fused-step", action="store_true",
+                   help="ZeRO-1/2 unclipped step as one NVLink kernel (reduce-scatter + norm + AdamW + all-gather)")
     p.add_argument("--cuda-graph", action="store_true",
                    help="run stages 0-2 as one captured CUDA graph per step (TrainSession cuda_graph mode)")
     p.add_argument("--model-size", type=str, default="baseline-small",
@@ -227,6 +229,8 @@ def run_mine(args) -> None:
     rank, world, local = dist_env()
     if world != args.gpus and rank == 0:
         print(f"[bench] note: --gpus {args.gpus} but WORLD_SIZE={world}; using {world}", file=sys.stderr)
+    if args.fused_step:
+        os.environ["ZB_FUSED_STEP"] = "1"
     impl = args.collective_impl
     if impl == "auto":
         impl = "nvls" if world > 1 else "torch"
@@ -322,6 +326,7 @@ def run_mine(args) -> None:
                    "seq_len": args.seq_len, "grad_accum": 1, "parallelism": f"dp{world}",
                    "zero_stage": args.headline_stage, "collective_impl": impl,
                    "cuda_graph": bool(args.cuda_graph and args.headline_stage != 3),
+                   "fused_step": bool(args.fused_step),
                    "l2": "no flush: each step touches >2 GB (activations, 1.2 GB fp32 optimizer state) vs 126 MB L2"},
         "per_stage": per_stage,
         "e2e": e2e,

@@ -121,6 +121,49 @@ class _FlatEngine(ZeROEngineBase):
         self._adamw(grads, scale, dev_scalars)
         self._allgather_params()
 
+    # -- the unclipped step as one kernel (stages 1 and 2) -------------------------------------------
+    def _setup_fused_step(self) -> None:
+        """``ZB_FUSED_STEP=1``: with the NVLink collectives and no clipping, the step is ONE kernel
+        (reduce-scatter of the flat fp32 gradients -> averaged shard -> squared norm -> AdamW ->
+        bf16 all-gather, ``rs_adamw_allgather``): no fp32 gradient shard is written and read back,
+        and the separate norm kernel and one launch + barrier pair go away.  Stage 2's
+        reduce-scatter then happens once per step instead of after every backward (the sum is the
+        same); stage 1's full all-reduce becomes that reduce-scatter (without clipping only this
+        rank's shard of the averaged gradient is needed; the norm over the shards equals the norm of
+        the full vector).  Steps with clipping take the unfused path."""
+        coll = self.collectives
+        self._fused_step = bool(
+            os.environ.get("ZB_FUSED_STEP", "0") == "1" and self.world_size > 1 and self.device.type == "cuda"
+            and not getattr(self, "_overlap", False) and getattr(coll, "supports_fused_step", False)
+            and coll.locate_symmetric(self.space.params) is not None
+            and coll.locate_symmetric(self.space.grads) is not None
+            and self.space.params.numel() == self.space.chunk * self.world_size)
+        self._fused_sq = torch.zeros(1, dtype=torch.float32, device=self.device) if self._fused_step else None
+
+    def _fused_update(self, labels: Tuple[str, ...]) -> Optional[torch.Tensor]:
+        """The unclipped step in one kernel; None (nothing done) if the collectives decline.
+        ``labels[0]`` is recorded before the kernel, the rest after it (memory trace)."""
+        self.space.fold_autograd_grads()
+        step = self.step_count + 1
+        dev_scalars = self._device_scalars()
+        nbytes = tensor_num_bytes(self.space.grads)
+        self._record_memory_event(labels[0])
+        category = "backward_reduce_scatter" if self.stage == 2 else "allreduce"
+        with self.clock.measure(category, nbytes):
+            with self.collectives.label_scope(f"stage{self.stage}.step.reduce_scatter_adamw_allgather"):
+                ok = self.collectives.reduce_scatter_adamw_allgather(
+                    self.space.params, self.space.grads, self._master, self._exp_avg, self._exp_avg_sq,
+                    1.0 / self.world_size, self.adam, step, dev_scalars, self._fused_sq)
+        if not ok:
+            if dev_scalars is not None:  # give back the device step taken for the declined kernel
+                self._dev_step[0].sub_(1)
+            return None
+        self.step_count = step
+        self.clock.count("post_allgather", tensor_num_bytes(self.space.shard(self.space.params)))
+        for label in labels[1:]:
+            self._record_memory_event(label)
+        return global_norm_from_local_sq(self._fused_sq, sharded=True, collectives=self.collectives)
+
     def _param_out(self) -> torch.Tensor:
         return self.space.shard(self.space.params) if self.shard_optimizer else self.space.params
 
@@ -229,7 +272,16 @@ class ZeROStage1Optimizer(_ShardedStateMixin, _FlatEngine):
     stage = 1
     shard_optimizer = True
 
+    def __init__(self, model: nn.Module, **kwargs) -> None:
+        super().__init__(model, **kwargs)
+        self._setup_fused_step()
+
     def _update(self, max_grad_norm: float) -> torch.Tensor:
+        if self._fused_step and max_grad_norm <= 0:
+            norm = self._fused_update(tuple(f"measured_step_stage1_{x}" for x in (
+                "pre_allreduce", "post_allreduce", "pre_allgather", "post_allgather")))
+            if norm is not None:
+                return norm
         self.space.fold_autograd_grads()
         grads = self.space.grads
         if self.world_size > 1:
@@ -267,46 +319,6 @@ class ZeROStage2Optimizer(_ShardedStateMixin, _FlatEngine):
         self._pending_flush = False
         self._setup_overlap()
         self._setup_fused_step()
-
-    # -- the unclipped step as one kernel ----------------------------------------------------------
-    def _setup_fused_step(self) -> None:
-        """``ZB_FUSED_STEP=1``: with the NVLink collectives and no clipping, the step is ONE kernel
-        (reduce-scatter of the flat fp32 gradients -> averaged shard -> squared norm -> AdamW ->
-        bf16 all-gather, ``rs_adamw_allgather``): no fp32 gradient shard is written and read back,
-        and the separate norm kernel and one launch + barrier pair go away.  The reduce-scatter then
-        happens once per step (after the last micro-batch) instead of after every backward; the sum
-        is the same.  Steps with clipping take the two-kernel path."""
-        coll = self.collectives
-        self._fused_step = bool(
-            os.environ.get("ZB_FUSED_STEP", "0") == "1" and self.world_size > 1 and self.device.type == "cuda"
-            and not self._overlap and getattr(coll, "supports_fused_step", False)
-            and coll.locate_symmetric(self.space.params) is not None
-            and coll.locate_symmetric(self.space.grads) is not None
-            and self.space.params.numel() == self.space.chunk * self.world_size)
-        self._fused_sq = torch.zeros(1, dtype=torch.float32, device=self.device) if self._fused_step else None
-
-    def _fused_update(self) -> Optional[torch.Tensor]:
-        """The unclipped step in one kernel; None (nothing done) if the collectives decline."""
-        self.space.fold_autograd_grads()
-        step = self.step_count + 1
-        dev_scalars = self._device_scalars()
-        nbytes = tensor_num_bytes(self.space.grads)
-        self._record_memory_event("measured_step_stage2_pre_reduce_scatter")
-        with self.clock.measure("backward_reduce_scatter", nbytes):
-            with self.collectives.label_scope("stage2.step.reduce_scatter_adamw_allgather"):
-                ok = self.collectives.reduce_scatter_adamw_allgather(
-                    self.space.params, self.space.grads, self._master, self._exp_avg, self._exp_avg_sq,
-                    1.0 / self.world_size, self.adam, step, dev_scalars, self._fused_sq)
-        if not ok:
-            if dev_scalars is not None:  # give back the device step taken for the declined kernel
-                self._dev_step[0].sub_(1)
-            return None
-        self.step_count = step
-        self.clock.count("post_allgather", tensor_num_bytes(self.space.shard(self.space.params)))
-        self._pending_flush = False
-        for label in ("post_reduce_scatter", "pre_allgather", "post_allgather", "post_step_free_grad_shard"):
-            self._record_memory_event(f"measured_step_stage2_{label}")
-        return global_norm_from_local_sq(self._fused_sq, sharded=True, collectives=self.collectives)
 
     # -- reduce-scatter overlapped with backward -------------------------------------------
     def _setup_overlap(self) -> None:
@@ -450,8 +462,11 @@ class ZeROStage2Optimizer(_ShardedStateMixin, _FlatEngine):
         if any(p.grad is not None for p in self.meta.params) and not hasattr(self.meta.params[0], "main_grad"):
             raise RuntimeError("Stage 2 expects gradients in the flat buffer")
         if self._fused_step and max_grad_norm <= 0 and self._pending_flush:
-            norm = self._fused_update()
+            norm = self._fused_update(tuple(f"measured_step_stage2_{x}" for x in (
+                "pre_reduce_scatter", "post_reduce_scatter", "pre_allgather", "post_allgather",
+                "post_step_free_grad_shard")))
             if norm is not None:
+                self._pending_flush = False
                 return norm
         self._flush_flat_grad_buffer()
         norm = global_norm_from_local_sq(sum_of_squares(self.grad_shard), sharded=self.world_size > 1)

@@ -1,9 +1,9 @@
-"""The one-kernel unclipped ZeRO-2 step (``rs_adamw_allgather``): reduce-scatter of the flat fp32
+"""The one-kernel unclipped ZeRO-1/2 step (``rs_adamw_allgather``): reduce-scatter of the flat fp32
 gradients, squared norm, AdamW and bf16 all-gather in one launch.
 
 * one GPU (a world of one rank, plain peer loads): the kernel against the step written out in
   fp32 PyTorch;
-* two GPUs: the stage-2 engine with ``ZB_FUSED_STEP=1`` trains like the NCCL engine.
+* two GPUs: the stage-1 and stage-2 engines with ``ZB_FUSED_STEP=1`` train like the NCCL engines.
 """
 
 from __future__ import annotations
@@ -79,13 +79,13 @@ def test_fused_step_kernel_matches_fp32_reference():
     mp.spawn(_kernel_worker, args=(1, find_free_port()), nprocs=1, join=True)
 
 
-def _engine_worker(rank: int, world: int, port: int) -> None:
+def _engine_worker(rank: int, world: int, port: int, stage: int) -> None:
     _init(rank, world, port)
     try:
         from cs244c_llama_zero_b200.models import LlamaForCausalLM, ModelConfig
         from cs244c_llama_zero_b200.parallel import TorchCollectives
         from cs244c_llama_zero_b200.parallel.comm.nvlink import NvlinkCollectives
-        from cs244c_llama_zero_b200.parallel.zero import ZeROStage2Optimizer
+        from cs244c_llama_zero_b200.parallel.zero import ENGINES
 
         cfg = ModelConfig(name="t", vocab_size=1024, max_seq_len=256, dim=256, n_layers=2, n_heads=4, n_kv_heads=2,
                           ffn_dim=512)
@@ -97,7 +97,7 @@ def _engine_worker(rank: int, world: int, port: int) -> None:
             model = LlamaForCausalLM(cfg).cuda().to(torch.bfloat16)
             model.set_backend("b200")
             models.append(model)
-            engines.append(ZeROStage2Optimizer(model=model, lr=1e-3, collectives=coll))
+            engines.append(ENGINES[stage](model=model, lr=1e-3, collectives=coll))
         assert engines[1]._fused_step and not engines[0]._fused_step
         ids = torch.randint(0, cfg.vocab_size, (2, cfg.max_seq_len), device="cuda",
                             generator=torch.Generator(device="cuda").manual_seed(rank))
@@ -119,6 +119,7 @@ def _engine_worker(rank: int, world: int, port: int) -> None:
         dist.destroy_process_group()
 
 
-def test_stage2_fused_step_trains_like_nccl():
+@pytest.mark.parametrize("stage", [1, 2])
+def test_fused_step_trains_like_nccl(stage):
     _need(2)
-    mp.spawn(_engine_worker, args=(2, find_free_port()), nprocs=2, join=True)
+    mp.spawn(_engine_worker, args=(2, find_free_port(), stage), nprocs=2, join=True)

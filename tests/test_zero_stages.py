@@ -286,6 +286,10 @@ class _FusedStepCollectives(TorchCollectives):
         self.rs_calls += 1
         return super().reduce_scatter_accumulate_(acc, flat, scale)
 
+    def allreduce_scaled_(self, flat, scale):
+        self.rs_calls += 1
+        return super().allreduce_scaled_(flat, scale)
+
     def reduce_scatter_adamw_allgather(self, params_flat, grads_flat, master, exp_avg, exp_avg_sq, grad_scale, cfg,
                                        step, dev_scalars=None, sq_out=None):
         from cs244c_llama_zero_b200.parallel.zero.optim import adamw_update_
@@ -302,7 +306,7 @@ class _FusedStepCollectives(TorchCollectives):
         return True
 
 
-def _fused_step_worker(rank: int, world: int, port: int, grad_accum: int) -> None:
+def _fused_step_worker(rank: int, world: int, port: int, stage: int, grad_accum: int) -> None:
     init_gloo(rank, world, port)
     try:
         cfg = _cfg()
@@ -314,7 +318,7 @@ def _fused_step_worker(rank: int, world: int, port: int, grad_accum: int) -> Non
         ref.load_state_dict(model.state_dict())
         hp = dict(lr=1e-3, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.05)
         coll = _FusedStepCollectives()
-        engine = ZeROStage2Optimizer(model=model, collectives=coll, **hp)
+        engine = ENGINES[stage](model=model, collectives=coll, **hp)
         engine._fused_step, engine._fused_sq = True, torch.zeros(1)  # what the NVLink setup enables on GPUs
         opt = torch.optim.AdamW(ref.parameters(), **hp)
         for step in range(3):
@@ -332,7 +336,7 @@ def _fused_step_worker(rank: int, world: int, port: int, grad_accum: int) -> Non
                 (ref(input_ids=g, labels=g).loss / grad_accum).backward()
             want_norm = torch.sqrt(sum(p.grad.float().pow(2).sum() for p in ref.parameters()))
             opt.step()
-            _assert_close(model, ref, f"fused step={step} rank={rank}")
+            _assert_close(model, ref, f"fused stage={stage} step={step} rank={rank}")
             torch.testing.assert_close(torch.tensor(stats["grad_norm"]), want_norm, rtol=1e-4, atol=1e-6)
         assert coll.fused_calls == 3 and coll.rs_calls == 0  # one fused collective per step, whatever grad_accum
         assert engine.step_count == 3
@@ -346,6 +350,6 @@ def _fused_step_worker(rank: int, world: int, port: int, grad_accum: int) -> Non
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("grad_accum", [1, 2])
-def test_stage2_fused_step_plumbing_matches_reference(grad_accum: int) -> None:
-    _spawn(_fused_step_worker, 2, grad_accum)
+@pytest.mark.parametrize("stage,grad_accum", [(1, 1), (2, 1), (2, 2)])
+def test_fused_step_plumbing_matches_reference(stage: int, grad_accum: int) -> None:
+    _spawn(_fused_step_worker, 2, stage, grad_accum)
