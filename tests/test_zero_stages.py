@@ -353,3 +353,27 @@ def _fused_step_worker(rank: int, world: int, port: int, stage: int, grad_accum:
 @pytest.mark.parametrize("stage,grad_accum", [(1, 1), (2, 1), (2, 2)])
 def test_fused_step_plumbing_matches_reference(stage: int, grad_accum: int) -> None:
     _spawn(_fused_step_worker, 2, stage, grad_accum)
+
+
+def test_stage2_on_one_rank_matches_stage0_with_grad_accum() -> None:
+    """On one rank stage 2's gradient shard is the flat gradient buffer itself (no copy); training
+    must equal stage 0 step for step, with several micro-batches per step."""
+    cfg = _cfg()
+    runs = []
+    for stage in (0, 2):
+        torch.manual_seed(1234)
+        model = LlamaForCausalLM(cfg)
+        engine = ENGINES[stage](model=model, lr=1e-3, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.05)
+        norms = []
+        for step in range(3):
+            engine.zero_grad()
+            engine.prepare_forward()
+            for m in range(2):
+                ids = _local_batch(step * 10 + m, 0, 3, cfg.max_seq_len, cfg.vocab_size)
+                engine.backward(model(input_ids=ids, labels=ids).loss / 2)
+            norms.append(engine.step(max_grad_norm=0.5))
+        runs.append((model, norms))
+        if stage == 2:
+            assert engine.grad_shard.data_ptr() == engine.space.grads.data_ptr()
+    _assert_close(runs[0][0], runs[1][0], "stage 2 vs stage 0 on one rank")
+    torch.testing.assert_close(torch.tensor(runs[1][1]), torch.tensor(runs[0][1]))
