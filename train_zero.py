@@ -112,6 +112,9 @@ def parse_args(argv=None) -> argparse.Namespace:
     p.add_argument("--memory-warmup-steps", type=int, default=0)
     p.add_argument("--tflops-mode", type=str, default="estimate", choices=["estimate", "profile", "off"])
     p.add_argument("--nvtx", action="store_true", help="name the step phases with NVTX ranges (Nsight timelines)")
+    p.add_argument("--fused-step", action="store_true",
+                   help="stages 1/2 with --collective-impl nvls|p2p and no clipping: the step as one NVLink kernel "
+                        "(reduce-scatter + norm + AdamW + all-gather)")
     p.add_argument("--verbose", action="store_true")
     p.add_argument("--verbose-memory", action="store_true")
     p.add_argument("--stage3-recompute", action="store_true",
@@ -228,6 +231,8 @@ def train(args: argparse.Namespace) -> None:
     verbose = bool(args.verbose)
     if getattr(args, "nvtx", False):
         nvtx.enable(True)
+    if getattr(args, "fused_step", False):
+        os.environ["ZB_FUSED_STEP"] = "1"  # read by the stage 1/2 engines when they are built
     configure_runtime(device)
     set_seed(args.seed)
     log_event(rank, f"initialized distributed world_size={world_size} device={device} pid={os.getpid()}", force=verbose)
