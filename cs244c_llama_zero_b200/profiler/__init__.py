@@ -4,6 +4,8 @@ from .flops import (
     estimate_transformer_train_flops,
     executed_train_flops,
     flops_to_tflops_per_second,
+    peak_bf16_tflops,
+    roofline_fraction,
 )
 from . import nvtx
 from .memory import MemorySnapshot, MemoryTracker, take_memory_snapshot
@@ -16,6 +18,8 @@ __all__ = [
     "estimate_transformer_train_flops",
     "executed_train_flops",
     "flops_to_tflops_per_second",
+    "peak_bf16_tflops",
+    "roofline_fraction",
     "MemorySnapshot",
     "MemoryTracker",
     "take_memory_snapshot",

@@ -9,8 +9,10 @@ recompute unless asked) for roofline fractions.
 
 from __future__ import annotations
 
+import json
+import os
 from dataclasses import asdict, dataclass
-from typing import TYPE_CHECKING, Callable, Dict, Generic, List, Optional, TypeVar
+from typing import TYPE_CHECKING, Callable, Dict, Generic, List, Optional, Tuple, TypeVar
 
 import torch
 
@@ -74,6 +76,39 @@ def executed_train_flops(cfg: "ModelConfig", batch_size: int, seq_len: int, reco
     if recompute_forward:
         total += matmul + attention
     return total
+
+
+FALLBACK_PEAK_BF16_TFLOPS = 1400.0  # sustained dense bf16 GEMM of a B200 under its 1 kW power cap
+
+
+def peak_bf16_tflops(root: Optional[str] = None) -> Tuple[float, str]:
+    """(dense bf16 TFLOP/s per GPU, where it came from) for roofline fractions.
+
+    Order: ``ZB_PEAK_TFLOPS``; ``bf16_tflops_sustained`` of a ``MEASURED_PEAKS.json`` (a cuBLAS bf16
+    GEMM timed on the same pool) in ``root`` or the repository root; else the fallback constant.
+    A training step runs for seconds under the power cap, so the sustained figure is the fair one.
+    """
+    env = os.environ.get("ZB_PEAK_TFLOPS", "").strip()
+    if env:
+        return float(env), "ZB_PEAK_TFLOPS"
+    base = root or os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+    path = os.path.join(base, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as fh:
+            data = json.load(fh)
+        value = float(data.get("bf16_tflops_sustained") or data["bf16_tflops"])
+        if value > 0:
+            return value, "measured"
+    except (OSError, ValueError, KeyError, TypeError):
+        pass
+    return FALLBACK_PEAK_BF16_TFLOPS, "fallback"
+
+
+def roofline_fraction(executed_flops: float, seconds: float, peak_tflops: float) -> Optional[float]:
+    """Achieved tensor-core FLOP/s over the peak (None without a positive time or peak)."""
+    if seconds <= 0 or peak_tflops <= 0:
+        return None
+    return executed_flops / seconds / (peak_tflops * 1e12)
 
 
 @dataclass

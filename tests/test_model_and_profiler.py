@@ -203,3 +203,18 @@ def test_nvtx_ranges_are_balanced_and_off_by_default(monkeypatch):
                          ("push", "raises"), ("pop",)]
     finally:
         nvtx.enable(was)
+
+
+def test_peak_lookup_and_roofline_fraction(tmp_path, monkeypatch):
+    import json as _json
+
+    from cs244c_llama_zero_b200.profiler import flops as F
+
+    monkeypatch.delenv("ZB_PEAK_TFLOPS", raising=False)
+    assert F.peak_bf16_tflops(str(tmp_path)) == (F.FALLBACK_PEAK_BF16_TFLOPS, "fallback")
+    (tmp_path / "MEASURED_PEAKS.json").write_text(_json.dumps({"bf16_tflops": 1646.4, "bf16_tflops_sustained": 1388.8}))
+    assert F.peak_bf16_tflops(str(tmp_path)) == (1388.8, "measured")
+    monkeypatch.setenv("ZB_PEAK_TFLOPS", "1000")
+    assert F.peak_bf16_tflops(str(tmp_path)) == (1000.0, "ZB_PEAK_TFLOPS")
+    assert F.roofline_fraction(5e14, 1.0, 1000.0) == pytest.approx(0.5)
+    assert F.roofline_fraction(1.0, 0.0, 1000.0) is None

@@ -37,8 +37,11 @@ from cs244c_llama_zero_b200.profiler import (
     MemoryTracker,
     TimerRegistry,
     estimate_transformer_train_flops,
+    executed_train_flops,
     flops_to_tflops_per_second,
     overlap_efficiency,
+    peak_bf16_tflops,
+    roofline_fraction,
 )
 from cs244c_llama_zero_b200.profiler import nvtx
 from cs244c_llama_zero_b200.profiler.nvtx import nvtx_range
@@ -292,6 +295,12 @@ def train(args: argparse.Namespace) -> None:
     if args.tflops_mode == "estimate":
         step_flops = estimate_transformer_train_flops(cfg, args.batch_size, args.seq_len, args.grad_accum_steps,
                                                       world_size, stage=args.zero_stage)
+    # roofline: the FLOPs this GPU really executes per step (no 4x stage-3 convention) over the peak
+    executed_flops = executed_train_flops(cfg, args.batch_size, args.seq_len,
+                                          recompute_forward=args.zero_stage == 3 and (
+                                              backend != "b200" or bool(getattr(args, "stage3_recompute", False)))
+                                          ) * args.grad_accum_steps
+    peak_tflops, peak_source = peak_bf16_tflops()
     step_profiles: List[Dict[str, object]] = []
     measured_step_memory = None
     recent: List[float] = []
@@ -386,7 +395,9 @@ def train(args: argparse.Namespace) -> None:
             record = {"step": step, "loss": step_loss, "tokens_per_second": tokens_per_second,
                       "tflops_per_second": tflops, "grad_norm": grad_norm, "forward_backward_ms": fb_ms,
                       "communication_ms": comm_ms, "optimizer_ms": float(stats["optim_ms"]), "iteration_ms": iter_ms,
-                      "iteration_ms_max_over_ranks": iter_ms_max}
+                      "iteration_ms_max_over_ranks": iter_ms_max,
+                      "executed_tflops_per_gpu": executed_flops / max(iter_ms_max, 1e-6) / 1e9,
+                      "roofline_fraction": roofline_fraction(executed_flops, iter_ms_max / 1000.0, peak_tflops)}
             for key in STEP_COMM_KEYS:
                 record[key] = float(stats.get(key, 0.0))
             record.update({"collective_trace": trace, "collective_trace_summary": trace_summary,
@@ -435,6 +446,8 @@ def train(args: argparse.Namespace) -> None:
             "state_memory_breakdown_mb": engine.memory_state_breakdown_mb(), "overlap_summary": overlap_summary,
             "measured_step_memory": measured_step_memory, "measured_step_state_timeline": recorder.timeline,
             "backend": backend,
+            "roofline": {"executed_flops_per_gpu_step": executed_flops, "peak_bf16_tflops": peak_tflops,
+                         "peak_source": peak_source},
         }
         path = Path(args.profile_json)
         if world_size > 1 and not args.profile_rank0_only:
