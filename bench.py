@@ -218,14 +218,27 @@ def base_record(args, world: int, impl: str) -> dict:
 
 
 # ----------------------------------------------------------------------------------- our arm
+def roofline_entry(sess, args, stage: int, ms: float, peak_tflops: float) -> dict:
+    """Executed tensor-core TFLOP/s of one GPU's step (causal attention halved, no recompute unless the
+    stage-3 engine recomputes) and its fraction of the peak."""
+    from cs244c_llama_zero_b200.profiler import executed_train_flops, roofline_fraction
+
+    recompute = stage == 3 and bool(getattr(sess.engine, "recompute", False))
+    executed = executed_train_flops(sess.model_cfg, args.batch_size, args.seq_len, recompute_forward=recompute)
+    return {"executed_tflops_per_gpu": executed / (ms / 1000.0) / 1e12,
+            "roofline_fraction": roofline_fraction(executed, ms / 1000.0, peak_tflops)}
+
+
 def run_mine(args) -> None:
     import torch
     import torch.distributed as dist
 
     from cs244c_llama_zero_b200 import ops
     from cs244c_llama_zero_b200.models import BASELINE_VOCAB_SIZE
+    from cs244c_llama_zero_b200.profiler import peak_bf16_tflops
     from cs244c_llama_zero_b200.train import SessionConfig, TrainSession
 
+    peak_tflops, peak_source = peak_bf16_tflops()
     rank, world, local = dist_env()
     if world != args.gpus and rank == 0:
         print(f"[bench] note: --gpus {args.gpus} but WORLD_SIZE={world}; using {world}", file=sys.stderr)
@@ -267,8 +280,9 @@ def run_mine(args) -> None:
             sampler.__exit__(None, None, None)
             clocks = sampler.summary()
         stage_launches = (ops.launch_count() - launches_before) // args.steps
-        entry ={"tokens_per_s": tokens_per_step / (ms / 1000.0), "ms_per_step": ms,
+        entry = {"tokens_per_s": tokens_per_step / (ms / 1000.0), "ms_per_step": ms,
                  "gpu_launches_per_step": stage_launches}
+        entry.update(roofline_entry(sess, args, stage, ms, peak_tflops))
         # comm time of one extra instrumented step (device events around each collective); the
         # barrier keeps host-side skew between ranks out of the measured intervals
         barrier_sync()
@@ -329,6 +343,10 @@ def run_mine(args) -> None:
                    "fused_step": bool(args.fused_step),
                    "l2": "no flush: each step touches >2 GB (activations, 1.2 GB fp32 optimizer state) vs 126 MB L2"},
         "per_stage": per_stage,
+        "roofline": {"executed_tflops_per_gpu": head["executed_tflops_per_gpu"],
+                     "fraction": head["roofline_fraction"], "peak_bf16_tflops": peak_tflops,
+                     "peak_source": peak_source, "note": "of measured sustained cuBLAS bf16 GEMM peak"
+                     if peak_source == "measured" else "of fallback peak"},
         "e2e": e2e,
         "gpu_launches": launches,
         "clocks": clocks,

@@ -70,3 +70,24 @@ def test_reference_suite_runner_maps_imports_and_stages(tmp_path):
     assert [p.name for p in staged] == ["test_x.py"]
     assert "cs244c_llama_zero_b200.models" in staged[0].read_text()
     assert (tmp_path / "staged" / "train_zero.py").exists()
+
+
+def test_bench_roofline_entry():
+    import types
+
+    sys.path.insert(0, str(ROOT))
+    try:
+        import bench
+    finally:
+        sys.path.pop(0)
+    from cs244c_llama_zero_b200.models import build_config
+    from cs244c_llama_zero_b200.profiler import executed_train_flops
+
+    cfg = build_config("baseline-small", vocab_size=32000, max_seq_len=1024)
+    sess = types.SimpleNamespace(model_cfg=cfg, engine=types.SimpleNamespace(recompute=False))
+    args = bench.parse_args(["--batch-size", "8", "--seq-len", "1024"])
+    e = bench.roofline_entry(sess, args, 2, 10.0, 1400.0)
+    flops = executed_train_flops(cfg, 8, 1024)
+    assert abs(e["executed_tflops_per_gpu"] - flops / 0.01 / 1e12) < 1e-6
+    assert abs(e["roofline_fraction"] - flops / 0.01 / 1.4e15) < 1e-9
+    assert 0.3 < e["roofline_fraction"] < 0.8  # ~5.4 TFLOP in 10 ms on a 1.4 PFLOP/s part
