@@ -164,6 +164,30 @@ void linear_wgrad(Tensor dy, Tensor x, Tensor dw, int64_t splits, int64_t bn) {
   b200::gemm_launch(op, p, b200::EPI_ACC_F32, true, true, (int)bn, cur_stream());
 }
 
+// dw = dy^T @ x with the reduce-scatter fused into the epilogue: element (n, k) of dw has flat index
+// flat0 + n * ld + k in a flat space split into `bases.size()` shards of `chunk` fp32 elements, and its
+// partial sum is added straight into the owning shard (`bases[r]`: rank r's shard as mapped on this
+// GPU; on one GPU they may all be local buffers).  Every rank calls this with its own dy / x; the
+// shards hold the sum over ranks once every rank's call has finished (order them with a barrier).
+void linear_wgrad_routed(Tensor dy, Tensor x, int64_t flat0, int64_t ld, int64_t chunk, std::vector<int64_t> bases,
+                         int64_t splits, int64_t bn) {
+  check_bf16_2d(dy, "dy");
+  check_bf16_2d(x, "x");
+  const int M = dy.size(0), N = dy.size(1), K = x.size(1);
+  TORCH_CHECK(x.size(0) == M, "linear_wgrad_routed: token counts differ");
+  TORCH_CHECK(!bases.empty() && (int)bases.size() <= b200::kRouteMaxWorld, "linear_wgrad_routed: 1..8 shards");
+  c10::cuda::CUDAGuard g(dy.device());
+  auto p = base_params(N, K, M);
+  p.splits = splits > 0 ? (int)splits : 0;
+  p.route_world = (int)bases.size();
+  for (size_t r = 0; r < bases.size(); ++r) p.route_base[r] = (uint64_t)bases[r];
+  p.route_ld = (int)ld;
+  p.route_chunk = chunk;
+  p.route_flat0 = flat0;
+  b200::GemmOperands op{dy.data_ptr(), x.data_ptr(), (uint64_t)dy.stride(0), (uint64_t)x.stride(0)};
+  b200::gemm_launch(op, p, b200::EPI_ACC_F32_ROUTED, true, true, (int)bn, cur_stream());
+}
+
 // dx = dy @ w and dw += dy^T @ x in one persistent launch (the two GEMMs of a linear layer's
 // backward pass share dy and are independent of each other).
 void linear_dgrad_wgrad(Tensor dy, Tensor w, Tensor x, Tensor dx, Tensor dw, int64_t splits) {
@@ -823,6 +847,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("linear_dgrad_wgrad", &linear_dgrad_wgrad, py::arg("dy"), py::arg("w"), py::arg("x"), py::arg("dx"),
         py::arg("dw"), py::arg("splits") = 0);
   m.def("swiglu_dgrad", &swiglu_dgrad);
+  m.def("linear_wgrad_routed", &linear_wgrad_routed, py::arg("dy"), py::arg("x"), py::arg("flat0"), py::arg("ld"),
+        py::arg("chunk"), py::arg("bases"), py::arg("splits") = 0, py::arg("bn") = 0);
   m.def("linear_wgrad", &linear_wgrad, py::arg("dy"), py::arg("x"), py::arg("dw"), py::arg("splits") = 0,
         py::arg("bn") = 0);
   m.def("gemm_raw", &gemm_raw);

@@ -201,6 +201,14 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
 
 // ---- TMA (tiled, non-multicast) -----------------------------------------------------------
 // Fetch the 128-byte line holding `ptr` into L2 (no register result, no completion to wait for).
+// dst[0..3] += {a, b, c, d} (fp32 bit patterns), one 16-byte vector reduction at system scope: the
+// address may be another GPU's memory mapped over NVLink, which other GPUs add into as well.
+__device__ __forceinline__ void red_add_f32x4_sys(float* dst, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+  asm volatile("red.relaxed.sys.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(dst), "f"(__uint_as_float(a)),
+               "f"(__uint_as_float(b)), "f"(__uint_as_float(c)), "f"(__uint_as_float(d))
+               : "memory");
+}
+
 __device__ __forceinline__ void prefetch_l2(const void* ptr) {
   asm volatile("prefetch.global.L2 [%0];" ::"l"(reinterpret_cast<uint64_t>(ptr)));
 }

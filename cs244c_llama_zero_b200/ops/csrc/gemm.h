@@ -17,7 +17,13 @@ enum GemmEpilogue : int {
   EPI_SWIGLU = 3,
   EPI_SWIGLU_BWD = 4,
   EPI_ACC_F32 = 5,
+  // Weight gradient with its reduce-scatter fused in: each fp32 partial sum is added straight into
+  // the gradient shard of the rank that owns that element (flat index / shard size), over NVLink
+  // peer mappings, with red.global.add.v4.f32 at system scope.  No local gradient buffer is written.
+  EPI_ACC_F32_ROUTED = 6,
 };
+
+constexpr int kRouteMaxWorld = 8;
 
 struct GemmOperands {
   const void* A;  // bf16; K-major: [M, K] with row stride lda; MN-major: [K, M] with row stride lda
@@ -49,6 +55,14 @@ struct GemmParams {
   // Grouped launches (gemm_launch_dgrad_wgrad): units [0, grp_units_first) belong to problem
   // grp_first, the rest (up to grp_units_total) to the other one.
   int grp_first, grp_units_first, grp_units_total;
+  // EPI_ACC_F32_ROUTED: output element (m, n) has flat index route_flat0 + m * route_ld + n; rank
+  // r = flat / route_chunk owns it and it lands at route_base[r][flat - r * route_chunk] (fp32 shard
+  // of rank r, mapped on this GPU).
+  uint64_t route_base[kRouteMaxWorld];
+  int route_world;
+  int route_ld;
+  long long route_chunk;
+  long long route_flat0;
 };
 
 struct GemmTile {

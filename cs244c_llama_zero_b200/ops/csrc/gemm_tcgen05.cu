@@ -22,6 +22,7 @@
 //   EPI_SWIGLU      B tile = [gate rows | up rows]; C = silu(g)*u, aux = [g | u]
 //   EPI_SWIGLU_BWD  acc = dA; reads [g | u]; C = [dG | dU]      (down_proj data gradient)
 //   EPI_ACC_F32     C32 += acc (fp32 atomics; split-K)          (weight gradients into main_grad)
+//   EPI_ACC_F32_ROUTED  owner's shard += acc over NVLink          (weight gradient + reduce-scatter)
 //
 // Every mbarrier wait is bounded (see common.cuh); a CTA whose wait expires records an error
 // and unwinds, releasing its tensor memory.
@@ -477,6 +478,33 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         }
       } else if constexpr (EPI == EPI_ACC_F32) {
         acc_f32_epilogue(&tmC);
+      } else if constexpr (EPI == EPI_ACC_F32_ROUTED) {
+        // Each 16-byte group of this row's partial sums goes to the rank owning it: the reduction
+        // across ranks happens in the owners' memory as the tiles finish, so no reduce-scatter runs
+        // after backward.  Groups never straddle owners (flat0, ld, chunk and the column are
+        // multiples of 4).
+        const int n0 = tn * BN + wg * (BN / 2);
+#pragma unroll 1
+        for (int c = 0; c < BN / 2; c += 16) {
+          uint32_t r[16];
+          tmem_ld_32x32b_x16(tbase + wg * (BN / 2) + c, r);
+          tc_wait_ld();
+          if (m < p.M) {
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const int col = n0 + c + 4 * j;
+              if (col >= p.N) continue;
+              const long long f = p.route_flat0 + (long long)m * p.route_ld + col;
+              const int owner = (int)(f / p.route_chunk);
+              if (owner < 0 || owner >= p.route_world) {
+                report_error(p.errs, kErrBadIndex, 200);
+                continue;
+              }
+              float* dst = reinterpret_cast<float*>(p.route_base[owner]) + (f - (long long)owner * p.route_chunk);
+              red_add_f32x4_sys(dst, r[4 * j], r[4 * j + 1], r[4 * j + 2], r[4 * j + 3]);
+            }
+          }
+        }
       } else if constexpr (EPI == EPI_ROPE) {
         const int n0 = tn * BN;
         const int half = p.head_dim >> 1;
@@ -681,6 +709,8 @@ static void launch_impl(const GemmOperands& op, GemmParams p, cudaStream_t strea
   CUtensorMap tmC = tmA, tmX = tmA, tmY = tmA;
   if (EPI == EPI_ACC_F32) {
     tmC = epi_map_f32(p.C32, p.M, p.N, p.ldc32);
+  } else if (EPI == EPI_ACC_F32_ROUTED) {
+    // no output map: the epilogue adds into the owners' shards with vector reductions
   } else if (EPI == EPI_SWIGLU) {
     tmC = epi_map_bf16(p.C, p.M, p.ffn, p.ldc);
     tmX = epi_map_bf16(p.aux, p.M, p.ffn, p.ld_aux);
@@ -784,20 +814,32 @@ GemmTile choose_gemm_tile(int M, int N, int K, int epi, int head_dim, bool allow
 
 void gemm_launch(const GemmOperands& op, GemmParams p, int epi, bool a_mn, bool b_mn, int bn, cudaStream_t stream) {
   int cg = 1;
+  const bool acc = epi == EPI_ACC_F32 || epi == EPI_ACC_F32_ROUTED;  // fp32-accumulating: K-split allowed
+  const int model_epi = acc ? EPI_ACC_F32 : epi;                        // same cost model for both
   if (bn <= 0) {  // automatic tile width, CTA group (and K-split for the fp32-accumulating epilogue)
-    const GemmTile t = choose_gemm_tile(p.M, p.N, p.K, epi, p.head_dim > 0 ? p.head_dim : 64,
-                                        epi == EPI_ACC_F32 && p.splits <= 0, b_mn, num_sms(), 0, 0);
+    const GemmTile t = choose_gemm_tile(p.M, p.N, p.K, model_epi, p.head_dim > 0 ? p.head_dim : 64,
+                                        acc && p.splits <= 0, b_mn, num_sms(), 0, 0);
     bn = t.bn;
     cg = t.cg;
-    if (epi == EPI_ACC_F32 && p.splits <= 0) p.splits = t.splits;
+    if (acc && p.splits <= 0) p.splits = t.splits;
   } else {
     if (bn >= 1000) {  // explicit CTA-pair request (tests, benchmarks): 1000 + tile width
       bn -= 1000;
       cg = 2;
       B200_CHECK(pair_supports(b_mn, bn), "CTA pairs with an MN-major B need BN / 2 to be a multiple of 64");
     }
-    if (epi == EPI_ACC_F32 && p.splits <= 0)  // explicit tile, automatic K-split
-      p.splits = choose_gemm_tile(p.M, p.N, p.K, epi, 64, true, b_mn, num_sms(), bn, cg).splits;
+    if (acc && p.splits <= 0)  // explicit tile, automatic K-split
+      p.splits = choose_gemm_tile(p.M, p.N, p.K, model_epi, 64, true, b_mn, num_sms(), bn, cg).splits;
+  }
+  if (epi == EPI_ACC_F32_ROUTED) {
+    B200_CHECK(p.route_world >= 1 && p.route_world <= kRouteMaxWorld, "routed wgrad: 1..8 ranks");
+    B200_CHECK(p.route_chunk > 0 && p.route_chunk % 4 == 0 && p.route_flat0 % 4 == 0 && p.route_ld % 4 == 0 &&
+                   p.route_ld >= p.N,
+               "routed wgrad: shard size, flat offset and row stride must be multiples of 4 (ld >= N)");
+    B200_CHECK(p.route_flat0 + (long long)(p.M - 1) * p.route_ld + p.N <= p.route_chunk * (long long)p.route_world,
+               "routed wgrad: the weight lies outside the sharded flat space");
+    for (int r = 0; r < p.route_world; ++r)
+      B200_CHECK(p.route_base[r] != 0 && p.route_base[r] % 16 == 0, "routed wgrad: shard bases must be 16-byte aligned");
   }
   if (p.splits <= 0) p.splits = 1;
   B200_CHECK(bn == 128 || bn == 192 || bn == 256, "BN must be 128, 192 or 256");
@@ -822,6 +864,7 @@ void gemm_launch(const GemmOperands& op, GemmParams p, int epi, bool a_mn, bool 
   } else if (a_mn && b_mn) {
     switch (epi) {
       case EPI_ACC_F32: return dispatch_bn<true, true, EPI_ACC_F32>(bn, cg, op, p, stream);
+      case EPI_ACC_F32_ROUTED: return dispatch_bn<true, true, EPI_ACC_F32_ROUTED>(bn, cg, op, p, stream);
       case EPI_STORE: return dispatch_bn<true, true, EPI_STORE>(bn, cg, op, p, stream);
     }
   }
