@@ -48,6 +48,8 @@ def parse_args(argv=None) -> argparse.Namespace:
     p.add_argument("--clocks-csv", type=str, default=None, help="keep the raw nvidia-smi clock samples here")
     p.add_argument("--fused-step", action="store_true",
                    help="ZeRO-1/2 unclipped step as one NVLink kernel (reduce-scatter + norm + AdamW + all-gather)")
+    p.add_argument("--routed-grads", action="store_true",
+                   help="ZeRO-2 without a full gradient buffer: gradients added into their owners' shards over NVLink")
     p.add_argument("--cuda-graph", action="store_true",
                    help="run stages 0-2 as one captured CUDA graph per step (TrainSession cuda_graph mode)")
     p.add_argument("--model-size", type=str, default="baseline-small",
@@ -244,6 +246,8 @@ def run_mine(args) -> None:
         print(f"[bench] note: --gpus {args.gpus} but WORLD_SIZE={world}; using {world}", file=sys.stderr)
     if args.fused_step:
         os.environ["ZB_FUSED_STEP"] = "1"
+    if args.routed_grads:
+        os.environ["ZB_ROUTED_GRADS"] = "1"
     impl = args.collective_impl
     if impl == "auto":
         impl = "nvls" if world > 1 else "torch"
@@ -341,6 +345,7 @@ def run_mine(args) -> None:
                    "zero_stage": args.headline_stage, "collective_impl": impl,
                    "cuda_graph": bool(args.cuda_graph and args.headline_stage != 3),
                    "fused_step": bool(args.fused_step),
+                   "routed_grads": bool(args.routed_grads),
                    "l2": "no flush: each step touches >2 GB (activations, 1.2 GB fp32 optimizer state) vs 126 MB L2"},
         "per_stage": per_stage,
         "roofline": {"executed_tflops_per_gpu": head["executed_tflops_per_gpu"],

@@ -188,6 +188,20 @@ void linear_wgrad_routed(Tensor dy, Tensor x, int64_t flat0, int64_t ld, int64_t
   b200::gemm_launch(op, p, b200::EPI_ACC_F32_ROUTED, true, true, (int)bn, cur_stream());
 }
 
+// Adds src (fp32, contiguous) into the owners' gradient shards: element k has flat index flat0 + k,
+// owned by rank (flat / chunk); bases[r] is rank r's shard as mapped on this GPU (see comm.h).
+void routed_add(Tensor src, int64_t flat0, int64_t chunk, std::vector<int64_t> bases) {
+  check_f32(src, "src");
+  TORCH_CHECK(src.is_contiguous(), "routed_add: contiguous source required");
+  TORCH_CHECK(!bases.empty() && (int)bases.size() <= b200::kCommMaxWorld, "routed_add: 1..8 shards");
+  b200::RouteTable t{};
+  t.world = (int)bases.size();
+  t.chunk = chunk;
+  for (size_t r = 0; r < bases.size(); ++r) t.base[r] = (uint64_t)bases[r];
+  c10::cuda::CUDAGuard g(src.device());
+  b200::comm_routed_add(src.data_ptr<float>(), (size_t)src.numel(), flat0, t, b200::device_errors_ptr(), cur_stream());
+}
+
 // dx = dy @ w and dw += dy^T @ x in one persistent launch (the two GEMMs of a linear layer's
 // backward pass share dy and are independent of each other).
 void linear_dgrad_wgrad(Tensor dy, Tensor w, Tensor x, Tensor dx, Tensor dw, int64_t splits) {
@@ -847,6 +861,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("linear_dgrad_wgrad", &linear_dgrad_wgrad, py::arg("dy"), py::arg("w"), py::arg("x"), py::arg("dx"),
         py::arg("dw"), py::arg("splits") = 0);
   m.def("swiglu_dgrad", &swiglu_dgrad);
+  m.def("routed_add", &routed_add, py::arg("src"), py::arg("flat0"), py::arg("chunk"), py::arg("bases"));
   m.def("linear_wgrad_routed", &linear_wgrad_routed, py::arg("dy"), py::arg("x"), py::arg("flat0"), py::arg("ld"),
         py::arg("chunk"), py::arg("bases"), py::arg("splits") = 0, py::arg("bn") = 0);
   m.def("linear_wgrad", &linear_wgrad, py::arg("dy"), py::arg("x"), py::arg("dw"), py::arg("splits") = 0,

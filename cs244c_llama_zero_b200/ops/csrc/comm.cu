@@ -454,6 +454,32 @@ __global__ void __launch_bounds__(kThreads) rs_adamw_allgather_kernel(CommCtx c,
   block_barrier(c, 2 * e + 1);
 }
 
+__global__ void routed_add_kernel(const float4* __restrict__ src, size_t n, long long flat0, RouteTable t,
+                                  DeviceErrors* errs) {
+  const size_t n4 = n / 4;
+  for (size_t i = gtid(); i < n4; i += gstride()) {
+    const long long f = flat0 + 4 * (long long)i;
+    const int owner = (int)(f / t.chunk);
+    if (owner >= t.world) {
+      report_error(errs, kErrBadIndex, 201);
+      continue;
+    }
+    const float4 v = src[i];
+    red_add_f32x4_sys(reinterpret_cast<float*>(t.base[owner]) + (f - (long long)owner * t.chunk),
+                      __float_as_uint(v.x), __float_as_uint(v.y), __float_as_uint(v.z), __float_as_uint(v.w));
+  }
+  const float* tail = reinterpret_cast<const float*>(src);
+  for (size_t k = n4 * 4 + gtid(); k < n; k += gstride()) {
+    const long long f = flat0 + (long long)k;
+    const int owner = (int)(f / t.chunk);
+    if (owner >= t.world) {
+      report_error(errs, kErrBadIndex, 202);
+      continue;
+    }
+    red_add_f32_sys(reinterpret_cast<float*>(t.base[owner]) + (f - (long long)owner * t.chunk), tail[k]);
+  }
+}
+
 __global__ void barrier_kernel(CommCtx c) {
   const uint32_t e = next_epoch(c);
   block_barrier(c, 2 * e);
@@ -663,6 +689,23 @@ void comm_rs_adamw_allgather(const CommCtx& c, const CommCtx& g, size_t g_off, s
   else
     rs_adamw_allgather_kernel<false><<<c.blocks, kThreads, 0, s>>>(c, g, g_off, param_off, chunk / 8, M, Mm, Vv,
                                                                    grad_scale, a, dev_sc, sq_out);
+  B200_CUDA_CHECK(cudaGetLastError());
+  count_launch();
+}
+
+void comm_routed_add(const float* src, size_t n, long long flat0, const RouteTable& t, DeviceErrors* errs,
+                     cudaStream_t s) {
+  B200_CHECK(t.world >= 1 && t.world <= kCommMaxWorld, "routed_add: 1..8 ranks");
+  B200_CHECK(t.chunk > 0 && t.chunk % 4 == 0 && flat0 % 4 == 0 && flat0 >= 0,
+             "routed_add: shard size and flat offset must be multiples of 4");
+  B200_CHECK((reinterpret_cast<uintptr_t>(src) & 15) == 0, "routed_add: source must be 16-byte aligned");
+  B200_CHECK(flat0 + (long long)n <= t.chunk * (long long)t.world, "routed_add: elements outside the sharded space");
+  for (int r = 0; r < t.world; ++r)
+    B200_CHECK(t.base[r] != 0 && t.base[r] % 16 == 0, "routed_add: shard bases must be 16-byte aligned");
+  if (n == 0) return;
+  const size_t work = std::max<size_t>(1, n / 4);
+  const int blocks = (int)std::min<size_t>((work + kThreads - 1) / kThreads, 4 * 148);
+  routed_add_kernel<<<blocks, kThreads, 0, s>>>(reinterpret_cast<const float4*>(src), n, flat0, t, errs);
   B200_CUDA_CHECK(cudaGetLastError());
   count_launch();
 }

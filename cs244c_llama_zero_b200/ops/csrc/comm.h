@@ -61,6 +61,17 @@ void comm_adamw_allgather(const CommCtx& c, size_t param_off_bytes, size_t chunk
 void comm_rs_adamw_allgather(const CommCtx& c, const CommCtx& g, size_t g_off, size_t param_off, size_t chunk,
                              float* master, float* m, float* v, float grad_scale, float lr, float beta1, float beta2,
                              float eps, float wd, int step, const float* dev_sc, float* sq_out, cudaStream_t s);
+// Routed gradient push (ZeRO-2 without a full gradient buffer): element k of src (fp32, n elements,
+// 16-byte aligned) has flat index flat0 + k; rank r = flat / chunk owns it and it is added at
+// bases[r] + (flat - r * chunk) with system-scope reductions (bases: every rank's fp32 gradient shard
+// as mapped on this GPU).  flat0 and chunk must be multiples of 4.
+struct RouteTable {
+  uint64_t base[kCommMaxWorld];
+  int world;
+  long long chunk;
+};
+void comm_routed_add(const float* src, size_t n, long long flat0, const RouteTable& t, DeviceErrors* errs,
+                     cudaStream_t s);
 // Standalone barrier among the ranks (every block of the communicator's grid).
 void comm_barrier(const CommCtx& c, cudaStream_t s);
 // A wait that nobody satisfies: used by tests to exercise the bounded-wait error path.

@@ -209,6 +209,10 @@ __device__ __forceinline__ void red_add_f32x4_sys(float* dst, uint32_t a, uint32
                : "memory");
 }
 
+__device__ __forceinline__ void red_add_f32_sys(float* dst, float a) {
+  asm volatile("red.relaxed.sys.global.add.f32 [%0], %1;" ::"l"(dst), "f"(a) : "memory");
+}
+
 __device__ __forceinline__ void prefetch_l2(const void* ptr) {
   asm volatile("prefetch.global.L2 [%0];" ::"l"(reinterpret_cast<uint64_t>(ptr)));
 }

@@ -59,13 +59,23 @@ def fused_weight(params: Sequence[torch.Tensor]) -> torch.Tensor:
 
 
 class _GradSink:
-    """fp32 accumulation target for the gradient of one (possibly fused) weight."""
+    """fp32 accumulation target for the gradient of one (possibly fused) weight.
+
+    Three modes: the engine's flat gradient buffer (``param.main_grad``, written in place); a ZeRO-2
+    gradient route (``param.grad_route = (route, flat offset)``: the kernels write a temporary fp32
+    buffer that ``finish`` adds straight into the owning ranks' gradient shards over NVLink); or a
+    temporary buffer handed back to autograd (plain model use)."""
 
     def __init__(self, params: Sequence[torch.nn.Parameter]) -> None:
         self.params = list(params)
         self.buffer: Optional[torch.Tensor] = None
+        self.routes = [getattr(p, "grad_route", None) for p in self.params]
+        if not all(r is not None for r in self.routes):
+            self.routes = None
         mains = [getattr(p, "main_grad", None) for p in self.params]
-        if all(m is not None for m in mains):
+        if self.routes is not None:
+            self.direct = False
+        elif all(m is not None for m in mains):
             self.buffer = fused_view(mains) if len(mains) > 1 else mains[0].view(self.params[0].shape)
             self.direct = self.buffer is not None
         else:
@@ -78,6 +88,13 @@ class _GradSink:
     def finish(self) -> List[Optional[torch.Tensor]]:
         """Per-parameter gradients to hand back to autograd (None when accumulated in place)."""
         if self.direct:
+            return [None] * len(self.params)
+        if self.routes is not None:  # into the owners' shards; nothing goes back to autograd
+            flat = self.buffer.reshape(-1)
+            start = 0
+            for p, (route, offset) in zip(self.params, self.routes):
+                route.push(flat[start : start + p.numel()], offset)
+                start += p.numel()
             return [None] * len(self.params)
         out: List[Optional[torch.Tensor]] = []
         row = 0

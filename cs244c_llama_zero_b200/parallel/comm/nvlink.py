@@ -292,6 +292,26 @@ class NvlinkCollectives(TorchCollectives):
         t.reshape(-1).copy_(buf[: t.numel()])
         return True
 
+    supports_routed_grads = True
+
+    def shard_bases(self, t: torch.Tensor) -> Optional[List[int]]:
+        """Every rank's address of symmetric tensor ``t`` (same offset in each rank's buffer), as mapped
+        on this GPU, or None when ``t`` is not in one of this object's symmetric buffers."""
+        hit = self._locate(t)
+        if hit is None:
+            return None
+        buf, off = hit
+        return [int(ptr) + off for ptr in buf.handle.buffer_ptrs]
+
+    def routed_push(self, src: torch.Tensor, flat0: int, chunk: int, bases: List[int]) -> None:
+        """Add fp32 ``src`` (flat indices ``flat0 ..``) into the owning ranks' shards (``bases``) over
+        NVLink; the owners see the sums after the next barrier."""
+        from ... import ops
+
+        if self._skipped("routed_push"):
+            return
+        ops.load_extension().routed_add(src, int(flat0), int(chunk), bases)
+
     supports_fused_step = True
 
     def reduce_scatter_adamw_allgather(self, params_flat: torch.Tensor, grads_flat: torch.Tensor, master: torch.Tensor,

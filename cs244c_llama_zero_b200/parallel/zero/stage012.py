@@ -40,6 +40,22 @@ from .common import (
 from .optim import adamw_update_, clip_coefficient, global_norm_from_local_sq, sum_of_squares
 
 
+class _ShardRoute:
+    """Where a weight gradient goes in routed stage 2: the fp32 shard of the rank owning each element
+    (flat index // chunk), addressed through the collectives' NVLink mappings."""
+
+    def __init__(self, collectives, chunk: int, bases: List[int]) -> None:
+        self.collectives = collectives
+        self.chunk = int(chunk)
+        self.bases = list(bases)
+
+    def push(self, src: torch.Tensor, flat0: int) -> None:
+        src = src.contiguous()
+        if src.data_ptr() % 16:
+            src = src.clone()
+        self.collectives.routed_push(src, flat0, self.chunk, self.bases)
+
+
 class _FlatEngine(ZeROEngineBase):
     """Common structure for the stages whose parameters are replicated between steps."""
 
@@ -49,7 +65,8 @@ class _FlatEngine(ZeROEngineBase):
         super().__init__(model, **kwargs)
         self.meta = build_flat_param_metadata(model)
         allocator = getattr(self.collectives, "alloc", None) if self.world_size > 1 and self.device.type == "cuda" else None
-        self.space = FlatParamSpace(self.meta, self.world_size, self.rank, with_grads=True, allocator=allocator)
+        self.space = FlatParamSpace(self.meta, self.world_size, self.rank, with_grads=self._full_grad_buffer(),
+                                    allocator=allocator)
         if self.shard_optimizer:
             master_src = self.space.shard(self.space.params)
         else:
@@ -57,6 +74,10 @@ class _FlatEngine(ZeROEngineBase):
         self._master = master_src.float().clone()
         self._exp_avg = torch.zeros_like(self._master)
         self._exp_avg_sq = torch.zeros_like(self._master)
+
+    def _full_grad_buffer(self) -> bool:
+        """Whether this engine keeps a full-size flat fp32 gradient buffer (``param.main_grad``)."""
+        return True
 
     # Names kept from the reference engines.
     @property
@@ -133,7 +154,8 @@ class _FlatEngine(ZeROEngineBase):
         the full vector).  Steps with clipping take the unfused path."""
         coll = self.collectives
         self._fused_step = bool(
-            os.environ.get("ZB_FUSED_STEP", "0") == "1" and self.world_size > 1 and self.device.type == "cuda"
+            os.environ.get("ZB_FUSED_STEP", "0") == "1" and self.space.grads is not None
+            and self.world_size > 1 and self.device.type == "cuda"
             and not getattr(self, "_overlap", False) and getattr(coll, "supports_fused_step", False)
             and coll.locate_symmetric(self.space.params) is not None
             and coll.locate_symmetric(self.space.grads) is not None
@@ -315,6 +337,10 @@ class ZeROStage2Optimizer(_ShardedStateMixin, _FlatEngine):
         super().__init__(model, **kwargs)
         # Accepted for CLI compatibility: buckets are transformer blocks (see _setup_overlap).
         self.grad_bucket_numel = grad_bucket_numel
+        self._routed = self.space.grads is None
+        if self._routed:
+            self._setup_routed()
+            return
         # On one rank the reduce-scatter is the identity, so the gradient shard IS the flat gradient
         # buffer: no copy of the gradients after backward, nothing extra to zero per step (stage 0's
         # memory traffic).  Several micro-batches accumulate in place, which gives the same sum.
@@ -326,6 +352,62 @@ class ZeROStage2Optimizer(_ShardedStateMixin, _FlatEngine):
         self._pending_flush = False
         self._setup_overlap()
         self._setup_fused_step()
+
+    # -- gradients routed to their owners (no full gradient buffer) --------------------------------
+    def _full_grad_buffer(self) -> bool:
+        return not self._routed_requested()
+
+    def _routed_requested(self) -> bool:
+        return bool(os.environ.get("ZB_ROUTED_GRADS", "0") == "1" and self.world_size > 1
+                    and self.device.type == "cuda" and getattr(self.collectives, "supports_routed_grads", False))
+
+    def _setup_routed(self) -> None:
+        """``ZB_ROUTED_GRADS=1`` (NVLink collectives): no rank keeps a full gradient buffer.  The
+        gradient shard of every rank is a symmetric fp32 buffer of ``chunk`` elements; every weight
+        gradient, as its kernel finishes it, is added straight into the owning ranks' shards over
+        NVLink (``param.grad_route``: the B200 kernels write a temporary buffer that the sink pushes
+        with system-scope vector reductions), so no reduce-scatter runs after backward and gradient
+        memory is the shard only (4 B/param / W instead of 4 B/param).  A barrier at ``zero_grad``
+        (every shard cleared before anyone adds) and one before the update (every addition landed)
+        order the pushes."""
+        coll = self.collectives
+        self.grad_shard = coll.alloc(self.space.chunk, torch.float32)  # rank r's buffer is shard r
+        bases = coll.shard_bases(self.grad_shard)
+        if bases is None:
+            raise RuntimeError("routed gradients need the shard in a symmetric buffer of the collectives")
+        route = _ShardRoute(coll, self.space.chunk, bases)
+        for p, off in zip(self.meta.params, self.space.offsets):
+            p.grad_route = (route, int(off))
+        self._route = route
+        self._shard_is_buffer = False
+        self._pending_flush = False
+        self._overlap = False
+        self._fused_step = False
+        self._fused_sq = None
+
+    def _push_autograd_grads(self) -> None:
+        """Gradients that reached ``param.grad`` through autograd (modules outside the B200 kernels)."""
+        for p, off in zip(self.meta.params, self.space.offsets):
+            if p.grad is not None:
+                self._route.push(p.grad.detach().to(torch.float32).reshape(-1), int(off))
+                p.grad = None
+
+    def _routed_update(self, max_grad_norm: float) -> torch.Tensor:
+        self._push_autograd_grads()
+        self._record_memory_event("measured_step_stage2_pre_reduce_scatter")
+        with self.clock.measure("backward_reduce_scatter", 0):
+            self.collectives.barrier()  # every rank's additions have landed in the owners' shards
+        self._record_memory_event("measured_step_stage2_post_reduce_scatter")
+        inv_w = 1.0 / self.world_size
+        # the shard holds the sum over ranks: the averaged gradient's norm is 1/W of its norm
+        norm = global_norm_from_local_sq(sum_of_squares(self.grad_shard), sharded=True) * inv_w
+        self.step_count += 1
+        self._record_memory_event("measured_step_stage2_pre_allgather")
+        with self.collectives.label_scope("stage2.step.allgather.updated_param_shard"):
+            self._adamw_and_gather(self.grad_shard, clip_coefficient(norm, max_grad_norm) * inv_w)
+        self._record_memory_event("measured_step_stage2_post_allgather")
+        self._record_memory_event("measured_step_stage2_post_step_free_grad_shard")
+        return norm
 
     # -- reduce-scatter overlapped with backward -------------------------------------------
     def _setup_overlap(self) -> None:
@@ -405,6 +487,14 @@ class ZeROStage2Optimizer(_ShardedStateMixin, _FlatEngine):
         return self.space.grads
 
     def zero_grad(self) -> None:
+        if self._routed:
+            self.clock.reset()
+            for p in self.meta.params:
+                p.grad = None
+            self.grad_shard.zero_()
+            self.collectives.barrier()  # no rank adds into a shard before its owner has cleared it
+            self._pending_flush = True
+            return
         super().zero_grad()
         if not self._shard_is_buffer:
             self.grad_shard.zero_()
@@ -420,7 +510,7 @@ class ZeROStage2Optimizer(_ShardedStateMixin, _FlatEngine):
             if self._overlap:
                 self._overlap_active = False
         self._pending_flush = True
-        if not self._fused_step:  # the fused step reduces once, inside the optimizer kernel
+        if not (self._fused_step or self._routed):  # those reduce inside the step / while backward runs
             self._flush_flat_grad_buffer()
 
     def _flush_overlapped(self) -> None:
@@ -468,6 +558,8 @@ class ZeROStage2Optimizer(_ShardedStateMixin, _FlatEngine):
         self._pending_flush = False
 
     def _update(self, max_grad_norm: float) -> torch.Tensor:
+        if self._routed:
+            return self._routed_update(max_grad_norm)
         if any(p.grad is not None for p in self.meta.params) and not hasattr(self.meta.params[0], "main_grad"):
             raise RuntimeError("Stage 2 expects gradients in the flat buffer")
         if self._fused_step and max_grad_norm <= 0 and self._pending_flush:
@@ -505,7 +597,8 @@ class ZeROStage2Optimizer(_ShardedStateMixin, _FlatEngine):
             "logical_grads_mb": bytes_to_mb(self._logical_grad_bytes()),
             "logical_optimizer_mb": bytes_to_mb(tensors_num_bytes([self._master, self._exp_avg, self._exp_avg_sq])),
             "live_full_grads_mb": 0.0,
-            "live_flat_grad_buffer_mb": bytes_to_mb(tensor_num_bytes(self.space.grads)),
+            "live_flat_grad_buffer_mb": bytes_to_mb(tensor_num_bytes(self.space.grads)) if self.space.grads is not None
+            else 0.0,
             "live_grad_shard_mb": bytes_to_mb(tensor_num_bytes(self.grad_shard)),
             "comm_temp_mb": 0.0,
         }
@@ -516,7 +609,8 @@ class ZeROStage2Optimizer(_ShardedStateMixin, _FlatEngine):
     def live_model_state_breakdown_mb(self) -> Dict[str, float]:
         base = self.memory_state_breakdown_mb()
         shard_bytes = 0 if self._shard_is_buffer else tensor_num_bytes(self.grad_shard)  # a view of the buffer
-        grads_mb = bytes_to_mb(tensor_num_bytes(self.space.grads) + shard_bytes)
+        flat_bytes = tensor_num_bytes(self.space.grads) if self.space.grads is not None else 0
+        grads_mb = bytes_to_mb(flat_bytes + shard_bytes)
         base["total_mb"] += grads_mb - base["grads_mb"]
         base["grads_mb"] = grads_mb
         return base

@@ -377,3 +377,86 @@ def test_stage2_on_one_rank_matches_stage0_with_grad_accum() -> None:
             assert engine.grad_shard.data_ptr() == engine.space.grads.data_ptr()
     _assert_close(runs[0][0], runs[1][0], "stage 2 vs stage 0 on one rank")
     torch.testing.assert_close(torch.tensor(runs[1][1]), torch.tensor(runs[0][1]))
+
+
+class _RoutedGradCollectives(TorchCollectives):
+    """Gloo stand-in for routed stage 2: a rank cannot add into another process's memory here, so
+    pushes land in a local full-size outbox and the barrier reduce-scatters it into the owners' shards
+    (what the NVLink pushes + barrier produce on GPUs)."""
+
+    supports_routed_grads = True
+
+    def __init__(self):
+        self.outbox = None
+        self.shard = None
+        self.pushes = 0
+
+    def alloc(self, numel, dtype):
+        self.shard = torch.zeros(numel, dtype=dtype)
+        return self.shard
+
+    def shard_bases(self, t):
+        return [1000 + r for r in range(dist.get_world_size())]
+
+    def routed_push(self, src, flat0, chunk, bases):
+        world = len(bases)
+        if self.outbox is None:
+            self.outbox = torch.zeros(chunk * world)
+        self.outbox[flat0:flat0 + src.numel()] += src
+        self.pushes += 1
+
+    def barrier(self):
+        if self.outbox is not None:
+            part = torch.zeros_like(self.shard)
+            self.reduce_scatter_into(part, self.outbox)
+            self.shard += part
+            self.outbox.zero_()
+        dist.barrier()
+
+
+def _routed_worker(rank: int, world: int, port: int, max_grad_norm: float, grad_accum: int) -> None:
+    init_gloo(rank, world, port)
+    try:
+        cfg = _cfg()
+        torch.manual_seed(1234)
+        model = LlamaForCausalLM(cfg)
+        for p in model.parameters():
+            dist.broadcast(p.data, src=0)
+        ref = LlamaForCausalLM(cfg)
+        ref.load_state_dict(model.state_dict())
+        hp = dict(lr=1e-3, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.05)
+        coll = _RoutedGradCollectives()
+        ZeROStage2Optimizer._routed_requested = lambda self: True  # what NVLink collectives enable on GPUs
+        engine = ZeROStage2Optimizer(model=model, collectives=coll, **hp)
+        assert engine._routed and engine.space.grads is None and engine.grad_shard is coll.shard
+        opt = torch.optim.AdamW(ref.parameters(), **hp)
+        for step in range(3):
+            micro = [_local_batch(step * 10 + m, rank, 3, cfg.max_seq_len, cfg.vocab_size) for m in range(grad_accum)]
+            engine.zero_grad()
+            engine.prepare_forward()
+            for ids in micro:
+                engine.backward(model(input_ids=ids, labels=ids).loss / grad_accum)
+            norm = engine.step(max_grad_norm=max_grad_norm)
+            opt.zero_grad(set_to_none=True)
+            for ids in micro:
+                parts = [torch.empty_like(ids) for _ in range(world)]
+                dist.all_gather(parts, ids)
+                g = torch.cat(parts)
+                (ref(input_ids=g, labels=g).loss / grad_accum).backward()
+            want = torch.sqrt(sum(p.grad.float().pow(2).sum() for p in ref.parameters()))
+            if max_grad_norm > 0:
+                torch.nn.utils.clip_grad_norm_(ref.parameters(), max_norm=max_grad_norm)
+            opt.step()
+            _assert_close(model, ref, f"routed step={step} rank={rank}")
+            torch.testing.assert_close(torch.tensor(norm), want, rtol=1e-4, atol=1e-6)
+        assert coll.pushes > 0 and engine.step_count == 3
+        live = engine.live_model_state_breakdown_mb()
+        assert live["grads_mb"] == pytest.approx(engine.space.chunk * 4 / 2 ** 20)  # the shard only
+    finally:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("max_grad_norm,grad_accum", [(0.0, 1), (0.5, 2)])
+def test_routed_stage2_matches_reference(max_grad_norm: float, grad_accum: int) -> None:
+    _spawn(_routed_worker, 2, max_grad_norm, grad_accum)

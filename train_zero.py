@@ -115,6 +115,9 @@ def parse_args(argv=None) -> argparse.Namespace:
     p.add_argument("--memory-warmup-steps", type=int, default=0)
     p.add_argument("--tflops-mode", type=str, default="estimate", choices=["estimate", "profile", "off"])
     p.add_argument("--nvtx", action="store_true", help="name the step phases with NVTX ranges (Nsight timelines)")
+    p.add_argument("--routed-grads", action="store_true",
+                   help="stage 2 with --collective-impl nvls|p2p: no full gradient buffer; gradients are added into "
+                        "their owners' shards over NVLink during backward")
     p.add_argument("--fused-step", action="store_true",
                    help="stages 1/2 with --collective-impl nvls|p2p and no clipping: the step as one NVLink kernel "
                         "(reduce-scatter + norm + AdamW + all-gather)")
@@ -236,6 +239,8 @@ def train(args: argparse.Namespace) -> None:
         nvtx.enable(True)
     if getattr(args, "fused_step", False):
         os.environ["ZB_FUSED_STEP"] = "1"  # read by the stage 1/2 engines when they are built
+    if getattr(args, "routed_grads", False):
+        os.environ["ZB_ROUTED_GRADS"] = "1"
     configure_runtime(device)
     set_seed(args.seed)
     log_event(rank, f"initialized distributed world_size={world_size} device={device} pid={os.getpid()}", force=verbose)
