@@ -68,7 +68,7 @@ class _GradSink:
 
     def __init__(self, params: Sequence[torch.nn.Parameter]) -> None:
         self.params = list(params)
-        self.buffer: Optional[torch.Tensor] = None
+        self._buffer: Optional[torch.Tensor] = None
         self.routes = [getattr(p, "grad_route", None) for p in self.params]
         if not all(r is not None for r in self.routes):
             self.routes = None
@@ -76,21 +76,37 @@ class _GradSink:
         if self.routes is not None:
             self.direct = False
         elif all(m is not None for m in mains):
-            self.buffer = fused_view(mains) if len(mains) > 1 else mains[0].view(self.params[0].shape)
-            self.direct = self.buffer is not None
+            self._buffer = fused_view(mains) if len(mains) > 1 else mains[0].view(self.params[0].shape)
+            self.direct = self._buffer is not None
         else:
             self.direct = False
-        if self.buffer is None:
+
+    @property
+    def buffer(self) -> torch.Tensor:
+        """The fp32 target the kernels accumulate into (a zeroed temporary unless written in place)."""
+        if self._buffer is None:
             rows = sum(p.shape[0] for p in self.params)
             shape = (rows,) + tuple(self.params[0].shape[1:])
-            self.buffer = torch.zeros(shape, dtype=torch.float32, device=self.params[0].device)
+            self._buffer = torch.zeros(shape, dtype=torch.float32, device=self.params[0].device)
+        return self._buffer
+
+    def wgrad_routed(self, dy: torch.Tensor, x: torch.Tensor) -> bool:
+        """Routed mode, one 2-D weight: ``dw = dy^T x`` straight into the owners' shards by the
+        weight-gradient GEMM's own epilogue (no temporary, no push).  False if not applicable."""
+        if self.routes is None or len(self.params) != 1 or self.params[0].dim() != 2 or self._buffer is not None:
+            return False
+        route, offset = self.routes[0]
+        _ext().linear_wgrad_routed(dy, x, offset, self.params[0].shape[1], route.chunk, route.bases)
+        return True
 
     def finish(self) -> List[Optional[torch.Tensor]]:
         """Per-parameter gradients to hand back to autograd (None when accumulated in place)."""
         if self.direct:
             return [None] * len(self.params)
         if self.routes is not None:  # into the owners' shards; nothing goes back to autograd
-            flat = self.buffer.reshape(-1)
+            if self._buffer is None:  # written by a routed kernel already
+                return [None] * len(self.params)
+            flat = self._buffer.reshape(-1)
             start = 0
             for p, (route, offset) in zip(self.params, self.routes):
                 route.push(flat[start : start + p.numel()], offset)
@@ -382,7 +398,10 @@ class _BlockFn(torch.autograd.Function):
         dgu = torch.empty_like(gu)
         C.swiglu_dgrad(dy3, wd.detach(), gu, dgu)
         sink_d = _GradSink([wd])
-        wgrad(dy3, act, sink_d.buffer)
+        if wgrad.side is None and sink_d.wgrad_routed(dy3, act):
+            pass  # the GEMM epilogue added it into the owners' shards (routed ZeRO-2)
+        else:
+            wgrad(dy3, act, sink_d.buffer)
         dh2 = torch.empty_like(xf)
         sink_gu = _GradSink([wg, wu])
         _dgrad_and_wgrad(dgu, w_gu, h2, dh2, sink_gu.buffer, wgrad)
