@@ -35,7 +35,8 @@ from pathlib import Path
 from typing import Callable, Dict, List, Optional, Sequence
 
 PROJECT_ROOT = Path(__file__).resolve().parents[2]
-EXCLUDED_PREFIXES = ("experiments/results/", "gpurun_out/", "_work/", "build/", "baseline/_ref/")
+# git-ignored paths (scratch folders among them) are already left out by --exclude-standard
+EXCLUDED_PREFIXES = ("experiments/results/", "build/", "baseline/_ref/")
 EXCLUDED_SUFFIXES = (".so", ".o", ".pyc", ".ncu-rep")
 PLOT_FILES = {"throughput": "throughput.svg", "comm": "comm.svg", "tflops": "tflops.svg",
               "stage-throughput": "stage_throughput.svg", "stage-comm": "stage_comm.svg", "loss": "loss.svg",

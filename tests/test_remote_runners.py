@@ -41,7 +41,10 @@ def _session(runner):
 def test_bundle_excludes_results_and_builds():
     paths = remote.bundle_paths(remote.PROJECT_ROOT)
     assert "bench.py" in paths and "setup.py" in paths
-    assert not any(p.endswith(".so") or p.startswith(("gpurun_out/", "_work/")) for p in paths)
+    assert not any(p.endswith(".so") or p.startswith(("build/", "baseline/_ref/")) for p in paths)
+    ignored = remote.subprocess.run(["git", "check-ignore", "--stdin"], input="\n".join(paths), text=True,
+                                    capture_output=True, cwd=remote.PROJECT_ROOT).stdout.split()
+    assert ignored == []  # nothing git ignores (scratch folders, results) goes into the bundle
 
 
 def test_remote_bandwidth_sweep_dry_run_roundtrip(tmp_path):
