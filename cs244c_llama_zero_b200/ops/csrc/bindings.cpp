@@ -228,6 +228,34 @@ void linear_dgrad_wgrad(Tensor dy, Tensor w, Tensor x, Tensor dx, Tensor dw, int
   b200::gemm_launch_dgrad_wgrad(op0, p0, op1, p1, cur_stream());
 }
 
+// The grouped launch with its weight gradient routed to the owners' shards (see linear_wgrad_routed):
+// dx = dy @ w, and dw = dy^T @ x added into the shards, element (o, i) at flat index flat0 + o * ld + i.
+void linear_dgrad_wgrad_routed(Tensor dy, Tensor w, Tensor x, Tensor dx, int64_t flat0, int64_t ld, int64_t chunk,
+                               std::vector<int64_t> bases, int64_t splits) {
+  check_bf16_2d(dy, "dy");
+  check_bf16_2d(w, "w");
+  check_bf16_2d(x, "x");
+  check_bf16_2d(dx, "dx");
+  const int T = dy.size(0), out = dy.size(1), in = w.size(1);
+  TORCH_CHECK(w.size(0) == out && dx.size(0) == T && dx.size(1) == in, "linear_dgrad_wgrad_routed: dgrad shapes");
+  TORCH_CHECK(x.size(0) == T && x.size(1) == in, "linear_dgrad_wgrad_routed: x shape");
+  TORCH_CHECK(!bases.empty() && (int)bases.size() <= b200::kRouteMaxWorld, "linear_dgrad_wgrad_routed: 1..8 shards");
+  c10::cuda::CUDAGuard g(dy.device());
+  auto p0 = base_params(T, in, out);
+  p0.C = reinterpret_cast<__nv_bfloat16*>(dx.data_ptr());
+  p0.ldc = dx.stride(0);
+  b200::GemmOperands op0{dy.data_ptr(), w.data_ptr(), (uint64_t)dy.stride(0), (uint64_t)w.stride(0)};
+  auto p1 = base_params(out, in, T);
+  p1.splits = splits > 0 ? (int)splits : 0;
+  p1.route_world = (int)bases.size();
+  for (size_t r = 0; r < bases.size(); ++r) p1.route_base[r] = (uint64_t)bases[r];
+  p1.route_ld = (int)ld;
+  p1.route_chunk = chunk;
+  p1.route_flat0 = flat0;
+  b200::GemmOperands op1{dy.data_ptr(), x.data_ptr(), (uint64_t)dy.stride(0), (uint64_t)x.stride(0)};
+  b200::gemm_launch_dgrad_wgrad(op0, p0, op1, p1, cur_stream());
+}
+
 // Host-only views of the GEMM schedulers (no GPU needed), for tests and tooling.
 // (bn, splits, cg) that the automatic tile choice picks for one GEMM on `sms` SMs.
 std::vector<int64_t> gemm_tile_choice(int64_t M, int64_t N, int64_t K, int64_t epi, int64_t head_dim, bool allow_split,
@@ -861,6 +889,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("linear_dgrad_wgrad", &linear_dgrad_wgrad, py::arg("dy"), py::arg("w"), py::arg("x"), py::arg("dx"),
         py::arg("dw"), py::arg("splits") = 0);
   m.def("swiglu_dgrad", &swiglu_dgrad);
+  m.def("linear_dgrad_wgrad_routed", &linear_dgrad_wgrad_routed, py::arg("dy"), py::arg("w"), py::arg("x"),
+        py::arg("dx"), py::arg("flat0"), py::arg("ld"), py::arg("chunk"), py::arg("bases"), py::arg("splits") = 0);
   m.def("routed_add", &routed_add, py::arg("src"), py::arg("flat0"), py::arg("chunk"), py::arg("bases"));
   m.def("linear_wgrad_routed", &linear_wgrad_routed, py::arg("dy"), py::arg("x"), py::arg("flat0"), py::arg("ld"),
         py::arg("chunk"), py::arg("bases"), py::arg("splits") = 0, py::arg("bn") = 0);

@@ -153,8 +153,9 @@ __device__ __forceinline__ Unit decode_unit(int u, const GemmParams& p, const Ge
 }
 
 // GROUPED: problem 0 is described by the template (A_MN, EPI = EPI_STORE, maps tmA/tmB/tmC, params
-// p) and problem 1 is a weight gradient (MN-major A, EPI_ACC_F32, maps tmX/tmY/tmZ, params p1).
-template <int BN, bool A_MN, bool B_MN, int EPI, int CG, bool GROUPED = false>
+// p) and problem 1 is a weight gradient (MN-major A, EPI_ACC_F32, maps tmX/tmY/tmZ, params p1); with
+// ROUTE1 problem 1's partial sums go to their owners' shards instead (EPI_ACC_F32_ROUTED, p1.route_*).
+template <int BN, bool A_MN, bool B_MN, int EPI, int CG, bool GROUPED = false, bool ROUTE1 = false>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                 const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmX,
@@ -165,6 +166,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   constexpr uint32_t IDESC = idesc_bf16_f32(BM * CG, BN, A_MN, B_MN);
   constexpr uint32_t IDESC_AMN = idesc_bf16_f32(BM * CG, BN, true, B_MN);  // grouped problem 1
   static_assert(!GROUPED || (EPI == EPI_STORE && !A_MN && B_MN), "grouped launches pair a dgrad with a wgrad");
+  static_assert(!ROUTE1 || GROUPED, "ROUTE1 applies to the grouped launch's weight gradient");
   static_assert(CG == 1 || CG == 2, "CTA group of 1 or 2");
   static_assert(CG == 1 || !B_MN || (BN / 2) % 64 == 0, "pair tiles with an MN-major B need BN/2 % 64 == 0");
 
@@ -428,8 +430,38 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           publish_chunk(map, buf, n0 + c, row0, true);
         }
       };
+      // Each 16-byte group of this row's partial sums goes to the rank owning it: the reduction across
+      // ranks happens in the owners' memory as the tiles finish, so no reduce-scatter runs after
+      // backward.  Groups never straddle owners (flat0, ld, chunk and the column are multiples of 4).
+      auto routed_f32_epilogue = [&](const GemmParams& q) {
+        const int n0 = tn * BN + wg * (BN / 2);
+#pragma unroll 1
+        for (int c = 0; c < BN / 2; c += 16) {
+          uint32_t r[16];
+          tmem_ld_32x32b_x16(tbase + wg * (BN / 2) + c, r);
+          tc_wait_ld();
+          if (m < q.M) {
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const int col = n0 + c + 4 * j;
+              if (col >= q.N) continue;
+              const long long f = q.route_flat0 + (long long)m * q.route_ld + col;
+              const int owner = (int)(f / q.route_chunk);
+              if (owner < 0 || owner >= q.route_world) {
+                report_error(q.errs, kErrBadIndex, 200);
+                continue;
+              }
+              float* dst = reinterpret_cast<float*>(q.route_base[owner]) + (f - (long long)owner * q.route_chunk);
+              red_add_f32x4_sys(dst, r[4 * j], r[4 * j + 1], r[4 * j + 2], r[4 * j + 3]);
+            }
+          }
+        }
+      };
       if (GROUPED && d.prob == 1) {
-        if constexpr (GROUPED) acc_f32_epilogue(&tmZ);
+        if constexpr (GROUPED && ROUTE1)
+          routed_f32_epilogue(p1);
+        else if constexpr (GROUPED)
+          acc_f32_epilogue(&tmZ);
       } else if constexpr (EPI == EPI_STORE || EPI == EPI_RESIDUAL) {
         const int n0 = tn * BN + wg * (BN / 2);
 #pragma unroll 1
@@ -479,32 +511,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       } else if constexpr (EPI == EPI_ACC_F32) {
         acc_f32_epilogue(&tmC);
       } else if constexpr (EPI == EPI_ACC_F32_ROUTED) {
-        // Each 16-byte group of this row's partial sums goes to the rank owning it: the reduction
-        // across ranks happens in the owners' memory as the tiles finish, so no reduce-scatter runs
-        // after backward.  Groups never straddle owners (flat0, ld, chunk and the column are
-        // multiples of 4).
-        const int n0 = tn * BN + wg * (BN / 2);
-#pragma unroll 1
-        for (int c = 0; c < BN / 2; c += 16) {
-          uint32_t r[16];
-          tmem_ld_32x32b_x16(tbase + wg * (BN / 2) + c, r);
-          tc_wait_ld();
-          if (m < p.M) {
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              const int col = n0 + c + 4 * j;
-              if (col >= p.N) continue;
-              const long long f = p.route_flat0 + (long long)m * p.route_ld + col;
-              const int owner = (int)(f / p.route_chunk);
-              if (owner < 0 || owner >= p.route_world) {
-                report_error(p.errs, kErrBadIndex, 200);
-                continue;
-              }
-              float* dst = reinterpret_cast<float*>(p.route_base[owner]) + (f - (long long)owner * p.route_chunk);
-              red_add_f32x4_sys(dst, r[4 * j], r[4 * j + 1], r[4 * j + 2], r[4 * j + 3]);
-            }
-          }
-        }
+        routed_f32_epilogue(p);
       } else if constexpr (EPI == EPI_ROPE) {
         const int n0 = tn * BN;
         const int half = p.head_dim >> 1;
@@ -812,6 +819,18 @@ GemmTile choose_gemm_tile(int M, int N, int K, int epi, int head_dim, bool allow
   return best;
 }
 
+// Host checks of a routed weight gradient's destination (see GemmParams::route_*).
+static void check_route(const GemmParams& p) {
+  B200_CHECK(p.route_world >= 1 && p.route_world <= kRouteMaxWorld, "routed wgrad: 1..8 ranks");
+  B200_CHECK(p.route_chunk > 0 && p.route_chunk % 4 == 0 && p.route_flat0 % 4 == 0 && p.route_ld % 4 == 0 &&
+                 p.route_ld >= p.N,
+             "routed wgrad: shard size, flat offset and row stride must be multiples of 4 (ld >= N)");
+  B200_CHECK(p.route_flat0 + (long long)(p.M - 1) * p.route_ld + p.N <= p.route_chunk * (long long)p.route_world,
+             "routed wgrad: the weight lies outside the sharded flat space");
+  for (int r = 0; r < p.route_world; ++r)
+    B200_CHECK(p.route_base[r] != 0 && p.route_base[r] % 16 == 0, "routed wgrad: shard bases must be 16-byte aligned");
+}
+
 void gemm_launch(const GemmOperands& op, GemmParams p, int epi, bool a_mn, bool b_mn, int bn, cudaStream_t stream) {
   int cg = 1;
   const bool acc = epi == EPI_ACC_F32 || epi == EPI_ACC_F32_ROUTED;  // fp32-accumulating: K-split allowed
@@ -831,16 +850,7 @@ void gemm_launch(const GemmOperands& op, GemmParams p, int epi, bool a_mn, bool 
     if (acc && p.splits <= 0)  // explicit tile, automatic K-split
       p.splits = choose_gemm_tile(p.M, p.N, p.K, model_epi, 64, true, b_mn, num_sms(), bn, cg).splits;
   }
-  if (epi == EPI_ACC_F32_ROUTED) {
-    B200_CHECK(p.route_world >= 1 && p.route_world <= kRouteMaxWorld, "routed wgrad: 1..8 ranks");
-    B200_CHECK(p.route_chunk > 0 && p.route_chunk % 4 == 0 && p.route_flat0 % 4 == 0 && p.route_ld % 4 == 0 &&
-                   p.route_ld >= p.N,
-               "routed wgrad: shard size, flat offset and row stride must be multiples of 4 (ld >= N)");
-    B200_CHECK(p.route_flat0 + (long long)(p.M - 1) * p.route_ld + p.N <= p.route_chunk * (long long)p.route_world,
-               "routed wgrad: the weight lies outside the sharded flat space");
-    for (int r = 0; r < p.route_world; ++r)
-      B200_CHECK(p.route_base[r] != 0 && p.route_base[r] % 16 == 0, "routed wgrad: shard bases must be 16-byte aligned");
-  }
+  if (epi == EPI_ACC_F32_ROUTED) check_route(p);
   if (p.splits <= 0) p.splits = 1;
   B200_CHECK(bn == 128 || bn == 192 || bn == 256, "BN must be 128, 192 or 256");
   B200_CHECK(epi_supports_bn(epi, bn), "this epilogue does not support BN = 192");
@@ -941,14 +951,17 @@ void gemm_launch_dgrad_wgrad(const GemmOperands& op0, GemmParams p0, const GemmO
   B200_CHECK(p0.N % 8 == 0 && p1.N % 8 == 0 && p0.K % 8 == 0 && p1.M % 8 == 0,
              "grouped dgrad/wgrad: N, K (dgrad) and M (wgrad) must be multiples of 8");
   const int G = std::max(1, num_sms() / CGG);
+  const bool routed = p1.route_world > 0;  // problem 1 to the owners' shards instead of p1.C32
+  if (routed) check_route(p1);
   plan_dgrad_wgrad(p0, p1, num_sms());
   p0.errs = p1.errs = device_errors_ptr();
 
-  auto kernel = gemm_kernel<BNG, false, true, EPI_STORE, CGG, true>;
-  static bool configured = false;
-  if (!configured) {
+  auto kernel = routed ? gemm_kernel<BNG, false, true, EPI_STORE, CGG, true, true>
+                       : gemm_kernel<BNG, false, true, EPI_STORE, CGG, true, false>;
+  static bool configured[2] = {false, false};
+  if (!configured[routed]) {
     B200_CUDA_CHECK(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_BYTES));
-    configured = true;
+    configured[routed] = true;
   }
   // problem 0: A = dY [M0, K0] K-major, B = W [K0, N0] MN-major, C = dX (bf16)
   const CUtensorMap tmA = make_tmap_bf16_2d(op0.A, (uint64_t)p0.K, (uint64_t)p0.M, op0.lda, 64, BM);
@@ -957,7 +970,7 @@ void gemm_launch_dgrad_wgrad(const GemmOperands& op0, GemmParams p0, const GemmO
   // problem 1: A = dY^T as [K1, M1] MN-major, B = X [K1, N1] MN-major, C = dW (fp32, accumulated)
   const CUtensorMap tmX = make_tmap_bf16_2d(op1.A, (uint64_t)p1.M, (uint64_t)p1.K, op1.lda, 64, 64);
   const CUtensorMap tmY = make_tmap_bf16_2d(op1.B, (uint64_t)p1.N, (uint64_t)p1.K, op1.ldb, 64, 64);
-  const CUtensorMap tmZ = epi_map_f32(p1.C32, p1.M, p1.N, p1.ldc32);
+  const CUtensorMap tmZ = routed ? tmX : epi_map_f32(p1.C32, p1.M, p1.N, p1.ldc32);  // unused when routed
   const int groups = std::max(1, std::min(p0.grp_units_total, G));
   launch_k(kernel, dim3(groups * CGG), dim3(NUM_THREADS), Cfg::SMEM_BYTES, stream, CGG, tmA, tmB, tmC, tmX, tmY, tmZ,
            p0, p1);

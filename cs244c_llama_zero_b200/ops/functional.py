@@ -90,6 +90,20 @@ class _GradSink:
             self._buffer = torch.zeros(shape, dtype=torch.float32, device=self.params[0].device)
         return self._buffer
 
+    def route_of_fused(self):
+        """(route, flat offset, row length) when the sink's weights are routed and lie back to back in the
+        flat space (a fused q|k|v or gate|up weight reads as one matrix there), else None."""
+        if self.routes is None or self._buffer is not None or any(p.dim() != 2 for p in self.params):
+            return None
+        route, first = self.routes[0]
+        cols = self.params[0].shape[1]
+        expected = first
+        for p, (r, off) in zip(self.params, self.routes):
+            if r is not route or off != expected or p.shape[1] != cols:
+                return None
+            expected += p.numel()
+        return route, first, cols
+
     def wgrad_routed(self, dy: torch.Tensor, x: torch.Tensor) -> bool:
         """Routed mode, one 2-D weight: ``dw = dy^T x`` straight into the owners' shards by the
         weight-gradient GEMM's own epilogue (no temporary, no push).  False if not applicable."""
@@ -312,6 +326,18 @@ def _grouped_backward_enabled() -> bool:
     return os.environ.get("ZB_GROUPED_BWD", "1") != "0"
 
 
+def _dgrad_and_wgrad_sink(dy: torch.Tensor, w: torch.Tensor, x: torch.Tensor, dx: torch.Tensor, sink: "_GradSink",
+                          wgrad: "_WgradLauncher") -> None:
+    """``_dgrad_and_wgrad`` into a gradient sink; a routed sink gets the weight gradient straight into
+    its owners' shards from the grouped launch's epilogue (no temporary buffer, no push)."""
+    fused = sink.route_of_fused() if wgrad.side is None and _grouped_backward_enabled() else None
+    if fused is not None:
+        route, flat0, cols = fused
+        _ext().linear_dgrad_wgrad_routed(dy, w, x, dx, flat0, cols, route.chunk, route.bases)
+        return
+    _dgrad_and_wgrad(dy, w, x, dx, sink.buffer, wgrad)
+
+
 def _dgrad_and_wgrad(dy: torch.Tensor, w: torch.Tensor, x: torch.Tensor, dx: torch.Tensor, dw: torch.Tensor,
                      wgrad: "_WgradLauncher") -> None:
     """dx = dy @ w and dw += dy^T @ x: one grouped persistent GEMM launch (both problems' tiles dealt
@@ -404,7 +430,7 @@ class _BlockFn(torch.autograd.Function):
             wgrad(dy3, act, sink_d.buffer)
         dh2 = torch.empty_like(xf)
         sink_gu = _GradSink([wg, wu])
-        _dgrad_and_wgrad(dgu, w_gu, h2, dh2, sink_gu.buffer, wgrad)
+        _dgrad_and_wgrad_sink(dgu, w_gu, h2, dh2, sink_gu, wgrad)
         del dgu
         dx2 = torch.empty_like(xf)
         sink_post = _GradSink([w_post])
@@ -412,12 +438,12 @@ class _BlockFn(torch.autograd.Function):
         # attention
         dattn = torch.empty_like(attn)
         sink_o = _GradSink([wo])
-        _dgrad_and_wgrad(dx2, wo.detach(), attn, dattn, sink_o.buffer, wgrad)
+        _dgrad_and_wgrad_sink(dx2, wo.detach(), attn, dattn, sink_o, wgrad)
         dqkv = torch.empty_like(qkv)
         attention_backward(qkv, attn, dattn, lse, B, S, H, KV, hd, dqkv, cos, sin)
         dh1 = torch.empty_like(xf)
         sink_qkv = _GradSink([wq, wk, wv])
-        _dgrad_and_wgrad(dqkv, w_qkv, h1, dh1, sink_qkv.buffer, wgrad)
+        _dgrad_and_wgrad_sink(dqkv, w_qkv, h1, dh1, sink_qkv, wgrad)
         dx = torch.empty_like(xf)
         sink_in = _GradSink([w_in])
         C.rmsnorm_bwd(dh1, xf, w_in.detach(), rstd1, dx2, dx, sink_in.buffer.view(-1))
@@ -477,7 +503,7 @@ class _LMHeadCEFn(torch.autograd.Function):
         w = ctx.weight
         dx = torch.empty_like(xf)
         sink = _GradSink([w])
-        _dgrad_and_wgrad(logits, w.detach(), xf, dx, sink.buffer, _WgradLauncher(xf.device))
+        _dgrad_and_wgrad_sink(logits, w.detach(), xf, dx, sink, _WgradLauncher(xf.device))
         if not sink.direct:
             join_weight_grads(xf.device)
         return dx.view(ctx.shape), sink.finish()[0], None

@@ -59,6 +59,25 @@ def test_routed_wgrad_lands_in_the_owners_shards(C, T, out, inp, world, splits, 
     torch.testing.assert_close(got, plain, rtol=1e-4, atol=1e-3)
 
 
+@pytest.mark.parametrize("T,out,inp,world", [(1024, 1280, 768, 4), (2048, 4096, 768, 2), (1000, 264, 392, 3)])
+def test_grouped_dgrad_with_routed_wgrad(C, T, out, inp, world):
+    dy, w, x = _bf(T, out, seed=5), _bf(out, inp, seed=6) * 0.05, _bf(T, inp, seed=7)
+    flat0 = 64
+    used = flat0 + out * inp
+    chunk = ((used + world - 1) // world + 3) // 4 * 4
+    shards = [torch.zeros(chunk, device="cuda") for _ in range(world)]
+    dx = torch.empty(T, inp, device="cuda", dtype=torch.bfloat16)
+    C.linear_dgrad_wgrad_routed(dy, w, x, dx, flat0, inp, chunk, [s.data_ptr() for s in shards])
+    dx_ref = torch.empty_like(dx)
+    dw_ref = torch.zeros(out, inp, device="cuda")
+    C.linear_dgrad_wgrad(dy, w, x, dx_ref, dw_ref)
+    torch.cuda.synchronize()
+    assert torch.equal(dx, dx_ref)  # the data-gradient problem is untouched by the routing
+    got = torch.cat(shards)[flat0:used].view(out, inp)
+    torch.testing.assert_close(got, dw_ref, rtol=1e-4, atol=1e-3)
+    assert torch.count_nonzero(torch.cat(shards)[:flat0]) == 0
+
+
 def test_routed_wgrad_rejects_a_weight_outside_the_shards(C):
     dy, x = _bf(256, 128, seed=3), _bf(256, 64, seed=4)
     shard = torch.zeros(1024, device="cuda")
