@@ -202,6 +202,24 @@ void routed_add(Tensor src, int64_t flat0, int64_t chunk, std::vector<int64_t> b
   b200::comm_routed_add(src.data_ptr<float>(), (size_t)src.numel(), flat0, t, b200::device_errors_ptr(), cur_stream());
 }
 
+// Embedding backward straight into the owners' shards (routed ZeRO-2): see comm.h.
+void embedding_bwd_routed(Tensor ids, Tensor dy, int64_t vocab, int64_t flat0, int64_t chunk,
+                          std::vector<int64_t> bases) {
+  check_cuda(ids, "ids");
+  check_bf16_2d(dy, "dy");
+  TORCH_CHECK(ids.scalar_type() == at::kLong && ids.is_contiguous() && ids.numel() == dy.size(0),
+              "embedding_bwd_routed: one int64 id per dy row");
+  TORCH_CHECK(dy.is_contiguous(), "embedding_bwd_routed: contiguous dy required");
+  TORCH_CHECK(!bases.empty() && (int)bases.size() <= b200::kCommMaxWorld, "embedding_bwd_routed: 1..8 shards");
+  b200::RouteTable t{};
+  t.world = (int)bases.size();
+  t.chunk = chunk;
+  for (size_t r = 0; r < bases.size(); ++r) t.base[r] = (uint64_t)bases[r];
+  c10::cuda::CUDAGuard g(dy.device());
+  b200::comm_embedding_bwd_routed(ids.data_ptr<int64_t>(), dy.data_ptr(), (int)dy.size(0), (int)dy.size(1), (int)vocab,
+                                  flat0, t, b200::device_errors_ptr(), cur_stream());
+}
+
 // dx = dy @ w and dw += dy^T @ x in one persistent launch (the two GEMMs of a linear layer's
 // backward pass share dy and are independent of each other).
 void linear_dgrad_wgrad(Tensor dy, Tensor w, Tensor x, Tensor dx, Tensor dw, int64_t splits) {
@@ -891,6 +909,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("swiglu_dgrad", &swiglu_dgrad);
   m.def("linear_dgrad_wgrad_routed", &linear_dgrad_wgrad_routed, py::arg("dy"), py::arg("w"), py::arg("x"),
         py::arg("dx"), py::arg("flat0"), py::arg("ld"), py::arg("chunk"), py::arg("bases"), py::arg("splits") = 0);
+  m.def("embedding_bwd_routed", &embedding_bwd_routed, py::arg("ids"), py::arg("dy"), py::arg("vocab"),
+        py::arg("flat0"), py::arg("chunk"), py::arg("bases"));
   m.def("routed_add", &routed_add, py::arg("src"), py::arg("flat0"), py::arg("chunk"), py::arg("bases"));
   m.def("linear_wgrad_routed", &linear_wgrad_routed, py::arg("dy"), py::arg("x"), py::arg("flat0"), py::arg("ld"),
         py::arg("chunk"), py::arg("bases"), py::arg("splits") = 0, py::arg("bn") = 0);

@@ -480,6 +480,31 @@ __global__ void routed_add_kernel(const float4* __restrict__ src, size_t n, long
   }
 }
 
+__global__ void embedding_bwd_routed_kernel(const int64_t* __restrict__ ids, const uint4* __restrict__ dy, int rows,
+                                            int d, int vocab, long long flat0, RouteTable t, DeviceErrors* errs) {
+  const int vec = d / 8;
+  const size_t total = (size_t)rows * vec;
+  for (size_t i = gtid(); i < total; i += gstride()) {
+    const int row = (int)(i / vec), v = (int)(i % vec);
+    const int64_t id = ids[row];
+    if (id < 0 || id >= vocab) continue;  // the forward pass recorded it already
+    float g[8];
+    bf16x8_to_f32(dy[i], g);
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const long long f = flat0 + (long long)id * d + v * 8 + 4 * h;
+      const int owner = (int)(f / t.chunk);
+      if (owner >= t.world) {
+        report_error(errs, kErrBadIndex, 203);
+        continue;
+      }
+      red_add_f32x4_sys(reinterpret_cast<float*>(t.base[owner]) + (f - (long long)owner * t.chunk),
+                        __float_as_uint(g[4 * h]), __float_as_uint(g[4 * h + 1]), __float_as_uint(g[4 * h + 2]),
+                        __float_as_uint(g[4 * h + 3]));
+    }
+  }
+}
+
 __global__ void barrier_kernel(CommCtx c) {
   const uint32_t e = next_epoch(c);
   block_barrier(c, 2 * e);
@@ -706,6 +731,25 @@ void comm_routed_add(const float* src, size_t n, long long flat0, const RouteTab
   const size_t work = std::max<size_t>(1, n / 4);
   const int blocks = (int)std::min<size_t>((work + kThreads - 1) / kThreads, 4 * 148);
   routed_add_kernel<<<blocks, kThreads, 0, s>>>(reinterpret_cast<const float4*>(src), n, flat0, t, errs);
+  B200_CUDA_CHECK(cudaGetLastError());
+  count_launch();
+}
+
+void comm_embedding_bwd_routed(const int64_t* ids, const void* dy, int rows, int d, int vocab, long long flat0,
+                               const RouteTable& t, DeviceErrors* errs, cudaStream_t s) {
+  B200_CHECK(t.world >= 1 && t.world <= kCommMaxWorld, "embedding_bwd_routed: 1..8 ranks");
+  B200_CHECK(d % 8 == 0 && flat0 % 4 == 0 && t.chunk > 0 && t.chunk % 4 == 0,
+             "embedding_bwd_routed: d must be a multiple of 8, flat offset and shard size of 4");
+  B200_CHECK(flat0 + (long long)vocab * d <= t.chunk * (long long)t.world,
+             "embedding_bwd_routed: the table lies outside the sharded flat space");
+  B200_CHECK((reinterpret_cast<uintptr_t>(dy) & 15) == 0, "embedding_bwd_routed: dy must be 16-byte aligned");
+  for (int r = 0; r < t.world; ++r)
+    B200_CHECK(t.base[r] != 0 && t.base[r] % 16 == 0, "embedding_bwd_routed: shard bases must be 16-byte aligned");
+  const size_t total = (size_t)rows * (d / 8);
+  if (total == 0) return;
+  const int blocks = (int)std::min<size_t>((total + kThreads - 1) / kThreads, 4 * 148);
+  embedding_bwd_routed_kernel<<<blocks, kThreads, 0, s>>>(ids, reinterpret_cast<const uint4*>(dy), rows, d, vocab,
+                                                          flat0, t, errs);
   B200_CUDA_CHECK(cudaGetLastError());
   count_launch();
 }

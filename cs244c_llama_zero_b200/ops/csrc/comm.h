@@ -72,6 +72,11 @@ struct RouteTable {
 };
 void comm_routed_add(const float* src, size_t n, long long flat0, const RouteTable& t, DeviceErrors* errs,
                      cudaStream_t s);
+// Embedding backward into the owners' shards: row r of dy (bf16 [rows, d], contiguous) is added at
+// table row ids[r] of the weight whose element (i, k) has flat index flat0 + i * d + k (ids outside
+// [0, vocab) are skipped).  d must be a multiple of 8, flat0 of 4.
+void comm_embedding_bwd_routed(const int64_t* ids, const void* dy, int rows, int d, int vocab, long long flat0,
+                               const RouteTable& t, DeviceErrors* errs, cudaStream_t s);
 // Standalone barrier among the ranks (every block of the communicator's grid).
 void comm_barrier(const CommCtx& c, cudaStream_t s);
 // A wait that nobody satisfies: used by tests to exercise the bounded-wait error path.

@@ -199,7 +199,13 @@ class _EmbeddingFn(torch.autograd.Function):
     def backward(ctx, dy: torch.Tensor):
         (flat,) = ctx.saved_tensors
         sink = _GradSink([ctx.weight])
-        _ext().embedding_bwd(flat, dy.reshape(flat.numel(), -1).contiguous(), sink.buffer)
+        dy2 = dy.reshape(flat.numel(), -1).contiguous()
+        fused = sink.route_of_fused()
+        if fused is not None:  # routed ZeRO-2: rows added straight into the owners' shards
+            route, flat0, cols = fused
+            _ext().embedding_bwd_routed(flat, dy2, ctx.weight.shape[0], flat0, route.chunk, route.bases)
+        else:
+            _ext().embedding_bwd(flat, dy2, sink.buffer)
         return None, sink.finish()[0]
 
 

@@ -2,6 +2,7 @@
 
 * ``linear_wgrad_routed``: the weight-gradient GEMM with the reduce-scatter fused into its epilogue;
 * ``routed_add``: the push of a finished gradient buffer into the owners' shards;
+* ``embedding_bwd_routed``: the embedding backward adding its rows straight into the owners' shards;
 * the B200 model's gradient sinks in routed mode against the engine's flat gradient buffer;
 * on two GPUs, the routed stage-2 engine against the NCCL engine.
 
@@ -97,6 +98,21 @@ def test_routed_add_pushes_into_owner_shards(C):
     assert torch.count_nonzero(flat[:flat0]) == 0 and torch.count_nonzero(flat[flat0 + n:]) == 0
     with pytest.raises(RuntimeError, match="outside the sharded space"):
         C.routed_add(src, chunk * world - 4, chunk, [s.data_ptr() for s in shards])
+
+
+def test_routed_embedding_backward(C):
+    V, d, T, world = 1000, 256, 4096, 3
+    ids = torch.randint(0, 50, (T,), device="cuda")  # many repeated rows: reductions must accumulate
+    dy = _bf(T, d, seed=9)
+    flat0 = 128
+    chunk = ((flat0 + V * d + world - 1) // world + 3) // 4 * 4
+    shards = [torch.zeros(chunk, device="cuda") for _ in range(world)]
+    C.embedding_bwd_routed(ids, dy, V, flat0, chunk, [s.data_ptr() for s in shards])
+    ref = torch.zeros(V, d, device="cuda")
+    C.embedding_bwd(ids, dy, ref)
+    torch.cuda.synchronize()
+    got = torch.cat(shards)[flat0:flat0 + V * d].view(V, d)
+    torch.testing.assert_close(got, ref, rtol=1e-5, atol=1e-4)
 
 
 def test_routed_sinks_match_the_flat_gradient_buffer(C):
