@@ -176,3 +176,38 @@ def test_paced_hold_on_device():
     t2 = timed(two)
     assert 2 * cost_ms * 0.97 <= t2 < 2 * cost_ms + 20.0
     assert ext.read_device_errors()[0] == 0
+
+
+def test_fused_step_and_routed_entry_points_pass_the_binding_arguments(monkeypatch):
+    """The NVLink collectives' fused-step and routing entry points hand the native bindings their
+    arguments in the bindings' order (checked here without a GPU)."""
+    from cs244c_llama_zero_b200.parallel.comm import nvlink
+    from cs244c_llama_zero_b200.parallel.zero.optim import AdamWConfig
+
+    monkeypatch.setattr(nvlink, "_world", lambda: 2)
+    coll = nvlink.NvlinkCollectives(device=torch.device("cpu"))
+    calls = []
+
+    class Ctx:
+        def rs_adamw_allgather(self, *args):
+            calls.append(args)
+
+    class Buf:
+        multicast = False
+
+        def __init__(self, dtype):
+            self.ctx = Ctx()
+            self.handle = type("H", (), {"buffer_ptrs": [4096, 8192]})()
+
+    bufs = {torch.bfloat16: Buf(torch.bfloat16), torch.float32: Buf(torch.float32)}
+    monkeypatch.setattr(coll, "_locate", lambda t: (bufs[t.dtype], 32 if t.dtype == torch.float32 else 16))
+    params, grads = torch.zeros(32, dtype=torch.bfloat16), torch.zeros(32)
+    master, m, v = torch.zeros(16), torch.zeros(16), torch.zeros(16)
+    cfg = AdamWConfig(lr=1e-3, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.1)
+    sq = torch.zeros(1)
+    assert coll.reduce_scatter_adamw_allgather(params, grads, master, m, v, 0.5, cfg, 7, None, sq)
+    (args,) = calls
+    assert args[0] is bufs[torch.float32].ctx and args[1:4] == (32, 16, 16)  # grads ctx, g_off, param_off, chunk
+    assert args[4] is master and args[5] is m and args[6] is v
+    assert args[7:13] == (0.5, 1e-3, 0.9, 0.95, 1e-8, 0.1) and args[13] == 7 and args[14] is None and args[15] is sq
+    assert coll.shard_bases(grads) == [4096 + 32, 8192 + 32]
