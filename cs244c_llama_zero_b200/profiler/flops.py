@@ -11,7 +11,7 @@ from __future__ import annotations
 
 import json
 import os
-from dataclasses import asdict, dataclass
+from dataclasses import dataclass
 from typing import TYPE_CHECKING, Callable, Dict, Generic, List, Optional, Tuple, TypeVar
 
 import torch
@@ -28,13 +28,14 @@ class FlopSnapshot:
     total_flops: float
 
     def to_dict(self) -> Dict[str, float | str]:
-        return asdict(self)
+        return {"label": self.label, "total_flops": self.total_flops}
 
 
 def flops_to_tflops_per_second(total_flops: float, step_time_s: float) -> float:
-    if total_flops < 0.0 or step_time_s <= 0.0:
+    """FLOPs done in ``step_time_s`` seconds, as TFLOP/s."""
+    if not (total_flops >= 0.0 and step_time_s > 0.0):
         raise ValueError("total_flops must be >= 0 and step_time_s must be > 0")
-    return float(total_flops) / 1e12 / float(step_time_s)
+    return total_flops / (step_time_s * 1e12)
 
 
 def _forward_terms(cfg: "ModelConfig", batch_size: int, seq_len: int) -> Dict[str, float]:
@@ -111,31 +112,34 @@ def roofline_fraction(executed_flops: float, seconds: float, peak_tflops: float)
     return executed_flops / seconds / (peak_tflops * 1e12)
 
 
-@dataclass
 class FlopTracker(Generic[T]):
-    device: Optional[torch.device] = None
-    snapshots: List[FlopSnapshot] = None
+    """Counts the FLOPs of one call by intercepting the ATen operators it dispatches.
 
-    def __post_init__(self) -> None:
-        if self.snapshots is None:
-            self.snapshots = []
+    Same surface as the reference's tracker (``profiler/flops.py:68-100``): ``measure(label, fn)``
+    returns ``(fn(), total FLOPs or None)`` and ``as_dicts()`` lists ``{label, total_flops}`` records.
+    Here the count comes from ``torch.utils.flop_counter.FlopCounterMode`` (a dispatch-mode
+    interpreter of matmul / convolution / attention FLOP formulas) instead of the profiler, so it
+    needs no trace and works the same on CPU and CUDA.  The package's own fused kernels are not ATen
+    operators; for the B200 backend use ``estimate_transformer_train_flops`` / ``executed_train_flops``.
+    """
 
-    def _activities(self):
-        acts = [torch.profiler.ProfilerActivity.CPU]
-        if self.device is not None and self.device.type == "cuda" and torch.cuda.is_available():
-            acts.append(torch.profiler.ProfilerActivity.CUDA)
-        return acts
+    def __init__(self, device: Optional[torch.device] = None) -> None:
+        self.device = device
+        self.snapshots: List[FlopSnapshot] = []
 
-    def measure(self, label: str, fn: Callable[[], T]) -> tuple[T, float | None]:
-        with torch.profiler.profile(activities=self._activities(), with_flops=True, acc_events=True) as prof:
+    def measure(self, label: str, fn: Callable[[], T]) -> Tuple[T, Optional[float]]:
+        from torch.utils.flop_counter import FlopCounterMode
+
+        counter = FlopCounterMode(display=False)
+        with counter:
             result = fn()
-            if self.device is not None and self.device.type == "cuda" and torch.cuda.is_available():
-                torch.cuda.synchronize(self.device)
-        total = float(sum(float(getattr(evt, "flops", 0.0) or 0.0) for evt in prof.key_averages()))
+        if self.device is not None and self.device.type == "cuda" and torch.cuda.is_available():
+            torch.cuda.synchronize(self.device)
+        total = float(counter.get_total_flops())
         if total <= 0.0:
             return result, None
         self.snapshots.append(FlopSnapshot(label=label, total_flops=total))
         return result, total
 
     def as_dicts(self) -> List[Dict[str, float | str]]:
-        return [s.to_dict() for s in self.snapshots]
+        return [snap.to_dict() for snap in self.snapshots]

@@ -1,16 +1,23 @@
-"""Named timers (reference ``profiler/timer.py:11-99``).
+"""Named interval timers for the training step's phases.
 
-On CUDA a timer records a pair of events on the current stream; ``stop()``
-synchronises on the *end event* only (not the whole device) and returns the
-device-measured interval.  On CPU it falls back to ``time.perf_counter``.
+Public surface as in the reference (``profiler/timer.py:11-99``): ``TimerRegistry(device).timer(name)``
+hands out a ``NamedTimer`` with ``start()`` / ``stop() -> ms`` / ``summary() -> TimerSummary``, and
+``TimerRegistry.summarize()`` maps every timer that has samples to its summary.
+
+Design here: the *clock* is a separate object chosen once per timer.  ``_DeviceClock`` brackets the
+interval with two CUDA events on the current stream and, at ``stop``, waits for the end event only,
+so other streams (collective prefetch, copy engines) keep running; ``_HostClock`` uses
+``time.perf_counter``.  Samples are kept as an ``array('d')`` and summarised with linearly
+interpolated percentiles.
 """
 
 from __future__ import annotations
 
-import statistics
+import math
 import time
-from dataclasses import dataclass, field
-from typing import Dict, List, Optional
+from array import array
+from dataclasses import dataclass
+from typing import Dict, Iterable, Optional, Tuple
 
 import torch
 
@@ -27,72 +34,101 @@ class TimerSummary:
     max_ms: float
 
 
-@dataclass
-class NamedTimer:
-    name: str
-    device: Optional[torch.device] = None
-    _samples_ms: List[float] = field(default_factory=list)
-    _start_wall: Optional[float] = None
-    _start_event: Optional[torch.cuda.Event] = None
-    _end_event: Optional[torch.cuda.Event] = None
+def _percentile(ordered: Tuple[float, ...], q: float) -> float:
+    """Percentile of sorted samples by linear interpolation between the two nearest ranks."""
+    pos = q * (len(ordered) - 1)
+    lo = math.floor(pos)
+    hi = min(lo + 1, len(ordered) - 1)
+    frac = pos - lo
+    return ordered[lo] + (ordered[hi] - ordered[lo]) * frac
 
-    def _cuda(self) -> bool:
-        return self.device is not None and self.device.type == "cuda" and torch.cuda.is_available()
+
+def summarize_samples(name: str, samples_ms: Iterable[float]) -> TimerSummary:
+    ordered = tuple(sorted(float(s) for s in samples_ms))
+    if not ordered:
+        raise RuntimeError(f"Timer '{name}' has no samples")
+    total = math.fsum(ordered)
+    return TimerSummary(name=name, count=len(ordered), total_ms=total, mean_ms=total / len(ordered),
+                        p50_ms=_percentile(ordered, 0.50), p95_ms=_percentile(ordered, 0.95),
+                        min_ms=ordered[0], max_ms=ordered[-1])
+
+
+class _HostClock:
+    def begin(self):
+        return time.perf_counter()
+
+    def end(self, token) -> float:
+        return (time.perf_counter() - token) * 1e3
+
+
+class _DeviceClock:
+    def begin(self):
+        pair = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+        pair[0].record()
+        return pair
+
+    def end(self, token) -> float:
+        first, last = token
+        last.record()
+        last.synchronize()
+        return float(first.elapsed_time(last))
+
+
+def _clock_for(device: Optional[torch.device]):
+    if device is not None and device.type == "cuda" and torch.cuda.is_available():
+        return _DeviceClock()
+    return _HostClock()
+
+
+class NamedTimer:
+    """One named interval timer; every ``start()``/``stop()`` pair adds one sample in milliseconds."""
+
+    def __init__(self, name: str, device: Optional[torch.device] = None) -> None:
+        self.name = name
+        self.device = device
+        self._clock = _clock_for(device)
+        self._open = None
+        self._samples = array("d")
+
+    @property
+    def count(self) -> int:
+        return len(self._samples)
+
+    @property
+    def samples_ms(self) -> Tuple[float, ...]:
+        return tuple(self._samples)
 
     def start(self) -> None:
-        if self._cuda():
-            self._start_event = torch.cuda.Event(enable_timing=True)
-            self._end_event = torch.cuda.Event(enable_timing=True)
-            self._start_event.record()
-        else:
-            self._start_wall = time.perf_counter()
+        self._open = self._clock.begin()
 
     def stop(self) -> float:
-        if self._start_event is not None and self._end_event is not None:
-            self._end_event.record()
-            self._end_event.synchronize()
-            elapsed = float(self._start_event.elapsed_time(self._end_event))
-            self._start_event = self._end_event = None
-        elif self._start_wall is not None:
-            elapsed = (time.perf_counter() - self._start_wall) * 1000.0
-            self._start_wall = None
-        else:
-            raise RuntimeError("Timer.stop() called before Timer.start()")
-        self._samples_ms.append(elapsed)
-        return elapsed
+        if self._open is None:
+            raise RuntimeError(f"timer '{self.name}': stop() without a matching start()")
+        token, self._open = self._open, None
+        ms = self._clock.end(token)
+        self._samples.append(ms)
+        return ms
 
     def add_sample(self, elapsed_ms: float) -> None:
-        self._samples_ms.append(float(elapsed_ms))
+        """Record an interval measured elsewhere (e.g. device-side stamps)."""
+        self._samples.append(float(elapsed_ms))
 
     def summary(self) -> TimerSummary:
-        if not self._samples_ms:
-            raise RuntimeError(f"Timer '{self.name}' has no samples")
-        ordered = sorted(self._samples_ms)
-
-        def pct(p: float) -> float:
-            return float(ordered[int(round((len(ordered) - 1) * p))])
-
-        return TimerSummary(
-            name=self.name,
-            count=len(ordered),
-            total_ms=float(sum(ordered)),
-            mean_ms=float(statistics.mean(ordered)),
-            p50_ms=pct(0.50),
-            p95_ms=pct(0.95),
-            min_ms=float(ordered[0]),
-            max_ms=float(ordered[-1]),
-        )
+        return summarize_samples(self.name, self._samples)
 
 
-@dataclass
 class TimerRegistry:
-    device: Optional[torch.device] = None
-    _timers: Dict[str, NamedTimer] = field(default_factory=dict)
+    """The process's timers by name, created on first use."""
+
+    def __init__(self, device: Optional[torch.device] = None) -> None:
+        self.device = device
+        self._by_name: Dict[str, NamedTimer] = {}
 
     def timer(self, name: str) -> NamedTimer:
-        if name not in self._timers:
-            self._timers[name] = NamedTimer(name=name, device=self.device)
-        return self._timers[name]
+        found = self._by_name.get(name)
+        if found is None:
+            found = self._by_name[name] = NamedTimer(name, self.device)
+        return found
 
     def summarize(self) -> Dict[str, TimerSummary]:
-        return {name: t.summary() for name, t in self._timers.items() if t._samples_ms}
+        return {name: t.summary() for name, t in self._by_name.items() if t.count}
