@@ -588,14 +588,13 @@ void attention_bwd(const AttnBwdParams& p, cudaStream_t s) {
   CUtensorMap tq = make_tmap_bf16_2d(p.qkv, (uint64_t)p.ld, (uint64_t)rows, (uint64_t)p.ld, 64, 128);
   CUtensorMap tdo = make_tmap_bf16_2d(p.dout, (uint64_t)p.ld_out, (uint64_t)rows, (uint64_t)p.ld_out, 64, 128);
   CUtensorMap tdq = make_dq_map(p);
-  static bool cfg = false;
-  if (!cfg) {
+  static std::atomic<unsigned long long> configured{0};
+  once_per_device(configured, [] {
     B200_CUDA_CHECK(cudaFuncSetAttribute(attn_bwd_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          AttnBwdCfg<64>::SMEM_BYTES));
     B200_CUDA_CHECK(cudaFuncSetAttribute(attn_bwd_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          AttnBwdCfg<128>::SMEM_BYTES));
-    cfg = true;
-  }
+  });
   if (p.head_dim == 64)
     launch_bwd<64>(p, tq, tdo, tdq, device_errors_ptr(), s);
   else
@@ -670,6 +669,28 @@ extern "C" int b200_attention_bwd_noalloc(const void* qkv, int ld, int k_col, in
                          "of 128, heads a multiple of kv_heads, pointers 16-byte aligned)\n");
     return B200_NOALLOC_ERR_INVALID;
   }
+  // Column extents: q, k and v must each fit before the next block and inside the row; the output
+  // rows must hold every query head.
+  const long long q_w = (long long)heads * head_dim, kv_w = (long long)kv_heads * head_dim;
+  if (q_w > k_col || k_col + kv_w > v_col || v_col + kv_w > ld || q_w > ld_out) {
+    std::fprintf(stderr,
+                 "b200_attention_bwd_noalloc: column layout does not fit (need heads*head_dim <= k_col, "
+                 "k_col + kv_heads*head_dim <= v_col, v_col + kv_heads*head_dim <= ld, heads*head_dim <= ld_out)\n");
+    return B200_NOALLOC_ERR_INVALID;
+  }
+  // The scratch address is per device: the stream must belong to the current device.
+  {
+    int cur = 0, sdev = 0;
+    if (cudaGetDevice(&cur) != cudaSuccess) return B200_NOALLOC_ERR_CUDA;
+    if (stream != nullptr) {
+      if (cudaStreamGetDevice(stream, &sdev) != cudaSuccess) return B200_NOALLOC_ERR_CUDA;
+      if (sdev != cur) {
+        std::fprintf(stderr, "b200_attention_bwd_noalloc: stream belongs to device %d but device %d is current\n",
+                     sdev, cur);
+        return B200_NOALLOC_ERR_INVALID;
+      }
+    }
+  }
   const size_t rows = (size_t)batch * seq;
   const size_t err_bytes = align256(sizeof(DeviceErrors));
   const size_t delta_bytes = align256((size_t)batch * heads * seq * sizeof(float));
@@ -734,5 +755,23 @@ extern "C" int b200_attention_bwd_noalloc(const void* qkv, int ld, int k_col, in
     std::fprintf(stderr, "b200_attention_bwd_noalloc: launch failed: %s\n", cudaGetErrorString(e));
     return B200_NOALLOC_ERR_CUDA;
   }
+  return B200_NOALLOC_OK;
+}
+
+extern "C" int b200_attention_bwd_noalloc_last_error(int* record4) {
+  using namespace b200;
+  if (record4 == nullptr) return B200_NOALLOC_ERR_INVALID;
+  unsigned char* scratch = noalloc_scratch_for_current_device();
+  if (scratch == nullptr) return B200_NOALLOC_ERR_CUDA;
+  DeviceErrors rec{};
+  const cudaError_t e = cudaMemcpy(&rec, scratch, sizeof(DeviceErrors), cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) {
+    std::fprintf(stderr, "b200_attention_bwd_noalloc_last_error: %s\n", cudaGetErrorString(e));
+    return B200_NOALLOC_ERR_CUDA;
+  }
+  record4[0] = rec.code;
+  record4[1] = rec.where;
+  record4[2] = rec.block;
+  record4[3] = rec.count;
   return B200_NOALLOC_OK;
 }

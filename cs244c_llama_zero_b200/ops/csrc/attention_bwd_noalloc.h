@@ -17,7 +17,11 @@
 //     does not (use the regular path there).
 //   * The first call on each device looks up the array's device address (cudaGetSymbolAddress)
 //     and sets the kernel's shared-memory attribute, with that device current.  Make that first
-//     call before capturing a stream into a CUDA graph.
+//     call before capturing a stream into a CUDA graph.  `stream` must belong to the current
+//     device (the call checks, and rejects a stream of another device with ERR_INVALID).
+//   * Errors inside the kernels (an expired bounded wait) do not change the return code, which
+//     only covers argument checks and launches: read b200_attention_bwd_noalloc_last_error after
+//     the call's work has finished to know whether `dqkv` is valid.
 //   * The call allocates nothing: no cudaMalloc / cudaFree and no allocating library routine.  The
 //     scratch is shared by every call on a device and keeps the previous call's contents; the
 //     parts that must start at zero are cleared on the caller's stream at the start of each call.
@@ -28,6 +32,8 @@
 // 0, k at k_col, v at v_col), `out` / `dout` the forward output and its gradient ([B*S, ld_out]),
 // `lse` the forward's base-2 log-sum-exp [B, H, S], and `dqkv` ([B*S, ld], written) receives the
 // gradient with respect to the pre-RoPE q|k|v columns; `rope_cos` / `rope_sin` are [S, hd/2] fp32.
+// Column layout: heads*head_dim <= k_col, k_col + kv_heads*head_dim <= v_col,
+// v_col + kv_heads*head_dim <= ld and heads*head_dim <= ld_out (checked).
 // Returns 0 on success or one of the negative codes below.
 #pragma once
 
@@ -48,6 +54,15 @@ int b200_attention_bwd_noalloc(const void* qkv, int ld, int k_col, int v_col, co
                                int ld_out, const float* lse, void* dqkv, const float* rope_cos,
                                const float* rope_sin, int batch, int seq, int heads, int kv_heads, int head_dim,
                                float scale, cudaStream_t stream);
+
+// The kernels' error record of the last call on the current device, as four ints: code (0 = no
+// error; 2 = a bounded wait inside the attention kernel expired, 7 = a range check of the
+// debug-bounds build failed), where (the wait or check site), block (reporting block) and count.
+// A non-zero code means that call's `dqkv` is not valid.  The record lives in the same fixed
+// scratch array and is cleared by the next call, so read it after the call's work has finished
+// (synchronise the call's stream first) and before the next call.  Copies 16 bytes with a
+// synchronous cudaMemcpy (no allocation).  Returns 0 or B200_NOALLOC_ERR_INVALID / _CUDA.
+int b200_attention_bwd_noalloc_last_error(int* record4);
 
 #ifdef __cplusplus
 }

@@ -395,11 +395,10 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
 template <int HD>
 void launch_fwd(const AttnParams& p, const CUtensorMap& tm, cudaStream_t s) {
   using C = AttnFwdCfg<HD>;
-  static bool cfg = false;
-  if (!cfg) {
+  static std::atomic<unsigned long long> configured{0};
+  once_per_device(configured, [] {
     B200_CUDA_CHECK(cudaFuncSetAttribute(attn_fwd_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES));
-    cfg = true;
-  }
+  });
   const int items = (p.seq / 128) * p.heads * p.batch;
   const int grid = std::max(1, std::min(items, num_sms_cached()));
   launch_k(attn_fwd_kernel<HD>, dim3(grid), dim3(ATT_THREADS), C::SMEM_BYTES, s, 1, tm, p, device_errors_ptr());

@@ -460,6 +460,17 @@ void cross_entropy_bwd(Tensor logits, Tensor targets, Tensor lse, Tensor grad_lo
                           grad_loss.data_ptr<float>(), count.data_ptr<float>(), cur_stream());
 }
 
+// Column layout of the fused q|k|v rows and of the attention output rows: q at 0, k at k_col, v at
+// v_col, each block inside the row and before the next one; every query head inside an output row.
+void check_attn_columns(int64_t qkv_ld, int64_t k_col, int64_t v_col, int64_t out_ld, int64_t heads, int64_t kv_heads,
+                        int64_t head_dim) {
+  const int64_t q_w = heads * head_dim, kv_w = kv_heads * head_dim;
+  TORCH_CHECK(q_w <= k_col, "attention: q columns (heads*head_dim = ", q_w, ") overlap k_col = ", k_col);
+  TORCH_CHECK(k_col + kv_w <= v_col, "attention: k columns end at ", k_col + kv_w, " past v_col = ", v_col);
+  TORCH_CHECK(v_col + kv_w <= qkv_ld, "attention: v columns end at ", v_col + kv_w, " past the row stride ", qkv_ld);
+  TORCH_CHECK(q_w <= out_ld, "attention: output rows (stride ", out_ld, ") hold fewer than heads*head_dim = ", q_w);
+}
+
 void attention_fwd(Tensor qkv, int64_t k_col, int64_t v_col, Tensor out, Tensor lse, int64_t batch, int64_t seq,
                    int64_t heads, int64_t kv_heads, int64_t head_dim, double scale) {
   check_bf16_2d(qkv, "qkv");
@@ -467,6 +478,9 @@ void attention_fwd(Tensor qkv, int64_t k_col, int64_t v_col, Tensor out, Tensor 
   check_f32(lse, "lse");
   TORCH_CHECK(qkv.size(0) == batch * seq && out.size(0) == batch * seq, "attention: row count");
   TORCH_CHECK(lse.numel() == batch * heads * seq, "attention: lse size");
+  TORCH_CHECK(out.size(1) >= heads * head_dim, "attention: out has fewer columns than heads*head_dim");
+  check_attn_columns(qkv.stride(0), k_col, v_col, out.stride(0), heads, kv_heads, head_dim);
+  TORCH_CHECK(qkv.size(1) >= v_col + kv_heads * head_dim, "attention: qkv has fewer columns than its v block needs");
   c10::cuda::CUDAGuard g(qkv.device());
   b200::AttnParams p{};
   p.qkv = reinterpret_cast<const __nv_bfloat16*>(qkv.data_ptr());
@@ -500,6 +514,13 @@ void attention_bwd(Tensor qkv, int64_t k_col, int64_t v_col, Tensor out, Tensor 
   check_f32(dq_acc, "dq_acc");
   TORCH_CHECK(dq_acc.numel() >= batch * seq * heads * head_dim, "dq_acc too small");
   TORCH_CHECK(dqkv.stride(0) == qkv.stride(0), "dqkv must share the qkv row stride");
+  TORCH_CHECK(qkv.size(0) == batch * seq && out.size(0) == batch * seq && dout.size(0) == batch * seq &&
+                  dqkv.size(0) == batch * seq, "attention_bwd: row count");
+  check_attn_columns(qkv.stride(0), k_col, v_col, out.stride(0), heads, kv_heads, head_dim);
+  TORCH_CHECK(qkv.size(1) >= v_col + kv_heads * head_dim && dqkv.size(1) >= v_col + kv_heads * head_dim,
+              "attention_bwd: qkv / dqkv have fewer columns than the v block needs");
+  TORCH_CHECK(out.size(1) >= heads * head_dim && dout.size(1) >= heads * head_dim,
+              "attention_bwd: out / dout have fewer columns than heads*head_dim");
   c10::cuda::CUDAGuard g(qkv.device());
   b200::AttnBwdParams p{};
   p.qkv = reinterpret_cast<const __nv_bfloat16*>(qkv.data_ptr());

@@ -38,6 +38,20 @@ inline void count_launch(int n = 1) { launch_counter().fetch_add(n, std::memory_
     if (!(cond)) throw std::runtime_error(std::string("b200 ops: ") + (msg));      \
   } while (0)
 
+// Runs `fn` once for each CUDA device, with that device current when it is first seen.  For settings
+// that belong to a device rather than to the process, such as a kernel's dynamic shared-memory limit
+// (cudaFuncSetAttribute applies to the current device only).  Devices 0..63.
+template <typename F>
+void once_per_device(std::atomic<unsigned long long>& done, F&& fn) {
+  int dev = 0;
+  B200_CUDA_CHECK(cudaGetDevice(&dev));
+  B200_CHECK(dev >= 0 && dev < 64, "device index out of range for the per-device setup mask");
+  const unsigned long long bit = 1ull << dev;
+  if (done.load(std::memory_order_acquire) & bit) return;
+  fn();
+  done.fetch_or(bit, std::memory_order_acq_rel);
+}
+
 // Programmatic dependent launch: a kernel launched with launch_k() may start (and run its setup:
 // barrier init, tensor-memory allocation, descriptor prefetch) while the previous kernel of the
 // stream is still finishing; it must call pdl_wait() before touching any global memory that an

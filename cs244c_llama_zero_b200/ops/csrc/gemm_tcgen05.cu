@@ -696,11 +696,10 @@ template <int BN, bool A_MN, bool B_MN, int EPI, int CG>
 static void launch_impl(const GemmOperands& op, GemmParams p, cudaStream_t stream) {
   using Cfg = GemmCfg<BN, CG>;
   auto kernel = gemm_kernel<BN, A_MN, B_MN, EPI, CG>;
-  static bool configured = false;
-  if (!configured) {
+  static std::atomic<unsigned long long> configured{0};
+  once_per_device(configured, [&] {
     B200_CUDA_CHECK(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_BYTES));
-    configured = true;
-  }
+  });
   // A operand: K-major -> global [M, K] (K contiguous); MN-major -> global [K, M] (M contiguous).
   CUtensorMap tmA = A_MN ? make_tmap_bf16_2d(op.A, (uint64_t)p.M, (uint64_t)p.K, op.lda, 64, 64)
                          : make_tmap_bf16_2d(op.A, (uint64_t)p.K, (uint64_t)p.M, op.lda, 64, BM);
@@ -958,11 +957,10 @@ void gemm_launch_dgrad_wgrad(const GemmOperands& op0, GemmParams p0, const GemmO
 
   auto kernel = routed ? gemm_kernel<BNG, false, true, EPI_STORE, CGG, true, true>
                        : gemm_kernel<BNG, false, true, EPI_STORE, CGG, true, false>;
-  static bool configured[2] = {false, false};
-  if (!configured[routed]) {
+  static std::atomic<unsigned long long> configured[2];
+  once_per_device(configured[routed], [&] {
     B200_CUDA_CHECK(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_BYTES));
-    configured[routed] = true;
-  }
+  });
   // problem 0: A = dY [M0, K0] K-major, B = W [K0, N0] MN-major, C = dX (bf16)
   const CUtensorMap tmA = make_tmap_bf16_2d(op0.A, (uint64_t)p0.K, (uint64_t)p0.M, op0.lda, 64, BM);
   const CUtensorMap tmB = make_tmap_bf16_2d(op0.B, (uint64_t)p0.N, (uint64_t)p0.K, op0.ldb, 64, 64);
