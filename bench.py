@@ -29,6 +29,11 @@ import tempfile
 import time
 
 HERE = os.path.dirname(os.path.abspath(__file__))
+# BASELINE.json shapes: model dimensions and the per-GPU micro-batch / sequence length they are run at.
+CONFIG_SHAPES = {
+    "baseline-small": dict(dim=768, n_layers=12, n_heads=12, n_kv_heads=4, ffn_dim=2048, batch=8, seq=1024),
+    "baseline-1.3b": dict(dim=2048, n_layers=24, n_heads=16, n_kv_heads=8, ffn_dim=5504, batch=4, seq=2048),
+}
 METRIC = "tokens/s (device-timed, max over ranks) per ZeRO stage 0–3 at 1/2/4/8 B200; comm_ms"
 MODEL_DESC = "small LLaMA d768/L12/H12/KV4/ffn2048/V32000 (tied embeddings)"
 
@@ -53,10 +58,14 @@ def parse_args(argv=None) -> argparse.Namespace:
     p.add_argument("--cuda-graph", action="store_true",
                    help="run stages 0-2 as one captured CUDA graph per step (TrainSession cuda_graph mode)")
     p.add_argument("--model-size", type=str, default="baseline-small",
-                   help="model preset: baseline-small (the headline config), baseline-1.3b, baseline-7b, ...")
+                   help="model preset of the headline: baseline-small (the headline config), baseline-1.3b, ...")
+    p.add_argument("--extra-configs", type=str, default="baseline-1.3b",
+                   help="comma-separated presets measured after the headline at their BASELINE shapes (every "
+                        "stage, same steps and warm-up), reported under per_config; '' for none")
     args = p.parse_args(argv)
     args.warmup = max(3, args.warmup)
     args.stage_list = [int(s) for s in args.stages.split(",") if s.strip()]
+    args.extra_list = [c.strip() for c in args.extra_configs.split(",") if c.strip() and c.strip() != args.model_size]
     if args.headline_stage not in args.stage_list:
         args.headline_stage = args.stage_list[0]
     return args
@@ -64,20 +73,65 @@ def parse_args(argv=None) -> argparse.Namespace:
 
 # ----------------------------------------------------------------------------------- clocks
 class ClockSampler:
-    """Samples SM clocks and throttle reasons with nvidia-smi while the timed region runs."""
+    """Samples SM clocks and clock-event (throttle) reasons while the timed region runs.
+
+    Through NVML every 5 ms on a background thread when the ``pynvml`` bindings load (a 20-step
+    region of ~9 ms steps still gets dozens of samples), else through ``nvidia-smi -lms 100``.
+    """
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    # NVML clocks-event reason bits
+    REASON_BITS = {"sw_power_cap": 0x4, "hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20,
+                   "hw_thermal_slowdown": 0x40}
+    PERIOD_S = 0.005
 
     def __init__(self, gpu_indices, path=None):
         self.gpu_indices = set(gpu_indices)
         self.proc = None
-        # The raw samples go to --clocks-csv when given (kept), else to a temporary file; the JSON
-        # line carries the summary either way.
+        self.thread = None
+        self.samples = []  # (index, sm_mhz, max_mhz, reason names)
+        # nvidia-smi fallback: the raw samples go to --clocks-csv when given (kept), else to a temp file
         self.path = path or os.path.join(tempfile.gettempdir(), f"zb_clocks_{os.getpid()}.csv")
+        self.keep_csv = path is not None
+
+    def _nvml_loop(self, nvml, handles):
+        import threading  # noqa: F401
+
+        while not self._stop.is_set():
+            for idx, h in handles:
+                try:
+                    mhz = nvml.nvmlDeviceGetClockInfo(h, nvml.NVML_CLOCK_SM)
+                    max_mhz = nvml.nvmlDeviceGetMaxClockInfo(h, nvml.NVML_CLOCK_SM)
+                    bits = nvml.nvmlDeviceGetCurrentClocksEventReasons(h)
+                except Exception:  # noqa: BLE001 - a failed read is a missing sample
+                    continue
+                names = [n for n, b in self.REASON_BITS.items() if bits & b]
+                self.samples.append((idx, float(mhz), float(max_mhz), names))
+            self._stop.wait(self.PERIOD_S)
 
     def __enter__(self):
+        import threading
+
+        try:
+            import pynvml as nvml
+
+            nvml.nvmlInit()
+            visible = os.environ.get("CUDA_VISIBLE_DEVICES")
+            order = [int(x) for x in visible.split(",")] if visible and all(
+                x.strip().isdigit() for x in visible.split(",")) else None
+            handles = []
+            for idx in sorted(self.gpu_indices):
+                phys = order[idx] if order and idx < len(order) else idx
+                handles.append((idx, nvml.nvmlDeviceGetHandleByIndex(phys)))
+            self._nvml = nvml
+            self._stop = threading.Event()
+            self.thread = threading.Thread(target=self._nvml_loop, args=(nvml, handles), daemon=True)
+            self.thread.start()
+            return self
+        except Exception:  # noqa: BLE001 - no NVML bindings / driver: use the CLI
+            self.thread = None
         try:
             os.makedirs(os.path.dirname(self.path), exist_ok=True)
             self.fh = open(self.path, "w")
@@ -88,6 +142,18 @@ class ClockSampler:
         return self
 
     def __exit__(self, *exc):
+        if self.thread is not None:
+            self._stop.set()
+            self.thread.join(timeout=5)
+            try:
+                self._nvml.nvmlShutdown()
+            except Exception:  # noqa: BLE001
+                pass
+            if self.keep_csv:
+                with open(self.path, "w") as fh:
+                    for idx, mhz, mx, names in self.samples:
+                        fh.write(f"{idx}, {mhz:.0f}, {mx:.0f}, {'|'.join(names) or 'none'}\n")
+            return
         if self.proc is not None:
             self.proc.terminate()
             try:
@@ -95,36 +161,35 @@ class ClockSampler:
             except subprocess.TimeoutExpired:
                 self.proc.kill()
             self.fh.close()
+            self._read_csv()
 
-    def summary(self):
-        if self.proc is None or not os.path.exists(self.path):
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unavailable"]}
-        mhz, max_mhz, reasons = [], [], set()
+    def _read_csv(self):
         names = ["active", "hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        if not os.path.exists(self.path):
+            return
         with open(self.path) as fh:
             for line in fh:
                 parts = [x.strip() for x in line.split(",")]
                 if len(parts) < 9:
                     continue
                 try:
-                    idx = int(parts[0])
+                    idx, mhz, mx = int(parts[0]), float(parts[1]), float(parts[2])
                 except ValueError:
                     continue
                 if self.gpu_indices and idx not in self.gpu_indices:
                     continue
-                try:
-                    mhz.append(float(parts[1]))
-                    max_mhz.append(float(parts[2]))
-                except ValueError:
-                    continue
-                for name, val in zip(names[1:], parts[5:9]):
-                    if val.lower().startswith("active"):
-                        reasons.add(name)
-        if not mhz:
+                active = [n for n, v in zip(names[1:], parts[5:9]) if v.lower().startswith("active")]
+                self.samples.append((idx, mhz, mx, active))
+
+    def summary(self):
+        if not self.samples:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        mhz = [x[1] for x in self.samples]
         loaded = [m for m in mhz if m > 0.5 * max(mhz)] or mhz
-        return {"sm_mhz": statistics.median(loaded), "sm_max_mhz": max(max_mhz), "reasons": sorted(reasons),
-                "samples": len(mhz)}
+        reasons = sorted({n for x in self.samples for n in x[3]})
+        return {"sm_mhz": statistics.median(loaded), "sm_max_mhz": max(x[2] for x in self.samples),
+                "reasons": reasons, "samples": len(mhz),
+                "source": "nvml" if self.thread is not None else "nvidia-smi"}
 
 
 # ----------------------------------------------------------------------------------- helpers
@@ -220,25 +285,118 @@ def base_record(args, world: int, impl: str) -> dict:
 
 
 # ----------------------------------------------------------------------------------- our arm
-def roofline_entry(sess, args, stage: int, ms: float, peak_tflops: float) -> dict:
+def roofline_entry(sess, batch: int, seq: int, stage: int, ms: float, peak_tflops: float) -> dict:
     """Executed tensor-core TFLOP/s of one GPU's step (causal attention halved, no recompute unless the
     stage-3 engine recomputes) and its fraction of the peak."""
     from cs244c_llama_zero_b200.profiler import executed_train_flops, roofline_fraction
 
     recompute = stage == 3 and bool(getattr(sess.engine, "recompute", False))
-    executed = executed_train_flops(sess.model_cfg, args.batch_size, args.seq_len, recompute_forward=recompute)
+    executed = executed_train_flops(sess.model_cfg, batch, seq, recompute_forward=recompute)
     return {"executed_tflops_per_gpu": executed / (ms / 1000.0) / 1e12,
             "roofline_fraction": roofline_fraction(executed, ms / 1000.0, peak_tflops)}
 
 
-def run_mine(args) -> None:
+def _measure_stages(args, size: str, batch: int, seq: int, world: int, rank: int, local: int, impl: str,
+                    peak_tflops: float, headline: bool) -> dict:
+    """Every stage of ``args.stage_list`` on one model config: W warm-up steps, then K device-timed
+    steps (max over ranks), then one instrumented step for comm_ms.  With ``headline`` the headline
+    stage also gets the clock samples, the launch count and the end-to-end run."""
     import torch
-    import torch.distributed as dist
 
     from cs244c_llama_zero_b200 import ops
     from cs244c_llama_zero_b200.models import BASELINE_VOCAB_SIZE
-    from cs244c_llama_zero_b200.profiler import peak_bf16_tflops
     from cs244c_llama_zero_b200.train import SessionConfig, TrainSession
+
+    out = {"per_stage": {}, "e2e": None, "launches": None, "clocks": None, "headline_ms": None}
+    tokens_per_step = batch * seq * world
+    for stage in args.stage_list:
+        sess = TrainSession(SessionConfig(model_size=size, vocab_size=BASELINE_VOCAB_SIZE,
+                                          seq_len=seq, batch_size=batch, zero_stage=stage,
+                                          collective_impl=impl, backend="b200",
+                                          cuda_graph=args.cuda_graph and stage != 3))
+        host = random_batches(4, batch, seq, BASELINE_VOCAB_SIZE, seed=1234 + rank * 100 + stage)
+        dev = [h.to(sess.device) for h in host]
+        it = {"i": 0}
+
+        def device_step():
+            sess.train_step(dev[it["i"] % len(dev)])
+            it["i"] += 1
+
+        is_head = headline and stage == args.headline_stage
+        # The sampler starts before the warm-up so that short timed regions still get samples taken
+        # under steady load; it stops right after the timed steps.
+        sampler = ClockSampler([local], args.clocks_csv) if is_head and rank == 0 else None
+        if sampler:
+            sampler.__enter__()
+        for _ in range(args.warmup):
+            device_step()
+        torch.cuda.synchronize()
+        launches_before = ops.launch_count()
+        ms = time_device(device_step, args.steps)
+        if sampler:
+            sampler.__exit__(None, None, None)
+            out["clocks"] = sampler.summary()
+        stage_launches = (ops.launch_count() - launches_before) // args.steps
+        entry = {"tokens_per_s": tokens_per_step / (ms / 1000.0), "ms_per_step": ms,
+                 "gpu_launches_per_step": stage_launches}
+        entry.update(roofline_entry(sess, batch, seq, stage, ms, peak_tflops))
+        # comm time of one extra instrumented step (device events around each collective); the
+        # barrier keeps host-side skew between ranks out of the measured intervals
+        barrier_sync()
+        sess.engine.clock.timing = True  # an eager instrumented step, also in graph mode
+        sess.engine.zero_grad()
+        sess.engine.prepare_forward()
+        sess.forward_backward([dev[0]])
+        st = sess.engine.step_with_stats(max_grad_norm=0.0)
+        entry["comm_ms"] = max_over_ranks(float(st["comm_ms"]))
+        if is_head:
+            out["headline_ms"] = ms
+            out["launches"] = stage_launches * args.steps
+            if not args.no_e2e:
+                out["e2e"] = _e2e(sess, host, it, args.steps, tokens_per_step)
+        out["per_stage"][str(stage)] = entry
+        del sess
+        torch.cuda.empty_cache()
+    return out
+
+
+def _e2e(sess, host, it, steps: int, tokens_per_step: int) -> dict:
+    """K steps through the public API: each step's pinned host batch is copied in by train_step and its
+    loss (+ the kernels' error record) comes back to the host, read one step later."""
+    h2d = host[0].numel() * host[0].element_size()
+    pending = []
+    losses = []
+    d2h = {"n": 0}
+
+    def e2e_step():
+        pending.append(sess.train_step_async(host[it["i"] % len(host)]))
+        d2h["n"] = pending[-1].nbytes  # loss + the kernels' error record
+        it["i"] += 1
+        if len(pending) > 1:
+            losses.append(pending.pop(0).item())
+
+    def e2e_finish():  # the last step's loss is read inside the timed region too
+        while pending:
+            losses.append(pending.pop(0).item())
+
+    for _ in range(2):
+        e2e_step()
+    e2e_finish()
+    losses.clear()
+    e2e_ms = time_wall(e2e_step, steps, finish=e2e_finish)
+    if len(losses) != steps or not all(math.isfinite(x) for x in losses):
+        raise RuntimeError(f"e2e: expected {steps} finite losses, got {losses}")
+    return {"value": tokens_per_step / (e2e_ms / 1000.0), "unit": "tokens/s",
+            "ms_per_step": e2e_ms, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h["n"],
+            "api": "cs244c_llama_zero_b200.train.TrainSession.train_step_async(pinned host int64 [B,S])"
+                   " + AsyncLoss.item() one step later (every step's loss and error record read on the host)"}
+
+
+def run_mine(args) -> None:
+    import torch.distributed as dist
+
+    from cs244c_llama_zero_b200 import ops
+    from cs244c_llama_zero_b200.profiler import peak_bf16_tflops
 
     peak_tflops, peak_source = peak_bf16_tflops()
     rank, world, local = dist_env()
@@ -251,110 +409,39 @@ def run_mine(args) -> None:
     impl = args.collective_impl
     if impl == "auto":
         impl = "nvls" if world > 1 else "torch"
-    per_stage = {}
-    e2e = None
-    launches = None
-    clocks = None
-    headline_ms = None
-    tokens_per_step = args.batch_size * args.seq_len * world
-    for stage in args.stage_list:
-        sess = TrainSession(SessionConfig(model_size=args.model_size, vocab_size=BASELINE_VOCAB_SIZE,
-                                          seq_len=args.seq_len, batch_size=args.batch_size, zero_stage=stage,
-                                          collective_impl=impl, backend="b200",
-                                          cuda_graph=args.cuda_graph and stage != 3))
-        host = random_batches(4, args.batch_size, args.seq_len, BASELINE_VOCAB_SIZE, seed=1234 + rank * 100 + stage)
-        dev = [h.to(sess.device) for h in host]
-        it = {"i": 0}
-
-        def device_step():
-            sess.train_step(dev[it["i"] % len(dev)])
-            it["i"] += 1
-
-        # The sampler starts before the warm-up so that short timed regions still get samples taken
-        # under steady load; it stops right after the timed steps.
-        sampler = ClockSampler([local], args.clocks_csv) if stage == args.headline_stage and rank == 0 else None
-        if sampler:
-            sampler.__enter__()
-        for _ in range(args.warmup):
-            device_step()
-        torch.cuda.synchronize()
-        launches_before = ops.launch_count()
-        ms = time_device(device_step, args.steps)
-        if sampler:
-            sampler.__exit__(None, None, None)
-            clocks = sampler.summary()
-        stage_launches = (ops.launch_count() - launches_before) // args.steps
-        entry = {"tokens_per_s": tokens_per_step / (ms / 1000.0), "ms_per_step": ms,
-                 "gpu_launches_per_step": stage_launches}
-        entry.update(roofline_entry(sess, args, stage, ms, peak_tflops))
-        # comm time of one extra instrumented step (device events around each collective); the
-        # barrier keeps host-side skew between ranks out of the measured intervals
-        barrier_sync()
-        sess.engine.clock.timing = True  # an eager instrumented step, also in graph mode
-        sess.engine.zero_grad()
-        sess.engine.prepare_forward()
-        sess.forward_backward([dev[0]])
-        st = sess.engine.step_with_stats(max_grad_norm=0.0)
-        entry["comm_ms"] = max_over_ranks(float(st["comm_ms"]))
-        if stage == args.headline_stage:
-            headline_ms = ms
-            launches = stage_launches * args.steps
-            if not args.no_e2e:
-                h2d = host[0].numel() * host[0].element_size()
-
-                pending = []
-                d2h = 0
-
-                def e2e_step():
-                    # pinned host batch -> device inside train_step; the step's loss is copied to
-                    # pinned host memory and read (.item()) after the next step has been queued
-                    nonlocal d2h
-                    pending.append(sess.train_step_async(host[it["i"] % len(host)]))
-                    d2h = pending[-1].nbytes  # loss + the kernels' error record
-                    it["i"] += 1
-                    if len(pending) > 1:
-                        losses.append(pending.pop(0).item())
-
-                def e2e_finish():  # the last step's loss is read inside the timed region too
-                    while pending:
-                        losses.append(pending.pop(0).item())
-
-                losses = []
-                for _ in range(2):
-                    e2e_step()
-                e2e_finish()
-                losses.clear()
-                e2e_ms = time_wall(e2e_step, args.steps, finish=e2e_finish)
-                if len(losses) != args.steps or not all(math.isfinite(x) for x in losses):
-                    raise RuntimeError(f"e2e: expected {args.steps} finite losses, got {losses}")
-                e2e = {"value": tokens_per_step / (e2e_ms / 1000.0), "unit": "tokens/s",
-                       "ms_per_step": e2e_ms, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                       "api": "cs244c_llama_zero_b200.train.TrainSession.train_step_async(pinned host int64 [B,S])"
-                              " + AsyncLoss.item() one step later (every step's loss and error record read on the host)"}
-        per_stage[str(stage)] = entry
-        del sess
-        torch.cuda.empty_cache()
+    head = _measure_stages(args, args.model_size, args.batch_size, args.seq_len, world, rank, local, impl,
+                           peak_tflops, headline=True)
+    per_config = {}
+    for size in args.extra_list:
+        shape = CONFIG_SHAPES[size]
+        extra = _measure_stages(args, size, shape["batch"], shape["seq"], world, rank, local, impl, peak_tflops,
+                                headline=False)
+        per_config[size] = {"model": model_desc(size), "global_batch": shape["batch"] * world,
+                            "micro_batch_per_gpu": shape["batch"], "seq_len": shape["seq"],
+                            "per_stage": extra["per_stage"]}
     errors = ops.load_extension().read_device_errors()
     rec = base_record(args, world, "mine")
-    head = per_stage[str(args.headline_stage)]
+    hs = head["per_stage"][str(args.headline_stage)]
     rec.update({
-        "value": head["tokens_per_s"],
-        "ms_per_step": headline_ms,
-        "config": {"model": model_desc(args.model_size), "global_batch": args.batch_size * world, "micro_batch_per_gpu": args.batch_size,
+        "value": hs["tokens_per_s"],
+        "ms_per_step": head["headline_ms"],
+        "config": {"model": model_desc(args.model_size), "global_batch": args.batch_size * world,
+                   "micro_batch_per_gpu": args.batch_size,
                    "seq_len": args.seq_len, "grad_accum": 1, "parallelism": f"dp{world}",
                    "zero_stage": args.headline_stage, "collective_impl": impl,
                    "cuda_graph": bool(args.cuda_graph and args.headline_stage != 3),
                    "fused_step": bool(args.fused_step),
                    "routed_grads": bool(args.routed_grads),
                    "l2": "no flush: each step touches >2 GB (activations, 1.2 GB fp32 optimizer state) vs 126 MB L2"},
-        "per_stage": per_stage,
-        "roofline": {"executed_tflops_per_gpu": head["executed_tflops_per_gpu"],
-                     "fraction": head["roofline_fraction"], "peak_bf16_tflops": peak_tflops,
+        "per_stage": head["per_stage"],
+        "per_config": per_config,
+        "roofline": {"executed_tflops_per_gpu": hs["executed_tflops_per_gpu"],
+                     "fraction": hs["roofline_fraction"], "peak_bf16_tflops": peak_tflops,
                      "peak_source": peak_source, "note": "of measured sustained cuBLAS bf16 GEMM peak"
                      if peak_source == "measured" else "of fallback peak"},
-        "e2e": e2e,
-        "gpu_launches": launches,
-        "clocks": clocks,
+        "e2e": head["e2e"],
+        "gpu_launches": head["launches"],
+        "clocks": head["clocks"],
         "device_errors": list(errors),
     })
     emit(rec, rank)
@@ -370,7 +457,7 @@ def main(argv=None) -> None:
         import run_reference
 
         run_reference.main(args, ClockSampler, base_record, emit, time_device, time_wall, random_batches,
-                           max_over_ranks, METRIC, MODEL_DESC)
+                           max_over_ranks, METRIC, MODEL_DESC, CONFIG_SHAPES)
         return
     run_mine(args)
 

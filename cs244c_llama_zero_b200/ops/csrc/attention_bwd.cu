@@ -116,7 +116,7 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
                     const __grid_constant__ CUtensorMap tm_dq, AttnBwdParams p, DeviceErrors* errs) {
   using C = AttnBwdCfg<HD>;
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* smem = align_smem_1024(smem_raw);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::BAR_OFF);
   uint64_t* kv_full = bars;
   uint64_t* kv_empty = bars + 1;
@@ -474,6 +474,407 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
   }
 }
 
+// ---------------------------------------------------------------------------------------------
+// head_dim 64: software-pipelined variant.
+//
+// Same work items and math as attn_bwd_kernel, with the tensor cores and the softmax warps
+// overlapped.  Per iteration g (one query block of one head) the MMA warp issues
+//     dV(g) | S^T(g+1) dP^T(g+1) | dK(g) dQ(g)
+// so the softmax of block g+1 runs while the tensor cores compute dK(g) and dQ(g).  What makes
+// that legal:
+//   * P^T(g) goes to TENSOR memory (bf16, into the columns of S^T(g) its warpgroup has already
+//     read) and dV(g) takes it from there (A operand in tensor memory); dV(g) is issued before
+//     S^T(g+1) overwrites those columns, and tcgen05.mma of one thread execute in order;
+//   * dS^T goes to shared memory (dK reads it K-major, dQ reads it MN-major as dS), double-buffered:
+//     the softmax of g+1 writes the buffer dK(g-1) / dQ(g-1) read, and the commit that releases
+//     S^T(g+1) to it comes after those MMAs;
+//   * dQ is double-buffered in tensor memory and read out by the softmax warps one iteration late
+//     (after handing over P^T / dS^T of the next block), so the readout never stalls the MMAs.
+// Tensor memory: S^T [0,128) | dP^T [128,256) | dV [256,320) | dK [320,384) | dQ0 [384,448) | dQ1.
+// 384 threads: warp 0 TMA, warp 1 MMA (+ tensor-memory allocation), warps 2-3 idle, warpgroups
+// 1 and 2 compute (thread = kv row for S^T / dP^T / dK / dV, query row for dQ; warpgroup w owns
+// query columns [64w, 64w + 64) and output columns [32w, 32w + 32)).
+// ---------------------------------------------------------------------------------------------
+struct AttnBwd64Cfg {
+  static constexpr int HD = 64;
+  static constexpr int TILE = 128 * HD * 2;    // 16 KB
+  static constexpr int STAGES = 2;             // (Q_i, dO_i, lse, delta) ring
+  static constexpr int K_OFF = 0;
+  static constexpr int V_OFF = TILE;
+  static constexpr int QD_OFF = 2 * TILE;
+  static constexpr int DST_OFF = QD_OFF + STAGES * 2 * TILE;  // two dS^T buffers of 128 x 128 bf16
+  static constexpr int LD_OFF = DST_OFF + 2 * 128 * 128 * 2;  // per stage: lse2[128] | delta[128]
+  static constexpr int STG_OFF = LD_OFF + STAGES * 1024;      // dQ staging: 8 warps x 2 chunks
+  static constexpr int BAR_OFF = STG_OFF + 8 * 2 * kBwdChunk;
+  static constexpr int SMEM_BYTES = BAR_OFF + 256 + 1024;
+  static_assert(SMEM_BYTES <= 232448, "attention backward (hd 64) shared memory exceeds 227 KB");
+  static constexpr int T_ST = 0, T_DPT = 128, T_DV = 256, T_DK = 320, T_DQ = 384;  // dQ buffer b at T_DQ + 64b
+  static constexpr int TMEM_COLS = 512;
+  static constexpr int THREADS = 384;
+  static constexpr int REGS_LOW = 64, REGS_HIGH = 216;  // 128 * 64 + 256 * 216 <= 384 * 168
+  static constexpr int EMU = 2;  // exponentials on the FMA pipe: columns with (c & 7) >= 8 - EMU
+};
+
+__global__ void __launch_bounds__(AttnBwd64Cfg::THREADS, 1)
+    attn_bwd_hd64_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __grid_constant__ CUtensorMap tm_do,
+                         const __grid_constant__ CUtensorMap tm_dq, AttnBwdParams p, DeviceErrors* errs) {
+  using C = AttnBwd64Cfg;
+  constexpr int HD = C::HD;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = align_smem_1024(smem_raw);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::BAR_OFF);
+  uint64_t* kv_full = bars;
+  uint64_t* kv_empty = bars + 1;
+  uint64_t* q_full = bars + 2;              // [STAGES]
+  uint64_t* q_empty = q_full + C::STAGES;   // [STAGES]
+  uint64_t* st_full = q_empty + C::STAGES;  // S^T and dP^T of the next block complete
+  uint64_t* p_ready = st_full + 1;          // 8 warps: P^T in tensor memory, dS^T in shared memory
+  uint64_t* dq_full = p_ready + 1;          // [2 buffers]
+  uint64_t* dq_free = dq_full + 2;          // [2 buffers], 8 warps
+  uint64_t* epi_done = dq_free + 2;         // 8 warps: the item's dK / dV have been read out
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(epi_done + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n_qb = p.seq / 128;
+  const int group = p.heads / p.kv_heads;
+  const int n_items = p.batch * p.kv_heads * n_qb;
+  const int G = gridDim.x, cta = blockIdx.x;
+
+  if (threadIdx.x == 0) {
+    mbar_init(kv_full, 1);
+    mbar_init(kv_empty, 1);
+    for (int s = 0; s < C::STAGES; ++s) {
+      mbar_init(&q_full[s], 1);
+      mbar_init(&q_empty[s], 1);
+    }
+    mbar_init(st_full, 1);
+    mbar_init(p_ready, 8);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&dq_full[b], 1);
+      mbar_init(&dq_free[b], 8);
+    }
+    mbar_init(epi_done, 8);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  pdl_wait_and_release();  // q|k|v, O, dO, lse, delta come from earlier kernels of the stream
+
+  if (warp < 4) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(C::REGS_LOW));
+    if (warp == 0 && lane == 0) {
+      tma_prefetch_desc(&tm_qkv);
+      tma_prefetch_desc(&tm_do);
+      int g = 0;  // global iteration counter (stage ring position)
+      bool ok = true;
+      for (int k = 0, u; ok && (u = bwd_item_index(k, cta, G, n_items)) >= 0; ++k) {
+        const BwdItem w = bwd_item(u, p.batch, p.kv_heads);
+        const int row0 = w.b * p.seq;
+        const int n_q = n_qb - w.j;
+        if (!mbar_wait_bounded(kv_empty, (k & 1) ^ 1u, abort_flag, errs, kErrAttnWait, 9)) break;
+        mbar_expect_tx(kv_full, 2 * C::TILE);
+        tma_load_2d(smem + C::K_OFF, &tm_qkv, kv_full, p.k_col + w.kvh * HD, row0 + w.j * 128);
+        tma_load_2d(smem + C::V_OFF, &tm_qkv, kv_full, p.v_col + w.kvh * HD, row0 + w.j * 128);
+        for (int it = 0; it < group * n_q; ++it, ++g) {
+          const int h = w.kvh * group + it / n_q;
+          const int i = w.j + it % n_q;
+          const int st = g % C::STAGES;
+          if (!mbar_wait_bounded(&q_empty[st], ((g / C::STAGES) & 1) ^ 1u, abort_flag, errs, kErrAttnWait, 10)) {
+            ok = false;
+            break;
+          }
+          uint8_t* qs = smem + C::QD_OFF + st * 2 * C::TILE;
+          uint8_t* ds = qs + C::TILE;
+          uint8_t* ls = smem + C::LD_OFF + st * 1024;
+          const size_t vec = ((size_t)w.b * p.heads + h) * p.seq + (size_t)i * 128;
+          mbar_expect_tx(&q_full[st], 2 * C::TILE + 1024);
+          tma_load_2d(qs, &tm_qkv, &q_full[st], h * HD, row0 + i * 128);
+          tma_load_2d(ds, &tm_do, &q_full[st], h * HD, row0 + i * 128);
+          if (B200_IN_BOUNDS(errs, vec, 128, (long long)p.batch * p.heads * p.seq, 110)) {
+            bulk_load(ls, p.lse + vec, 512, &q_full[st]);
+            bulk_load(ls + 512, p.delta + vec, 512, &q_full[st]);
+          } else {  // the 1024 skipped bytes were announced above: mark them complete without an arrival
+            asm volatile("mbarrier.complete_tx.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(&q_full[st])), "r"(1024)
+                         : "memory");
+          }
+        }
+      }
+    } else if (warp == 1 && lane == 0) {
+      constexpr uint32_t ID_S = idesc_bf16_f32(128, 128, false, false);
+      constexpr uint32_t ID_KV = idesc_bf16_f32(128, HD, false, true);
+      constexpr uint32_t ID_Q = idesc_bf16_f32(128, HD, true, true);
+      const uint32_t k_addr = smem_u32(smem + C::K_OFF);
+      const uint32_t v_addr = smem_u32(smem + C::V_OFF);
+      int g = 0;
+      bool ok = true;
+      // S^T = K Q^T and dP^T = V dO^T of global iteration gg (stage gg % STAGES)
+      auto issue_scores = [&](int gg) -> bool {
+        const int st = gg % C::STAGES;
+        if (!mbar_wait_bounded(&q_full[st], (gg / C::STAGES) & 1, abort_flag, errs, kErrAttnWait, 12)) return false;
+        tc_fence_after();
+        const uint32_t q_addr = smem_u32(smem + C::QD_OFF + st * 2 * C::TILE);
+        const uint32_t do_addr = q_addr + C::TILE;
+#pragma unroll
+        for (int ks = 0; ks < HD / 16; ++ks) {
+          const uint32_t off = ks * 32;
+          tc_mma_f16(tmem + C::T_ST, smem_desc_sw128(k_addr + off, 16, 1024), smem_desc_sw128(q_addr + off, 16, 1024),
+                     ID_S, ks > 0 ? 1u : 0u);
+        }
+#pragma unroll
+        for (int ks = 0; ks < HD / 16; ++ks) {
+          const uint32_t off = ks * 32;
+          tc_mma_f16(tmem + C::T_DPT, smem_desc_sw128(v_addr + off, 16, 1024),
+                     smem_desc_sw128(do_addr + off, 16, 1024), ID_S, ks > 0 ? 1u : 0u);
+        }
+        tc_commit(st_full);
+        return true;
+      };
+      for (int k = 0, u; ok && (u = bwd_item_index(k, cta, G, n_items)) >= 0; ++k) {
+        const BwdItem w = bwd_item(u, p.batch, p.kv_heads);
+        const int n_it = group * (n_qb - w.j);
+        if (!mbar_wait_bounded(kv_full, k & 1, abort_flag, errs, kErrAttnWait, 11)) break;
+        tc_fence_after();
+        if (!issue_scores(g)) break;
+        for (int it = 0; it < n_it; ++it, ++g) {
+          const int st = g % C::STAGES;
+          const int b = g & 1;
+          if (!mbar_wait_bounded(p_ready, g & 1, abort_flag, errs, kErrAttnWait, 14)) {
+            ok = false;
+            break;
+          }
+          // The previous item's dK / dV must be read out before this item's first MMAs overwrite them.
+          if (it == 0 && k > 0 && !mbar_wait_bounded(epi_done, (k - 1) & 1, abort_flag, errs, kErrAttnWait, 18)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t q_addr = smem_u32(smem + C::QD_OFF + st * 2 * C::TILE);
+          const uint32_t do_addr = q_addr + C::TILE;
+          const uint32_t dst_addr = smem_u32(smem + C::DST_OFF + b * 128 * 128 * 2);
+          // dV += P^T dO: P^T from tensor memory (query columns 0-63 packed at S^T columns 0-31,
+          // 64-127 at 64-95), dO MN-major
+#pragma unroll
+          for (int ks = 0; ks < 8; ++ks) {
+            const uint32_t a_col = C::T_ST + (ks >> 2) * 64 + (ks & 3) * 8;
+            tc_mma_f16_ts(tmem + C::T_DV, tmem + a_col, smem_desc_sw128(do_addr + ks * 2048, 16384, 1024), ID_KV,
+                          (it > 0 || ks > 0) ? 1u : 0u);
+          }
+          if (it + 1 < n_it && !issue_scores(g + 1)) {
+            ok = false;
+            break;
+          }
+          // dK += dS^T Q (A = dS^T K-major, B = Q MN-major)
+#pragma unroll
+          for (int ks = 0; ks < 8; ++ks) {
+            const uint32_t aoff = (ks >> 2) * 16384 + (ks & 3) * 32;
+            tc_mma_f16(tmem + C::T_DK, smem_desc_sw128(dst_addr + aoff, 16, 1024),
+                       smem_desc_sw128(q_addr + ks * 2048, 16384, 1024), ID_KV, (it > 0 || ks > 0) ? 1u : 0u);
+          }
+          // dQ = dS K into buffer b, once the readout of iteration g - 2 has emptied it
+          if (g >= 2 && !mbar_wait_bounded(&dq_free[b], ((g - 2) >> 1) & 1, abort_flag, errs, kErrAttnWait, 15)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+#pragma unroll
+          for (int ks = 0; ks < 8; ++ks)
+            tc_mma_f16(tmem + C::T_DQ + b * 64, smem_desc_sw128(dst_addr + ks * 2048, 16384, 1024),
+                       smem_desc_sw128(k_addr + ks * 2048, 16384, 1024), ID_Q, ks > 0 ? 1u : 0u);
+          tc_commit(&dq_full[b]);
+          tc_commit(&q_empty[st]);
+        }
+        if (!ok) break;
+        tc_commit(kv_empty);  // K_j / V_j no longer read once this item's MMAs complete
+      }
+    }
+  } else {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(C::REGS_HIGH));
+    const int wg = (warp - 4) >> 2;  // query columns [64*wg, 64*wg + 64) of S^T / dP^T
+    const int q4 = warp & 3;
+    const int r = q4 * 32 + lane;    // kv row for S^T / dK / dV; query row for dQ
+    const int col0 = wg * 64;
+    const uint32_t lane_base = tmem + ((uint32_t)(q4 * 32) << 16);
+    const float scale2 = p.scale * 1.4426950408889634f;
+    uint8_t* stg = smem + C::STG_OFF + (warp - 4) * 2 * kBwdChunk;
+    int g = 0;
+    bool ok = true;
+    // dQ of iteration gq (query block i, head h) -> scaled fp32 TMA add-reductions into dq_acc
+    auto dq_readout = [&](int gq, int h, int i, int row0) -> bool {
+      const int b = gq & 1;
+      if (!mbar_wait_bounded(&dq_full[b], (gq >> 1) & 1, abort_flag, errs, kErrAttnWait, 17)) return false;
+      tc_fence_after();
+      if (lane == 0) bulk_wait_group_read<0>();  // both staging chunks of this warp are free
+      __syncwarp();
+#pragma unroll
+      for (int hc = 0; hc < 2; ++hc) {
+        uint32_t qv[16];
+        tmem_ld_32x32b_x16(lane_base + C::T_DQ + b * 64 + wg * 32 + 16 * hc, qv);
+        tc_wait_ld();
+        uint8_t* buf = stg + hc * kBwdChunk;
+#pragma unroll
+        for (int jj = 0; jj < 4; ++jj) {
+          const int off = lane * 64 + ((jj ^ ((lane >> 1) & 3)) << 4);
+          *reinterpret_cast<float4*>(buf + off) =
+              make_float4(__uint_as_float(qv[4 * jj]) * p.scale, __uint_as_float(qv[4 * jj + 1]) * p.scale,
+                          __uint_as_float(qv[4 * jj + 2]) * p.scale, __uint_as_float(qv[4 * jj + 3]) * p.scale);
+        }
+      }
+      fence_async_smem();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(&dq_free[b]);
+#pragma unroll
+        for (int hc = 0; hc < 2; ++hc)
+          tma_reduce_add_2d(&tm_dq, stg + hc * kBwdChunk, h * HD + wg * 32 + 16 * hc, row0 + i * 128 + q4 * 32);
+        bulk_commit_group();
+      }
+      return true;
+    };
+    for (int k = 0, u; ok && (u = bwd_item_index(k, cta, G, n_items)) >= 0; ++k) {
+      const BwdItem w = bwd_item(u, p.batch, p.kv_heads);
+      const int n_q = n_qb - w.j;
+      const int n_it = group * n_q;
+      const int row0 = w.b * p.seq;
+      for (int it = 0; it < n_it; ++it, ++g) {
+        const int i = w.j + it % n_q;
+        if (!mbar_wait_bounded(st_full, g & 1, abort_flag, errs, kErrAttnWait, 16)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const bool diag = (i == w.j);
+        const float* lds = reinterpret_cast<const float*>(smem + C::LD_OFF + (g % C::STAGES) * 1024);
+        uint8_t* dst = smem + C::DST_OFF + (g & 1) * 128 * 128 * 2;
+        uint32_t ppk[32];  // this thread's 64 bf16 probabilities, packed in pairs
+#pragma unroll
+        for (int c = 0; c < 64; c += 32) {
+          uint32_t sv[32], dpv[32];
+          tmem_ld_32x32b_x32(lane_base + C::T_ST + col0 + c, sv);
+          tmem_ld_32x32b_x32(lane_base + C::T_DPT + col0 + c, dpv);
+          float lse_v[32], del_v[32];  // this chunk's query columns: shared-memory broadcasts, 16 B each
+          const float4* l4 = reinterpret_cast<const float4*>(lds + col0 + c);
+          const float4* d4 = reinterpret_cast<const float4*>(lds + 128 + col0 + c);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            const float4 a = l4[e], dd = d4[e];
+            lse_v[4 * e] = a.x; lse_v[4 * e + 1] = a.y; lse_v[4 * e + 2] = a.z; lse_v[4 * e + 3] = a.w;
+            del_v[4 * e] = dd.x; del_v[4 * e + 1] = dd.y; del_v[4 * e + 2] = dd.z; del_v[4 * e + 3] = dd.w;
+          }
+          tc_wait_ld();
+          if (diag) {  // key row r sees query columns >= r only: masked scores exponentiate to 0
+#pragma unroll
+            for (int e = 0; e < 32; ++e)
+              if (col0 + c + e < r) sv[e] = __float_as_uint(-INFINITY);
+          }
+          uint32_t dk[16];
+#pragma unroll
+          for (int e = 0; e < 32; e += 2) {
+            float pv[2], dv[2];
+#pragma unroll
+            for (int t = 0; t < 2; ++t) {
+              const float x = fmaf(__uint_as_float(sv[e + t]), scale2, -lse_v[e + t]);
+              // (the FMA-pipe exp2 gives 2^-125 for a masked score: nothing at bf16 precision)
+              const float pr = (((e + t) & 7) >= 8 - C::EMU) ? exp2_fma(x) : ex2_approx(x);
+              pv[t] = pr;
+              dv[t] = pr * (__uint_as_float(dpv[e + t]) - del_v[e + t]);
+            }
+            ppk[(c + e) >> 1] = pack_bf16(pv[0], pv[1]);
+            dk[e >> 1] = pack_bf16(dv[0], dv[1]);
+          }
+          store_swizzled_row(dst, r, col0 + c, dk);
+        }
+        // P^T into this warpgroup's already-read S^T columns (packed: 32 columns from col0)
+        tmem_st_32x32b_x32(lane_base + C::T_ST + col0, ppk);
+        tc_wait_st();
+        fence_async_smem();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(p_ready);
+        if (it > 0) {  // dQ of the previous block, read out one iteration late
+          const int ip = w.j + (it - 1) % n_q;
+          const int hp = w.kvh * group + (it - 1) / n_q;
+          if (!dq_readout(g - 1, hp, ip, row0)) {
+            ok = false;
+            break;
+          }
+        }
+      }
+      if (!ok) break;
+      // the item's last dQ, then dK / dV (its last dq_full also covers the final dV / dK MMAs)
+      if (!dq_readout(g - 1, w.kvh * group + (n_it - 1) / n_q, w.j + (n_it - 1) % n_q, row0)) break;
+      const int kv_row = row0 + w.j * 128 + r;
+      const int pos = w.j * 128 + r;
+      constexpr int HALF = HD / 2;
+      constexpr int QTR = HALF / 2;  // RoPE pairs per warpgroup
+      __nv_bfloat16* dk_out = p.dqkv + (size_t)kv_row * p.ld + p.k_col + w.kvh * HD;
+      __nv_bfloat16* dv_out = p.dqkv + (size_t)kv_row * p.ld + p.v_col + w.kvh * HD + wg * HALF;
+      {
+        uint32_t vv[32];
+        tmem_ld_32x32b_x32(lane_base + C::T_DV + wg * HALF, vv);
+        tc_wait_ld();
+#pragma unroll
+        for (int e = 0; e < 32; e += 8) {
+          uint4 o;
+          o.x = pack_bf16(__uint_as_float(vv[e]), __uint_as_float(vv[e + 1]));
+          o.y = pack_bf16(__uint_as_float(vv[e + 2]), __uint_as_float(vv[e + 3]));
+          o.z = pack_bf16(__uint_as_float(vv[e + 4]), __uint_as_float(vv[e + 5]));
+          o.w = pack_bf16(__uint_as_float(vv[e + 6]), __uint_as_float(vv[e + 7]));
+          *reinterpret_cast<uint4*>(dv_out + e) = o;
+        }
+      }
+      {
+        const int c0 = wg * QTR;  // this warpgroup's RoPE pair range [c0, c0 + QTR)
+        uint32_t lo[QTR], hi[QTR];
+        tmem_ld_32x32b_x16(lane_base + C::T_DK + c0, lo);
+        tmem_ld_32x32b_x16(lane_base + C::T_DK + HALF + c0, hi);
+        tc_wait_ld();
+        const float* cs = p.rope_cos + (size_t)pos * HALF + c0;
+        const float* sn = p.rope_sin + (size_t)pos * HALF + c0;
+#pragma unroll
+        for (int e = 0; e < QTR; e += 8) {
+          float a[8], bb[8];
+#pragma unroll
+          for (int t = 0; t < 8; ++t) {
+            const float x0 = __uint_as_float(lo[e + t]) * p.scale;
+            const float x1 = __uint_as_float(hi[e + t]) * p.scale;
+            const float cv = cs[e + t], sv = sn[e + t];
+            a[t] = x0 * cv + x1 * sv;
+            bb[t] = x1 * cv - x0 * sv;
+          }
+          uint4 wa, wb;
+          wa.x = pack_bf16(a[0], a[1]); wa.y = pack_bf16(a[2], a[3]);
+          wa.z = pack_bf16(a[4], a[5]); wa.w = pack_bf16(a[6], a[7]);
+          wb.x = pack_bf16(bb[0], bb[1]); wb.y = pack_bf16(bb[2], bb[3]);
+          wb.z = pack_bf16(bb[4], bb[5]); wb.w = pack_bf16(bb[6], bb[7]);
+          *reinterpret_cast<uint4*>(dk_out + c0 + e) = wa;
+          *reinterpret_cast<uint4*>(dk_out + HALF + c0 + e) = wb;
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(epi_done);
+    }
+    if (lane == 0) bulk_wait_group<0>();
+    __syncwarp();
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, C::TMEM_COLS);
+  }
+}
+
 // delta[b, h, s] = sum_c dO[row, h*hd + c] * O[row, h*hd + c].  One warp per row: lane l takes the
 // 16-byte column groups l, l+32, ...; a head spans hd/8 consecutive groups (8 or 16 lanes), reduced
 // with butterfly shuffles inside that lane group, so every lane loads on every round.
@@ -570,11 +971,17 @@ int bwd_grid(const AttnBwdParams& p) {
   return std::max(1, std::min(items, num_sms_cached()));
 }
 
+// head_dim 64 runs the software-pipelined kernel, 128 the original one.
 template <int HD>
 void launch_bwd(const AttnBwdParams& p, const CUtensorMap& tq, const CUtensorMap& tdo, const CUtensorMap& tdq,
                 DeviceErrors* errs, cudaStream_t s) {
-  using C = AttnBwdCfg<HD>;
-  launch_k(attn_bwd_kernel<HD>, dim3(bwd_grid(p)), dim3(BWD_THREADS), C::SMEM_BYTES, s, 1, tq, tdo, tdq, p, errs);
+  if constexpr (HD == 64) {
+    launch_k(attn_bwd_hd64_kernel, dim3(bwd_grid(p)), dim3(AttnBwd64Cfg::THREADS), AttnBwd64Cfg::SMEM_BYTES, s, 1,
+             tq, tdo, tdq, p, errs);
+  } else {
+    using C = AttnBwdCfg<HD>;
+    launch_k(attn_bwd_kernel<HD>, dim3(bwd_grid(p)), dim3(BWD_THREADS), C::SMEM_BYTES, s, 1, tq, tdo, tdq, p, errs);
+  }
 }
 
 }  // namespace
@@ -590,8 +997,8 @@ void attention_bwd(const AttnBwdParams& p, cudaStream_t s) {
   CUtensorMap tdq = make_dq_map(p);
   static std::atomic<unsigned long long> configured{0};
   once_per_device(configured, [] {
-    B200_CUDA_CHECK(cudaFuncSetAttribute(attn_bwd_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         AttnBwdCfg<64>::SMEM_BYTES));
+    B200_CUDA_CHECK(cudaFuncSetAttribute(attn_bwd_hd64_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         AttnBwd64Cfg::SMEM_BYTES));
     B200_CUDA_CHECK(cudaFuncSetAttribute(attn_bwd_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          AttnBwdCfg<128>::SMEM_BYTES));
   });
@@ -638,7 +1045,7 @@ unsigned char* noalloc_scratch_for_current_device() {
                  cudaGetErrorString(e));
     return nullptr;
   }
-  e = cudaFuncSetAttribute(attn_bwd_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, AttnBwdCfg<64>::SMEM_BYTES);
+  e = cudaFuncSetAttribute(attn_bwd_hd64_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, AttnBwd64Cfg::SMEM_BYTES);
   if (e == cudaSuccess)
     e = cudaFuncSetAttribute(attn_bwd_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              AttnBwdCfg<128>::SMEM_BYTES);

@@ -1,23 +1,37 @@
 // Causal GQA flash-attention forward on the 5th-generation tensor cores (sm_100a).
 //
-// Persistent: one CTA per SM walks a longest-first list of (query block of 128 rows, query head,
-// batch) items, 320 threads:
-//   warp 0      TMA producer: Q once, then K_j / V_j tiles into a STAGES-deep ring.  Q, K and V
-//               are column blocks of the fused [B*S, ld] q|k|v projection output, so one tensor
-//               map serves all three and K/V are never repeated for grouped heads: query head h
-//               reads kv head h / (H / KV).
-//   warp 1      allocates tensor memory; lane 0 issues S_j = Q K_j^T (M=128, N=128, K=hd) into a
-//               double-buffered S accumulator, and O_j = P_j V_j (M=128, N=hd, K=128) into a
-//               double-buffered O accumulator once the softmax warps have written P_j.
-//   warps 2..9  softmax, two warpgroups.  Thread (wg, r) owns query row r and the 64 score columns
-//               [64*wg, 64*wg+64) and the output columns [wg*hd/2, (wg+1)*hd/2).  Row maxima are
-//               combined through shared memory once per block (one named barrier); row sums stay
-//               per warpgroup until the end.  Scores are read from tensor memory, masked only on
-//               the diagonal block, exponentiated with one FFMA + ex2.approx in the base-2 domain,
-//               written as bf16 P in the 128-byte-swizzled K-major layout the MMA reads, and
-//               O_{j-1} is folded into registers with the running rescale factor.
-// The log-sum-exp of every row is stored in base-2 units scaled by log2(e)/sqrt(hd) so the
-// backward pass can rebuild P with one exp2.
+// Persistent: one CTA per SM walks a longest-first list of work items.  An item is a PAIR of
+// query tiles (rows [256p, 256p + 128) = tile A and [256p + 128, 256p + 256) = tile B) of one query
+// head and batch; the two tiles share every key/value tile both need and are processed ping-pong,
+// so the tensor cores work on one tile while the softmax warps work on the other.
+//
+// 384 threads (three warpgroups; the first hands registers to the other two with setmaxnreg):
+//   warp 0      TMA producer: the item's two Q tiles, then K_j / V_j tiles into a STAGES-deep ring.
+//               Q, K and V are column blocks of the fused [B*S, ld] q|k|v projection output, so one
+//               tensor map serves all three and K/V are never repeated for grouped heads: query head
+//               h reads kv head h / (H / KV).
+//   warp 1      allocates the 512 tensor-memory columns; lane 0 issues the MMAs:
+//                 S_t = Q_t K_j^T   (M = 128, N = 128, K = hd; A and B from shared memory)
+//                 O_t += P_t V_j    (M = 128, N = hd, K = 128; A = P_t from TENSOR memory, B = V_j)
+//               in the order S_A(0) S_B(0) | PV_A(j) S_A(j+1) PV_B(j) S_B(j+1) | ..., so while the
+//               softmax warps of tile A work on S_A(j+1), the tensor cores run PV_B(j) and S_B(j+1).
+//   warps 2, 3  idle after set-up.
+//   warps 4..7  softmax of tile A, warps 8..11 softmax of tile B: ONE THREAD PER QUERY ROW.  The thread
+//               reads its row's 128 scores from tensor memory into registers (no cross-thread max
+//               exchange), exponentiates in the base-2 domain (a share of the columns on the FMA pipe
+//               through exp2_fma, the rest on MUFU), writes the bf16 probabilities back into the
+//               same tensor-memory columns (P aliases S: the PV MMA reads them from there), and keeps
+//               the row sum.  The running maximum is raised lazily: O is rescaled (read, scaled and
+//               written back in tensor memory by the same thread) only when a new score exceeds the
+//               maximum in use by more than 2^8, so most blocks skip the correction.
+// At the end of its tile the thread reads O, divides by the row sum and stores bf16; the row's
+// log-sum-exp is stored in base-2 units scaled by log2(e)/sqrt(hd), from which the backward pass
+// rebuilds P with one exp2.
+//
+// Tensor memory: S_A [0,128) | S_B [128,256) | O_A [256, 256+hd) | O_B [256+hd, 256+2hd).
+// Ordering facts used: tcgen05.mma of one thread execute in issue order, so S_t(j+1) (which writes
+// the columns P_t(j) occupies) runs after PV_t(j) has read them, and the commit after S_t(j+1)
+// also covers PV_t(j): a softmax thread that sees S_t(j+1) may read and rescale O_t.
 #include <cuda.h>
 
 #include <algorithm>
@@ -30,75 +44,88 @@ namespace b200 {
 
 namespace {
 
-constexpr int ATT_THREADS = 320;
+constexpr int ATT_THREADS = 384;
+// Register split (setmaxnreg): the launch gives 168 per thread (384 x 168 = 64512); the producer /
+// MMA warpgroup drops to REGS_LOW and the two softmax warpgroups rise to REGS_HIGH, with
+// 128 * REGS_LOW + 256 * REGS_HIGH <= 64512 (checked in AttnFwdCfg).
+constexpr int kLaunchRegs = 168;
 constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kRescaleThreshold = 8.0f;  // log2 units: rescale O only when the max grows by > 2^8
 
 template <int HD>
 struct AttnFwdCfg {
   static constexpr int KB = HD / 64;                 // 64-column swizzle blocks per row
   static constexpr int TILE_BYTES = 128 * HD * 2;    // one 128-row tile of Q, K or V
-  static constexpr int STAGES = (HD == 64) ? 3 : 2;
-  static constexpr int Q_BUFS = (HD == 64) ? 2 : 1;  // the next item's Q loads during this item
-  static constexpr int P_BYTES = 128 * 128 * 2;
-  static constexpr int P_BUFS = (HD == 64) ? 2 : 1;
+  static constexpr int STAGES = (HD == 64) ? 3 : 2;  // K/V ring
+  static constexpr int Q_BUFS = (HD == 64) ? 2 : 1;  // Q pairs: the next item's Q loads during this one
+  // Share of the exponentials done on the FMA pipe: columns c with (c & 7) >= 8 - EMU.  hd 64 is
+  // bound by the MUFU exponential rate; hd 128 by the tensor cores.
+  static constexpr int EMU = (HD == 64) ? 2 : 1;
+  static constexpr int REGS_LOW = (HD == 64) ? 64 : 88;
+  static constexpr int REGS_HIGH = (HD == 64) ? 216 : 208;
+  static_assert(128 * REGS_LOW + 256 * REGS_HIGH <= ATT_THREADS * kLaunchRegs, "register split over budget");
+  // hd 64: the row sums come from the tensor cores.  Each ring stage holds K, V and a 16 KB block of
+  // bf16 ones right after V, so the PV MMA runs with N = hd + 16 over [V | 1] and column hd of O
+  // accumulates sum_k P[r, k] (the same bf16 P that O sums, rescaled with O) - no per-element adds.
+  // hd 128 has no tensor-memory room for the extra columns and adds the sums in registers.
+  static constexpr bool ONES = (HD == 64);
+  static constexpr int O_COLS = ONES ? HD + 16 : HD;  // O columns per tile in tensor memory
+  static constexpr int STAGE_BYTES = (ONES ? 3 : 2) * TILE_BYTES;
   static constexpr int Q_OFF = 0;
-  static constexpr int KV_OFF = Q_BUFS * TILE_BYTES;
-  static constexpr int P_OFF = KV_OFF + STAGES * 2 * TILE_BYTES;
-  static constexpr int RED_OFF = P_OFF + P_BUFS * P_BYTES;  // row-max exchange [2 parity][2 wg][128]
-  static constexpr int BAR_OFF = RED_OFF + 3 * 2 * 128 * 4;
+  static constexpr int KV_OFF = Q_BUFS * 2 * TILE_BYTES;
+  static constexpr int BAR_OFF = KV_OFF + STAGES * STAGE_BYTES;
   static constexpr int SMEM_BYTES = BAR_OFF + 256 + 1024;
+  static_assert(SMEM_BYTES <= 232448, "attention forward shared memory exceeds 227 KB");
   static constexpr int TMEM_COLS = 512;
-  static constexpr int O_TMEM = 256;  // O accumulators start after the two S buffers
-  static constexpr int HALF_O = HD / 2;
+  static constexpr int T_S = 0;      // + 128 * tile
+  static constexpr int T_O = 256;    // + O_COLS * tile
+  static_assert(T_O + 2 * O_COLS <= TMEM_COLS, "attention forward tensor memory");
 };
 
-__device__ __forceinline__ void fence_async_smem() {
-  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-}
-
-// Work items are (query block, head, batch), numbered longest causal row first: item u has query
-// block n_qb - 1 - u / (H * B).  CTA c of G takes items c, 2G - 1 - c, 2G + c, ... (boustrophedon
-// deal), so every CTA's list runs from long to short and the totals even out.
+// Work items are (query-tile pair, head, batch), numbered longest first (pair index n_pairs - 1
+// first).  CTA c of G takes items c, 2G - 1 - c, 2G + c, ... (boustrophedon deal), so every CTA's
+// list runs from long to short and the totals even out.
 struct FwdItem {
-  int qb, h, b;
+  int pair, h, b;
 };
 __device__ __forceinline__ int fwd_item_index(int k, int c, int G, int n_items) {
   const int u = k * G + ((k & 1) ? (G - 1 - c) : c);
   return u < n_items ? u : -1;
 }
-__device__ __forceinline__ FwdItem fwd_item(int u, int n_qb, int heads, int batch) {
+__device__ __forceinline__ FwdItem fwd_item(int u, int n_pairs, int heads, int batch) {
   const int per = heads * batch;
   const int r = u % per;
-  return {n_qb - 1 - u / per, r % heads, r / heads};
+  return {n_pairs - 1 - u / per, r % heads, r / heads};
+}
+// Number of key/value blocks tile t (0 = A, 1 = B) of pair `pair` attends to; 0 if the tile lies
+// past the sequence end (odd number of 128-row blocks).
+__device__ __forceinline__ int tile_kv_blocks(int pair, int t, int n_qb) {
+  const int qb = 2 * pair + t;
+  return qb < n_qb ? qb + 1 : 0;
 }
 
-// Persistent: one CTA per SM walks its item list.  Every barrier phase comes from counters that run
-// across items (g: key/value block, score, probability and PV index; k: item index), so the
-// producer loads the next item's Q and K/V and the MMA warp issues its first score block while the
-// softmax warps still finish the current item.
 template <int HD>
 __global__ void __launch_bounds__(ATT_THREADS, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tm, AttnParams p, DeviceErrors* errs) {
   using C = AttnFwdCfg<HD>;
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* smem = align_smem_1024(smem_raw);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::BAR_OFF);
-  uint64_t* q_full = bars;                    // [Q_BUFS]
-  uint64_t* q_empty = q_full + C::Q_BUFS;     // [Q_BUFS]
+  uint64_t* q_full = bars;                 // [Q_BUFS]
+  uint64_t* q_empty = q_full + C::Q_BUFS;  // [Q_BUFS]
   uint64_t* kv_full = q_empty + C::Q_BUFS;
   uint64_t* kv_empty = kv_full + C::STAGES;
-  uint64_t* s_full = kv_empty + C::STAGES;
-  uint64_t* p_full = s_full + 2;
-  uint64_t* o_full = p_full + 2;
-  uint64_t* o_free = o_full + 2;
-  uint64_t* red_bar = o_free + 2;  // [0..1]: row-max exchange per parity, [2]: final row-sum exchange
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(red_bar + 3);
+  uint64_t* s_full = kv_empty + C::STAGES;  // [2 tiles]
+  uint64_t* p_full = s_full + 2;            // [2 tiles], 4 warps each
+  uint64_t* o_done = p_full + 2;            // [2 tiles]: the tile's last PV of the item completed
+  uint64_t* o_free = o_done + 2;            // [2 tiles], 4 warps: the epilogue has read O
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_free + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  float* red = reinterpret_cast<float*>(smem + C::RED_OFF);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n_qb = p.seq / 128;
-  const int n_items = n_qb * p.heads * p.batch;
+  const int n_pairs = (n_qb + 1) / 2;
+  const int n_items = n_pairs * p.heads * p.batch;
   const int G = gridDim.x, c = blockIdx.x;
   const int group = p.heads / p.kv_heads;
 
@@ -111,13 +138,12 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
       mbar_init(&kv_full[s], 1);
       mbar_init(&kv_empty[s], 1);
     }
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(&s_full[i], 1);
-      mbar_init(&p_full[i], 8);
-      mbar_init(&o_full[i], 1);
-      mbar_init(&o_free[i], 8);
+    for (int t = 0; t < 2; ++t) {
+      mbar_init(&s_full[t], 1);
+      mbar_init(&p_full[t], 4);
+      mbar_init(&o_done[t], 1);
+      mbar_init(&o_free[t], 4);
     }
-    for (int i = 0; i < 3; ++i) mbar_init(&red_bar[i], 8);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -125,41 +151,54 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
     tmem_alloc(tmem_slot, C::TMEM_COLS);
     tmem_relinquish();
   }
+  if constexpr (C::ONES) {  // the ones block after every V tile (never written by TMA)
+    for (int st = 0; st < C::STAGES; ++st) {
+      uint4* ones = reinterpret_cast<uint4*>(smem + C::KV_OFF + st * C::STAGE_BYTES + 2 * C::TILE_BYTES);
+      for (int i = threadIdx.x; i < C::TILE_BYTES / 16; i += ATT_THREADS)
+        ones[i] = make_uint4(0x3F803F80u, 0x3F803F80u, 0x3F803F80u, 0x3F803F80u);
+    }
+    fence_proxy_async_smem();  // generic-proxy writes read by the tensor cores
+  }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   pdl_wait_and_release();  // q|k|v come from the previous kernel of the stream
 
-  if (warp == 0) {
-    if (lane == 0) {
+  if (warp < 4) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(C::REGS_LOW));
+    if (warp == 0 && lane == 0) {
       tma_prefetch_desc(&tm);
-      int g = 0;
+      int g = 0;  // global key/value block counter (ring position)
       bool ok = true;
       for (int k = 0; ok; ++k) {
         const int u = fwd_item_index(k, c, G, n_items);
         if (u < 0) break;
-        const FwdItem it = fwd_item(u, n_qb, p.heads, p.batch);
+        const FwdItem it = fwd_item(u, n_pairs, p.heads, p.batch);
         const int row0 = it.b * p.seq;
         const int kvh = it.h / group;
+        const int nA = tile_kv_blocks(it.pair, 0, n_qb), nB = tile_kv_blocks(it.pair, 1, n_qb);
         const int qs = k % C::Q_BUFS;
-        // The slot's previous Q is free once every score MMA of that item has completed.
+        // The slot's previous Q pair is free once every score MMA of that item has completed.
         if (k >= C::Q_BUFS &&
             !mbar_wait_bounded(&q_empty[qs], ((k / C::Q_BUFS) - 1) & 1, abort_flag, errs, kErrAttnWait, 10))
           break;
-        mbar_expect_tx(&q_full[qs], C::TILE_BYTES);
+        uint8_t* qbase = smem + C::Q_OFF + qs * 2 * C::TILE_BYTES;
+        const int n_tiles = nB > 0 ? 2 : 1;
+        mbar_expect_tx(&q_full[qs], n_tiles * C::TILE_BYTES);
+        for (int t = 0; t < n_tiles; ++t)
 #pragma unroll
-        for (int kb = 0; kb < C::KB; ++kb)
-          tma_load_2d(smem + C::Q_OFF + qs * C::TILE_BYTES + kb * 16384, &tm, &q_full[qs], it.h * HD + 64 * kb,
-                      row0 + it.qb * 128);
-        for (int j = 0; j <= it.qb; ++j, ++g) {
+          for (int kb = 0; kb < C::KB; ++kb)
+            tma_load_2d(qbase + t * C::TILE_BYTES + kb * 16384, &tm, &q_full[qs], it.h * HD + 64 * kb,
+                        row0 + (2 * it.pair + t) * 128);
+        const int nkv = max(nA, nB);
+        for (int j = 0; j < nkv; ++j, ++g) {
           const int st = g % C::STAGES;
-          const uint32_t ph = (g / C::STAGES) & 1;
-          if (!mbar_wait_bounded(&kv_empty[st], ph ^ 1u, abort_flag, errs, kErrAttnWait, 0)) {
+          if (!mbar_wait_bounded(&kv_empty[st], ((g / C::STAGES) & 1) ^ 1u, abort_flag, errs, kErrAttnWait, 0)) {
             ok = false;
             break;
           }
-          uint8_t* ks = smem + C::KV_OFF + st * 2 * C::TILE_BYTES;
+          uint8_t* ks = smem + C::KV_OFF + st * C::STAGE_BYTES;
           uint8_t* vs = ks + C::TILE_BYTES;
           mbar_expect_tx(&kv_full[st], 2 * C::TILE_BYTES);
 #pragma unroll
@@ -169,218 +208,223 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
           }
         }
       }
-    }
-  } else if (warp == 1) {
-    if (lane == 0) {
+    } else if (warp == 1 && lane == 0) {
       constexpr uint32_t IDESC_S = idesc_bf16_f32(128, 128, false, false);
-      constexpr uint32_t IDESC_O = idesc_bf16_f32(128, HD, false, true);
-      // Score MMAs run one block ahead of the PV MMAs, across item boundaries: `sk`/`sj` is the
-      // item / block of the next score block to issue, `sg` its global index.
-      int sk = 0, sj = 0, sg = 0;
-      int s_u = fwd_item_index(0, c, G, n_items);
-      int s_nkv = s_u >= 0 ? fwd_item(s_u, n_qb, p.heads, p.batch).qb + 1 : 0;
-      auto issue_s = [&]() -> bool {
-        const int qs = sk % C::Q_BUFS;
-        if (sj == 0 && !mbar_wait_bounded(&q_full[qs], (sk / C::Q_BUFS) & 1, abort_flag, errs, kErrAttnWait, 2))
-          return false;
-        const int st = sg % C::STAGES;
-        if (!mbar_wait_bounded(&kv_full[st], (sg / C::STAGES) & 1, abort_flag, errs, kErrAttnWait, 1)) return false;
-        tc_fence_after();
-        const uint32_t q_addr = smem_u32(smem + C::Q_OFF + qs * C::TILE_BYTES);
-        const uint32_t k_addr = smem_u32(smem + C::KV_OFF + st * 2 * C::TILE_BYTES);
+      constexpr uint32_t IDESC_O = idesc_bf16_f32(128, C::O_COLS, false, true);
+      int g = 0;             // global key/value block counter
+      int pn[2] = {0, 0};    // P handed over per tile (p_full phases)
+      int on[2] = {0, 0};    // items finished per tile (o_done / o_free phases)
+      bool ok = true;
+      for (int k = 0; ok; ++k) {
+        const int u = fwd_item_index(k, c, G, n_items);
+        if (u < 0) break;
+        const FwdItem it = fwd_item(u, n_pairs, p.heads, p.batch);
+        const int n[2] = {tile_kv_blocks(it.pair, 0, n_qb), tile_kv_blocks(it.pair, 1, n_qb)};
+        const int nkv = max(n[0], n[1]);
+        const int qs = k % C::Q_BUFS;
+        const uint32_t q_addr = smem_u32(smem + C::Q_OFF + qs * 2 * C::TILE_BYTES);
+        if (!mbar_wait_bounded(&q_full[qs], (k / C::Q_BUFS) & 1, abort_flag, errs, kErrAttnWait, 2)) break;
+        // S_t = Q_t K^T for the K tile in ring stage st
+        auto issue_s = [&](int t, int st) {
+          const uint32_t qa = q_addr + t * C::TILE_BYTES;
+          const uint32_t ka = smem_u32(smem + C::KV_OFF + st * C::STAGE_BYTES);
 #pragma unroll
-        for (int ks = 0; ks < HD / 16; ++ks) {
-          const uint32_t off = (ks >> 2) * 16384 + (ks & 3) * 32;
-          tc_mma_f16(tmem + (sg & 1) * 128, smem_desc_sw128(q_addr + off, 16, 1024),
-                     smem_desc_sw128(k_addr + off, 16, 1024), IDESC_S, ks > 0 ? 1u : 0u);
-        }
-        tc_commit(&s_full[sg & 1]);
-        ++sg;
-        if (++sj == s_nkv) {  // last score block of this item: its Q slot frees when these MMAs finish
-          tc_commit(&q_empty[qs]);
-          ++sk;
-          sj = 0;
-          s_u = fwd_item_index(sk, c, G, n_items);
-          s_nkv = s_u >= 0 ? fwd_item(s_u, n_qb, p.heads, p.batch).qb + 1 : 0;
-        }
-        return true;
-      };
-      bool ok = s_u < 0 || issue_s();
-      // PV of global block g, after the score block g + 1 has been issued (if there is one).
-      for (int g = 0; ok && g < sg; ++g) {
-        if (s_u >= 0 && !issue_s()) break;
-        if (!mbar_wait_bounded(&p_full[g & 1], (g >> 1) & 1, abort_flag, errs, kErrAttnWait, 3)) break;
-        if (g >= 2 && !mbar_wait_bounded(&o_free[g & 1], ((g - 2) >> 1) & 1, abort_flag, errs, kErrAttnWait, 4)) break;
+          for (int ks = 0; ks < HD / 16; ++ks) {
+            const uint32_t off = (ks >> 2) * 16384 + (ks & 3) * 32;
+            tc_mma_f16(tmem + C::T_S + t * 128, smem_desc_sw128(qa + off, 16, 1024),
+                       smem_desc_sw128(ka + off, 16, 1024), IDESC_S, ks > 0 ? 1u : 0u);
+          }
+          tc_commit(&s_full[t]);
+        };
+        int st = g % C::STAGES;
+        if (!mbar_wait_bounded(&kv_full[st], (g / C::STAGES) & 1, abort_flag, errs, kErrAttnWait, 1)) break;
         tc_fence_after();
-        const int st = g % C::STAGES;
-        const uint32_t v_addr = smem_u32(smem + C::KV_OFF + st * 2 * C::TILE_BYTES + C::TILE_BYTES);
-        const uint32_t p_addr = smem_u32(smem + C::P_OFF + (g % C::P_BUFS) * C::P_BYTES);
 #pragma unroll
-        for (int ks = 0; ks < 8; ++ks) {
-          const uint32_t poff = (ks >> 2) * 16384 + (ks & 3) * 32;
-          tc_mma_f16(tmem + C::O_TMEM + (g & 1) * HD, smem_desc_sw128(p_addr + poff, 16, 1024),
-                     smem_desc_sw128(v_addr + ks * 2048, 16384, 1024), IDESC_O, ks > 0 ? 1u : 0u);
+        for (int t = 0; t < 2; ++t)
+          if (n[t] > 0) issue_s(t, st);
+        for (int j = 0; ok && j < nkv; ++j) {
+          st = (g + j) % C::STAGES;
+          const int st1 = (g + j + 1) % C::STAGES;
+          bool next_loaded = false;
+#pragma unroll
+          for (int t = 0; t < 2; ++t) {
+            if (!ok) break;
+            if (j >= n[t]) continue;
+            if (!mbar_wait_bounded(&p_full[t], pn[t] & 1, abort_flag, errs, kErrAttnWait, 3 + t)) {
+              ok = false;
+              break;
+            }
+            ++pn[t];
+            // the tile's first PV of this item overwrites O_t: the previous item's epilogue must have read it
+            if (j == 0 && on[t] > 0 &&
+                !mbar_wait_bounded(&o_free[t], (on[t] - 1) & 1, abort_flag, errs, kErrAttnWait, 5 + t)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            // O_t (+)= P_t V_j; P_t is read from tile t's S columns
+            const uint32_t va = smem_u32(smem + C::KV_OFF + st * C::STAGE_BYTES + C::TILE_BYTES);
+#pragma unroll
+            for (int ks = 0; ks < 8; ++ks)
+              tc_mma_f16_ts(tmem + C::T_O + t * C::O_COLS, tmem + C::T_S + t * 128 + ks * 8,
+                            smem_desc_sw128(va + ks * 2048, 16384, 1024), IDESC_O, (j == 0 && ks == 0) ? 0u : 1u);
+            if (j + 1 == n[t]) {
+              tc_commit(&o_done[t]);
+              ++on[t];
+            } else {
+              if (!next_loaded) {
+                if (!mbar_wait_bounded(&kv_full[st1], ((g + j + 1) / C::STAGES) & 1, abort_flag, errs,
+                                       kErrAttnWait, 1)) {
+                  ok = false;
+                  break;
+                }
+                next_loaded = true;
+                tc_fence_after();
+              }
+              issue_s(t, st1);
+            }
+          }
+          if (!ok) break;
+          tc_commit(&kv_empty[st]);  // K_j / V_j free once this block's MMAs have completed
         }
-        tc_commit(&o_full[g & 1]);
-        tc_commit(&kv_empty[st]);
+        g += nkv;
+        tc_commit(&q_empty[qs]);  // every score MMA of the item has been issued
       }
     }
   } else {
-    const int wg = (warp - 2) >> 2;   // warpgroup: score columns [64*wg, 64*wg+64)
-    const int q = warp & 3;            // tensor-memory lane quarter
-    const int r = q * 32 + lane;       // query row within the block
-    const int col0 = wg * 64;
-    const int ocol0 = wg * C::HALF_O;
-    const uint32_t lane_base = tmem + ((uint32_t)(q * 32) << 16);
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(C::REGS_HIGH));
+    // softmax: tile t, query row r of the tile
+    const int t = (warp - 4) >> 2;
+    const int quarter = warp & 3;
+    const int r = quarter * 32 + lane;
+    const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+    const uint32_t s_cols = tmem + lane_off + C::T_S + t * 128;
+    const uint32_t o_cols = tmem + lane_off + C::T_O + t * C::O_COLS;
     const float scale2 = p.scale * kLog2e;
-    int g = 0;
-    bool ok = true;
-    for (int k = 0; ok; ++k) {
+    int sn = 0, on = 0;
+    for (int k = 0;; ++k) {
       const int u = fwd_item_index(k, c, G, n_items);
       if (u < 0) break;
-      const FwdItem it = fwd_item(u, n_qb, p.heads, p.batch);
-      const int n_kv = it.qb + 1;
-      const int row0 = it.b * p.seq;
-      float m = -INFINITY, l = 0.f;
-      float o[C::HALF_O];
-#pragma unroll
-      for (int i = 0; i < C::HALF_O; ++i) o[i] = 0.f;
-      for (int j = 0; j < n_kv; ++j, ++g) {
-        if (!mbar_wait_bounded(&s_full[g & 1], (g >> 1) & 1, abort_flag, errs, kErrAttnWait, 5)) {
+      const FwdItem it = fwd_item(u, n_pairs, p.heads, p.batch);
+      const int n = tile_kv_blocks(it.pair, t, n_qb);
+      if (n == 0) continue;  // tile past the end of the sequence
+      float m_used = 0.f, l = 0.f;
+      bool ok = true;
+      for (int j = 0; j < n; ++j) {
+        if (!mbar_wait_bounded(&s_full[t], sn & 1, abort_flag, errs, kErrAttnWait, 11 + t)) {
           ok = false;
           break;
         }
+        ++sn;
         tc_fence_after();
-        const uint32_t sbase = lane_base + (g & 1) * 128 + col0;
-        const bool diag = (j == it.qb);
-        // pass 1: partial row max of the raw scores over this warpgroup's 64 columns
-        float pmx = -INFINITY;
+        uint32_t s[4][32];  // the row's 128 scores (fp32 bits), later its 64 bf16 pairs of P
 #pragma unroll
-        for (int cc = 0; cc < 64; cc += 32) {
-          uint32_t sv[32];
-          tmem_ld_32x32b_x32(sbase + cc, sv);
-          tc_wait_ld();
-          if (diag) {
+        for (int q4 = 0; q4 < 4; ++q4) tmem_ld_32x32b_x32(s_cols + 32 * q4, s[q4]);
+        tc_wait_ld();
+        const bool diag = (j == n - 1);  // key block == query block: mask columns past the row
+        if (diag) {  // masked scores become -inf: they drop out of the max and exponentiate to 0
 #pragma unroll
-            for (int e = 0; e < 32; ++e)
-              if (col0 + cc + e <= r) pmx = fmaxf(pmx, __uint_as_float(sv[e]));
-          } else {
-#pragma unroll
-            for (int e = 0; e < 32; ++e) pmx = fmaxf(pmx, __uint_as_float(sv[e]));
-          }
+          for (int e = 0; e < 128; ++e)
+            if (e > r) s[e >> 5][e & 31] = __float_as_uint(-INFINITY);
         }
-        float* red_slot = red + (g & 1) * 256;
-        red_slot[wg * 128 + r] = pmx;
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&red_bar[g & 1]);
-        if (!mbar_wait_bounded(&red_bar[g & 1], (g >> 1) & 1, abort_flag, errs, kErrAttnWait, 8)) {
-          ok = false;
-          break;
-        }
-        const float other = red_slot[(wg ^ 1) * 128 + r];
-        const float mx = fmaxf(m, fmaxf(pmx, other) * scale2);  // scaled, base-2 domain
-        const float alpha = ex2_approx(m - mx);
-        // P buffer reuse: PV_{g-1} must have finished reading it (and PV_{g-2}, folded at g - 1).
-        if (j >= 1 &&
-            !mbar_wait_bounded(&o_full[(g - 1) & 1], ((g - 1) >> 1) & 1, abort_flag, errs, kErrAttnWait, 6)) {
-          ok = false;
-          break;
-        }
-        // pass 2: probabilities, partial row sum, bf16 P into swizzled shared memory
-        uint8_t* pbuf = smem + C::P_OFF + (g % C::P_BUFS) * C::P_BYTES;
-        float rs = 0.f;
+        // row max: 8 independent chains of three-input maxes (one chain would serialise 128 ops)
+        float mx8[8];
 #pragma unroll
-        for (int cc = 0; cc < 64; cc += 32) {
-          uint32_t sv[32];
-          tmem_ld_32x32b_x32(sbase + cc, sv);
-          tc_wait_ld();
-          uint32_t pk[16];
+        for (int e = 0; e < 8; ++e) mx8[e] = __uint_as_float(s[0][e]);
 #pragma unroll
-          for (int e = 0; e < 32; e += 2) {
-            float p0 = ex2_approx(fmaf(__uint_as_float(sv[e]), scale2, -mx));
-            float p1 = ex2_approx(fmaf(__uint_as_float(sv[e + 1]), scale2, -mx));
-            if (diag) {
-              if (col0 + cc + e > r) p0 = 0.f;
-              if (col0 + cc + e + 1 > r) p1 = 0.f;
-            }
-            rs += p0 + p1;
-            pk[e >> 1] = pack_bf16(p0, p1);
-          }
-          const int col = col0 + cc;
-          const int kblk = col >> 6;
+        for (int e = 8; e < 128; e += 2)
+          mx8[(e >> 1) & 7] = fmax3f(mx8[(e >> 1) & 7], __uint_as_float(s[e >> 5][e & 31]),
+                                     __uint_as_float(s[e >> 5][(e + 1) & 31]));
+        const float mx = fmax3f(fmax3f(mx8[0], mx8[1], mx8[2]), fmax3f(mx8[3], mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7]));
+        const float m_row = mx * scale2;
+        if (j == 0) {
+          m_used = m_row;
+        } else if (m_row > m_used + kRescaleThreshold) {
+          // O_t holds the sum up to block j-1 (complete: the commit of S_t(j) covers PV_t(j-1)).
+          const float alpha = ex2_approx(m_used - m_row);
+          l *= alpha;
 #pragma unroll
-          for (int ch = 0; ch < 4; ++ch) {
-            const int chunk = ((col & 63) >> 3) + ch;  // 16-byte chunk within the 128-byte row
-            const int sw = chunk ^ (r & 7);
-            *reinterpret_cast<uint4*>(pbuf + kblk * 16384 + r * 128 + sw * 16) =
-                make_uint4(pk[4 * ch], pk[4 * ch + 1], pk[4 * ch + 2], pk[4 * ch + 3]);
-          }
-        }
-        l = l * alpha + rs;
-        fence_async_smem();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&p_full[g & 1]);
-        if (j >= 1) {
-          tc_fence_after();
-          const uint32_t obase = lane_base + C::O_TMEM + ((g - 1) & 1) * HD + ocol0;
-#pragma unroll
-          for (int cc = 0; cc < C::HALF_O; cc += 32) {
+          for (int cc = 0; cc < HD; cc += 32) {
             uint32_t ov[32];
-            tmem_ld_32x32b_x32(obase + cc, ov);
+            tmem_ld_32x32b_x32(o_cols + cc, ov);
             tc_wait_ld();
 #pragma unroll
-            for (int e = 0; e < 32; ++e) o[cc + e] = (o[cc + e] + __uint_as_float(ov[e])) * alpha;
+            for (int e = 0; e < 32; ++e) ov[e] = __float_as_uint(__uint_as_float(ov[e]) * alpha);
+            tmem_st_32x32b_x32(o_cols + cc, ov);
           }
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&o_free[(g - 1) & 1]);
-        } else {
+          if constexpr (C::ONES) {  // the row-sum columns scale with O
+            uint32_t lv[16];
+            tmem_ld_32x32b_x16(o_cols + HD, lv);
+            tc_wait_ld();
 #pragma unroll
-          for (int i = 0; i < C::HALF_O; ++i) o[i] *= alpha;
+            for (int e = 0; e < 16; ++e) lv[e] = __float_as_uint(__uint_as_float(lv[e]) * alpha);
+            tmem_st_32x32b_x16(o_cols + HD, lv);
+          }
+          m_used = m_row;
         }
-        m = mx;
+        // probabilities, row sum (8 chains), bf16 P into the same tensor-memory columns.  A masked
+        // score is -inf: ex2 gives 0 and the FMA-pipe exp2 gives 2^-125 (its input is clamped), which
+        // is no contribution at fp32 / bf16 precision next to the row maximum's 1.
+        float rs8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int e = 0; e < 128; e += 2) {
+          const float x0 = fmaf(__uint_as_float(s[e >> 5][e & 31]), scale2, -m_used);
+          const float x1 = fmaf(__uint_as_float(s[e >> 5][(e + 1) & 31]), scale2, -m_used);
+          const float p0 = ((e & 7) >= 8 - C::EMU) ? exp2_fma(x0) : ex2_approx(x0);
+          const float p1 = (((e + 1) & 7) >= 8 - C::EMU) ? exp2_fma(x1) : ex2_approx(x1);
+          if constexpr (!C::ONES) {
+            rs8[e & 7] += p0;
+            rs8[(e + 1) & 7] += p1;
+          }
+          s[e >> 6][(e >> 1) & 31] = pack_bf16(p0, p1);  // pair e/2 lands below column e: already read
+        }
+        if constexpr (!C::ONES) l += ((rs8[0] + rs8[1]) + (rs8[2] + rs8[3])) + ((rs8[4] + rs8[5]) + (rs8[6] + rs8[7]));
+        tmem_st_32x32b_x32(s_cols + 0, s[0]);
+        tmem_st_32x32b_x32(s_cols + 32, s[1]);
+        tc_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&p_full[t]);
       }
       if (!ok) break;
-      // Combine the two warpgroups' partial row sums (the slot is reused per item: both
-      // warpgroups pass the next item's first row-max exchange before either writes it again).
-      float* lred = red + 512;
-      lred[wg * 128 + r] = l;
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&red_bar[2]);
-      if (!mbar_wait_bounded(&red_bar[2], k & 1, abort_flag, errs, kErrAttnWait, 9)) break;
-      const float l_total = l + lred[(wg ^ 1) * 128 + r];
-      const int gl = g - 1;  // global index of this item's last block
-      if (!mbar_wait_bounded(&o_full[gl & 1], (gl >> 1) & 1, abort_flag, errs, kErrAttnWait, 7)) break;
+      // epilogue: O / l -> bf16 rows, base-2 log-sum-exp
+      if (!mbar_wait_bounded(&o_done[t], on & 1, abort_flag, errs, kErrAttnWait, 13 + t)) break;
+      ++on;
       tc_fence_after();
-      const uint32_t obase = lane_base + C::O_TMEM + (gl & 1) * HD + ocol0;
-      const float inv_l = 1.0f / l_total;
-      const size_t out_idx = (size_t)(row0 + it.qb * 128 + r) * p.ld_out + it.h * HD + ocol0;
-      __nv_bfloat16* dst = p.out + out_idx;
-      const bool out_in =
-          B200_IN_BOUNDS(errs, out_idx, C::HALF_O, (long long)p.batch * p.seq * p.ld_out, 120);
-#pragma unroll
-      for (int cc = 0; cc < C::HALF_O; cc += 32) {
-        uint32_t ov[32];
-        tmem_ld_32x32b_x32(obase + cc, ov);
+      const int q_row = (2 * it.pair + t) * 128 + r;
+      if constexpr (C::ONES) {  // the row sum accumulated by the tensor cores
+        uint32_t lv[16];
+        tmem_ld_32x32b_x16(o_cols + HD, lv);
         tc_wait_ld();
+        l = __uint_as_float(lv[0]);
+      }
+      const float inv_l = 1.0f / l;
+      const size_t out_idx = (size_t)(it.b * p.seq + q_row) * p.ld_out + it.h * HD;
+      __nv_bfloat16* dst = p.out + out_idx;
+      const bool out_in = B200_IN_BOUNDS(errs, out_idx, HD, (long long)p.batch * p.seq * p.ld_out, 120);
+#pragma unroll
+      for (int cc = 0; cc < HD; cc += 32) {
+        uint32_t ov[32];
+        tmem_ld_32x32b_x32(o_cols + cc, ov);
+        tc_wait_ld();
+        if (cc + 32 >= HD) {  // every column read: O_t may be overwritten by the next item
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&o_free[t]);
+        }
 #pragma unroll
         for (int e = 0; e < 32; e += 8) {
           uint4 w;
-          w.x = pack_bf16((o[cc + e] + __uint_as_float(ov[e])) * inv_l, (o[cc + e + 1] + __uint_as_float(ov[e + 1])) * inv_l);
-          w.y = pack_bf16((o[cc + e + 2] + __uint_as_float(ov[e + 2])) * inv_l, (o[cc + e + 3] + __uint_as_float(ov[e + 3])) * inv_l);
-          w.z = pack_bf16((o[cc + e + 4] + __uint_as_float(ov[e + 4])) * inv_l, (o[cc + e + 5] + __uint_as_float(ov[e + 5])) * inv_l);
-          w.w = pack_bf16((o[cc + e + 6] + __uint_as_float(ov[e + 6])) * inv_l, (o[cc + e + 7] + __uint_as_float(ov[e + 7])) * inv_l);
+          w.x = pack_bf16(__uint_as_float(ov[e]) * inv_l, __uint_as_float(ov[e + 1]) * inv_l);
+          w.y = pack_bf16(__uint_as_float(ov[e + 2]) * inv_l, __uint_as_float(ov[e + 3]) * inv_l);
+          w.z = pack_bf16(__uint_as_float(ov[e + 4]) * inv_l, __uint_as_float(ov[e + 5]) * inv_l);
+          w.w = pack_bf16(__uint_as_float(ov[e + 6]) * inv_l, __uint_as_float(ov[e + 7]) * inv_l);
           if (out_in) *reinterpret_cast<uint4*>(dst + cc + e) = w;
         }
       }
-      // The last O buffer of the item is free for the PV two blocks later.
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&o_free[gl & 1]);
-      const size_t lse_idx = ((size_t)it.b * p.heads + it.h) * p.seq + it.qb * 128 + r;
-      if (wg == 0 && B200_IN_BOUNDS(errs, lse_idx, 1, (long long)p.batch * p.heads * p.seq, 121))
-        p.lse[lse_idx] = m + log2f(l_total);
+      const size_t lse_idx = ((size_t)it.b * p.heads + it.h) * p.seq + q_row;
+      if (B200_IN_BOUNDS(errs, lse_idx, 1, (long long)p.batch * p.heads * p.seq, 121))
+        p.lse[lse_idx] = m_used + log2f(l);
     }
   }
 
@@ -399,7 +443,8 @@ void launch_fwd(const AttnParams& p, const CUtensorMap& tm, cudaStream_t s) {
   once_per_device(configured, [] {
     B200_CUDA_CHECK(cudaFuncSetAttribute(attn_fwd_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES));
   });
-  const int items = (p.seq / 128) * p.heads * p.batch;
+  const int n_qb = p.seq / 128;
+  const int items = ((n_qb + 1) / 2) * p.heads * p.batch;
   const int grid = std::max(1, std::min(items, num_sms_cached()));
   launch_k(attn_fwd_kernel<HD>, dim3(grid), dim3(ATT_THREADS), C::SMEM_BYTES, s, 1, tm, p, device_errors_ptr());
 }

@@ -171,7 +171,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   static_assert(CG == 1 || !B_MN || (BN / 2) % 64 == 0, "pair tiles with an MN-major B need BN/2 % 64 == 0");
 
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* smem = align_smem_1024(smem_raw);
   uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + STAGES * Cfg::STAGE_BYTES + Cfg::STAGING_BYTES);
   uint64_t* empty_bar = full_bar + STAGES;
   uint64_t* tfull_bar = empty_bar + STAGES;

@@ -32,7 +32,7 @@ __device__ __forceinline__ float warp_max(float v) {
 struct AdamArgs {
   float lr, beta1, beta2, eps, wd;
   float one_minus_b1, one_minus_b2;
-  float inv_bc1, inv_sqrt_bc2;
+  float step_size, inv_sqrt_bc2;  // lr / (1 - beta1^t) and 1 / sqrt(1 - beta2^t)
 };
 
 template <bool BF16_OUT>
@@ -43,7 +43,7 @@ __global__ void adamw_kernel(float* __restrict__ master, float* __restrict__ m, 
   pdl_wait_and_release();
   const float scale = (scale_ptr != nullptr ? *scale_ptr : 1.0f) * scale_const;
   const float decay = 1.0f - a.lr * a.wd;
-  const float step = dev_sc != nullptr ? dev_sc[0] : a.lr * a.inv_bc1;
+  const float step = dev_sc != nullptr ? dev_sc[0] : a.step_size;
   if (dev_sc != nullptr) a.inv_sqrt_bc2 = dev_sc[1];
   const size_t n4 = n / 4;
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n4; i += (size_t)gridDim.x * blockDim.x) {
@@ -240,12 +240,15 @@ __global__ void finalize_loss_kernel(const float* loss_sum, const float* count, 
 }
 
 // Advances the device step counter and writes the bias-corrected scalars for it (one thread).
+// The scalars are computed in double and rounded once to float, exactly as the host computes them
+// for a host-side step number (adam_step_size / adam_inv_sqrt_bc2), so a captured step replays with
+// the bits of the eager step.
 __global__ void adam_advance_kernel(int* step_count, float* dev_sc, float lr, float beta1, float beta2) {
   if (threadIdx.x != 0 || blockIdx.x != 0) return;
   const int t = step_count[0] + 1;
   step_count[0] = t;
-  dev_sc[0] = lr / (1.0f - powf(beta1, (float)t));
-  dev_sc[1] = 1.0f / sqrtf(1.0f - powf(beta2, (float)t));
+  dev_sc[0] = (float)((double)lr / (1.0 - pow((double)beta1, (double)t)));
+  dev_sc[1] = (float)(1.0 / sqrt(1.0 - pow((double)beta2, (double)t)));
 }
 
 }  // namespace
@@ -272,7 +275,7 @@ void adamw_step(float* master, float* m, float* v, const float* g, void* param_o
   a.wd = wd;
   a.one_minus_b1 = 1.0f - beta1;
   a.one_minus_b2 = 1.0f - beta2;
-  a.inv_bc1 = (float)(1.0 / (1.0 - std::pow((double)beta1, (double)step)));
+  a.step_size = (float)((double)lr / (1.0 - std::pow((double)beta1, (double)step)));
   a.inv_sqrt_bc2 = (float)(1.0 / std::sqrt(1.0 - std::pow((double)beta2, (double)step)));
   const int threads = 256;
   const size_t work = std::max<size_t>(1, n / 4);

@@ -86,8 +86,35 @@ def test_bench_roofline_entry():
     cfg = build_config("baseline-small", vocab_size=32000, max_seq_len=1024)
     sess = types.SimpleNamespace(model_cfg=cfg, engine=types.SimpleNamespace(recompute=False))
     args = bench.parse_args(["--batch-size", "8", "--seq-len", "1024"])
-    e = bench.roofline_entry(sess, args, 2, 10.0, 1400.0)
+    assert args.extra_list == ["baseline-1.3b"] and set(args.extra_list) <= set(bench.CONFIG_SHAPES)
+    e = bench.roofline_entry(sess, 8, 1024, 2, 10.0, 1400.0)
     flops = executed_train_flops(cfg, 8, 1024)
     assert abs(e["executed_tflops_per_gpu"] - flops / 0.01 / 1e12) < 1e-6
     assert abs(e["roofline_fraction"] - flops / 0.01 / 1.4e15) < 1e-9
     assert 0.3 < e["roofline_fraction"] < 0.8  # ~5.4 TFLOP in 10 ms on a 1.4 PFLOP/s part
+
+
+def test_bench_config_shapes_match_the_presets():
+    sys.path.insert(0, str(ROOT))
+    try:
+        import bench
+    finally:
+        sys.path.pop(0)
+    from cs244c_llama_zero_b200.models import build_config
+
+    for size, shape in bench.CONFIG_SHAPES.items():
+        cfg = build_config(size, vocab_size=32000, max_seq_len=shape["seq"])
+        for key in ("dim", "n_layers", "n_heads", "n_kv_heads", "ffn_dim"):
+            assert getattr(cfg, key) == shape[key], (size, key)
+
+
+def test_clock_sampler_summary_from_samples():
+    sys.path.insert(0, str(ROOT))
+    try:
+        import bench
+    finally:
+        sys.path.pop(0)
+    cs = bench.ClockSampler([0])
+    cs.samples = [(0, 1965.0, 1965.0, []), (0, 1900.0, 1965.0, ["sw_power_cap"]), (0, 300.0, 1965.0, [])]
+    s = cs.summary()
+    assert s["sm_mhz"] == 1932.5 and s["sm_max_mhz"] == 1965.0 and s["reasons"] == ["sw_power_cap"]

@@ -28,6 +28,7 @@ def test_graph_replay_trains_like_eager(stage):
     pair = [torch.randint(0, 1024, (2, 256), generator=g) for _ in range(2)]
     batches = [pair[i % 2] for i in range(7)]
     eager = _session(stage, False)
+    init = eager.engine.master_params.detach().clone()
     want = [float(eager.train_step(b)) for b in batches]
     graphed = _session(stage, True)
     got = []
@@ -39,7 +40,15 @@ def test_graph_replay_trains_like_eager(stage):
     assert graphed._graph is not None
     assert graphed.engine.step_count == eager.engine.step_count == len(batches)
     torch.testing.assert_close(torch.tensor(got), torch.tensor(want), rtol=2e-3, atol=2e-3)
-    torch.testing.assert_close(graphed.engine.master_params, eager.engine.master_params, rtol=1e-3, atol=1e-5)
+    # Training in bf16 is chaotic at the rounding level: one fp32 rounding difference (the order of the
+    # fp32 atomic accumulations in the embedding, RMSNorm and split-K weight-gradient kernels differs from
+    # run to run) eventually flips the bf16 rounding of a weight, and from then on two runs drift apart by
+    # up to ~2e-4 per weight after 7 steps at lr 1e-3 - two eager runs as much as eager and graph.  A
+    # replay bug (stale input, wrong step number or bias correction, gradients not cleared) changes the
+    # updates themselves, so the drift is measured against the size of the whole update.
+    drift = (graphed.engine.master_params - eager.engine.master_params).norm().item()
+    update = (eager.engine.master_params - init).norm().item()
+    assert update > 0 and drift <= 0.05 * update, f"graph vs eager drift {drift:.3e} vs update {update:.3e}"
     assert got[-1] < got[0] and got[-2] < got[1]
     ops.check_device_errors()
     graphed.reset_graph()  # the next step captures again
