@@ -75,8 +75,8 @@ def parse_args(argv=None) -> argparse.Namespace:
 class ClockSampler:
     """Samples SM clocks and clock-event (throttle) reasons while the timed region runs.
 
-    Through NVML every 5 ms on a background thread when the ``pynvml`` bindings load (a 20-step
-    region of ~9 ms steps still gets dozens of samples), else through ``nvidia-smi -lms 100``.
+    Through ``nvidia-smi -lms 50`` (default), or with ``ZB_CLOCK_SAMPLER=nvml`` through NVML every
+    5 ms on a background thread (a 20-step region of ~9 ms steps then gets dozens of samples).
     """
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
@@ -115,6 +115,8 @@ class ClockSampler:
         import threading
 
         try:
+            if os.environ.get("ZB_CLOCK_SAMPLER", "smi") != "nvml":
+                raise RuntimeError("nvidia-smi sampler selected")
             import pynvml as nvml
 
             nvml.nvmlInit()
@@ -136,7 +138,7 @@ class ClockSampler:
             os.makedirs(os.path.dirname(self.path), exist_ok=True)
             self.fh = open(self.path, "w")
             self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                                          "-lms", "100"], stdout=self.fh, stderr=subprocess.DEVNULL)
+                                          "-lms", "50"], stdout=self.fh, stderr=subprocess.DEVNULL)
         except (OSError, FileNotFoundError):
             self.proc = None
         return self
@@ -263,6 +265,12 @@ def random_batches(n: int, batch: int, seq: int, vocab: int, seed: int):
     return [torch.randint(0, vocab, (batch, seq), generator=g, dtype=torch.long).pin_memory() for _ in range(n)]
 
 
+def progress(rank: int, msg: str) -> None:
+    """One timestamped line on stderr per phase (the JSON result goes to stdout at the end)."""
+    if rank == 0:
+        print(f"[bench {time.strftime('%H:%M:%S')}] {msg}", file=sys.stderr, flush=True)
+
+
 def emit(record: dict, rank: int) -> None:
     if rank == 0:
         print(json.dumps(record), flush=True)
@@ -310,6 +318,7 @@ def _measure_stages(args, size: str, batch: int, seq: int, world: int, rank: int
     out = {"per_stage": {}, "e2e": None, "launches": None, "clocks": None, "headline_ms": None}
     tokens_per_step = batch * seq * world
     for stage in args.stage_list:
+        progress(rank, f"{size} stage {stage}: building (B{batch} S{seq})")
         sess = TrainSession(SessionConfig(model_size=size, vocab_size=BASELINE_VOCAB_SIZE,
                                           seq_len=seq, batch_size=batch, zero_stage=stage,
                                           collective_impl=impl, backend="b200",
@@ -331,8 +340,10 @@ def _measure_stages(args, size: str, batch: int, seq: int, world: int, rank: int
         for _ in range(args.warmup):
             device_step()
         torch.cuda.synchronize()
+        progress(rank, f"{size} stage {stage}: warm-up done")
         launches_before = ops.launch_count()
         ms = time_device(device_step, args.steps)
+        progress(rank, f"{size} stage {stage}: {ms:.3f} ms/step")
         if sampler:
             sampler.__exit__(None, None, None)
             out["clocks"] = sampler.summary()

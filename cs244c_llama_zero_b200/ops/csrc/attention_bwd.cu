@@ -26,6 +26,7 @@
 #include <cuda.h>
 
 #include <cstdio>
+#include <cstdlib>
 #include <mutex>
 
 #include "attention_bwd_noalloc.h"
@@ -512,9 +513,10 @@ struct AttnBwd64Cfg {
   static constexpr int TMEM_COLS = 512;
   static constexpr int THREADS = 384;
   static constexpr int REGS_LOW = 64, REGS_HIGH = 216;  // 128 * 64 + 256 * 216 <= 384 * 168
-  static constexpr int EMU = 2;  // exponentials on the FMA pipe: columns with (c & 7) >= 8 - EMU
+  static constexpr int EMU = 0;  // exponentials on the FMA pipe: columns with (c & 7) >= 8 - EMU (0 measured fastest)
 };
 
+template <int EMU>
 __global__ void __launch_bounds__(AttnBwd64Cfg::THREADS, 1)
     attn_bwd_hd64_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __grid_constant__ CUtensorMap tm_do,
                          const __grid_constant__ CUtensorMap tm_dq, AttnBwdParams p, DeviceErrors* errs) {
@@ -783,7 +785,7 @@ __global__ void __launch_bounds__(AttnBwd64Cfg::THREADS, 1)
             for (int t = 0; t < 2; ++t) {
               const float x = fmaf(__uint_as_float(sv[e + t]), scale2, -lse_v[e + t]);
               // (the FMA-pipe exp2 gives 2^-125 for a masked score: nothing at bf16 precision)
-              const float pr = (((e + t) & 7) >= 8 - C::EMU) ? exp2_fma(x) : ex2_approx(x);
+              const float pr = (((e + t) & 7) >= 8 - EMU) ? exp2_fma(x) : ex2_approx(x);
               pv[t] = pr;
               dv[t] = pr * (__uint_as_float(dpv[e + t]) - del_v[e + t]);
             }
@@ -971,13 +973,41 @@ int bwd_grid(const AttnBwdParams& p) {
   return std::max(1, std::min(items, num_sms_cached()));
 }
 
+// ZB_ATTN_BWD_EMU=0..3 overrides the share of FMA-pipe exponentials (eighths of the columns), for tuning.
+int bwd_emu_override() {
+  static const int v = [] {
+    const char* e = std::getenv("ZB_ATTN_BWD_EMU");
+    return (e != nullptr && *e >= '0' && *e <= '3' && e[1] == 0) ? (*e - '0') : -1;
+  }();
+  return v;
+}
+
+// Raise the dynamic shared-memory limit of every hd-64 variant (a per-device attribute).
+cudaError_t set_bwd64_smem_limits() {
+  cudaError_t e = cudaSuccess;
+  void (*variants[4])(CUtensorMap, CUtensorMap, CUtensorMap, AttnBwdParams, DeviceErrors*) = {
+      attn_bwd_hd64_kernel<0>, attn_bwd_hd64_kernel<1>, attn_bwd_hd64_kernel<2>, attn_bwd_hd64_kernel<3>};
+  for (auto k : variants)
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, AttnBwd64Cfg::SMEM_BYTES);
+  return e;
+}
+
 // head_dim 64 runs the software-pipelined kernel, 128 the original one.
 template <int HD>
 void launch_bwd(const AttnBwdParams& p, const CUtensorMap& tq, const CUtensorMap& tdo, const CUtensorMap& tdq,
                 DeviceErrors* errs, cudaStream_t s) {
   if constexpr (HD == 64) {
-    launch_k(attn_bwd_hd64_kernel, dim3(bwd_grid(p)), dim3(AttnBwd64Cfg::THREADS), AttnBwd64Cfg::SMEM_BYTES, s, 1,
-             tq, tdo, tdq, p, errs);
+    auto kernel = attn_bwd_hd64_kernel<AttnBwd64Cfg::EMU>;
+    switch (bwd_emu_override()) {
+      case 0: kernel = attn_bwd_hd64_kernel<0>; break;
+      case 1: kernel = attn_bwd_hd64_kernel<1>; break;
+      case 2: kernel = attn_bwd_hd64_kernel<2>; break;
+      case 3: kernel = attn_bwd_hd64_kernel<3>; break;
+      default: break;
+    }
+    launch_k(kernel, dim3(bwd_grid(p)), dim3(AttnBwd64Cfg::THREADS), AttnBwd64Cfg::SMEM_BYTES, s, 1, tq, tdo, tdq, p,
+             errs);
   } else {
     using C = AttnBwdCfg<HD>;
     launch_k(attn_bwd_kernel<HD>, dim3(bwd_grid(p)), dim3(BWD_THREADS), C::SMEM_BYTES, s, 1, tq, tdo, tdq, p, errs);
@@ -997,8 +1027,7 @@ void attention_bwd(const AttnBwdParams& p, cudaStream_t s) {
   CUtensorMap tdq = make_dq_map(p);
   static std::atomic<unsigned long long> configured{0};
   once_per_device(configured, [] {
-    B200_CUDA_CHECK(cudaFuncSetAttribute(attn_bwd_hd64_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         AttnBwd64Cfg::SMEM_BYTES));
+    B200_CUDA_CHECK(set_bwd64_smem_limits());
     B200_CUDA_CHECK(cudaFuncSetAttribute(attn_bwd_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          AttnBwdCfg<128>::SMEM_BYTES));
   });
@@ -1045,7 +1074,7 @@ unsigned char* noalloc_scratch_for_current_device() {
                  cudaGetErrorString(e));
     return nullptr;
   }
-  e = cudaFuncSetAttribute(attn_bwd_hd64_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, AttnBwd64Cfg::SMEM_BYTES);
+  e = set_bwd64_smem_limits();
   if (e == cudaSuccess)
     e = cudaFuncSetAttribute(attn_bwd_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              AttnBwdCfg<128>::SMEM_BYTES);

@@ -35,6 +35,7 @@
 #include <cuda.h>
 
 #include <algorithm>
+#include <cstdlib>
 
 #include "common.cuh"
 #include "gemm.h"
@@ -58,9 +59,11 @@ struct AttnFwdCfg {
   static constexpr int TILE_BYTES = 128 * HD * 2;    // one 128-row tile of Q, K or V
   static constexpr int STAGES = (HD == 64) ? 3 : 2;  // K/V ring
   static constexpr int Q_BUFS = (HD == 64) ? 2 : 1;  // Q pairs: the next item's Q loads during this one
-  // Share of the exponentials done on the FMA pipe: columns c with (c & 7) >= 8 - EMU.  hd 64 is
-  // bound by the MUFU exponential rate; hd 128 by the tensor cores.
-  static constexpr int EMU = (HD == 64) ? 2 : 1;
+  // Default share of the exponentials done on the FMA pipe (columns c with (c & 7) >= 8 - EMU; the
+  // kernel is instantiated for 0..3).  Measured on B200 at the benchmark shape: 0 (all on MUFU) is
+  // fastest for hd 64 (43.0 us vs 45.1 / 45.1 / 47.1 us for 1 / 2 / 3): the softmax is bound by
+  // issue and latency, not by the MUFU rate, so the 9-instruction polynomial only adds work.
+  static constexpr int EMU = (HD == 64) ? 0 : 1;
   static constexpr int REGS_LOW = (HD == 64) ? 64 : 88;
   static constexpr int REGS_HIGH = (HD == 64) ? 216 : 208;
   static_assert(128 * REGS_LOW + 256 * REGS_HIGH <= ATT_THREADS * kLaunchRegs, "register split over budget");
@@ -104,7 +107,16 @@ __device__ __forceinline__ int tile_kv_blocks(int pair, int t, int n_qb) {
   return qb < n_qb ? qb + 1 : 0;
 }
 
-template <int HD>
+// Debug phase clocks (ZB_ATTN_TRACE=1): role r of CTA 0 appends (event, clock64) pairs.
+__device__ __forceinline__ void trace_ev(const AttnParams& p, int role, int& n, int ev) {
+  if (p.trace != nullptr && blockIdx.x == 0 && n < kAttnTraceWords / 2) {
+    p.trace[role * kAttnTraceWords + 2 * n] = (unsigned long long)ev;
+    p.trace[role * kAttnTraceWords + 2 * n + 1] = clock64();
+    ++n;
+  }
+}
+
+template <int HD, int EMU>
 __global__ void __launch_bounds__(ATT_THREADS, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tm, AttnParams p, DeviceErrors* errs) {
   using C = AttnFwdCfg<HD>;
@@ -212,6 +224,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
       constexpr uint32_t IDESC_S = idesc_bf16_f32(128, 128, false, false);
       constexpr uint32_t IDESC_O = idesc_bf16_f32(128, C::O_COLS, false, true);
       int g = 0;             // global key/value block counter
+      int tn = 0;            // trace entries
       int pn[2] = {0, 0};    // P handed over per tile (p_full phases)
       int on[2] = {0, 0};    // items finished per tile (o_done / o_free phases)
       bool ok = true;
@@ -250,6 +263,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
           for (int t = 0; t < 2; ++t) {
             if (!ok) break;
             if (j >= n[t]) continue;
+            trace_ev(p, 0, tn, 10 + t);
             if (!mbar_wait_bounded(&p_full[t], pn[t] & 1, abort_flag, errs, kErrAttnWait, 3 + t)) {
               ok = false;
               break;
@@ -268,6 +282,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
             for (int ks = 0; ks < 8; ++ks)
               tc_mma_f16_ts(tmem + C::T_O + t * C::O_COLS, tmem + C::T_S + t * 128 + ks * 8,
                             smem_desc_sw128(va + ks * 2048, 16384, 1024), IDESC_O, (j == 0 && ks == 0) ? 0u : 1u);
+            trace_ev(p, 0, tn, 20 + t);
             if (j + 1 == n[t]) {
               tc_commit(&o_done[t]);
               ++on[t];
@@ -302,6 +317,11 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
     const uint32_t o_cols = tmem + lane_off + C::T_O + t * C::O_COLS;
     const float scale2 = p.scale * kLog2e;
     int sn = 0, on = 0;
+    int tn = 0;
+    const int trole = (lane == 0 && quarter == 0) ? 1 + t : -1;  // the first row of each tile traces
+    auto tev = [&](int ev) {
+      if (trole > 0) trace_ev(p, trole, tn, ev);
+    };
     for (int k = 0;; ++k) {
       const int u = fwd_item_index(k, c, G, n_items);
       if (u < 0) break;
@@ -311,6 +331,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
       float m_used = 0.f, l = 0.f;
       bool ok = true;
       for (int j = 0; j < n; ++j) {
+        tev(1);
         if (!mbar_wait_bounded(&s_full[t], sn & 1, abort_flag, errs, kErrAttnWait, 11 + t)) {
           ok = false;
           break;
@@ -321,6 +342,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
 #pragma unroll
         for (int q4 = 0; q4 < 4; ++q4) tmem_ld_32x32b_x32(s_cols + 32 * q4, s[q4]);
         tc_wait_ld();
+        tev(2);
         const bool diag = (j == n - 1);  // key block == query block: mask columns past the row
         if (diag) {  // masked scores become -inf: they drop out of the max and exponentiate to 0
 #pragma unroll
@@ -337,6 +359,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
                                      __uint_as_float(s[e >> 5][(e + 1) & 31]));
         const float mx = fmax3f(fmax3f(mx8[0], mx8[1], mx8[2]), fmax3f(mx8[3], mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7]));
         const float m_row = mx * scale2;
+        tev(3);
         if (j == 0) {
           m_used = m_row;
         } else if (m_row > m_used + kRescaleThreshold) {
@@ -370,8 +393,8 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
         for (int e = 0; e < 128; e += 2) {
           const float x0 = fmaf(__uint_as_float(s[e >> 5][e & 31]), scale2, -m_used);
           const float x1 = fmaf(__uint_as_float(s[e >> 5][(e + 1) & 31]), scale2, -m_used);
-          const float p0 = ((e & 7) >= 8 - C::EMU) ? exp2_fma(x0) : ex2_approx(x0);
-          const float p1 = (((e + 1) & 7) >= 8 - C::EMU) ? exp2_fma(x1) : ex2_approx(x1);
+          const float p0 = ((e & 7) >= 8 - EMU) ? exp2_fma(x0) : ex2_approx(x0);
+          const float p1 = (((e + 1) & 7) >= 8 - EMU) ? exp2_fma(x1) : ex2_approx(x1);
           if constexpr (!C::ONES) {
             rs8[e & 7] += p0;
             rs8[(e + 1) & 7] += p1;
@@ -379,16 +402,20 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
           s[e >> 6][(e >> 1) & 31] = pack_bf16(p0, p1);  // pair e/2 lands below column e: already read
         }
         if constexpr (!C::ONES) l += ((rs8[0] + rs8[1]) + (rs8[2] + rs8[3])) + ((rs8[4] + rs8[5]) + (rs8[6] + rs8[7]));
+        tev(4);
         tmem_st_32x32b_x32(s_cols + 0, s[0]);
         tmem_st_32x32b_x32(s_cols + 32, s[1]);
         tc_wait_st();
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&p_full[t]);
+        tev(5);
       }
       if (!ok) break;
       // epilogue: O / l -> bf16 rows, base-2 log-sum-exp
+      tev(6);
       if (!mbar_wait_bounded(&o_done[t], on & 1, abort_flag, errs, kErrAttnWait, 13 + t)) break;
+      tev(7);
       ++on;
       tc_fence_after();
       const int q_row = (2 * it.pair + t) * 128 + r;
@@ -425,6 +452,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
       const size_t lse_idx = ((size_t)it.b * p.heads + it.h) * p.seq + q_row;
       if (B200_IN_BOUNDS(errs, lse_idx, 1, (long long)p.batch * p.heads * p.seq, 121))
         p.lse[lse_idx] = m_used + log2f(l);
+      tev(8);
     }
   }
 
@@ -436,22 +464,65 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
   }
 }
 
-template <int HD>
-void launch_fwd(const AttnParams& p, const CUtensorMap& tm, cudaStream_t s) {
+template <int HD, int EMU>
+void launch_fwd_emu(const AttnParams& p, const CUtensorMap& tm, cudaStream_t s) {
   using C = AttnFwdCfg<HD>;
   static std::atomic<unsigned long long> configured{0};
   once_per_device(configured, [] {
-    B200_CUDA_CHECK(cudaFuncSetAttribute(attn_fwd_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES));
+    B200_CUDA_CHECK(cudaFuncSetAttribute(attn_fwd_kernel<HD, EMU>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         C::SMEM_BYTES));
   });
   const int n_qb = p.seq / 128;
   const int items = ((n_qb + 1) / 2) * p.heads * p.batch;
   const int grid = std::max(1, std::min(items, num_sms_cached()));
-  launch_k(attn_fwd_kernel<HD>, dim3(grid), dim3(ATT_THREADS), C::SMEM_BYTES, s, 1, tm, p, device_errors_ptr());
+  launch_k(attn_fwd_kernel<HD, EMU>, dim3(grid), dim3(ATT_THREADS), C::SMEM_BYTES, s, 1, tm, p, device_errors_ptr());
+}
+
+// ZB_ATTN_FWD_EMU=0..3 overrides the share of FMA-pipe exponentials (eighths of the columns), for tuning.
+int fwd_emu_override() {
+  static const int v = [] {
+    const char* e = std::getenv("ZB_ATTN_FWD_EMU");
+    return (e != nullptr && *e >= '0' && *e <= '3' && e[1] == 0) ? (*e - '0') : -1;
+  }();
+  return v;
+}
+
+template <int HD>
+void launch_fwd(const AttnParams& p, const CUtensorMap& tm, cudaStream_t s) {
+  const int emu = fwd_emu_override() >= 0 ? fwd_emu_override() : AttnFwdCfg<HD>::EMU;
+  switch (emu) {
+    case 1: launch_fwd_emu<HD, 1>(p, tm, s); break;
+    case 2: launch_fwd_emu<HD, 2>(p, tm, s); break;
+    case 3: launch_fwd_emu<HD, 3>(p, tm, s); break;
+    default: launch_fwd_emu<HD, 0>(p, tm, s); break;
+  }
 }
 
 }  // namespace
 
-void attention_fwd(const AttnParams& p, cudaStream_t s) {
+namespace {
+unsigned long long* g_trace = nullptr;  // debug tracing buffer (ZB_ATTN_TRACE=1), one per process
+bool trace_enabled() {
+  static const bool on = [] {
+    const char* e = std::getenv("ZB_ATTN_TRACE");
+    return e != nullptr && e[0] == '1';
+  }();
+  return on;
+}
+}  // namespace
+
+void attention_trace_read(unsigned long long* host_out) {
+  B200_CHECK(g_trace != nullptr, "attention trace: run a forward with ZB_ATTN_TRACE=1 first");
+  B200_CUDA_CHECK(cudaMemcpy(host_out, g_trace, 3 * kAttnTraceWords * 8, cudaMemcpyDeviceToHost));
+}
+
+void attention_fwd(const AttnParams& p_in, cudaStream_t s) {
+  AttnParams p = p_in;
+  if (trace_enabled()) {  // debug only: one buffer, cleared before each traced launch
+    if (g_trace == nullptr) B200_CUDA_CHECK(cudaMalloc(&g_trace, 3 * kAttnTraceWords * 8));
+    B200_CUDA_CHECK(cudaMemsetAsync(g_trace, 0, 3 * kAttnTraceWords * 8, s));
+    p.trace = g_trace;
+  }
   B200_CHECK(p.head_dim == 64 || p.head_dim == 128, "attention: head_dim must be 64 or 128");
   B200_CHECK(p.seq % 128 == 0, "attention: seq_len must be a multiple of 128");
   B200_CHECK(p.heads % p.kv_heads == 0, "attention: heads must be a multiple of kv_heads");

@@ -951,6 +951,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("cross_entropy_fwd", &cross_entropy_fwd);
   m.def("cross_entropy_bwd", &cross_entropy_bwd);
   m.def("attention_fwd", &attention_fwd);
+  m.def("attention_trace", []() {
+    auto out = torch::empty({3, b200::kAttnTraceWords}, torch::dtype(torch::kInt64));
+    b200::attention_trace_read(reinterpret_cast<unsigned long long*>(out.data_ptr<int64_t>()));
+    return out;
+  }, "debug: phase clocks of CTA 0 of the last attention forward run with ZB_ATTN_TRACE=1");
   m.def("attention_bwd", &attention_bwd, py::arg("qkv"), py::arg("k_col"), py::arg("v_col"), py::arg("out"),
         py::arg("dout"), py::arg("lse"), py::arg("delta"), py::arg("dq_acc"), py::arg("dqkv"), py::arg("cos"),
         py::arg("sin"), py::arg("batch"), py::arg("seq"), py::arg("heads"), py::arg("kv_heads"), py::arg("head_dim"),

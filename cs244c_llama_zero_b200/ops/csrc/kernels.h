@@ -44,8 +44,13 @@ struct AttnParams {
   float* lse;          // [B, H, S] (natural-log units)
   int batch, seq, heads, kv_heads, head_dim;
   float scale;
+  unsigned long long* trace = nullptr;  // debug: per-role phase clocks of CTA 0 (ZB_ATTN_TRACE=1), else null
 };
 void attention_fwd(const AttnParams& p, cudaStream_t s);
+// Debug (ZB_ATTN_TRACE=1): phase clocks of CTA 0 of the last forward launch, kAttnTraceWords 64-bit words
+// per role (role 0: MMA thread, 1: first softmax thread of tile A, 2: of tile B), as (event, clock64) pairs.
+constexpr int kAttnTraceWords = 2048;
+void attention_trace_read(unsigned long long* host_out);
 
 struct AttnBwdParams {
   const __nv_bfloat16* qkv;
