@@ -327,9 +327,15 @@ def _measure_stages(args, size: str, batch: int, seq: int, world: int, rank: int
         dev = [h.to(sess.device) for h in host]
         it = {"i": 0}
 
+        debug = os.environ.get("ZB_BENCH_DEBUG", "0") == "1"
+
         def device_step():
             sess.train_step(dev[it["i"] % len(dev)])
             it["i"] += 1
+            if debug:  # diagnosis only: per-step synchronisation (timings are not valid then)
+                torch.cuda.synchronize()
+                progress(rank, f"{size} stage {stage}: step {it['i']} done, device errors "
+                               f"{list(ops.load_extension().read_device_errors())}")
 
         is_head = headline and stage == args.headline_stage
         # The sampler starts before the warm-up so that short timed regions still get samples taken

@@ -781,14 +781,19 @@ __global__ void __launch_bounds__(AttnBwd64Cfg::THREADS, 1)
 #pragma unroll
           for (int e = 0; e < 32; e += 2) {
             float pv[2], dv[2];
+            if constexpr (EMU == 4) {  // one MUFU operation for the pair (fp16 inputs)
+              ex2_pair_f16(fmaf(__uint_as_float(sv[e]), scale2, -lse_v[e]),
+                           fmaf(__uint_as_float(sv[e + 1]), scale2, -lse_v[e + 1]), pv[0], pv[1]);
+            } else {
 #pragma unroll
-            for (int t = 0; t < 2; ++t) {
-              const float x = fmaf(__uint_as_float(sv[e + t]), scale2, -lse_v[e + t]);
-              // (the FMA-pipe exp2 gives 2^-125 for a masked score: nothing at bf16 precision)
-              const float pr = (((e + t) & 7) >= 8 - EMU) ? exp2_fma(x) : ex2_approx(x);
-              pv[t] = pr;
-              dv[t] = pr * (__uint_as_float(dpv[e + t]) - del_v[e + t]);
+              for (int t = 0; t < 2; ++t) {
+                const float x = fmaf(__uint_as_float(sv[e + t]), scale2, -lse_v[e + t]);
+                // (the FMA-pipe exp2 gives 2^-125 for a masked score: nothing at bf16 precision)
+                pv[t] = (((e + t) & 7) >= 8 - EMU) ? exp2_fma(x) : ex2_approx(x);
+              }
             }
+#pragma unroll
+            for (int t = 0; t < 2; ++t) dv[t] = pv[t] * (__uint_as_float(dpv[e + t]) - del_v[e + t]);
             ppk[(c + e) >> 1] = pack_bf16(pv[0], pv[1]);
             dk[e >> 1] = pack_bf16(dv[0], dv[1]);
           }
@@ -973,11 +978,12 @@ int bwd_grid(const AttnBwdParams& p) {
   return std::max(1, std::min(items, num_sms_cached()));
 }
 
-// ZB_ATTN_BWD_EMU=0..3 overrides the share of FMA-pipe exponentials (eighths of the columns), for tuning.
+// ZB_ATTN_BWD_EMU=0..3 overrides the share of FMA-pipe exponentials (eighths of the columns), 4 selects
+// half-precision pairs (one MUFU operation per two exponentials); for tuning.
 int bwd_emu_override() {
   static const int v = [] {
     const char* e = std::getenv("ZB_ATTN_BWD_EMU");
-    return (e != nullptr && *e >= '0' && *e <= '3' && e[1] == 0) ? (*e - '0') : -1;
+    return (e != nullptr && *e >= '0' && *e <= '4' && e[1] == 0) ? (*e - '0') : -1;
   }();
   return v;
 }
@@ -985,8 +991,9 @@ int bwd_emu_override() {
 // Raise the dynamic shared-memory limit of every hd-64 variant (a per-device attribute).
 cudaError_t set_bwd64_smem_limits() {
   cudaError_t e = cudaSuccess;
-  void (*variants[4])(CUtensorMap, CUtensorMap, CUtensorMap, AttnBwdParams, DeviceErrors*) = {
-      attn_bwd_hd64_kernel<0>, attn_bwd_hd64_kernel<1>, attn_bwd_hd64_kernel<2>, attn_bwd_hd64_kernel<3>};
+  void (*variants[5])(CUtensorMap, CUtensorMap, CUtensorMap, AttnBwdParams, DeviceErrors*) = {
+      attn_bwd_hd64_kernel<0>, attn_bwd_hd64_kernel<1>, attn_bwd_hd64_kernel<2>, attn_bwd_hd64_kernel<3>,
+      attn_bwd_hd64_kernel<4>};
   for (auto k : variants)
     if (e == cudaSuccess)
       e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, AttnBwd64Cfg::SMEM_BYTES);
@@ -1004,6 +1011,7 @@ void launch_bwd(const AttnBwdParams& p, const CUtensorMap& tq, const CUtensorMap
       case 1: kernel = attn_bwd_hd64_kernel<1>; break;
       case 2: kernel = attn_bwd_hd64_kernel<2>; break;
       case 3: kernel = attn_bwd_hd64_kernel<3>; break;
+      case 4: kernel = attn_bwd_hd64_kernel<4>; break;
       default: break;
     }
     launch_k(kernel, dim3(bwd_grid(p)), dim3(AttnBwd64Cfg::THREADS), AttnBwd64Cfg::SMEM_BYTES, s, 1, tq, tdo, tdq, p,

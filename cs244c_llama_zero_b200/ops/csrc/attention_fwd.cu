@@ -52,6 +52,9 @@ constexpr int ATT_THREADS = 384;
 constexpr int kLaunchRegs = 168;
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units: rescale O only when the max grows by > 2^8
+// EMU value selecting the half-precision-pair exponential (two results per MUFU operation) instead of
+// an fp32 MUFU / FMA-polynomial split.
+constexpr int kEmuHalfPairs = 4;
 
 template <int HD>
 struct AttnFwdCfg {
@@ -239,13 +242,14 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
         if (!mbar_wait_bounded(&q_full[qs], (k / C::Q_BUFS) & 1, abort_flag, errs, kErrAttnWait, 2)) break;
         // S_t = Q_t K^T for the K tile in ring stage st
         auto issue_s = [&](int t, int st) {
-          const uint32_t qa = q_addr + t * C::TILE_BYTES;
-          const uint32_t ka = smem_u32(smem + C::KV_OFF + st * C::STAGE_BYTES);
+          // descriptors built once; a k-step moves the start-address field (bytes >> 4, no carry:
+          // shared addresses stay below 2^18)
+          const uint64_t dq = smem_desc_sw128(q_addr + t * C::TILE_BYTES, 16, 1024);
+          const uint64_t dk = smem_desc_sw128(smem_u32(smem + C::KV_OFF + st * C::STAGE_BYTES), 16, 1024);
 #pragma unroll
           for (int ks = 0; ks < HD / 16; ++ks) {
-            const uint32_t off = (ks >> 2) * 16384 + (ks & 3) * 32;
-            tc_mma_f16(tmem + C::T_S + t * 128, smem_desc_sw128(qa + off, 16, 1024),
-                       smem_desc_sw128(ka + off, 16, 1024), IDESC_S, ks > 0 ? 1u : 0u);
+            const uint64_t off = ((ks >> 2) * 16384 + (ks & 3) * 32) >> 4;
+            tc_mma_f16(tmem + C::T_S + t * 128, dq + off, dk + off, IDESC_S, ks > 0 ? 1u : 0u);
           }
           tc_commit(&s_full[t]);
         };
@@ -277,11 +281,12 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
             }
             tc_fence_after();
             // O_t (+)= P_t V_j; P_t is read from tile t's S columns
-            const uint32_t va = smem_u32(smem + C::KV_OFF + st * C::STAGE_BYTES + C::TILE_BYTES);
+            const uint64_t dv =
+                smem_desc_sw128(smem_u32(smem + C::KV_OFF + st * C::STAGE_BYTES + C::TILE_BYTES), 16384, 1024);
 #pragma unroll
             for (int ks = 0; ks < 8; ++ks)
-              tc_mma_f16_ts(tmem + C::T_O + t * C::O_COLS, tmem + C::T_S + t * 128 + ks * 8,
-                            smem_desc_sw128(va + ks * 2048, 16384, 1024), IDESC_O, (j == 0 && ks == 0) ? 0u : 1u);
+              tc_mma_f16_ts(tmem + C::T_O + t * C::O_COLS, tmem + C::T_S + t * 128 + ks * 8, dv + ks * (2048 >> 4),
+                            IDESC_O, (j == 0 && ks == 0) ? 0u : 1u);
             trace_ev(p, 0, tn, 20 + t);
             if (j + 1 == n[t]) {
               tc_commit(&o_done[t]);
@@ -362,9 +367,13 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
         tev(3);
         if (j == 0) {
           m_used = m_row;
-        } else if (m_row > m_used + kRescaleThreshold) {
+        } else if (__any_sync(0xffffffffu, m_row > m_used + kRescaleThreshold)) {
+          // The decision is taken for the whole warp: tcgen05.ld / tcgen05.st are warp-collective
+          // (.sync.aligned) and must not run in divergent code.  Lanes whose maximum did not grow
+          // past the threshold keep theirs (alpha = 1); the others raise it to the block maximum.
           // O_t holds the sum up to block j-1 (complete: the commit of S_t(j) covers PV_t(j-1)).
-          const float alpha = ex2_approx(m_used - m_row);
+          const float m_new = (m_row > m_used + kRescaleThreshold) ? m_row : m_used;
+          const float alpha = ex2_approx(m_used - m_new);
           l *= alpha;
 #pragma unroll
           for (int cc = 0; cc < HD; cc += 32) {
@@ -383,7 +392,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
             for (int e = 0; e < 16; ++e) lv[e] = __float_as_uint(__uint_as_float(lv[e]) * alpha);
             tmem_st_32x32b_x16(o_cols + HD, lv);
           }
-          m_used = m_row;
+          m_used = m_new;
         }
         // probabilities, row sum (8 chains), bf16 P into the same tensor-memory columns.  A masked
         // score is -inf: ex2 gives 0 and the FMA-pipe exp2 gives 2^-125 (its input is clamped), which
@@ -393,8 +402,13 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
         for (int e = 0; e < 128; e += 2) {
           const float x0 = fmaf(__uint_as_float(s[e >> 5][e & 31]), scale2, -m_used);
           const float x1 = fmaf(__uint_as_float(s[e >> 5][(e + 1) & 31]), scale2, -m_used);
-          const float p0 = ((e & 7) >= 8 - EMU) ? exp2_fma(x0) : ex2_approx(x0);
-          const float p1 = (((e + 1) & 7) >= 8 - EMU) ? exp2_fma(x1) : ex2_approx(x1);
+          float p0, p1;
+          if constexpr (EMU == kEmuHalfPairs) {
+            ex2_pair_f16(x0, x1, p0, p1);
+          } else {
+            p0 = ((e & 7) >= 8 - EMU) ? exp2_fma(x0) : ex2_approx(x0);
+            p1 = (((e + 1) & 7) >= 8 - EMU) ? exp2_fma(x1) : ex2_approx(x1);
+          }
           if constexpr (!C::ONES) {
             rs8[e & 7] += p0;
             rs8[(e + 1) & 7] += p1;
@@ -478,11 +492,12 @@ void launch_fwd_emu(const AttnParams& p, const CUtensorMap& tm, cudaStream_t s) 
   launch_k(attn_fwd_kernel<HD, EMU>, dim3(grid), dim3(ATT_THREADS), C::SMEM_BYTES, s, 1, tm, p, device_errors_ptr());
 }
 
-// ZB_ATTN_FWD_EMU=0..3 overrides the share of FMA-pipe exponentials (eighths of the columns), for tuning.
+// ZB_ATTN_FWD_EMU=0..3 overrides the share of FMA-pipe exponentials (eighths of the columns), 4 selects
+// the half-precision pairs; for tuning.
 int fwd_emu_override() {
   static const int v = [] {
     const char* e = std::getenv("ZB_ATTN_FWD_EMU");
-    return (e != nullptr && *e >= '0' && *e <= '3' && e[1] == 0) ? (*e - '0') : -1;
+    return (e != nullptr && *e >= '0' && *e <= '4' && e[1] == 0) ? (*e - '0') : -1;
   }();
   return v;
 }
@@ -494,6 +509,7 @@ void launch_fwd(const AttnParams& p, const CUtensorMap& tm, cudaStream_t s) {
     case 1: launch_fwd_emu<HD, 1>(p, tm, s); break;
     case 2: launch_fwd_emu<HD, 2>(p, tm, s); break;
     case 3: launch_fwd_emu<HD, 3>(p, tm, s); break;
+    case kEmuHalfPairs: launch_fwd_emu<HD, kEmuHalfPairs>(p, tm, s); break;
     default: launch_fwd_emu<HD, 0>(p, tm, s); break;
   }
 }

@@ -200,18 +200,31 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar_addr, uint32_t parity
   return ok != 0;
 }
 
+// try_wait with an explicit suspend-time hint: a thread whose phase is not complete is suspended
+// (it issues nothing) until the phase completes or `hint_ns` passes, instead of returning at once.
+// Waiting warps then leave the issue slots of their sub-partition to the warps that compute.
+__device__ __forceinline__ bool mbar_try_wait_suspend(uint32_t bar_addr, uint32_t parity, uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar_addr), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
+
 // Wait until the phase with the given parity has completed.  Returns false (after
 // recording an error) if the deadline passes or another thread already aborted.
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
                                                   DeviceErrors* errs, int code, int where) {
   const uint32_t addr = smem_u32(bar);
-#pragma unroll 1
-  for (int i = 0; i < 256; ++i)
-    if (mbar_try_wait(addr, parity)) return true;
+  if (mbar_try_wait(addr, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
 #pragma unroll 1
   while (true) {
-    if (mbar_try_wait(addr, parity)) return true;
+    if (mbar_try_wait_suspend(addr, parity, 100000u)) return true;  // sleeps up to 0.1 ms per try
     if (abort_flag != nullptr && *abort_flag) return false;
     if (globaltimer_ns() - t0 > B200_WAIT_TIMEOUT_NS) {
       if (abort_flag != nullptr) *abort_flag = 1;
@@ -506,6 +519,19 @@ __device__ __forceinline__ float exp2_fma(float x) {
   p = fmaf(p, f, 0.69326097f);
   p = fmaf(p, f, 0.99992806f);
   return __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
+}
+
+// 2^x0 and 2^x1 with ONE MUFU operation on a packed half-precision pair (ex2.approx.f16x2), returned
+// as fp32.  The inputs are rounded to fp16 first (10-bit mantissa: for |x| < 16 the result is within
+// ~0.5% of 2^x, below the bf16 precision the callers round to anyway); inputs under -24 give 0.
+// Halves the MUFU work of a softmax whose probabilities end up in bf16.
+__device__ __forceinline__ void ex2_pair_f16(float x0, float x1, float& p0, float& p1) {
+  uint32_t h;
+  asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(h) : "f"(x1), "f"(x0));  // x0 in the low half
+  asm("ex2.approx.f16x2 %0, %0;" : "+r"(h));
+  asm("{\n\t.reg .f16 lo, hi;\n\tmov.b32 {lo, hi}, %2;\n\tcvt.f32.f16 %0, lo;\n\tcvt.f32.f16 %1, hi;\n\t}"
+      : "=f"(p0), "=f"(p1)
+      : "r"(h));
 }
 
 // max(a, b, c) in one instruction (three-input max.f32).
