@@ -400,7 +400,8 @@ class ZeROStage2Optimizer(_ShardedStateMixin, _FlatEngine):
         self._record_memory_event("measured_step_stage2_post_reduce_scatter")
         inv_w = 1.0 / self.world_size
         # the shard holds the sum over ranks: the averaged gradient's norm is 1/W of its norm
-        norm = global_norm_from_local_sq(sum_of_squares(self.grad_shard), sharded=True) * inv_w
+        norm = global_norm_from_local_sq(sum_of_squares(self.grad_shard), sharded=True,
+                                         collectives=self.collectives) * inv_w
         self.step_count += 1
         self._record_memory_event("measured_step_stage2_pre_allgather")
         with self.collectives.label_scope("stage2.step.allgather.updated_param_shard"):
@@ -570,7 +571,8 @@ class ZeROStage2Optimizer(_ShardedStateMixin, _FlatEngine):
                 self._pending_flush = False
                 return norm
         self._flush_flat_grad_buffer()
-        norm = global_norm_from_local_sq(sum_of_squares(self.grad_shard), sharded=self.world_size > 1)
+        norm = global_norm_from_local_sq(sum_of_squares(self.grad_shard), sharded=self.world_size > 1,
+                                         collectives=self.collectives)
         self.step_count += 1
         self._record_memory_event("measured_step_stage2_pre_allgather")
         with self.collectives.label_scope("stage2.step.allgather.updated_param_shard"):

@@ -42,7 +42,7 @@ from .common import (
 )
 from ..collectives import _maybe_simulate_collective_delay
 from ...profiler import nvtx
-from .optim import adamw_update_, clip_coefficient, sum_of_squares
+from .optim import adamw_update_, clip_coefficient, global_norm_from_local_sq, sum_of_squares
 
 
 class Stage3ParamHandle:
@@ -602,9 +602,9 @@ class ZeROStage3Optimizer(ZeROEngineBase):
             total = torch.zeros(1, dtype=torch.float32, device=self.device)
             for h in self._handle_order:
                 total += sum_of_squares(h.grad_shard)
-        if dist.is_available() and dist.is_initialized() and self.world_size > 1:
-            dist.all_reduce(total)
-        return total.sqrt().reshape(())
+        # the NVLink collectives sum the scalar with their own kernel (whose device barrier orders the
+        # ranks like the NCCL call it replaces); other implementations use torch.distributed
+        return global_norm_from_local_sq(total, sharded=self.world_size > 1, collectives=self.collectives)
 
     def _update(self, max_grad_norm: float) -> torch.Tensor:
         if self._pull is not None:
