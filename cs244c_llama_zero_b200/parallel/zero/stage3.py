@@ -105,6 +105,9 @@ class Stage3ParamHandle:
         if self.materialized:
             return
         eng = self.engine
+        if self.world_size == 1:  # one rank holds everything: the shard is the full parameter vector
+            self._bind(self.param_shard, cache=True)
+            return
         if eng._pull is not None and phase in ("forward", "backward"):
             full = eng._pull.materialize(self, phase)
             if full is not None:
@@ -138,8 +141,14 @@ class Stage3ParamHandle:
     def reset_grad(self) -> None:
         self.grad_shard.zero_()
 
-    def begin_grad(self) -> torch.Tensor:
-        """Full-size fp32 gradient buffer bound to every parameter's ``main_grad``."""
+    def begin_grad(self) -> Optional[torch.Tensor]:
+        """Full-size fp32 gradient buffer bound to every parameter's ``main_grad``.  On one rank the
+        gradient shard is that buffer (the reduce-scatter would be the identity): the weight-gradient
+        kernels accumulate into it directly and None is returned."""
+        if self.world_size == 1:
+            for p, v in zip(self.meta.params, self._views(self.grad_shard, True)):
+                p.main_grad = v
+            return None
         buf = self.engine._staging_grads(self.padded_numel)
         persistent = buf is not None
         if buf is None:
@@ -161,6 +170,8 @@ class Stage3ParamHandle:
         for p in self.meta.params:
             if hasattr(p, "main_grad"):
                 del p.main_grad
+        if buf is None:  # one rank: accumulated into the gradient shard in place
+            return
         eng = self.engine
         with eng.clock.measure("backward_reduce_scatter", self.full_param_bytes):
             with eng.collectives.label_scope(f"stage3.backward.reduce_scatter.{self.name}"):
