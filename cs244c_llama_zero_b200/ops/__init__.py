@@ -70,7 +70,8 @@ class CommTimeoutError(DeviceWaitError):
 
 ERROR_NAMES = {1: "gemm pipeline wait", 2: "attention pipeline wait", 3: "collective wait",
                4: "collective barrier", 5: "paced link hold", 6: "index out of range (access skipped)",
-               7: "out-of-bounds access caught by the debug-bounds build (skipped)"}
+               7: "out-of-bounds access caught by the debug-bounds build (skipped)",
+               8: "LM-head gradients computed in forward for a loss scale that backward did not use"}
 COMM_CODES = (3, 4)
 
 

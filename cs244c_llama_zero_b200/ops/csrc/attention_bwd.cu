@@ -480,18 +480,18 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
 //
 // Same work items and math as attn_bwd_kernel, with the tensor cores and the softmax warps
 // overlapped.  Per iteration g (one query block of one head) the MMA warp issues
-//     dV(g) | S^T(g+1) dP^T(g+1) | dK(g) dQ(g)
-// so the softmax of block g+1 runs while the tensor cores compute dK(g) and dQ(g).  What makes
-// that legal:
-//   * P^T(g) goes to TENSOR memory (bf16, into the columns of S^T(g) its warpgroup has already
-//     read) and dV(g) takes it from there (A operand in tensor memory); dV(g) is issued before
-//     S^T(g+1) overwrites those columns, and tcgen05.mma of one thread execute in order;
+//     S^T(g+1) dP^T(g+1) | dV(g) | dK(g) dQ(g)
+// as soon as the softmax warps hand over block g, so the softmax of block g+1 starts after two MMAs
+// and runs while the tensor cores compute dV(g), dK(g) and dQ(g).  What makes that legal:
+//   * P^T(g) goes to TENSOR memory (bf16, in columns of its own) and dV(g) takes it from there (A
+//     operand in tensor memory); the softmax of g+1 writes P^T(g+1) there only after the commit
+//     behind dV(g) (pt_free);
 //   * dS^T goes to shared memory (dK reads it K-major, dQ reads it MN-major as dS), double-buffered:
 //     the softmax of g+1 writes the buffer dK(g-1) / dQ(g-1) read, and the commit that releases
 //     S^T(g+1) to it comes after those MMAs;
-//   * dQ is double-buffered in tensor memory and read out by the softmax warps one iteration late
-//     (after handing over P^T / dS^T of the next block), so the readout never stalls the MMAs.
-// Tensor memory: S^T [0,128) | dP^T [128,256) | dV [256,320) | dK [320,384) | dQ0 [384,448) | dQ1.
+//   * dQ is read out by the softmax warps one iteration late (after handing over P^T / dS^T of the
+//     next block); dQ(g+1) waits for that readout (dq_free), which is due long before.
+// Tensor memory: S^T [0,128) | dP^T [128,256) | dV [256,320) | dK [320,384) | dQ [384,448) | P^T.
 // 384 threads: warp 0 TMA, warp 1 MMA (+ tensor-memory allocation), warps 2-3 idle, warpgroups
 // 1 and 2 compute (thread = kv row for S^T / dP^T / dK / dV, query row for dQ; warpgroup w owns
 // query columns [64w, 64w + 64) and output columns [32w, 32w + 32)).
@@ -509,10 +509,11 @@ struct AttnBwd64Cfg {
   static constexpr int BAR_OFF = STG_OFF + 8 * 2 * kBwdChunk;
   static constexpr int SMEM_BYTES = BAR_OFF + 256 + 1024;
   static_assert(SMEM_BYTES <= 232448, "attention backward (hd 64) shared memory exceeds 227 KB");
-  static constexpr int T_ST = 0, T_DPT = 128, T_DV = 256, T_DK = 320, T_DQ = 384;  // dQ buffer b at T_DQ + 64b
+  // tensor memory: S^T | dP^T | dV | dK | dQ | P^T (bf16, packed two per column)
+  static constexpr int T_ST = 0, T_DPT = 128, T_DV = 256, T_DK = 320, T_DQ = 384, T_PT = 448;
   static constexpr int TMEM_COLS = 512;
   static constexpr int THREADS = 384;
-  static constexpr int REGS_LOW = 64, REGS_HIGH = 216;  // 128 * 64 + 256 * 216 <= 384 * 168
+  static constexpr int REGS_LOW = 72, REGS_HIGH = 216;  // 128 * 72 + 256 * 216 = 384 * 168
   static constexpr int EMU = 0;  // exponentials on the FMA pipe: columns with (c & 7) >= 8 - EMU (0 measured fastest)
 };
 
@@ -531,9 +532,10 @@ __global__ void __launch_bounds__(AttnBwd64Cfg::THREADS, 1)
   uint64_t* q_empty = q_full + C::STAGES;   // [STAGES]
   uint64_t* st_full = q_empty + C::STAGES;  // S^T and dP^T of the next block complete
   uint64_t* p_ready = st_full + 1;          // 8 warps: P^T in tensor memory, dS^T in shared memory
-  uint64_t* dq_full = p_ready + 1;          // [2 buffers]
-  uint64_t* dq_free = dq_full + 2;          // [2 buffers], 8 warps
-  uint64_t* epi_done = dq_free + 2;         // 8 warps: the item's dK / dV have been read out
+  uint64_t* dq_full = p_ready + 1;          // dQ of the block complete
+  uint64_t* dq_free = dq_full + 1;          // 8 warps: dQ read out
+  uint64_t* pt_free = dq_free + 1;          // dV has read P^T: the next block's P^T may be written
+  uint64_t* epi_done = pt_free + 1;         // 8 warps: the item's dK / dV have been read out
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(epi_done + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -552,10 +554,9 @@ __global__ void __launch_bounds__(AttnBwd64Cfg::THREADS, 1)
     }
     mbar_init(st_full, 1);
     mbar_init(p_ready, 8);
-    for (int b = 0; b < 2; ++b) {
-      mbar_init(&dq_full[b], 1);
-      mbar_init(&dq_free[b], 8);
-    }
+    mbar_init(dq_full, 1);
+    mbar_init(dq_free, 8);
+    mbar_init(pt_free, 1);
     mbar_init(epi_done, 8);
     *abort_flag = 0;
     fence_mbar_init();
@@ -661,36 +662,40 @@ __global__ void __launch_bounds__(AttnBwd64Cfg::THREADS, 1)
           const uint32_t q_addr = smem_u32(smem + C::QD_OFF + st * 2 * C::TILE);
           const uint32_t do_addr = q_addr + C::TILE;
           const uint32_t dst_addr = smem_u32(smem + C::DST_OFF + b * 128 * 128 * 2);
-          // dV += P^T dO: P^T from tensor memory (query columns 0-63 packed at S^T columns 0-31,
-          // 64-127 at 64-95), dO MN-major
-#pragma unroll
-          for (int ks = 0; ks < 8; ++ks) {
-            const uint32_t a_col = C::T_ST + (ks >> 2) * 64 + (ks & 3) * 8;
-            tc_mma_f16_ts(tmem + C::T_DV, tmem + a_col, smem_desc_sw128(do_addr + ks * 2048, 16384, 1024), ID_KV,
-                          (it > 0 || ks > 0) ? 1u : 0u);
-          }
+          // the next block's scores first: its softmax then overlaps this block's dV / dK / dQ
           if (it + 1 < n_it && !issue_scores(g + 1)) {
             ok = false;
             break;
           }
+          // dV += P^T dO: P^T from its own tensor-memory columns (query columns packed two per
+          // column), dO MN-major
+          const uint64_t d_do = smem_desc_sw128(do_addr, 16384, 1024);
+#pragma unroll
+          for (int ks = 0; ks < 8; ++ks)
+            tc_mma_f16_ts(tmem + C::T_DV, tmem + C::T_PT + ks * 8, d_do + ks * (2048 >> 4), ID_KV,
+                          (it > 0 || ks > 0) ? 1u : 0u);
+          tc_commit(pt_free);
           // dK += dS^T Q (A = dS^T K-major, B = Q MN-major)
+          const uint64_t d_ds = smem_desc_sw128(dst_addr, 16, 1024);
+          const uint64_t d_q = smem_desc_sw128(q_addr, 16384, 1024);
 #pragma unroll
           for (int ks = 0; ks < 8; ++ks) {
             const uint32_t aoff = (ks >> 2) * 16384 + (ks & 3) * 32;
-            tc_mma_f16(tmem + C::T_DK, smem_desc_sw128(dst_addr + aoff, 16, 1024),
-                       smem_desc_sw128(q_addr + ks * 2048, 16384, 1024), ID_KV, (it > 0 || ks > 0) ? 1u : 0u);
+            tc_mma_f16(tmem + C::T_DK, d_ds + (aoff >> 4), d_q + ks * (2048 >> 4), ID_KV,
+                       (it > 0 || ks > 0) ? 1u : 0u);
           }
-          // dQ = dS K into buffer b, once the readout of iteration g - 2 has emptied it
-          if (g >= 2 && !mbar_wait_bounded(&dq_free[b], ((g - 2) >> 1) & 1, abort_flag, errs, kErrAttnWait, 15)) {
+          // dQ = dS K, once the previous block's dQ has been read out
+          if (g >= 1 && !mbar_wait_bounded(dq_free, (g - 1) & 1, abort_flag, errs, kErrAttnWait, 15)) {
             ok = false;
             break;
           }
           tc_fence_after();
+          const uint64_t d_dsq = smem_desc_sw128(dst_addr, 16384, 1024);
+          const uint64_t d_k = smem_desc_sw128(k_addr, 16384, 1024);
 #pragma unroll
           for (int ks = 0; ks < 8; ++ks)
-            tc_mma_f16(tmem + C::T_DQ + b * 64, smem_desc_sw128(dst_addr + ks * 2048, 16384, 1024),
-                       smem_desc_sw128(k_addr + ks * 2048, 16384, 1024), ID_Q, ks > 0 ? 1u : 0u);
-          tc_commit(&dq_full[b]);
+            tc_mma_f16(tmem + C::T_DQ, d_dsq + ks * (2048 >> 4), d_k + ks * (2048 >> 4), ID_Q, ks > 0 ? 1u : 0u);
+          tc_commit(dq_full);
           tc_commit(&q_empty[st]);
         }
         if (!ok) break;
@@ -710,15 +715,14 @@ __global__ void __launch_bounds__(AttnBwd64Cfg::THREADS, 1)
     bool ok = true;
     // dQ of iteration gq (query block i, head h) -> scaled fp32 TMA add-reductions into dq_acc
     auto dq_readout = [&](int gq, int h, int i, int row0) -> bool {
-      const int b = gq & 1;
-      if (!mbar_wait_bounded(&dq_full[b], (gq >> 1) & 1, abort_flag, errs, kErrAttnWait, 17)) return false;
+      if (!mbar_wait_bounded(dq_full, gq & 1, abort_flag, errs, kErrAttnWait, 17)) return false;
       tc_fence_after();
       if (lane == 0) bulk_wait_group_read<0>();  // both staging chunks of this warp are free
       __syncwarp();
 #pragma unroll
       for (int hc = 0; hc < 2; ++hc) {
         uint32_t qv[16];
-        tmem_ld_32x32b_x16(lane_base + C::T_DQ + b * 64 + wg * 32 + 16 * hc, qv);
+        tmem_ld_32x32b_x16(lane_base + C::T_DQ + wg * 32 + 16 * hc, qv);
         tc_wait_ld();
         uint8_t* buf = stg + hc * kBwdChunk;
 #pragma unroll
@@ -733,7 +737,7 @@ __global__ void __launch_bounds__(AttnBwd64Cfg::THREADS, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) {
-        mbar_arrive(&dq_free[b]);
+        mbar_arrive(dq_free);
 #pragma unroll
         for (int hc = 0; hc < 2; ++hc)
           tma_reduce_add_2d(&tm_dq, stg + hc * kBwdChunk, h * HD + wg * 32 + 16 * hc, row0 + i * 128 + q4 * 32);
@@ -799,8 +803,14 @@ __global__ void __launch_bounds__(AttnBwd64Cfg::THREADS, 1)
           }
           store_swizzled_row(dst, r, col0 + c, dk);
         }
-        // P^T into this warpgroup's already-read S^T columns (packed: 32 columns from col0)
-        tmem_st_32x32b_x32(lane_base + C::T_ST + col0, ppk);
+        // P^T into its own columns (this warpgroup's 64 query columns packed into 32), once dV of the
+        // previous block has read them
+        if (g >= 1 && !mbar_wait_bounded(pt_free, (g - 1) & 1, abort_flag, errs, kErrAttnWait, 19)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        tmem_st_32x32b_x32(lane_base + C::T_PT + wg * 32, ppk);
         tc_wait_st();
         fence_async_smem();
         tc_fence_before();

@@ -948,6 +948,12 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("wd"), py::arg("step"), py::arg("dev_scalars") = py::none());
   m.def("adam_advance", &adam_advance);
   m.def("sum_squares", &sum_squares);
+  m.def("record_if_different", [](Tensor a, Tensor b, int64_t code) {
+    check_f32(a, "a");
+    check_f32(b, "b");
+    c10::cuda::CUDAGuard g(a.device());
+    b200::record_if_different(a.data_ptr<float>(), b.data_ptr<float>(), (int)code, cur_stream());
+  }, "error record gets `code` when the two device scalars differ");
   m.def("cross_entropy_fwd", &cross_entropy_fwd);
   m.def("cross_entropy_bwd", &cross_entropy_bwd);
   m.def("attention_fwd", &attention_fwd);

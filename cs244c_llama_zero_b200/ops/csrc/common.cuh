@@ -105,6 +105,7 @@ enum : int {
   kErrPaceWait = 5,
   kErrBadIndex = 6,  // an index input out of range (e.g. a token id >= vocab); the access was skipped
   kErrBounds = 7,    // debug bounds build: a hand-indexed global access fell outside its buffer (skipped)
+  kErrGradScale = 8, // the LM head's gradients were computed in forward for a loss scale that backward did not see
 };
 
 // ---------------------------------------------------------------------------------------

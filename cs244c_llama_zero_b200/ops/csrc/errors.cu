@@ -39,4 +39,17 @@ DeviceErrors* device_errors_ptr() {
   return per_device[dev];
 }
 
+namespace {
+// Records `code` in the error record when a == b does not hold (two device scalars; one thread).
+__global__ void record_if_different_kernel(const float* a, const float* b, int code, DeviceErrors* errs) {
+  if (threadIdx.x == 0 && blockIdx.x == 0 && *a != *b) report_error(errs, code, 0);
+}
+}  // namespace
+
+void record_if_different(const float* a, const float* b, int code, cudaStream_t s) {
+  record_if_different_kernel<<<1, 32, 0, s>>>(a, b, code, device_errors_ptr());
+  B200_CUDA_CHECK(cudaGetLastError());
+  count_launch();
+}
+
 }  // namespace b200

@@ -29,6 +29,8 @@ void adamw_step(float* master, float* m, float* v, const float* g, void* param_o
 // step_count[0] += 1 on the device, then dev_sc = {lr / (1 - beta1^t), 1 / sqrt(1 - beta2^t)} for the new t.
 void adam_advance(int* step_count, float* dev_sc, float lr, float beta1, float beta2, cudaStream_t s);
 void sum_squares(const void* x, bool is_bf16, size_t n, float* out, cudaStream_t s);
+// Error record gets `code` if the device scalars *a and *b differ (no host synchronisation).
+void record_if_different(const float* a, const float* b, int code, cudaStream_t s);
 void cross_entropy_fwd(const __nv_bfloat16* logits, int ld, const int64_t* targets, int rows, int vocab, float* lse,
                        float* loss_sum, float* count, float* loss, cudaStream_t s);
 void cross_entropy_bwd(__nv_bfloat16* logits, int ld, const int64_t* targets, int rows, int vocab, const float* lse,

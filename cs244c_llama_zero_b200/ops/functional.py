@@ -479,9 +479,47 @@ def shifted_targets(labels: torch.Tensor) -> torch.Tensor:
     return tgt.reshape(-1).contiguous()
 
 
+# The training loops of this package scale every micro-batch's loss by a known factor (1 / gradient
+# accumulation steps) before backward.  Inside ``loss_gradient_scale(scale)`` the LM head + cross-
+# entropy computes its gradients during the forward pass already, a block of rows at a time, with that
+# scale: no [tokens, vocab] logits tensor is ever allocated (one block of rows is), the weight
+# gradient goes straight into the flat fp32 gradient buffer, and backward only hands back the input
+# gradient.  Backward checks on the device that the scale it receives is the announced one and
+# records an error (``kErrGradScale``) otherwise.
+_LOSS_GRAD_SCALE: List[Optional[torch.Tensor]] = [None]
+LM_HEAD_BLOCK_BYTES = 128 << 20  # logits block of the gradient-in-forward path (rows rounded to 128)
+
+
+class loss_gradient_scale:
+    """Context manager: losses computed inside will be back-propagated with gradient ``scale``
+    (a float32 device scalar, e.g. ``1 / grad_accum_steps``).  Enables the LM head's gradient-in-
+    forward path; without it the head keeps the whole logits tensor for its backward."""
+
+    def __init__(self, scale: Optional[torch.Tensor]) -> None:
+        self.scale = scale
+
+    def __enter__(self):
+        self._prev = _LOSS_GRAD_SCALE[0]
+        _LOSS_GRAD_SCALE[0] = self.scale
+        return self
+
+    def __exit__(self, *exc):
+        _LOSS_GRAD_SCALE[0] = self._prev
+        return False
+
+
+def _lm_block_rows(vocab: int, total: int) -> int:
+    import os
+
+    budget = int(os.environ.get("ZB_LM_BLOCK_MB", "0") or 0) << 20 or LM_HEAD_BLOCK_BYTES
+    rows = max(128, (budget // (2 * vocab)) // 128 * 128)
+    return min(rows, total)
+
+
 class _LMHeadCEFn(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, x: torch.Tensor, weight: torch.nn.Parameter, labels: torch.Tensor):
+    def forward(ctx, x: torch.Tensor, weight: torch.nn.Parameter, labels: torch.Tensor,
+                scale: Optional[torch.Tensor] = None):
         _require_cuda(x, weight)
         B, S, d = x.shape
         T = B * S
@@ -489,21 +527,59 @@ class _LMHeadCEFn(torch.autograd.Function):
         C = _ext()
         xf = x.reshape(T, d).contiguous()
         targets = shifted_targets(labels)
+        ctx.weight = weight
+        ctx.shape = (B, S, d)
+        sink = _GradSink([weight]) if scale is not None else None
+        if sink is not None and sink.direct:
+            return _LMHeadCEFn._forward_with_gradients(ctx, C, xf, weight, targets, scale, sink, T, V)
         logits = torch.empty(T, V, dtype=x.dtype, device=x.device)
         C.linear_fwd(xf, weight.detach(), logits, None)
         lse = torch.empty(T, dtype=torch.float32, device=x.device)
         scratch = torch.empty(3, dtype=torch.float32, device=x.device)
         loss_sum, count, loss = scratch[0:1], scratch[1:2], scratch[2:3]
         C.cross_entropy_fwd(logits, targets, lse, loss_sum, count, loss)
+        ctx.eager_grads = False
         ctx.save_for_backward(xf, logits, targets, lse, scratch)
-        ctx.weight = weight
-        ctx.shape = (B, S, d)
         return loss.view(())
 
     @staticmethod
+    def _forward_with_gradients(ctx, C, xf, weight, targets, scale, sink, T, V):
+        """Blocks of rows: logits -> loss terms -> dlogits (in place, times scale / count) -> the input
+        gradient rows and the weight gradient (into the flat buffer).  Only one block of logits lives."""
+        dev = xf.device
+        count = ((targets >= 0) & (targets < V)).sum().to(torch.float32).reshape(1)
+        rows = _lm_block_rows(V, T)
+        block = torch.empty(rows, V, dtype=xf.dtype, device=dev)
+        lse = torch.empty(T, dtype=torch.float32, device=dev)
+        dx = torch.empty_like(xf)
+        n_blocks = (T + rows - 1) // rows
+        scratch = torch.empty(n_blocks, 3, dtype=torch.float32, device=dev)  # per block: loss sum, count, mean
+        w = weight.detach()
+        launcher = _WgradLauncher(dev)
+        for bi, r0 in enumerate(range(0, T, rows)):
+            r1 = min(T, r0 + rows)
+            logits = block[: r1 - r0]
+            C.linear_fwd(xf[r0:r1], w, logits, None)
+            C.cross_entropy_fwd(logits, targets[r0:r1], lse[r0:r1], scratch[bi, 0:1], scratch[bi, 1:2],
+                                scratch[bi, 2:3])
+            C.cross_entropy_bwd(logits, targets[r0:r1], lse[r0:r1], scale.reshape(1), count)
+            _dgrad_and_wgrad_sink(logits, w, xf[r0:r1], dx[r0:r1], sink, launcher)
+        loss = scratch[:, 0].sum() / count.clamp_min(1.0)[0]
+        ctx.eager_grads = True
+        ctx.save_for_backward(dx, scale.reshape(1))
+        return loss
+
+    @staticmethod
     def backward(ctx, grad_loss: torch.Tensor):
-        xf, logits, targets, lse, scratch = ctx.saved_tensors
         C = _ext()
+        if ctx.eager_grads:
+            dx, scale = ctx.saved_tensors
+            g = grad_loss.reshape(1).to(torch.float32).contiguous()
+            C.record_if_different(g, scale, 8)
+            # exact for any incoming scale (a ratio of 1 keeps the bits); the weight gradient was added
+            # with the announced scale
+            return (dx * (g / scale).reshape(())).view(ctx.shape), None, None, None
+        xf, logits, targets, lse, scratch = ctx.saved_tensors
         g = grad_loss.reshape(1).to(torch.float32).contiguous()
         C.cross_entropy_bwd(logits, targets, lse, g, scratch[1:2])
         w = ctx.weight
@@ -512,11 +588,14 @@ class _LMHeadCEFn(torch.autograd.Function):
         _dgrad_and_wgrad_sink(logits, w.detach(), xf, dx, sink, _WgradLauncher(xf.device))
         if not sink.direct:
             join_weight_grads(xf.device)
-        return dx.view(ctx.shape), sink.finish()[0], None
+        return dx.view(ctx.shape), sink.finish()[0], None, None
 
 
 def lm_head_cross_entropy(x: torch.Tensor, weight: torch.nn.Parameter, labels: torch.Tensor) -> torch.Tensor:
-    return _LMHeadCEFn.apply(x, weight, labels)
+    """Mean next-token cross-entropy of ``x @ weight^T`` against ``labels`` shifted by one."""
+    scale = _LOSS_GRAD_SCALE[0]
+    eager = scale is not None and torch.is_grad_enabled() and (x.requires_grad or weight.requires_grad)
+    return _LMHeadCEFn.apply(x, weight, labels, scale if eager else None)
 
 
 # ------------------------------------------------------------------------------ optimizer

@@ -24,6 +24,7 @@ that replaces the engine's buffers (``load_state_dict``); the next step captures
 
 from __future__ import annotations
 
+import contextlib
 import os
 from dataclasses import dataclass, field
 from datetime import timedelta
@@ -199,6 +200,19 @@ class TrainSession:
         self._staging.copy_(input_ids, non_blocking=True)
         return self._staging
 
+    def _loss_scale_context(self, n: int):
+        """On the B200 backend: announce that each micro-batch loss is back-propagated as ``loss / n``,
+        which lets the LM head compute its gradients during the forward pass (no logits tensor)."""
+        if self.backend != "b200" or self.device.type != "cuda":
+            return contextlib.nullcontext()
+        from ..ops import functional as B
+
+        if not hasattr(self, "_loss_scales"):
+            self._loss_scales = {}
+        if n not in self._loss_scales:
+            self._loss_scales[n] = torch.full((), 1.0 / n, dtype=torch.float32, device=self.device)
+        return B.loss_gradient_scale(self._loss_scales[n])
+
     def forward_backward(self, micro_batches: Sequence[torch.Tensor]) -> torch.Tensor:
         """Run every micro-batch; returns the mean loss as a device scalar (no host sync)."""
         total = torch.zeros((), dtype=torch.float32, device=self.device)
@@ -206,7 +220,8 @@ class TrainSession:
         for ids in micro_batches:
             ids = self._to_device(ids)
             with nvtx_range("forward"), torch.autocast(device_type=self.device.type, dtype=torch.bfloat16,
-                                                       enabled=self.autocast, cache_enabled=self._autocast_cache):
+                                                       enabled=self.autocast, cache_enabled=self._autocast_cache), \
+                    self._loss_scale_context(n):
                 loss = self.model(input_ids=ids, labels=ids, return_logits=False).loss
             with nvtx_range("backward"):
                 self.engine.backward(loss / n)

@@ -262,6 +262,73 @@ def test_cross_entropy(C):
     _close(work, lf.grad, 1e-2)
 
 
+def _lm_head_case(seed: int):
+    B, S, d, V = 2, 512, 256, 1024
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    x = (torch.randn(B, S, d, device="cuda", generator=g) * 0.5).to(torch.bfloat16).requires_grad_()
+    w = torch.nn.Parameter((torch.randn(V, d, device="cuda", generator=g) * 0.05).to(torch.bfloat16))
+    labels = torch.randint(0, V, (B, S), device="cuda", generator=g)
+    labels[0, ::5] = -100
+    return x, w, labels
+
+
+def _lm_head_reference(x, w, labels, scale):
+    xf = x.detach().float().requires_grad_()
+    wf = w.detach().float().requires_grad_()
+    logits = xf @ wf.t()
+    loss = F.cross_entropy(logits[:, :-1].reshape(-1, w.shape[0]), labels[:, 1:].reshape(-1), ignore_index=-100)
+    (loss * scale).backward()
+    return loss.detach(), xf.grad, wf.grad
+
+
+def test_lm_head_gradients_in_forward_match_fp32_and_the_logits_path(C, monkeypatch):
+    """With the loss-gradient scale announced, the LM head + cross-entropy computes dx and dW during the
+    forward pass in blocks of rows (no [T, V] logits tensor); loss and both gradients must match fp32
+    PyTorch and the path that keeps the logits for backward."""
+    from cs244c_llama_zero_b200.ops import functional as B
+
+    monkeypatch.setenv("ZB_LM_BLOCK_MB", "1")  # 512-row blocks: two blocks for 1024 tokens
+    scale = 0.5
+    x, w, labels = _lm_head_case(31)
+    loss_ref, dx_ref, dw_ref = _lm_head_reference(x, w, labels, scale)
+    w.main_grad = torch.zeros(w.shape, dtype=torch.float32, device="cuda")  # the flat-buffer sink
+    s_t = torch.full((), scale, dtype=torch.float32, device="cuda")
+    torch.cuda.synchronize()
+    torch.cuda.reset_peak_memory_stats()
+    before = torch.cuda.memory_allocated()
+    with B.loss_gradient_scale(s_t):
+        loss = B.lm_head_cross_entropy(x, w, labels)
+    # one 512-row block of logits (1 MB) and dx (0.5 MB) live, never the 2 MB of [T, V] logits
+    assert torch.cuda.max_memory_allocated() - before < 1024 * 1024 * 2
+    (loss * scale).backward()
+    torch.testing.assert_close(loss.detach(), loss_ref, rtol=2e-3, atol=2e-3)
+    _close(x.grad, dx_ref, 2e-2)
+    _close(w.main_grad, dw_ref, 2e-2)
+    assert list(C.read_device_errors()) == [0, 0, 0, 0]
+    # the logits-keeping path (no scale announced) gives the same gradients
+    x2, w2, _ = _lm_head_case(31)
+    w2.main_grad = torch.zeros(w2.shape, dtype=torch.float32, device="cuda")
+    loss2 = B.lm_head_cross_entropy(x2, w2, labels)
+    (loss2 * scale).backward()
+    torch.testing.assert_close(loss2.detach(), loss.detach(), rtol=1e-4, atol=1e-4)
+    _close(x.grad, x2.grad, 1e-2)
+    _close(w.main_grad, w2.main_grad, 1e-2)
+
+
+def test_lm_head_gradients_in_forward_flag_a_wrong_backward_scale(C, monkeypatch):
+    from cs244c_llama_zero_b200.ops import functional as B
+
+    monkeypatch.setenv("ZB_LM_BLOCK_MB", "1")
+    x, w, labels = _lm_head_case(32)
+    w.main_grad = torch.zeros(w.shape, dtype=torch.float32, device="cuda")
+    with B.loss_gradient_scale(torch.full((), 0.5, dtype=torch.float32, device="cuda")):
+        loss = B.lm_head_cross_entropy(x, w, labels)
+    loss.backward()  # scale 1, not the announced 0.5
+    torch.cuda.synchronize()
+    assert C.read_device_errors()[0] == 8
+    C.reset_device_errors()
+
+
 def _attn_ref(qkv, B, S, H, KV, hd):
     q = qkv[:, : H * hd].view(B, S, H, hd).transpose(1, 2)
     k = qkv[:, H * hd : (H + KV) * hd].view(B, S, KV, hd).transpose(1, 2)

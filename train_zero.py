@@ -12,6 +12,7 @@ device-timed iteration time maximised over ranks.
 from __future__ import annotations
 
 import argparse
+import contextlib
 import json
 import os
 import time
@@ -338,6 +339,19 @@ def train(args: argparse.Namespace) -> None:
         fb_timer = timers.timer("forward_backward")
         fb_timer.start()
 
+        loss_scales: Dict[int, torch.Tensor] = {}
+
+        def loss_scale_context(n: int):
+            """B200 backend: each micro-batch loss is back-propagated as loss / n, so the LM head may
+            compute its gradients during the forward pass (no [tokens, vocab] logits tensor)."""
+            if backend != "b200" or device.type != "cuda":
+                return contextlib.nullcontext()
+            from cs244c_llama_zero_b200.ops import functional as B
+
+            if n not in loss_scales:
+                loss_scales[n] = torch.full((), 1.0 / n, dtype=torch.float32, device=device)
+            return B.loss_gradient_scale(loss_scales[n])
+
         def run_microbatches() -> List[torch.Tensor]:
             nonlocal data_iter
             losses = []
@@ -350,7 +364,8 @@ def train(args: argparse.Namespace) -> None:
                 batch = batch_from_chunk(chunk)
                 ids = batch.input_ids.to(device, non_blocking=True)
                 labels = batch.labels.to(device, non_blocking=True)
-                with nvtx_range(f"forward.micro{micro + 1}"), autocast_context(device, args.dtype):
+                with nvtx_range(f"forward.micro{micro + 1}"), autocast_context(device, args.dtype), \
+                        loss_scale_context(args.grad_accum_steps):
                     loss = model(input_ids=ids, labels=labels, return_logits=False).loss
                 snap(f"micro_{micro + 1}_after_forward")
                 losses.append(loss.detach().float())
