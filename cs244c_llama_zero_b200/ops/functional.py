@@ -487,7 +487,7 @@ def shifted_targets(labels: torch.Tensor) -> torch.Tensor:
 # gradient.  Backward checks on the device that the scale it receives is the announced one and
 # records an error (``kErrGradScale``) otherwise.
 _LOSS_GRAD_SCALE: List[Optional[torch.Tensor]] = [None]
-LM_HEAD_BLOCK_BYTES = 128 << 20  # logits block of the gradient-in-forward path (rows rounded to 128)
+LM_HEAD_BLOCK_BYTES = 256 << 20  # logits block of the gradient-in-forward path (rows rounded to 128)
 
 
 class loss_gradient_scale:
