@@ -48,6 +48,8 @@ def parse_args(argv=None) -> argparse.Namespace:
     p.add_argument("--warmup", type=int, default=1)
     p.add_argument("--collective-impl", default="auto")
     p.add_argument("--output-json", default="")
+    p.add_argument("--pg-timeout", type=float, default=300.0,
+                   help="seconds a collective may wait before the process group reports an error")
     return p.parse_args(argv)
 
 
@@ -142,7 +144,7 @@ def main(argv=None) -> None:
     args = parse_args(argv)
     from ..train.session import init_distributed
 
-    rank, world, _ = init_distributed(600.0)
+    rank, world, _ = init_distributed(args.pg_timeout)
     impl = args.collective_impl
     if impl == "auto":
         impl = "nvls" if world > 1 else "torch"
