@@ -449,6 +449,9 @@ def run_mine(args) -> None:
                    "cuda_graph": bool(args.cuda_graph and args.headline_stage != 3),
                    "fused_step": bool(args.fused_step),
                    "routed_grads": bool(args.routed_grads),
+                   "stage2_grads": ("routed" if args.routed_grads else "full" if (
+                       args.fused_step or world == 1 or impl not in ("nvls", "p2p")
+                       or os.environ.get("ZB_STAGE2_GRADS", "ring") != "ring") else "ring"),
                    "l2": "no flush: each step touches >2 GB (activations, 1.2 GB fp32 optimizer state) vs 126 MB L2"},
         "per_stage": head["per_stage"],
         "per_config": per_config,

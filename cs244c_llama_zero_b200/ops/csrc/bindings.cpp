@@ -596,6 +596,19 @@ class CommContext {
     b200::comm_reduce_scatter_range_acc_f32(c_, off, lo, hi, acc.data_ptr<float>(), (float)scale, (int)blocks,
                                             cur_stream());
   }
+  // One gradient bucket of this buffer into the owners' shards (bases: every rank's fp32 shard as
+  // mapped on this GPU); the bucket region is zero afterwards on every rank.
+  void bucket_reduce(int64_t off, int64_t n, int64_t flat0, int64_t chunk, std::vector<int64_t> bases, double scale,
+                     bool balanced, int64_t blocks) {
+    TORCH_CHECK((int)bases.size() == c_.world, "bucket_reduce: one shard base per rank");
+    b200::RouteTable t{};
+    t.world = (int)bases.size();
+    t.chunk = chunk;
+    for (size_t r = 0; r < bases.size(); ++r) t.base[r] = (uint64_t)bases[r];
+    c10::cuda::CUDAGuard g(device_);
+    prepare();
+    b200::comm_bucket_reduce(c_, off, n, flat0, t, (float)scale, balanced, (int)blocks, cur_stream());
+  }
   void reduce_scatter_acc_bf16(int64_t off, int64_t chunk, Tensor acc, double scale) {
     check_acc(acc, chunk);
     c10::cuda::CUDAGuard g(device_);
@@ -978,6 +991,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
       .def("reduce_scatter_acc_f32", &CommContext::reduce_scatter_acc_f32)
       .def("reduce_scatter_acc_bf16", &CommContext::reduce_scatter_acc_bf16)
       .def("reduce_scatter_range_acc_f32", &CommContext::reduce_scatter_range_acc_f32)
+      .def("bucket_reduce", &CommContext::bucket_reduce, py::arg("off"), py::arg("n"), py::arg("flat0"),
+           py::arg("chunk"), py::arg("bases"), py::arg("scale"), py::arg("balanced"), py::arg("blocks") = 0)
       .def("allgather", &CommContext::allgather)
       .def("gather_ce", &CommContext::gather_ce)
       .def("adamw_allgather", &CommContext::adamw_allgather, py::arg("param_off"), py::arg("chunk"),

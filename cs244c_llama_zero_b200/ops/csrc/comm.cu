@@ -16,6 +16,8 @@
 //   rs_adamw_allgather   the whole ZeRO-2 step without clipping in one kernel: each rank ld_reduces
 //                        its chunk of the flat fp32 gradients, averages it, adds its squares to the
 //                        norm, runs AdamW and multicasts the bf16 result (no gradient shard in HBM)
+//   bucket_reduce        one gradient bucket (a transformer block's weights) reduced into the owners'
+//                        fp32 shards and the bucket buffer cleared for reuse (ZeRO-2 gradient ring)
 //
 // Ordering: every block of every rank runs the same grid, and block b synchronises with block b of
 // every peer at kernel start (all inputs written) and at kernel end (all outputs delivered).  The
@@ -292,27 +294,42 @@ __global__ void __launch_bounds__(kThreads) reduce_scatter_acc_bf16_kernel(CommC
   const uint32_t e = next_epoch(c);
   if (!block_barrier(c, 2 * e)) return;
   const size_t base = off + (size_t)c.rank * chunk8 * 16;
-  for (size_t i = gtid(); i < chunk8; i += gstride()) {
-    const size_t b = base + i * 16;
-    float v[8];
-    if constexpr (MC) {
-      bf16x8_to_f32(mc_ld_reduce_bf16x8(c.mc + b), v);
-    } else {
+  const size_t stride = gstride();
+  // kUnroll independent 16-byte loads in flight per thread (peer loads: W x kUnroll), as in the
+  // fp32 kernels: the reduction is bound by NVLink latency x bytes in flight.
+  for (size_t i0 = gtid(); i0 < chunk8; i0 += stride * kUnroll) {
+    uint4 q[kUnroll];
+    float v[kUnroll][8];
 #pragma unroll
-      for (int t = 0; t < 8; ++t) v[t] = 0.f;
-      for (int w = 0; w < c.world; ++w) {
-        float x[8];
-        bf16x8_to_f32(__ldcg(reinterpret_cast<const uint4*>(c.peers[w] + b)), x);
+    for (int u = 0; u < kUnroll; ++u) {
+      const size_t i = i0 + u * stride;
+      if (i >= chunk8) break;
+      const size_t b = base + i * 16;
+      if constexpr (MC) {
+        q[u] = mc_ld_reduce_bf16x8(c.mc + b);
+      } else {
 #pragma unroll
-        for (int t = 0; t < 8; ++t) v[t] += x[t];
+        for (int t = 0; t < 8; ++t) v[u][t] = 0.f;
+        for (int w = 0; w < c.world; ++w) {
+          float x[8];
+          bf16x8_to_f32(__ldcg(reinterpret_cast<const uint4*>(c.peers[w] + b)), x);
+#pragma unroll
+          for (int t = 0; t < 8; ++t) v[u][t] += x[t];
+        }
       }
     }
-    float4* a4 = reinterpret_cast<float4*>(acc + i * 8);
-    float4 a0 = a4[0], a1 = a4[1];
-    a0.x += scale * v[0]; a0.y += scale * v[1]; a0.z += scale * v[2]; a0.w += scale * v[3];
-    a1.x += scale * v[4]; a1.y += scale * v[5]; a1.z += scale * v[6]; a1.w += scale * v[7];
-    a4[0] = a0;
-    a4[1] = a1;
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+      const size_t i = i0 + u * stride;
+      if (i >= chunk8) break;
+      if constexpr (MC) bf16x8_to_f32(q[u], v[u]);
+      float4* a4 = reinterpret_cast<float4*>(acc + i * 8);
+      float4 a0 = a4[0], a1 = a4[1];
+      a0.x += scale * v[u][0]; a0.y += scale * v[u][1]; a0.z += scale * v[u][2]; a0.w += scale * v[u][3];
+      a1.x += scale * v[u][4]; a1.y += scale * v[u][5]; a1.z += scale * v[u][6]; a1.w += scale * v[u][7];
+      a4[0] = a0;
+      a4[1] = a1;
+    }
   }
   block_barrier(c, 2 * e + 1);
 }
@@ -323,13 +340,24 @@ __global__ void __launch_bounds__(kThreads) allgather_kernel(CommCtx c, size_t o
   const uint32_t e = next_epoch(c);
   if (!block_barrier(c, 2 * e)) return;
   const size_t base = off + (size_t)c.rank * chunk16 * 16;
-  for (size_t i = gtid(); i < chunk16; i += gstride()) {
-    const uint4 v = shard[i];
-    const size_t b = base + i * 16;
-    if constexpr (MC) {
-      mc_st_b128(c.mc + b, v);
-    } else {
-      for (int w = 0; w < c.world; ++w) __stcg(reinterpret_cast<uint4*>(c.peers[w] + b), v);
+  const size_t stride = gstride();
+  for (size_t i0 = gtid(); i0 < chunk16; i0 += stride * kUnroll) {
+    uint4 v[kUnroll];
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+      const size_t i = i0 + u * stride;
+      if (i < chunk16) v[u] = shard[i];
+    }
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+      const size_t i = i0 + u * stride;
+      if (i >= chunk16) break;
+      const size_t b = base + i * 16;
+      if constexpr (MC) {
+        mc_st_b128(c.mc + b, v[u]);
+      } else {
+        for (int w = 0; w < c.world; ++w) __stcg(reinterpret_cast<uint4*>(c.peers[w] + b), v[u]);
+      }
     }
   }
   block_barrier(c, 2 * e + 1);
@@ -502,6 +530,90 @@ __global__ void embedding_bwd_routed_kernel(const int64_t* __restrict__ ids, con
                         __float_as_uint(g[4 * h]), __float_as_uint(g[4 * h + 1]), __float_as_uint(g[4 * h + 2]),
                         __float_as_uint(g[4 * h + 3]));
     }
+  }
+}
+
+// Part of a gradient bucket that rank q reduces, in 16-byte vectors [lo, hi) from the bucket start.
+// balanced: the q-th of W equal slices.  Otherwise the slice inside rank q's own shard (flat
+// elements [q*chunk, (q+1)*chunk)); flat0 and chunk are multiples of 4, so vectors never straddle.
+__device__ __forceinline__ void bucket_part(int q, int world, size_t n4, long long flat0, long long chunk,
+                                            bool balanced, size_t& lo, size_t& hi) {
+  if (balanced) {
+    const size_t per = (n4 + world - 1) / world;
+    lo = min(n4, (size_t)q * per);
+    hi = min(n4, lo + per);
+    return;
+  }
+  long long a = (long long)q * chunk - flat0, b = a + chunk;
+  a = a < 0 ? 0 : a;
+  b = b > 4 * (long long)n4 ? 4 * (long long)n4 : b;
+  lo = hi = 0;
+  if (b > a) {
+    lo = (size_t)(a / 4);
+    hi = (size_t)(b / 4);
+  }
+}
+
+// One gradient bucket reduced into its owners' shards (ZeRO-2 with a ring of bucket buffers in
+// place of a full gradient buffer).  Region [off, off + 16*n4) of every rank's bucket buffer holds
+// that rank's gradient of flat elements [flat0, flat0 + 4*n4).  This rank reduces its part (see
+// bucket_part), scales it and adds each vector to the fp32 shard of the owning rank at
+// t.base[owner] + (flat - owner*chunk): in place when it owns the vector, with a system-scope
+// vector reduction over NVLink otherwise (each vector has exactly one writer).  After the closing
+// barrier every rank has read every bucket, and block b zeroes the vectors that block b of every
+// rank read from this rank's buffer, which leaves the buffer ready for the next bucket.
+template <bool MC>
+__global__ void __launch_bounds__(kThreads) bucket_reduce_kernel(CommCtx c, size_t off, size_t n4, long long flat0,
+                                                                  RouteTable t, float scale, int balanced) {
+  const uint32_t e = next_epoch(c);
+  if (!block_barrier(c, 2 * e)) return;
+  size_t lo, hi;
+  bucket_part(c.rank, c.world, n4, flat0, t.chunk, balanced != 0, lo, hi);
+  const size_t stride = gstride();
+  for (size_t i0 = lo + gtid(); i0 < hi; i0 += stride * kUnroll) {
+    float4 v[kUnroll];
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+      const size_t i = i0 + u * stride;
+      if (i >= hi) break;
+      const size_t b = off + i * 16;
+      if constexpr (MC) {
+        v[u] = mc_ld_reduce_f32x4(c.mc + b);
+      } else {
+        v[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int w = 0; w < c.world; ++w) {
+          const float4 x = __ldcg(reinterpret_cast<const float4*>(c.peers[w] + b));
+          v[u].x += x.x; v[u].y += x.y; v[u].z += x.z; v[u].w += x.w;
+        }
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+      const size_t i = i0 + u * stride;
+      if (i >= hi) break;
+      const long long f = flat0 + 4 * (long long)i;
+      const int owner = (int)(f / t.chunk);
+      if (owner >= t.world) {
+        report_error(c.errs, kErrBadIndex, 204);
+        continue;
+      }
+      float* dst = reinterpret_cast<float*>(t.base[owner]) + (f - (long long)owner * t.chunk);
+      const float4 x = make_float4(scale * v[u].x, scale * v[u].y, scale * v[u].z, scale * v[u].w);
+      if (owner == c.rank) {
+        float4 a = *reinterpret_cast<float4*>(dst);
+        a.x += x.x; a.y += x.y; a.z += x.z; a.w += x.w;
+        *reinterpret_cast<float4*>(dst) = a;
+      } else {
+        red_add_f32x4_sys(dst, __float_as_uint(x.x), __float_as_uint(x.y), __float_as_uint(x.z), __float_as_uint(x.w));
+      }
+    }
+  }
+  if (!block_barrier(c, 2 * e + 1)) return;
+  float4* mine = reinterpret_cast<float4*>(c.peers[c.rank] + off);
+  for (int q = 0; q < c.world; ++q) {
+    size_t a, b;
+    bucket_part(q, c.world, n4, flat0, t.chunk, balanced != 0, a, b);
+    for (size_t i = a + gtid(); i < b; i += stride) mine[i] = make_float4(0.f, 0.f, 0.f, 0.f);
   }
 }
 
@@ -750,6 +862,24 @@ void comm_embedding_bwd_routed(const int64_t* ids, const void* dy, int rows, int
   const int blocks = (int)std::min<size_t>((total + kThreads - 1) / kThreads, 4 * 148);
   embedding_bwd_routed_kernel<<<blocks, kThreads, 0, s>>>(ids, reinterpret_cast<const uint4*>(dy), rows, d, vocab,
                                                           flat0, t, errs);
+  B200_CUDA_CHECK(cudaGetLastError());
+  count_launch();
+}
+
+void comm_bucket_reduce(const CommCtx& c, size_t off, size_t n, long long flat0, const RouteTable& t, float scale,
+                        bool balanced, int blocks, cudaStream_t s) {
+  check_ctx(c);
+  B200_CHECK(t.world == c.world, "bucket_reduce: route table and context of different groups");
+  B200_CHECK(n % 4 == 0 && off % 16 == 0 && flat0 % 4 == 0 && flat0 >= 0 && t.chunk > 0 && t.chunk % 4 == 0,
+             "bucket_reduce: size, flat offset and shard size must be multiples of 4, offset 16-aligned");
+  B200_CHECK(flat0 + (long long)n <= t.chunk * (long long)t.world, "bucket_reduce: bucket outside the sharded space");
+  for (int r = 0; r < t.world; ++r)
+    B200_CHECK(t.base[r] != 0 && t.base[r] % 16 == 0, "bucket_reduce: shard bases must be 16-byte aligned");
+  const int grid = (blocks > 0 && blocks < c.blocks) ? blocks : c.blocks;
+  if (c.mc)
+    bucket_reduce_kernel<true><<<grid, kThreads, 0, s>>>(c, off, n / 4, flat0, t, scale, balanced ? 1 : 0);
+  else
+    bucket_reduce_kernel<false><<<grid, kThreads, 0, s>>>(c, off, n / 4, flat0, t, scale, balanced ? 1 : 0);
   B200_CUDA_CHECK(cudaGetLastError());
   count_launch();
 }

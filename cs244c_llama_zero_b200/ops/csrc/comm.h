@@ -72,6 +72,14 @@ struct RouteTable {
 };
 void comm_routed_add(const float* src, size_t n, long long flat0, const RouteTable& t, DeviceErrors* errs,
                      cudaStream_t s);
+// One gradient bucket into its owners' shards (ZeRO-2 with a ring of bucket buffers): region
+// [off, off + 4n) of every rank's buffer holds its fp32 gradient of flat elements [flat0, flat0 + n).
+// The sum over ranks times `scale` is added to the owners' shards (t, as for comm_routed_add); each
+// rank reduces 1/W of the bucket (`balanced`) or the part inside its own shard.  The buffer region
+// is zero on every rank when the kernel ends.  n, flat0 multiples of 4; `blocks` as for the range
+// reduce-scatter.
+void comm_bucket_reduce(const CommCtx& c, size_t off_bytes, size_t n, long long flat0, const RouteTable& t,
+                        float scale, bool balanced, int blocks, cudaStream_t s);
 // Embedding backward into the owners' shards: row r of dy (bf16 [rows, d], contiguous) is added at
 // table row ids[r] of the weight whose element (i, k) has flat index flat0 + i * d + k (ids outside
 // [0, vocab) are skipped).  d must be a multiple of 8, flat0 of 4.

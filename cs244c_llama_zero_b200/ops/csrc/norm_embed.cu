@@ -171,6 +171,71 @@ __global__ void __launch_bounds__(32 * kWarpsPerBlock)
   }
 }
 
+// Wide rows (d > 2048, e.g. the 7B model's 4096): the per-lane register tiles of the kernel above
+// would not fit, so each warp takes rows in turn and reads each row twice - pass 1 for the row's
+// dot product sum(dy * w * x_hat), pass 2 (L1 / L2 hits) to write dx and to add dy * x_hat into
+// its own fp32 weight-gradient row in shared memory (lane l owns columns 256k + 8l .. + 7, so the
+// updates need no atomics).  The block sums its warps' rows and adds them with one fp32 atomic per
+// column.
+constexpr int kWideWarps = 4;
+constexpr int kWideMaxD = 12288;  // kWideWarps fp32 rows of d columns in 192 KB of shared memory
+__global__ void __launch_bounds__(32 * kWideWarps)
+    rmsnorm_bwd_wide_kernel(const __nv_bfloat16* __restrict__ dy, const __nv_bfloat16* __restrict__ x,
+                            const __nv_bfloat16* __restrict__ w, const float* __restrict__ rstd,
+                            const __nv_bfloat16* __restrict__ dres, __nv_bfloat16* __restrict__ dx,
+                            float* __restrict__ dw, int rows, int d) {
+  pdl_wait_and_release();
+  extern __shared__ float4 dw_rows4[];  // [kWideWarps][d / 4]
+  float* dw_rows = reinterpret_cast<float*>(dw_rows4);
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  for (int c = threadIdx.x; c < kWideWarps * d; c += blockDim.x) dw_rows[c] = 0.f;
+  __syncthreads();
+  float* mine = dw_rows + (size_t)warp * d;
+  for (int row = blockIdx.x * kWideWarps + warp; row < rows; row += gridDim.x * kWideWarps) {
+    const float r = rstd[row];
+    const size_t base = (size_t)row * d;
+    float dot = 0.f;
+    for (int c = lane * 8; c < d; c += 256) {
+      float xv[8], dyv[8], wf[8];
+      unpack8(*reinterpret_cast<const uint4*>(x + base + c), xv);
+      unpack8(*reinterpret_cast<const uint4*>(dy + base + c), dyv);
+      unpack8(*reinterpret_cast<const uint4*>(w + c), wf);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) dot += dyv[e] * wf[e] * xv[e];
+    }
+    dot = warp_sum(dot) * r / (float)d;
+    for (int c = lane * 8; c < d; c += 256) {
+      float xv[8], dyv[8], wf[8], rv[8], o[8];
+      unpack8(*reinterpret_cast<const uint4*>(x + base + c), xv);
+      unpack8(*reinterpret_cast<const uint4*>(dy + base + c), dyv);
+      unpack8(*reinterpret_cast<const uint4*>(w + c), wf);
+      if (dres != nullptr) {
+        unpack8(*reinterpret_cast<const uint4*>(dres + base + c), rv);
+      } else {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) rv[e] = 0.f;
+      }
+#pragma unroll
+      for (int e = 0; e < 8; ++e) o[e] = rv[e] + r * (dyv[e] * wf[e] - xv[e] * r * dot);
+      *reinterpret_cast<uint4*>(dx + base + c) = pack8(o);
+      float4* acc = reinterpret_cast<float4*>(mine + c);
+      float4 a0 = acc[0], a1 = acc[1];
+      a0.x += dyv[0] * xv[0] * r; a0.y += dyv[1] * xv[1] * r; a0.z += dyv[2] * xv[2] * r; a0.w += dyv[3] * xv[3] * r;
+      a1.x += dyv[4] * xv[4] * r; a1.y += dyv[5] * xv[5] * r; a1.z += dyv[6] * xv[6] * r; a1.w += dyv[7] * xv[7] * r;
+      acc[0] = a0;
+      acc[1] = a1;
+    }
+  }
+  __syncthreads();
+  for (int c = threadIdx.x; c < d; c += blockDim.x) {
+    float t = 0.f;
+#pragma unroll
+    for (int k = 0; k < kWideWarps; ++k) t += dw_rows[(size_t)k * d + c];
+    atomicAdd(dw + c, t);
+  }
+}
+
 __global__ void embedding_fwd_kernel(const int64_t* __restrict__ ids, const __nv_bfloat16* __restrict__ table,
                                      __nv_bfloat16* __restrict__ out, int rows, int d, int vocab,
                                      DeviceErrors* errs) {
@@ -278,7 +343,21 @@ void rmsnorm_fwd(const __nv_bfloat16* x, const __nv_bfloat16* w, __nv_bfloat16* 
 
 void rmsnorm_bwd(const __nv_bfloat16* dy, const __nv_bfloat16* x, const __nv_bfloat16* w, const float* rstd,
                  const __nv_bfloat16* dres, __nv_bfloat16* dx, float* dw, int rows, int d, cudaStream_t s) {
-  B200_CHECK(d % 8 == 0 && d <= 256 * 8, "rmsnorm_bwd: d must be a multiple of 8 and at most 2048");
+  B200_CHECK(d % 8 == 0 && d <= kWideMaxD, "rmsnorm_bwd: d must be a multiple of 8 and at most 12288");
+  if (d > 256 * 8) {
+    const size_t smem = (size_t)kWideWarps * d * sizeof(float);
+    static std::atomic<unsigned long long> configured{0};
+    once_per_device(configured, [&] {
+      B200_CUDA_CHECK(cudaFuncSetAttribute(rmsnorm_bwd_wide_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           (int)((size_t)kWideWarps * kWideMaxD * sizeof(float))));
+    });
+    const int blocks = std::max(1, std::min((rows + kWideWarps - 1) / kWideWarps, 2 * num_sms_cached()));
+    launch_k(rmsnorm_bwd_wide_kernel, dim3(blocks), dim3(32 * kWideWarps), smem, s, 1, dy, x, w, rstd, dres, dx, dw,
+             rows, d);
+    B200_CUDA_CHECK(cudaGetLastError());
+    count_launch();
+    return;
+  }
   const int vec = (d + 255) / 256;
   const int per_block = kWarpsPerBlock * (vec <= 4 ? 2 : 1);
   const int blocks = std::max(1, (rows + per_block - 1) / per_block);

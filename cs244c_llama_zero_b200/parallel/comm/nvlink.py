@@ -208,6 +208,31 @@ class NvlinkCollectives(TorchCollectives):
         self._pace_end(slot, "reduce_scatter", (hi - lo) * 4)
         return True
 
+    supports_bucket_reduce = True
+
+    def bucket_reduce_to_owners_(self, bucket: torch.Tensor, flat0: int, chunk: int, bases: List[int], scale: float,
+                                 balanced: bool = True, blocks: int = 0) -> bool:
+        """Add ``scale * sum_ranks(bucket)`` into the owners' fp32 gradient shards and clear ``bucket``.
+
+        ``bucket`` (fp32, inside one of this object's symmetric buffers) holds this rank's gradient of
+        flat elements ``[flat0, flat0 + bucket.numel())``; ``bases`` is every rank's shard address as
+        mapped on this GPU (``shard_bases``), ``chunk`` the shard length.  With ``balanced`` each rank
+        reduces 1/W of the bucket and sends each sum to its owner; otherwise each rank reduces the
+        part it owns.  When the kernel ends the bucket is zero on every rank.  A collective: every
+        rank calls it for the same buckets in the same order.  Returns False, doing nothing, when the
+        bucket does not qualify (not symmetric fp32, sizes not multiples of 4)."""
+        hit = self._locate(bucket)
+        n = bucket.numel()
+        if hit is None or bucket.dtype != torch.float32 or n % 4 or flat0 % 4 or chunk % 4:
+            return False
+        buf, off = hit
+        if self._skipped("bucket_reduce"):
+            return True
+        slot = self._pace_begin()
+        buf.ctx.bucket_reduce(off, n, int(flat0), int(chunk), list(bases), float(scale), bool(balanced), int(blocks))
+        self._pace_end(slot, "reduce_scatter", n * 4)
+        return True
+
     def reduce_scatter_into(self, out: torch.Tensor, flat: torch.Tensor) -> torch.Tensor:
         if out.dtype == torch.float32 and self._locate(flat) is not None:
             out.zero_()

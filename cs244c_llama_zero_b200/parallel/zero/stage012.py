@@ -334,13 +334,19 @@ class ZeROStage2Optimizer(_ShardedStateMixin, _FlatEngine):
     shard_optimizer = True
 
     def __init__(self, model: nn.Module, grad_bucket_numel: int = 16 * 1024 * 1024, **kwargs) -> None:
+        self._ring = False
         super().__init__(model, **kwargs)
-        # Accepted for CLI compatibility: buckets are transformer blocks (see _setup_overlap).
+        # Accepted for CLI compatibility: buckets are transformer blocks (see _setup_ring).
         self.grad_bucket_numel = grad_bucket_numel
-        self._routed = self.space.grads is None
+        self._routed = self.space.grads is None and self._routed_requested()
         if self._routed:
             self._setup_routed()
             return
+        if self.space.grads is None:  # the gradient ring was requested
+            if self._setup_ring():
+                return
+            self.space.grads = self.collectives.alloc(self.space.padded_numel, torch.float32)
+            self.space.bind_grads()
         # On one rank the reduce-scatter is the identity, so the gradient shard IS the flat gradient
         # buffer: no copy of the gradients after backward, nothing extra to zero per step (stage 0's
         # memory traffic).  Several micro-batches accumulate in place, which gives the same sum.
@@ -355,7 +361,147 @@ class ZeROStage2Optimizer(_ShardedStateMixin, _FlatEngine):
 
     # -- gradients routed to their owners (no full gradient buffer) --------------------------------
     def _full_grad_buffer(self) -> bool:
-        return not self._routed_requested()
+        return not (self._routed_requested() or self._ring_requested())
+
+    # -- gradient ring: per-block buckets reduced into the owners' shards during backward ----------
+    def _ring_requested(self) -> bool:
+        """The default stage-2 gradient path with the NVLink collectives on several GPUs (unless
+        ``ZB_STAGE2_GRADS=full``, the fused one-kernel step or the overlapped flat-buffer
+        reduce-scatter is asked for)."""
+        mode = os.environ.get("ZB_STAGE2_GRADS", "ring")
+        return bool(mode == "ring" and self.world_size > 1 and self.device.type == "cuda"
+                    and os.environ.get("ZB_FUSED_STEP", "0") != "1"
+                    and os.environ.get("ZB_OVERLAP_REDUCE_SCATTER", "0") != "1"
+                    and getattr(self.collectives, "supports_bucket_reduce", False))
+
+    def _block_ranges(self) -> List[Tuple[int, int, List[nn.Parameter]]]:
+        """(lo, hi, params) of every transformer block's contiguous flat range, in flat order; hi is
+        rounded up to a multiple of 4 (parameters start 64-element aligned, so ranges stay disjoint)."""
+        offset = {id(p): off for p, off in zip(self.meta.params, self.space.offsets)}
+        out = []
+        for module in self.model.modules():
+            if type(module).__name__ != "TransformerBlock":
+                continue
+            ps = [p for p in module.parameters() if id(p) in offset]
+            if not ps:
+                continue
+            lo = min(offset[id(p)] for p in ps)
+            hi = max(offset[id(p)] + p.numel() for p in ps)
+            out.append((lo, (hi + 3) // 4 * 4, ps))
+        out.sort(key=lambda r: r[0])
+        for (_, hi0, _), (lo1, _, _) in zip(out, out[1:]):
+            if lo1 < hi0:
+                return []
+        if any(lo % 4 for lo, _, _ in out):
+            return []
+        return out
+
+    def _setup_ring(self) -> bool:
+        """Gradient memory without a full fp32 buffer, and the reduce-scatter spread over backward.
+
+        Each transformer block's weight gradients accumulate into one of ``ZB_STAGE2_RING_SLOTS``
+        (default 2) symmetric bucket buffers (block j uses slot j mod slots); the parameters outside
+        the blocks (embedding, final norm, LM head) into their own symmetric buffers.  As soon as a
+        block's backward has issued its weight gradients (the block kernels' grad-ready hook), one
+        kernel on the same stream reduces that bucket over NVLink straight into the owners' fp32
+        shards, averaged, and clears it (``bucket_reduce_to_owners_``); the slot is free for block
+        j - slots, which the stream runs afterwards.  The other buffers are reduced when backward
+        ends.  Gradient memory: the shard (4 B/param / W) plus the slots and the edge buffers,
+        instead of 4 B/param.  ``ZB_STAGE2_RING_SPLIT=owner`` makes each rank reduce the part of a
+        bucket it owns instead of 1/W of every bucket."""
+        ranges = self._block_ranges()
+        coll = self.collectives
+        if not ranges:
+            return False
+        self.grad_shard = coll.alloc(self.space.chunk, torch.float32)
+        bases = coll.shard_bases(self.grad_shard)
+        if bases is None:
+            return False
+        used = (self.space.numel + 3) // 4 * 4
+        edges, cursor = [], 0
+        for lo, hi, _ in ranges:
+            if lo > cursor:
+                edges.append((cursor, lo))
+            cursor = hi
+        if cursor < used:
+            edges.append((cursor, used))
+        n_slots = max(1, int(os.environ.get("ZB_STAGE2_RING_SLOTS", "2")))
+        slot_numel = max(hi - lo for lo, hi, _ in ranges)
+        self._ring_bases = bases
+        self._ring_ranges = [(lo, hi) for lo, hi, _ in ranges]
+        self._ring_slots = [coll.alloc(slot_numel, torch.float32) for _ in range(n_slots)]
+        self._ring_edges = [(lo, hi, coll.alloc(hi - lo, torch.float32)) for lo, hi in edges]
+        self._ring_balanced = os.environ.get("ZB_STAGE2_RING_SPLIT", "balanced") != "owner"
+        self._ring_block_of = {}
+        for j, (_, _, ps) in enumerate(ranges):
+            for p in ps:
+                self._ring_block_of[id(p)] = j
+        self._ring_params: List[List[Tuple[nn.Parameter, int]]] = [[] for _ in ranges]
+        self._ring_edge_params: List[List[Tuple[nn.Parameter, int]]] = [[] for _ in edges]
+        for p, off in zip(self.meta.params, self.space.offsets):
+            j = self._ring_block_of.get(id(p))
+            if j is not None:
+                lo = self._ring_ranges[j][0]
+                buf = self._ring_slots[j % n_slots]
+                self._ring_params[j].append((p, off))
+            else:
+                e = next(i for i, (lo_e, hi_e, _) in enumerate(self._ring_edges) if lo_e <= off < hi_e)
+                lo, _, buf = self._ring_edges[e]
+                self._ring_edge_params[e].append((p, off))
+            p.main_grad = buf[off - lo : off - lo + p.numel()].view(p.shape)
+        from ...ops import functional as F
+
+        self._ring = True
+        self._ring_hook = F.register_grad_ready_hook(self._on_ring_block_ready)
+        self._shard_is_buffer = False
+        self._pending_flush = False
+        self._overlap = False
+        self._fused_step = False
+        self._fused_sq = None
+        return True
+
+    def _ring_reduce(self, bucket: torch.Tensor, flat0: int) -> None:
+        with self.clock.measure("backward_reduce_scatter", bucket.numel() * 4):
+            with self.collectives.label_scope("stage2.backward.reduce_scatter.bucket"):
+                ok = self.collectives.bucket_reduce_to_owners_(bucket, flat0, self.space.chunk, self._ring_bases,
+                                                               1.0 / self.world_size, self._ring_balanced)
+        if not ok:
+            raise RuntimeError("gradient ring: bucket reduce unavailable")
+
+    def _ring_reduce_block(self, j: int) -> None:
+        lo, hi = self._ring_ranges[j]
+        self._ring_reduce(self._ring_slots[j % len(self._ring_slots)][: hi - lo], lo)
+
+    def _on_ring_block_ready(self, params) -> None:
+        """Every backward of a block writes its slot once and reduces it once, whoever runs it."""
+        j = self._ring_block_of.get(id(params[0])) if params else None
+        if j is not None:
+            self._ring_reduce_block(j)
+
+    @staticmethod
+    def _fold(pairs) -> None:
+        for p, _ in pairs:
+            if p.grad is not None:
+                p.main_grad.add_(p.grad.detach().to(torch.float32))
+                p.grad = None
+
+    def _ring_flush(self) -> None:
+        """After backward: blocks whose gradients autograd left in ``param.grad`` (modules that do not
+        run as one block kernel, so no hook fired), then the edge buffers."""
+        self._record_memory_event("measured_step_stage2_pre_reduce_scatter")
+        for j in reversed(range(len(self._ring_ranges))):
+            if any(p.grad is not None for p, _ in self._ring_params[j]):
+                self._fold(self._ring_params[j])
+                self._ring_reduce_block(j)
+        for (lo, _, buf), pairs in zip(self._ring_edges, self._ring_edge_params):
+            self._fold(pairs)
+            self._ring_reduce(buf, lo)
+        self._record_memory_event("measured_step_stage2_post_reduce_scatter")
+
+    def _ring_bytes(self) -> int:
+        if not self._ring:
+            return 0
+        return tensors_num_bytes(list(self._ring_slots) + [b for _, _, b in self._ring_edges])
 
     def _routed_requested(self) -> bool:
         return bool(os.environ.get("ZB_ROUTED_GRADS", "0") == "1" and self.world_size > 1
@@ -488,6 +634,13 @@ class ZeROStage2Optimizer(_ShardedStateMixin, _FlatEngine):
         return self.space.grads
 
     def zero_grad(self) -> None:
+        if self._ring:  # the buckets are cleared by the kernels that reduce them
+            self.clock.reset()
+            for p in self.meta.params:
+                p.grad = None
+            self.grad_shard.zero_()
+            self._pending_flush = True
+            return
         if self._routed:
             self.clock.reset()
             for p in self.meta.params:
@@ -502,6 +655,11 @@ class ZeROStage2Optimizer(_ShardedStateMixin, _FlatEngine):
         self._pending_flush = True
 
     def backward(self, loss: torch.Tensor) -> None:
+        if self._ring:
+            loss.backward()
+            self._ring_flush()
+            self._pending_flush = False
+            return
         if self._overlap:
             self._launched = []
             self._overlap_active = True
@@ -561,6 +719,9 @@ class ZeROStage2Optimizer(_ShardedStateMixin, _FlatEngine):
     def _update(self, max_grad_norm: float) -> torch.Tensor:
         if self._routed:
             return self._routed_update(max_grad_norm)
+        if self._ring and self._pending_flush:  # backward ran outside engine.backward()
+            self._ring_flush()
+            self._pending_flush = False
         if any(p.grad is not None for p in self.meta.params) and not hasattr(self.meta.params[0], "main_grad"):
             raise RuntimeError("Stage 2 expects gradients in the flat buffer")
         if self._fused_step and max_grad_norm <= 0 and self._pending_flush:
@@ -570,7 +731,8 @@ class ZeROStage2Optimizer(_ShardedStateMixin, _FlatEngine):
             if norm is not None:
                 self._pending_flush = False
                 return norm
-        self._flush_flat_grad_buffer()
+        if not self._ring:
+            self._flush_flat_grad_buffer()
         norm = global_norm_from_local_sq(sum_of_squares(self.grad_shard), sharded=self.world_size > 1,
                                          collectives=self.collectives)
         self.step_count += 1
@@ -600,7 +762,7 @@ class ZeROStage2Optimizer(_ShardedStateMixin, _FlatEngine):
             "logical_optimizer_mb": bytes_to_mb(tensors_num_bytes([self._master, self._exp_avg, self._exp_avg_sq])),
             "live_full_grads_mb": 0.0,
             "live_flat_grad_buffer_mb": bytes_to_mb(tensor_num_bytes(self.space.grads)) if self.space.grads is not None
-            else 0.0,
+            else bytes_to_mb(self._ring_bytes()),
             "live_grad_shard_mb": bytes_to_mb(tensor_num_bytes(self.grad_shard)),
             "comm_temp_mb": 0.0,
         }
@@ -611,7 +773,7 @@ class ZeROStage2Optimizer(_ShardedStateMixin, _FlatEngine):
     def live_model_state_breakdown_mb(self) -> Dict[str, float]:
         base = self.memory_state_breakdown_mb()
         shard_bytes = 0 if self._shard_is_buffer else tensor_num_bytes(self.grad_shard)  # a view of the buffer
-        flat_bytes = tensor_num_bytes(self.space.grads) if self.space.grads is not None else 0
+        flat_bytes = tensor_num_bytes(self.space.grads) if self.space.grads is not None else self._ring_bytes()
         grads_mb = bytes_to_mb(flat_bytes + shard_bytes)
         base["total_mb"] += grads_mb - base["grads_mb"]
         base["grads_mb"] = grads_mb

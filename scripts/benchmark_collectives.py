@@ -4,7 +4,11 @@ CLI-compatible with the reference's ``scripts/benchmark_collectives.py`` (``--op
 elements, ``--impl``, ``--dtype``, ``--iters``, ``--warmup``, ``--device``, ``--output-json``,
 ``--seed``; values ``randn`` seeded with ``1234 + rank``), extended with ``--impl nvls|p2p|all``,
 ``--sizes-bytes`` (e.g. the 1 KB .. 1 GB power-of-two sweep) and ``--check`` (compare every result
-with NCCL).  Times are device times (CUDA events around each call after a barrier), max over ranks;
+with NCCL).  On GPUs ``mean_ms`` is the device time per call of ``--iters`` calls enqueued back to
+back (CUDA events, max over ranks), so small messages show the collective's latency rather than the
+Python launch path; ``p50_ms`` / ``p95_ms`` / ``synced_mean_ms`` come from calls timed one at a time
+after a barrier and a synchronize (host launch included).  On CPU every figure is the one-at-a-time
+wall time, max over ranks;
 bus bandwidth uses the usual conventions: all-reduce ``2(W-1)/W * bytes``, reduce-scatter and
 all-gather ``(W-1)/W * bytes`` where bytes is the full (unsharded) buffer.  Each row also reports the
 fraction of the 900 GB/s-per-direction NVLink 5 figure and of the measured 770 GB/s peer copy.
@@ -51,6 +55,7 @@ class OpResult:
     frac_of_nvlink: float = 0.0
     frac_of_measured_peer: float = 0.0
     max_abs_err_vs_nccl: float = float("nan")
+    synced_mean_ms: float = float("nan")  # mean of the individually synchronised calls (host launch included)
 
 
 def parse_args(argv=None) -> argparse.Namespace:
@@ -97,7 +102,24 @@ def init(device_choice: str) -> torch.device:
     return torch.device("cuda", local) if use_cuda else torch.device("cpu")
 
 
+def _back_to_back_ms(fn, iters: int, device: torch.device) -> float:
+    """Device time per call of ``iters`` calls enqueued back to back (max over ranks): the host stays
+    ahead of the device, so the figure is the collective's own latency, not the launch path's."""
+    dist.barrier()
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(iters):
+        fn()
+    e.record()
+    e.synchronize()
+    t = torch.tensor([s.elapsed_time(e) / iters], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
 def _timed(fn, iters: int, warmup: int, device: torch.device) -> List[float]:
+    """Per-call samples, each bracketed by a barrier and a synchronize (includes the host launch)."""
     for _ in range(warmup):
         fn()
     samples = []
@@ -168,14 +190,15 @@ def run(op: str, impl: str, numel: int, dtype: torch.dtype, args, device, nvl: D
         else:
             fn = lambda: coll.allgather(shard, sizes=[chunk] * world)  # noqa: E731
     samples = sorted(_timed(fn, args.iters, args.warmup, device))
-    mean = sum(samples) / len(samples)
+    synced = sum(samples) / len(samples)
+    mean = _back_to_back_ms(fn, args.iters, device) if device.type == "cuda" else synced
     nbytes = numel * x.element_size()
     bus = bus_factor(op, world) * nbytes / (mean / 1000.0) / 1e9
     return OpResult(op=op, impl=impl, numel=numel, dtype=str(dtype).replace("torch.", ""),
                     bytes_sent_per_rank=bytes_per_rank(op, numel, world, x.element_size()), mean_ms=mean,
                     p50_ms=samples[len(samples) // 2], p95_ms=samples[min(len(samples) - 1, int(0.95 * len(samples)))],
                     bus_gbps=bus, frac_of_nvlink=bus / NVLINK_GBPS, frac_of_measured_peer=bus / MEASURED_PEER_GBPS,
-                    max_abs_err_vs_nccl=err)
+                    max_abs_err_vs_nccl=err, synced_mean_ms=synced)
 
 
 def main(argv=None) -> None:

@@ -460,3 +460,94 @@ def _routed_worker(rank: int, world: int, port: int, max_grad_norm: float, grad_
 @pytest.mark.parametrize("max_grad_norm,grad_accum", [(0.0, 1), (0.5, 2)])
 def test_routed_stage2_matches_reference(max_grad_norm: float, grad_accum: int) -> None:
     _spawn(_routed_worker, 2, max_grad_norm, grad_accum)
+
+
+class _RingCollectives(TorchCollectives):
+    """Gloo stand-in for the stage-2 gradient ring: a bucket reduce all-reduces the bucket, adds this
+    rank's share of the averaged sum into its shard and clears the bucket (what the NVLink bucket
+    kernel produces on GPUs)."""
+
+    supports_bucket_reduce = True
+
+    def __init__(self):
+        self.shard = None
+        self.reduces = []
+
+    def alloc(self, numel, dtype):
+        t = torch.zeros(numel, dtype=dtype)
+        if self.shard is None:  # the engine allocates its gradient shard first
+            self.shard = t
+        return t
+
+    def shard_bases(self, t):
+        return [2000 + r for r in range(dist.get_world_size())]
+
+    def bucket_reduce_to_owners_(self, bucket, flat0, chunk, bases, scale, balanced=True, blocks=0):
+        total = bucket.clone()
+        dist.all_reduce(total)
+        r = dist.get_rank()
+        lo, hi = max(flat0, r * chunk), min(flat0 + bucket.numel(), (r + 1) * chunk)
+        if hi > lo:
+            self.shard[lo - r * chunk:hi - r * chunk] += scale * total[lo - flat0:hi - flat0]
+        bucket.zero_()
+        self.reduces.append((flat0, bucket.numel()))
+        return True
+
+
+def _ring_worker(rank: int, world: int, port: int, max_grad_norm: float, grad_accum: int) -> None:
+    init_gloo(rank, world, port)
+    try:
+        cfg = _cfg()
+        torch.manual_seed(1234)
+        model = LlamaForCausalLM(cfg)
+        for p in model.parameters():
+            dist.broadcast(p.data, src=0)
+        ref = LlamaForCausalLM(cfg)
+        ref.load_state_dict(model.state_dict())
+        hp = dict(lr=1e-3, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.05)
+        coll = _RingCollectives()
+        ZeROStage2Optimizer._ring_requested = lambda self: True  # what NVLink collectives enable on GPUs
+        engine = ZeROStage2Optimizer(model=model, collectives=coll, **hp)
+        assert engine._ring and engine.space.grads is None and engine.grad_shard is coll.shard
+        assert len(engine._ring_ranges) == cfg.n_layers and len(engine._ring_slots) == 2
+        opt = torch.optim.AdamW(ref.parameters(), **hp)
+        for step in range(3):
+            micro = [_local_batch(step * 10 + m, rank, 3, cfg.max_seq_len, cfg.vocab_size) for m in range(grad_accum)]
+            engine.zero_grad()
+            engine.prepare_forward()
+            for ids in micro:
+                engine.backward(model(input_ids=ids, labels=ids).loss / grad_accum)
+            norm = engine.step(max_grad_norm=max_grad_norm)
+            opt.zero_grad(set_to_none=True)
+            for ids in micro:
+                parts = [torch.empty_like(ids) for _ in range(world)]
+                dist.all_gather(parts, ids)
+                g = torch.cat(parts)
+                (ref(input_ids=g, labels=g).loss / grad_accum).backward()
+            want = torch.sqrt(sum(p.grad.float().pow(2).sum() for p in ref.parameters()))
+            if max_grad_norm > 0:
+                torch.nn.utils.clip_grad_norm_(ref.parameters(), max_norm=max_grad_norm)
+            opt.step()
+            _assert_close(model, ref, f"ring step={step} rank={rank}")
+            torch.testing.assert_close(torch.tensor(norm), want, rtol=1e-4, atol=1e-6)
+        # every block bucket and every edge bucket reduced once per backward, and nothing else
+        per_backward = len(engine._ring_ranges) + len(engine._ring_edges)
+        assert len(coll.reduces) == 3 * grad_accum * per_backward
+        covered = sorted(set(coll.reduces))
+        cursor = 0
+        for flat0, n in covered:
+            assert flat0 == cursor, (flat0, cursor)
+            cursor = flat0 + n
+        assert cursor >= engine.space.numel
+        live = engine.live_model_state_breakdown_mb()
+        # the shard plus the ring's slots and edge buffers (no full gradient buffer)
+        assert live["grads_mb"] == pytest.approx((engine.space.chunk * 4 + engine._ring_bytes()) / 2 ** 20)
+        assert all(t.numel() == max(hi - lo for lo, hi in engine._ring_ranges) for t in engine._ring_slots)
+    finally:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("max_grad_norm,grad_accum", [(0.0, 1), (0.5, 2)])
+def test_ring_stage2_matches_reference(max_grad_norm: float, grad_accum: int) -> None:
+    _spawn(_ring_worker, 2, max_grad_norm, grad_accum)
