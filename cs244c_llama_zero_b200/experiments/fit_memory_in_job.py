@@ -8,8 +8,8 @@ its time building the model, and a probe that runs out of memory on one rank can
 waiting inside a collective.  This runner keeps one process group per GPU count and, per stage:
 
 1. builds the engine once (parameters created on the GPUs),
-2. runs two training steps at each probe batch size (``--probe-batches``, default 1 and 2) and reads
-   the allocator's peak (max over ranks),
+2. runs two training steps at each probe batch size (``--probe-batches``, default 1 and 2), with the
+   allocator's cache emptied first, and reads the allocated peak (max over ranks),
 3. fits ``peak(b) = slope * b + base`` (the reference's ``memory_model`` predictor kind) and takes
    ``b_max = floor((capacity_fraction * total_memory - base) / slope)``, min over ranks,
 4. times ``--steps`` steps at ``b_max`` (device events, max over ranks) and records tokens/s and the
@@ -41,8 +41,9 @@ def parse_args(argv=None) -> argparse.Namespace:
     p.add_argument("--seq-len", type=int, default=2048)
     p.add_argument("--stages", default="0,1,2,3")
     p.add_argument("--probe-batches", default="1,2")
-    p.add_argument("--capacity-fraction", type=float, default=0.88,
-                   help="share of the GPU's memory the predicted batch may use (the rest is headroom)")
+    p.add_argument("--capacity-fraction", type=float, default=0.85,
+                   help="share of the GPU's memory the predicted batch's allocated peak may use (the rest is "
+                        "headroom for the allocator's fragmentation)")
     p.add_argument("--max-batch", type=int, default=256)
     p.add_argument("--steps", type=int, default=3)
     p.add_argument("--warmup", type=int, default=1)
@@ -98,12 +99,15 @@ def measure_stage(args, stage: int, rank: int, world: int, impl: str) -> Dict[st
     points = []
     for b in [int(x) for x in args.probe_batches.split(",")]:
         ids = _batch(b, args.seq_len, BASELINE_VOCAB_SIZE, 7 + rank).to(dev)
+        # The allocator's cache from the build (or the previous probe) would absorb this probe's
+        # activations and flatten the fitted slope: release it, and fit the allocated peak.
         torch.cuda.synchronize(dev)
+        torch.cuda.empty_cache()
         torch.cuda.reset_peak_memory_stats(dev)
         for _ in range(2):
             sess.train_step(ids)
         torch.cuda.synchronize(dev)
-        points.append((b, _max_over_ranks(torch.cuda.max_memory_reserved(dev) / 2**20)))
+        points.append((b, _max_over_ranks(torch.cuda.max_memory_allocated(dev) / 2**20)))
         del ids
     slope, base = fit_line(points)
     b_max = predict_max_batch(slope, base, total_mb, args.capacity_fraction, args.max_batch)
@@ -112,7 +116,7 @@ def measure_stage(args, stage: int, rank: int, world: int, impl: str) -> Dict[st
         dist.all_reduce(t, op=dist.ReduceOp.MIN)
         b_max = int(t.item())
     rec: Dict[str, object] = {"stage": stage, "world_size": world, "build_s": build_s,
-                              "probe_peak_reserved_mb": points, "slope_mb_per_sample": slope,
+                              "probe_peak_allocated_mb": points, "slope_mb_per_sample": slope,
                               "base_mb": base, "gpu_total_mb": total_mb,
                               "capacity_fraction": args.capacity_fraction, "selected_batch_size": b_max}
     if b_max >= 1:

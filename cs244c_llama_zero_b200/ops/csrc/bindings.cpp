@@ -596,18 +596,39 @@ class CommContext {
     b200::comm_reduce_scatter_range_acc_f32(c_, off, lo, hi, acc.data_ptr<float>(), (float)scale, (int)blocks,
                                             cur_stream());
   }
-  // One gradient bucket of this buffer into the owners' shards (bases: every rank's fp32 shard as
-  // mapped on this GPU); the bucket region is zero afterwards on every rank.
-  void bucket_reduce(int64_t off, int64_t n, int64_t flat0, int64_t chunk, std::vector<int64_t> bases, double scale,
-                     bool balanced, int64_t blocks) {
-    TORCH_CHECK((int)bases.size() == c_.world, "bucket_reduce: one shard base per rank");
-    b200::RouteTable t{};
-    t.world = (int)bases.size();
-    t.chunk = chunk;
-    for (size_t r = 0; r < bases.size(); ++r) t.base[r] = (uint64_t)bases[r];
+  // Gradient ring: acc[0, part) += scale * sum_ranks(slice `rank` of the bucket at off); the bucket is
+  // zero on every rank afterwards (see comm.h).
+  void bucket_reduce(int64_t off, int64_t part, Tensor acc, double scale, int64_t blocks) {
+    check_acc(acc, part);
     c10::cuda::CUDAGuard g(device_);
     prepare();
-    b200::comm_bucket_reduce(c_, off, n, flat0, t, (float)scale, balanced, (int)blocks, cur_stream());
+    b200::comm_bucket_reduce(c_, off, part, acc.data_ptr<float>(), (float)scale, (int)blocks, cur_stream());
+  }
+  // AdamW on an interleaved ring shard + bf16 all-gather into this (parameter) buffer.  segs: int64
+  // CUDA tensor [nseg, 4] of (shard8, part8, valid8, param_off) rows.
+  void adamw_allgather_seg(Tensor segs, int64_t total, Tensor master, Tensor m, Tensor v, Tensor grad,
+                           std::optional<Tensor> scale, double scale_const, double lr, double beta1, double beta2,
+                           double eps, double wd, int64_t step, std::optional<Tensor> dev_scalars) {
+    TORCH_CHECK(segs.is_cuda() && segs.scalar_type() == at::kLong && segs.dim() == 2 && segs.size(1) == 4 &&
+                    segs.is_contiguous() && segs.size(0) >= 1,
+                "adamw_allgather_seg: segments must be a contiguous CUDA int64 [n, 4] tensor");
+    for (auto* t : {&master, &m, &v, &grad}) {
+      check_f32(*t, "adam state");
+      TORCH_CHECK(t->is_contiguous() && t->numel() >= total, "adam state too small");
+    }
+    const float* sp = nullptr;
+    if (scale.has_value()) {
+      check_f32(*scale, "scale");
+      sp = scale->data_ptr<float>();
+    }
+    c10::cuda::CUDAGuard g(device_);
+    prepare();
+    static_assert(sizeof(b200::RingSeg) == 4 * sizeof(int64_t), "RingSeg layout");
+    b200::comm_adamw_allgather_seg(c_, reinterpret_cast<const b200::RingSeg*>(segs.data_ptr<int64_t>()),
+                                   (int)segs.size(0), (size_t)total, master.data_ptr<float>(), m.data_ptr<float>(),
+                                   v.data_ptr<float>(), grad.data_ptr<float>(), sp, (float)scale_const, (float)lr,
+                                   (float)beta1, (float)beta2, (float)eps, (float)wd, (int)step, cur_stream(),
+                                   dev_scalars_ptr(dev_scalars));
   }
   void reduce_scatter_acc_bf16(int64_t off, int64_t chunk, Tensor acc, double scale) {
     check_acc(acc, chunk);
@@ -991,8 +1012,12 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
       .def("reduce_scatter_acc_f32", &CommContext::reduce_scatter_acc_f32)
       .def("reduce_scatter_acc_bf16", &CommContext::reduce_scatter_acc_bf16)
       .def("reduce_scatter_range_acc_f32", &CommContext::reduce_scatter_range_acc_f32)
-      .def("bucket_reduce", &CommContext::bucket_reduce, py::arg("off"), py::arg("n"), py::arg("flat0"),
-           py::arg("chunk"), py::arg("bases"), py::arg("scale"), py::arg("balanced"), py::arg("blocks") = 0)
+      .def("bucket_reduce", &CommContext::bucket_reduce, py::arg("off"), py::arg("part"), py::arg("acc"),
+           py::arg("scale"), py::arg("blocks") = 0)
+      .def("adamw_allgather_seg", &CommContext::adamw_allgather_seg, py::arg("segs"), py::arg("total"),
+           py::arg("master"), py::arg("m"), py::arg("v"), py::arg("grad"), py::arg("scale"), py::arg("scale_const"),
+           py::arg("lr"), py::arg("beta1"), py::arg("beta2"), py::arg("eps"), py::arg("wd"), py::arg("step"),
+           py::arg("dev_scalars") = py::none())
       .def("allgather", &CommContext::allgather)
       .def("gather_ce", &CommContext::gather_ce)
       .def("adamw_allgather", &CommContext::adamw_allgather, py::arg("param_off"), py::arg("chunk"),

@@ -16,8 +16,11 @@
 //   rs_adamw_allgather   the whole ZeRO-2 step without clipping in one kernel: each rank ld_reduces
 //                        its chunk of the flat fp32 gradients, averages it, adds its squares to the
 //                        norm, runs AdamW and multicasts the bf16 result (no gradient shard in HBM)
-//   bucket_reduce        one gradient bucket (a transformer block's weights) reduced into the owners'
-//                        fp32 shards and the bucket buffer cleared for reuse (ZeRO-2 gradient ring)
+//   bucket_reduce        one gradient bucket (a transformer block's weights): each rank reduces its
+//                        slice into its fp32 gradient segment, then the bucket buffer is cleared for
+//                        reuse (ZeRO-2 gradient ring, interleaved shards)
+//   adamw_allgather_seg  AdamW on the interleaved shard and the bf16 result multicast into every
+//                        rank's parameter buffer, segment by segment
 //
 // Ordering: every block of every rank runs the same grid, and block b synchronises with block b of
 // every peer at kernel start (all inputs written) and at kernel end (all outputs delivered).  The
@@ -533,50 +536,27 @@ __global__ void embedding_bwd_routed_kernel(const int64_t* __restrict__ ids, con
   }
 }
 
-// Part of a gradient bucket that rank q reduces, in 16-byte vectors [lo, hi) from the bucket start.
-// balanced: the q-th of W equal slices.  Otherwise the slice inside rank q's own shard (flat
-// elements [q*chunk, (q+1)*chunk)); flat0 and chunk are multiples of 4, so vectors never straddle.
-__device__ __forceinline__ void bucket_part(int q, int world, size_t n4, long long flat0, long long chunk,
-                                            bool balanced, size_t& lo, size_t& hi) {
-  if (balanced) {
-    const size_t per = (n4 + world - 1) / world;
-    lo = min(n4, (size_t)q * per);
-    hi = min(n4, lo + per);
-    return;
-  }
-  long long a = (long long)q * chunk - flat0, b = a + chunk;
-  a = a < 0 ? 0 : a;
-  b = b > 4 * (long long)n4 ? 4 * (long long)n4 : b;
-  lo = hi = 0;
-  if (b > a) {
-    lo = (size_t)(a / 4);
-    hi = (size_t)(b / 4);
-  }
-}
-
-// One gradient bucket reduced into its owners' shards (ZeRO-2 with a ring of bucket buffers in
-// place of a full gradient buffer).  Region [off, off + 16*n4) of every rank's bucket buffer holds
-// that rank's gradient of flat elements [flat0, flat0 + 4*n4).  This rank reduces its part (see
-// bucket_part), scales it and adds each vector to the fp32 shard of the owning rank at
-// t.base[owner] + (flat - owner*chunk): in place when it owns the vector, with a system-scope
-// vector reduction over NVLink otherwise (each vector has exactly one writer).  After the closing
-// barrier every rank has read every bucket, and block b zeroes the vectors that block b of every
-// rank read from this rank's buffer, which leaves the buffer ready for the next bucket.
+// One gradient bucket of the ZeRO-2 gradient ring.  The bucket region [off, off + 16*W*part4) of
+// every rank's bucket buffer holds that rank's gradient of one transformer block (zero past the
+// block's end); rank r owns slice r (vectors [r*part4, (r+1)*part4)) of every bucket, so it reduces
+// that slice over the ranks and adds scale * sum into its local fp32 gradient segment acc[0, part4)
+// - no remote writes.  After the closing barrier every rank has read every slice, and block b
+// zeroes the vectors that block b of every rank read from this rank's buffer: the buffer is ready
+// for the next bucket.
 template <bool MC>
-__global__ void __launch_bounds__(kThreads) bucket_reduce_kernel(CommCtx c, size_t off, size_t n4, long long flat0,
-                                                                  RouteTable t, float scale, int balanced) {
+__global__ void __launch_bounds__(kThreads) bucket_reduce_kernel(CommCtx c, size_t off, size_t part4, float4* acc,
+                                                                  float scale) {
   const uint32_t e = next_epoch(c);
   if (!block_barrier(c, 2 * e)) return;
-  size_t lo, hi;
-  bucket_part(c.rank, c.world, n4, flat0, t.chunk, balanced != 0, lo, hi);
+  const size_t base = off + (size_t)c.rank * part4 * 16;
   const size_t stride = gstride();
-  for (size_t i0 = lo + gtid(); i0 < hi; i0 += stride * kUnroll) {
+  for (size_t i0 = gtid(); i0 < part4; i0 += stride * kUnroll) {
     float4 v[kUnroll];
 #pragma unroll
     for (int u = 0; u < kUnroll; ++u) {
       const size_t i = i0 + u * stride;
-      if (i >= hi) break;
-      const size_t b = off + i * 16;
+      if (i >= part4) break;
+      const size_t b = base + i * 16;
       if constexpr (MC) {
         v[u] = mc_ld_reduce_f32x4(c.mc + b);
       } else {
@@ -590,31 +570,72 @@ __global__ void __launch_bounds__(kThreads) bucket_reduce_kernel(CommCtx c, size
 #pragma unroll
     for (int u = 0; u < kUnroll; ++u) {
       const size_t i = i0 + u * stride;
-      if (i >= hi) break;
-      const long long f = flat0 + 4 * (long long)i;
-      const int owner = (int)(f / t.chunk);
-      if (owner >= t.world) {
-        report_error(c.errs, kErrBadIndex, 204);
-        continue;
-      }
-      float* dst = reinterpret_cast<float*>(t.base[owner]) + (f - (long long)owner * t.chunk);
-      const float4 x = make_float4(scale * v[u].x, scale * v[u].y, scale * v[u].z, scale * v[u].w);
-      if (owner == c.rank) {
-        float4 a = *reinterpret_cast<float4*>(dst);
-        a.x += x.x; a.y += x.y; a.z += x.z; a.w += x.w;
-        *reinterpret_cast<float4*>(dst) = a;
-      } else {
-        red_add_f32x4_sys(dst, __float_as_uint(x.x), __float_as_uint(x.y), __float_as_uint(x.z), __float_as_uint(x.w));
-      }
+      if (i >= part4) break;
+      float4 a = acc[i];
+      a.x += scale * v[u].x; a.y += scale * v[u].y; a.z += scale * v[u].z; a.w += scale * v[u].w;
+      acc[i] = a;
     }
   }
   if (!block_barrier(c, 2 * e + 1)) return;
+  // Block b of rank q read vectors q*part4 + j with j on the grid-stride walk from gtid(); the same
+  // walk over every slice here clears exactly what block b of every rank has finished reading.
   float4* mine = reinterpret_cast<float4*>(c.peers[c.rank] + off);
   for (int q = 0; q < c.world; ++q) {
-    size_t a, b;
-    bucket_part(q, c.world, n4, flat0, t.chunk, balanced != 0, a, b);
-    for (size_t i = a + gtid(); i < b; i += stride) mine[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+    float4* slice = mine + (size_t)q * part4;
+    for (size_t j = gtid(); j < part4; j += stride) slice[j] = make_float4(0.f, 0.f, 0.f, 0.f);
   }
+}
+
+// AdamW on this rank's fp32 shard of the gradient ring's interleaved layout, with the bf16 result
+// multicast into every rank's parameter buffer.  The shard is the concatenation of segments: segment
+// s holds, at shard positions [seg[s].shard8 * 8, + part8 * 8), slice `rank` of one bucket, i.e. flat
+// parameters starting at seg[s].param_off (bytes) + rank * part8 * 16; only its first seg[s].valid8
+// groups of 8 lie inside the bucket (the rest pad the slice to a common length and are not written).
+template <bool MC>
+__global__ void __launch_bounds__(kThreads) adamw_allgather_seg_kernel(CommCtx c, const RingSeg* __restrict__ seg,
+                                                                       int nseg, size_t total8, float4* master,
+                                                                       float4* m, float4* v, const float4* g,
+                                                                       const float* scale_ptr, AdamScalars a,
+                                                                       const float* dev_sc) {
+  const uint32_t e = next_epoch(c);
+  if (!block_barrier(c, 2 * e)) return;
+  const float scale = (scale_ptr != nullptr ? *scale_ptr : 1.0f) * a.scale_const;
+  if (dev_sc != nullptr) {
+    a.step = dev_sc[0];
+    a.inv_sqrt_bc2 = dev_sc[1];
+  }
+  int s = 0;
+  for (size_t i = gtid(); i < total8; i += gstride()) {
+    while (s + 1 < nseg && (size_t)seg[s + 1].shard8 <= i) ++s;  // i only grows within a thread
+    float out[8];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const size_t k = 2 * i + h;
+      float4 gp = g[k], mp = m[k], vp = v[k], pp = master[k];
+      float gg[4] = {gp.x * scale, gp.y * scale, gp.z * scale, gp.w * scale};
+      float mm[4] = {mp.x, mp.y, mp.z, mp.w}, vv[4] = {vp.x, vp.y, vp.z, vp.w}, pw[4] = {pp.x, pp.y, pp.z, pp.w};
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        mm[t] = a.beta1 * mm[t] + (1.0f - a.beta1) * gg[t];
+        vv[t] = a.beta2 * vv[t] + (1.0f - a.beta2) * gg[t] * gg[t];
+        pw[t] = pw[t] * a.decay - a.step * mm[t] / (sqrtf(vv[t]) * a.inv_sqrt_bc2 + a.eps);
+        out[4 * h + t] = pw[t];
+      }
+      m[k] = make_float4(mm[0], mm[1], mm[2], mm[3]);
+      v[k] = make_float4(vv[0], vv[1], vv[2], vv[3]);
+      master[k] = make_float4(pw[0], pw[1], pw[2], pw[3]);
+    }
+    const long long j = (long long)i - seg[s].shard8;
+    if (j >= seg[s].valid8) continue;
+    const uint4 o = f32_to_bf16x8(out);
+    const size_t b = (size_t)seg[s].param_off + ((size_t)c.rank * seg[s].part8 + (size_t)j) * 16;
+    if constexpr (MC) {
+      mc_st_b128(c.mc + b, o);
+    } else {
+      for (int w = 0; w < c.world; ++w) __stcg(reinterpret_cast<uint4*>(c.peers[w] + b), o);
+    }
+  }
+  block_barrier(c, 2 * e + 1);
 }
 
 __global__ void barrier_kernel(CommCtx c) {
@@ -866,20 +887,49 @@ void comm_embedding_bwd_routed(const int64_t* ids, const void* dy, int rows, int
   count_launch();
 }
 
-void comm_bucket_reduce(const CommCtx& c, size_t off, size_t n, long long flat0, const RouteTable& t, float scale,
-                        bool balanced, int blocks, cudaStream_t s) {
+void comm_bucket_reduce(const CommCtx& c, size_t off, size_t part, float* acc, float scale, int blocks,
+                        cudaStream_t s) {
   check_ctx(c);
-  B200_CHECK(t.world == c.world, "bucket_reduce: route table and context of different groups");
-  B200_CHECK(n % 4 == 0 && off % 16 == 0 && flat0 % 4 == 0 && flat0 >= 0 && t.chunk > 0 && t.chunk % 4 == 0,
-             "bucket_reduce: size, flat offset and shard size must be multiples of 4, offset 16-aligned");
-  B200_CHECK(flat0 + (long long)n <= t.chunk * (long long)t.world, "bucket_reduce: bucket outside the sharded space");
-  for (int r = 0; r < t.world; ++r)
-    B200_CHECK(t.base[r] != 0 && t.base[r] % 16 == 0, "bucket_reduce: shard bases must be 16-byte aligned");
+  B200_CHECK(part % 4 == 0 && off % 16 == 0 && (reinterpret_cast<uintptr_t>(acc) & 15) == 0,
+             "bucket_reduce: slice length must be a multiple of 4, offset and acc 16-aligned");
   const int grid = (blocks > 0 && blocks < c.blocks) ? blocks : c.blocks;
+  auto* a4 = reinterpret_cast<float4*>(acc);
   if (c.mc)
-    bucket_reduce_kernel<true><<<grid, kThreads, 0, s>>>(c, off, n / 4, flat0, t, scale, balanced ? 1 : 0);
+    bucket_reduce_kernel<true><<<grid, kThreads, 0, s>>>(c, off, part / 4, a4, scale);
   else
-    bucket_reduce_kernel<false><<<grid, kThreads, 0, s>>>(c, off, n / 4, flat0, t, scale, balanced ? 1 : 0);
+    bucket_reduce_kernel<false><<<grid, kThreads, 0, s>>>(c, off, part / 4, a4, scale);
+  B200_CUDA_CHECK(cudaGetLastError());
+  count_launch();
+}
+
+void comm_adamw_allgather_seg(const CommCtx& c, const RingSeg* segs, int nseg, size_t total, float* master, float* m,
+                              float* v, const float* grad, const float* scale_ptr, float scale_const, float lr,
+                              float beta1, float beta2, float eps, float wd, int step, cudaStream_t s,
+                              const float* dev_sc) {
+  check_ctx(c);
+  B200_CHECK(total % 8 == 0 && nseg >= 1, "adamw_allgather_seg: shard length must be a multiple of 8");
+  B200_CHECK(((reinterpret_cast<uintptr_t>(master) | reinterpret_cast<uintptr_t>(m) | reinterpret_cast<uintptr_t>(v) |
+               reinterpret_cast<uintptr_t>(grad)) & 15) == 0,
+             "adamw_allgather_seg: optimizer state and gradient must be 16-byte aligned");
+  AdamScalars a;
+  a.lr = lr;
+  a.beta1 = beta1;
+  a.beta2 = beta2;
+  a.eps = eps;
+  a.decay = 1.0f - lr * wd;
+  a.step = (float)(lr / (1.0 - std::pow((double)beta1, (double)step)));
+  a.inv_sqrt_bc2 = (float)(1.0 / std::sqrt(1.0 - std::pow((double)beta2, (double)step)));
+  a.scale_const = scale_const;
+  auto* M = reinterpret_cast<float4*>(master);
+  auto* Mm = reinterpret_cast<float4*>(m);
+  auto* Vv = reinterpret_cast<float4*>(v);
+  auto* G = reinterpret_cast<const float4*>(grad);
+  if (c.mc)
+    adamw_allgather_seg_kernel<true><<<c.blocks, kThreads, 0, s>>>(c, segs, nseg, total / 8, M, Mm, Vv, G, scale_ptr,
+                                                                    a, dev_sc);
+  else
+    adamw_allgather_seg_kernel<false><<<c.blocks, kThreads, 0, s>>>(c, segs, nseg, total / 8, M, Mm, Vv, G,
+                                                                     scale_ptr, a, dev_sc);
   B200_CUDA_CHECK(cudaGetLastError());
   count_launch();
 }

@@ -72,14 +72,28 @@ struct RouteTable {
 };
 void comm_routed_add(const float* src, size_t n, long long flat0, const RouteTable& t, DeviceErrors* errs,
                      cudaStream_t s);
-// One gradient bucket into its owners' shards (ZeRO-2 with a ring of bucket buffers): region
-// [off, off + 4n) of every rank's buffer holds its fp32 gradient of flat elements [flat0, flat0 + n).
-// The sum over ranks times `scale` is added to the owners' shards (t, as for comm_routed_add); each
-// rank reduces 1/W of the bucket (`balanced`) or the part inside its own shard.  The buffer region
-// is zero on every rank when the kernel ends.  n, flat0 multiples of 4; `blocks` as for the range
-// reduce-scatter.
-void comm_bucket_reduce(const CommCtx& c, size_t off_bytes, size_t n, long long flat0, const RouteTable& t,
-                        float scale, bool balanced, int blocks, cudaStream_t s);
+// ZeRO-2 gradient ring (interleaved shards): region [off, off + 4*W*part) of every rank's bucket
+// buffer holds its fp32 gradient of one bucket; rank r owns slice r = [r*part, (r+1)*part) and gets
+// acc[0, part) += scale * sum_ranks(slice r).  When the kernel ends the whole region is zero on every
+// rank.  part a multiple of 4; `blocks` as for the range reduce-scatter.
+void comm_bucket_reduce(const CommCtx& c, size_t off_bytes, size_t part, float* acc, float scale, int blocks,
+                        cudaStream_t s);
+// One segment of an interleaved shard (all fields in units of 8 elements except param_off): shard
+// groups [shard8, shard8 + part8) are slice `rank` of a bucket whose parameters start at byte
+// param_off of the parameter buffer; the first valid8 groups of the slice lie inside the bucket.
+struct RingSeg {
+  long long shard8;
+  long long part8;
+  long long valid8;
+  long long param_off;
+};
+// AdamW over the whole interleaved shard (total elements, multiple of 8; master / m / v / grad in
+// shard order) and the bf16 results of the valid groups written into every rank's parameter buffer
+// at param_off + (rank * part8 + j) * 16.  `segs` is a device array of nseg entries sorted by shard8.
+void comm_adamw_allgather_seg(const CommCtx& c, const RingSeg* segs, int nseg, size_t total, float* master, float* m,
+                              float* v, const float* grad, const float* scale_ptr, float scale_const, float lr,
+                              float beta1, float beta2, float eps, float wd, int step, cudaStream_t s,
+                              const float* dev_sc = nullptr);
 // Embedding backward into the owners' shards: row r of dy (bf16 [rows, d], contiguous) is added at
 // table row ids[r] of the weight whose element (i, k) has flat index flat0 + i * d + k (ids outside
 // [0, vocab) are skipped).  d must be a multiple of 8, flat0 of 4.

@@ -210,27 +210,49 @@ class NvlinkCollectives(TorchCollectives):
 
     supports_bucket_reduce = True
 
-    def bucket_reduce_to_owners_(self, bucket: torch.Tensor, flat0: int, chunk: int, bases: List[int], scale: float,
-                                 balanced: bool = True, blocks: int = 0) -> bool:
-        """Add ``scale * sum_ranks(bucket)`` into the owners' fp32 gradient shards and clear ``bucket``.
+    def bucket_reduce_(self, bucket: torch.Tensor, acc: torch.Tensor, scale: float, blocks: int = 0) -> bool:
+        """Gradient ring: ``acc += scale * sum_ranks(slice rank of bucket)`` and ``bucket`` cleared.
 
-        ``bucket`` (fp32, inside one of this object's symmetric buffers) holds this rank's gradient of
-        flat elements ``[flat0, flat0 + bucket.numel())``; ``bases`` is every rank's shard address as
-        mapped on this GPU (``shard_bases``), ``chunk`` the shard length.  With ``balanced`` each rank
-        reduces 1/W of the bucket and sends each sum to its owner; otherwise each rank reduces the
-        part it owns.  When the kernel ends the bucket is zero on every rank.  A collective: every
-        rank calls it for the same buckets in the same order.  Returns False, doing nothing, when the
-        bucket does not qualify (not symmetric fp32, sizes not multiples of 4)."""
+        ``bucket`` (fp32, inside one of this object's symmetric buffers, ``W * part`` elements) holds
+        this rank's gradient of one bucket; rank r owns slice ``[r*part, (r+1)*part)`` and ``acc``
+        (``part`` elements, local fp32) is its gradient segment.  When the kernel ends the bucket is
+        zero on every rank.  A collective: every rank calls it for the same buckets in the same order.
+        Returns False, doing nothing, when the bucket does not qualify."""
         hit = self._locate(bucket)
+        world = self._w()
         n = bucket.numel()
-        if hit is None or bucket.dtype != torch.float32 or n % 4 or flat0 % 4 or chunk % 4:
+        if hit is None or bucket.dtype != torch.float32 or n % (4 * world) or acc.numel() != n // world:
             return False
         buf, off = hit
         if self._skipped("bucket_reduce"):
             return True
         slot = self._pace_begin()
-        buf.ctx.bucket_reduce(off, n, int(flat0), int(chunk), list(bases), float(scale), bool(balanced), int(blocks))
+        buf.ctx.bucket_reduce(off, n // world, acc, float(scale), int(blocks))
         self._pace_end(slot, "reduce_scatter", n * 4)
+        return True
+
+    def adamw_allgather_segments(self, params_flat: torch.Tensor, segs: torch.Tensor, master: torch.Tensor,
+                                 exp_avg: torch.Tensor, exp_avg_sq: torch.Tensor, grad: torch.Tensor, scale, cfg,
+                                 step: int, dev_scalars: Optional[torch.Tensor] = None) -> bool:
+        """AdamW on an interleaved ring shard + the bf16 all-gather of every segment into
+        ``params_flat`` (the symmetric parameter buffer; ``segs`` as for the native kernel, with byte
+        offsets relative to ``params_flat``).  False, doing nothing, when the buffers do not qualify."""
+        hit = self._locate(params_flat)
+        total = master.numel()
+        if hit is None or params_flat.dtype != torch.bfloat16 or total % 8 or grad.dtype != torch.float32:
+            return False
+        buf, off = hit
+        if off:
+            segs = segs.clone()
+            segs[:, 3] += off
+        scale_t = scale.reshape(1).float() if isinstance(scale, torch.Tensor) else None
+        scale_c = 1.0 if isinstance(scale, torch.Tensor) else float(scale if scale is not None else 1.0)
+        if self._skipped("adamw_allgather"):
+            return True
+        slot = self._pace_begin()
+        buf.ctx.adamw_allgather_seg(segs, total, master, exp_avg, exp_avg_sq, grad.contiguous(), scale_t, scale_c,
+                                    cfg.lr, cfg.betas[0], cfg.betas[1], cfg.eps, cfg.weight_decay, step, dev_scalars)
+        self._pace_end(slot, "allgather", total * 2 * self._w())
         return True
 
     def reduce_scatter_into(self, out: torch.Tensor, flat: torch.Tensor) -> torch.Tensor:

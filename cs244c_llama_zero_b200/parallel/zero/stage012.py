@@ -376,7 +376,7 @@ class ZeROStage2Optimizer(_ShardedStateMixin, _FlatEngine):
 
     def _block_ranges(self) -> List[Tuple[int, int, List[nn.Parameter]]]:
         """(lo, hi, params) of every transformer block's contiguous flat range, in flat order; hi is
-        rounded up to a multiple of 4 (parameters start 64-element aligned, so ranges stay disjoint)."""
+        rounded up to a multiple of 8 (parameters start 64-element aligned, so ranges stay disjoint)."""
         offset = {id(p): off for p, off in zip(self.meta.params, self.space.offsets)}
         out = []
         for module in self.model.modules():
@@ -387,68 +387,83 @@ class ZeROStage2Optimizer(_ShardedStateMixin, _FlatEngine):
                 continue
             lo = min(offset[id(p)] for p in ps)
             hi = max(offset[id(p)] + p.numel() for p in ps)
-            out.append((lo, (hi + 3) // 4 * 4, ps))
+            out.append((lo, (hi + 7) // 8 * 8, ps))
         out.sort(key=lambda r: r[0])
         for (_, hi0, _), (lo1, _, _) in zip(out, out[1:]):
             if lo1 < hi0:
                 return []
-        if any(lo % 4 for lo, _, _ in out):
+        if any(lo % 8 for lo, _, _ in out):
             return []
         return out
 
     def _setup_ring(self) -> bool:
-        """Gradient memory without a full fp32 buffer, and the reduce-scatter spread over backward.
+        """Gradient memory without a full fp32 buffer, with the reduce-scatter spread over backward.
 
-        Each transformer block's weight gradients accumulate into one of ``ZB_STAGE2_RING_SLOTS``
-        (default 2) symmetric bucket buffers (block j uses slot j mod slots); the parameters outside
-        the blocks (embedding, final norm, LM head) into their own symmetric buffers.  As soon as a
-        block's backward has issued its weight gradients (the block kernels' grad-ready hook), one
-        kernel on the same stream reduces that bucket over NVLink straight into the owners' fp32
-        shards, averaged, and clears it (``bucket_reduce_to_owners_``); the slot is free for block
-        j - slots, which the stream runs afterwards.  The other buffers are reduced when backward
-        ends.  Gradient memory: the shard (4 B/param / W) plus the slots and the edge buffers,
-        instead of 4 B/param.  ``ZB_STAGE2_RING_SPLIT=owner`` makes each rank reduce the part of a
-        bucket it owns instead of 1/W of every bucket."""
+        Buckets: every transformer block's flat range, and the ranges between them (embedding, final
+        norm, LM head: the edge buckets).  Each bucket of n elements is cut into W slices of ``part``
+        elements (n rounded up to 8W); rank r owns slice r of EVERY bucket, so its shard - gradient,
+        fp32 master, Adam moments - is the concatenation of its slices (the interleaved layout), and a
+        bucket's reduce-scatter is balanced and writes nothing remote.  Each block's weight gradients
+        accumulate into one of ``ZB_STAGE2_RING_SLOTS`` (default 2) symmetric bucket buffers (block j
+        uses slot j mod slots), the edge buckets into their own.  As soon as a block's backward has
+        issued its weight gradients (the block kernels' grad-ready hook), one kernel on the same
+        stream reduces this rank's slice of the bucket into its gradient segment, averaged, and
+        clears the bucket; the slot is free for block j - slots, which the stream runs afterwards.
+        The edge buckets are reduced when backward ends.  The update is one kernel: AdamW over the
+        shard and the bf16 all-gather of every slice.  Gradient memory: the shard (4 B/param / W)
+        plus the slots and edge buffers, instead of 4 B/param."""
         ranges = self._block_ranges()
-        coll = self.collectives
         if not ranges:
             return False
-        self.grad_shard = coll.alloc(self.space.chunk, torch.float32)
-        bases = coll.shard_bases(self.grad_shard)
-        if bases is None:
-            return False
-        used = (self.space.numel + 3) // 4 * 4
-        edges, cursor = [], 0
-        for lo, hi, _ in ranges:
+        W, r = self.world_size, self.rank
+        used = (self.space.numel + 7) // 8 * 8
+        buckets, cursor = [], 0  # (lo, hi, block index or -1)
+        for j, (lo, hi, _) in enumerate(ranges):
             if lo > cursor:
-                edges.append((cursor, lo))
+                buckets.append((cursor, lo, -1))
+            buckets.append((lo, hi, j))
             cursor = hi
         if cursor < used:
-            edges.append((cursor, used))
+            buckets.append((cursor, used, -1))
+        coll = self.collectives
         n_slots = max(1, int(os.environ.get("ZB_STAGE2_RING_SLOTS", "2")))
-        slot_numel = max(hi - lo for lo, hi, _ in ranges)
-        self._ring_bases = bases
-        self._ring_ranges = [(lo, hi) for lo, hi, _ in ranges]
+        seg_rows, shard_off = [], 0
+        self._ring_buckets = []  # (lo, hi, part, shard offset, block index or -1)
+        for lo, hi, j in buckets:
+            part = -(-(hi - lo) // (8 * W)) * 8
+            valid = max(0, min(part, (hi - lo) - r * part))
+            seg_rows.append((shard_off // 8, part // 8, valid // 8, lo * self.space.params.element_size()))
+            self._ring_buckets.append((lo, hi, part, shard_off, j))
+            shard_off += part
+        total = shard_off
+        slot_numel = max(W * part for lo, hi, part, off, j in self._ring_buckets if j >= 0)
         self._ring_slots = [coll.alloc(slot_numel, torch.float32) for _ in range(n_slots)]
-        self._ring_edges = [(lo, hi, coll.alloc(hi - lo, torch.float32)) for lo, hi in edges]
-        self._ring_balanced = os.environ.get("ZB_STAGE2_RING_SPLIT", "balanced") != "owner"
+        self._ring_edge_bufs = {i: coll.alloc(W * part, torch.float32)
+                                for i, (lo, hi, part, off, j) in enumerate(self._ring_buckets) if j < 0}
+        self._ring_segs = torch.tensor(seg_rows, dtype=torch.int64, device=self.device)
+        self._ring_seg_rows = seg_rows
+        self._ring_block_bucket = {j: i for i, (_, _, _, _, j) in enumerate(self._ring_buckets) if j >= 0}
         self._ring_block_of = {}
         for j, (_, _, ps) in enumerate(ranges):
             for p in ps:
                 self._ring_block_of[id(p)] = j
-        self._ring_params: List[List[Tuple[nn.Parameter, int]]] = [[] for _ in ranges]
-        self._ring_edge_params: List[List[Tuple[nn.Parameter, int]]] = [[] for _ in edges]
+        self._ring_params: List[List[nn.Parameter]] = [[] for _ in self._ring_buckets]
         for p, off in zip(self.meta.params, self.space.offsets):
-            j = self._ring_block_of.get(id(p))
-            if j is not None:
-                lo = self._ring_ranges[j][0]
-                buf = self._ring_slots[j % n_slots]
-                self._ring_params[j].append((p, off))
-            else:
-                e = next(i for i, (lo_e, hi_e, _) in enumerate(self._ring_edges) if lo_e <= off < hi_e)
-                lo, _, buf = self._ring_edges[e]
-                self._ring_edge_params[e].append((p, off))
+            i = next(i for i, (lo, hi, _, _, _) in enumerate(self._ring_buckets) if lo <= off < hi)
+            lo, _, _, _, j = self._ring_buckets[i]
+            buf = self._ring_slots[j % n_slots] if j >= 0 else self._ring_edge_bufs[i]
             p.main_grad = buf[off - lo : off - lo + p.numel()].view(p.shape)
+            self._ring_params[i].append(p)
+        # the shard in interleaved order: gradient, fp32 master and Adam moments
+        self.grad_shard = torch.zeros(total, dtype=torch.float32, device=self.device)
+        master = torch.zeros(total, dtype=torch.float32, device=self.device)
+        for (lo, hi, part, off, _), row in zip(self._ring_buckets, seg_rows):
+            valid = row[2] * 8
+            if valid:
+                master[off : off + valid].copy_(self.space.params[lo + r * part : lo + r * part + valid])
+        self._master = master
+        self._exp_avg = torch.zeros_like(master)
+        self._exp_avg_sq = torch.zeros_like(master)
         from ...ops import functional as F
 
         self._ring = True
@@ -460,48 +475,68 @@ class ZeROStage2Optimizer(_ShardedStateMixin, _FlatEngine):
         self._fused_sq = None
         return True
 
-    def _ring_reduce(self, bucket: torch.Tensor, flat0: int) -> None:
-        with self.clock.measure("backward_reduce_scatter", bucket.numel() * 4):
+    def _ring_reduce(self, i: int) -> None:
+        lo, hi, part, off, j = self._ring_buckets[i]
+        W = self.world_size
+        bucket = (self._ring_slots[j % len(self._ring_slots)] if j >= 0 else self._ring_edge_bufs[i])[: W * part]
+        with self.clock.measure("backward_reduce_scatter", W * part * 4):
             with self.collectives.label_scope("stage2.backward.reduce_scatter.bucket"):
-                ok = self.collectives.bucket_reduce_to_owners_(bucket, flat0, self.space.chunk, self._ring_bases,
-                                                               1.0 / self.world_size, self._ring_balanced)
+                ok = self.collectives.bucket_reduce_(bucket, self.grad_shard[off : off + part], 1.0 / W)
         if not ok:
             raise RuntimeError("gradient ring: bucket reduce unavailable")
-
-    def _ring_reduce_block(self, j: int) -> None:
-        lo, hi = self._ring_ranges[j]
-        self._ring_reduce(self._ring_slots[j % len(self._ring_slots)][: hi - lo], lo)
 
     def _on_ring_block_ready(self, params) -> None:
         """Every backward of a block writes its slot once and reduces it once, whoever runs it."""
         j = self._ring_block_of.get(id(params[0])) if params else None
         if j is not None:
-            self._ring_reduce_block(j)
-
-    @staticmethod
-    def _fold(pairs) -> None:
-        for p, _ in pairs:
-            if p.grad is not None:
-                p.main_grad.add_(p.grad.detach().to(torch.float32))
-                p.grad = None
+            self._ring_reduce(self._ring_block_bucket[j])
 
     def _ring_flush(self) -> None:
         """After backward: blocks whose gradients autograd left in ``param.grad`` (modules that do not
-        run as one block kernel, so no hook fired), then the edge buffers."""
+        run as one block kernel, so no hook fired), then the edge buckets."""
         self._record_memory_event("measured_step_stage2_pre_reduce_scatter")
-        for j in reversed(range(len(self._ring_ranges))):
-            if any(p.grad is not None for p, _ in self._ring_params[j]):
-                self._fold(self._ring_params[j])
-                self._ring_reduce_block(j)
-        for (lo, _, buf), pairs in zip(self._ring_edges, self._ring_edge_params):
-            self._fold(pairs)
-            self._ring_reduce(buf, lo)
+        for i in reversed(range(len(self._ring_buckets))):
+            j = self._ring_buckets[i][4]
+            pending = [p for p in self._ring_params[i] if p.grad is not None]
+            for p in pending:
+                p.main_grad.add_(p.grad.detach().to(torch.float32))
+                p.grad = None
+            if j < 0 or pending:
+                self._ring_reduce(i)
         self._record_memory_event("measured_step_stage2_post_reduce_scatter")
+
+    def _ring_update(self, scale: torch.Tensor) -> None:
+        """AdamW on the interleaved shard and the bf16 all-gather of every slice (one kernel with the
+        NVLink collectives; otherwise AdamW on the master and per-bucket all-gathers)."""
+        dev_scalars = self._device_scalars()
+        fused = getattr(self.collectives, "adamw_allgather_segments", None)
+        if fused is not None and self.device.type == "cuda":
+            with self.clock.measure("post_allgather", self._master.numel() * 2):
+                if fused(self.space.params, self._ring_segs, self._master, self._exp_avg, self._exp_avg_sq,
+                         self.grad_shard, scale, self.adam, self.step_count, dev_scalars):
+                    return
+        with self.clock.measure("optimizer"):
+            adamw_update_(self._master, self._exp_avg, self._exp_avg_sq, self.grad_shard, self.adam, self.step_count,
+                          grad_scale=scale, param_out=None, dev_scalars=dev_scalars)
+        self._ring_write_params()
+
+    def _ring_write_params(self) -> None:
+        """Every rank's parameters from every rank's master slices (per bucket: an all-gather of the
+        model-dtype slices, then the valid part copied into the flat parameter buffer)."""
+        import torch.distributed as dist
+
+        W = self.world_size
+        with self.clock.measure("post_allgather", self._master.numel() * 2):
+            for lo, hi, part, off, _ in self._ring_buckets:
+                mine = self._master[off : off + part].to(self.space.params.dtype)
+                parts = [torch.empty_like(mine) for _ in range(W)]
+                dist.all_gather(parts, mine)
+                self.space.params[lo:hi].copy_(torch.cat(parts)[: hi - lo])
 
     def _ring_bytes(self) -> int:
         if not self._ring:
             return 0
-        return tensors_num_bytes(list(self._ring_slots) + [b for _, _, b in self._ring_edges])
+        return tensors_num_bytes(list(self._ring_slots) + list(self._ring_edge_bufs.values()))
 
     def _routed_requested(self) -> bool:
         return bool(os.environ.get("ZB_ROUTED_GRADS", "0") == "1" and self.world_size > 1
@@ -719,9 +754,8 @@ class ZeROStage2Optimizer(_ShardedStateMixin, _FlatEngine):
     def _update(self, max_grad_norm: float) -> torch.Tensor:
         if self._routed:
             return self._routed_update(max_grad_norm)
-        if self._ring and self._pending_flush:  # backward ran outside engine.backward()
-            self._ring_flush()
-            self._pending_flush = False
+        if self._ring:
+            return self._ring_step(max_grad_norm)
         if any(p.grad is not None for p in self.meta.params) and not hasattr(self.meta.params[0], "main_grad"):
             raise RuntimeError("Stage 2 expects gradients in the flat buffer")
         if self._fused_step and max_grad_norm <= 0 and self._pending_flush:
@@ -743,6 +777,20 @@ class ZeROStage2Optimizer(_ShardedStateMixin, _FlatEngine):
         self._record_memory_event("measured_step_stage2_post_step_free_grad_shard")
         return norm
 
+    def _ring_step(self, max_grad_norm: float) -> torch.Tensor:
+        if self._pending_flush:  # backward ran outside engine.backward()
+            self._ring_flush()
+            self._pending_flush = False
+        norm = global_norm_from_local_sq(sum_of_squares(self.grad_shard), sharded=True,
+                                         collectives=self.collectives)
+        self.step_count += 1
+        self._record_memory_event("measured_step_stage2_pre_allgather")
+        with self.collectives.label_scope("stage2.step.allgather.updated_param_shard"):
+            self._ring_update(clip_coefficient(norm, max_grad_norm))
+        self._record_memory_event("measured_step_stage2_post_allgather")
+        self._record_memory_event("measured_step_stage2_post_step_free_grad_shard")
+        return norm
+
     def step_async(self, max_grad_norm: float = 0.0) -> torch.Tensor:
         return self._update(max_grad_norm)
 
@@ -751,6 +799,30 @@ class ZeROStage2Optimizer(_ShardedStateMixin, _FlatEngine):
         norm = self._update(max_grad_norm)
         return self._stats(norm, t0, {"backward_reduce_scatter": "backward_reduce_scatter",
                                       "post_allgather": "post_allgather"})
+
+    def state_dict(self) -> Dict[str, object]:
+        state = super().state_dict()
+        if self._ring:  # the shard holds slice `rank` of every bucket, in bucket order
+            state["layout"] = "ring_interleaved_v1"
+            state["ring_segments"] = [(lo, hi, part, off) for lo, hi, part, off, _ in self._ring_buckets]
+            state.pop("shard_start", None)
+            state.pop("shard_end", None)
+        return state
+
+    def load_state_dict(self, state: Dict[str, object]) -> None:
+        if not self._ring:
+            super().load_state_dict(state)
+            return
+        if state.get("layout") != "ring_interleaved_v1" or [tuple(x) for x in state["ring_segments"]] != [
+                (lo, hi, part, off) for lo, hi, part, off, _ in self._ring_buckets]:
+            raise ValueError("checkpoint shard layout differs from this engine's gradient-ring layout")
+        self.step_count = int(state["step_count"])
+        self._master.copy_(state["local_master_param_shard"].to(self.device, torch.float32))
+        self._exp_avg.copy_(state["exp_avg"].to(self.device, torch.float32))
+        self._exp_avg_sq.copy_(state["exp_avg_sq"].to(self.device, torch.float32))
+        if "grad_shard" in state:
+            self.grad_shard.copy_(state["grad_shard"].to(self.device, torch.float32))
+        self._ring_write_params()
 
     def _logical_grad_bytes(self) -> int:
         return self.space.chunk * self.space.params.element_size()

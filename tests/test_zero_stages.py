@@ -464,33 +464,25 @@ def test_routed_stage2_matches_reference(max_grad_norm: float, grad_accum: int) 
 
 class _RingCollectives(TorchCollectives):
     """Gloo stand-in for the stage-2 gradient ring: a bucket reduce all-reduces the bucket, adds this
-    rank's share of the averaged sum into its shard and clears the bucket (what the NVLink bucket
-    kernel produces on GPUs)."""
+    rank's slice of the averaged sum into its gradient segment and clears the bucket (what the NVLink
+    bucket kernel produces on GPUs)."""
 
     supports_bucket_reduce = True
 
     def __init__(self):
-        self.shard = None
         self.reduces = []
 
     def alloc(self, numel, dtype):
-        t = torch.zeros(numel, dtype=dtype)
-        if self.shard is None:  # the engine allocates its gradient shard first
-            self.shard = t
-        return t
+        return torch.zeros(numel, dtype=dtype)
 
-    def shard_bases(self, t):
-        return [2000 + r for r in range(dist.get_world_size())]
-
-    def bucket_reduce_to_owners_(self, bucket, flat0, chunk, bases, scale, balanced=True, blocks=0):
+    def bucket_reduce_(self, bucket, acc, scale, blocks=0):
         total = bucket.clone()
         dist.all_reduce(total)
+        part = acc.numel()
         r = dist.get_rank()
-        lo, hi = max(flat0, r * chunk), min(flat0 + bucket.numel(), (r + 1) * chunk)
-        if hi > lo:
-            self.shard[lo - r * chunk:hi - r * chunk] += scale * total[lo - flat0:hi - flat0]
+        acc += scale * total[r * part:(r + 1) * part]
         bucket.zero_()
-        self.reduces.append((flat0, bucket.numel()))
+        self.reduces.append(bucket.numel())
         return True
 
 
@@ -508,8 +500,9 @@ def _ring_worker(rank: int, world: int, port: int, max_grad_norm: float, grad_ac
         coll = _RingCollectives()
         ZeROStage2Optimizer._ring_requested = lambda self: True  # what NVLink collectives enable on GPUs
         engine = ZeROStage2Optimizer(model=model, collectives=coll, **hp)
-        assert engine._ring and engine.space.grads is None and engine.grad_shard is coll.shard
-        assert len(engine._ring_ranges) == cfg.n_layers and len(engine._ring_slots) == 2
+        assert engine._ring and engine.space.grads is None and len(engine._ring_slots) == 2
+        blocks = [b for b in engine._ring_buckets if b[4] >= 0]
+        assert len(blocks) == cfg.n_layers
         opt = torch.optim.AdamW(ref.parameters(), **hp)
         for step in range(3):
             micro = [_local_batch(step * 10 + m, rank, 3, cfg.max_seq_len, cfg.vocab_size) for m in range(grad_accum)]
@@ -530,19 +523,27 @@ def _ring_worker(rank: int, world: int, port: int, max_grad_norm: float, grad_ac
             opt.step()
             _assert_close(model, ref, f"ring step={step} rank={rank}")
             torch.testing.assert_close(torch.tensor(norm), want, rtol=1e-4, atol=1e-6)
-        # every block bucket and every edge bucket reduced once per backward, and nothing else
-        per_backward = len(engine._ring_ranges) + len(engine._ring_edges)
-        assert len(coll.reduces) == 3 * grad_accum * per_backward
-        covered = sorted(set(coll.reduces))
+        # every bucket reduced once per backward; the buckets tile the flat space and the shard holds
+        # one W-th of each
+        assert len(coll.reduces) == 3 * grad_accum * len(engine._ring_buckets)
         cursor = 0
-        for flat0, n in covered:
-            assert flat0 == cursor, (flat0, cursor)
-            cursor = flat0 + n
+        for lo, hi, part, off, _ in engine._ring_buckets:
+            assert lo == cursor and world * part >= hi - lo
+            cursor = hi
         assert cursor >= engine.space.numel
+        assert engine.grad_shard.numel() == sum(b[2] for b in engine._ring_buckets)
         live = engine.live_model_state_breakdown_mb()
         # the shard plus the ring's slots and edge buffers (no full gradient buffer)
-        assert live["grads_mb"] == pytest.approx((engine.space.chunk * 4 + engine._ring_bytes()) / 2 ** 20)
-        assert all(t.numel() == max(hi - lo for lo, hi in engine._ring_ranges) for t in engine._ring_slots)
+        assert live["grads_mb"] == pytest.approx((engine.grad_shard.numel() * 4 + engine._ring_bytes()) / 2 ** 20)
+        # checkpoint round trip: a fresh engine restored from the state continues identically
+        state = engine.state_dict()
+        assert state["layout"] == "ring_interleaved_v1"
+        torch.manual_seed(99)
+        model2 = LlamaForCausalLM(cfg)
+        engine2 = ZeROStage2Optimizer(model=model2, collectives=_RingCollectives(), **hp)
+        engine2.load_state_dict(state)
+        for (n, a), (_, b) in zip(model.named_parameters(), model2.named_parameters()):
+            assert torch.equal(a, b), n
     finally:
         dist.barrier()
         dist.destroy_process_group()
