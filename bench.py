@@ -356,6 +356,8 @@ def _measure_stages(args, size: str, batch: int, seq: int, world: int, rank: int
         stage_launches = (ops.launch_count() - launches_before) // args.steps
         entry = {"tokens_per_s": tokens_per_step / (ms / 1000.0), "ms_per_step": ms,
                  "gpu_launches_per_step": stage_launches}
+        if stage == 2:
+            entry["gradient_mode"] = getattr(sess.engine, "gradient_mode", "full")
         entry.update(roofline_entry(sess, batch, seq, stage, ms, peak_tflops))
         # comm time of one extra instrumented step (device events around each collective); the
         # barrier keeps host-side skew between ranks out of the measured intervals
@@ -449,9 +451,6 @@ def run_mine(args) -> None:
                    "cuda_graph": bool(args.cuda_graph and args.headline_stage != 3),
                    "fused_step": bool(args.fused_step),
                    "routed_grads": bool(args.routed_grads),
-                   "stage2_grads": ("routed" if args.routed_grads else "full" if (
-                       args.fused_step or world == 1 or impl not in ("nvls", "p2p")
-                       or os.environ.get("ZB_STAGE2_GRADS", "ring") != "ring") else "ring"),
                    "l2": "no flush: each step touches >2 GB (activations, 1.2 GB fp32 optimizer state) vs 126 MB L2"},
         "per_stage": head["per_stage"],
         "per_config": per_config,

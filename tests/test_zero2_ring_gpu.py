@@ -119,6 +119,7 @@ def _engine_worker(rank: int, world: int, port: int, slots: str) -> None:
         from cs244c_llama_zero_b200.parallel.zero import ZeROStage2Optimizer
 
         os.environ["ZB_STAGE2_RING_SLOTS"] = slots
+        os.environ["ZB_STAGE2_GRADS"] = "ring"  # "auto" keeps the full buffer for a model this small
         cfg = ModelConfig(name="t", vocab_size=1024, max_seq_len=256, dim=256, n_layers=3, n_heads=4, n_kv_heads=2,
                           ffn_dim=512)
         dev = torch.device("cuda", rank)

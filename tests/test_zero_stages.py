@@ -552,3 +552,32 @@ def _ring_worker(rank: int, world: int, port: int, max_grad_norm: float, grad_ac
 @pytest.mark.parametrize("max_grad_norm,grad_accum", [(0.0, 1), (0.5, 2)])
 def test_ring_stage2_matches_reference(max_grad_norm: float, grad_accum: int) -> None:
     _spawn(_ring_worker, 2, max_grad_norm, grad_accum)
+
+
+def test_stage2_gradient_mode_auto_policy(monkeypatch) -> None:
+    """``ZB_STAGE2_GRADS=auto`` picks the gradient ring only when the full fp32 gradient buffer would
+    reach the size threshold; ``ring`` / ``full`` force it; collectives without the bucket kernel
+    and single-GPU runs never get it."""
+    from types import SimpleNamespace
+
+    from cs244c_llama_zero_b200.parallel.zero.common import build_flat_param_metadata
+
+    model = LlamaForCausalLM(_cfg())
+    stub = SimpleNamespace(world_size=2, device=torch.device("cuda", 0), meta=build_flat_param_metadata(model),
+                           collectives=SimpleNamespace(supports_bucket_reduce=True),
+                           RING_AUTO_MIN_BYTES=ZeROStage2Optimizer.RING_AUTO_MIN_BYTES)
+    want = ZeROStage2Optimizer._ring_requested
+    monkeypatch.delenv("ZB_STAGE2_GRADS", raising=False)
+    assert not want(stub)  # a small model keeps the full buffer
+    stub.RING_AUTO_MIN_BYTES = 1
+    assert want(stub)
+    monkeypatch.setenv("ZB_STAGE2_GRADS", "full")
+    assert not want(stub)
+    monkeypatch.setenv("ZB_STAGE2_GRADS", "ring")
+    stub.RING_AUTO_MIN_BYTES = 1 << 60
+    assert want(stub)
+    stub.collectives = SimpleNamespace()
+    assert not want(stub)
+    stub.collectives = SimpleNamespace(supports_bucket_reduce=True)
+    stub.world_size = 1
+    assert not want(stub)
