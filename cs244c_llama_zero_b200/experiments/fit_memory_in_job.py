@@ -11,7 +11,8 @@ waiting inside a collective.  This runner keeps one process group per GPU count 
 2. runs two training steps at each probe batch size (``--probe-batches``, default 1 and 2), with the
    allocator's cache emptied first, and reads the allocated peak (max over ranks),
 3. fits ``peak(b) = slope * b + base`` (the reference's ``memory_model`` predictor kind) and takes
-   ``b_max = floor((capacity_fraction * total_memory - base) / slope)``, min over ranks,
+   ``b_max = floor((capacity_fraction * total_memory - base - outside) / slope)``, min over ranks,
+   where ``outside`` is the memory held outside PyTorch's allocator (the symmetric NVLink buffers),
 4. times ``--steps`` steps at ``b_max`` (device events, max over ranks) and records tokens/s and the
    measured peak.
 
@@ -109,15 +110,21 @@ def measure_stage(args, stage: int, rank: int, world: int, impl: str) -> Dict[st
         torch.cuda.synchronize(dev)
         points.append((b, _max_over_ranks(torch.cuda.max_memory_allocated(dev) / 2**20)))
         del ids
+    # Memory outside PyTorch's caching allocator (symmetric NVLink buffers of the parameters and
+    # gradients, NCCL, the CUDA context) does not show in the allocator's statistics but fills the
+    # same HBM: measured after the probes (lazy allocations included) and subtracted from the budget.
+    torch.cuda.synchronize(dev)
+    free_b, total_b = torch.cuda.mem_get_info(dev)
+    other_mb = _max_over_ranks((total_b - free_b - torch.cuda.memory_reserved(dev)) / 2**20)
     slope, base = fit_line(points)
-    b_max = predict_max_batch(slope, base, total_mb, args.capacity_fraction, args.max_batch)
+    b_max = predict_max_batch(slope, base + other_mb, total_mb, args.capacity_fraction, args.max_batch)
     if dist.is_initialized() and world > 1:  # every rank runs the same batch
         t = torch.tensor([b_max], dtype=torch.int64, device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MIN)
         b_max = int(t.item())
     rec: Dict[str, object] = {"stage": stage, "world_size": world, "build_s": build_s,
                               "probe_peak_allocated_mb": points, "slope_mb_per_sample": slope,
-                              "base_mb": base, "gpu_total_mb": total_mb,
+                              "base_mb": base, "outside_allocator_mb": other_mb, "gpu_total_mb": total_mb,
                               "capacity_fraction": args.capacity_fraction, "selected_batch_size": b_max}
     if b_max >= 1:
         ids = _batch(b_max, args.seq_len, BASELINE_VOCAB_SIZE, 11 + rank).to(dev)

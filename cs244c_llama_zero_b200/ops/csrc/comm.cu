@@ -40,7 +40,7 @@ namespace b200 {
 namespace {
 
 constexpr int kThreads = 512;
-constexpr int kUnroll = 4;  // independent 16-byte vectors in flight per thread
+constexpr int kUnroll = 8;  // independent 16-byte vectors in flight per thread
 
 __device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
   asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
