@@ -630,6 +630,18 @@ class CommContext {
                                    (float)beta1, (float)beta2, (float)eps, (float)wd, (int)step, cur_stream(),
                                    dev_scalars_ptr(dev_scalars));
   }
+  // Push reduce-scatter with this buffer as the landing area (see comm.h).
+  void push_reduce_scatter_f32(Tensor src, int64_t src_stride, int64_t land_off, int64_t part, Tensor acc,
+                               double scale, bool clear_src) {
+    check_f32(src, "src");
+    TORCH_CHECK(src.is_contiguous() && src_stride >= part && src.numel() >= src_stride * (c_.world - 1) + part,
+                "push_reduce_scatter: src too small for W slices");
+    check_acc(acc, part);
+    c10::cuda::CUDAGuard g(device_);
+    prepare();
+    b200::comm_push_reduce_scatter_f32(c_, src.data_ptr<float>(), src_stride, land_off, part, acc.data_ptr<float>(),
+                                       (float)scale, clear_src, cur_stream());
+  }
   void reduce_scatter_acc_bf16(int64_t off, int64_t chunk, Tensor acc, double scale) {
     check_acc(acc, chunk);
     c10::cuda::CUDAGuard g(device_);
@@ -1012,6 +1024,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
       .def("reduce_scatter_acc_f32", &CommContext::reduce_scatter_acc_f32)
       .def("reduce_scatter_acc_bf16", &CommContext::reduce_scatter_acc_bf16)
       .def("reduce_scatter_range_acc_f32", &CommContext::reduce_scatter_range_acc_f32)
+      .def("push_reduce_scatter_f32", &CommContext::push_reduce_scatter_f32, py::arg("src"), py::arg("src_stride"),
+           py::arg("land_off"), py::arg("part"), py::arg("acc"), py::arg("scale"), py::arg("clear_src") = false)
       .def("bucket_reduce", &CommContext::bucket_reduce, py::arg("off"), py::arg("part"), py::arg("acc"),
            py::arg("scale"), py::arg("blocks") = 0)
       .def("adamw_allgather_seg", &CommContext::adamw_allgather_seg, py::arg("segs"), py::arg("total"),

@@ -21,6 +21,8 @@
 //                        reuse (ZeRO-2 gradient ring, interleaved shards)
 //   adamw_allgather_seg  AdamW on the interleaved shard and the bf16 result multicast into every
 //                        rank's parameter buffer, segment by segment
+//   push_rs              reduce-scatter by peer stores into a landing area + a local sum (each byte
+//                        crosses NVLink once; the better choice at 2 and 4 ranks)
 //
 // Ordering: every block of every rank runs the same grid, and block b synchronises with block b of
 // every peer at kernel start (all inputs written) and at kernel end (all outputs delivered).  The
@@ -638,6 +640,60 @@ __global__ void __launch_bounds__(kThreads) adamw_allgather_seg_kernel(CommCtx c
   block_barrier(c, 2 * e + 1);
 }
 
+// Push reduce-scatter (fp32): the data moves as posted peer stores instead of switch reductions or
+// peer loads.  src (this rank's local data: W slices of part4 vectors, slice q starting at vector
+// q * sstride4, so a call can cover one piece of every slice of a larger buffer) need not be
+// symmetric; the
+// context's buffer holds the landing area at land_off: W rows of part4 vectors, row q written by
+// rank q.  Phase 1 stores slice q of src into rank q's row `rank`; after the middle barrier (block b
+// of every rank has stored its vectors, which are the same j positions block b reads below) each
+// rank adds its own slice and the W - 1 landed rows into acc.  A store crosses NVLink once, where a
+// multicast reduction at two ranks reads every byte of both GPUs through the switch.  With clear_src
+// the block zeroes the src vectors it has finished with (src is read by this rank only).
+template <bool CLEAR>
+__global__ void __launch_bounds__(kThreads) push_rs_f32_kernel(CommCtx c, float4* __restrict__ src, size_t sstride4,
+                                                                size_t land_off, size_t part4, float4* acc,
+                                                                float scale) {
+  const uint32_t e = next_epoch(c);
+  if (!block_barrier(c, 2 * e)) return;  // every rank's landing area is free again
+  const size_t stride = gstride();
+  for (int qi = 1; qi < c.world; ++qi) {
+    const int q = (c.rank + qi) % c.world;  // each rank starts with a different destination
+    float4* dst = reinterpret_cast<float4*>(c.peers[q] + land_off) + (size_t)c.rank * part4;
+    const float4* s = src + (size_t)q * sstride4;
+    for (size_t j0 = gtid(); j0 < part4; j0 += stride * kUnroll) {
+      float4 v[kUnroll];
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u) {
+        const size_t j = j0 + u * stride;
+        if (j < part4) v[u] = s[j];
+      }
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u) {
+        const size_t j = j0 + u * stride;
+        if (j < part4) __stcg(dst + j, v[u]);
+      }
+    }
+  }
+  if (!block_barrier(c, 2 * e + 1)) return;
+  const float4* land = reinterpret_cast<const float4*>(c.peers[c.rank] + land_off);
+  float4* own = src + (size_t)c.rank * sstride4;
+  for (size_t j = gtid(); j < part4; j += stride) {
+    float4 t = own[j];
+    for (int q = 0; q < c.world; ++q) {
+      if (q == c.rank) continue;
+      const float4 x = __ldcg(land + (size_t)q * part4 + j);  // written over NVLink: skip L1
+      t.x += x.x; t.y += x.y; t.z += x.z; t.w += x.w;
+    }
+    float4 a = acc[j];
+    a.x += scale * t.x; a.y += scale * t.y; a.z += scale * t.z; a.w += scale * t.w;
+    acc[j] = a;
+    if constexpr (CLEAR) {
+      for (int q = 0; q < c.world; ++q) src[(size_t)q * sstride4 + j] = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+  }
+}
+
 __global__ void barrier_kernel(CommCtx c) {
   const uint32_t e = next_epoch(c);
   block_barrier(c, 2 * e);
@@ -930,6 +986,22 @@ void comm_adamw_allgather_seg(const CommCtx& c, const RingSeg* segs, int nseg, s
   else
     adamw_allgather_seg_kernel<false><<<c.blocks, kThreads, 0, s>>>(c, segs, nseg, total / 8, M, Mm, Vv, G,
                                                                      scale_ptr, a, dev_sc);
+  B200_CUDA_CHECK(cudaGetLastError());
+  count_launch();
+}
+
+void comm_push_reduce_scatter_f32(const CommCtx& c, float* src, size_t src_stride, size_t land_off, size_t part,
+                                  float* acc, float scale, bool clear_src, cudaStream_t s) {
+  check_ctx(c);
+  B200_CHECK(part % 4 == 0 && src_stride % 4 == 0 && src_stride >= part && land_off % 16 == 0 &&
+                 ((reinterpret_cast<uintptr_t>(src) | reinterpret_cast<uintptr_t>(acc)) & 15) == 0,
+             "push_reduce_scatter: slice a multiple of 4 elements, landing offset, src and acc 16-aligned");
+  auto* s4 = reinterpret_cast<float4*>(src);
+  auto* a4 = reinterpret_cast<float4*>(acc);
+  if (clear_src)
+    push_rs_f32_kernel<true><<<c.blocks, kThreads, 0, s>>>(c, s4, src_stride / 4, land_off, part / 4, a4, scale);
+  else
+    push_rs_f32_kernel<false><<<c.blocks, kThreads, 0, s>>>(c, s4, src_stride / 4, land_off, part / 4, a4, scale);
   B200_CUDA_CHECK(cudaGetLastError());
   count_launch();
 }

@@ -94,6 +94,12 @@ void comm_adamw_allgather_seg(const CommCtx& c, const RingSeg* segs, int nseg, s
                               float* v, const float* grad, const float* scale_ptr, float scale_const, float lr,
                               float beta1, float beta2, float eps, float wd, int step, cudaStream_t s,
                               const float* dev_sc = nullptr);
+// Push reduce-scatter: src (local fp32, not necessarily symmetric) holds W slices of `part` elements,
+// slice q at src + q * src_stride; this context's buffer holds a landing area of W x part fp32 at
+// land_off.  acc[0, part) += scale * (src slice rank + the other ranks' slice `rank`).  With
+// clear_src the W slices of src are zero afterwards.
+void comm_push_reduce_scatter_f32(const CommCtx& c, float* src, size_t src_stride, size_t land_off, size_t part,
+                                  float* acc, float scale, bool clear_src, cudaStream_t s);
 // Embedding backward into the owners' shards: row r of dy (bf16 [rows, d], contiguous) is added at
 // table row ids[r] of the weight whose element (i, k) has flat index flat0 + i * d + k (ids outside
 // [0, vocab) are skipped).  d must be a multiple of 8, flat0 of 4.

@@ -4,8 +4,10 @@
   into its gradient segment, the bucket cleared afterwards, accumulation over two calls;
 * ``adamw_allgather_segments``: AdamW on an interleaved shard against the formula, and the bf16
   all-gather writing exactly the valid part of every slice; multicast and peer loads for both;
+* the push reduce-scatter (peer stores into a landing area, several pieces per call) against NCCL,
+  and the push variant of the bucket reduce;
 * the stage-2 engine in ring mode (no full gradient buffer) against the NCCL engine with its full
-  buffer, with clipping and two micro-batches per step.
+  buffer, with clipping and two micro-batches per step, with switch and push reductions.
 
 Both run as two processes on two GPUs.
 """
@@ -110,7 +112,54 @@ def test_bucket_reduce_and_segmented_adamw():
     mp.spawn(_bucket_worker, args=(2, find_free_port()), nprocs=2, join=True)
 
 
-def _engine_worker(rank: int, world: int, port: int, slots: str) -> None:
+def _push_worker(rank: int, world: int, port: int) -> None:
+    _init(rank, world, port)
+    try:
+        from cs244c_llama_zero_b200 import ops
+        from cs244c_llama_zero_b200.parallel.comm.nvlink import NvlinkCollectives
+
+        ops.load_extension().reset_device_errors()
+        os.environ["ZB_RS_MODE"] = "push"
+        dev = torch.device("cuda", rank)
+        for multicast in (True, False):
+            coll = NvlinkCollectives(device=dev, use_multicast=multicast)
+            assert coll.rs_push()
+            coll.LANDING_MAX_BYTES = 4096 * 4 * world  # several pieces per call
+            for n in (8 * world * 1000, 8 * world * 7):
+                g = torch.Generator(device="cuda").manual_seed(rank + n)
+                flat = torch.randn(n, device=dev, generator=g)  # ordinary (not symmetric) memory
+                keep = flat.clone()
+                part = n // world
+                acc = torch.full((part,), 0.25, device=dev)
+                coll.reduce_scatter_accumulate_(acc, flat, 0.5)
+                ref = flat.clone()
+                dist.all_reduce(ref)
+                torch.testing.assert_close(acc, 0.25 + 0.5 * ref[rank * part:(rank + 1) * part], rtol=1e-5, atol=1e-5)
+                assert torch.equal(flat, keep)  # the source is left as it was
+            bucket = coll.alloc(world * 2000, torch.float32)
+            g = torch.Generator(device="cuda").manual_seed(50 + rank)
+            data = torch.randn(world * 2000, device=dev, generator=g)
+            bucket.copy_(data)
+            acc = torch.zeros(2000, device=dev)
+            assert coll.bucket_reduce_(bucket, acc, 1.0)
+            ref = data.clone()
+            dist.all_reduce(ref)
+            torch.testing.assert_close(acc, ref[rank * 2000:(rank + 1) * 2000], rtol=1e-5, atol=1e-5)
+            torch.cuda.synchronize()
+            assert torch.count_nonzero(bucket) == 0  # cleared by the push kernel
+            coll.check_errors()
+    finally:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def test_push_reduce_scatter():
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    mp.spawn(_push_worker, args=(2, find_free_port()), nprocs=2, join=True)
+
+
+def _engine_worker(rank: int, world: int, port: int, slots: str, rs_mode: str) -> None:
     _init(rank, world, port)
     try:
         from cs244c_llama_zero_b200.models import LlamaForCausalLM, ModelConfig
@@ -119,6 +168,7 @@ def _engine_worker(rank: int, world: int, port: int, slots: str) -> None:
         from cs244c_llama_zero_b200.parallel.zero import ZeROStage2Optimizer
 
         os.environ["ZB_STAGE2_RING_SLOTS"] = slots
+        os.environ["ZB_RS_MODE"] = rs_mode
         os.environ["ZB_STAGE2_GRADS"] = "ring"  # "auto" keeps the full buffer for a model this small
         cfg = ModelConfig(name="t", vocab_size=1024, max_seq_len=256, dim=256, n_layers=3, n_heads=4, n_kv_heads=2,
                           ffn_dim=512)
@@ -161,8 +211,8 @@ def _engine_worker(rank: int, world: int, port: int, slots: str) -> None:
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("slots", ["2", "1"])
-def test_ring_stage2_trains_like_nccl(slots):
+@pytest.mark.parametrize("slots,rs_mode", [("2", "switch"), ("1", "switch"), ("2", "push")])
+def test_ring_stage2_trains_like_nccl(slots, rs_mode):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
-    mp.spawn(_engine_worker, args=(2, find_free_port(), slots), nprocs=2, join=True)
+    mp.spawn(_engine_worker, args=(2, find_free_port(), slots, rs_mode), nprocs=2, join=True)
