@@ -55,8 +55,9 @@ def parse_args(argv=None) -> argparse.Namespace:
                    help="ZeRO-1/2 unclipped step as one NVLink kernel (reduce-scatter + norm + AdamW + all-gather)")
     p.add_argument("--routed-grads", action="store_true",
                    help="ZeRO-2 without a full gradient buffer: gradients added into their owners' shards over NVLink")
-    p.add_argument("--cuda-graph", action="store_true",
-                   help="run stages 0-2 as one captured CUDA graph per step (TrainSession cuda_graph mode)")
+    p.add_argument("--cuda-graph", nargs="?", const="on", default="auto", choices=["auto", "on", "off"],
+                   help="run stages 0-2 as one captured CUDA graph per step (TrainSession cuda_graph mode); "
+                        "auto (default): on for one GPU, where it measured 8.04-8.08 vs 8.41-8.44 ms per step")
     p.add_argument("--model-size", type=str, default="baseline-small",
                    help="model preset of the headline: baseline-small (the headline config), baseline-1.3b, ...")
     p.add_argument("--extra-configs", type=str, default="baseline-1.3b",
@@ -68,6 +69,8 @@ def parse_args(argv=None) -> argparse.Namespace:
     args.extra_list = [c.strip() for c in args.extra_configs.split(",") if c.strip() and c.strip() != args.model_size]
     if args.headline_stage not in args.stage_list:
         args.headline_stage = args.stage_list[0]
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    args.cuda_graph = args.cuda_graph == "on" or (args.cuda_graph == "auto" and world == 1)
     return args
 
 
