@@ -222,6 +222,22 @@ class NvlinkCollectives(TorchCollectives):
         _maybe_simulate_collective_delay(acc.numel() * flat.element_size(), world)
         return acc
 
+    def reduce_scatter_accumulate_clear_(self, acc: torch.Tensor, flat: torch.Tensor, scale: float) -> bool:
+        """``reduce_scatter_accumulate_`` that also leaves ``flat`` zero, when the push reduce-scatter
+        is on (its kernel clears the source it has finished with, saving the caller a memset before
+        the buffer's next accumulation).  False, doing nothing, otherwise."""
+        world = self._w()
+        if not (self.rs_push() and world > 1 and flat.dtype == torch.float32 and flat.is_cuda
+                and flat.is_contiguous() and acc.dtype == torch.float32 and flat.numel() % (8 * world) == 0):
+            return False
+        if self._skipped("reduce_scatter"):
+            return True
+        slot = self._pace_begin()
+        self._push_rs(flat, flat.numel() // world, acc, scale, True)
+        self._pace_end(slot, "reduce_scatter", flat.numel() * 4)
+        _maybe_simulate_collective_delay(acc.numel() * 4, world)
+        return True
+
     supports_range_reduce_scatter = True
 
     def reduce_scatter_range_accumulate_(self, shard_acc: torch.Tensor, flat: torch.Tensor, lo: int, hi: int,
