@@ -123,11 +123,11 @@ class NvlinkCollectives(TorchCollectives):
 
     def rs_push(self) -> bool:
         """Whether fp32 reduce-scatters run as peer stores into a landing area plus a local sum
-        (``ZB_RS_MODE=push``) or as multicast reductions / peer loads (``switch``).  ``auto``: push at
-        2 and 4 ranks and whenever multicast is off.  Measured at 2 B200 (1 GiB fp32): multicast 320 GB/s
-        bus, peer loads 127 GB/s, while peer stores (the all-gather) reach 634 GB/s: at two ranks a
-        multicast reduction reads both GPUs' copies through the switch (twice the link bytes of a
-        push) and peer loads are latency-bound."""
+        (``ZB_RS_MODE=push``) or as multicast reductions / peer loads (``switch``, the default).
+        ``auto``: push at 2 and 4 ranks and whenever multicast is off.  Measured at 2 B200 (fp32,
+        1 GiB): multicast 323 GB/s bus, push 220 GB/s, peer loads 127 GB/s; `small` stage 2 / 3 steps
+        8.87 / 10.09 ms with multicast vs 9.25 / 10.31 ms with push.  So multicast stays the default;
+        push is kept for switches without multicast."""
         mode = os.environ.get("ZB_RS_MODE", "switch")
         if mode in ("push", "switch"):
             return mode == "push"
@@ -221,22 +221,6 @@ class NvlinkCollectives(TorchCollectives):
         self._pace_end(slot, "reduce_scatter", flat.numel() * flat.element_size())
         _maybe_simulate_collective_delay(acc.numel() * flat.element_size(), world)
         return acc
-
-    def reduce_scatter_accumulate_clear_(self, acc: torch.Tensor, flat: torch.Tensor, scale: float) -> bool:
-        """``reduce_scatter_accumulate_`` that also leaves ``flat`` zero, when the push reduce-scatter
-        is on (its kernel clears the source it has finished with, saving the caller a memset before
-        the buffer's next accumulation).  False, doing nothing, otherwise."""
-        world = self._w()
-        if not (self.rs_push() and world > 1 and flat.dtype == torch.float32 and flat.is_cuda
-                and flat.is_contiguous() and acc.dtype == torch.float32 and flat.numel() % (8 * world) == 0):
-            return False
-        if self._skipped("reduce_scatter"):
-            return True
-        slot = self._pace_begin()
-        self._push_rs(flat, flat.numel() // world, acc, scale, True)
-        self._pace_end(slot, "reduce_scatter", flat.numel() * 4)
-        _maybe_simulate_collective_delay(acc.numel() * 4, world)
-        return True
 
     supports_range_reduce_scatter = True
 

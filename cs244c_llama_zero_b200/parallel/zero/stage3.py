@@ -154,10 +154,7 @@ class Stage3ParamHandle:
         if buf is None:
             buf = torch.zeros(self.padded_numel, dtype=torch.float32, device=self.device)
         else:
-            eng = self.engine
-            if eng._stage_grads_dirty:  # what the previous module left behind
-                eng._stage_grads[: eng._stage_grads_dirty].zero_()
-            eng._stage_grads_dirty = 0
+            buf.zero_()
         for p, v in zip(self.meta.params, self._views(buf, persistent)):
             p.main_grad = v
         return buf
@@ -179,14 +176,7 @@ class Stage3ParamHandle:
         with eng.clock.measure("backward_reduce_scatter", self.full_param_bytes):
             with eng.collectives.label_scope(f"stage3.backward.reduce_scatter.{self.name}"):
                 if self.world_size > 1:
-                    # the staging buffer stays clean when the reduce-scatter clears what it read
-                    # (push mode), so the next module skips its memset; every other path dirties it
-                    clear = getattr(eng.collectives, "reduce_scatter_accumulate_clear_", None)
-                    staged = eng._stage_grads is not None and buf.data_ptr() == eng._stage_grads.data_ptr()
-                    if not (staged and clear is not None and clear(self.grad_shard, buf, 1.0 / self.world_size)):
-                        eng.collectives.reduce_scatter_accumulate_(self.grad_shard, buf, 1.0 / self.world_size)
-                        if staged:
-                            eng._stage_grads_dirty = buf.numel()
+                    eng.collectives.reduce_scatter_accumulate_(self.grad_shard, buf, 1.0 / self.world_size)
                 else:
                     self.grad_shard.add_(buf)
 
@@ -506,10 +496,6 @@ class ZeROStage3Optimizer(ZeROEngineBase):
         self._stage_params: List[torch.Tensor] = []
         self._stage_slot = 0
         self._stage_grads: Optional[torch.Tensor] = None
-        # Elements [0, dirty) of the staging gradient buffer may be non-zero: the next module zeroes
-        # them first.  It is allocated zeroed, a clearing reduce-scatter leaves it zero, and a plain
-        # one leaves the reduced module's extent behind.
-        self._stage_grads_dirty = 0
         alloc = getattr(self.collectives, "alloc", None)
         use_pull = False
         if alloc is not None and self.world_size > 1 and self.device.type == "cuda":
