@@ -118,3 +118,18 @@ def test_clock_sampler_summary_from_samples():
     cs.samples = [(0, 1965.0, 1965.0, []), (0, 1900.0, 1965.0, ["sw_power_cap"]), (0, 300.0, 1965.0, [])]
     s = cs.summary()
     assert s["sm_mhz"] == 1932.5 and s["sm_max_mhz"] == 1965.0 and s["reasons"] == ["sw_power_cap"]
+
+
+def test_bench_cuda_graph_default_follows_world_size(monkeypatch):
+    """``--cuda-graph auto`` (the default) captures stages 0-2 at one GPU only; on/off force it."""
+    sys.path.insert(0, str(ROOT))
+    try:
+        import bench
+    finally:
+        sys.path.pop(0)
+    monkeypatch.delenv("WORLD_SIZE", raising=False)
+    assert bench.parse_args([]).cuda_graph is True
+    assert bench.parse_args(["--cuda-graph", "off"]).cuda_graph is False
+    monkeypatch.setenv("WORLD_SIZE", "8")
+    assert bench.parse_args(["--gpus", "8"]).cuda_graph is False
+    assert bench.parse_args(["--gpus", "8", "--cuda-graph"]).cuda_graph is True
