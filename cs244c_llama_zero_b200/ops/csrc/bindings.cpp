@@ -66,7 +66,7 @@ void linear_fwd(Tensor x, Tensor w, Tensor out, std::optional<Tensor> residual, 
 }
 
 void qkv_rope_fwd(Tensor x, Tensor w, Tensor out, Tensor cos, Tensor sin, int64_t seq_len, int64_t head_dim,
-                  int64_t rope_cols) {
+                  int64_t rope_cols, int64_t bn) {
   check_bf16_2d(x, "x");
   check_bf16_2d(w, "w");
   check_bf16_2d(out, "out");
@@ -86,11 +86,11 @@ void qkv_rope_fwd(Tensor x, Tensor w, Tensor out, Tensor cos, Tensor sin, int64_
   p.head_dim = head_dim;
   p.rope_cols = rope_cols;
   b200::GemmOperands op{x.data_ptr(), w.data_ptr(), (uint64_t)x.stride(0), (uint64_t)w.stride(0)};
-  b200::gemm_launch(op, p, b200::EPI_ROPE, false, false, 0, cur_stream());
+  b200::gemm_launch(op, p, b200::EPI_ROPE, false, false, (int)bn, cur_stream());
 }
 
 // h = silu(x @ Wg^T) * (x @ Wu^T); gu = [x @ Wg^T | x @ Wu^T].  w_gu = [Wg; Wu] of shape [2*ffn, K].
-void swiglu_fwd(Tensor x, Tensor w_gu, Tensor h, Tensor gu) {
+void swiglu_fwd(Tensor x, Tensor w_gu, Tensor h, Tensor gu, int64_t bn) {
   check_bf16_2d(x, "x");
   check_bf16_2d(w_gu, "w_gu");
   check_bf16_2d(h, "h");
@@ -107,7 +107,7 @@ void swiglu_fwd(Tensor x, Tensor w_gu, Tensor h, Tensor gu) {
   p.ld_aux = gu.stride(0);
   p.ffn = ffn;
   b200::GemmOperands op{x.data_ptr(), w_gu.data_ptr(), (uint64_t)x.stride(0), (uint64_t)w_gu.stride(0)};
-  b200::gemm_launch(op, p, b200::EPI_SWIGLU, false, false, 0, cur_stream());
+  b200::gemm_launch(op, p, b200::EPI_SWIGLU, false, false, (int)bn, cur_stream());
 }
 
 // dx[M,K] = dy[M,N] @ w[N,K]
@@ -964,8 +964,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "sm_100a kernels: tcgen05 GEMMs with fused epilogues, flash attention, norms, optimizer, collectives";
   m.def("linear_fwd", &linear_fwd, py::arg("x"), py::arg("w"), py::arg("out"), py::arg("residual") = py::none(),
         py::arg("bn") = 0);
-  m.def("qkv_rope_fwd", &qkv_rope_fwd);
-  m.def("swiglu_fwd", &swiglu_fwd);
+  m.def("qkv_rope_fwd", &qkv_rope_fwd, py::arg("x"), py::arg("w"), py::arg("out"), py::arg("cos"), py::arg("sin"),
+        py::arg("seq_len"), py::arg("head_dim"), py::arg("rope_cols"), py::arg("bn") = 0);
+  m.def("swiglu_fwd", &swiglu_fwd, py::arg("x"), py::arg("w_gu"), py::arg("h"), py::arg("gu"), py::arg("bn") = 0);
   m.def("linear_dgrad", &linear_dgrad, py::arg("dy"), py::arg("w"), py::arg("dx"), py::arg("bn") = 0);
   m.def("gemm_tile_choice", &gemm_tile_choice, py::arg("M"), py::arg("N"), py::arg("K"), py::arg("epi"),
         py::arg("head_dim"), py::arg("allow_split"), py::arg("b_mn"), py::arg("sms"));

@@ -853,6 +853,8 @@ void gemm_launch(const GemmOperands& op, GemmParams p, int epi, bool a_mn, bool 
   if (p.splits <= 0) p.splits = 1;
   B200_CHECK(bn == 128 || bn == 192 || bn == 256, "BN must be 128, 192 or 256");
   B200_CHECK(epi_supports_bn(epi, bn), "this epilogue does not support BN = 192");
+  B200_CHECK(epi != EPI_ROPE || (p.head_dim > 0 && (bn / 2) % p.head_dim == 0),
+             "RoPE epilogue: half the tile width must be a multiple of head_dim");
   B200_CHECK(p.N % 8 == 0, "GEMM output width N must be a multiple of 8");
   B200_CHECK((a_mn || p.K % 8 == 0) && (b_mn || p.K % 8 == 0), "GEMM K must be a multiple of 8 for K-major operands");
   B200_CHECK(!a_mn || p.M % 8 == 0, "GEMM M must be a multiple of 8 for an MN-major A operand");

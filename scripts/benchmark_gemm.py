@@ -8,6 +8,11 @@ of the operands.  It prints TFLOP/s per variant and the fraction of the measured
 variants keep the automatic K-split for their tile.
 
     python scripts/benchmark_gemm.py --shapes 8192x768x4096:dgrad 8192x2048x768:fwd 1280x768x8192:wgrad
+    python scripts/benchmark_gemm.py --shapes 8192x1280x768:rope64-1024 8192x4096x768:swiglu 8192x768x768:res
+
+(`rope<hd>-<cols>`: the fused q|k|v projection with RoPE on its first `cols` columns (the q and k
+heads); `swiglu`: gate|up with the SwiGLU epilogue, N = 2 * ffn; `res`: forward with the
+residual-add epilogue.)
 
 `T x out x in:pair` shapes time a linear layer's backward pair (dx = dy @ w and dw += dy^T @ x):
 the two automatic launches one after the other vs the grouped launch that deals both problems'
@@ -74,9 +79,27 @@ def main(argv=None) -> None:
         g = torch.Generator(device="cuda").manual_seed(0)
         rnd = lambda *s: (torch.randn(*s, device="cuda", generator=g) * 0.05).to(torch.bfloat16)  # noqa: E731
         flops = 2.0 * M * N * K
-        if kind == "fwd":  # y[M,N] = x[M,K] w[N,K]^T
+        if kind in ("fwd", "res"):  # y[M,N] = x[M,K] w[N,K]^T (+ residual r[M,N] for "res")
             x, w, y = rnd(M, K), rnd(N, K), torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
-            run = lambda bn: C.linear_fwd(x, w, y, None, bn)  # noqa: E731
+            r = rnd(M, N) if kind == "res" else None
+            run = lambda bn: C.linear_fwd(x, w, y, r, bn)  # noqa: E731
+            ref = lambda: torch.matmul(x, w.t())  # noqa: E731
+        elif kind.startswith("rope"):  # fused q|k|v projection, RoPE on the first columns: "rope64-1024"
+            hd_s, _, cols_s = kind[4:].partition("-")
+            hd = int(hd_s or 64)
+            rope_cols = int(cols_s) if cols_s else N
+            from cs244c_llama_zero_b200.ops.functional import rope_tables
+
+            seq = 1024 if M % 1024 == 0 else M
+            cos, sin = rope_tables(seq, hd, 10000.0, torch.device("cuda"))
+            x, w, y = rnd(M, K), rnd(N, K), torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+            run = lambda bn: C.qkv_rope_fwd(x, w, y, cos, sin, seq, hd, rope_cols, bn)  # noqa: E731
+            ref = lambda: torch.matmul(x, w.t())  # noqa: E731
+        elif kind == "swiglu":  # h[M,N/2] = silu(x Wg^T) * (x Wu^T), N = 2 * ffn
+            x, w = rnd(M, K), rnd(N, K)
+            h = torch.empty(M, N // 2, device="cuda", dtype=torch.bfloat16)
+            gu = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+            run = lambda bn: C.swiglu_fwd(x, w, h, gu, bn)  # noqa: E731
             ref = lambda: torch.matmul(x, w.t())  # noqa: E731
         elif kind == "dgrad":  # dx[M,N] = dy[M,K] w[K,N]
             dy, w, dx = rnd(M, K), rnd(K, N), torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
