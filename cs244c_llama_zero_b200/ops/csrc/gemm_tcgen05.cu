@@ -31,6 +31,8 @@
 #include <cudaTypedefs.h>
 
 #include <algorithm>
+#include <cstdlib>
+#include <string>
 #include <mutex>
 #include <vector>
 
@@ -779,6 +781,16 @@ static void dispatch_bn(int bn, int cg, const GemmOperands& op, const GemmParams
 // sms / CG concurrent units; its time is (k-blocks + 3 for the pipeline fill) x the per-SM time of one
 // 64-deep k-block, measured on B200 for each variant (microseconds; the bigger the per-SM tile, the
 // better the time per FLOP, pairs better than single CTAs), plus the exposed last epilogue.
+// ZB_GEMM_PAIR_EPI=1 lets the residual / SwiGLU / SwiGLU-backward epilogues run on CTA pairs (the
+// cost model's own choice); by default they stay on single CTAs (see below).
+static bool pair_heavy_epilogues() {
+  static const bool on = [] {
+    const char* v = std::getenv("ZB_GEMM_PAIR_EPI");
+    return v != nullptr && std::string(v) == "1";
+  }();
+  return on;
+}
+
 GemmTile choose_gemm_tile(int M, int N, int K, int epi, int head_dim, bool allow_split, bool b_mn, int sms,
                           int only_bn, int only_cg) {
   struct Variant {
@@ -797,7 +809,9 @@ GemmTile choose_gemm_tile(int M, int N, int K, int epi, int head_dim, bool allow
     // Measured in the model's step: epilogues that read or write several tiles per output tile
     // (residual, SwiGLU forward / backward) ran slower as pairs, whose two CTAs release the shared
     // accumulator together.
-    if (only_cg == 0 && v.cg == 2 && (epi == EPI_RESIDUAL || epi == EPI_SWIGLU || epi == EPI_SWIGLU_BWD)) continue;
+    if (only_cg == 0 && v.cg == 2 && !pair_heavy_epilogues() &&
+        (epi == EPI_RESIDUAL || epi == EPI_SWIGLU || epi == EPI_SWIGLU_BWD))
+      continue;
     if (epi == EPI_ROPE && ((v.bn / 2) % head_dim) != 0) continue;
     const int out_cols = (epi == EPI_SWIGLU) ? v.bn / 2 : v.bn;
     const long tiles = (long)((M + BM * v.cg - 1) / (BM * v.cg)) * ((N + out_cols - 1) / out_cols);
