@@ -75,7 +75,9 @@ void qkv_rope_fwd(Tensor x, Tensor w, Tensor out, Tensor cos, Tensor sin, int64_
   const int M = x.size(0), K = x.size(1), N = w.size(0);
   TORCH_CHECK(w.size(1) == K && out.size(0) == M && out.size(1) == N, "qkv_rope_fwd: shape mismatch");
   TORCH_CHECK(N % head_dim == 0 && 256 % head_dim == 0, "qkv_rope_fwd: head_dim must divide 256 and N");
-  TORCH_CHECK(cos.numel() >= seq_len * head_dim / 2, "rope table too small");
+  TORCH_CHECK(cos.numel() >= seq_len * head_dim / 2 && sin.numel() >= seq_len * head_dim / 2 &&
+                  cos.is_contiguous() && sin.is_contiguous(),
+              "rope tables too small (frequency-major [head_dim/2, seq_len], contiguous)");
   c10::cuda::CUDAGuard g(x.device());
   auto p = base_params(M, N, K);
   p.C = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());

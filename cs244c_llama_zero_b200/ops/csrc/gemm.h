@@ -41,7 +41,7 @@ struct GemmParams {
   int ldr;
   float* C32;
   int ldc32;
-  const float* rope_cos;  // [seq_len, head_dim/2]
+  const float* rope_cos;  // [head_dim/2, seq_len] (frequency-major, see rope_tables_t)
   const float* rope_sin;
   int seq_len;
   int head_dim;

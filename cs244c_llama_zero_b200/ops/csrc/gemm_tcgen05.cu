@@ -528,16 +528,24 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             tmem_ld_32x32b_x32(tbase + h0 + j0, lo);
             tmem_ld_32x32b_x32(tbase + h0 + half + j0, hi);
             tc_wait_ld();
-            if (rotate && B200_IN_BOUNDS(p.errs, (long long)pos * half + j0, 32, (long long)p.seq_len * half, 102)) {
-              const float4* c4 = reinterpret_cast<const float4*>(p.rope_cos + (size_t)pos * half + j0);
-              const float4* s4 = reinterpret_cast<const float4*>(p.rope_sin + (size_t)pos * half + j0);
+            // The tables are frequency-major ([head_dim/2, seq_len]): for one frequency the 32 lanes
+            // of a warp (32 consecutive rows, so consecutive positions) read 32 consecutive floats,
+            // one 128-byte line per load instead of 32 lines for position-major rows.
+            if (rotate && B200_IN_BOUNDS(p.errs, (long long)(j0 + 31) * p.seq_len + pos, 1,
+                                         (long long)p.seq_len * half, 102)) {
+              const float* ct = p.rope_cos + (size_t)j0 * p.seq_len + pos;
+              const float* st = p.rope_sin + (size_t)j0 * p.seq_len + pos;
 #pragma unroll
-              for (int e4 = 0; e4 < 8; ++e4) {
-                const float4 cv = c4[e4], sv = s4[e4];
-                const float cs[4] = {cv.x, cv.y, cv.z, cv.w}, sn[4] = {sv.x, sv.y, sv.z, sv.w};
+              for (int e8 = 0; e8 < 32; e8 += 8) {
+                float cs[8], sn[8];
 #pragma unroll
-                for (int k = 0; k < 4; ++k) {
-                  const int e = 4 * e4 + k;
+                for (int k = 0; k < 8; ++k) {
+                  cs[k] = __ldg(ct + (size_t)(e8 + k) * p.seq_len);
+                  sn[k] = __ldg(st + (size_t)(e8 + k) * p.seq_len);
+                }
+#pragma unroll
+                for (int k = 0; k < 8; ++k) {
+                  const int e = e8 + k;
                   const float x0 = __uint_as_float(lo[e]), x1 = __uint_as_float(hi[e]);
                   lo[e] = __float_as_uint(x0 * cs[k] - x1 * sn[k]);
                   hi[e] = __float_as_uint(x1 * cs[k] + x0 * sn[k]);

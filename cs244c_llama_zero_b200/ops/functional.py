@@ -153,6 +153,16 @@ def rope_tables(seq_len: int, head_dim: int, theta: float, device: torch.device)
     return _ROPE_CACHE[key]
 
 
+def rope_tables_t(seq_len: int, head_dim: int, theta: float, device: torch.device) -> Tuple[torch.Tensor, torch.Tensor]:
+    """The same tables frequency-major, ``[head_dim/2, seq_len]``: the layout the q|k|v GEMM's RoPE
+    epilogue reads (a warp's 32 consecutive positions of one frequency are one 128-byte line)."""
+    key = ("t", seq_len, head_dim, float(theta), str(device))
+    if key not in _ROPE_CACHE:
+        cos, sin = rope_tables(seq_len, head_dim, theta, device)
+        _ROPE_CACHE[key] = (cos.t().contiguous(), sin.t().contiguous())
+    return _ROPE_CACHE[key]
+
+
 # ------------------------------------------------------------------------------ RMSNorm
 class _RMSNormFn(torch.autograd.Function):
     @staticmethod
@@ -392,7 +402,8 @@ class _BlockFn(torch.autograd.Function):
         rstd1 = torch.empty(T, dtype=torch.float32, device=x.device)
         C.rmsnorm_fwd(xf, w_in.detach(), h1, rstd1, eps)
         qkv = torch.empty(T, (H + 2 * KV) * hd, dtype=x.dtype, device=x.device)
-        C.qkv_rope_fwd(h1, w_qkv, qkv, cos, sin, S, hd, (H + KV) * hd)
+        cos_t, sin_t = rope_tables_t(S, hd, cfg.rope_theta, x.device)
+        C.qkv_rope_fwd(h1, w_qkv, qkv, cos_t, sin_t, S, hd, (H + KV) * hd)
         attn, lse = attention_forward(qkv, B, S, H, KV, hd)
         x2 = torch.empty_like(xf)
         C.linear_fwd(attn, wo.detach(), x2, xf)

@@ -88,10 +88,10 @@ def main(argv=None) -> None:
             hd_s, _, cols_s = kind[4:].partition("-")
             hd = int(hd_s or 64)
             rope_cols = int(cols_s) if cols_s else N
-            from cs244c_llama_zero_b200.ops.functional import rope_tables
+            from cs244c_llama_zero_b200.ops.functional import rope_tables_t
 
             seq = 1024 if M % 1024 == 0 else M
-            cos, sin = rope_tables(seq, hd, 10000.0, torch.device("cuda"))
+            cos, sin = rope_tables_t(seq, hd, 10000.0, torch.device("cuda"))
             x, w, y = rnd(M, K), rnd(N, K), torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
             run = lambda bn: C.qkv_rope_fwd(x, w, y, cos, sin, seq, hd, rope_cols, bn)  # noqa: E731
             ref = lambda: torch.matmul(x, w.t())  # noqa: E731

@@ -100,13 +100,14 @@ def _rope_ref(t, S, hd, theta):
 
 @pytest.mark.parametrize("hd,H,KV", [(64, 4, 2), (128, 4, 2)])
 def test_qkv_rope_epilogue(C, hd, H, KV):
-    from cs244c_llama_zero_b200.ops.functional import rope_tables
+    from cs244c_llama_zero_b200.ops.functional import rope_tables, rope_tables_t
 
     B, S, d = 2, 256, 256
     x, w = _bf(B * S, d, seed=8), _bf((H + 2 * KV) * hd, d, scale=0.05, seed=9)
     cos, sin = rope_tables(S, hd, 10000.0, x.device)
+    cos_t, sin_t = rope_tables_t(S, hd, 10000.0, x.device)  # the epilogue's frequency-major layout
     out = torch.empty(B * S, (H + 2 * KV) * hd, device="cuda", dtype=torch.bfloat16)
-    C.qkv_rope_fwd(x, w, out, cos, sin, S, hd, (H + KV) * hd)
+    C.qkv_rope_fwd(x, w, out, cos_t, sin_t, S, hd, (H + KV) * hd)
     full = x.float() @ w.float().t()
     qk = full[:, : (H + KV) * hd]
     ref = torch.cat([_rope_ref(qk.contiguous(), S, hd, 10000.0), full[:, (H + KV) * hd:]], 1)
