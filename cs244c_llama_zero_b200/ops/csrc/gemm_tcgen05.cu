@@ -789,12 +789,15 @@ static void dispatch_bn(int bn, int cg, const GemmOperands& op, const GemmParams
 // sms / CG concurrent units; its time is (k-blocks + 3 for the pipeline fill) x the per-SM time of one
 // 64-deep k-block, measured on B200 for each variant (microseconds; the bigger the per-SM tile, the
 // better the time per FLOP, pairs better than single CTAs), plus the exposed last epilogue.
-// ZB_GEMM_PAIR_EPI=1 lets the residual / SwiGLU / SwiGLU-backward epilogues run on CTA pairs (the
-// cost model's own choice); by default they stay on single CTAs (see below).
+// Whether the residual / SwiGLU / SwiGLU-backward epilogues may run on CTA pairs (the cost model's
+// own choice, the default) or stay on single CTAs (ZB_GEMM_PAIR_EPI=0).  Measured on B200 (isolated,
+// L2 flushed, TFLOP/s single -> pair): SwiGLU 8192x4096x768 988 -> 1071, 8192x11008x2048 1449 -> 1618;
+// residual 8192x768x2048 680 -> 720, 8192x2048x5504 1135 -> 1377; in the training step the 1.3B
+// model's stage 0 went from 76.2 to 74.4 ms and `small` from 7.99 to 7.97 ms.
 static bool pair_heavy_epilogues() {
   static const bool on = [] {
     const char* v = std::getenv("ZB_GEMM_PAIR_EPI");
-    return v != nullptr && std::string(v) == "1";
+    return v == nullptr || std::string(v) != "0";
   }();
   return on;
 }
@@ -814,9 +817,8 @@ GemmTile choose_gemm_tile(int M, int N, int K, int epi, int head_dim, bool allow
   for (const Variant& v : kVariants) {
     if (!epi_supports_bn(epi, v.bn) || (v.cg == 2 && !pair_supports(b_mn, v.bn))) continue;
     if ((only_bn > 0 && v.bn != only_bn) || (only_cg > 0 && v.cg != only_cg)) continue;
-    // Measured in the model's step: epilogues that read or write several tiles per output tile
-    // (residual, SwiGLU forward / backward) ran slower as pairs, whose two CTAs release the shared
-    // accumulator together.
+    // An earlier build measured the epilogues that read or write several tiles per output tile
+    // (residual, SwiGLU forward / backward) slower as pairs; ZB_GEMM_PAIR_EPI=0 restores that choice.
     if (only_cg == 0 && v.cg == 2 && !pair_heavy_epilogues() &&
         (epi == EPI_RESIDUAL || epi == EPI_SWIGLU || epi == EPI_SWIGLU_BWD))
       continue;
