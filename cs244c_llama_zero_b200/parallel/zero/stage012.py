@@ -195,6 +195,43 @@ class _FlatEngine(ZeROEngineBase):
         with self.clock.measure("post_allgather", tensor_num_bytes(self.space.shard(self.space.params))):
             self.collectives.allgather_into(self.space.params, self.space.shard(self.space.params))
 
+    # -- gradient wire format ------------------------------------------------------------
+    def _wire_bf16(self) -> Optional[torch.Tensor]:
+        """``ZB_GRAD_COMM=bf16``: the gradient all-reduce / reduce-scatter moves bf16 (the reference's
+        gradient dtype, half the link bytes of the fp32 ``main_grad`` buffer): the fp32 gradients are
+        cast into a bf16 staging buffer (symmetric when the collectives allocate, so the NVLink
+        kernels reduce it with fp32 accumulation in the switch) and reduced there.  Returns that
+        buffer, or None for the default fp32 wire format."""
+        if os.environ.get("ZB_GRAD_COMM", "fp32") != "bf16" or self.world_size == 1 or self.space.grads is None:
+            return None
+        stage = getattr(self, "_bf16_wire", None)
+        if stage is None:
+            alloc = getattr(self.collectives, "alloc", None) if self.device.type == "cuda" else None
+            n = self.space.grads.numel()
+            stage = alloc(n, torch.bfloat16) if alloc is not None else torch.zeros(n, dtype=torch.bfloat16,
+                                                                                   device=self.device)
+            self._bf16_wire = stage
+        return stage
+
+    def _allreduce_grads(self, grads: torch.Tensor, scale: float) -> None:
+        """``grads = scale * sum_ranks(grads)`` in the configured wire format."""
+        wire = self._wire_bf16()
+        if wire is None:
+            self.collectives.allreduce_scaled_(grads, scale)
+            return
+        wire.copy_(grads)
+        self.collectives.allreduce_scaled_(wire, scale)
+        grads.copy_(wire)
+
+    def _reduce_scatter_grads(self, acc: torch.Tensor, grads: torch.Tensor, scale: float) -> None:
+        """``acc += scale * chunk_rank(sum_ranks(grads))`` in the configured wire format."""
+        wire = self._wire_bf16()
+        if wire is None:
+            self.collectives.reduce_scatter_accumulate_(acc, grads, scale)
+            return
+        wire.copy_(grads)
+        self.collectives.reduce_scatter_accumulate_(acc, wire, scale)
+
     # -- state dict ---------------------------------------------------------------------
     def _hparams(self) -> Dict[str, object]:
         return {"lr": self.lr, "betas": self.betas, "eps": self.eps, "weight_decay": self.weight_decay}
@@ -222,7 +259,7 @@ class ZeROStage0DDP(_FlatEngine):
         if self.world_size > 1:
             self._record_memory_event("measured_step_stage0_pre_allreduce")
             with self.clock.measure("allreduce", tensor_num_bytes(grads)):
-                self.collectives.allreduce_scaled_(grads, inv_w)
+                self._allreduce_grads(grads, inv_w)
             self._record_memory_event("measured_step_stage0_post_allreduce")
         norm = sum_of_squares(grads).sqrt()
         self.step_count += 1
@@ -309,7 +346,7 @@ class ZeROStage1Optimizer(_ShardedStateMixin, _FlatEngine):
         if self.world_size > 1:
             self._record_memory_event("measured_step_stage1_pre_allreduce")
             with self.clock.measure("allreduce", tensor_num_bytes(grads)):
-                self.collectives.allreduce_scaled_(grads, 1.0 / self.world_size)
+                self._allreduce_grads(grads, 1.0 / self.world_size)
             self._record_memory_event("measured_step_stage1_post_allreduce")
         norm = sum_of_squares(grads).sqrt()
         self.step_count += 1
@@ -765,7 +802,7 @@ class ZeROStage2Optimizer(_ShardedStateMixin, _FlatEngine):
         with self.clock.measure("backward_reduce_scatter", tensor_num_bytes(grads)):
             with self.collectives.label_scope("stage2.backward.reduce_scatter.flat_grad_buffer"):
                 if self.world_size > 1:
-                    self.collectives.reduce_scatter_accumulate_(self.grad_shard, grads, 1.0 / self.world_size)
+                    self._reduce_scatter_grads(self.grad_shard, grads, 1.0 / self.world_size)
                 elif not self._shard_is_buffer:
                     self.grad_shard.add_(grads)
         self._record_memory_event("measured_step_stage2_post_reduce_scatter")

@@ -7,6 +7,8 @@ trains on its local batch; a replica trains on the all-gathered global batch wit
 
 from __future__ import annotations
 
+import os
+
 from contextlib import nullcontext
 
 import pytest
@@ -581,3 +583,49 @@ def test_stage2_gradient_mode_auto_policy(monkeypatch) -> None:
     stub.collectives = SimpleNamespace(supports_bucket_reduce=True)
     stub.world_size = 1
     assert not want(stub)
+
+
+def _bf16_wire_worker(rank: int, world: int, port: int, stage: int) -> None:
+    init_gloo(rank, world, port)
+    os.environ["ZB_GRAD_COMM"] = "bf16"
+    try:
+        cfg = _cfg()
+        torch.manual_seed(1234)
+        model = LlamaForCausalLM(cfg)
+        for p in model.parameters():
+            dist.broadcast(p.data, src=0)
+        ref = LlamaForCausalLM(cfg)
+        ref.load_state_dict(model.state_dict())
+        hp = dict(lr=1e-3, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.05)
+        engine = ENGINES[stage](model=model, collectives=TorchCollectives(), **hp)
+        opt = torch.optim.AdamW(ref.parameters(), **hp)
+        for step in range(3):
+            ids = _local_batch(step * 10, rank, 3, cfg.max_seq_len, cfg.vocab_size)
+            engine.zero_grad()
+            engine.prepare_forward()
+            engine.backward(model(input_ids=ids, labels=ids).loss)
+            engine.step(max_grad_norm=0.0)
+            opt.zero_grad(set_to_none=True)
+            parts = [torch.empty_like(ids) for _ in range(world)]
+            dist.all_gather(parts, ids)
+            g = torch.cat(parts)
+            ref(input_ids=g, labels=g).loss.backward()
+            opt.step()
+        assert engine._bf16_wire is not None and engine._bf16_wire.dtype == torch.bfloat16
+        # bf16 gradients on the wire.  AdamW normalises each element's gradient, so an update differs
+        # from the fp32 one by a small part of lr, except where rounding the cross-rank sum of nearly
+        # cancelling contributions flips a tiny gradient's sign (at most 2 lr per step there).
+        lr = hp["lr"]
+        for (n, a), (_, b) in zip(model.named_parameters(), ref.named_parameters()):
+            d = (a - b).abs()
+            assert d.max().item() <= 3 * 2 * lr + 1e-6, (n, d.max().item())
+            assert (d > 0.3 * lr).float().mean().item() <= 0.02, (n, (d > 0.3 * lr).float().mean().item())
+    finally:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("stage", [0, 1, 2])
+def test_bf16_gradient_wire_format(stage: int) -> None:
+    """``ZB_GRAD_COMM=bf16``: gradients reduced in bf16 (the reference's dtype) train like fp32."""
+    _spawn(_bf16_wire_worker, 2, stage)
