@@ -828,11 +828,15 @@ GemmTile choose_gemm_tile(int M, int N, int K, int epi, int head_dim, bool allow
     const int max_split = allow_split ? std::max(1, std::min(32, kb / 4)) : 1;
     const int slots = std::max(1, sms / v.cg);
     const double epi_us = (heavy ? 3.0 : 0.5) * v.bn / 256.0;
+    // A residual tile on a CTA pair waits for both CTAs' epilogues before the shared accumulator is
+    // released: ~1 us per round, which decides short-K shapes (8192x768x768: 450 TFLOP/s single vs
+    // 410 as pairs) and not long ones (8192x768x2048: 681 vs 720).
+    const double round_extra = (v.cg == 2 && epi == EPI_RESIDUAL) ? 1.0 : 0.0;
     for (int s = 1; s <= max_split; ++s) {
       const int kbs = (kb + s - 1) / s;
       const long units = tiles * ((kb + kbs - 1) / kbs);
       const long rounds = (units + slots - 1) / slots;
-      const double cost = rounds * (kbs + 3.0) * v.us_per_kblock + epi_us;
+      const double cost = rounds * ((kbs + 3.0) * v.us_per_kblock + round_extra) + epi_us;
       if (cost < best_cost * 0.98) {
         best_cost = cost;
         best = {v.bn, s, v.cg};
