@@ -7,6 +7,7 @@ and the same loss definition (in-model label shift, mean over all shifted tokens
 
 from __future__ import annotations
 
+import math
 import time
 
 import pytest
@@ -218,3 +219,18 @@ def test_peak_lookup_and_roofline_fraction(tmp_path, monkeypatch):
     assert F.peak_bf16_tflops(str(tmp_path)) == (1000.0, "ZB_PEAK_TFLOPS")
     assert F.roofline_fraction(5e14, 1.0, 1000.0) == pytest.approx(0.5)
     assert F.roofline_fraction(1.0, 0.0, 1000.0) is None
+
+
+def test_rope_tables_frequency_major_layout():
+    """The q|k|v GEMM's RoPE epilogue reads the same angles frequency-major: [head_dim/2, seq_len]."""
+    import torch
+
+    from cs244c_llama_zero_b200.ops.functional import rope_tables, rope_tables_t
+
+    cos, sin = rope_tables(64, 32, 10000.0, torch.device("cpu"))
+    cos_t, sin_t = rope_tables_t(64, 32, 10000.0, torch.device("cpu"))
+    assert cos.shape == (64, 16) and cos_t.shape == (16, 64) and cos_t.is_contiguous()
+    assert torch.equal(cos_t, cos.t()) and torch.equal(sin_t, sin.t())
+    pos, i = 37, 5
+    angle = pos * 10000.0 ** (-2 * i / 32)
+    assert abs(float(cos_t[i, pos]) - math.cos(angle)) < 1e-5 and abs(float(sin_t[i, pos]) - math.sin(angle)) < 1e-5
